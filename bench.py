@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""MoE-layer throughput on B200: the north-star metric of this repository.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c3|c4d|c4p] [--tokens T]
+
+One step = one forward of the GLM-style MoE layer (router, dispatch, routed +
+shared SwiGLU experts over Q8_0 weights, weighted combine) on one batch of
+synthetic tokens.  Default workload: BASELINE config 1 (H=6144, I=2048, E=256,
+top-8, 1 shared expert, Q8_0, bf16 activations), decode batch T=32 per GPU.
+
+Prints ONE JSON line (rank 0).  `value` is device-timed tokens/s over all ranks
+(CUDA events on the launch stream, max over ranks, L2 flushed between steps);
+`e2e` is the same metric through the public API with host (pinned) buffers and
+the H2D/D2H copies inside the timed region; `roofline` is the dominant kernel
+(the expert gate/up GEMV) against measured HBM bandwidth; `cpu_baseline` is the
+numpy oracle timed on a bounded sample on this host.
+
+`--impl reference` times the reference algorithm's CPU implementation (the numpy
+restatement of native/glm53/moe_ref.py, which is what the reference runs on CPU;
+its Vyb GPU kernels cannot be built here) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MoE-layer tokens/s (decode b1/b32, prefill 4k) + % HBM/TC roofline, 1-8 GPU"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def args_parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4d", "c4p"])
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--fmt", default=None, choices=[None, "q8_0", "exl3"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+def algorithmic_bytes(cfg, n_distinct_experts, has_shared=True):
+    H, I, E, T = cfg.hidden, cfg.inter, cfg.n_experts, cfg.tokens
+    per_expert = 3 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 3 * (H * I * 3 // 8 + 2 * (H + I))
+    gate_up = 2 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 2 * (H * I * 3 // 8 + 2 * (H + I))
+    layer = (n_distinct_experts + (1 if has_shared else 0)) * per_expert + E * H * 4 + T * H * 4
+    gu = (n_distinct_experts + (1 if has_shared else 0)) * gate_up
+    return layer, gu
+
+
+def build_ours(cfg, rank):
+    import torch
+    from vybforge_b200 import synth
+    from vybforge_b200.moe import MoELayer, quantizer
+    x, w_r, bias, rng = synth.router_inputs(cfg)
+    dev = synth.expert_q8_cuda(cfg, quantizer)
+    E = cfg.n_experts
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
+                     router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
+                     gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
+                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    return layer, xd, (x, w_r, bias), dev
+
+
+def cpu_baseline_ours(cfg, host, dev, idx, budget_s):
+    """Oracle (numpy, f64) on a bounded sample of this step's tokens, same bytes as the GPU."""
+    from oracle import moe_oracle as orc
+    x, w_r, bias = host
+    H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+    # sample: the first n tokens whose distinct experts fit the CPU budget (~0.2 s per expert)
+    n = 1
+    while n < cfg.tokens and len(np.unique(idx[:n + 1])) + 1 <= max(4, int(budget_s / 0.25)):
+        n += 1
+    need = sorted(set(np.unique(idx[:n]).tolist()) | {E})
+    raw = {e: tuple(dev[p][e].cpu().numpy() for p in range(3)) for e in need}
+
+    def get(e):
+        g, u, d = raw[e]
+        return (orc.q8_0_expert_inout(g, I, H), orc.q8_0_expert_inout(u, I, H), orc.q8_0_expert_inout(d, H, I))
+    t0 = time.perf_counter()
+    orc.moe_block_grouped(x[:n], w_r, bias, get, lambda: get(E), E, cfg.topk)
+    dt = time.perf_counter() - t0
+    cores = os.cpu_count()
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"first {n} of {cfg.tokens} tokens ({len(need)} experts incl. shared), oracle "
+                      f"dequant+f64 GEMM per expert, numpy/OpenBLAS on {cores} host threads, {dt:.1f} s"}
+
+
+def run_ours(a, rank, world, local_rank):
+    import torch
+    from vybforge_b200 import synth, _lib
+    from vybforge_b200.moe import init
+    import ctypes as C
+    torch.cuda.set_device(local_rank)
+    init(local_rank)
+    cfg = synth.config(a.workload, tokens=a.tokens, fmt=a.fmt, seed=rank)
+    if cfg.fmt != "q8_0" or a.workload not in ("c1", "c4d"):
+        raise SystemExit(f"workload {a.workload}/{cfg.fmt} not wired into bench yet")
+    layer, xd, host, dev = build_ours(cfg, rank)
+    T = cfg.tokens
+    st = torch.cuda.current_stream()
+    out = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty((T, cfg.topk), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, cfg.topk), dtype=torch.float32, device="cuda")
+    ws = layer.workspace(T)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")   # > 126 MB L2
+    for _ in range(max(3, a.warmup)):
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+    torch.cuda.synchronize()
+    lib = layer.lib
+    lib.vfmoe_profile_enable(layer.handle, 1)
+    lib.vfmoe_profile_read(layer.handle, (C.c_double * 8)(), 8, None)  # reset
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    clocks = ClockSampler(local_rank)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for i in range(a.steps):
+        flush.zero_()
+        ev[i][0].record(st)
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+        ev[i][1].record(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    step_ms = [s.elapsed_time(e) for s, e in ev]
+    stage = (C.c_double * 8)()
+    launches = C.c_int64(0)
+    nf = lib.vfmoe_profile_read(layer.handle, stage, 8, C.byref(launches))
+    lib.vfmoe_profile_enable(layer.handle, 0)
+    ms = float(np.mean(step_ms))
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T / (ms * 1e-3)
+
+    # e2e through the public API with pinned host buffers, copies inside the timed region
+    xh = xd.cpu().pin_memory()
+    oh = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    xin = torch.empty_like(xd)
+    for i in range(a.steps):
+        flush.zero_()
+        ev2[i][0].record(st)
+        xin.copy_(xh, non_blocking=True)
+        o = layer.forward(xin, out=out, workspace=ws)
+        oh.copy_(o, non_blocking=True)
+        ev2[i][1].record(st)
+    torch.cuda.synchronize()
+    e2e_ms = float(np.mean([s.elapsed_time(e) for s, e in ev2]))
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    idx_np = idx.cpu().numpy()
+    n_distinct = len(np.unique(idx_np))
+    layer_bytes, gu_bytes = algorithmic_bytes(cfg, n_distinct)
+    pk, pk_kind = peaks()
+    gu_ms = stage[2] / max(nf, 1)
+    layer_gbs = layer_bytes / (ms * 1e-3) / 1e9
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": "expert gate/up GEMV (Q8_0, fused SwiGLU)", "achieved": round(achieved, 1),
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+            "peak_source": pk_kind, "traffic": None,
+            "algorithmic_bytes_per_launch": gu_bytes,
+            "layer_hbm_frac": round(layer_gbs / pk["hbm_gbs"], 4),
+            "stage_ms_per_step": {n: round(stage[i] / max(nf, 1), 4) for i, n in
+                                  enumerate(["router", "dispatch_gather", "gate_up", "down", "combine"])}}
+    res = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "q8_0 weights x fp16 MMA operands, fp32 accumulate; bf16 in/out",
+           "data": "synthetic (seeded N(0,1) bf16 tokens, N(0,0.02) weights quantized to Q8_0)",
+           "config": {"workload": f"{a.workload}: decode T={T}/GPU, H={cfg.hidden}, I={cfg.inter}, "
+                                  f"E={cfg.n_experts}, top-{cfg.topk} + 1 shared, Q8_0",
+                      "tokens_per_gpu": T, "global_batch": T * world, "parallelism":
+                          "replicas" if world > 1 else "single",
+                      "distinct_experts": n_distinct,
+                      "l2": "256 MiB memset between timed steps, outside the step events"},
+           "gpu_launches": int(launches.value), "clocks": clk, "roofline": roof,
+           "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                   "h2d_bytes_per_step": T * cfg.hidden * 2, "d2h_bytes_per_step": T * cfg.hidden * 2,
+                   "ms_per_step": round(e2e_ms, 4)}}
+    if rank == 0 and not a.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_ours(cfg, host, dev, idx_np, a.cpu_budget_s)
+    return res
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(a):
+    """The reference algorithm on the host cores (numpy restatement of
+    native/glm53/moe_ref.py; Q8_0 decode of native/tools/q8_0_ref.py)."""
+    from oracle import moe_oracle as orc
+    from vybforge_b200 import synth
+    cfg = synth.config(a.workload, tokens=a.tokens, fmt=a.fmt, seed=0)
+    x, w_r, bias, rng = synth.router_inputs(cfg)
+    H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+    idx, wt = orc.route(x, w_r, bias, cfg.topk)
+    n = 1
+    while n < cfg.tokens and len(np.unique(idx[:n + 1])) + 1 <= max(4, int(a.cpu_budget_s / 0.25)):
+        n += 1
+    need = sorted(set(np.unique(idx[:n]).tolist()) | {E})
+    gen = np.random.default_rng(1)
+
+    def rand_q8(rows, cols):   # random Q8_0 bytes: dequant+GEMM cost does not depend on values
+        b = gen.integers(0, 256, size=(rows, cols // 32, 34), dtype=np.uint8)
+        b[:, :, 0:2] = np.frombuffer(np.full(rows * cols // 32, 6e-4, np.float16).tobytes(),
+                                     np.uint8).reshape(rows, cols // 32, 2)
+        return b.reshape(rows, -1)
+    raw = {e: (rand_q8(I, H), rand_q8(I, H), rand_q8(H, I)) for e in need}
+
+    def get(e):
+        g, u, d = raw[e]
+        return (orc.q8_0_expert_inout(g, I, H), orc.q8_0_expert_inout(u, I, H), orc.q8_0_expert_inout(d, H, I))
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        orc.moe_block_grouped(x[:n], w_r, bias, get, lambda: get(E), E, cfg.topk)
+        if i >= a.warmup:
+            times.append(time.perf_counter() - t0)
+        if sum(times) > 120:
+            break
+    dt = float(np.mean(times))
+    v = n / dt
+    cores = os.cpu_count()
+    sample = (f"first {n} of {cfg.tokens} tokens ({len(need)} experts incl. shared) per step; "
+              f"numpy f64 dequant + GEMM per expert on {cores} host threads; {len(times)} timed steps")
+    return {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": "tokens/s", "n_gpus": a.gpus,
+            "steps": len(times), "warmup": a.warmup, "ms_per_step": round(dt * 1e3 * cfg.tokens / n, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded); expert bytes random Q8_0 blocks",
+            "config": {"workload": f"{a.workload}: decode T={cfg.tokens}, H={H}, I={I}, E={E}, top-{cfg.topk}",
+                       "tokens_per_gpu": cfg.tokens},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    a = args_parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(a)), flush=True)
+        return
+    import torch
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    res = run_ours(a, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

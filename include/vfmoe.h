@@ -1,0 +1,176 @@
+/*
+ * vfmoe.h -- C ABI of libvfmoe.so, the B200 (sm_100a) GLM-style MoE layer.
+ *
+ * Drop-in for the MoE path of rickenator/VybForge (paths relative to that
+ * project).  The reference crosses its device boundary with PTX kernels that
+ * take ONE pointer to a params block of 8-byte words
+ * (native/kernels/moe.vyb:15-19), launched through cuda_launch4i /
+ * tensor::launch1 (native/host/moe_driver.vyb:20-23,150; native/tensor/tensor.vyb:173-181),
+ * and with host loops in native/glm53/glm_engine.vyb:2728-2991.  This header
+ * replaces those entry points with plain extern "C" functions:
+ *
+ *   - every device address, stream and handle is an int64_t (a Vyb `Int`);
+ *   - every status is an int: 0 = OK, negative = error (VFMOE_ERR_*), mirroring
+ *     the CUresult checks of moe_driver.vyb:101-160; the library never exits
+ *     or aborts, and vfmoe_last_error() returns the message;
+ *   - descriptors are structs made only of 8-byte words (int64_t / double), so
+ *     a host without struct FFI can build one as a params block of words;
+ *   - all device work is enqueued on the caller's stream (0 = legacy default
+ *     stream); no call synchronizes except where stated;
+ *   - the caller owns activations, outputs and weights (weights are borrowed,
+ *     never freed); the library owns handle state and, only when the caller
+ *     passes workspace = 0, an internal workspace it grows on demand.
+ *
+ * Data formats
+ *   x        [T, hidden], dtype VFMOE_DT_BF16 or VFMOE_DT_F32
+ *   router   W_r fp32 [n_experts, hidden], selection bias fp32 [n_experts]
+ *   Q8_0     per matrix: output rows, each K/32 GGUF blocks of 34 bytes
+ *            (fp16 d, int8 q[32]); gate/up [inter][hidden], down [hidden][inter]
+ *   EXL3     per matrix (in, out) = (K, N): trellis uint16 [K/16][N/16][16*bits],
+ *            suh fp16 [K], svh fp16 [N] (native/exl3/README.md:26-31)
+ *   idx      int32 [T, topk] (the reference stores float32, moe.vyb:76)
+ *   w        fp32 [T, topk]
+ *   out      [T, hidden], dtype VFMOE_DT_BF16 or VFMOE_DT_F32
+ */
+#ifndef VFMOE_H
+#define VFMOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VFMOE_ABI_VERSION 1
+
+/* status codes */
+#define VFMOE_OK 0
+#define VFMOE_ERR_INVALID (-1)     /* bad argument or descriptor */
+#define VFMOE_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define VFMOE_ERR_NOMEM (-3)       /* device allocation failed */
+#define VFMOE_ERR_HANDLE (-4)      /* unknown or destroyed handle */
+#define VFMOE_ERR_WORKSPACE (-5)   /* caller workspace smaller than vfmoe_workspace_bytes */
+#define VFMOE_ERR_DEVICE (-6)      /* a kernel flagged an error (bounded wait expired, bad id) */
+#define VFMOE_ERR_UNSUPPORTED (-7) /* shape or format not supported by this build */
+#define VFMOE_ERR_NCCL (-8)        /* NCCL unavailable or an NCCL call failed */
+
+/* dtype ids: identical to native/dtype/dtype.vyb:26-28 (dt_f32/dt_f16/dt_bf16) */
+#define VFMOE_DT_F32 0
+#define VFMOE_DT_F16 1
+#define VFMOE_DT_BF16 2
+
+/* expert weight formats */
+#define VFMOE_WFMT_Q8_0 1
+#define VFMOE_WFMT_EXL3 2
+
+/* One projection (gate, up or down) of a stack of experts.  Expert e's data
+ * starts at data + e * expert_stride (bytes); for EXL3 its suh/svh start at
+ * suh + e * suh_stride and svh + e * svh_stride.  For a single matrix (the
+ * shared expert) the strides are ignored. */
+typedef struct vfmoe_matrix {
+    int64_t data;
+    int64_t expert_stride;
+    int64_t suh;
+    int64_t suh_stride;
+    int64_t svh;
+    int64_t svh_stride;
+} vfmoe_matrix;
+
+/* One MoE layer (native/glm53/moe_ref.py:25-30 constants become fields;
+ * moe.vyb's params block +8 gateW, +16 bias, +56..+96 expert/shared weights). */
+typedef struct vfmoe_layer_desc {
+    int64_t hidden;         /* H */
+    int64_t inter;          /* moe_intermediate I */
+    int64_t n_experts;      /* routed experts E */
+    int64_t topk;           /* k */
+    int64_t weight_format;  /* VFMOE_WFMT_* */
+    int64_t exl3_bits;      /* 3 or 4 when weight_format == VFMOE_WFMT_EXL3 */
+    int64_t x_dtype;        /* VFMOE_DT_BF16 or VFMOE_DT_F32 */
+    int64_t out_dtype;      /* VFMOE_DT_BF16 or VFMOE_DT_F32 */
+    double routed_scale;    /* routed_scaling_factor, 2.5 in GLM (moe_ref.py:29) */
+    double swiglu_limit;    /* 10.0 in GLM (moe_ref.py:30) */
+    int64_t router_w;       /* fp32 [E, H] */
+    int64_t router_bias;    /* fp32 [E], e_score_correction_bias (selection only) */
+    vfmoe_matrix gate, up, down;          /* routed experts, stacked over E */
+    vfmoe_matrix sh_gate, sh_up, sh_down; /* shared expert; sh_gate.data == 0: none */
+} vfmoe_layer_desc;
+
+/* ABI version (VFMOE_ABI_VERSION). */
+int vfmoe_version(void);
+
+/* Select the CUDA device for the calling thread and check it is sm_100.
+ * Replaces tensor_init (native/tensor/tensor.vyb:32-45). */
+int vfmoe_init(int device);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated,
+ * at most n bytes).  Returns the message length. */
+int vfmoe_last_error(char *buf, int64_t n);
+
+/* Validate a layer descriptor and build its launch state (tensor maps, tile
+ * plans).  Returns a handle > 0, or a negative VFMOE_ERR_*. */
+int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc);
+
+/* Release a handle and any internal workspace it owns. */
+int vfmoe_layer_destroy(int64_t handle);
+
+/* Bytes of workspace vfmoe_forward / vfmoe_route need for up to t_max tokens. */
+int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max);
+
+/* Router only: idx int32 [T, topk], w fp32 [T, topk] from x [T, H].
+ * logits = x . W_r^T (fp64 accumulation), score = sigmoid(logit), top-k on
+ * score + bias (lowest index wins ties), w = score / (sum + 1e-20) * scale.
+ * Replaces moe_route (native/kernels/moe.vyb:32-95) and the host router of
+ * glm_engine.vyb:2728-2803.  workspace may be 0 (internal). */
+int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out,
+                int64_t workspace, int64_t ws_bytes, int64_t stream);
+
+/* Full MoE layer: out = sum_l w[t,l] * FFN_{idx[t,l]}(x[t]) + FFN_shared(x[t]),
+ * FFN = clamped SwiGLU (moe_ref.py:81-112).  idx_out / w_out may be 0.
+ * Replaces moe_route + moe_act + moe_down (moe.vyb:32-170) and tail_site's
+ * router, expert loop and shared expert (glm_engine.vyb:2728-2991). */
+int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out,
+                  int64_t idx_out, int64_t w_out,
+                  int64_t workspace, int64_t ws_bytes, int64_t stream);
+
+/* Synchronize `stream` and report whether any kernel of this handle flagged a
+ * device-side error since the last call (VFMOE_ERR_DEVICE), then clear it. */
+int vfmoe_check_device_error(int64_t handle, int64_t stream);
+
+/* Per-stage device timing (replaces the reference's T_MOE / MMT / DEQT wall-clock tag
+ * lines, native/glm53/glm_engine.vyb:2951).  enable = 1 makes every later
+ * vfmoe_forward on this handle record CUDA events on its stream between stages. */
+int vfmoe_profile_enable(int64_t handle, int enable);
+
+/* Synchronize on the recorded events and return, in stage_ms[0..n), the summed
+ * device milliseconds per stage since the last read: 0 router, 1 dispatch+gather,
+ * 2 gate/up+SwiGLU, 3 down, 4 combine.  *launches (if non-null) gets the number of
+ * kernels launched by those forwards.  Returns the number of forwards measured and
+ * resets the accumulators. */
+int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *launches);
+
+/* RMSNorm: y = x * w / sqrt(mean(x^2) + eps) over rows of D, x/y dtype
+ * VFMOE_DT_BF16 or VFMOE_DT_F32, w fp32 [D].  Replaces tensor::rmsnorm
+ * (native/tensor/tensor.vyb:217-231, kernel native/kernels/rmsnorm.vyb). */
+int vfmoe_rmsnorm(int64_t x, int64_t w, int64_t y, int64_t S, int64_t D, double eps,
+                  int64_t dtype, int64_t stream);
+
+/* Q8_0 rows -> dense [rows, k] (dst_dtype VFMOE_DT_F32 or VFMOE_DT_F16).
+ * Replaces q8_0deq (native/kernels/q8_0.vyb:11-30, which widens to f64). */
+int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k,
+                       int64_t dst_dtype, int64_t stream);
+
+/* fp32 [rows, k] -> Q8_0 rows (ggml quantize_row_q8_0_ref rule; the reference
+ * has no quantizer, it reads GGUF bytes). */
+int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, int64_t stream);
+
+/* EXL3 trellis -> rotated-basis values W^ as fp16 [K, N] (no Hadamard).
+ * Replaces exl3deq / exl3deq32 (native/kernels/exl3.vyb:207-242,375-422).
+ * bits = 3 (layout defined by this library) or 4 (reference slot map). */
+int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, int64_t bits,
+                      int64_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VFMOE_H */

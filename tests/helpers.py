@@ -1,0 +1,71 @@
+"""Shared builders for the GPU tests: synthetic layers on the device plus the
+matching oracle getters (the oracle reads back exactly the bytes the GPU uses)."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import moe_oracle as orc
+from vybforge_b200 import synth
+from vybforge_b200.moe import MoELayer, quantizer
+
+TOL_MAX_ABS = 2e-2   # north_star: max-abs 2e-2 on the combined output
+TOL_REL_L2 = 1e-3    # north_star: rel-L2 1e-3
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def to_dev_x(x, cfg):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    return (t.to(torch.bfloat16) if cfg.x_dtype == "bf16" else t).cuda()
+
+
+class Built:
+    """A device layer + host-side copies for the oracle."""
+
+    def __init__(self, cfg, weights="numpy", out_dtype=torch.float32, zipf=False):
+        self.cfg = cfg
+        x, w_r, bias, rng = synth.router_inputs(cfg)
+        self.x, self.w_r, self.bias = x, w_r, bias
+        H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+        if weights == "numpy":
+            ex = synth.expert_q8_numpy(cfg, rng)
+            self.dev = {p: torch.from_numpy(ex[p]).cuda() for p in range(3)}
+        else:
+            self.dev = synth.expert_q8_cuda(cfg, quantizer)
+        self.x_dev = to_dev_x(x, cfg)
+        self.wr_dev = torch.from_numpy(w_r).cuda()
+        self.bias_dev = torch.from_numpy(bias).cuda()
+        self.layer = self.make_layer(out_dtype)
+        self._cache = {}
+
+    def make_layer(self, out_dtype):
+        cfg, E = self.cfg, self.cfg.n_experts
+        g, u, d = self.dev[0], self.dev[1], self.dev[2]
+        return MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
+                        router_w=self.wr_dev, router_bias=self.bias_dev,
+                        gate=g[:E], up=u[:E], down=d[:E], shared=(g[E], u[E], d[E]),
+                        x_dtype=torch.bfloat16 if cfg.x_dtype == "bf16" else torch.float32,
+                        out_dtype=out_dtype)
+
+    def expert(self, e):
+        if e not in self._cache:
+            H, I = self.cfg.hidden, self.cfg.inter
+            g = self.dev[0][e].cpu().numpy()
+            u = self.dev[1][e].cpu().numpy()
+            d = self.dev[2][e].cpu().numpy()
+            self._cache[e] = (orc.q8_0_expert_inout(g, I, H), orc.q8_0_expert_inout(u, I, H),
+                              orc.q8_0_expert_inout(d, H, I))
+        return self._cache[e]
+
+    def oracle(self, tokens=None):
+        """Oracle (out, idx, w) for all tokens or a subset (routing is per token)."""
+        cfg = self.cfg
+        x = self.x if tokens is None else self.x[tokens]
+        return orc.moe_block_grouped(x, self.w_r, self.bias, self.expert,
+                                     lambda: self.expert(cfg.n_experts), cfg.n_experts, cfg.topk)

@@ -1,0 +1,105 @@
+"""CPU checks of the C ABI: libvfmoe.so loads, exports every symbol that
+include/*.h declares, and rejects bad input with status codes (no GPU work)."""
+
+import ctypes as C
+import glob
+import os
+import re
+
+import pytest
+
+from vybforge_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:int|int64_t|void|const char\s*\*)\s+(vfmoe_\w+)\s*\(", src, re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def header_defines():
+    src = open(os.path.join(REPO, "include", "vfmoe.h")).read()
+    return {m.group(1): int(m.group(2)) for m in re.finditer(r"#define\s+(VFMOE_\w+)\s+\(?(-?\d+)\)?", src)}
+
+
+def test_library_exports_every_header_symbol(built_lib):
+    names = header_functions()
+    assert "vfmoe_forward" in names and "vfmoe_route" in names
+    missing = [n for n in names if not hasattr(built_lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    assert set(header_functions()) <= set(_lib._SIGS)
+
+
+def test_constants_match_header():
+    d = header_defines()
+    assert d["VFMOE_ABI_VERSION"] == 1
+    for k in ("OK", "ERR_INVALID", "ERR_CUDA", "ERR_NOMEM", "ERR_HANDLE", "ERR_WORKSPACE", "ERR_DEVICE",
+              "ERR_UNSUPPORTED", "ERR_NCCL"):
+        assert d["VFMOE_" + k] == getattr(_lib, k)
+    assert (d["VFMOE_DT_F32"], d["VFMOE_DT_F16"], d["VFMOE_DT_BF16"]) == (0, 1, 2)  # native/dtype/dtype.vyb
+    assert (d["VFMOE_WFMT_Q8_0"], d["VFMOE_WFMT_EXL3"]) == (_lib.WFMT_Q8_0, _lib.WFMT_EXL3)
+
+
+def test_descriptor_is_a_block_of_8_byte_words():
+    assert C.sizeof(_lib.Matrix) == 6 * 8
+    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6) * 8
+
+
+def test_version(built_lib):
+    assert built_lib.vfmoe_version() == 1
+
+
+def _desc(**kw):
+    d = _lib.LayerDesc()
+    d.hidden, d.inter, d.n_experts, d.topk = 1024, 512, 16, 4
+    d.weight_format, d.x_dtype, d.out_dtype = _lib.WFMT_Q8_0, _lib.DT_F32, _lib.DT_F32
+    d.routed_scale, d.swiglu_limit = 2.5, 10.0
+    d.router_w, d.router_bias = 4096, 8192
+    d.gate.data, d.up.data, d.down.data = 1 << 20, 2 << 20, 3 << 20
+    d.gate.expert_stride = d.up.expert_stride = 512 * 1088
+    d.down.expert_stride = 1024 * 544
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("field,value", [("hidden", 1000), ("topk", 40), ("topk", 0), ("x_dtype", 7),
+                                         ("weight_format", 9), ("n_experts", 0), ("router_w", 0)])
+def test_invalid_descriptor_rejected(built_lib, field, value):
+    d = _desc(**{field: value})
+    rc = built_lib.vfmoe_layer_create(C.byref(d))
+    assert rc == _lib.ERR_INVALID
+    assert "invalid layer descriptor" in _lib.last_error()
+
+
+def test_null_descriptor_and_unknown_handle(built_lib):
+    assert built_lib.vfmoe_layer_create(None) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_layer_destroy(12345) == _lib.ERR_HANDLE
+    assert built_lib.vfmoe_workspace_bytes(12345, 8) == _lib.ERR_HANDLE
+    assert built_lib.vfmoe_forward(12345, 0, 1, 0, 0, 0, 0, 0, 0) == _lib.ERR_HANDLE
+    assert "unknown layer handle" in _lib.last_error()
+
+
+def test_standalone_ops_validate_arguments(built_lib):
+    assert built_lib.vfmoe_q8_0_dequant(0, 0, 4, 33, 0, 0) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_q8_0_quantize(0, 0, 4, 30, 0) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_exl3_decode(0, 0, 15, 16, 3, 0) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_rmsnorm(0, 0, 0, 2, 0, 1e-5, 0, 0) == _lib.ERR_INVALID
+
+
+def test_init_without_device_returns_status(built_lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    rc = built_lib.vfmoe_init(0)
+    assert rc < 0
+    assert _lib.last_error()

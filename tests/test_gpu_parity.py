@@ -1,0 +1,172 @@
+"""GPU parity: the CUDA path (through the C ABI) against the oracle.
+
+Bars (north_star): expert ids and the permutation bit-exact (lowest-index ties);
+combined output max-abs <= 2e-2 and rel-L2 <= 1e-3; standalone weight decoders
+bit-exact."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from vybforge_b200 import synth, moe
+from vybforge_b200.quant import quantize_q8_0
+
+from helpers import Built, rel_l2, TOL_MAX_ABS, TOL_REL_L2
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def c0():
+    moe.init(0)
+    return Built(synth.config("c0"))
+
+
+def test_c0_matches_reference_golden(c0):
+    g = np.load(os.path.join(GOLD, "c0_moe_block.npz"))
+    out, idx, w = c0.layer.moe_block(c0.x_dev)
+    torch.cuda.synchronize()
+    c0.layer.check_device_error()
+    np.testing.assert_array_equal(idx.cpu().numpy(), g["idx"])
+    np.testing.assert_allclose(w.cpu().numpy(), g["w"], rtol=0, atol=1e-6)
+    o = out.cpu().numpy()
+    assert np.abs(o - g["out"]).max() <= TOL_MAX_ABS
+    assert rel_l2(o, g["out"]) <= TOL_REL_L2
+
+
+def test_c0_bf16_output_is_rounded_fp32_output(c0):
+    l16 = c0.make_layer(torch.bfloat16)
+    o16 = l16.forward(c0.x_dev)
+    o32 = c0.layer.forward(c0.x_dev)
+    torch.testing.assert_close(o16, o32.to(torch.bfloat16), rtol=0, atol=0)
+
+
+def test_c0_deterministic(c0):
+    a = c0.layer.forward(c0.x_dev).clone()
+    b = c0.layer.forward(c0.x_dev)
+    assert torch.equal(a, b)
+
+
+def test_route_only_matches_forward_routing(c0):
+    idx, w = c0.layer.route(c0.x_dev)
+    _, idx2, w2 = c0.layer.moe_block(c0.x_dev)
+    assert torch.equal(idx, idx2) and torch.equal(w, w2)
+
+
+@pytest.mark.parametrize("T", [1, 3, 16])
+def test_c0_token_counts(c0, T):
+    out, idx, w = c0.layer.moe_block(c0.x_dev[:T].contiguous())
+    ro, ri, rw = c0.oracle(np.arange(T))
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    o = out.cpu().numpy()
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
+
+
+def test_zero_tokens_is_noop(c0):
+    out = torch.full((0, c0.cfg.hidden), 7.0, device="cuda")
+    c0.layer.forward(c0.x_dev[:0], out=out)
+    torch.cuda.synchronize()
+
+
+def test_workspace_too_small_is_an_error(c0):
+    from vybforge_b200 import _lib
+    ws = torch.empty(256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(_lib.VfmoeError) as ei:
+        c0.layer.forward(c0.x_dev, workspace=ws)
+    assert ei.value.code == _lib.ERR_WORKSPACE
+
+
+def test_route_ties_lowest_index():
+    moe.init(0)
+    cfg = synth.config("c0")
+    b = Built(cfg)
+    w_r = b.w_r.copy()
+    w_r[2] = 0.0                    # experts 2 and 9: logit exactly 0 on every token
+    w_r[9] = 0.0
+    bias = np.zeros_like(b.bias)
+    bias[2] = bias[9] = 1.0         # choice 1.5 for both: top-2, exact tie -> 2 before 9
+    b.wr_dev = torch.from_numpy(w_r).cuda()
+    b.bias_dev = torch.from_numpy(bias).cuda()
+    layer = b.make_layer(torch.float32)
+    idx, w = layer.route(b.x_dev)
+    ri, rw = orc.route(b.x, w_r, bias, cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+
+
+# ----------------------------------------------------------------------------- full-size C1 (Q8_0 decode)
+@pytest.fixture(scope="module")
+def c1():
+    moe.init(0)
+    return Built(synth.config("c1", tokens=32), weights="cuda")
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_c1_decode_parity(c1, T):
+    x = c1.x_dev[:T].contiguous()
+    out, idx, w = c1.layer.moe_block(x)
+    ro, ri, rw = c1.oracle(np.arange(T))
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    o = out.cpu().numpy()
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS
+    assert rel_l2(o, ro) <= TOL_REL_L2
+
+
+def test_c1_t32_routing_and_token_subset(c1):
+    out, idx, w = c1.layer.moe_block(c1.x_dev)
+    ri, rw = orc.route(c1.x, c1.w_r, c1.bias, c1.cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    sub = np.array([0, 13, 31])
+    ro, _, _ = c1.oracle(sub)
+    o = out.cpu().numpy()[sub]
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
+    c1.layer.check_device_error()
+
+
+# ----------------------------------------------------------------------------- standalone decoders
+def test_q8_0_quantize_bit_exact():
+    moe.init(0)
+    rng = np.random.default_rng(4)
+    w = rng.normal(0, 0.02, (64, 512)).astype(np.float32)
+    w[1, :32] = 0
+    w[2, :] = rng.normal(0, 50.0, 512)
+    dst = torch.empty((64, 512 // 32 * 34), dtype=torch.uint8, device="cuda")
+    moe.q8_0_quantize(torch.from_numpy(w).cuda(), dst)
+    np.testing.assert_array_equal(dst.cpu().numpy(), quantize_q8_0(w))
+
+
+def test_q8_0_dequant_bit_exact():
+    g = np.load(os.path.join(GOLD, "q8_0_kat.npz"))
+    raw, deq = g["raw"], g["deq"]
+    rows, k = raw.shape[0], raw.shape[1] // 34 * 32
+    d32 = moe.q8_0_dequant(torch.from_numpy(raw).cuda(), rows, k, torch.float32)
+    np.testing.assert_array_equal(d32.cpu().numpy().astype(np.float64), deq)
+    d16 = moe.q8_0_dequant(torch.from_numpy(raw).cuda(), rows, k, torch.float16)
+    np.testing.assert_array_equal(d16.cpu().numpy(), deq.astype(np.float16))
+
+
+def test_exl3_3bpw_decode_bit_exact():
+    rng = np.random.default_rng(8)
+    K, N = 256, 384
+    tr = rng.integers(0, 1 << 16, size=(K // 16, N // 16, 48), dtype=np.uint32).astype(np.uint16)
+    got = moe.exl3_decode(torch.from_numpy(tr.view(np.int16)).cuda(), K, N, 3)
+    want = orc.exl3_what(tr, 3).astype(np.float16)
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rmsnorm(dtype):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((7, 6144)).astype(np.float32) * 3
+    w = (1 + rng.normal(0, 0.02, 6144)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda().to(dtype)
+    y = moe.rmsnorm(xd, torch.from_numpy(w).cuda(), 1e-5).float().cpu().numpy()
+    ref = orc.rmsnorm(xd.float().cpu().numpy(), w, 1e-5)
+    tol = 1e-5 if dtype == torch.float32 else 8e-3
+    assert rel_l2(y, ref) < tol

@@ -1,0 +1,101 @@
+"""ctypes binding of libvfmoe.so (the C ABI in include/vfmoe.h).
+
+This is the same binding a non-Python host makes (INTEGRATION.md shows the Vyb
+``extern "C"`` block): plain int64 addresses, int status codes.  If the library
+is missing the import fails loudly -- there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvfmoe.so")
+
+# status codes (vfmoe.h)
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_NOMEM = -3
+ERR_HANDLE = -4
+ERR_WORKSPACE = -5
+ERR_DEVICE = -6
+ERR_UNSUPPORTED = -7
+ERR_NCCL = -8
+
+# dtype ids (native/dtype/dtype.vyb:26-28)
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+# weight formats
+WFMT_Q8_0, WFMT_EXL3 = 1, 2
+
+
+class VfmoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"vfmoe error {code}: {msg}")
+        self.code = code
+
+
+class Matrix(C.Structure):
+    _fields_ = [("data", C.c_int64), ("expert_stride", C.c_int64), ("suh", C.c_int64),
+                ("suh_stride", C.c_int64), ("svh", C.c_int64), ("svh_stride", C.c_int64)]
+
+
+class LayerDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int64), ("inter", C.c_int64), ("n_experts", C.c_int64), ("topk", C.c_int64),
+                ("weight_format", C.c_int64), ("exl3_bits", C.c_int64), ("x_dtype", C.c_int64),
+                ("out_dtype", C.c_int64), ("routed_scale", C.c_double), ("swiglu_limit", C.c_double),
+                ("router_w", C.c_int64), ("router_bias", C.c_int64),
+                ("gate", Matrix), ("up", Matrix), ("down", Matrix),
+                ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix)]
+
+
+I64 = C.c_int64
+_SIGS = {
+    "vfmoe_version": (C.c_int, []),
+    "vfmoe_init": (C.c_int, [C.c_int]),
+    "vfmoe_last_error": (C.c_int, [C.c_char_p, I64]),
+    "vfmoe_layer_create": (I64, [C.POINTER(LayerDesc)]),
+    "vfmoe_layer_destroy": (C.c_int, [I64]),
+    "vfmoe_workspace_bytes": (I64, [I64, I64]),
+    "vfmoe_route": (C.c_int, [I64] * 8),
+    "vfmoe_forward": (C.c_int, [I64] * 9),
+    "vfmoe_check_device_error": (C.c_int, [I64, I64]),
+    "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),
+    "vfmoe_profile_read": (C.c_int, [I64, C.POINTER(C.c_double), I64, C.POINTER(I64)]),
+    "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),
+    "vfmoe_q8_0_dequant": (C.c_int, [I64] * 6),
+    "vfmoe_q8_0_quantize": (C.c_int, [I64] * 5),
+    "vfmoe_exl3_decode": (C.c_int, [I64] * 6),
+}
+
+_lib = None
+
+
+def load():
+    """Load libvfmoe.so once (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m vybforge_b200.build` "
+                               "(there is no CPU fallback for the MoE path)")
+        lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(lib, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = C.create_string_buffer(2048)
+    lib.vfmoe_last_error(buf, 2048)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> int:
+    if rc < 0:
+        raise VfmoeError(rc, last_error())
+    return rc

@@ -1,0 +1,506 @@
+// C-ABI entry points of libvfmoe.so (declared in include/vfmoe.h).
+//
+// Host orchestration of one MoE layer forward (the reference does this with host
+// loops in native/glm53/glm_engine.vyb:2728-2991 and three PTX launches in
+// native/host/moe_driver.vyb:150-160).  Here every step is a kernel enqueued on the
+// caller's stream, with no host synchronization:
+//
+//   router (fp64 logits, top-k, counts) -> dispatch (canonical permutation)
+//   -> gather (fp16 rows) -> gate/up + SwiGLU -> down -> weighted combine.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "expert_tc.h"
+
+namespace vfmoe {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+}
+
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line) {
+    set_error("%s failed: %s (%s:%d)", what, cudaGetErrorString(e), file, line);
+    return e == cudaErrorMemoryAllocation ? VFMOE_ERR_NOMEM : VFMOE_ERR_CUDA;
+}
+
+struct Layer {
+    vfmoe_layer_desc d;
+    int device = 0;
+    int H = 0, I = 0, E = 0, k = 0;
+    int has_shared = 0;
+    int64_t q8_row_gate = 0, q8_row_down = 0;
+    int *dev_err = nullptr;      // device error word (allocated at create)
+    void *own_ws = nullptr;      // internal workspace when the caller passes none
+    int64_t own_ws_bytes = 0;
+    TcPlan tc;                   // tensor-core launch state (tensor maps)
+    int use_tc = 1;
+    // profiling (vfmoe_profile_enable / vfmoe_profile_read)
+    int prof = 0;
+    std::vector<cudaEvent_t> ev_pool;         // free events
+    std::vector<std::vector<cudaEvent_t>> ev_pending;  // per forward: kNumStages + 1 events
+    double stage_ms[8] = {0};
+    int64_t n_fwd = 0, launches = 0;
+};
+
+static constexpr int kNumStages = 5;
+
+static cudaEvent_t take_event(Layer &L) {
+    cudaEvent_t e = nullptr;
+    if (!L.ev_pool.empty()) {
+        e = L.ev_pool.back();
+        L.ev_pool.pop_back();
+    } else if (cudaEventCreate(&e) != cudaSuccess) {
+        e = nullptr;
+    }
+    return e;
+}
+
+static std::mutex g_mu;
+static std::unordered_map<int64_t, Layer *> g_layers;
+static int64_t g_next_handle = 1;
+
+static Layer *get_layer(int64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_layers.find(h);
+    if (it == g_layers.end()) {
+        set_error("unknown layer handle %lld", (long long)h);
+        return nullptr;
+    }
+    return it->second;
+}
+
+// ----------------------------------------------------------------------------- workspace
+struct WsLayout {
+    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, total;
+};
+
+static WsLayout ws_layout(const Layer &L, int64_t T) {
+    WsLayout o{};
+    const int64_t rows = T * L.k + T;
+    int64_t p = 0;
+    auto take = [&](int64_t bytes) {
+        const int64_t at = p;
+        p = align_up(p + bytes, 256);
+        return at;
+    };
+    o.counts = take((L.E + 2) * 4);
+    o.offsets = take((L.E + 2) * 4);
+    o.perm_tok = take(rows * 4);
+    o.pos_of = take(T * L.k * 4);
+    o.idx = take(T * L.k * 4);
+    o.w = take(T * L.k * 4);
+    o.part = take(router_partial_doubles((int)T, L.H, L.E) * 8);
+    o.xp = take(rows * L.H * 2);
+    o.act = take(rows * L.I * 2);
+    o.y = take(rows * L.H * 4);
+    o.total = p;
+    return o;
+}
+
+static int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **base) {
+    const WsLayout lay = ws_layout(L, T);
+    if (ws) {
+        if (ws_bytes < lay.total) {
+            set_error("workspace too small: %lld < %lld bytes for T=%lld", (long long)ws_bytes,
+                      (long long)lay.total, (long long)T);
+            return VFMOE_ERR_WORKSPACE;
+        }
+        if (ws % 256) {
+            set_error("workspace must be 256-byte aligned");
+            return VFMOE_ERR_INVALID;
+        }
+        *base = reinterpret_cast<char *>(ws);
+        return VFMOE_OK;
+    }
+    if (L.own_ws_bytes < lay.total) {
+        if (L.own_ws) VF_CUDA(cudaFree(L.own_ws));
+        L.own_ws = nullptr;
+        L.own_ws_bytes = 0;
+        VF_CUDA(cudaMalloc(&L.own_ws, lay.total));
+        L.own_ws_bytes = lay.total;
+    }
+    *base = reinterpret_cast<char *>(L.own_ws);
+    return VFMOE_OK;
+}
+
+static MatrixRef mref(const vfmoe_matrix &m) {
+    MatrixRef r;
+    r.data = reinterpret_cast<const uint8_t *>(m.data);
+    r.expert_stride = m.expert_stride;
+    r.suh = reinterpret_cast<const __half *>(m.suh);
+    r.suh_stride = m.suh_stride;
+    r.svh = reinterpret_cast<const __half *>(m.svh);
+    r.svh_stride = m.svh_stride;
+    return r;
+}
+
+static bool aligned16(int64_t p) { return (p & 15) == 0; }
+
+static int validate(const vfmoe_layer_desc &d) {
+    auto bad = [](const char *m) {
+        set_error("invalid layer descriptor: %s", m);
+        return VFMOE_ERR_INVALID;
+    };
+    if (d.hidden <= 0 || d.inter <= 0 || d.n_experts <= 0 || d.topk <= 0) return bad("non-positive shape");
+    if (d.hidden % 256 || d.inter % 256) return bad("hidden and inter must be multiples of 256");
+    if (d.n_experts > 1024) return bad("n_experts > 1024");
+    if (d.topk > 32 || d.topk > d.n_experts) return bad("topk must be <= 32 and <= n_experts");
+    if (d.x_dtype != VFMOE_DT_BF16 && d.x_dtype != VFMOE_DT_F32) return bad("x_dtype must be BF16 or F32");
+    if (d.out_dtype != VFMOE_DT_BF16 && d.out_dtype != VFMOE_DT_F32) return bad("out_dtype must be BF16 or F32");
+    if (!d.router_w || !d.router_bias) return bad("router weights missing");
+    if (!aligned16(d.router_w)) return bad("router_w must be 16-byte aligned");
+    if (d.weight_format == VFMOE_WFMT_Q8_0) {
+        const int64_t rg = d.hidden / 32 * 34, rd = d.inter / 32 * 34;
+        if (!d.gate.data || !d.up.data || !d.down.data) return bad("routed expert weights missing");
+        if (d.n_experts > 1 && (d.gate.expert_stride < d.inter * rg || d.up.expert_stride < d.inter * rg ||
+                                d.down.expert_stride < d.hidden * rd))
+            return bad("expert_stride smaller than one expert matrix");
+        const int64_t ptrs[6] = {d.gate.data, d.up.data, d.down.data, d.sh_gate.data, d.sh_up.data, d.sh_down.data};
+        for (int i = 0; i < 6; ++i)
+            if (ptrs[i] && !aligned16(ptrs[i])) return bad("weight pointers must be 16-byte aligned");
+        if ((d.gate.expert_stride | d.up.expert_stride | d.down.expert_stride) & 15)
+            return bad("expert strides must be multiples of 16 bytes");
+        if (d.sh_gate.data && (!d.sh_up.data || !d.sh_down.data)) return bad("shared expert incomplete");
+    } else if (d.weight_format == VFMOE_WFMT_EXL3) {
+        if (d.exl3_bits != 3 && d.exl3_bits != 4) return bad("exl3_bits must be 3 or 4");
+        if (d.hidden % 128 || d.inter % 128) return bad("EXL3 needs multiples of 128");
+        return bad("EXL3 expert products are not available in this build yet");
+    } else {
+        return bad("unknown weight_format");
+    }
+    return VFMOE_OK;
+}
+
+}  // namespace vfmoe
+
+using namespace vfmoe;
+
+extern "C" {
+
+int vfmoe_version(void) { return VFMOE_ABI_VERSION; }
+
+int vfmoe_last_error(char *buf, int64_t n) {
+    const int len = (int)g_last_error.size();
+    if (buf && n > 0) {
+        const int64_t c = len < n - 1 ? len : n - 1;
+        memcpy(buf, g_last_error.data(), (size_t)c);
+        buf[c] = 0;
+    }
+    return len;
+}
+
+int vfmoe_init(int device) {
+    int n = 0;
+    VF_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) {
+        set_error("device %d out of range (%d devices)", device, n);
+        return VFMOE_ERR_INVALID;
+    }
+    VF_CUDA(cudaSetDevice(device));
+    cudaDeviceProp p;
+    VF_CUDA(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10) {
+        set_error("device %d is sm_%d%d; libvfmoe is built for sm_100a", device, p.major, p.minor);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    return VFMOE_OK;
+}
+
+int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
+    if (!desc) {
+        set_error("null descriptor");
+        return VFMOE_ERR_INVALID;
+    }
+    int rc = validate(*desc);
+    if (rc) return rc;
+    Layer *L = new Layer();
+    L->d = *desc;
+    L->H = (int)desc->hidden;
+    L->I = (int)desc->inter;
+    L->E = (int)desc->n_experts;
+    L->k = (int)desc->topk;
+    L->has_shared = desc->sh_gate.data != 0;
+    L->q8_row_gate = desc->hidden / 32 * 34;
+    L->q8_row_down = desc->inter / 32 * 34;
+    cudaGetDevice(&L->device);
+    cudaError_t e = cudaMalloc(&L->dev_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(L->dev_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cuda_fail(e, "cudaMalloc(error word)", __FILE__, __LINE__);
+        delete L;
+        return VFMOE_ERR_CUDA;
+    }
+    rc = tc_plan_create(L->d, L->tc);
+    if (rc) {
+        cudaFree(L->dev_err);
+        delete L;
+        return rc;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int64_t h = g_next_handle++;
+    g_layers[h] = L;
+    return h;
+}
+
+int vfmoe_layer_destroy(int64_t handle) {
+    Layer *L;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_layers.find(handle);
+        if (it == g_layers.end()) {
+            set_error("unknown layer handle %lld", (long long)handle);
+            return VFMOE_ERR_HANDLE;
+        }
+        L = it->second;
+        g_layers.erase(it);
+    }
+    if (L->own_ws) cudaFree(L->own_ws);
+    if (L->dev_err) cudaFree(L->dev_err);
+    for (auto &ev : L->ev_pending)
+        for (auto e : ev) L->ev_pool.push_back(e);
+    for (auto e : L->ev_pool) cudaEventDestroy(e);
+    delete L;
+    return VFMOE_OK;
+}
+
+int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (t_max < 0) {
+        set_error("negative t_max");
+        return VFMOE_ERR_INVALID;
+    }
+    return ws_layout(*L, t_max).total;
+}
+
+static int route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout &lay, int32_t **idx_p,
+                      float **w_p, cudaStream_t st) {
+    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
+    VF_CUDA(cudaMemsetAsync(counts, 0, (L.E + 2) * sizeof(int32_t), st));
+    int32_t *idx = *idx_p ? *idx_p : reinterpret_cast<int32_t *>(base + lay.idx);
+    float *w = *w_p ? *w_p : reinterpret_cast<float *>(base + lay.w);
+    int rc = launch_router(reinterpret_cast<const void *>(x), (int)L.d.x_dtype,
+                           reinterpret_cast<const float *>(L.d.router_w),
+                           reinterpret_cast<const float *>(L.d.router_bias), (int)T, L.H, L.E, L.k,
+                           L.d.routed_scale, reinterpret_cast<double *>(base + lay.part), idx, w, counts, st);
+    *idx_p = idx;
+    *w_p = w;
+    return rc;
+}
+
+int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out, int64_t workspace,
+                int64_t ws_bytes, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (T < 0 || (T > 0 && (!x || !idx_out || !w_out))) {
+        set_error("vfmoe_route: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    if (T == 0) return VFMOE_OK;
+    char *base;
+    int rc = ensure_ws(*L, T, workspace, ws_bytes, &base);
+    if (rc) return rc;
+    const WsLayout lay = ws_layout(*L, T);
+    int32_t *idx = reinterpret_cast<int32_t *>(idx_out);
+    float *w = reinterpret_cast<float *>(w_out);
+    return route_impl(*L, x, T, base, lay, &idx, &w, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx_out, int64_t w_out,
+                  int64_t workspace, int64_t ws_bytes, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (T < 0 || (T > 0 && (!x || !out))) {
+        set_error("vfmoe_forward: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    if (T == 0) return VFMOE_OK;
+    if (T > (int64_t)1 << 24) {
+        set_error("vfmoe_forward: T=%lld exceeds 2^24", (long long)T);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char *base;
+    int rc = ensure_ws(*L, T, workspace, ws_bytes, &base);
+    if (rc) return rc;
+    const WsLayout lay = ws_layout(*L, T);
+    int32_t *idx = reinterpret_cast<int32_t *>(idx_out);
+    float *w = reinterpret_cast<float *>(w_out);
+    std::vector<cudaEvent_t> ev;
+    auto mark = [&]() {
+        if (!L->prof) return;
+        cudaEvent_t e = take_event(*L);
+        if (e) {
+            cudaEventRecord(e, st);
+            ev.push_back(e);
+        }
+    };
+    mark();
+    rc = route_impl(*L, x, T, base, lay, &idx, &w, st);
+    if (rc) return rc;
+    mark();
+    int64_t nlaunch = 2;
+
+    MoeArgs a{};
+    a.T = (int)T;
+    a.H = L->H;
+    a.I = L->I;
+    a.E = L->E;
+    a.k = L->k;
+    a.has_shared = L->has_shared;
+    a.fmt = (int)L->d.weight_format;
+    a.exl3_bits = (int)L->d.exl3_bits;
+    a.limit = (float)L->d.swiglu_limit;
+    a.gate = mref(L->d.gate);
+    a.up = mref(L->d.up);
+    a.down = mref(L->d.down);
+    a.sh_gate = mref(L->d.sh_gate);
+    a.sh_up = mref(L->d.sh_up);
+    a.sh_down = mref(L->d.sh_down);
+    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
+    int32_t *offsets = reinterpret_cast<int32_t *>(base + lay.offsets);
+    int32_t *perm_tok = reinterpret_cast<int32_t *>(base + lay.perm_tok);
+    int32_t *pos_of = reinterpret_cast<int32_t *>(base + lay.pos_of);
+    a.offsets = offsets;
+    a.perm_tok = perm_tok;
+    a.xp = reinterpret_cast<__half *>(base + lay.xp);
+    a.act = reinterpret_cast<__half *>(base + lay.act);
+    a.y = reinterpret_cast<float *>(base + lay.y);
+    a.err = L->dev_err;
+
+    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, perm_tok, pos_of, offsets, L->dev_err, st);
+    if (rc) return rc;
+    const int64_t rows = T * L->k + (L->has_shared ? T : 0);
+    rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
+                       reinterpret_cast<__half *>(base + lay.xp), st);
+    if (rc) return rc;
+    nlaunch += 2;
+    mark();
+    if (L->use_tc && tc_supported(L->tc, a)) {
+        rc = launch_experts_tc(L->tc, a, st, [&]() { mark(); });
+    } else {
+        rc = launch_experts_simt(a, st, [&]() { mark(); });
+    }
+    if (rc) return rc;
+    nlaunch += 2;
+    mark();
+    rc = launch_combine(a.y, pos_of, w, (int)T, L->H, L->k, L->has_shared, reinterpret_cast<void *>(out),
+                        (int)L->d.out_dtype, st);
+    if (rc) return rc;
+    nlaunch += 1;
+    mark();
+    if (L->prof) {
+        if ((int)ev.size() == kNumStages + 1) {
+            L->ev_pending.push_back(ev);
+        } else {
+            for (auto e : ev) L->ev_pool.push_back(e);
+        }
+        L->launches += nlaunch;
+    }
+    return VFMOE_OK;
+}
+
+int vfmoe_profile_enable(int64_t handle, int enable) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    L->prof = enable ? 1 : 0;
+    return VFMOE_OK;
+}
+
+int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *launches) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    for (auto &ev : L->ev_pending) {
+        VF_CUDA(cudaEventSynchronize(ev.back()));
+        for (int s = 0; s < kNumStages; ++s) {
+            float ms = 0.f;
+            VF_CUDA(cudaEventElapsedTime(&ms, ev[s], ev[s + 1]));
+            L->stage_ms[s] += ms;
+        }
+        for (auto e : ev) L->ev_pool.push_back(e);
+        L->n_fwd += 1;
+    }
+    L->ev_pending.clear();
+    for (int64_t s = 0; s < n && s < 8; ++s) stage_ms[s] = L->stage_ms[s];
+    if (launches) *launches = L->launches;
+    const int nf = (int)L->n_fwd;
+    for (int s = 0; s < 8; ++s) L->stage_ms[s] = 0;
+    L->n_fwd = 0;
+    L->launches = 0;
+    return nf;
+}
+
+int vfmoe_check_device_error(int64_t handle, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    VF_CUDA(cudaStreamSynchronize(st));
+    int h = 0;
+    VF_CUDA(cudaMemcpy(&h, L->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        VF_CUDA(cudaMemset(L->dev_err, 0, sizeof(int)));
+        set_error("device-side error code %d", h);
+        return VFMOE_ERR_DEVICE;
+    }
+    return VFMOE_OK;
+}
+
+int vfmoe_rmsnorm(int64_t x, int64_t w, int64_t y, int64_t S, int64_t D, double eps, int64_t dtype,
+                  int64_t stream) {
+    if (S < 0 || D <= 0 || (S > 0 && (!x || !w || !y)) ||
+        (dtype != VFMOE_DT_BF16 && dtype != VFMOE_DT_F32 && dtype != VFMOE_DT_F16)) {
+        set_error("vfmoe_rmsnorm: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_rmsnorm(reinterpret_cast<const void *>(x), reinterpret_cast<const float *>(w),
+                          reinterpret_cast<void *>(y), S, (int)D, (float)eps, (int)dtype,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k, int64_t dst_dtype, int64_t stream) {
+    if (rows < 0 || k <= 0 || k % 32 || (rows > 0 && (!src || !dst)) ||
+        (dst_dtype != VFMOE_DT_F32 && dst_dtype != VFMOE_DT_F16)) {
+        set_error("vfmoe_q8_0_dequant: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_q8_0_dequant(reinterpret_cast<const uint8_t *>(src), reinterpret_cast<void *>(dst), rows, k,
+                               (int)dst_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, int64_t stream) {
+    if (rows < 0 || k <= 0 || k % 32 || (rows > 0 && (!src_f32 || !dst)) || (src_f32 & 15)) {
+        set_error("vfmoe_q8_0_quantize: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_q8_0_quantize(reinterpret_cast<const float *>(src_f32), reinterpret_cast<uint8_t *>(dst), rows,
+                                k, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, int64_t bits, int64_t stream) {
+    if (K <= 0 || N <= 0 || K % 16 || N % 16 || !trellis || !dst_f16) {
+        set_error("vfmoe_exl3_decode: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    if (bits != 3) {
+        set_error("vfmoe_exl3_decode: bits=%lld not supported by this build", (long long)bits);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    return launch_exl3_decode(reinterpret_cast<const uint16_t *>(trellis), reinterpret_cast<__half *>(dst_f16), K,
+                              N, (int)bits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

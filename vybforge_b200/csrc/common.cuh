@@ -1,0 +1,97 @@
+// Shared device/host helpers for libvfmoe (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/vfmoe.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libvfmoe is built for sm_100a only"
+#endif
+
+namespace vfmoe {
+
+// ----------------------------------------------------------------------------- host errors
+void set_error(const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
+
+#define VF_CUDA(call)                                                                  \
+    do {                                                                               \
+        cudaError_t _e = (call);                                                       \
+        if (_e != cudaSuccess) return ::vfmoe::cuda_fail(_e, #call, __FILE__, __LINE__); \
+    } while (0)
+
+#define VF_LAUNCH_CHECK(name)                                                          \
+    do {                                                                               \
+        cudaError_t _e = cudaGetLastError();                                           \
+        if (_e != cudaSuccess) return ::vfmoe::cuda_fail(_e, name, __FILE__, __LINE__); \
+    } while (0)
+
+// Device-side error codes written to a layer's error word (first error wins).
+enum DevErr : int {
+    DEV_OK = 0,
+    DEV_BAD_EXPERT_ID = 1,   // router produced an id outside [0, E)
+    DEV_WAIT_TIMEOUT = 2,    // a bounded mbarrier / flag wait expired
+    DEV_BAD_COUNT = 3,       // dispatch counts inconsistent with T*k
+};
+
+__device__ __forceinline__ void raise_dev_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// ----------------------------------------------------------------------------- numerics
+__device__ __forceinline__ float ld_act(const void *p, int64_t i, int dtype) {
+    if (dtype == VFMOE_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+    if (dtype == VFMOE_DT_F16) return __half2float(reinterpret_cast<const __half *>(p)[i]);
+    return reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void st_act(void *p, int64_t i, float v, int dtype) {
+    if (dtype == VFMOE_DT_BF16) reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+    else if (dtype == VFMOE_DT_F16) reinterpret_cast<__half *>(p)[i] = __float2half_rn(v);
+    else reinterpret_cast<float *>(p)[i] = v;
+}
+
+// Clamped SwiGLU of native/glm53/moe_ref.py:81-84: silu(min(g, L)) * clip(u, -L, L).
+__device__ __forceinline__ float swiglu_clamped(float g, float u, float lim) {
+    g = fminf(g, lim);
+    u = fminf(fmaxf(u, -lim), lim);
+    return (g / (1.0f + expf(-g))) * u;
+}
+
+// EXL3 "mcg" codebook decode of one 16-bit window (native/exl3/exl3_ref.py:37-47):
+// prod = w * 0xCBAC1FED mod 2^32; y = (prod & 0x8FFF8FFF) ^ 0x3B603B60;
+// value = fp16(lo(y)) + fp16(hi(y)) in fp16 arithmetic.
+__device__ __forceinline__ __half exl3_mcg(uint32_t w16) {
+    uint32_t prod = w16 * 0xCBAC1FEDu;
+    uint32_t y = (prod & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    __half lo = __ushort_as_half((unsigned short)(y & 0xFFFFu));
+    __half hi = __ushort_as_half((unsigned short)(y >> 16));
+    return __hadd(lo, hi);
+}
+
+// Q8_0 block: fp16 d at +0, int8 q[32] at +2 (34 bytes, 2-byte aligned).
+__device__ __forceinline__ float q8_scale(const uint8_t *blk) {
+    return __half2float(*reinterpret_cast<const __half *>(blk));
+}
+
+// ----------------------------------------------------------------------------- warp helpers
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t align_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+}  // namespace vfmoe

@@ -1,0 +1,171 @@
+// Token dispatch (permutation + gather) and weighted combine.
+//
+// Canonical order follows the reference host gather (native/glm53/glm_engine.vyb:2827-2845):
+// for each expert e ascending, the tokens t ascending with idx[t, l] == e.  The shared
+// expert is segment E and holds every token in order (glm_engine.vyb:2955-2989).
+//
+//   dispatch_kernel  one CTA per expert (+1 for the shared expert): offset = sum of lower
+//                    counts, then a block-wide ordered compaction of the tokens that chose e
+//                    (ballot + prefix), writing perm_tok[pos] and pos_of[t*k + l].
+//   gather_kernel    x_perm[pos] = fp16(x[perm_tok[pos]]): 16-byte vector copies.
+//   combine_kernel   out[t] = sum_l w[t,l] * y[pos_of[t,l]] + y[shared row of t]
+//                    (glm_engine.vyb:2925-2938, :2991), lanes summed in lane order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vfmoe {
+
+__global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict__ idx, const int32_t *__restrict__ counts,
+                                                       int T, int E, int k, int32_t *__restrict__ perm_tok,
+                                                       int32_t *__restrict__ pos_of, int32_t *__restrict__ offsets,
+                                                       int *__restrict__ err) {
+    __shared__ int red[8];
+    __shared__ int warp_tot[8];
+    const int e = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t tk = (int64_t)T * k;
+    if (e == E) {  // shared expert: identity segment after the routed rows
+        for (int t = tid; t < T; t += 256) perm_tok[tk + t] = t;
+        if (tid == 0) {
+            offsets[E] = (int32_t)tk;
+            offsets[E + 1] = (int32_t)(tk + T);
+        }
+        return;
+    }
+    int s = 0;
+    for (int i = tid; i < e; i += 256) s += counts[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    int off = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) off += red[w];
+    if (tid == 0) offsets[e] = off;
+    const int ne = counts[e];
+    if (ne == 0) return;
+    int running = 0;
+    for (int base = 0; base < T; base += 256) {
+        const int t = base + tid;
+        int hit_lane = -1;
+        if (t < T) {
+            for (int l = 0; l < k; ++l)
+                if (idx[(int64_t)t * k + l] == e) hit_lane = l;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hit_lane >= 0);
+        if (lane == 0) warp_tot[warp] = __popc(m);
+        __syncthreads();
+        int before = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const int c = warp_tot[w];
+            before += (w < warp) ? c : 0;
+            total += c;
+        }
+        if (hit_lane >= 0) {
+            const int pos = off + running + before + __popc(m & ((1u << lane) - 1u));
+            perm_tok[pos] = t;
+            pos_of[(int64_t)t * k + hit_lane] = pos;
+        }
+        running += total;
+        __syncthreads();
+    }
+    if (tid == 0 && running != ne) raise_dev_error(err, DEV_BAD_COUNT);
+}
+
+// One CTA (128 threads) per permuted row; H % 8 == 0.
+__global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x, int x_dtype,
+                                                     const int32_t *__restrict__ perm_tok, int H,
+                                                     __half *__restrict__ xp) {
+    const int64_t pos = blockIdx.x;
+    const int t = perm_tok[pos];
+    __half *dst = xp + pos * H;
+    if (x_dtype == VFMOE_DT_BF16) {
+        const __nv_bfloat16 *src = reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H;
+        for (int c = threadIdx.x * 8; c < H; c += 128 * 8) {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(src + c);
+            const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float a = __uint_as_float(in[i] << 16), b = __uint_as_float(in[i] & 0xFFFF0000u);
+                const __half2 h = __floats2half2_rn(a, b);
+                o[i] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+            *reinterpret_cast<uint4 *>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+        const float *src = reinterpret_cast<const float *>(x) + (int64_t)t * H;
+        for (int c = threadIdx.x * 8; c < H; c += 128 * 8) {
+            const float4 a = *reinterpret_cast<const float4 *>(src + c);
+            const float4 b = *reinterpret_cast<const float4 *>(src + c + 4);
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            *reinterpret_cast<uint4 *>(dst + c) =
+                make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                           *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+        }
+    }
+}
+
+// One CTA (256 threads) per token; H % 4 == 0.  `shared_rows` = 0 when there is no shared expert.
+__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
+                                                      const float *__restrict__ w, int T, int H, int k,
+                                                      int has_shared, void *__restrict__ out, int out_dtype) {
+    const int t = blockIdx.x;
+    const int64_t tk = (int64_t)T * k;
+    for (int c = threadIdx.x * 4; c < H; c += 256 * 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int l = 0; l < k; ++l) {
+            const int64_t p = pos_of[(int64_t)t * k + l];
+            const float wl = w[(int64_t)t * k + l];
+            const float4 v = *reinterpret_cast<const float4 *>(y + p * H + c);
+            acc.x = fmaf(wl, v.x, acc.x);
+            acc.y = fmaf(wl, v.y, acc.y);
+            acc.z = fmaf(wl, v.z, acc.z);
+            acc.w = fmaf(wl, v.w, acc.w);
+        }
+        if (has_shared) {
+            const float4 v = *reinterpret_cast<const float4 *>(y + (tk + t) * H + c);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int64_t o = (int64_t)t * H + c;
+        if (out_dtype == VFMOE_DT_BF16) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 pk;
+            pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+            pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + o) = pk;
+        } else {
+            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + o) = acc;
+        }
+    }
+}
+
+int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
+                    int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st) {
+    dispatch_kernel<<<E + 1, 256, 0, st>>>(idx, counts, T, E, k, perm_tok, pos_of, offsets, err);
+    VF_LAUNCH_CHECK("dispatch_kernel");
+    return VFMOE_OK;
+}
+
+int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
+                  cudaStream_t st) {
+    if (rows == 0) return VFMOE_OK;
+    gather_kernel<<<(unsigned)rows, 128, 0, st>>>(x, x_dtype, perm_tok, H, xp);
+    VF_LAUNCH_CHECK("gather_kernel");
+    return VFMOE_OK;
+}
+
+int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, int has_shared,
+                   void *out, int out_dtype, cudaStream_t st) {
+    if (T == 0) return VFMOE_OK;
+    combine_kernel<<<T, 256, 0, st>>>(y, pos_of, w, T, H, k, has_shared, out, out_dtype);
+    VF_LAUNCH_CHECK("combine_kernel");
+    return VFMOE_OK;
+}
+
+}  // namespace vfmoe

@@ -1,0 +1,57 @@
+// Internal launch interface between the C-ABI layer (api.cu) and the kernels.
+#pragma once
+
+#include <functional>
+
+#include "common.cuh"
+
+namespace vfmoe {
+
+struct MatrixRef {
+    const uint8_t *data;     // Q8_0 rows or EXL3 trellis of expert 0
+    int64_t expert_stride;   // bytes
+    const __half *suh;       // EXL3 only
+    int64_t suh_stride;      // bytes
+    const __half *svh;
+    int64_t svh_stride;
+};
+
+// Everything the expert kernels need for one forward (passed by value).
+struct MoeArgs {
+    int T, H, I, E, k;
+    int has_shared;
+    int fmt, exl3_bits;
+    float limit;
+    MatrixRef gate, up, down, sh_gate, sh_up, sh_down;
+    const int32_t *offsets;    // [E+2]: segment e = rows [offsets[e], offsets[e+1]); E = shared
+    const int32_t *perm_tok;   // [T*k + T]
+    const __half *xp;          // [T*k + T, H] gathered activations (fp16)
+    __half *act;               // [T*k + T, I] SwiGLU output (fp16)
+    float *y;                  // [T*k + T, H] expert outputs (fp32)
+    int *err;
+};
+
+int launch_router(const void *x, int x_dtype, const float *wr, const float *bias, int T, int H, int E,
+                  int k, double scale, double *part, int32_t *idx, float *w, int32_t *counts,
+                  cudaStream_t st);
+int64_t router_partial_doubles(int T, int H, int E);
+
+int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
+                    int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);
+int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
+                  cudaStream_t st);
+int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, int has_shared,
+                   void *out, int out_dtype, cudaStream_t st);
+
+// `mid` runs between the gate/up and the down launches (profiling marks).
+int launch_experts_simt(const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
+
+int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, float eps, int dtype,
+                   cudaStream_t st);
+int launch_q8_0_dequant(const uint8_t *src, void *dst, int64_t rows, int64_t k, int dst_dtype,
+                        cudaStream_t st);
+int launch_q8_0_quantize(const float *src, uint8_t *dst, int64_t rows, int64_t k, cudaStream_t st);
+int launch_exl3_decode(const uint16_t *trellis, __half *dst, int64_t K, int64_t N, int bits,
+                       cudaStream_t st);
+
+}  // namespace vfmoe

@@ -1,0 +1,148 @@
+// Weight-format kernels: Q8_0 quantize/dequantize, EXL3 trellis decode, RMSNorm.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vfmoe {
+
+// ----------------------------------------------------------------------------- Q8_0
+// One thread per output value.  dst_dtype F32: exact d*q; F16: fp16(d*q) (the value
+// the tensor-core kernels feed to the MMA).  native/kernels/q8_0.vyb:11-30.
+__global__ void q8_0_dequant_kernel(const uint8_t *__restrict__ src, void *__restrict__ dst, int64_t rows,
+                                    int64_t k, int dst_dtype) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= rows * k) return;
+    const int64_t r = i / k, c = i % k;
+    const uint8_t *blk = src + r * (k / 32) * 34 + (c / 32) * 34;
+    const float d = q8_scale(blk);
+    const float v = d * (float)(int8_t)blk[2 + (c % 32)];
+    if (dst_dtype == VFMOE_DT_F16)
+        reinterpret_cast<__half *>(dst)[i] = __float2half_rn(v);
+    else
+        reinterpret_cast<float *>(dst)[i] = v;
+}
+
+// One thread per 32-value block (ggml quantize_row_q8_0_ref): d = amax/127,
+// q = sign(v) * (floor|v| + floor(2(|v| - floor|v|))) with v = x * (1/d), all fp32.
+__global__ void q8_0_quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, int64_t nblk) {
+    const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const float *x = src + b * 32;
+    float v[32];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = reinterpret_cast<const float4 *>(x)[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float inv = d == 0.f ? 0.f : __fdiv_rn(1.0f, d);
+    uint8_t *o = dst + b * 34;
+    const __half dh = __float2half_rn(d);
+    const uint16_t dbits = __half_as_ushort(dh);
+    o[0] = (uint8_t)(dbits & 0xFF);
+    o[1] = (uint8_t)(dbits >> 8);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float s = __fmul_rn(v[i], inv);
+        const float a = fabsf(s);
+        const float fl = floorf(a);
+        float q = __fadd_rn(fl, floorf(__fmul_rn(2.0f, __fsub_rn(a, fl))));
+        q = s < 0.f ? -q : (s > 0.f ? q : 0.f);
+        o[2 + i] = (uint8_t)(int8_t)(int)q;
+    }
+}
+
+// ----------------------------------------------------------------------------- EXL3
+// 3 bpw layout (defined by this library; the reference has only 4 bpw): a 16x16 tile is
+// 48 uint16 words = a 768-bit circular stream, LSB-first.  Window j = bits [3j, 3j+16)
+// (mod 768) decodes the weight at tile row r = j % 16, column c = j / 16, so column c's
+// 16 rows are the consecutive windows 16c..16c+15 = bits [48c, 48c+61).
+__device__ __forceinline__ uint64_t exl3_col_bits_3bpw(const uint16_t *tile, int c) {
+    const int w0 = 3 * c;  // 48c / 16
+    uint64_t v = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v |= (uint64_t)tile[(w0 + i) % 48] << (16 * i);
+    return v;
+}
+
+// One thread per (tile, column): writes the 16 values of W^[16kb + r][16nb + c].
+__global__ void exl3_decode_kernel(const uint16_t *__restrict__ trellis, __half *__restrict__ dst, int64_t K,
+                                   int64_t N, int bits) {
+    const int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t nbk = N / 16;
+    const int64_t ntiles = (K / 16) * nbk;
+    if (g >= ntiles * 16) return;
+    const int c = (int)(g & 15);
+    const int64_t tile = g >> 4;
+    const int64_t kb = tile / nbk, nb = tile % nbk;
+    const uint16_t *tp = trellis + tile * (16 * bits);
+    if (bits == 3) {
+        const uint64_t v = exl3_col_bits_3bpw(tp, c);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const uint32_t w16 = (uint32_t)(v >> (3 * r)) & 0xFFFFu;
+            dst[(kb * 16 + r) * N + nb * 16 + c] = exl3_mcg(w16);
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------- RMSNorm
+// One CTA (256 threads) per row: fp32 sum of squares, y = x * rsqrt(mean + eps) * w
+// (native/kernels/rmsnorm.vyb; reference recomputes the row stat per element).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x, const float *__restrict__ w,
+                                                      void *__restrict__ y, int D, float eps, int dtype) {
+    __shared__ float red[8];
+    const int64_t row = blockIdx.x;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < D; c += 256) {
+        const float v = ld_act(x, row * D + c, dtype);
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum_f32(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float r = rsqrtf(tot / (float)D + eps);
+    for (int c = threadIdx.x; c < D; c += 256) {
+        const float v = ld_act(x, row * D + c, dtype);
+        st_act(y, row * D + c, v * r * w[c], dtype);
+    }
+}
+
+int launch_q8_0_dequant(const uint8_t *src, void *dst, int64_t rows, int64_t k, int dst_dtype, cudaStream_t st) {
+    const int64_t n = rows * k;
+    if (n == 0) return VFMOE_OK;
+    q8_0_dequant_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(src, dst, rows, k, dst_dtype);
+    VF_LAUNCH_CHECK("q8_0_dequant_kernel");
+    return VFMOE_OK;
+}
+
+int launch_q8_0_quantize(const float *src, uint8_t *dst, int64_t rows, int64_t k, cudaStream_t st) {
+    const int64_t nblk = rows * (k / 32);
+    if (nblk == 0) return VFMOE_OK;
+    q8_0_quantize_kernel<<<(unsigned)cdiv(nblk, 128), 128, 0, st>>>(src, dst, nblk);
+    VF_LAUNCH_CHECK("q8_0_quantize_kernel");
+    return VFMOE_OK;
+}
+
+int launch_exl3_decode(const uint16_t *trellis, __half *dst, int64_t K, int64_t N, int bits, cudaStream_t st) {
+    const int64_t n = (K / 16) * (N / 16) * 16;
+    if (n == 0) return VFMOE_OK;
+    exl3_decode_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(trellis, dst, K, N, bits);
+    VF_LAUNCH_CHECK("exl3_decode_kernel");
+    return VFMOE_OK;
+}
+
+int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, float eps, int dtype,
+                   cudaStream_t st) {
+    if (S == 0) return VFMOE_OK;
+    rmsnorm_kernel<<<(unsigned)S, 256, 0, st>>>(x, w, y, D, eps, dtype);
+    VF_LAUNCH_CHECK("rmsnorm_kernel");
+    return VFMOE_OK;
+}
+
+}  // namespace vfmoe

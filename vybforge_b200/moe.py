@@ -1,0 +1,174 @@
+"""Host-side mirror of the reference MoE interface over libvfmoe.so.
+
+The reference's operator surface for this path is the numpy gate
+(native/glm53/moe_ref.py: ``route``, ``ffn``, ``moe_block``) and the three PTX
+kernels of native/kernels/moe.vyb (``moe_route``, ``moe_act``, ``moe_down``)
+driven by native/host/moe_driver.vyb.  ``MoELayer`` keeps those names and
+argument meanings:
+
+* ``MoELayer.route(x)``    -> (idx int32 [T,k], w fp32 [T,k])   (moe_ref.route)
+* ``MoELayer.moe_block(x)`` -> (out [T,H], idx, w)               (moe_ref.moe_block)
+
+Device memory and streams come from torch; every computation is a libvfmoe
+kernel reached through the C ABI.  A missing library raises on import.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import check, DT_BF16, DT_F16, DT_F32, WFMT_Q8_0, WFMT_EXL3
+
+_DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream() -> int:
+    return int(torch.cuda.current_stream().cuda_stream)
+
+
+def init(device: int = 0) -> None:
+    check(_lib.load().vfmoe_init(device))
+
+
+class MoELayer:
+    """One GLM-style MoE layer (router + routed experts + shared expert) on one GPU.
+
+    Q8_0 weights: ``gate``/``up`` uint8 [E, I, H/32*34], ``down`` uint8 [E, H, I/32*34]
+    (GGUF block rows = output channels); ``shared`` = (gate [I, ...], up, down) or None.
+    EXL3 weights: each projection is a tuple (trellis int16 [E, K/16, N/16, 16*bits],
+    suh fp16 [E, K], svh fp16 [E, N]); shared likewise without the leading E.
+    """
+
+    def __init__(self, *, hidden, inter, n_experts, topk, router_w, router_bias, gate, up, down,
+                 shared=None, fmt="q8_0", exl3_bits=3, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
+                 scale=2.5, limit=10.0):
+        self.lib = _lib.load()
+        self.H, self.I, self.E, self.k = hidden, inter, n_experts, topk
+        self.x_dtype, self.out_dtype = x_dtype, out_dtype
+        self.fmt = fmt
+        d = _lib.LayerDesc()
+        d.hidden, d.inter, d.n_experts, d.topk = hidden, inter, n_experts, topk
+        d.weight_format = WFMT_Q8_0 if fmt == "q8_0" else WFMT_EXL3
+        d.exl3_bits = exl3_bits
+        d.x_dtype, d.out_dtype = _DT[x_dtype], _DT[out_dtype]
+        d.routed_scale, d.swiglu_limit = scale, limit
+        d.router_w, d.router_bias = _ptr(router_w), _ptr(router_bias)
+        self._keep = [router_w, router_bias, gate, up, down, shared]
+
+        def fill(m, w, stacked):
+            if fmt == "q8_0":
+                m.data = _ptr(w)
+                m.expert_stride = w[0].numel() * w.element_size() if stacked else 0
+            else:
+                tr, suh, svh = w
+                m.data, m.suh, m.svh = _ptr(tr), _ptr(suh), _ptr(svh)
+                if stacked:
+                    m.expert_stride = tr[0].numel() * tr.element_size()
+                    m.suh_stride = suh[0].numel() * suh.element_size()
+                    m.svh_stride = svh[0].numel() * svh.element_size()
+
+        fill(d.gate, gate, True)
+        fill(d.up, up, True)
+        fill(d.down, down, True)
+        if shared is not None:
+            fill(d.sh_gate, shared[0], False)
+            fill(d.sh_up, shared[1], False)
+            fill(d.sh_down, shared[2], False)
+        self.desc = d
+        self.handle = check(self.lib.vfmoe_layer_create(C.byref(d)))
+        self._ws = None
+
+    # ------------------------------------------------------------------ workspace
+    def workspace_bytes(self, T: int) -> int:
+        return check(self.lib.vfmoe_workspace_bytes(self.handle, T))
+
+    def workspace(self, T: int) -> torch.Tensor:
+        need = self.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        return self._ws
+
+    # ------------------------------------------------------------------ ops
+    def route(self, x: torch.Tensor):
+        T = x.shape[0]
+        idx = torch.empty((T, self.k), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, self.k), dtype=torch.float32, device=x.device)
+        ws = self.workspace(T)
+        check(self.lib.vfmoe_route(self.handle, _ptr(x), T, _ptr(idx), _ptr(w), _ptr(ws), ws.numel(), _stream()))
+        return idx, w
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, idx=None, w=None,
+                workspace: torch.Tensor | None = None):
+        assert x.dtype == self.x_dtype and x.is_contiguous() and x.shape[1] == self.H
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, self.H), dtype=self.out_dtype, device=x.device)
+        ws = workspace if workspace is not None else self.workspace(T)
+        check(self.lib.vfmoe_forward(self.handle, _ptr(x), T, _ptr(out), _ptr(idx), _ptr(w), _ptr(ws),
+                                     ws.numel(), _stream()))
+        return out
+
+    def moe_block(self, x: torch.Tensor):
+        """(out, idx, w) like native/glm53/moe_ref.py:92-112."""
+        T = x.shape[0]
+        idx = torch.empty((T, self.k), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, self.k), dtype=torch.float32, device=x.device)
+        out = self.forward(x, idx=idx, w=w)
+        return out, idx, w
+
+    def check_device_error(self):
+        check(self.lib.vfmoe_check_device_error(self.handle, _stream()))
+
+    def close(self):
+        if getattr(self, "handle", 0) > 0:
+            self.lib.vfmoe_layer_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------- standalone ops
+def q8_0_quantize(src_f32: torch.Tensor, dst_u8: torch.Tensor) -> None:
+    rows, k = src_f32.shape
+    check(_lib.load().vfmoe_q8_0_quantize(_ptr(src_f32), _ptr(dst_u8), rows, k, _stream()))
+
+
+def q8_0_dequant(src_u8: torch.Tensor, rows: int, k: int, dtype=torch.float32) -> torch.Tensor:
+    out = torch.empty((rows, k), dtype=dtype, device=src_u8.device)
+    check(_lib.load().vfmoe_q8_0_dequant(_ptr(src_u8), _ptr(out), rows, k, _DT[dtype], _stream()))
+    return out
+
+
+def exl3_decode(trellis: torch.Tensor, K: int, N: int, bits: int) -> torch.Tensor:
+    out = torch.empty((K, N), dtype=torch.float16, device=trellis.device)
+    check(_lib.load().vfmoe_exl3_decode(_ptr(trellis), _ptr(out), K, N, bits, _stream()))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    y = torch.empty_like(x)
+    S, D = x.shape
+    check(_lib.load().vfmoe_rmsnorm(_ptr(x), _ptr(w), _ptr(y), S, D, eps, _DT[x.dtype], _stream()))
+    return y
+
+
+class _Quantizer:
+    """Adapter used by synth.expert_q8_cuda."""
+
+    @staticmethod
+    def q8_0_quantize(src, dst):
+        q8_0_quantize(src, dst.view(src.shape[0], -1))
+
+
+quantizer = _Quantizer()
