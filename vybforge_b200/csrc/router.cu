@@ -143,7 +143,8 @@ __global__ void __launch_bounds__(256) router_topk(const double *__restrict__ pa
             for (int s = 0; s < nks; ++s) logit += part[((int64_t)s * T + t) * E + e];
             const double sc = 1.0 / (1.0 + exp(-logit));
             score[j] = sc;
-            choice[j] = sc + (double)bias[e];
+            const double c = sc + (double)bias[e];
+            choice[j] = isnan(c) ? -INFINITY : c;  // NaN never wins; keeps the argmax total
         } else {
             score[j] = 0.0;
             choice[j] = -INFINITY;
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(256) router_topk(const double *__restrict__ pa
         const double wv = my_s / (sum + 1e-20) * scale;
         idx_out[(int64_t)t * k + lane] = my_e;
         w_out[(int64_t)t * k + lane] = (float)wv;
-        atomicAdd(&counts[my_e], 1);
+        if (my_e >= 0 && my_e < E) atomicAdd(&counts[my_e], 1);
     }
 }
 
