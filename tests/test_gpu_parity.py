@@ -170,3 +170,24 @@ def test_rmsnorm(dtype):
     ref = orc.rmsnorm(xd.float().cpu().numpy(), w, 1e-5)
     tol = 1e-5 if dtype == torch.float32 else 8e-3
     assert rel_l2(y, ref) < tol
+
+
+# ----------------------------------------------------------------------------- tcgen05 path vs SIMT path
+def _simt_layer(built, out_dtype=torch.float32):
+    os.environ["VFMOE_DISABLE_TC"] = "1"
+    try:
+        return built.make_layer(out_dtype)
+    finally:
+        del os.environ["VFMOE_DISABLE_TC"]
+
+
+@pytest.mark.parametrize("cfg_name,T", [("c0", 16), ("c1", 1), ("c1", 32)])
+def test_tensor_core_path_matches_simt_path(c0, c1, cfg_name, T):
+    b = c0 if cfg_name == "c0" else c1
+    x = b.x_dev[:T].contiguous()
+    tc = b.layer.forward(x).cpu().numpy()
+    simt = _simt_layer(b).forward(x).cpu().numpy()
+    torch.cuda.synchronize()
+    b.layer.check_device_error()
+    assert rel_l2(tc, simt) < 1e-4, rel_l2(tc, simt)
+    assert np.abs(tc - simt).max() < 2e-3

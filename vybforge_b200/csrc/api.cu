@@ -85,7 +85,7 @@ static Layer *get_layer(int64_t h) {
 
 // ----------------------------------------------------------------------------- workspace
 struct WsLayout {
-    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, total;
+    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, tiles, tile_counts, tiles_cap, total;
 };
 
 static WsLayout ws_layout(const Layer &L, int64_t T) {
@@ -107,6 +107,9 @@ static WsLayout ws_layout(const Layer &L, int64_t T) {
     o.xp = take(rows * L.H * 2);
     o.act = take(rows * L.I * 2);
     o.y = take(rows * L.H * 4);
+    o.tiles_cap = tc_tiles_capacity((int)T, L.k, L.E);
+    o.tiles = take(2 * o.tiles_cap * 16);
+    o.tile_counts = take(2 * 4);
     o.total = p;
     return o;
 }
@@ -381,6 +384,9 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.act = reinterpret_cast<__half *>(base + lay.act);
     a.y = reinterpret_cast<float *>(base + lay.y);
     a.err = L->dev_err;
+    a.tiles = reinterpret_cast<int4 *>(base + lay.tiles);
+    a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
+    a.tiles_cap = lay.tiles_cap;
 
     rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, perm_tok, pos_of, offsets, L->dev_err, st);
     if (rc) return rc;
@@ -392,6 +398,7 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     mark();
     if (L->use_tc && tc_supported(L->tc, a)) {
         rc = launch_experts_tc(L->tc, a, st, [&]() { mark(); });
+        nlaunch += 1;
     } else {
         rc = launch_experts_simt(a, st, [&]() { mark(); });
     }

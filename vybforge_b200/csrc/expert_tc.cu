@@ -1,18 +1,541 @@
-// Tensor-core (tcgen05) grouped expert GEMMs.
+// Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05), Q8_0 weights.
+//
+// One persistent kernel serves the decode and the prefill shapes (N = tokens per tile):
+//   gate/up:  act[rows, ch] = fp16(swiglu(x . Wg[ch], x . Wu[ch]))  (moe.vyb:98-134)
+//   down:     y[rows, ch]   = act . Wd[ch]                          (moe.vyb:137-170)
+//
+// Operand placement (per CTA tile of 128 output channels x N token rows):
+//   A = weights, M = 128 channels, dequantized Q8_0 -> fp16 by 8 "dequant" warps and
+//       written straight into TMEM with tcgen05.st (no shared-memory round trip);
+//   B = token rows (fp16), N x 64 per sub-stage, TMA SWIZZLE_128B tiles in shared memory;
+//   D = fp32 accumulators in TMEM (gate and up side by side for the fused SwiGLU).
+// Raw Q8_0 bytes stream in by TMA as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage.
+//
+// Warp roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// warp 2 TMEM allocator, warps 4..11 dequant + epilogue (warp w owns TMEM lanes
+// 32*(w%4)..+31; warps 4-7 and 8-11 form two sets).
+// Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT,
+// drains what it issued and returns.
+//
+// Work list: the (expert, token-tile) list built on the device by tc_plan_kernel, times
+// the M/128 channel tiles, strided over a grid of one CTA per SM.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdlib>
+
 #include "expert_tc.h"
+#include "sm100.cuh"
 
 namespace vfmoe {
 
-int tc_plan_create(const vfmoe_layer_desc &, TcPlan &plan) {
-    plan.ready = 0;
+using namespace sm100;
+
+constexpr int kThreads = 384;
+constexpr int kRawRow = 272;            // 8 Q8_0 blocks = 256 K values
+constexpr int kRawMat = 128 * kRawRow;  // one matrix, one stage
+constexpr int kSA = 4;                  // TMEM A ring slots (K = 64 each)
+
+template <bool GATEUP, int N>
+struct TcCfg {
+    static constexpr int MATS = GATEUP ? 2 : 1;
+    static constexpr int SW = GATEUP ? (N <= 32 ? 3 : 2) : (N <= 32 ? 5 : (N == 64 ? 4 : (N == 128 ? 3 : 2)));
+    static constexpr int SB = 4;
+    static constexpr int RAW_BYTES = SW * MATS * kRawMat;
+    static constexpr int TOK_STAGE = N * 128;
+    static constexpr int TOK_BYTES = SB * TOK_STAGE;
+    static constexpr int BAR_OFF = RAW_BYTES + TOK_BYTES;
+    static constexpr int NBAR = 2 * SW + 2 * kSA + 2 * SB + 3;
+    static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;  // + alignment slack
+    static constexpr int D_COLS = MATS * N;
+    static constexpr int A_COL0 = D_COLS;
+    static_assert(D_COLS + kSA * MATS * 32 <= 512, "TMEM budget");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+struct TcParams {
+    CUtensorMap wa, wb, swa, swb;   // weights: routed A/B matrices, shared A/B (3D u16 maps)
+    CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B
+    const int4 *tiles;              // {expert, row0, nrows, 0}
+    const int32_t *n_tiles;
+    int E, K, M;
+    int ld_out;
+    void *out;
+    float limit;
+    int *err;
+};
+
+// ----------------------------------------------------------------------------- dequant
+// 68 bytes = two Q8_0 blocks (K = 64) of one weight row -> 32 packed fp16 pairs
+// (column c holds k = 2c in the low half, 2c + 1 in the high half), value fp16(d * q).
+// g[0..16] are the 17 little-endian words of the two blocks.
+__device__ __forceinline__ uint32_t q8_pair(uint32_t word, uint32_t sel, __half2 d2) {
+    const uint32_t h = __byte_perm(word, 0x64646464u, sel);  // {0x64, q_hi, 0x64, q_lo}: 1024 + (q ^ 0x80)
+    __half2 v = *reinterpret_cast<const __half2 *>(&h);
+    v = __hsub2(v, __half2half2(__ushort_as_half(0x6480)));  // - 1152 -> exact q
+    v = __hmul2(v, d2);                                      // one rounding: fp16(d * q)
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void q8_two_blocks(const uint32_t (&g)[17], uint32_t (&v)[32]) {
+    const __half2 d0 = __half2half2(__ushort_as_half((unsigned short)(g[0] & 0xFFFFu)));
+    const __half2 d1 = __half2half2(__ushort_as_half((unsigned short)(g[8] >> 16)));
+    uint32_t x[17];
+    x[0] = g[0] ^ 0x80800000u;
+#pragma unroll
+    for (int i = 1; i < 8; ++i) x[i] = g[i] ^ 0x80808080u;
+    x[8] = g[8] ^ 0x00008080u;
+#pragma unroll
+    for (int i = 9; i < 17; ++i) x[i] = g[i] ^ 0x80808080u;
+    // block 0: pair c = bytes 2+2c, 3+2c of the group
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const int b = 2 + 2 * c;
+        v[c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d0);
+    }
+    // block 1: pair c = bytes 36+2c, 37+2c
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const int b = 36 + 2 * c;
+        v[16 + c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d1);
+    }
+}
+
+// ----------------------------------------------------------------------------- plan
+// Token tiles of N rows for every expert segment (routed experts ascending, then shared).
+__global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict__ offsets, int E, int has_shared,
+                                                       int n_gu, int n_dn, int4 *__restrict__ tiles, int64_t cap,
+                                                       int32_t *__restrict__ counts) {
+    __shared__ int sc[2][1024];
+    const int tid = threadIdx.x;
+    const int nexp = E + (has_shared ? 1 : 0);
+    for (int which = 0; which < 2; ++which) {
+        const int N = which == 0 ? n_gu : n_dn;
+        int4 *out = tiles + which * cap;
+        // each thread owns experts [tid*per, (tid+1)*per)
+        const int per = (nexp + 1023) / 1024;
+        int mine = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = tid * per + i;
+            if (e < nexp) {
+                const int n = offsets[e + 1] - offsets[e];
+                mine += (n + N - 1) / N;
+            }
+        }
+        sc[which][tid] = mine;
+        __syncthreads();
+        for (int o = 1; o < 1024; o <<= 1) {
+            const int v = tid >= o ? sc[which][tid - o] : 0;
+            __syncthreads();
+            sc[which][tid] += v;
+            __syncthreads();
+        }
+        int pos = sc[which][tid] - mine;
+        for (int i = 0; i < per; ++i) {
+            const int e = tid * per + i;
+            if (e < nexp) {
+                const int r0 = offsets[e], n = offsets[e + 1] - r0;
+                for (int j = 0; j * N < n; ++j) {
+                    if (pos < cap) out[pos] = make_int4(e, r0 + j * N, min(N, n - j * N), 0);
+                    ++pos;
+                }
+            }
+        }
+        if (tid == 1023) counts[which] = (int32_t)(sc[which][1023] < cap ? sc[which][1023] : cap);
+        __syncthreads();
+    }
+}
+
+// ----------------------------------------------------------------------------- GEMM
+template <bool GATEUP, int N>
+__global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_constant__ TcParams p) {
+    using C = TcCfg<GATEUP, N>;
+    constexpr int MATS = C::MATS, SW = C::SW, SB = C::SB;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *raw = smem;
+    uint8_t *tok = smem + C::RAW_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *raw_full = bars, *raw_empty = bars + SW;
+    uint64_t *a_full = bars + 2 * SW, *a_empty = a_full + kSA;
+    uint64_t *b_full = a_empty + kSA, *b_empty = b_full + SB;
+    uint64_t *d_full = b_empty + SB, *d_empty = d_full + 1, *mma_done = d_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBAR);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int MT = p.M / 128;
+    const int KR = p.K / 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SW; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], 8);
+        }
+        for (int i = 0; i < kSA; ++i) {
+            mbar_init(&a_full[i], GATEUP ? 8 : 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < SB; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        mbar_init(d_full, 1);
+        mbar_init(d_empty, 8);
+        mbar_init(mma_done, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.wa);
+        prefetch_tmap(&p.swa);
+        prefetch_tmap(&p.xt);
+        if (GATEUP) {
+            prefetch_tmap(&p.wb);
+            prefetch_tmap(&p.swb);
+        }
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_items = (*p.n_tiles) * MT;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t nraw = 0, ntok = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int4 t = p.tiles[item / MT];
+                const int m0 = (item % MT) * 128;
+                const bool sh = t.x == p.E;
+                const CUtensorMap *ma = sh ? &p.swa : &p.wa;
+                const CUtensorMap *mb = sh ? &p.swb : &p.wb;
+                const int z = sh ? 0 : t.x;
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    const uint32_t rs = nraw % SW;
+                    if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
+                    mbar_arrive_expect_tx(&raw_full[rs], MATS * kRawMat);
+                    uint8_t *dst = raw + rs * (MATS * kRawMat);
+                    tma_load_3d(dst, ma, &raw_full[rs], kr * (kRawRow / 2), m0, z);
+                    if (GATEUP) tma_load_3d(dst + kRawMat, mb, &raw_full[rs], kr * (kRawRow / 2), m0, z);
+                    ++nraw;
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t bs = ntok % SB;
+                        if (!(ok = mbar_wait(&b_empty[bs], ((ntok / SB) & 1) ^ 1, abort))) break;
+                        mbar_arrive_expect_tx(&b_full[bs], C::TOK_STAGE);
+                        tma_load_2d(tok + bs * C::TOK_STAGE, &p.xt, &b_full[bs], kr * 256 + 64 * s, t.y);
+                        ++ntok;
+                    }
+                }
+            }
+            if (!ok) {
+                // drain copies still in flight before the CTA exits (bounded)
+                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+                int dummy = 0;
+                for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
+                    mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
+                for (uint32_t i = (ntok > (uint32_t)SB ? ntok - SB : 0); i < ntok; ++i)
+                    mbar_wait(&b_full[i % SB], (i / SB) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(128, N);
+            uint32_t na = 0, ntok = 0, it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+                if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
+                tc_fence_after();
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t as = na % kSA, bs = ntok % SB;
+                        if (!(ok = mbar_wait(&a_full[as], (na / kSA) & 1, abort))) break;
+                        if (!(ok = mbar_wait(&b_full[bs], (ntok / SB) & 1, abort))) break;
+                        tc_fence_after();
+                        const uint32_t bsm = smem_u32(tok + bs * C::TOK_STAGE);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const uint32_t a_t = tmem + C::A_COL0 + (as * MATS + m) * 32 + 8 * j;
+                                const uint64_t b_d = smem_desc_sw128(bsm + 32 * j);
+                                mma_f16_ts(tmem + m * N, a_t, b_d, idesc, (kr | s | j) != 0);
+                            }
+                        }
+                        mma_commit(&a_empty[as]);
+                        mma_commit(&b_empty[bs]);
+                        ++na;
+                        ++ntok;
+                    }
+                }
+                if (ok) mma_commit(d_full);
+            }
+            // all issued MMAs complete before TMEM is released
+            mma_commit(mma_done);
+            int dummy = 0;
+            mbar_wait(mma_done, 0, (volatile int *)&dummy, 200000000ull);
+            if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------------ dequant + epilogue
+        const int q = warp & 3;            // TMEM lane quarter
+        const int set = (warp - 4) >> 2;   // 0: warps 4-7, 1: warps 8-11
+        const int r = 32 * q + lane;       // weight row within the tile = TMEM lane
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t nraw = 0, na = 0, it = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+            for (int kr = 0; kr < KR && ok; ++kr) {
+                const uint32_t rs = nraw % SW;
+                if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
+                const int mat = GATEUP ? set : 0;
+                const uint8_t *row = raw + rs * (MATS * kRawMat) + mat * kRawMat + r * kRawRow;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const bool mine = GATEUP || ((s & 1) == set);
+                    if (mine) {
+                        const uint32_t as = na % kSA;
+                        if (!(ok = mbar_wait(&a_empty[as], ((na / kSA) & 1) ^ 1, abort))) break;
+                        uint32_t w[20];
+#pragma unroll
+                        for (int c = 0; c < 5; ++c) {
+                            const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 64 * s + 16 * c);
+                            w[4 * c] = v4.x;
+                            w[4 * c + 1] = v4.y;
+                            w[4 * c + 2] = v4.z;
+                            w[4 * c + 3] = v4.w;
+                        }
+                        uint32_t g[17];
+#pragma unroll
+                        for (int j = 0; j < 17; ++j) g[j] = w[s + j];
+                        uint32_t v[32];
+                        q8_two_blocks(g, v);
+                        tmem_st_32x32b_x32(tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32, v);
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[as]);
+                    }
+                    ++na;
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                ++nraw;
+            }
+            if (!ok) break;
+            // epilogue
+            if (!(ok = mbar_wait(d_full, it & 1, abort))) break;
+            tc_fence_after();
+            const int item_tile = item / MT;
+            const int4 t = p.tiles[item_tile];
+            const int ch = (item % MT) * 128 + r;
+            constexpr int HALF = N / 2;
+            const int c_beg = set * HALF;
+#pragma unroll 1
+            for (int c0 = c_beg; c0 < c_beg + HALF; c0 += 8) {
+                if (c0 >= t.z) break;
+                uint32_t dg[8];
+                tmem_ld_32x32b_x8(tmem + lane_base + c0, dg);
+                if (GATEUP) {
+                    uint32_t du[8];
+                    tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du);
+                    tmem_wait_ld();
+                    __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (c0 + j < t.z) {
+                            const float a = swiglu_clamped(__uint_as_float(dg[j]), __uint_as_float(du[j]), p.limit);
+                            out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(a);
+                        }
+                    }
+                } else {
+                    tmem_wait_ld();
+                    float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __uint_as_float(dg[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty);
+        }
+        if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
+// ----------------------------------------------------------------------------- host
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// Q8_0 matrix stack [experts][rows][row_bytes] as u16 elements; box = 128 rows x 272 B.
+static int make_q8_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k, int64_t experts,
+                       int64_t expert_stride) {
+    auto enc = get_encode();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return VFMOE_ERR_CUDA;
+    }
+    const int64_t row_bytes = k / 32 * 34;
+    if (experts <= 1) expert_stride = rows * row_bytes;
+    cuuint64_t dims[3] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)rows, (cuuint64_t)experts};
+    cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)expert_stride};
+    cuuint32_t box[3] = {kRawRow / 2, 128, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (Q8_0 weights) failed: %d", (int)r);
+        return VFMOE_ERR_CUDA;
+    }
     return VFMOE_OK;
 }
 
-bool tc_supported(const TcPlan &plan, const MoeArgs &) { return plan.ready != 0; }
+// fp16 token rows [rows][k]; box = N rows x 64 halves (128 B), SWIZZLE_128B.
+static int make_tok_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k, int n) {
+    auto enc = get_encode();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return VFMOE_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)n};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (token rows) failed: %d", (int)r);
+        return VFMOE_ERR_CUDA;
+    }
+    return VFMOE_OK;
+}
 
-int launch_experts_tc(const TcPlan &, const MoeArgs &, cudaStream_t, const std::function<void()> &) {
-    set_error("tensor-core expert path not built");
-    return VFMOE_ERR_UNSUPPORTED;
+int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
+    plan.ready = 0;
+    if (d.weight_format != VFMOE_WFMT_Q8_0) return VFMOE_OK;
+    if (getenv("VFMOE_DISABLE_TC")) return VFMOE_OK;
+    int dev = 0;
+    VF_CUDA(cudaGetDevice(&dev));
+    VF_CUDA(cudaDeviceGetAttribute(&plan.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t H = d.hidden, I = d.inter, E = d.n_experts;
+    int rc;
+    if ((rc = make_q8_map(&plan.gate, (void *)d.gate.data, I, H, E, d.gate.expert_stride))) return rc;
+    if ((rc = make_q8_map(&plan.up, (void *)d.up.data, I, H, E, d.up.expert_stride))) return rc;
+    if ((rc = make_q8_map(&plan.down, (void *)d.down.data, H, I, E, d.down.expert_stride))) return rc;
+    const bool sh = d.sh_gate.data != 0;
+    if ((rc = make_q8_map(&plan.sh_gate, (void *)(sh ? d.sh_gate.data : d.gate.data), I, H, 1, 0))) return rc;
+    if ((rc = make_q8_map(&plan.sh_up, (void *)(sh ? d.sh_up.data : d.up.data), I, H, 1, 0))) return rc;
+    if ((rc = make_q8_map(&plan.sh_down, (void *)(sh ? d.sh_down.data : d.down.data), H, I, 1, 0))) return rc;
+    plan.ready = 1;
+    return VFMOE_OK;
+}
+
+bool tc_supported(const TcPlan &plan, const MoeArgs &a) {
+    return plan.ready && a.fmt == VFMOE_WFMT_Q8_0 && a.tiles != nullptr && a.H % 256 == 0 && a.I % 256 == 0;
+}
+
+int64_t tc_tiles_capacity(int T, int k, int E) { return ((int64_t)T * k + T) / 16 + E + 2; }
+
+static int pick_n(int T, int k, int E) {
+    const double avg = (double)T * k / E;
+    const int want = (int)std::max(2.0 * avg, (double)std::min(T, 32));
+    int n = 16;
+    while (n < want && n < 256) n <<= 1;
+    return n;
+}
+
+template <bool GATEUP, int N>
+static int launch_one(const TcParams &prm, int grid, cudaStream_t st) {
+    using C = TcCfg<GATEUP, N>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        VF_CUDA(cudaFuncSetAttribute(expert_gemm_tc<GATEUP, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done = true;
+    }
+    expert_gemm_tc<GATEUP, N><<<grid, kThreads, C::SMEM, st>>>(prm);
+    VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_tc<gate_up>" : "expert_gemm_tc<down>");
+    return VFMOE_OK;
+}
+
+int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
+    const int n = pick_n(a.T, a.k, a.E);
+    const int n_gu = std::min(n, 128);
+    const int n_dn = n;
+    const int64_t rows = (int64_t)a.T * a.k + a.T;
+    tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap,
+                                       a.tile_counts);
+    VF_LAUNCH_CHECK("tc_plan_kernel");
+    int rc;
+    TcParams g{};
+    g.wa = plan.gate;
+    g.wb = plan.up;
+    g.swa = plan.sh_gate;
+    g.swb = plan.sh_up;
+    if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, n_gu))) return rc;
+    g.tiles = a.tiles;
+    g.n_tiles = a.tile_counts;
+    g.E = a.E;
+    g.K = a.H;
+    g.M = a.I;
+    g.ld_out = a.I;
+    g.out = a.act;
+    g.limit = a.limit;
+    g.err = a.err;
+    const int grid = plan.num_sms;
+    switch (n_gu) {
+        case 16: rc = launch_one<true, 16>(g, grid, st); break;
+        case 32: rc = launch_one<true, 32>(g, grid, st); break;
+        case 64: rc = launch_one<true, 64>(g, grid, st); break;
+        default: rc = launch_one<true, 128>(g, grid, st); break;
+    }
+    if (rc) return rc;
+    mid();
+    TcParams dn{};
+    dn.wa = plan.down;
+    dn.wb = plan.down;
+    dn.swa = plan.sh_down;
+    dn.swb = plan.sh_down;
+    if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, n_dn))) return rc;
+    dn.tiles = a.tiles + a.tiles_cap;
+    dn.n_tiles = a.tile_counts + 1;
+    dn.E = a.E;
+    dn.K = a.I;
+    dn.M = a.H;
+    dn.ld_out = a.H;
+    dn.out = a.y;
+    dn.limit = a.limit;
+    dn.err = a.err;
+    switch (n_dn) {
+        case 16: return launch_one<false, 16>(dn, grid, st);
+        case 32: return launch_one<false, 32>(dn, grid, st);
+        case 64: return launch_one<false, 64>(dn, grid, st);
+        case 128: return launch_one<false, 128>(dn, grid, st);
+        default: return launch_one<false, 256>(dn, grid, st);
+    }
 }
 
 }  // namespace vfmoe

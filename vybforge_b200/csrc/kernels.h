@@ -29,6 +29,9 @@ struct MoeArgs {
     __half *act;               // [T*k + T, I] SwiGLU output (fp16)
     float *y;                  // [T*k + T, H] expert outputs (fp32)
     int *err;
+    int4 *tiles;               // tensor-core path: two tile lists of tiles_cap entries each
+    int32_t *tile_counts;      // [2]
+    int64_t tiles_cap;
 };
 
 int launch_router(const void *x, int x_dtype, const float *wr, const float *bias, int T, int H, int E,

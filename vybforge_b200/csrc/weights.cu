@@ -38,19 +38,23 @@ __global__ void q8_0_quantize_kernel(const float *__restrict__ src, uint8_t *__r
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float inv = d == 0.f ? 0.f : __fdiv_rn(1.0f, d);
-    uint8_t *o = dst + b * 34;
-    const __half dh = __float2half_rn(d);
-    const uint16_t dbits = __half_as_ushort(dh);
-    o[0] = (uint8_t)(dbits & 0xFF);
-    o[1] = (uint8_t)(dbits >> 8);
+    // The 34-byte block is 2-byte aligned: write it as 17 little-endian 16-bit words
+    // (word 0 = fp16 d, word 1+j = q[2j] | q[2j+1] << 8).
+    uint16_t *o = reinterpret_cast<uint16_t *>(dst + b * 34);
+    o[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const float s = __fmul_rn(v[i], inv);
-        const float a = fabsf(s);
-        const float fl = floorf(a);
-        float q = __fadd_rn(fl, floorf(__fmul_rn(2.0f, __fsub_rn(a, fl))));
-        q = s < 0.f ? -q : (s > 0.f ? q : 0.f);
-        o[2 + i] = (uint8_t)(int8_t)(int)q;
+    for (int j = 0; j < 16; ++j) {
+        uint32_t pair = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float s = __fmul_rn(v[2 * j + h], inv);
+            const float a = fabsf(s);
+            const float fl = floorf(a);
+            float q = __fadd_rn(fl, floorf(__fmul_rn(2.0f, __fsub_rn(a, fl))));
+            q = s < 0.f ? -q : q;
+            pair |= ((uint32_t)(int)q & 0xFFu) << (8 * h);
+        }
+        o[1 + j] = (uint16_t)pair;
     }
 }
 
