@@ -108,40 +108,49 @@ __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x,
     }
 }
 
-// One CTA (256 threads) per token; H % 4 == 0.  `shared_rows` = 0 when there is no shared expert.
+// grid (T, H / 1024): 256 threads x 4 columns; H % 4 == 0.  The token's k row positions and
+// weights are staged in shared memory so the k row loads are independent of each other.
 __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
                                                       const float *__restrict__ w, int T, int H, int k,
                                                       int has_shared, void *__restrict__ out, int out_dtype) {
+    __shared__ int64_t sp[33];
+    __shared__ float sw[32];
     const int t = blockIdx.x;
     const int64_t tk = (int64_t)T * k;
-    for (int c = threadIdx.x * 4; c < H; c += 256 * 4) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int l = 0; l < k; ++l) {
-            const int64_t p = pos_of[(int64_t)t * k + l];
-            const float wl = w[(int64_t)t * k + l];
-            const float4 v = *reinterpret_cast<const float4 *>(y + p * H + c);
-            acc.x = fmaf(wl, v.x, acc.x);
-            acc.y = fmaf(wl, v.y, acc.y);
-            acc.z = fmaf(wl, v.z, acc.z);
-            acc.w = fmaf(wl, v.w, acc.w);
-        }
-        if (has_shared) {
-            const float4 v = *reinterpret_cast<const float4 *>(y + (tk + t) * H + c);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        const int64_t o = (int64_t)t * H + c;
-        if (out_dtype == VFMOE_DT_BF16) {
-            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 pk;
-            pk.x = *reinterpret_cast<const uint32_t *>(&lo);
-            pk.y = *reinterpret_cast<const uint32_t *>(&hi);
-            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + o) = pk;
-        } else {
-            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + o) = acc;
-        }
+    if (threadIdx.x < k) {
+        sp[threadIdx.x] = (int64_t)pos_of[(int64_t)t * k + threadIdx.x] * H;
+        sw[threadIdx.x] = w[(int64_t)t * k + threadIdx.x];
+    }
+    if (threadIdx.x == 32) sp[32] = (tk + t) * H;
+    __syncthreads();
+    const int c = (blockIdx.y * 256 + threadIdx.x) * 4;
+    if (c >= H) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int l = 0; l < k; ++l) {
+        const float wl = sw[l];
+        const float4 v = *reinterpret_cast<const float4 *>(y + sp[l] + c);
+        acc.x = fmaf(wl, v.x, acc.x);
+        acc.y = fmaf(wl, v.y, acc.y);
+        acc.z = fmaf(wl, v.z, acc.z);
+        acc.w = fmaf(wl, v.w, acc.w);
+    }
+    if (has_shared) {
+        const float4 v = *reinterpret_cast<const float4 *>(y + sp[32] + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    const int64_t o = (int64_t)t * H + c;
+    if (out_dtype == VFMOE_DT_BF16) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + o) = pk;
+    } else {
+        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + o) = acc;
     }
 }
 
@@ -163,7 +172,8 @@ int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t r
 int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, int has_shared,
                    void *out, int out_dtype, cudaStream_t st) {
     if (T == 0) return VFMOE_OK;
-    combine_kernel<<<T, 256, 0, st>>>(y, pos_of, w, T, H, k, has_shared, out, out_dtype);
+    dim3 grid((unsigned)T, (unsigned)cdiv(H, 1024));
+    combine_kernel<<<grid, 256, 0, st>>>(y, pos_of, w, T, H, k, has_shared, out, out_dtype);
     VF_LAUNCH_CHECK("combine_kernel");
     return VFMOE_OK;
 }

@@ -6,64 +6,72 @@
 // output by 335%, native/glm53/README.md:367-379), so logits are accumulated in
 // float64 from the exact bf16/fp32 inputs.
 //
-//   router_logits_small  T <= 32 (decode): warp per expert, split over K, all T
-//                        tokens per pass; reads W_r once (HBM-bound).
+//   router_logits_small  T <= 32 (decode): 2 experts per CTA, K split over 4 warps,
+//                        all T tokens per pass; reads W_r once (HBM-bound).
 //   router_logits_tiled  T > 32 (prefill): 64x64 output tiles, fp64 FMA.
-//   router_topk          warp per token: sum K-split partials in a fixed order,
-//                        sigmoid, k rounds of warp argmax (ties -> lowest id),
+//   router_topk          warp per token: sigmoid, k rounds of warp argmax (ties -> lowest id),
 //                        renormalise, per-expert counts for dispatch.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace vfmoe {
 
+// Decode shapes (T <= 32): two experts per CTA, each expert's K split over 4 warps;
+// every lane keeps TB token accumulators in fp64.  Partials are reduced in a fixed order
+// through shared memory, so logits are deterministic and written once (no K-split pass).
 template <int TB>
 __global__ void __launch_bounds__(256) router_logits_small(const void *__restrict__ x, int x_dtype,
                                                            const float *__restrict__ wr, int T, int H,
-                                                           int E, int kc, double *__restrict__ part) {
+                                                           int E, double *__restrict__ logits) {
+    __shared__ double red[2][4][TB];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 8 + warp;
-    const int ks = blockIdx.y;
-    if (e >= E) return;
-    const int k0 = ks * kc;
-    const int k1 = min(H, k0 + kc);
+    const int le = warp >> 2, kq = warp & 3;
+    const int e = blockIdx.x * 2 + le;
+    const int kc = H / 4;  // H % 512 == 0 -> kc % 128 == 0
     double acc[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t) acc[t] = 0.0;
-    const float *wrow = wr + (int64_t)e * H;
-    for (int k = k0 + lane * 4; k < k1; k += 128) {
-        const float4 w4 = *reinterpret_cast<const float4 *>(wrow + k);
+    if (e < E) {
+        const float *wrow = wr + (int64_t)e * H;
+        for (int k = kq * kc + lane * 4; k < (kq + 1) * kc; k += 128) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(wrow + k);
 #pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            if (t < T) {
-                float xv[4];
-                if (x_dtype == VFMOE_DT_BF16) {
-                    const uint2 raw = *reinterpret_cast<const uint2 *>(
-                        reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H + k);
-                    xv[0] = __uint_as_float(raw.x << 16);
-                    xv[1] = __uint_as_float(raw.x & 0xFFFF0000u);
-                    xv[2] = __uint_as_float(raw.y << 16);
-                    xv[3] = __uint_as_float(raw.y & 0xFFFF0000u);
-                } else {
-                    const float4 f = *reinterpret_cast<const float4 *>(
-                        reinterpret_cast<const float *>(x) + (int64_t)t * H + k);
-                    xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
+            for (int t = 0; t < TB; ++t) {
+                if (t < T) {
+                    float xv[4];
+                    if (x_dtype == VFMOE_DT_BF16) {
+                        const uint2 raw = *reinterpret_cast<const uint2 *>(
+                            reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H + k);
+                        xv[0] = __uint_as_float(raw.x << 16);
+                        xv[1] = __uint_as_float(raw.x & 0xFFFF0000u);
+                        xv[2] = __uint_as_float(raw.y << 16);
+                        xv[3] = __uint_as_float(raw.y & 0xFFFF0000u);
+                    } else {
+                        const float4 f = *reinterpret_cast<const float4 *>(
+                            reinterpret_cast<const float *>(x) + (int64_t)t * H + k);
+                        xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
+                    }
+                    double a = acc[t];
+                    a = fma((double)xv[0], (double)w4.x, a);
+                    a = fma((double)xv[1], (double)w4.y, a);
+                    a = fma((double)xv[2], (double)w4.z, a);
+                    a = fma((double)xv[3], (double)w4.w, a);
+                    acc[t] = a;
                 }
-                double a = acc[t];
-                a = fma((double)xv[0], (double)w4.x, a);
-                a = fma((double)xv[1], (double)w4.y, a);
-                a = fma((double)xv[2], (double)w4.z, a);
-                a = fma((double)xv[3], (double)w4.w, a);
-                acc[t] = a;
             }
         }
     }
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
-        if (t < T) {
-            const double s = warp_sum_f64(acc[t]);
-            if (lane == 0) part[((int64_t)ks * T + t) * E + e] = s;
-        }
+        const double v = warp_sum_f64(acc[t]);
+        if (lane == 0) red[le][kq][t] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * TB) {
+        const int l2 = threadIdx.x / TB, t = threadIdx.x % TB;
+        const int e2 = blockIdx.x * 2 + l2;
+        if (t < T && e2 < E)
+            logits[(int64_t)t * E + e2] = ((red[l2][0][t] + red[l2][1][t]) + red[l2][2][t]) + red[l2][3][t];
     }
 }
 
@@ -127,7 +135,7 @@ __global__ void __launch_bounds__(256) router_logits_tiled(const void *__restric
 
 // Warp per token.  NPL = experts per lane (E <= 32 * NPL).
 template <int NPL>
-__global__ void __launch_bounds__(256) router_topk(const double *__restrict__ part, int nks, int T, int E,
+__global__ void __launch_bounds__(256) router_topk(const double *__restrict__ logits, int T, int E,
                                                    int k, const float *__restrict__ bias, double scale,
                                                    int32_t *__restrict__ idx_out, float *__restrict__ w_out,
                                                    int32_t *__restrict__ counts) {
@@ -139,8 +147,7 @@ __global__ void __launch_bounds__(256) router_topk(const double *__restrict__ pa
     for (int j = 0; j < NPL; ++j) {
         const int e = lane + 32 * j;
         if (e < E) {
-            double logit = 0.0;
-            for (int s = 0; s < nks; ++s) logit += part[((int64_t)s * T + t) * E + e];
+            const double logit = logits[(int64_t)t * E + e];
             const double sc = 1.0 / (1.0 + exp(-logit));
             score[j] = sc;
             const double c = sc + (double)bias[e];
@@ -201,44 +208,32 @@ __global__ void __launch_bounds__(256) router_topk(const double *__restrict__ pa
 int launch_router(const void *x, int x_dtype, const float *wr, const float *bias, int T, int H, int E,
                   int k, double scale, double *part, int32_t *idx, float *w, int32_t *counts,
                   cudaStream_t st) {
-    int nks;
-    if (T <= 32) {
-        nks = H >= 4096 ? 32 : (H >= 1024 ? 8 : 1);
-        int kc = (int)align_up(cdiv(H, nks), 128);
-        nks = (int)cdiv(H, kc);
-        dim3 grid((unsigned)cdiv(E, 8), (unsigned)nks);
+    if (T <= 32 && H % 512 == 0) {
+        const unsigned grid = (unsigned)cdiv(E, 2);
         if (T <= 8)
-            router_logits_small<8><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, kc, part);
+            router_logits_small<8><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
         else
-            router_logits_small<32><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, kc, part);
+            router_logits_small<32><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
         VF_LAUNCH_CHECK("router_logits_small");
     } else {
-        nks = 1;
         dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 64));
         router_logits_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
         VF_LAUNCH_CHECK("router_logits_tiled");
     }
     const unsigned tb = (unsigned)cdiv(T, 8);
     const int npl = (int)cdiv(E, 32);
-    if (npl <= 1)
-        router_topk<1><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
-    else if (npl <= 2)
-        router_topk<2><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
-    else if (npl <= 4)
-        router_topk<4><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
-    else if (npl <= 8)
-        router_topk<8><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
-    else if (npl <= 16)
-        router_topk<16><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
-    else
-        router_topk<32><<<tb, 256, 0, st>>>(part, nks, T, E, k, bias, scale, idx, w, counts);
+#define VF_TOPK(NPL) router_topk<NPL><<<tb, 256, 0, st>>>(part, T, E, k, bias, scale, idx, w, counts)
+    if (npl <= 1) VF_TOPK(1);
+    else if (npl <= 2) VF_TOPK(2);
+    else if (npl <= 4) VF_TOPK(4);
+    else if (npl <= 8) VF_TOPK(8);
+    else if (npl <= 16) VF_TOPK(16);
+    else VF_TOPK(32);
+#undef VF_TOPK
     VF_LAUNCH_CHECK("router_topk");
     return VFMOE_OK;
 }
 
-int64_t router_partial_doubles(int T, int H, int E) {
-    if (T <= 32) return (int64_t)32 * T * E;
-    return (int64_t)T * E;
-}
+int64_t router_partial_doubles(int T, int H, int E) { return (int64_t)T * E; }
 
 }  // namespace vfmoe
