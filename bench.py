@@ -58,6 +58,8 @@ def args_parse():
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4d", "c4p"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--fmt", default=None, choices=[None, "q8_0", "exl3"])
+    ap.add_argument("--experts", type=int, default=None,
+                    help="override the routed expert count (small cases for ncu captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     return ap.parse_args()
@@ -171,6 +173,8 @@ def run_ours(a, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     init(local_rank)
     cfg = synth.config(a.workload, tokens=a.tokens, fmt=a.fmt, seed=rank)
+    if a.experts:
+        cfg.n_experts = a.experts
     if cfg.fmt != "q8_0" or a.workload not in ("c1", "c4d"):
         raise SystemExit(f"workload {a.workload}/{cfg.fmt} not wired into bench yet")
     layer, xd, host, dev = build_ours(cfg, rank)
