@@ -197,3 +197,51 @@ def test_tensor_core_path_matches_simt_path(c0, c1, cfg_name, T):
     print(f"[tc-vs-simt {cfg_name} T={T}] rel-L2 {rel_l2(tc, simt):.3e} max-abs {np.abs(tc - simt).max():.3e}")
     assert rel_l2(tc, simt) < 5e-4, rel_l2(tc, simt)
     assert np.abs(tc - simt).max() < 5e-3
+
+
+# ----------------------------------------------------------------------------- router precision levels
+def _router_layer(w_r, bias, H, E, k, x_dtype=torch.bfloat16):
+    """A routing-only layer (expert weights are never read by vfmoe_route)."""
+    from vybforge_b200.moe import MoELayer
+    I = 256
+    gu = torch.zeros((E, I, H // 32 * 34), dtype=torch.uint8, device="cuda")
+    dn = torch.zeros((E, H, I // 32 * 34), dtype=torch.uint8, device="cuda")
+    return MoELayer(hidden=H, inter=I, n_experts=E, topk=k, router_w=torch.from_numpy(w_r).cuda(),
+                    router_bias=torch.from_numpy(bias).cuda(), gate=gu, up=gu, down=dn, x_dtype=x_dtype,
+                    out_dtype=torch.float32)
+
+
+@pytest.mark.parametrize("T", [16, 96])
+def test_router_near_ties_take_the_f64_level(T):
+    """Pairs of experts whose router rows differ by one fp32 ulp in one element: their
+    logits differ by ~1e-9, below the float-float bound, so the f64 level must order them."""
+    moe.init(0)
+    rng = np.random.default_rng(21)
+    H, E, k = 6144, 256, 8
+    from vybforge_b200.quant import round_bf16
+    x = round_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    w_r = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    bias = rng.normal(0, 0.01, E).astype(np.float32)
+    for p in range(4):
+        a = 10 + 2 * p
+        w_r[a + 1] = w_r[a]
+        w_r[a + 1, 7 * p] = np.nextafter(w_r[a, 7 * p], np.float32(1.0))   # one ulp up
+        bias[a] = bias[a + 1] = 1.0                                          # both always selected
+    layer = _router_layer(w_r, bias, H, E, k)
+    idx, w = layer.route(torch.from_numpy(x).to(torch.bfloat16).cuda())
+    ri, rw = orc.route(x, w_r, bias, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    layer.check_device_error()
+
+
+def test_router_prefill_size_bit_exact():
+    moe.init(0)
+    cfg = synth.config("c3", tokens=4096)
+    x, w_r, bias, _ = synth.router_inputs(cfg)
+    layer = _router_layer(w_r, bias, cfg.hidden, cfg.n_experts, cfg.topk)
+    idx, w = layer.route(torch.from_numpy(x).to(torch.bfloat16).cuda())
+    ri, rw = orc.route(x, w_r, bias, cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    layer.check_device_error()

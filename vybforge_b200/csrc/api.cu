@@ -44,6 +44,7 @@ struct Layer {
     int has_shared = 0;
     int64_t q8_row_gate = 0, q8_row_down = 0;
     int *dev_err = nullptr;      // device error word (allocated at create)
+    float *nw = nullptr;         // |W_r row|_2 upper bounds (allocated at create)
     void *own_ws = nullptr;      // internal workspace when the caller passes none
     int64_t own_ws_bytes = 0;
     TcPlan tc;                   // tensor-core launch state (tensor maps)
@@ -103,7 +104,7 @@ static WsLayout ws_layout(const Layer &L, int64_t T) {
     o.pos_of = take(T * L.k * 4);
     o.idx = take(T * L.k * 4);
     o.w = take(T * L.k * 4);
-    o.part = take(router_partial_doubles((int)T, L.H, L.E) * 8);
+    o.part = take(router_logit_floats((int)T, L.E) * 4);
     o.xp = take(rows * L.H * 2);
     o.act = take(rows * L.I * 2);
     o.y = take(rows * L.H * 4);
@@ -242,14 +243,21 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
     cudaGetDevice(&L->device);
     cudaError_t e = cudaMalloc(&L->dev_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(L->dev_err, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&L->nw, L->E * sizeof(float));
+    if (e == cudaSuccess && launch_router_norms(reinterpret_cast<const float *>(desc->router_w), L->H, L->E, L->nw, 0))
+        e = cudaErrorLaunchFailure;
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
-        cuda_fail(e, "cudaMalloc(error word)", __FILE__, __LINE__);
+        cuda_fail(e, "layer set-up (error word, router norms)", __FILE__, __LINE__);
+        if (L->dev_err) cudaFree(L->dev_err);
+        if (L->nw) cudaFree(L->nw);
         delete L;
         return VFMOE_ERR_CUDA;
     }
     rc = tc_plan_create(L->d, L->tc);
     if (rc) {
         cudaFree(L->dev_err);
+        cudaFree(L->nw);
         delete L;
         return rc;
     }
@@ -273,6 +281,7 @@ int vfmoe_layer_destroy(int64_t handle) {
     }
     if (L->own_ws) cudaFree(L->own_ws);
     if (L->dev_err) cudaFree(L->dev_err);
+    if (L->nw) cudaFree(L->nw);
     for (auto &ev : L->ev_pending)
         for (auto e : ev) L->ev_pool.push_back(e);
     for (auto e : L->ev_pool) cudaEventDestroy(e);
@@ -297,9 +306,10 @@ static int route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout
     int32_t *idx = *idx_p ? *idx_p : reinterpret_cast<int32_t *>(base + lay.idx);
     float *w = *w_p ? *w_p : reinterpret_cast<float *>(base + lay.w);
     int rc = launch_router(reinterpret_cast<const void *>(x), (int)L.d.x_dtype,
-                           reinterpret_cast<const float *>(L.d.router_w),
+                           reinterpret_cast<const float *>(L.d.router_w), L.nw,
                            reinterpret_cast<const float *>(L.d.router_bias), (int)T, L.H, L.E, L.k,
-                           L.d.routed_scale, reinterpret_cast<double *>(base + lay.part), idx, w, counts, st);
+                           L.d.routed_scale, reinterpret_cast<float *>(base + lay.part), idx, w, counts, L.dev_err,
+                           st);
     *idx_p = idx;
     *w_p = w;
     return rc;

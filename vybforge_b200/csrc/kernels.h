@@ -34,10 +34,13 @@ struct MoeArgs {
     int64_t tiles_cap;
 };
 
-int launch_router(const void *x, int x_dtype, const float *wr, const float *bias, int T, int H, int E,
-                  int k, double scale, double *part, int32_t *idx, float *w, int32_t *counts,
+// Router: fp32 logits -> candidate filter -> float-float / f64 refinement (exact f64 ordering).
+// nw = |W_r row|_2 upper bounds (launch_router_norms, once per layer); logits = T*E floats scratch.
+int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
+                  int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
                   cudaStream_t st);
-int64_t router_partial_doubles(int T, int H, int E);
+int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t st);
+int64_t router_logit_floats(int T, int E);
 
 int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);

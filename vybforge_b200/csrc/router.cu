@@ -1,36 +1,65 @@
 // Sigmoid + selection-bias top-k router (native/glm53/moe_ref.py:64-78,
 // native/kernels/moe.vyb:32-95).
 //
-// Expert ids must match a float64 numpy oracle bit for bit, and selection is
-// chaotically sensitive (one bf16 ulp on the router input moved a reference MoE
-// output by 335%, native/glm53/README.md:367-379), so logits are accumulated in
-// float64 from the exact bf16/fp32 inputs.
+// Expert ids must equal those of a float64 numpy oracle, and selection is chaotically
+// sensitive (one bf16 ulp on the router input moved a reference MoE output by 335%,
+// native/glm53/README.md:367-379).  Vector fp64 on this part runs at ~2 FMA/clk/SM,
+// so the router establishes the f64 ordering in three levels, each with a rigorous
+// error bound:
 //
-//   router_logits_small  T <= 32 (decode): 2 experts per CTA, K split over 4 warps,
-//                        all T tokens per pass; reads W_r once (HBM-bound).
-//   router_logits_tiled  T > 32 (prefill): 64x64 output tiles, fp64 FMA.
-//   router_topk          warp per token: sigmoid, k rounds of warp argmax (ties -> lowest id),
-//                        renormalise, per-expert counts for dispatch.
+//   L1  router_logits_f32_*  fp32 logits for every (token, expert).  Error bound
+//       |L1 - exact| <= c1 * |x_t|_2 * |w_e|_2 (Cauchy-Schwarz on sum |x_i w_i|, c1 = the
+//       gamma_n of the kernel's summation depth, doubled for safety).
+//   L2  router_refine        keeps every expert that can still be in the top k
+//       (approx choice + bound >= k-th largest of approx choice - bound), recomputes
+//       their logits with float-float arithmetic (TwoProduct + TwoSum, error
+//       <= c2 * |x|*|w| with c2 ~ 1e-9) and sorts them in f64.
+//   L3  (same kernel)        if two neighbours among the top k+1 are closer than the L2
+//       bound, their logits are recomputed with fp64 FMA and re-sorted (lowest id wins
+//       exact ties).  Rare: ~1e-4 of tokens on random inputs; exact ties always take it.
+//
+// Weights w = score / (sum + 1e-20) * scale use the L2/L3 f64 scores.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace vfmoe {
 
-// Decode shapes (T <= 32): two experts per CTA, each expert's K split over 4 warps;
-// every lane keeps TB token accumulators in fp64.  Partials are reduced in a fixed order
-// through shared memory, so logits are deterministic and written once (no K-split pass).
+constexpr int kMaxCand = 64;
+
+__device__ __forceinline__ void two_sum(float a, float b, float &s, float &t) {
+    s = a + b;
+    const float bb = s - a;
+    t = (a - (s - bb)) + (b - bb);
+}
+
+__device__ __forceinline__ void ld_x4(const void *x, int x_dtype, int64_t off, float (&v)[4]) {
+    if (x_dtype == VFMOE_DT_BF16) {
+        const uint2 raw = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(x) + off);
+        v[0] = __uint_as_float(raw.x << 16);
+        v[1] = __uint_as_float(raw.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(raw.y << 16);
+        v[3] = __uint_as_float(raw.y & 0xFFFF0000u);
+    } else {
+        const float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + off);
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    }
+}
+
+// ----------------------------------------------------------------------------- L1, decode
+// T <= 32: two experts per CTA, each expert's K split over 4 warps, lanes stride 128.
+// Summation depth per logit: H/128 sequential FMAs + 5 (warp tree) + 2 (4-warp tree).
 template <int TB>
-__global__ void __launch_bounds__(256) router_logits_small(const void *__restrict__ x, int x_dtype,
-                                                           const float *__restrict__ wr, int T, int H,
-                                                           int E, double *__restrict__ logits) {
-    __shared__ double red[2][4][TB];
+__global__ void __launch_bounds__(256) router_logits_f32_small(const void *__restrict__ x, int x_dtype,
+                                                               const float *__restrict__ wr, int T, int H, int E,
+                                                               float *__restrict__ logits) {
+    __shared__ float red[2][4][TB];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int le = warp >> 2, kq = warp & 3;
     const int e = blockIdx.x * 2 + le;
-    const int kc = H / 4;  // H % 512 == 0 -> kc % 128 == 0
-    double acc[TB];
+    const int kc = H / 4;
+    float acc[TB];
 #pragma unroll
-    for (int t = 0; t < TB; ++t) acc[t] = 0.0;
+    for (int t = 0; t < TB; ++t) acc[t] = 0.f;
     if (e < E) {
         const float *wrow = wr + (int64_t)e * H;
         for (int k = kq * kc + lane * 4; k < (kq + 1) * kc; k += 128) {
@@ -39,23 +68,12 @@ __global__ void __launch_bounds__(256) router_logits_small(const void *__restric
             for (int t = 0; t < TB; ++t) {
                 if (t < T) {
                     float xv[4];
-                    if (x_dtype == VFMOE_DT_BF16) {
-                        const uint2 raw = *reinterpret_cast<const uint2 *>(
-                            reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H + k);
-                        xv[0] = __uint_as_float(raw.x << 16);
-                        xv[1] = __uint_as_float(raw.x & 0xFFFF0000u);
-                        xv[2] = __uint_as_float(raw.y << 16);
-                        xv[3] = __uint_as_float(raw.y & 0xFFFF0000u);
-                    } else {
-                        const float4 f = *reinterpret_cast<const float4 *>(
-                            reinterpret_cast<const float *>(x) + (int64_t)t * H + k);
-                        xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
-                    }
-                    double a = acc[t];
-                    a = fma((double)xv[0], (double)w4.x, a);
-                    a = fma((double)xv[1], (double)w4.y, a);
-                    a = fma((double)xv[2], (double)w4.z, a);
-                    a = fma((double)xv[3], (double)w4.w, a);
+                    ld_x4(x, x_dtype, (int64_t)t * H + k, xv);
+                    float a = acc[t];
+                    a = fmaf(xv[0], w4.x, a);
+                    a = fmaf(xv[1], w4.y, a);
+                    a = fmaf(xv[2], w4.z, a);
+                    a = fmaf(xv[3], w4.w, a);
                     acc[t] = a;
                 }
             }
@@ -63,53 +81,58 @@ __global__ void __launch_bounds__(256) router_logits_small(const void *__restric
     }
 #pragma unroll
     for (int t = 0; t < TB; ++t) {
-        const double v = warp_sum_f64(acc[t]);
+        const float v = warp_sum_f32(acc[t]);
         if (lane == 0) red[le][kq][t] = v;
     }
     __syncthreads();
     if (threadIdx.x < 2 * TB) {
         const int l2 = threadIdx.x / TB, t = threadIdx.x % TB;
         const int e2 = blockIdx.x * 2 + l2;
-        if (t < T && e2 < E)
-            logits[(int64_t)t * E + e2] = ((red[l2][0][t] + red[l2][1][t]) + red[l2][2][t]) + red[l2][3][t];
+        if (t < T && e2 < E) logits[(int64_t)t * E + e2] = (red[l2][0][t] + red[l2][1][t]) + (red[l2][2][t] + red[l2][3][t]);
     }
 }
 
-// 64 tokens x 64 experts per CTA, 256 threads, each 4 tokens x 4 experts, K in chunks of 16.
-__global__ void __launch_bounds__(256) router_logits_tiled(const void *__restrict__ x, int x_dtype,
-                                                           const float *__restrict__ wr, int T, int H,
-                                                           int E, double *__restrict__ part) {
-    constexpr int BT = 64, BE = 64, KC = 16;
-    __shared__ double xs[KC][BT + 1];
-    __shared__ double ws[KC][BE + 1];
+// ----------------------------------------------------------------------------- L1, prefill
+// 64 tokens x 64 experts per CTA, 256 threads x (4 x 4) outputs, K in chunks of 32;
+// each chunk is summed separately then added to the running total, so the summation
+// depth is 32 + H/32.
+__global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__restrict__ x, int x_dtype,
+                                                               const float *__restrict__ wr, int T, int H, int E,
+                                                               float *__restrict__ logits) {
+    constexpr int BT = 64, BE = 64, KC = 32;
+    __shared__ float xs[KC][BT + 4];
+    __shared__ float ws[KC][BE + 4];
     const int t0 = blockIdx.y * BT, e0 = blockIdx.x * BE;
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;  // experts e0 + tx + 16j, tokens t0 + ty + 16i
-    double acc[4][4];
+    const int tx = tid & 15, ty = tid >> 4;
+    float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
     for (int kb = 0; kb < H; kb += KC) {
-        // 64 rows x 16 k for each operand = 1024 values; 4 per thread.
+        // 64 rows x 32 k per operand = 2048 values, 8 per thread (two float4 / bf16x4 loads)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int idx = tid + r * 256;
-            const int row = idx >> 4, kk = idx & 15;
-            const int k = kb + kk;
-            const int t = t0 + row;
-            double xv = 0.0;
-            if (t < T && k < H) xv = (double)ld_act(x, (int64_t)t * H + k, x_dtype);
-            xs[kk][row] = xv;
-            const int e = e0 + row;
-            double wv = 0.0;
-            if (e < E && k < H) wv = (double)wr[(int64_t)e * H + k];
-            ws[kk][row] = wv;
+        for (int r = 0; r < 2; ++r) {
+            const int idx = tid + r * 256;       // 512 groups of 4 k
+            const int row = idx >> 3, kq = (idx & 7) * 4;
+            const int t = t0 + row, e = e0 + row;
+            float xv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (t < T) ld_x4(x, x_dtype, (int64_t)t * H + kb + kq, xv);
+            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < E) w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)e * H + kb + kq);
+            xs[kq][row] = xv[0]; xs[kq + 1][row] = xv[1]; xs[kq + 2][row] = xv[2]; xs[kq + 3][row] = xv[3];
+            ws[kq][row] = w4.x; ws[kq + 1][row] = w4.y; ws[kq + 2][row] = w4.z; ws[kq + 3][row] = w4.w;
         }
         __syncthreads();
+        float part[4][4];
 #pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) part[i][j] = 0.f;
+#pragma unroll 8
         for (int kk = 0; kk < KC; ++kk) {
-            double xr[4], wc[4];
+            float xr[4], wc[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) xr[i] = xs[kk][ty + 16 * i];
 #pragma unroll
@@ -117,8 +140,12 @@ __global__ void __launch_bounds__(256) router_logits_tiled(const void *__restric
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fma(xr[i], wc[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) part[i][j] = fmaf(xr[i], wc[j], part[i][j]);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] += part[i][j];
         __syncthreads();
     }
 #pragma unroll
@@ -128,112 +155,302 @@ __global__ void __launch_bounds__(256) router_logits_tiled(const void *__restric
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int e = e0 + tx + 16 * j;
-            if (e < E) part[(int64_t)t * E + e] = acc[i][j];
+            if (e < E) logits[(int64_t)t * E + e] = acc[i][j];
         }
     }
 }
 
-// Warp per token.  NPL = experts per lane (E <= 32 * NPL).
-template <int NPL>
-__global__ void __launch_bounds__(256) router_topk(const double *__restrict__ logits, int T, int E,
-                                                   int k, const float *__restrict__ bias, double scale,
-                                                   int32_t *__restrict__ idx_out, float *__restrict__ w_out,
-                                                   int32_t *__restrict__ counts) {
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= T) return;
-    double score[NPL], choice[NPL];
-#pragma unroll
-    for (int j = 0; j < NPL; ++j) {
-        const int e = lane + 32 * j;
-        if (e < E) {
-            const double logit = logits[(int64_t)t * E + e];
-            const double sc = 1.0 / (1.0 + exp(-logit));
-            score[j] = sc;
-            const double c = sc + (double)bias[e];
-            choice[j] = isnan(c) ? -INFINITY : c;  // NaN never wins; keeps the argmax total
-        } else {
-            score[j] = 0.0;
-            choice[j] = -INFINITY;
-        }
+// ----------------------------------------------------------------------------- |w_e|_2
+__global__ void __launch_bounds__(256) row_norms_kernel(const float *__restrict__ wr, int H, int E,
+                                                        float *__restrict__ nw) {
+    const int e = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (e >= E) return;
+    double s = 0.0;
+    for (int k = lane; k < H; k += 32) {
+        const double v = wr[(int64_t)e * H + k];
+        s = fma(v, v, s);
     }
-    unsigned taken = 0;  // bit j: this lane's expert lane+32j already selected
-    int my_e = -1;
-    double my_s = 0.0, sum = 0.0;
-    for (int r = 0; r < k; ++r) {
-        double bv = -INFINITY;
-        int bi = 0x7fffffff, bj = -1;
+    s = warp_sum_f64(s);
+    if (lane == 0) nw[e] = (float)(sqrt(s) * (1.0 + 1e-6));  // rounded up: an upper bound
+}
+
+// ----------------------------------------------------------------------------- L2 + L3
+// One CTA (256 threads) per token.  NPL = experts per lane (E <= 32 * NPL).
+template <int NPL>
+__global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x, int x_dtype,
+                                                     const float *__restrict__ wr, const float *__restrict__ logits,
+                                                     const float *__restrict__ nw, const float *__restrict__ bias,
+                                                     int T, int H, int E, int k, float c1, float c2, double scale,
+                                                     int32_t *__restrict__ idx_out, float *__restrict__ w_out,
+                                                     int32_t *__restrict__ counts, int *__restrict__ err) {
+    __shared__ float s_red[8];
+    __shared__ int s_cand[kMaxCand];
+    __shared__ double s_logit[kMaxCand];   // L2/L3 logit, then the choice (score + bias)
+    __shared__ double s_score[kMaxCand];   // sigmoid(logit)
+    __shared__ int s_ncand, s_amb;
+    __shared__ int s_order[kMaxCand];
+    __shared__ unsigned char s_redo[kMaxCand];
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // |x_t|_2 (upper bound)
+    float ss = 0.f;
+    for (int h = threadIdx.x * 4; h < H; h += 1024) {
+        float v[4];
+        ld_x4(x, x_dtype, (int64_t)t * H + h, v);
+        ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
+    }
+    ss = warp_sum_f32(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += s_red[i];
+    const float nx = sqrtf(tot) * 1.001f;
+
+    // ---- L2 candidate selection (warp 0)
+    if (warp == 0) {
+        float ca[NPL], lo[NPL], hi[NPL];
 #pragma unroll
         for (int j = 0; j < NPL; ++j) {
             const int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u)) {
-                if (choice[j] > bv || bj < 0) {  // ascending e within a lane: strict > keeps lowest
-                    bv = choice[j];
+            if (e < E) {
+                const float l = logits[(int64_t)t * E + e];
+                const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
+                ca[j] = 1.f / (1.f + expf(-l)) + bias[e];
+                if (isnan(ca[j])) ca[j] = -INFINITY;
+                lo[j] = ca[j] - b1;
+                hi[j] = ca[j] + b1;
+            } else {
+                ca[j] = lo[j] = hi[j] = -INFINITY;
+            }
+        }
+        // tau = k-th largest lower bound
+        unsigned taken = 0;
+        float tau = -INFINITY;
+        for (int r = 0; r < k; ++r) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) {
+                const int e = lane + 32 * j;
+                if (e < E && !((taken >> j) & 1u) && (lo[j] > bv || bi == 0x7fffffff)) {
+                    bv = lo[j];
                     bi = e;
-                    bj = j;
                 }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            tau = bv;
+        }
+        int n = 0;
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            const int e = lane + 32 * j;
+            const bool c = e < E && hi[j] >= tau;
+            const unsigned m = __ballot_sync(0xffffffffu, c);
+            if (c) {
+                const int pos = n + __popc(m & ((1u << lane) - 1u));
+                if (pos < kMaxCand) s_cand[pos] = e;
+            }
+            n += __popc(m);
+        }
+        if (lane == 0) {
+            if (n > kMaxCand) {
+                raise_dev_error(err, DEV_BAD_COUNT);
+                n = kMaxCand;
+            }
+            s_ncand = n;
+            s_amb = 0;
+        }
+    }
+    __syncthreads();
+    const int nc = s_ncand;
+
+    // ---- L2 float-float logits of the candidates (warp per candidate)
+    for (int c = warp; c < nc; c += 8) {
+        const int e = s_cand[c];
+        const float *wrow = wr + (int64_t)e * H;
+        float shi = 0.f, slo = 0.f;
+        for (int h = lane * 4; h < H; h += 128) {
+            float xv[4];
+            ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
+            const float4 w4 = *reinterpret_cast<const float4 *>(wrow + h);
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float p = xv[i] * wv[i];
+                const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
+                float s, r;
+                two_sum(shi, p, s, r);
+                shi = s;
+                slo += r + pe;
             }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
+            const float oh = __shfl_xor_sync(0xffffffffu, shi, o);
+            const float ol = __shfl_xor_sync(0xffffffffu, slo, o);
+            float s, r;
+            two_sum(shi, oh, s, r);
+            shi = s;
+            slo = slo + ol + r;
+        }
+        if (lane == 0) s_logit[c] = (double)shi + (double)slo;
+    }
+    __syncthreads();
+
+    // ---- order candidates in f64; flag neighbours closer than the L2 bound (warp 0)
+    if (warp == 0) {
+        // rank of candidate c = #candidates strictly better (choice desc, id asc)
+        for (int c = lane; c < nc; c += 32) {
+            const int e = s_cand[c];
+            const double sc = 1.0 / (1.0 + exp(-s_logit[c]));
+            s_score[c] = sc;
+            s_logit[c] = sc + (double)bias[e];  // reuse: now the choice
+        }
+        __syncwarp();
+        for (int c = lane; c < nc; c += 32) {
+            const double ch = s_logit[c];
+            const int e = s_cand[c];
+            int rank = 0;
+            for (int o = 0; o < nc; ++o) {
+                const double oc = s_logit[o];
+                rank += (oc > ch || (oc == ch && s_cand[o] < e)) ? 1 : 0;
+            }
+            s_order[rank] = c;
+            s_redo[c] = 0;
+        }
+        __syncwarp();
+        for (int r = lane; r < k && r + 1 < nc; r += 32) {
+            const int a = s_order[r], b = s_order[r + 1];
+            const double ba = 0.25 * (double)c2 * nx * nw[s_cand[a]], bb = 0.25 * (double)c2 * nx * nw[s_cand[b]];
+            if (s_logit[a] - s_logit[b] <= 2.0 * (ba + bb) + 1e-15) {
+                s_redo[a] = 1;
+                s_redo[b] = 1;
+                s_amb = 1;
             }
         }
-        // bi is now warp-uniform: the winner.
-        const int owner = bi & 31, wj = bi >> 5;
-        double ws = 0.0;
-#pragma unroll
-        for (int j = 0; j < NPL; ++j)
-            if (j == wj) ws = score[j];
-        ws = __shfl_sync(0xffffffffu, ws, owner);
-        if (lane == owner) taken |= 1u << wj;
-        sum += ws;
-        if (lane == r) {
-            my_e = bi;
-            my_s = ws;
-        }
     }
-    if (lane < k) {
-        const double wv = my_s / (sum + 1e-20) * scale;
-        idx_out[(int64_t)t * k + lane] = my_e;
-        w_out[(int64_t)t * k + lane] = (float)wv;
-        if (my_e >= 0 && my_e < E) atomicAdd(&counts[my_e], 1);
+    __syncthreads();
+
+    // ---- L3: fp64 logits for ambiguous neighbours (rare)
+    if (s_amb) {
+        for (int c = warp; c < nc; c += 8) {
+            if (!s_redo[c]) continue;
+            const int e = s_cand[c];
+            const float *wrow = wr + (int64_t)e * H;
+            double acc = 0.0;
+            for (int h = lane * 4; h < H; h += 128) {
+                float xv[4];
+                ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
+                const float4 w4 = *reinterpret_cast<const float4 *>(wrow + h);
+                acc = fma((double)xv[0], (double)w4.x, acc);
+                acc = fma((double)xv[1], (double)w4.y, acc);
+                acc = fma((double)xv[2], (double)w4.z, acc);
+                acc = fma((double)xv[3], (double)w4.w, acc);
+            }
+            acc = warp_sum_f64(acc);
+            if (lane == 0) {
+                const double sc = 1.0 / (1.0 + exp(-acc));
+                s_score[c] = sc;
+                s_logit[c] = sc + (double)bias[e];
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int c = lane; c < nc; c += 32) {
+                const double ch = s_logit[c];
+                const int e = s_cand[c];
+                int rank = 0;
+                for (int o = 0; o < nc; ++o) {
+                    const double oc = s_logit[o];
+                    rank += (oc > ch || (oc == ch && s_cand[o] < e)) ? 1 : 0;
+                }
+                s_order[rank] = c;
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- final top-k and weights (warp 0): scores = choice - bias, in f64
+    if (warp == 0) {
+        double sc = 0.0;
+        int e = -1;
+        if (lane < k && lane < nc) {
+            const int c = s_order[lane];
+            e = s_cand[c];
+            sc = s_score[c];
+        }
+        double sum = 0.0;
+        for (int r = 0; r < k; ++r) sum += __shfl_sync(0xffffffffu, sc, r);
+        if (lane < k) {
+            idx_out[(int64_t)t * k + lane] = e;
+            w_out[(int64_t)t * k + lane] = (float)(sc / (sum + 1e-20) * scale);
+            if (e >= 0 && e < E)
+                atomicAdd(&counts[e], 1);
+            else
+                raise_dev_error(err, DEV_BAD_EXPERT_ID);
+        }
     }
 }
 
-int launch_router(const void *x, int x_dtype, const float *wr, const float *bias, int T, int H, int E,
-                  int k, double scale, double *part, int32_t *idx, float *w, int32_t *counts,
-                  cudaStream_t st) {
-    if (T <= 32 && H % 512 == 0) {
-        const unsigned grid = (unsigned)cdiv(E, 2);
-        if (T <= 8)
-            router_logits_small<8><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
-        else
-            router_logits_small<32><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
-        VF_LAUNCH_CHECK("router_logits_small");
-    } else {
-        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 64));
-        router_logits_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, part);
-        VF_LAUNCH_CHECK("router_logits_tiled");
-    }
-    const unsigned tb = (unsigned)cdiv(T, 8);
-    const int npl = (int)cdiv(E, 32);
-#define VF_TOPK(NPL) router_topk<NPL><<<tb, 256, 0, st>>>(part, T, E, k, bias, scale, idx, w, counts)
-    if (npl <= 1) VF_TOPK(1);
-    else if (npl <= 2) VF_TOPK(2);
-    else if (npl <= 4) VF_TOPK(4);
-    else if (npl <= 8) VF_TOPK(8);
-    else if (npl <= 16) VF_TOPK(16);
-    else VF_TOPK(32);
-#undef VF_TOPK
-    VF_LAUNCH_CHECK("router_topk");
+// Router summation-depth error constants (gamma_n with u = 2^-24, doubled for safety).
+static float gamma_bound(int depth) { return 2.0f * (float)depth * 5.9604645e-8f / (1.0f - (float)depth * 5.96e-8f); }
+
+int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t st) {
+    row_norms_kernel<<<(unsigned)cdiv(E, 8), 256, 0, st>>>(wr, H, E, nw);
+    VF_LAUNCH_CHECK("row_norms_kernel");
     return VFMOE_OK;
 }
 
-int64_t router_partial_doubles(int T, int H, int E) { return (int64_t)T * E; }
+int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
+                  int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
+                  cudaStream_t st) {
+    float c1;
+    if (T <= 32 && H % 512 == 0) {
+        const unsigned grid = (unsigned)cdiv(E, 2);
+        if (T <= 8)
+            router_logits_f32_small<8><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
+        else
+            router_logits_f32_small<32><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
+        VF_LAUNCH_CHECK("router_logits_f32_small");
+        c1 = gamma_bound(H / 128 + 7);
+    } else {
+        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 64));
+        router_logits_f32_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
+        VF_LAUNCH_CHECK("router_logits_f32_tiled");
+        c1 = gamma_bound(32 + H / 32);
+    }
+    // L2: per lane n = H/32 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
+    // exactly (TwoProduct), so the only error is lo's fp32 summation of 2n values r, pe with
+    // sum(|r| + |pe|) <= (n + 1) u S:  |err| <= gamma_{2n} (n + 1) u S; the 5-level lane
+    // tree adds gamma_10-sized terms of the same magnitude.  hi + lo is formed exactly in f64.
+    const int n2 = H / 32;
+    const float c2 = gamma_bound(2 * n2 + 10) * (float)(n2 + 1) * 5.9604645e-8f;
+    const int npl = (int)cdiv(E, 32);
+#define VF_REFINE(NPL)                                                                                       \
+    router_refine<NPL><<<(unsigned)T, 256, 0, st>>>(x, x_dtype, wr, logits, nw, bias, T, H, E, k, c1, c2, scale, \
+                                                    idx, w, counts, err)
+    if (npl <= 1) VF_REFINE(1);
+    else if (npl <= 2) VF_REFINE(2);
+    else if (npl <= 4) VF_REFINE(4);
+    else if (npl <= 8) VF_REFINE(8);
+    else if (npl <= 16) VF_REFINE(16);
+    else VF_REFINE(32);
+#undef VF_REFINE
+    VF_LAUNCH_CHECK("router_refine");
+    return VFMOE_OK;
+}
+
+int64_t router_logit_floats(int T, int E) { return (int64_t)T * E; }
 
 }  // namespace vfmoe
