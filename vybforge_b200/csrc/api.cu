@@ -104,7 +104,7 @@ static WsLayout ws_layout(const Layer &L, int64_t T) {
     o.pos_of = take(T * L.k * 4);
     o.idx = take(T * L.k * 4);
     o.w = take(T * L.k * 4);
-    o.part = take(router_logit_floats((int)T, L.E) * 4);
+    o.part = take(router_logit_floats((int)T, L.H, L.E) * 4);
     o.xp = take(rows * L.H * 2);
     o.act = take(rows * L.I * 2);
     o.y = take(rows * L.H * 4);

@@ -40,7 +40,7 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
                   int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
                   cudaStream_t st);
 int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t st);
-int64_t router_logit_floats(int T, int E);
+int64_t router_logit_floats(int T, int H, int E);
 
 int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);

@@ -19,6 +19,8 @@
 //       exact ties).  Rare: ~1e-4 of tokens on random inputs; exact ties always take it.
 //
 // Weights w = score / (sum + 1e-20) * scale use the L2/L3 f64 scores.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -46,50 +48,65 @@ __device__ __forceinline__ void ld_x4(const void *x, int x_dtype, int64_t off, f
 }
 
 // ----------------------------------------------------------------------------- L1, decode
-// T <= 32: two experts per CTA, each expert's K split over 4 warps, lanes stride 128.
-// Summation depth per logit: H/128 sequential FMAs + 5 (warp tree) + 2 (4-warp tree).
-template <int TB>
+// T <= 32: CTA = 16 experts x one K chunk of KCH (768 or 512); x[0..T)[chunk] is staged in
+// shared memory as fp32, each thread issues all of its W loads before any FMA.  Lane l owns
+// k = 4l + 128j + i of the chunk.  Per-chunk partials part[chunk][t][e] are summed in chunk
+// order by router_refine.  Summation depth: KCH/32 sequential FMAs + 5 (warp tree) + nchunk.
+template <int TB, int KCH>
 __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__restrict__ x, int x_dtype,
                                                                const float *__restrict__ wr, int T, int H, int E,
-                                                               float *__restrict__ logits) {
-    __shared__ float red[2][4][TB];
+                                                               float *__restrict__ part) {
+    extern __shared__ float xs[];  // [TB][KCH]
+    constexpr int J = KCH / 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int le = warp >> 2, kq = warp & 3;
-    const int e = blockIdx.x * 2 + le;
-    const int kc = H / 4;
-    float acc[TB];
+    const int kc = blockIdx.y, k0 = kc * KCH;
+    for (int i = threadIdx.x * 4; i < T * KCH; i += 1024) {
+        const int t = i / KCH, kk = i % KCH;
+        float v[4];
+        ld_x4(x, x_dtype, (int64_t)t * H + k0 + kk, v);
+        *reinterpret_cast<float4 *>(xs + i) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    const int e0 = blockIdx.x * 16 + warp * 2;
+    float4 w4[2][J];
 #pragma unroll
-    for (int t = 0; t < TB; ++t) acc[t] = 0.f;
-    if (e < E) {
-        const float *wrow = wr + (int64_t)e * H;
-        for (int k = kq * kc + lane * 4; k < (kq + 1) * kc; k += 128) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(wrow + k);
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int t = 0; t < TB; ++t) {
-                if (t < T) {
-                    float xv[4];
-                    ld_x4(x, x_dtype, (int64_t)t * H + k, xv);
-                    float a = acc[t];
-                    a = fmaf(xv[0], w4.x, a);
-                    a = fmaf(xv[1], w4.y, a);
-                    a = fmaf(xv[2], w4.z, a);
-                    a = fmaf(xv[3], w4.w, a);
-                    acc[t] = a;
+        for (int j = 0; j < J; ++j)
+            w4[a][j] = (e0 + a < E) ? *reinterpret_cast<const float4 *>(wr + (int64_t)(e0 + a) * H + k0 + 4 * lane + 128 * j)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    float acc[2][TB];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int t = 0; t < TB; ++t) acc[a][t] = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            if (t < T) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xs + t * KCH + 4 * lane + 128 * j);
+#pragma unroll
+                for (int a = 0; a < 2; ++a) {
+                    float v = acc[a][t];
+                    v = fmaf(xv.x, w4[a][j].x, v);
+                    v = fmaf(xv.y, w4[a][j].y, v);
+                    v = fmaf(xv.z, w4[a][j].z, v);
+                    v = fmaf(xv.w, w4[a][j].w, v);
+                    acc[a][t] = v;
                 }
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < TB; ++t) {
-        const float v = warp_sum_f32(acc[t]);
-        if (lane == 0) red[le][kq][t] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < 2 * TB) {
-        const int l2 = threadIdx.x / TB, t = threadIdx.x % TB;
-        const int e2 = blockIdx.x * 2 + l2;
-        if (t < T && e2 < E) logits[(int64_t)t * E + e2] = (red[l2][0][t] + red[l2][1][t]) + (red[l2][2][t] + red[l2][3][t]);
-    }
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            if (t < T) {
+                const float v = warp_sum_f32(acc[a][t]);
+                if (lane == 0 && e0 + a < E) part[((int64_t)kc * T + t) * E + e0 + a] = v;
+            }
+        }
 }
 
 // ----------------------------------------------------------------------------- L1, prefill
@@ -179,6 +196,7 @@ __global__ void __launch_bounds__(256) row_norms_kernel(const float *__restrict_
 template <int NPL>
 __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x, int x_dtype,
                                                      const float *__restrict__ wr, const float *__restrict__ logits,
+                                                     int nchunk,
                                                      const float *__restrict__ nw, const float *__restrict__ bias,
                                                      int T, int H, int E, int k, float c1, float c2, double scale,
                                                      int32_t *__restrict__ idx_out, float *__restrict__ w_out,
@@ -190,6 +208,8 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     __shared__ int s_ncand, s_amb;
     __shared__ int s_order[kMaxCand];
     __shared__ unsigned char s_redo[kMaxCand];
+    __shared__ float s_phi[8][8], s_plo[8][8];
+    __shared__ double s_pd[8][8];
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -215,7 +235,8 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
         for (int j = 0; j < NPL; ++j) {
             const int e = lane + 32 * j;
             if (e < E) {
-                const float l = logits[(int64_t)t * E + e];
+                float l = 0.f;
+                for (int c = 0; c < nchunk; ++c) l += logits[((int64_t)c * T + t) * E + e];
                 const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
                 ca[j] = 1.f / (1.f + expf(-l)) + bias[e];
                 if (isnan(ca[j])) ca[j] = -INFINITY;
@@ -275,38 +296,65 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     __syncthreads();
     const int nc = s_ncand;
 
-    // ---- L2 float-float logits of the candidates (warp per candidate)
-    for (int c = warp; c < nc; c += 8) {
-        const int e = s_cand[c];
-        const float *wrow = wr + (int64_t)e * H;
-        float shi = 0.f, slo = 0.f;
-        for (int h = lane * 4; h < H; h += 128) {
+    // ---- L2 float-float logits of the candidates: thread owns k = 4*tid + 1024*j + i,
+    // 8 candidates per pass (all loads of a pass are independent); then a fixed-order
+    // TwoSum tree over lanes and warps.
+    for (int c0 = 0; c0 < nc; c0 += 8) {
+        float shi[8], slo[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) shi[c] = slo[c] = 0.f;
+        for (int h = threadIdx.x * 4; h < H; h += 1024) {
             float xv[4];
             ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
-            const float4 w4 = *reinterpret_cast<const float4 *>(wrow + h);
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            float4 w4[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float p = xv[i] * wv[i];
-                const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
-                float s, r;
-                two_sum(shi, p, s, r);
-                shi = s;
-                slo += r + pe;
+            for (int c = 0; c < 8; ++c)
+                w4[c] = (c0 + c < nc) ? *reinterpret_cast<const float4 *>(wr + (int64_t)s_cand[c0 + c] * H + h)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float wv[4] = {w4[c].x, w4[c].y, w4[c].z, w4[c].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float p = xv[i] * wv[i];
+                    const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
+                    float sum, r;
+                    two_sum(shi[c], p, sum, r);
+                    shi[c] = sum;
+                    slo[c] += r + pe;
+                }
             }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float oh = __shfl_xor_sync(0xffffffffu, shi, o);
-            const float ol = __shfl_xor_sync(0xffffffffu, slo, o);
-            float s, r;
-            two_sum(shi, oh, s, r);
-            shi = s;
-            slo = slo + ol + r;
+        for (int c = 0; c < 8; ++c) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oh = __shfl_xor_sync(0xffffffffu, shi[c], o);
+                const float ol = __shfl_xor_sync(0xffffffffu, slo[c], o);
+                float sum, r;
+                two_sum(shi[c], oh, sum, r);
+                shi[c] = sum;
+                slo[c] = slo[c] + ol + r;
+            }
+            if (lane == 0) {
+                s_phi[warp][c] = shi[c];
+                s_plo[warp][c] = slo[c];
+            }
         }
-        if (lane == 0) s_logit[c] = (double)shi + (double)slo;
+        __syncthreads();
+        if (threadIdx.x < 8 && c0 + threadIdx.x < nc) {
+            const int c = threadIdx.x;
+            float hi = s_phi[0][c], lo = s_plo[0][c];
+            for (int w = 1; w < 8; ++w) {
+                float sum, r;
+                two_sum(hi, s_phi[w][c], sum, r);
+                hi = sum;
+                lo = lo + s_plo[w][c] + r;
+            }
+            s_logit[c0 + c] = (double)hi + (double)lo;
+        }
+        __syncthreads();
     }
-    __syncthreads();
 
     // ---- order candidates in f64; flag neighbours closer than the L2 bound (warp 0)
     if (warp == 0) {
@@ -342,30 +390,43 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     }
     __syncthreads();
 
-    // ---- L3: fp64 logits for ambiguous neighbours (rare)
+    // ---- L3: fp64 logits for ambiguous neighbours (rare); same decomposition as L2
     if (s_amb) {
-        for (int c = warp; c < nc; c += 8) {
-            if (!s_redo[c]) continue;
-            const int e = s_cand[c];
-            const float *wrow = wr + (int64_t)e * H;
-            double acc = 0.0;
-            for (int h = lane * 4; h < H; h += 128) {
+        for (int c0 = 0; c0 < nc; c0 += 8) {
+            double acc[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] = 0.0;
+            for (int h = threadIdx.x * 4; h < H; h += 1024) {
                 float xv[4];
                 ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
-                const float4 w4 = *reinterpret_cast<const float4 *>(wrow + h);
-                acc = fma((double)xv[0], (double)w4.x, acc);
-                acc = fma((double)xv[1], (double)w4.y, acc);
-                acc = fma((double)xv[2], (double)w4.z, acc);
-                acc = fma((double)xv[3], (double)w4.w, acc);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (c0 + c < nc && s_redo[c0 + c]) {
+                        const float4 w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)s_cand[c0 + c] * H + h);
+                        acc[c] = fma((double)xv[0], (double)w4.x, acc[c]);
+                        acc[c] = fma((double)xv[1], (double)w4.y, acc[c]);
+                        acc[c] = fma((double)xv[2], (double)w4.z, acc[c]);
+                        acc[c] = fma((double)xv[3], (double)w4.w, acc[c]);
+                    }
+                }
             }
-            acc = warp_sum_f64(acc);
-            if (lane == 0) {
-                const double sc = 1.0 / (1.0 + exp(-acc));
-                s_score[c] = sc;
-                s_logit[c] = sc + (double)bias[e];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const double v = warp_sum_f64(acc[c]);
+                if (lane == 0) s_pd[warp][c] = v;
             }
+            __syncthreads();
+            if (threadIdx.x < 8 && c0 + threadIdx.x < nc && s_redo[c0 + threadIdx.x]) {
+                const int c = threadIdx.x;
+                double v = 0.0;
+                for (int w = 0; w < 8; ++w) v += s_pd[w][c];
+                const int e = s_cand[c0 + c];
+                const double sc = 1.0 / (1.0 + exp(-v));
+                s_score[c0 + c] = sc;
+                s_logit[c0 + c] = sc + (double)bias[e];
+            }
+            __syncthreads();
         }
-        __syncthreads();
         if (warp == 0) {
             for (int c = lane; c < nc; c += 32) {
                 const double ch = s_logit[c];
@@ -412,34 +473,54 @@ int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t s
     return VFMOE_OK;
 }
 
+template <int TB, int KCH>
+static int launch_l1_small(const void *x, int x_dtype, const float *wr, int T, int H, int E, float *part,
+                           cudaStream_t st) {
+    const int smem = TB * KCH * 4;
+    static bool attr = false;
+    if (!attr) {
+        VF_CUDA(cudaFuncSetAttribute(router_logits_f32_small<TB, KCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+        attr = true;
+    }
+    dim3 grid((unsigned)cdiv(E, 16), (unsigned)(H / KCH));
+    router_logits_f32_small<TB, KCH><<<grid, 256, smem, st>>>(x, x_dtype, wr, T, H, E, part);
+    VF_LAUNCH_CHECK("router_logits_f32_small");
+    return VFMOE_OK;
+}
+
 int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
                   int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
                   cudaStream_t st) {
     float c1;
-    if (T <= 32 && H % 512 == 0) {
-        const unsigned grid = (unsigned)cdiv(E, 2);
-        if (T <= 8)
-            router_logits_f32_small<8><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
+    int nchunk = 1, rc = VFMOE_OK;
+    const int kch = H % 768 == 0 ? 768 : (H % 512 == 0 ? 512 : 0);
+    if (T <= 32 && kch) {
+        nchunk = H / kch;
+        if (kch == 768)
+            rc = T <= 8 ? launch_l1_small<8, 768>(x, x_dtype, wr, T, H, E, logits, st)
+                        : launch_l1_small<32, 768>(x, x_dtype, wr, T, H, E, logits, st);
         else
-            router_logits_f32_small<32><<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
-        VF_LAUNCH_CHECK("router_logits_f32_small");
-        c1 = gamma_bound(H / 128 + 7);
+            rc = T <= 8 ? launch_l1_small<8, 512>(x, x_dtype, wr, T, H, E, logits, st)
+                        : launch_l1_small<32, 512>(x, x_dtype, wr, T, H, E, logits, st);
+        if (rc) return rc;
+        c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
         dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 64));
         router_logits_f32_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
         VF_LAUNCH_CHECK("router_logits_f32_tiled");
         c1 = gamma_bound(32 + H / 32);
     }
-    // L2: per lane n = H/32 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
-    // exactly (TwoProduct), so the only error is lo's fp32 summation of 2n values r, pe with
-    // sum(|r| + |pe|) <= (n + 1) u S:  |err| <= gamma_{2n} (n + 1) u S; the 5-level lane
-    // tree adds gamma_10-sized terms of the same magnitude.  hi + lo is formed exactly in f64.
-    const int n2 = H / 32;
-    const float c2 = gamma_bound(2 * n2 + 10) * (float)(n2 + 1) * 5.9604645e-8f;
+    // L2: thread owns n = H/256 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
+    // exactly (TwoProduct), so the only error is lo's fp32 summation of the r and pe values,
+    // sum(|r| + |pe|) <= (n + 1) u S:  |err| <= gamma_{2n} (n + 1) u S; the 5 + 7 level lane and
+    // warp trees add terms of the same size (bounded with gamma_{2n+24}).  hi + lo is exact in f64.
+    const int n2 = H / 256;
+    const float c2 = gamma_bound(2 * n2 + 24) * (float)(n2 + 1 + 24) * 5.9604645e-8f;
     const int npl = (int)cdiv(E, 32);
-#define VF_REFINE(NPL)                                                                                       \
-    router_refine<NPL><<<(unsigned)T, 256, 0, st>>>(x, x_dtype, wr, logits, nw, bias, T, H, E, k, c1, c2, scale, \
-                                                    idx, w, counts, err)
+#define VF_REFINE(NPL)                                                                                          \
+    router_refine<NPL><<<(unsigned)T, 256, 0, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, E, k, c1, c2, \
+                                                    scale, idx, w, counts, err)
     if (npl <= 1) VF_REFINE(1);
     else if (npl <= 2) VF_REFINE(2);
     else if (npl <= 4) VF_REFINE(4);
@@ -451,6 +532,6 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     return VFMOE_OK;
 }
 
-int64_t router_logit_floats(int T, int E) { return (int64_t)T * E; }
+int64_t router_logit_floats(int T, int H, int E) { return (int64_t)T * E * (T <= 32 ? std::max(1, H / 512) : 1); }
 
 }  // namespace vfmoe
