@@ -11,9 +11,13 @@
 //   D = fp32 accumulators in TMEM (gate and up side by side for the fused SwiGLU).
 // Raw Q8_0 bytes stream in by TMA as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage.
 //
-// Warp roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
-// warp 2 TMEM allocator, warps 4..11 dequant + epilogue (warp w owns TMEM lanes
-// 32*(w%4)..+31; warps 4-7 and 8-11 form two sets).
+// Warp roles (640 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
+// warp 2 TMEM allocator, warps 4..19 dequant + epilogue.  Dequant warp w owns TMEM lanes
+// 32*(w%4)..+31 (= weight rows of the tile) and belongs to group g = (w-4)/4: for gate/up,
+// g selects the matrix (g&1) and which of the sub-stage's two Q8_0 blocks it converts (g>>1);
+// for down, g selects the sub-stage (each raw stage holds 4).  Sixteen dequant warps (four
+// per scheduler) keep enough independent work in flight to cover shared-memory and TMEM
+// latencies.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT,
 // drains what it issued and returns.
 //
@@ -31,7 +35,8 @@ namespace vfmoe {
 
 using namespace sm100;
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 640;
+constexpr int kDqWarps = 16;
 constexpr int kRawRow = 272;            // 8 Q8_0 blocks = 256 K values
 constexpr int kRawMat = 128 * kRawRow;  // one matrix, one stage
 constexpr int kSA = 4;                  // TMEM A ring slots (K = 64 each)
@@ -98,6 +103,22 @@ __device__ __forceinline__ void q8_two_blocks(const uint32_t (&g)[17], uint32_t 
     for (int c = 0; c < 16; ++c) {
         const int b = 36 + 2 * c;
         v[16 + c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d1);
+    }
+}
+
+// One Q8_0 block of a row -> 16 packed fp16 pairs.  g[0..8] are 9 little-endian words that
+// start at the block's word; HB = 0: d is the low half of g[0] and q[j] is byte 2 + j;
+// HB = 1 (block starts at byte 2 of g[0]): d is the high half of g[0], q[j] is byte 4 + j.
+template <int HB>
+__device__ __forceinline__ void q8_one_block(const uint32_t (&g)[9], uint32_t (&v)[16]) {
+    const __half2 d = __half2half2(__ushort_as_half((unsigned short)(HB ? (g[0] >> 16) : (g[0] & 0xFFFFu))));
+    uint32_t x[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) x[i] = g[i] ^ 0x80808080u;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const int b = 2 + 2 * HB + 2 * c;
+        v[c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d);
     }
 }
 
@@ -170,10 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     if (threadIdx.x == 0) {
         for (int i = 0; i < SW; ++i) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], 8);
+            mbar_init(&raw_empty[i], kDqWarps);
         }
         for (int i = 0; i < kSA; ++i) {
-            mbar_init(&a_full[i], GATEUP ? 8 : 4);
+            mbar_init(&a_full[i], GATEUP ? kDqWarps : 4);
             mbar_init(&a_empty[i], 1);
         }
         for (int i = 0; i < SB; ++i) {
@@ -181,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
             mbar_init(&b_empty[i], 1);
         }
         mbar_init(d_full, 1);
-        mbar_init(d_empty, 8);
+        mbar_init(d_empty, kDqWarps);
         mbar_init(mma_done, 1);
         *abort = 0;
         fence_mbar_init();
@@ -286,38 +307,63 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     } else if (warp >= 4) {
         // ------------------------------------------------------------------ dequant + epilogue
         const int q = warp & 3;            // TMEM lane quarter
-        const int set = (warp - 4) >> 2;   // 0: warps 4-7, 1: warps 8-11
+        const int grp = (warp - 4) >> 2;   // 0..3
         const int r = 32 * q + lane;       // weight row within the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const int mat = GATEUP ? (grp & 1) : 0;
+        const int hb = GATEUP ? (grp >> 1) : 0;
         uint32_t nraw = 0, na = 0, it = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
             for (int kr = 0; kr < KR && ok; ++kr) {
                 const uint32_t rs = nraw % SW;
                 if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
-                const int mat = GATEUP ? set : 0;
                 const uint8_t *row = raw + rs * (MATS * kRawMat) + mat * kRawMat + r * kRawRow;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const bool mine = GATEUP || ((s & 1) == set);
+                    const bool mine = GATEUP || (s == grp);
                     if (mine) {
                         const uint32_t as = na % kSA;
                         if (!(ok = mbar_wait(&a_empty[as], ((na / kSA) & 1) ^ 1, abort))) break;
-                        uint32_t w[20];
+                        const uint32_t tcol = tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32;
+                        if (GATEUP) {
+                            // one block: 9 words at word (17s + 8hb) = 3 x 16 B loads from chunk (68s+32hb)/16
+                            const int c0 = (68 * s + 32 * hb) >> 4;
+                            uint32_t w[12];
 #pragma unroll
-                        for (int c = 0; c < 5; ++c) {
-                            const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 64 * s + 16 * c);
-                            w[4 * c] = v4.x;
-                            w[4 * c + 1] = v4.y;
-                            w[4 * c + 2] = v4.z;
-                            w[4 * c + 3] = v4.w;
+                            for (int c = 0; c < 3; ++c) {
+                                const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 16 * (c0 + c));
+                                w[4 * c] = v4.x;
+                                w[4 * c + 1] = v4.y;
+                                w[4 * c + 2] = v4.z;
+                                w[4 * c + 3] = v4.w;
+                            }
+                            uint32_t g9[9];
+#pragma unroll
+                            for (int j = 0; j < 9; ++j) g9[j] = w[s + j];
+                            uint32_t v[16];
+                            if (hb == 0)
+                                q8_one_block<0>(g9, v);
+                            else
+                                q8_one_block<1>(g9, v);
+                            tmem_st_32x32b_x16(tcol + 16 * hb, v);
+                        } else {
+                            uint32_t w[20];
+#pragma unroll
+                            for (int c = 0; c < 5; ++c) {
+                                const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 64 * s + 16 * c);
+                                w[4 * c] = v4.x;
+                                w[4 * c + 1] = v4.y;
+                                w[4 * c + 2] = v4.z;
+                                w[4 * c + 3] = v4.w;
+                            }
+                            uint32_t g[17];
+#pragma unroll
+                            for (int j = 0; j < 17; ++j) g[j] = w[s + j];
+                            uint32_t v[32];
+                            q8_two_blocks(g, v);
+                            tmem_st_32x32b_x32(tcol, v);
                         }
-                        uint32_t g[17];
-#pragma unroll
-                        for (int j = 0; j < 17; ++j) g[j] = w[s + j];
-                        uint32_t v[32];
-                        q8_two_blocks(g, v);
-                        tmem_st_32x32b_x32(tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32, v);
                         tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
@@ -331,16 +377,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                 ++nraw;
             }
             if (!ok) break;
-            // epilogue
+            // epilogue: 8-column chunks of the N token columns, chunk c handled by group c % 4
             if (!(ok = mbar_wait(d_full, it & 1, abort))) break;
             tc_fence_after();
-            const int item_tile = item / MT;
-            const int4 t = p.tiles[item_tile];
+            const int4 t = p.tiles[item / MT];
             const int ch = (item % MT) * 128 + r;
-            constexpr int HALF = N / 2;
-            const int c_beg = set * HALF;
 #pragma unroll 1
-            for (int c0 = c_beg; c0 < c_beg + HALF; c0 += 8) {
+            for (int c0 = 8 * grp; c0 < N; c0 += 32) {
                 if (c0 >= t.z) break;
                 uint32_t dg[8];
                 tmem_ld_32x32b_x8(tmem + lane_base + c0, dg);
