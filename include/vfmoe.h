@@ -124,6 +124,17 @@ int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max);
 int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out,
                 int64_t workspace, int64_t ws_bytes, int64_t stream);
 
+/* Router with no device allocation, for hosts that cannot call cudaMalloc at routing
+ * time (it may synchronize the device, and it fails once the host has reserved all of
+ * device memory in its own pool).  No counterpart in the reference.  Same result as
+ * vfmoe_route.  Scratch is a fixed VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES device array inside
+ * the library, held on every GPU that loads it until exit; larger T is rejected with
+ * VFMOE_ERR_UNSUPPORTED (about T <= 4000 at E = 256).  The first call on a device looks
+ * up the array's address; make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race. */
+#define VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES (4 << 20)
+int vfmoe_route_noalloc(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out, int64_t stream);
+
 /* Full MoE layer: out = sum_l w[t,l] * FFN_{idx[t,l]}(x[t]) + FFN_shared(x[t]),
  * FFN = clamped SwiGLU (moe_ref.py:81-112).  idx_out / w_out may be 0.
  * Replaces moe_route + moe_act + moe_down (moe.vyb:32-170) and tail_site's

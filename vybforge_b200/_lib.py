@@ -59,6 +59,7 @@ _SIGS = {
     "vfmoe_layer_destroy": (C.c_int, [I64]),
     "vfmoe_workspace_bytes": (I64, [I64, I64]),
     "vfmoe_route": (C.c_int, [I64] * 8),
+    "vfmoe_route_noalloc": (C.c_int, [I64] * 6),
     "vfmoe_forward": (C.c_int, [I64] * 9),
     "vfmoe_check_device_error": (C.c_int, [I64, I64]),
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),

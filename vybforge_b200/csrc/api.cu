@@ -521,3 +521,31 @@ int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, in
 }
 
 }  // extern "C"
+
+namespace vfmoe {
+
+// Router into a caller-provided device scratch range (no allocation, no workspace layout):
+// router logits/partials, then the per-expert counts.  Used by vfmoe_route_noalloc.
+int route_into_scratch(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out, char *scratch,
+                       int64_t scratch_bytes, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    const int64_t logit_bytes = align_up(router_logit_floats((int)T, L->H, L->E) * 4, 256);
+    const int64_t need = logit_bytes + align_up((L->E + 2) * 4, 256);
+    if (need > scratch_bytes) {
+        set_error("vfmoe_route_noalloc: T=%lld needs %lld bytes of router scratch; the static scratch holds %lld "
+                  "(use vfmoe_route with a workspace for this size)",
+                  (long long)T, (long long)need, (long long)scratch_bytes);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t *counts = reinterpret_cast<int32_t *>(scratch + logit_bytes);
+    VF_CUDA(cudaMemsetAsync(counts, 0, (L->E + 2) * sizeof(int32_t), st));
+    return launch_router(reinterpret_cast<const void *>(x), (int)L->d.x_dtype,
+                         reinterpret_cast<const float *>(L->d.router_w), L->nw,
+                         reinterpret_cast<const float *>(L->d.router_bias), (int)T, L->H, L->E, L->k,
+                         L->d.routed_scale, reinterpret_cast<float *>(scratch), reinterpret_cast<int32_t *>(idx_out),
+                         reinterpret_cast<float *>(w_out), counts, L->dev_err, st);
+}
+
+}  // namespace vfmoe
