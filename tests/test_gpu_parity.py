@@ -245,3 +245,54 @@ def test_router_prefill_size_bit_exact():
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
     layer.check_device_error()
+
+
+# ----------------------------------------------------------------------------- decode GEMV vs tcgen05 GEMM
+def _layer_with_env(built, var):
+    os.environ[var] = "1"
+    try:
+        return built.make_layer(torch.float32)
+    finally:
+        del os.environ[var]
+
+
+@pytest.mark.parametrize("T", [1, 32])
+def test_decode_gemv_matches_tcgen05_gemm(c1, T):
+    """The decode path (register-operand MMA GEMV) and the tcgen05 GEMM forced onto the
+    same decode shapes compute the same fp16 operands; they differ in accumulation order."""
+    x = c1.x_dev[:T].contiguous()
+    gv = c1.layer.forward(x).cpu().numpy()
+    tc = _layer_with_env(c1, "VFMOE_DECODE_TC").forward(x).cpu().numpy()
+    torch.cuda.synchronize()
+    c1.layer.check_device_error()
+    print(f"[gemv-vs-tcgen05 c1 T={T}] rel-L2 {rel_l2(gv, tc):.3e}")
+    assert rel_l2(gv, tc) < 5e-4
+
+
+def test_c0_prefill_size_tcgen05_path(c0):
+    """T=256 at C0 shapes: 64 tokens per routed expert on average -> tcgen05 GEMM path."""
+    cfg = synth.config("c0", tokens=256)
+    b = Built(cfg)
+    out, idx, w = b.layer.moe_block(b.x_dev)
+    ro, ri, rw = b.oracle()
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    o = out.cpu().numpy()
+    print(f"[parity c0 T=256 tcgen05] max-abs {np.abs(o - ro).max():.3e} rel-L2 {rel_l2(o, ro):.3e}")
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
+    b.layer.check_device_error()
+
+
+def test_c1_prefill_1024_tcgen05_path():
+    """T=1024 at C1 shapes (32 tokens per routed expert on average -> tcgen05 GEMM):
+    routing bit-exact for all tokens, output checked on a token subset."""
+    moe.init(0)
+    b = Built(synth.config("c1", tokens=1024), weights="cuda")
+    out, idx, w = b.layer.moe_block(b.x_dev)
+    ri, rw = orc.route(b.x, b.w_r, b.bias, b.cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    sub = np.array([0, 511, 1023])
+    ro, _, _ = b.oracle(sub)
+    o = out.cpu().numpy()[sub]
+    print(f"[parity c1 T=1024 tcgen05 tokens {sub.tolist()}] max-abs {np.abs(o - ro).max():.3e} rel-L2 {rel_l2(o, ro):.3e}")
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
+    b.layer.check_device_error()

@@ -1,0 +1,311 @@
+// Decode expert GEMV (few tokens per expert): TMA-fed, register-operand tensor-core MMA.
+//
+//   gate/up:  act[rows, ch] = fp16(swiglu(x . Wg[ch], x . Wu[ch]))  (moe.vyb:98-134)
+//   down:     y[rows, ch]   = act . Wd[ch]                          (moe.vyb:137-170)
+//
+// At decode every Q8_0 weight byte is used by only a handful of tokens, so the kernel is
+// HBM-bound: its job is to stream the weights once at full bandwidth.  A tcgen05 MMA
+// reads its whole A tile from TMEM or shared memory per instruction; at N <= 32 tokens
+// that operand traffic, not HBM, becomes the limit.  Here the dequantized weights go from
+// registers straight into mma.sync m16n8k16 (fp16 x fp16 -> fp32), so weights are read
+// from shared memory exactly once, as raw Q8_0 bytes.
+//
+// Data path per CTA (one per SM, persistent over (expert, token tile, channel tile)):
+//   warp 8       TMA producer: per stage, 8 Q8_0 blocks (272 B) of each weight row of the
+//                tile plus the 256-K slice of the tile's N token rows (fp16, SWIZZLE_128B).
+//   warps 0..7   consumers, 16 weight rows each: LDS raw bytes -> fp16(d*q) fragments in
+//                registers -> mma.sync against token fragments -> fp32 accumulators.
+//                gate/up tile = 64 channels x (gate, up): warps 0-3 gate, 4-7 up, SwiGLU
+//                after an exchange through shared memory; down tile = 128 channels.
+// K permutation: within each 64-K pair of Q8_0 blocks, thread (g, c) of the MMA quad owns
+// actual k in [16c, 16c + 16) for both A and B, so each thread converts 16 consecutive
+// quants of a row and loads 32 consecutive token bytes.
+//
+// Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT and exits
+// after draining its TMA loads.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "expert_tc.h"
+#include "sm100.cuh"
+
+namespace vfmoe {
+
+using namespace sm100;
+
+constexpr int kGvConsumers = 8;
+constexpr int kGvThreads = 32 * (kGvConsumers + 1);
+constexpr int kRow = 272;            // 8 Q8_0 blocks (256 K) of one weight row
+constexpr int kWBytes = 128 * kRow;  // weights per stage: 64 rows x 2 matrices or 128 rows
+
+template <bool GATEUP, int NT>
+struct GvCfg {
+    static constexpr int N = 8 * NT;
+    static constexpr int ROWS = GATEUP ? 64 : 128;  // channels per tile
+    static constexpr int TOK = N * 512;             // N rows x 256 K fp16
+    static constexpr int STAGE = kWBytes + TOK;
+    static constexpr int XCH = GATEUP ? ROWS * N * 4 : 0;
+    static constexpr int SW = (230000 - XCH - 1024) / STAGE > 6 ? 6 : (230000 - XCH - 1024) / STAGE;
+    static constexpr int SMEM = SW * STAGE + XCH + 2 * SW * 8 + 16 + 1024;
+    static_assert(SW >= 2, "at least double buffering");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t q8_pair16(uint32_t word, uint32_t sel, __half2 d2) {
+    const uint32_t h = __byte_perm(word, 0x64646464u, sel);  // 1024 + (q ^ 0x80) per half
+    __half2 v = *reinterpret_cast<const __half2 *>(&h);
+    v = __hsub2(v, __half2half2(__ushort_as_half(0x6480)));  // exact q
+    v = __hmul2(v, d2);                                      // fp16(d * q), one rounding
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// 16 consecutive quants of one row inside a 64-K pair (thread c of the quad) -> 8 fp16
+// pairs.  `row` points at the row's 272-byte stage slice, p = pair (0..3), c = 0..3.
+// Quants start at byte 68p + 34*(c>>1) + 2 + 16*(c&1); the scale d at 68p + 34*(c>>1).
+__device__ __forceinline__ void q8_frag(const uint8_t *row, int p, int c, uint32_t (&out)[8]) {
+    const int blk = 68 * p + 34 * (c >> 1);
+    const int qb = blk + 2 + 16 * (c & 1);            // first quant byte (2 mod 4 for c<2)
+    const int w0 = qb >> 2;                            // aligned word holding it
+    const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
+    uint32_t w[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) w[i] = rw[w0 + i];
+    const uint32_t dw = rw[blk >> 2];
+    const unsigned short dbits = (blk & 2) ? (unsigned short)(dw >> 16) : (unsigned short)(dw & 0xFFFFu);
+    const __half2 d2 = __half2half2(__ushort_as_half(dbits));
+    const int sh = qb & 3;                             // 0 or 2
+    uint32_t q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = (sh ? __funnelshift_r(w[i], w[i + 1], 16) : w[i]) ^ 0x80808080u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[2 * i] = q8_pair16(q[i], 0x4140u, d2);
+        out[2 * i + 1] = q8_pair16(q[i], 0x4342u, d2);
+    }
+}
+
+template <bool GATEUP, int NT>
+__global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_constant__ TcParams p) {
+    using C = GvCfg<GATEUP, NT>;
+    constexpr int SW = C::SW, N = C::N, ROWS = C::ROWS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *xch = reinterpret_cast<float *>(smem + SW * C::STAGE);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + SW * C::STAGE + C::XCH);
+    uint64_t *empty = full + SW;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + SW);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int MT = p.M / ROWS;
+    const int KR = p.K / 256;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SW; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kGvConsumers);
+        }
+        *abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int n_items = (*p.n_tiles) * MT;
+
+    if (warp == kGvConsumers) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tmap(&p.wa);
+            prefetch_tmap(&p.swa);
+            prefetch_tmap(&p.xt);
+            uint32_t n = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int4 t = p.tiles[item / MT];
+                const int m0 = (item % MT) * ROWS;
+                const bool sh = t.x == p.E;
+                const CUtensorMap *ma = sh ? &p.swa : &p.wa;
+                const CUtensorMap *mb = sh ? &p.swb : &p.wb;
+                const int z = sh ? 0 : t.x;
+                for (int kr = 0; kr < KR; ++kr, ++n) {
+                    const uint32_t s = n % SW;
+                    if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort))) break;
+                    uint8_t *st = smem + s * C::STAGE;
+                    mbar_arrive_expect_tx(&full[s], C::STAGE);
+                    tma_load_3d(st, ma, &full[s], kr * (kRow / 2), m0, z);
+                    if (GATEUP) tma_load_3d(st + ROWS * kRow, mb, &full[s], kr * (kRow / 2), m0, z);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[s], kr * 256 + 64 * q, t.y);
+                }
+            }
+            if (!ok) {
+                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+                int dummy = 0;
+                for (uint32_t i = (n > (uint32_t)SW ? n - SW : 0); i < n; ++i)
+                    mbar_wait(&full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ consumers
+        const int g = lane >> 2, c = lane & 3;
+        const int mat = GATEUP ? (warp >> 2) : 0;
+        const int r0 = GATEUP ? 16 * (warp & 3) : 16 * warp;  // first row of this warp in its matrix tile
+        uint32_t n = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+            const int4 t = p.tiles[item / MT];
+            const int m0 = (item % MT) * ROWS;
+            const int ntv = (t.z + 7) >> 3;                     // n8 tiles with valid token rows
+            float acc[NT][4];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+            for (int kr = 0; kr < KR; ++kr, ++n) {
+                const uint32_t s = n % SW;
+                if (!(ok = mbar_wait(&full[s], (n / SW) & 1, abort))) break;
+                const uint8_t *st = smem + s * C::STAGE;
+                const uint8_t *rowA = st + (mat * ROWS + r0 + g) * kRow;
+                const uint8_t *rowB = rowA + 8 * kRow;
+#pragma unroll
+                for (int pq = 0; pq < 4; ++pq) {
+                    uint32_t wa[8], wb[8];
+                    q8_frag(rowA, pq, c, wa);
+                    q8_frag(rowB, pq, c, wb);
+                    const uint8_t *tq = st + kWBytes + pq * (N * 128);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        if (j < ntv) {
+                            // token row 8j+g, 16-byte chunks 2c and 2c+1 (SWIZZLE_128B: chunk ^ (row & 7))
+                            const int rr = 8 * j + g;
+                            const uint4 x0 = *reinterpret_cast<const uint4 *>(tq + rr * 128 + (((2 * c) ^ (rr & 7)) << 4));
+                            const uint4 x1 = *reinterpret_cast<const uint4 *>(tq + rr * 128 + (((2 * c + 1) ^ (rr & 7)) << 4));
+                            const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                            for (int s4 = 0; s4 < 4; ++s4) {
+                                const uint32_t a[4] = {wa[2 * s4], wb[2 * s4], wa[2 * s4 + 1], wb[2 * s4 + 1]};
+                                mma_16816(acc[j], a, xb[2 * s4], xb[2 * s4 + 1]);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            if (!ok) break;
+            // ---------------------------------------------------------------- epilogue
+            // acc[j]: rows r0+g (0,1) and r0+g+8 (2,3) x tokens 8j+2c, 8j+2c+1
+            if (GATEUP) {
+                if (mat == 1) {
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                            xch[rr * N + tok] = acc[j][e];
+                        }
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(32 * kGvConsumers) : "memory");
+                if (mat == 0) {
+                    __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                            if (tok < t.z) {
+                                const float a = swiglu_clamped(acc[j][e], xch[rr * N + tok], p.limit);
+                                out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = __float2half_rn(a);
+                            }
+                        }
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(32 * kGvConsumers) : "memory");
+            } else {
+                float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                        if (tok < t.z) out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = acc[j][e];
+                    }
+            }
+        }
+        if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+    }
+}
+
+template <bool GATEUP, int NT>
+static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
+    using C = GvCfg<GATEUP, NT>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        VF_CUDA(cudaFuncSetAttribute(expert_gemv_mma<GATEUP, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done = true;
+    }
+    expert_gemv_mma<GATEUP, NT><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+    VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_mma<gate_up>" : "expert_gemv_mma<down>");
+    return VFMOE_OK;
+}
+
+int gemv_tokens_per_tile(int T, int k, int E) {
+    const double avg = (double)T * k / E;
+    int nt = 1;
+    while (8 * nt < 2 * avg && nt < 4) nt <<= 1;
+    return 8 * nt;
+}
+
+int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
+                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn) {
+    const int N = gemv_tokens_per_tile(a.T, a.k, a.E);
+    TcParams g{};
+    g.wa = plan.gate64;
+    g.wb = plan.up64;
+    g.swa = plan.sh_gate64;
+    g.swb = plan.sh_up64;
+    g.xt = tok_gu;
+    g.tiles = a.tiles;
+    g.n_tiles = a.tile_counts;
+    g.E = a.E;
+    g.K = a.H;
+    g.M = a.I;
+    g.ld_out = a.I;
+    g.out = a.act;
+    g.limit = a.limit;
+    g.err = a.err;
+    const int grid = plan.num_sms;
+    int rc;
+    switch (N) {
+        case 8: rc = launch_gv<true, 1>(g, grid, st); break;
+        case 16: rc = launch_gv<true, 2>(g, grid, st); break;
+        default: rc = launch_gv<true, 4>(g, grid, st); break;
+    }
+    if (rc) return rc;
+    mid();
+    TcParams dn{};
+    dn.wa = plan.down;
+    dn.wb = plan.down;
+    dn.swa = plan.sh_down;
+    dn.swb = plan.sh_down;
+    dn.xt = tok_dn;
+    dn.tiles = a.tiles;            // same token tiles as gate/up (same N)
+    dn.n_tiles = a.tile_counts;
+    dn.E = a.E;
+    dn.K = a.I;
+    dn.M = a.H;
+    dn.ld_out = a.H;
+    dn.out = a.y;
+    dn.limit = a.limit;
+    dn.err = a.err;
+    switch (N) {
+        case 8: return launch_gv<false, 1>(dn, grid, st);
+        case 16: return launch_gv<false, 2>(dn, grid, st);
+        default: return launch_gv<false, 4>(dn, grid, st);
+    }
+}
+
+}  // namespace vfmoe

@@ -58,18 +58,6 @@ struct TcCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-struct TcParams {
-    CUtensorMap wa, wb, swa, swb;   // weights: routed A/B matrices, shared A/B (3D u16 maps)
-    CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B
-    const int4 *tiles;              // {expert, row0, nrows, 0}
-    const int32_t *n_tiles;
-    int E, K, M;
-    int ld_out;
-    void *out;
-    float limit;
-    int *err;
-};
-
 // ----------------------------------------------------------------------------- dequant
 // 68 bytes = two Q8_0 blocks (K = 64) of one weight row -> 32 packed fp16 pairs
 // (column c holds k = 2c in the low half, 2c + 1 in the high half), value fp16(d * q).
@@ -434,7 +422,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 // Q8_0 matrix stack [experts][rows][row_bytes] as u16 elements; box = 128 rows x 272 B.
 static int make_q8_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k, int64_t experts,
-                       int64_t expert_stride) {
+                       int64_t expert_stride, int box_rows = 128) {
     auto enc = get_encode();
     if (!enc) {
         set_error("cuTensorMapEncodeTiled unavailable from the driver");
@@ -444,7 +432,7 @@ static int make_q8_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k
     if (experts <= 1) expert_stride = rows * row_bytes;
     cuuint64_t dims[3] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)rows, (cuuint64_t)experts};
     cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)expert_stride};
-    cuuint32_t box[3] = {kRawRow / 2, 128, 1};
+    cuuint32_t box[3] = {kRawRow / 2, (cuuint32_t)box_rows, 1};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(base), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -493,6 +481,11 @@ int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     if ((rc = make_q8_map(&plan.sh_gate, (void *)(sh ? d.sh_gate.data : d.gate.data), I, H, 1, 0))) return rc;
     if ((rc = make_q8_map(&plan.sh_up, (void *)(sh ? d.sh_up.data : d.up.data), I, H, 1, 0))) return rc;
     if ((rc = make_q8_map(&plan.sh_down, (void *)(sh ? d.sh_down.data : d.down.data), H, I, 1, 0))) return rc;
+    if ((rc = make_q8_map(&plan.gate64, (void *)d.gate.data, I, H, E, d.gate.expert_stride, 64))) return rc;
+    if ((rc = make_q8_map(&plan.up64, (void *)d.up.data, I, H, E, d.up.expert_stride, 64))) return rc;
+    if ((rc = make_q8_map(&plan.sh_gate64, (void *)(sh ? d.sh_gate.data : d.gate.data), I, H, 1, 0, 64))) return rc;
+    if ((rc = make_q8_map(&plan.sh_up64, (void *)(sh ? d.sh_up.data : d.up.data), I, H, 1, 0, 64))) return rc;
+    plan.decode_tc = getenv("VFMOE_DECODE_TC") != nullptr;
     plan.ready = 1;
     return VFMOE_OK;
 }
@@ -525,10 +518,21 @@ static int launch_one(const TcParams &prm, int grid, cudaStream_t st) {
 }
 
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
+    const int64_t rows = (int64_t)a.T * a.k + a.T;
+    if ((double)a.T * a.k / a.E <= 16.0 && !plan.decode_tc) {
+        // decode: register-operand GEMV, one token-tile size for both GEMMs
+        const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
+        tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, ng, ng, a.tiles, a.tiles_cap, a.tile_counts);
+        VF_LAUNCH_CHECK("tc_plan_kernel");
+        CUtensorMap tg, td;
+        int rc;
+        if ((rc = make_tok_map(&tg, a.xp, rows, a.H, ng))) return rc;
+        if ((rc = make_tok_map(&td, a.act, rows, a.I, ng))) return rc;
+        return launch_experts_gemv(plan, a, st, mid, tg, td);
+    }
     const int n = pick_n(a.T, a.k, a.E);
     const int n_gu = std::min(n, 128);
     const int n_dn = n;
-    const int64_t rows = (int64_t)a.T * a.k + a.T;
     tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap,
                                        a.tile_counts);
     VF_LAUNCH_CHECK("tc_plan_kernel");

@@ -10,14 +10,35 @@ namespace vfmoe {
 struct TcPlan {
     int ready = 0;
     int num_sms = 0;
+    int decode_tc = 0;  // 1: use the tcgen05 GEMM for decode shapes too (VFMOE_DECODE_TC at create)
     // Q8_0 weight tensor maps (3D: [experts][rows][row bytes as u16]).
     CUtensorMap gate, up, down;          // routed, stacked
     CUtensorMap sh_gate, sh_up, sh_down; // shared expert (one "expert")
+    // 64-row boxes for the decode GEMV's gate/up tiles
+    CUtensorMap gate64, up64, sh_gate64, sh_up64;
+};
+
+// Kernel parameters shared by the tcgen05 GEMM and the decode GEMV (passed __grid_constant__).
+struct TcParams {
+    CUtensorMap wa, wb, swa, swb;   // weights: routed A/B matrices, shared A/B (3D u16 maps)
+    CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B
+    const int4 *tiles;              // {expert, row0, nrows, 0}
+    const int32_t *n_tiles;
+    int E, K, M;
+    int ld_out;
+    void *out;
+    float limit;
+    int *err;
 };
 
 int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan);
 bool tc_supported(const TcPlan &plan, const MoeArgs &a);
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
+
+// Decode path (few tokens per expert): TMA + register-operand MMA GEMV (expert_gemv.cu).
+int gemv_tokens_per_tile(int T, int k, int E);
+int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
+                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn);
 
 // Workspace the tensor-core path needs beyond MoeArgs: tile lists for both GEMMs.
 int64_t tc_tiles_capacity(int T, int k, int E);
