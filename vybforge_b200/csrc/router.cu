@@ -27,6 +27,8 @@
 namespace vfmoe {
 
 constexpr int kMaxCand = 64;
+constexpr int kMaxH = 16384;     // router_refine keeps x_t in shared memory (fp32)
+constexpr int kMaxChunks = 32;   // L1 decode partial-sum chunks (H / 512)
 
 __device__ __forceinline__ void two_sum(float a, float b, float &s, float &t) {
     s = a + b;
@@ -60,11 +62,43 @@ __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__res
     constexpr int J = KCH / 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kc = blockIdx.y, k0 = kc * KCH;
-    for (int i = threadIdx.x * 4; i < T * KCH; i += 1024) {
-        const int t = i / KCH, kk = i % KCH;
-        float v[4];
-        ld_x4(x, x_dtype, (int64_t)t * H + k0 + kk, v);
-        *reinterpret_cast<float4 *>(xs + i) = make_float4(v[0], v[1], v[2], v[3]);
+    // stage x[0..T)[chunk] as fp32: all loads of a thread are issued before any store
+    {
+        constexpr int PER = (TB * KCH / 8 + 255) / 256;  // 8-element groups per thread
+        uint4 raw[PER];
+        float4 rawf[2 * PER];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int gi = (threadIdx.x + 256 * i) * 8;
+            const int t = gi / KCH, kk = gi % KCH;
+            if (t < T) {
+                if (x_dtype == VFMOE_DT_BF16) {
+                    raw[i] = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H + k0 + kk);
+                } else {
+                    const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + (int64_t)t * H + k0 + kk);
+                    rawf[2 * i] = src[0];
+                    rawf[2 * i + 1] = src[1];
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int gi = (threadIdx.x + 256 * i) * 8;
+            if (gi / KCH < T) {
+                float4 a, b;
+                if (x_dtype == VFMOE_DT_BF16) {
+                    a = make_float4(__uint_as_float(raw[i].x << 16), __uint_as_float(raw[i].x & 0xFFFF0000u),
+                                    __uint_as_float(raw[i].y << 16), __uint_as_float(raw[i].y & 0xFFFF0000u));
+                    b = make_float4(__uint_as_float(raw[i].z << 16), __uint_as_float(raw[i].z & 0xFFFF0000u),
+                                    __uint_as_float(raw[i].w << 16), __uint_as_float(raw[i].w & 0xFFFF0000u));
+                } else {
+                    a = rawf[2 * i];
+                    b = rawf[2 * i + 1];
+                }
+                *reinterpret_cast<float4 *>(xs + gi) = a;
+                *reinterpret_cast<float4 *>(xs + gi + 4) = b;
+            }
+        }
     }
     const int e0 = blockIdx.x * 16 + warp * 2;
     float4 w4[2][J];
@@ -201,6 +235,7 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
                                                      int T, int H, int E, int k, float c1, float c2, double scale,
                                                      int32_t *__restrict__ idx_out, float *__restrict__ w_out,
                                                      int32_t *__restrict__ counts, int *__restrict__ err) {
+    extern __shared__ float s_x[];  // [H] fp32 copy of x_t
     __shared__ float s_red[8];
     __shared__ int s_cand[kMaxCand];
     __shared__ double s_logit[kMaxCand];   // L2/L3 logit, then the choice (score + bias)
@@ -213,12 +248,27 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // |x_t|_2 (upper bound)
+    // x_t -> shared memory as fp32 (all loads issued first) and |x_t|_2 (upper bound)
     float ss = 0.f;
-    for (int h = threadIdx.x * 4; h < H; h += 1024) {
-        float v[4];
-        ld_x4(x, x_dtype, (int64_t)t * H + h, v);
-        ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
+    {
+        float4 v[kMaxH / 1024];
+#pragma unroll
+        for (int i = 0; i < kMaxH / 1024; ++i) {
+            const int h = threadIdx.x * 4 + 1024 * i;
+            if (h < H) {
+                float a[4];
+                ld_x4(x, x_dtype, (int64_t)t * H + h, a);
+                v[i] = make_float4(a[0], a[1], a[2], a[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxH / 1024; ++i) {
+            const int h = threadIdx.x * 4 + 1024 * i;
+            if (h < H) {
+                *reinterpret_cast<float4 *>(s_x + h) = v[i];
+                ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
+            }
+        }
     }
     ss = warp_sum_f32(ss);
     if (lane == 0) s_red[warp] = ss;
@@ -235,8 +285,14 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
         for (int j = 0; j < NPL; ++j) {
             const int e = lane + 32 * j;
             if (e < E) {
+                float pv[kMaxChunks];
+#pragma unroll
+                for (int c = 0; c < kMaxChunks; ++c)
+                    pv[c] = c < nchunk ? logits[((int64_t)c * T + t) * E + e] : 0.f;
                 float l = 0.f;
-                for (int c = 0; c < nchunk; ++c) l += logits[((int64_t)c * T + t) * E + e];
+#pragma unroll
+                for (int c = 0; c < kMaxChunks; ++c)
+                    if (c < nchunk) l += pv[c];
                 const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
                 ca[j] = 1.f / (1.f + expf(-l)) + bias[e];
                 if (isnan(ca[j])) ca[j] = -INFINITY;
@@ -303,25 +359,37 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
         float shi[8], slo[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) shi[c] = slo[c] = 0.f;
-        for (int h = threadIdx.x * 4; h < H; h += 1024) {
-            float xv[4];
-            ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
-            float4 w4[8];
+        int ec[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) ec[c] = (c0 + c < nc) ? s_cand[c0 + c] : -1;
+        for (int hb = 0; hb < H; hb += 3072) {          // 3 float4 per candidate per batch
+            float4 w4[8][3];
 #pragma unroll
             for (int c = 0; c < 8; ++c)
-                w4[c] = (c0 + c < nc) ? *reinterpret_cast<const float4 *>(wr + (int64_t)s_cand[c0 + c] * H + h)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float wv[4] = {w4[c].x, w4[c].y, w4[c].z, w4[c].w};
+                for (int j = 0; j < 3; ++j) {
+                    const int h = hb + threadIdx.x * 4 + 1024 * j;
+                    w4[c][j] = (ec[c] >= 0 && h < H) ? *reinterpret_cast<const float4 *>(wr + (int64_t)ec[c] * H + h)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float p = xv[i] * wv[i];
-                    const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
-                    float sum, r;
-                    two_sum(shi[c], p, sum, r);
-                    shi[c] = sum;
-                    slo[c] += r + pe;
+            for (int j = 0; j < 3; ++j) {
+                const int h = hb + threadIdx.x * 4 + 1024 * j;
+                if (h >= H) break;
+                const float4 x4 = *reinterpret_cast<const float4 *>(s_x + h);
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float wv[4] = {w4[c][j].x, w4[c][j].y, w4[c][j].z, w4[c][j].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float p = xv[i] * wv[i];
+                        const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
+                        float sum, r;
+                        two_sum(shi[c], p, sum, r);
+                        shi[c] = sum;
+                        slo[c] += r + pe;
+                    }
                 }
             }
         }
@@ -397,8 +465,8 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
 #pragma unroll
             for (int c = 0; c < 8; ++c) acc[c] = 0.0;
             for (int h = threadIdx.x * 4; h < H; h += 1024) {
-                float xv[4];
-                ld_x4(x, x_dtype, (int64_t)t * H + h, xv);
+                const float4 x4 = *reinterpret_cast<const float4 *>(s_x + h);
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     if (c0 + c < nc && s_redo[c0 + c]) {
@@ -518,8 +586,24 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     const int n2 = H / 256;
     const float c2 = gamma_bound(2 * n2 + 24) * (float)(n2 + 1 + 24) * 5.9604645e-8f;
     const int npl = (int)cdiv(E, 32);
+    if (H > kMaxH || H / 512 > kMaxChunks) {
+        set_error("router: hidden size %d exceeds %d", H, kMaxH);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    if (H * 4 > 48 * 1024) {
+        static bool attr = false;
+        if (!attr) {
+            VF_CUDA(cudaFuncSetAttribute(router_refine<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            attr = true;
+        }
+    }
 #define VF_REFINE(NPL)                                                                                          \
-    router_refine<NPL><<<(unsigned)T, 256, 0, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, E, k, c1, c2, \
+    router_refine<NPL><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, E, k, c1, c2, \
                                                     scale, idx, w, counts, err)
     if (npl <= 1) VF_REFINE(1);
     else if (npl <= 2) VF_REFINE(2);
