@@ -61,6 +61,7 @@ def args_parse():
     ap.add_argument("--experts", type=int, default=None,
                     help="override the routed expert count (small cases for ncu captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the extra T=1 and prefill measurements")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     return ap.parse_args()
 
@@ -165,6 +166,77 @@ def cpu_baseline_ours(cfg, host, dev, idx, budget_s):
                       f"dequant+f64 GEMM per expert, numpy/OpenBLAS on {cores} host threads, {dt:.1f} s"}
 
 
+def time_layer(layer, xd, steps, warmup, flush, with_profile=True):
+    """Device time per forward (CUDA events on the launch stream, L2 flushed between steps),
+    per-stage times from the library's event marks and the kernel launch count."""
+    import ctypes as C
+    import torch
+    st = torch.cuda.current_stream()
+    T = xd.shape[0]
+    out = torch.empty((T, layer.H), dtype=layer.out_dtype, device="cuda")
+    idx = torch.empty((T, layer.k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, layer.k), dtype=torch.float32, device="cuda")
+    ws = layer.workspace(T)
+    for _ in range(max(3, warmup)):
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+    torch.cuda.synchronize()
+    lib = layer.lib
+    if with_profile:
+        lib.vfmoe_profile_enable(layer.handle, 1)
+        lib.vfmoe_profile_read(layer.handle, (C.c_double * 8)(), 8, None)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(st)
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+        ev[i][1].record(st)
+    torch.cuda.synchronize()
+    ms = float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+    stage = (C.c_double * 8)()
+    launches = C.c_int64(0)
+    nf = max(1, lib.vfmoe_profile_read(layer.handle, stage, 8, C.byref(launches))) if with_profile else 1
+    lib.vfmoe_profile_enable(layer.handle, 0)
+    names = ["router", "dispatch_gather", "gate_up", "down", "combine"]
+    return ms, {n: stage[i] / nf for i, n in enumerate(names)}, int(launches.value), idx
+
+
+def prefill_extra(a, cfg1, dev, flush):
+    """C3: T=4096 prefill, Zipf(1.1)-skewed routing, same Q8_0 expert weights as C1."""
+    import torch
+    from vybforge_b200 import synth
+    from vybforge_b200.moe import MoELayer
+    cfg = synth.config("c3", tokens=4096)
+    x, w_r, bias, tgt, _ = synth.zipf_router_inputs(cfg)
+    E = cfg.n_experts
+    layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
+                     router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
+                     gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
+                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    ms, stages, launches, idx = time_layer(layer, xd, max(5, a.steps // 2), a.warmup, flush)
+    T, H, I, k = cfg.tokens, cfg.hidden, cfg.inter, cfg.topk
+    rows = T * k + T
+    flops = 6.0 * H * I * rows + 2.0 * H * E * T
+    gu_flops, dn_flops = 4.0 * H * I * rows, 2.0 * H * I * rows
+    pk, pk_kind = peaks()
+    cnt = np.bincount(idx.cpu().numpy().reshape(-1), minlength=E)
+    gu_tf = gu_flops / (stages["gate_up"] * 1e-3) / 1e12
+    dn_tf = dn_flops / (stages["down"] * 1e-3) / 1e12
+    layer.close()
+    return {"workload": "c3: prefill T=4096, Zipf(1.1) routing, Q8_0, same layer shapes as c1",
+            "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+            "layer_tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "roofline": {"bound": "tensor", "kernel": "expert gate/up grouped GEMM (tcgen05, Q8_0 -> fp16 in TMEM)",
+                         "achieved": round(gu_tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(gu_tf / pk["bf16_tflops"], 4),
+                         "frac_of_sustained": round(gu_tf / pk.get("bf16_tflops_sustained", pk["bf16_tflops"]), 4),
+                         "down_achieved": round(dn_tf, 1), "peak_source": pk_kind,
+                         "algorithmic_flops_per_launch": gu_flops},
+            "stage_ms_per_step": {n: round(v, 4) for n, v in stages.items()}, "gpu_launches": launches,
+            "expert_tokens": {"max": int(cnt.max()), "median": float(np.median(cnt)), "min": int(cnt.min()),
+                              "zipf_target_max": float(tgt.max())}}
+
+
 def run_ours(a, rank, world, local_rank):
     import torch
     from vybforge_b200 import synth, _lib
@@ -265,6 +337,16 @@ def run_ours(a, rank, world, local_rank):
            "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                    "h2d_bytes_per_step": T * cfg.hidden * 2, "d2h_bytes_per_step": T * cfg.hidden * 2,
                    "ms_per_step": round(e2e_ms, 4)}}
+    if not a.no_extra and a.workload == "c1" and a.tokens is None and not a.experts:
+        extra = {}
+        ms1, st1, _, idx1 = time_layer(layer, xd[:1].contiguous(), a.steps, a.warmup, flush)
+        l1b, gu1b = algorithmic_bytes(synth.config("c1", tokens=1), len(np.unique(idx1.cpu().numpy())))
+        extra["c1_t1"] = {"tokens_per_s": round(1 / (ms1 * 1e-3), 1), "ms_per_step": round(ms1, 4),
+                          "gate_up_hbm_frac": round(gu1b / (st1["gate_up"] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                          "layer_hbm_frac": round(l1b / (ms1 * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                          "stage_ms_per_step": {n: round(v, 4) for n, v in st1.items()}}
+        extra["c3_prefill_q8_0"] = prefill_extra(a, cfg, dev, flush)
+        res["extra"] = extra
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_ours(cfg, host, dev, idx_np, a.cpu_budget_s)
     return res

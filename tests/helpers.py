@@ -28,9 +28,13 @@ def to_dev_x(x, cfg):
 class Built:
     """A device layer + host-side copies for the oracle."""
 
-    def __init__(self, cfg, weights="numpy", out_dtype=torch.float32, zipf=False):
+    def __init__(self, cfg, weights="numpy", out_dtype=torch.float32, router=None):
         self.cfg = cfg
-        x, w_r, bias, rng = synth.router_inputs(cfg)
+        if router is None:
+            x, w_r, bias, rng = synth.router_inputs(cfg)
+        else:
+            x, w_r, bias = router
+            rng = np.random.default_rng(cfg.seed)
         self.x, self.w_r, self.bias = x, w_r, bias
         H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
         if weights == "numpy":

@@ -296,3 +296,27 @@ def test_c1_prefill_1024_tcgen05_path():
     print(f"[parity c1 T=1024 tcgen05 tokens {sub.tolist()}] max-abs {np.abs(o - ro).max():.3e} rel-L2 {rel_l2(o, ro):.3e}")
     assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
     b.layer.check_device_error()
+
+
+def test_c3_zipf_prefill_parity():
+    """BASELINE C3: T=4096 prefill with Zipf(1.1)-skewed routing (the hottest expert gets
+    ~4000 tokens, the tail a handful).  Routing bit-exact for every token; output within
+    tolerance on tokens of the hottest and of a tail expert."""
+    moe.init(0)
+    cfg = synth.config("c3", tokens=4096)
+    x, w_r, bias, tgt, _ = synth.zipf_router_inputs(cfg)
+    b = Built(cfg, weights="cuda", router=(x, w_r, bias))
+    out, idx, w = b.layer.moe_block(b.x_dev)
+    ri, rw = orc.route(x, w_r, bias, cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    cnt = np.bincount(ri.reshape(-1), minlength=cfg.n_experts)
+    assert cnt.max() > 3000                                   # skew reached the kernels
+    hot, cold = int(np.argmax(cnt)), int(np.argmin(np.where(cnt > 0, cnt, 10**9)))
+    toks = sorted({int(np.nonzero((ri == hot).any(1))[0][-1]), int(np.nonzero((ri == cold).any(1))[0][0]), 2048})
+    sub = np.array(toks)
+    ro, _, _ = b.oracle(sub)
+    o = out.cpu().numpy()[sub]
+    print(f"[parity c3 zipf T=4096 tokens {toks}] max-abs {np.abs(o - ro).max():.3e} rel-L2 {rel_l2(o, ro):.3e}")
+    assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
+    b.layer.check_device_error()

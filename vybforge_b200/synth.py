@@ -127,6 +127,21 @@ def calibrate_zipf_bias(logits, base_bias, topk, targets, iters=400):
     return b.astype(np.float32)
 
 
+def zipf_router_inputs(cfg: LayerConfig):
+    """x, W_r and a selection bias whose realized expert popularity on these tokens follows
+    Zipf(cfg.zipf_s) over a seeded random rank order (BASELINE C3/C4 prefill).
+
+    x and W_r are the config's ordinary draws; the bias starts from the ordinary
+    N(0, 0.01) draw and is calibrated on the f64 logits of these very tokens, so the
+    router itself is the unmodified reference router (selection-only bias).
+    Returns (x, w_r, bias, targets, rng)."""
+    x, w_r, bias0, rng = router_inputs(cfg)
+    logits = x.astype(np.float64) @ w_r.astype(np.float64).T
+    tgt = zipf_targets(cfg.n_experts, cfg.tokens, cfg.topk, cfg.zipf_s, np.random.default_rng(cfg.seed + 7))
+    bias = calibrate_zipf_bias(logits, bias0, cfg.topk, tgt)
+    return x, w_r, bias, tgt, rng
+
+
 def realized_counts(idx, n_experts):
     return np.bincount(np.asarray(idx).reshape(-1), minlength=n_experts)
 
