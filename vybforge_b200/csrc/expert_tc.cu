@@ -111,7 +111,8 @@ __device__ __forceinline__ void q8_one_block(const uint32_t (&g)[9], uint32_t (&
 }
 
 // ----------------------------------------------------------------------------- plan
-// Token tiles of N rows for every expert segment (routed experts ascending, then shared).
+// Token tiles of at most N rows for every expert segment (routed experts ascending, then
+// shared); an expert's rows are split into equal-size tiles.
 __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict__ offsets, int E, int has_shared,
                                                        int n_gu, int n_dn, int4 *__restrict__ tiles, int64_t cap,
                                                        int32_t *__restrict__ counts) {
@@ -143,9 +144,14 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict
         for (int i = 0; i < per; ++i) {
             const int e = tid * per + i;
             if (e < nexp) {
+                // ceil(n / N) tiles of near-equal size (no mostly-empty tail tile)
                 const int r0 = offsets[e], n = offsets[e + 1] - r0;
-                for (int j = 0; j * N < n; ++j) {
-                    if (pos < cap) out[pos] = make_int4(e, r0 + j * N, min(N, n - j * N), 0);
+                const int nt = (n + N - 1) / N;
+                int row = r0;
+                for (int j = 0; j < nt; ++j) {
+                    const int rows = n / nt + (j < n % nt ? 1 : 0);
+                    if (pos < cap) out[pos] = make_int4(e, row, rows, 0);
+                    row += rows;
                     ++pos;
                 }
             }
@@ -234,11 +240,14 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                     tma_load_3d(dst, ma, &raw_full[rs], kr * (kRawRow / 2), m0, z);
                     if (GATEUP) tma_load_3d(dst + kRawMat, mb, &raw_full[rs], kr * (kRawRow / 2), m0, z);
                     ++nraw;
+                    const int n16 = (t.z + 15) >> 4;  // 16-row token boxes actually needed
                     for (int s = 0; s < 4; ++s) {
                         const uint32_t bs = ntok % SB;
                         if (!(ok = mbar_wait(&b_empty[bs], ((ntok / SB) & 1) ^ 1, abort))) break;
-                        mbar_arrive_expect_tx(&b_full[bs], C::TOK_STAGE);
-                        tma_load_2d(tok + bs * C::TOK_STAGE, &p.xt, &b_full[bs], kr * 256 + 64 * s, t.y);
+                        mbar_arrive_expect_tx(&b_full[bs], n16 * 16 * 128);
+                        for (int b = 0; b < n16; ++b)
+                            tma_load_2d(tok + bs * C::TOK_STAGE + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s,
+                                        t.y + 16 * b);
                         ++ntok;
                     }
                 }
@@ -256,10 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(128, N);
             uint32_t na = 0, ntok = 0, it = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+                const int ntok_rows = p.tiles[item / MT].z;
+                const uint32_t idesc = idesc_f16_f32(128, 16 * ((ntok_rows + 15) >> 4));  // N = rows rounded to 16
                 if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
                 tc_fence_after();
                 for (int kr = 0; kr < KR && ok; ++kr) {
@@ -542,7 +552,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     g.wb = plan.up;
     g.swa = plan.sh_gate;
     g.swb = plan.sh_up;
-    if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, n_gu))) return rc;
+    if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, 16))) return rc;
     g.tiles = a.tiles;
     g.n_tiles = a.tile_counts;
     g.E = a.E;
@@ -566,7 +576,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     dn.wb = plan.down;
     dn.swa = plan.sh_down;
     dn.swb = plan.sh_down;
-    if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, n_dn))) return rc;
+    if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, 16))) return rc;
     dn.tiles = a.tiles + a.tiles_cap;
     dn.n_tiles = a.tile_counts + 1;
     dn.E = a.E;

@@ -144,69 +144,112 @@ __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__res
 }
 
 // ----------------------------------------------------------------------------- L1, prefill
-// 64 tokens x 64 experts per CTA, 256 threads x (4 x 4) outputs, K in chunks of 32;
-// each chunk is summed separately then added to the running total, so the summation
-// depth is 32 + H/32.
+// 128 tokens x 64 experts per CTA, 256 threads x (8 tokens x 4 experts), K in chunks of 32
+// staged k-major in shared memory (float4 reads: 3 per 32 FMAs); the next chunk is loaded
+// into registers while the current one is consumed.  Each chunk is summed on its own and
+// then added to the running total, so the summation depth is 32 + H/32.
 __global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__restrict__ x, int x_dtype,
                                                                const float *__restrict__ wr, int T, int H, int E,
                                                                float *__restrict__ logits) {
-    constexpr int BT = 64, BE = 64, KC = 32;
-    __shared__ float xs[KC][BT + 4];
-    __shared__ float ws[KC][BE + 4];
+    constexpr int BT = 128, BE = 64, KC = 32;
+    __shared__ __align__(16) float xs[KC][BT];
+    __shared__ __align__(16) float ws[KC][BE];
     const int t0 = blockIdx.y * BT, e0 = blockIdx.x * BE;
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    for (int kb = 0; kb < H; kb += KC) {
-        // 64 rows x 32 k per operand = 2048 values, 8 per thread (two float4 / bf16x4 loads)
+    const int tx = tid & 15, ty = tid >> 4;  // experts e0 + 4tx .. +3, tokens t0 + 8ty .. +7
+    // loader mapping: x tile 128 rows x 32 k = 512 groups of 8 k (2 per thread);
+    // w tile 64 rows x 32 k = 512 float4 (2 per thread)
+    float xr[2][8], wv[2][4];
+    auto load = [&](int kb) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int idx = tid + r * 256;       // 512 groups of 4 k
-            const int row = idx >> 3, kq = (idx & 7) * 4;
-            const int t = t0 + row, e = e0 + row;
-            float xv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (t < T) ld_x4(x, x_dtype, (int64_t)t * H + kb + kq, xv);
-            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < E) w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)e * H + kb + kq);
-            xs[kq][row] = xv[0]; xs[kq + 1][row] = xv[1]; xs[kq + 2][row] = xv[2]; xs[kq + 3][row] = xv[3];
-            ws[kq][row] = w4.x; ws[kq + 1][row] = w4.y; ws[kq + 2][row] = w4.z; ws[kq + 3][row] = w4.w;
-        }
-        __syncthreads();
-        float part[4][4];
+            const int gi = tid + 256 * r;
+            const int row = gi >> 2, kq = (gi & 3) * 8;
+            const int t = t0 + row;
+            if (t < T) {
+                if (x_dtype == VFMOE_DT_BF16) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(x) +
+                                                                     (int64_t)t * H + kb + kq);
+                    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+                    for (int i = 0; i < 4; ++i) {
+                        xr[r][2 * i] = __uint_as_float(uu[i] << 16);
+                        xr[r][2 * i + 1] = __uint_as_float(uu[i] & 0xFFFF0000u);
+                    }
+                } else {
+                    const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) +
+                                                                         (int64_t)t * H + kb + kq);
+                    const float4 a = src[0], b = src[1];
+                    xr[r][0] = a.x; xr[r][1] = a.y; xr[r][2] = a.z; xr[r][3] = a.w;
+                    xr[r][4] = b.x; xr[r][5] = b.y; xr[r][6] = b.z; xr[r][7] = b.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xr[r][i] = 0.f;
+            }
+            const int erow = gi >> 3, ek = (gi & 7) * 4;
+            const int e = e0 + erow;
+            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < E) w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)e * H + kb + ek);
+            wv[r][0] = w4.x; wv[r][1] = w4.y; wv[r][2] = w4.z; wv[r][3] = w4.w;
+        }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int gi = tid + 256 * r;
+            const int row = gi >> 2, kq = (gi & 3) * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xs[kq + i][row] = xr[r][i];
+            const int erow = gi >> 3, ek = (gi & 7) * 4;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) ws[ek + i][erow] = wv[r][i];
+        }
+    };
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    load(0);
+    for (int kb = 0; kb < H; kb += KC) {
+        __syncthreads();
+        store();
+        __syncthreads();
+        if (kb + KC < H) load(kb + KC);
+        float part[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) part[i][j] = 0.f;
-#pragma unroll 8
+#pragma unroll 4
         for (int kk = 0; kk < KC; ++kk) {
-            float xr[4], wc[4];
+            const float4 xa = *reinterpret_cast<const float4 *>(&xs[kk][8 * ty]);
+            const float4 xb = *reinterpret_cast<const float4 *>(&xs[kk][8 * ty + 4]);
+            const float4 w4 = *reinterpret_cast<const float4 *>(&ws[kk][4 * tx]);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const float wc[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xr[i] = xs[kk][ty + 16 * i];
+            for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wc[j] = ws[kk][tx + 16 * j];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) part[i][j] = fmaf(xr[i], wc[j], part[i][j]);
+                for (int j = 0; j < 4; ++j) part[i][j] = fmaf(xv[i], wc[j], part[i][j]);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[i][j] += part[i][j];
-        __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int t = t0 + ty + 16 * i;
+    for (int i = 0; i < 8; ++i) {
+        const int t = t0 + 8 * ty + i;
         if (t >= T) continue;
+        if (e0 + 4 * tx + 3 < E) {
+            *reinterpret_cast<float4 *>(logits + (int64_t)t * E + e0 + 4 * tx) =
+                make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = e0 + tx + 16 * j;
-            if (e < E) logits[(int64_t)t * E + e] = acc[i][j];
+            for (int j = 0; j < 4; ++j)
+                if (e0 + 4 * tx + j < E) logits[(int64_t)t * E + e0 + 4 * tx + j] = acc[i][j];
         }
     }
 }
@@ -574,7 +617,7 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
         if (rc) return rc;
         c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
-        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 64));
+        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 128));
         router_logits_f32_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
         VF_LAUNCH_CHECK("router_logits_f32_tiled");
         c1 = gamma_bound(32 + H / 32);
