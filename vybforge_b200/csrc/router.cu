@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(256) row_norms_kernel(const float *__restrict_
 
 // ----------------------------------------------------------------------------- L2 + L3
 // One CTA (256 threads) per token.  NPL = experts per lane (E <= 32 * NPL).
-template <int NPL>
-__global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x, int x_dtype,
+template <int NPL, int CPP, int MINB>
+__global__ void __launch_bounds__(256, MINB) router_refine(const void *__restrict__ x, int x_dtype,
                                                      const float *__restrict__ wr, const float *__restrict__ logits,
                                                      int nchunk,
                                                      const float *__restrict__ nw, const float *__restrict__ bias,
@@ -291,25 +291,46 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // x_t -> shared memory as fp32 (all loads issued first) and |x_t|_2 (upper bound)
+    // x_t -> shared memory as fp32 (16-byte loads, issued four at a time) and |x_t|_2 (upper bound)
     float ss = 0.f;
-    {
-        float4 v[kMaxH / 1024];
+    if (x_dtype == VFMOE_DT_BF16) {
+        for (int i0 = 0; i0 < kMaxH / 2048; i0 += 4) {
+            uint4 u[4];
 #pragma unroll
-        for (int i = 0; i < kMaxH / 1024; ++i) {
-            const int h = threadIdx.x * 4 + 1024 * i;
-            if (h < H) {
-                float a[4];
-                ld_x4(x, x_dtype, (int64_t)t * H + h, a);
-                v[i] = make_float4(a[0], a[1], a[2], a[3]);
+            for (int i = 0; i < 4; ++i) {
+                const int h = (threadIdx.x + 256 * (i0 + i)) * 8;
+                if (h < H) u[i] = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H + h);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int h = (threadIdx.x + 256 * (i0 + i)) * 8;
+                if (h < H) {
+                    const float4 a = make_float4(__uint_as_float(u[i].x << 16), __uint_as_float(u[i].x & 0xFFFF0000u),
+                                                 __uint_as_float(u[i].y << 16), __uint_as_float(u[i].y & 0xFFFF0000u));
+                    const float4 b = make_float4(__uint_as_float(u[i].z << 16), __uint_as_float(u[i].z & 0xFFFF0000u),
+                                                 __uint_as_float(u[i].w << 16), __uint_as_float(u[i].w & 0xFFFF0000u));
+                    *reinterpret_cast<float4 *>(s_x + h) = a;
+                    *reinterpret_cast<float4 *>(s_x + h + 4) = b;
+                    ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+                    ss = fmaf(b.x, b.x, fmaf(b.y, b.y, fmaf(b.z, b.z, fmaf(b.w, b.w, ss))));
+                }
             }
         }
+    } else {
+        for (int i0 = 0; i0 < kMaxH / 1024; i0 += 4) {
+            float4 f[4];
 #pragma unroll
-        for (int i = 0; i < kMaxH / 1024; ++i) {
-            const int h = threadIdx.x * 4 + 1024 * i;
-            if (h < H) {
-                *reinterpret_cast<float4 *>(s_x + h) = v[i];
-                ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
+            for (int i = 0; i < 4; ++i) {
+                const int h = (threadIdx.x + 256 * (i0 + i)) * 4;
+                if (h < H) f[i] = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + (int64_t)t * H + h);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int h = (threadIdx.x + 256 * (i0 + i)) * 4;
+                if (h < H) {
+                    *reinterpret_cast<float4 *>(s_x + h) = f[i];
+                    ss = fmaf(f[i].x, f[i].x, fmaf(f[i].y, f[i].y, fmaf(f[i].z, f[i].z, fmaf(f[i].w, f[i].w, ss))));
+                }
             }
         }
     }
@@ -328,14 +349,15 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
         for (int j = 0; j < NPL; ++j) {
             const int e = lane + 32 * j;
             if (e < E) {
-                float pv[kMaxChunks];
-#pragma unroll
-                for (int c = 0; c < kMaxChunks; ++c)
-                    pv[c] = c < nchunk ? logits[((int64_t)c * T + t) * E + e] : 0.f;
                 float l = 0.f;
+                for (int c0 = 0; c0 < nchunk; c0 += 8) {   // 8 partial loads in flight, summed in chunk order
+                    float pv[8];
 #pragma unroll
-                for (int c = 0; c < kMaxChunks; ++c)
-                    if (c < nchunk) l += pv[c];
+                    for (int c = 0; c < 8; ++c) pv[c] = c0 + c < nchunk ? logits[((int64_t)(c0 + c) * T + t) * E + e] : 0.f;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        if (c0 + c < nchunk) l += pv[c];
+                }
                 const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
                 ca[j] = 1.f / (1.f + expf(-l)) + bias[e];
                 if (isnan(ca[j])) ca[j] = -INFINITY;
@@ -398,17 +420,17 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
     // ---- L2 float-float logits of the candidates: thread owns k = 4*tid + 1024*j + i,
     // 8 candidates per pass (all loads of a pass are independent); then a fixed-order
     // TwoSum tree over lanes and warps.
-    for (int c0 = 0; c0 < nc; c0 += 8) {
-        float shi[8], slo[8];
+    for (int c0 = 0; c0 < nc; c0 += CPP) {
+        float shi[CPP], slo[CPP];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) shi[c] = slo[c] = 0.f;
-        int ec[8];
+        for (int c = 0; c < CPP; ++c) shi[c] = slo[c] = 0.f;
+        int ec[CPP];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) ec[c] = (c0 + c < nc) ? s_cand[c0 + c] : -1;
+        for (int c = 0; c < CPP; ++c) ec[c] = (c0 + c < nc) ? s_cand[c0 + c] : -1;
         for (int hb = 0; hb < H; hb += 3072) {          // 3 float4 per candidate per batch
-            float4 w4[8][3];
+            float4 w4[CPP][3];
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
+            for (int c = 0; c < CPP; ++c)
 #pragma unroll
                 for (int j = 0; j < 3; ++j) {
                     const int h = hb + threadIdx.x * 4 + 1024 * j;
@@ -422,7 +444,7 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
                 const float4 x4 = *reinterpret_cast<const float4 *>(s_x + h);
                 const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < CPP; ++c) {
                     const float wv[4] = {w4[c][j].x, w4[c][j].y, w4[c][j].z, w4[c][j].w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -437,7 +459,7 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
             }
         }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < CPP; ++c) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 const float oh = __shfl_xor_sync(0xffffffffu, shi[c], o);
@@ -453,7 +475,7 @@ __global__ void __launch_bounds__(256) router_refine(const void *__restrict__ x,
             }
         }
         __syncthreads();
-        if (threadIdx.x < 8 && c0 + threadIdx.x < nc) {
+        if (threadIdx.x < CPP && c0 + threadIdx.x < nc) {
             const int c = threadIdx.x;
             float hi = s_phi[0][c], lo = s_plo[0][c];
             for (int w = 1; w < 8; ++w) {
@@ -636,18 +658,30 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     if (H * 4 > 48 * 1024) {
         static bool attr = false;
         if (!attr) {
-            VF_CUDA(cudaFuncSetAttribute(router_refine<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<1, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<1, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<2, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<2, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<4, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<4, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<8, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<8, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<16, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<16, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<32, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
+            VF_CUDA(cudaFuncSetAttribute(router_refine<32, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
             attr = true;
         }
     }
-#define VF_REFINE(NPL)                                                                                          \
-    router_refine<NPL><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, E, k, c1, c2, \
-                                                    scale, idx, w, counts, err)
+#define VF_REFINE(NPL)                                                                                             \
+    do {                                                                                                          \
+        if (T <= 64)                                                                                              \
+            router_refine<NPL, 8, 1><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, \
+                                                                      E, k, c1, c2, scale, idx, w, counts, err);  \
+        else                                                                                                      \
+            router_refine<NPL, 4, 3><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, \
+                                                                      E, k, c1, c2, scale, idx, w, counts, err);  \
+    } while (0)
     if (npl <= 1) VF_REFINE(1);
     else if (npl <= 2) VF_REFINE(2);
     else if (npl <= 4) VF_REFINE(4);
