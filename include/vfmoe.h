@@ -93,6 +93,8 @@ typedef struct vfmoe_layer_desc {
     int64_t router_bias;    /* fp32 [E], e_score_correction_bias (selection only) */
     vfmoe_matrix gate, up, down;          /* routed experts, stacked over E */
     vfmoe_matrix sh_gate, sh_up, sh_down; /* shared expert; sh_gate.data == 0: none */
+    int64_t n_local_experts; /* routed experts whose weights gate/up/down hold; 0 = n_experts.
+                                Fewer on an expert-parallel rank (vfmoe_forward_rows only). */
 } vfmoe_layer_desc;
 
 /* ABI version (VFMOE_ABI_VERSION). */
@@ -142,6 +144,36 @@ int vfmoe_route_noalloc(int64_t handle, int64_t x, int64_t T, int64_t idx_out, i
 int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out,
                   int64_t idx_out, int64_t w_out,
                   int64_t workspace, int64_t ws_bytes, int64_t stream);
+
+/* ---- expert parallelism (no counterpart in the reference, which has no multi-GPU code;
+ * the exchange itself is NCCL all-to-all between these calls) ---- */
+
+/* Bytes of workspace vfmoe_forward_rows needs for up to n_max rows. */
+int64_t vfmoe_rows_workspace_bytes(int64_t handle, int64_t n_max);
+
+/* Expert FFN on arbitrary rows: y_out[i] = FFN_{slots[i]}(rows[i]), fp32 [n, H].  slots
+ * are local expert indices in [0, n_local_experts); slot == n_local_experts selects the
+ * shared expert.  rows: [n, H] bf16 or fp32 (rows_dtype).  The per-expert products are the
+ * ones vfmoe_forward runs (moe.vyb:98-170). */
+int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t slots, int64_t n, int64_t y_out,
+                       int64_t workspace, int64_t ws_bytes, int64_t stream);
+
+/* Send plan of an expert-parallel dispatch: the T*k (token, lane) pairs of idx int32 [T,k]
+ * sorted by owner rank placement[expert] (int32 [n_experts]), stable in t*k+l order.
+ * send_counts int32 [n_ranks]; send_perm int32 [T*k] (slot -> t*k+l); inv_perm int32
+ * [T*k] (t*k+l -> slot).  err_word: device int that records a bad id (may be 0). */
+int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t placement, int64_t n_ranks,
+                  int64_t send_counts, int64_t send_perm, int64_t inv_perm, int64_t err_word, int64_t stream);
+
+/* Pack the send buffer: rows_out[s] = x[send_perm[s] / k] (x dtype, [n_slots, H]) and
+ * slots_out[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index). */
+int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
+                  int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream);
+
+/* Weighted combine: out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] + y_shared[t] (fp32 y rows;
+ * w may be 0 for weight 1, y_shared may be 0).  glm_engine.vyb:2925-2938, :2991. */
+int vfmoe_combine(int64_t y, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H, int64_t y_shared,
+                  int64_t out, int64_t out_dtype, int64_t stream);
 
 /* Synchronize `stream` and report whether any kernel of this handle flagged a
  * device-side error since the last call (VFMOE_ERR_DEVICE), then clear it. */

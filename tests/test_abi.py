@@ -51,7 +51,7 @@ def test_constants_match_header():
 
 def test_descriptor_is_a_block_of_8_byte_words():
     assert C.sizeof(_lib.Matrix) == 6 * 8
-    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6) * 8
+    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6 + 1) * 8
 
 
 def test_version(built_lib):

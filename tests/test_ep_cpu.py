@@ -1,0 +1,153 @@
+"""Expert-parallel orchestration on CPU: 2 gloo ranks (and N virtual ranks) whose per-rank
+compute is the numpy oracle, checked end to end against the single-device oracle.  This
+covers the host logic of vybforge_b200/ep.py (placement, send plan, pack order, all-to-all
+splits, combine) without a GPU; the CUDA kernels of the same steps are covered by
+tests/test_gpu_ep.py."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from vybforge_b200 import ep, synth
+
+
+class NumpyBackend:
+    """Oracle compute for one rank (test infrastructure only)."""
+
+    def __init__(self, cfg, w_r, bias, experts, placement, rank):
+        self.cfg, self.w_r, self.bias = cfg, w_r, bias
+        self.placement = np.asarray(placement)
+        self.local = ep.local_slots(placement)
+        self.my = np.nonzero(self.placement == rank)[0]          # global ids of local slots
+        self.shared_slot = len(self.my)
+        H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+
+        def mats(e):
+            return (orc.q8_0_expert_inout(experts[0][e], I, H), orc.q8_0_expert_inout(experts[1][e], I, H),
+                    orc.q8_0_expert_inout(experts[2][e], H, I))
+        self.mats = {int(e): mats(e) for e in self.my}
+        self.mats[-1] = mats(E)                                  # shared
+
+    def route(self, x):
+        idx, w = orc.route(x.numpy().astype(np.float64), self.w_r, self.bias, self.cfg.topk)
+        return torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w.astype(np.float32))
+
+    def plan(self, idx):
+        flat = idx.numpy().reshape(-1)
+        owner = self.placement[flat]
+        perm = np.argsort(owner, kind="stable").astype(np.int32)
+        inv = np.empty_like(perm)
+        inv[perm] = np.arange(len(perm), dtype=np.int32)
+        counts = np.bincount(owner, minlength=len(np.unique(self.placement))).astype(np.int32)
+        return torch.from_numpy(counts), torch.from_numpy(perm), torch.from_numpy(inv)
+
+    def pack(self, x, idx, perm):
+        k = idx.shape[1]
+        p = perm.numpy()
+        rows = x[torch.from_numpy(p // k).long()]
+        slots = self.local[idx.numpy().reshape(-1)[p]]
+        return rows, torch.from_numpy(slots.astype(np.int32))
+
+    def rows(self, rows, slots):
+        r = rows.numpy().astype(np.float64)
+        s = slots.numpy()
+        y = np.zeros_like(r)
+        for sl in np.unique(s):
+            sel = s == sl
+            key = -1 if sl == self.shared_slot else int(self.my[sl])
+            y[sel] = orc.ffn(r[sel], *self.mats[key])
+        return torch.from_numpy(y)
+
+    def combine(self, y_back, inv, w, T, y_shared):
+        k = self.cfg.topk
+        yb = y_back.numpy()
+        wv = w.numpy().astype(np.float64)
+        out = np.zeros((T, yb.shape[1]))
+        for t in range(T):
+            for l in range(k):
+                out[t] += wv[t, l] * yb[inv[t * k + l]]
+        return torch.from_numpy(out + y_shared.numpy())
+
+
+def _setup(world):
+    cfg = synth.config("c0", tokens=24)
+    x, w_r, bias, rng = synth.router_inputs(cfg)
+    experts = synth.expert_q8_numpy(cfg, rng)
+    idx_all, _ = orc.route(x, w_r, bias, cfg.topk)
+    load = np.bincount(idx_all.reshape(-1), minlength=cfg.n_experts)
+    placement = ep.balanced_placement(load, world)
+    return cfg, x, w_r, bias, experts, placement
+
+
+def _reference(cfg, x, w_r, bias, experts):
+    H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+
+    def mats(e):
+        return (orc.q8_0_expert_inout(experts[0][e], I, H), orc.q8_0_expert_inout(experts[1][e], I, H),
+                orc.q8_0_expert_inout(experts[2][e], H, I))
+    out, _, _ = orc.moe_block_grouped(x, w_r, bias, mats, lambda: mats(E), E, cfg.topk)
+    return out
+
+
+def test_placements():
+    load = np.array([100, 1, 50, 2, 30, 3, 20, 4])
+    p = ep.balanced_placement(load, 2)
+    assert np.bincount(p).tolist() == [4, 4]
+    tot = [load[p == r].sum() for r in range(2)]
+    assert max(tot) - min(tot) <= 40
+    assert ep.contiguous_placement(8, 4).tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
+    assert ep.local_slots(np.array([1, 0, 1, 0])).tolist() == [0, 0, 1, 1]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_virtual_ranks_match_single_device_oracle(world):
+    cfg, x, w_r, bias, experts, placement = _setup(world)
+    shards = np.array_split(np.arange(cfg.tokens), world)
+    ranks = [ep.EpRank(r, world, NumpyBackend(cfg, w_r, bias, experts, placement, r)) for r in range(world)]
+    outs = ep.ep_forward_virtual(ranks, [torch.from_numpy(x[s]) for s in shards], ep.VirtualTransport(world))
+    got = np.concatenate([o.numpy() for o in outs])
+    ref = _reference(cfg, x, w_r, bias, experts)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=1e-6)  # routing weights are fp32, as on the GPU
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg, x, w_r, bias, experts, placement = _setup(world)
+        shard = np.array_split(np.arange(cfg.tokens), world)[rank]
+        r = ep.EpRank(rank, world, NumpyBackend(cfg, w_r, bias, experts, placement, rank))
+        out = ep.ep_forward_dist(r, torch.from_numpy(x[shard]), ep.DistTransport())
+        q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_match_single_device_oracle():
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg, x, w_r, bias, experts, placement = _setup(world)
+    got = np.concatenate([res[r] for r in range(world)])
+    np.testing.assert_allclose(got, _reference(cfg, x, w_r, bias, experts), rtol=0, atol=1e-6)

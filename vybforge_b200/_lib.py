@@ -47,7 +47,7 @@ class LayerDesc(C.Structure):
                 ("out_dtype", C.c_int64), ("routed_scale", C.c_double), ("swiglu_limit", C.c_double),
                 ("router_w", C.c_int64), ("router_bias", C.c_int64),
                 ("gate", Matrix), ("up", Matrix), ("down", Matrix),
-                ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix)]
+                ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix), ("n_local_experts", C.c_int64)]
 
 
 I64 = C.c_int64
@@ -62,6 +62,11 @@ _SIGS = {
     "vfmoe_route_noalloc": (C.c_int, [I64] * 6),
     "vfmoe_forward": (C.c_int, [I64] * 9),
     "vfmoe_check_device_error": (C.c_int, [I64, I64]),
+    "vfmoe_rows_workspace_bytes": (I64, [I64, I64]),
+    "vfmoe_forward_rows": (C.c_int, [I64] * 9),
+    "vfmoe_ep_plan": (C.c_int, [I64] * 11),
+    "vfmoe_ep_pack": (C.c_int, [I64] * 11),
+    "vfmoe_combine": (C.c_int, [I64] * 10),
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),
     "vfmoe_profile_read": (C.c_int, [I64, C.POINTER(C.c_double), I64, C.POINTER(I64)]),
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),

@@ -41,6 +41,7 @@ struct Layer {
     vfmoe_layer_desc d;
     int device = 0;
     int H = 0, I = 0, E = 0, k = 0;
+    int n_local = 0;             // routed experts whose weights this handle holds (E unless expert-parallel)
     int has_shared = 0;
     int64_t q8_row_gate = 0, q8_row_down = 0;
     int *dev_err = nullptr;      // device error word (allocated at create)
@@ -89,34 +90,36 @@ struct WsLayout {
     int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, tiles, tile_counts, tiles_cap, total;
 };
 
-static WsLayout ws_layout(const Layer &L, int64_t T) {
+static WsLayout ws_layout(const Layer &L, int64_t T, int k = -1) {
     WsLayout o{};
-    const int64_t rows = T * L.k + T;
+    if (k < 0) k = L.k;
+    const int64_t rows = T * k + T;
+    const int nb = (L.E > L.n_local ? L.E : L.n_local) + 2;
     int64_t p = 0;
     auto take = [&](int64_t bytes) {
         const int64_t at = p;
         p = align_up(p + bytes, 256);
         return at;
     };
-    o.counts = take((L.E + 2) * 4);
-    o.offsets = take((L.E + 2) * 4);
+    o.counts = take((nb + 1) * 4);
+    o.offsets = take((nb + 1) * 4);
     o.perm_tok = take(rows * 4);
-    o.pos_of = take(T * L.k * 4);
-    o.idx = take(T * L.k * 4);
-    o.w = take(T * L.k * 4);
+    o.pos_of = take(T * k * 4);
+    o.idx = take(T * k * 4);
+    o.w = take(T * k * 4);
     o.part = take(router_logit_floats((int)T, L.H, L.E) * 4);
     o.xp = take(rows * L.H * 2);
     o.act = take(rows * L.I * 2);
     o.y = take(rows * L.H * 4);
-    o.tiles_cap = tc_tiles_capacity((int)T, L.k, L.E);
+    o.tiles_cap = tc_tiles_capacity((int)T, k, L.n_local > L.E ? L.n_local : L.E);
     o.tiles = take(2 * o.tiles_cap * 16);
     o.tile_counts = take(2 * 4);
     o.total = p;
     return o;
 }
 
-static int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **base) {
-    const WsLayout lay = ws_layout(L, T);
+static int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **base, int k = -1) {
+    const WsLayout lay = ws_layout(L, T, k);
     if (ws) {
         if (ws_bytes < lay.total) {
             set_error("workspace too small: %lld < %lld bytes for T=%lld", (long long)ws_bytes,
@@ -162,6 +165,7 @@ static int validate(const vfmoe_layer_desc &d) {
     if (d.hidden <= 0 || d.inter <= 0 || d.n_experts <= 0 || d.topk <= 0) return bad("non-positive shape");
     if (d.hidden % 256 || d.inter % 256) return bad("hidden and inter must be multiples of 256");
     if (d.n_experts > 1024) return bad("n_experts > 1024");
+    if (d.n_local_experts < 0 || d.n_local_experts > 1024) return bad("n_local_experts out of range");
     if (d.topk > 32 || d.topk > d.n_experts) return bad("topk must be <= 32 and <= n_experts");
     if (d.x_dtype != VFMOE_DT_BF16 && d.x_dtype != VFMOE_DT_F32) return bad("x_dtype must be BF16 or F32");
     if (d.out_dtype != VFMOE_DT_BF16 && d.out_dtype != VFMOE_DT_F32) return bad("out_dtype must be BF16 or F32");
@@ -170,8 +174,9 @@ static int validate(const vfmoe_layer_desc &d) {
     if (d.weight_format == VFMOE_WFMT_Q8_0) {
         const int64_t rg = d.hidden / 32 * 34, rd = d.inter / 32 * 34;
         if (!d.gate.data || !d.up.data || !d.down.data) return bad("routed expert weights missing");
-        if (d.n_experts > 1 && (d.gate.expert_stride < d.inter * rg || d.up.expert_stride < d.inter * rg ||
-                                d.down.expert_stride < d.hidden * rd))
+        const int64_t nl = d.n_local_experts ? d.n_local_experts : d.n_experts;
+        if (nl > 1 && (d.gate.expert_stride < d.inter * rg || d.up.expert_stride < d.inter * rg ||
+                       d.down.expert_stride < d.hidden * rd))
             return bad("expert_stride smaller than one expert matrix");
         const int64_t ptrs[6] = {d.gate.data, d.up.data, d.down.data, d.sh_gate.data, d.sh_up.data, d.sh_down.data};
         for (int i = 0; i < 6; ++i)
@@ -237,6 +242,7 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
     L->I = (int)desc->inter;
     L->E = (int)desc->n_experts;
     L->k = (int)desc->topk;
+    L->n_local = (int)(desc->n_local_experts ? desc->n_local_experts : desc->n_experts);
     L->has_shared = desc->sh_gate.data != 0;
     L->q8_row_gate = desc->hidden / 32 * 34;
     L->q8_row_down = desc->inter / 32 * 34;
@@ -346,6 +352,11 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
         set_error("vfmoe_forward: T=%lld exceeds 2^24", (long long)T);
         return VFMOE_ERR_UNSUPPORTED;
     }
+    if (L->n_local != L->E) {
+        set_error("vfmoe_forward: this handle holds %d of %d experts (expert-parallel); use vfmoe_forward_rows",
+                  L->n_local, L->E);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     char *base;
     int rc = ensure_ws(*L, T, workspace, ws_bytes, &base);
@@ -398,7 +409,7 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
     a.tiles_cap = lay.tiles_cap;
 
-    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, perm_tok, pos_of, offsets, L->dev_err, st);
+    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, L->has_shared, perm_tok, pos_of, offsets, L->dev_err, st);
     if (rc) return rc;
     const int64_t rows = T * L->k + (L->has_shared ? T : 0);
     rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
@@ -415,8 +426,8 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     if (rc) return rc;
     nlaunch += 2;
     mark();
-    rc = launch_combine(a.y, pos_of, w, (int)T, L->H, L->k, L->has_shared, reinterpret_cast<void *>(out),
-                        (int)L->d.out_dtype, st);
+    rc = launch_combine(a.y, pos_of, w, (int)T, L->H, L->k, L->has_shared ? a.y + T * L->k * L->H : nullptr,
+                        reinterpret_cast<void *>(out), (int)L->d.out_dtype, st);
     if (rc) return rc;
     nlaunch += 1;
     mark();
@@ -459,6 +470,130 @@ int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *lau
     L->n_fwd = 0;
     L->launches = 0;
     return nf;
+}
+
+int64_t vfmoe_rows_workspace_bytes(int64_t handle, int64_t n_max) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (n_max < 0) {
+        set_error("negative n_max");
+        return VFMOE_ERR_INVALID;
+    }
+    return ws_layout(*L, n_max, 1).total;
+}
+
+int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t slots, int64_t n, int64_t y_out,
+                       int64_t workspace, int64_t ws_bytes, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (n < 0 || (n > 0 && (!rows || !slots || !y_out)) || (rows & 15) ||
+        (rows_dtype != VFMOE_DT_BF16 && rows_dtype != VFMOE_DT_F32)) {
+        set_error("vfmoe_forward_rows: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    if (n == 0) return VFMOE_OK;
+    if (n > (int64_t)1 << 24) {
+        set_error("vfmoe_forward_rows: n=%lld exceeds 2^24", (long long)n);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char *base;
+    int rc = ensure_ws(*L, n, workspace, ws_bytes, &base, 1);
+    if (rc) return rc;
+    const WsLayout lay = ws_layout(*L, n, 1);
+    const int nl = L->n_local;
+    // slot nl = the shared expert: an ordinary bucket of a k = 1 dispatch over nl + 1 buckets
+    const int nb = nl + (L->has_shared ? 1 : 0);
+    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
+    int32_t *offsets = reinterpret_cast<int32_t *>(base + lay.offsets);
+    int32_t *perm_tok = reinterpret_cast<int32_t *>(base + lay.perm_tok);
+    int32_t *pos_of = reinterpret_cast<int32_t *>(base + lay.pos_of);
+    const int32_t *sl = reinterpret_cast<const int32_t *>(slots);
+    VF_CUDA(cudaMemsetAsync(counts, 0, (nb + 2) * sizeof(int32_t), st));
+    if ((rc = launch_count(sl, n, nb, counts, L->dev_err, st))) return rc;
+    if ((rc = launch_dispatch(sl, counts, (int)n, nb, 1, 0, perm_tok, pos_of, offsets, L->dev_err, st))) return rc;
+    MoeArgs a{};
+    a.T = (int)n;
+    a.H = L->H;
+    a.I = L->I;
+    a.E = nl;
+    a.k = 1;
+    a.has_shared = L->has_shared;
+    a.fmt = (int)L->d.weight_format;
+    a.exl3_bits = (int)L->d.exl3_bits;
+    a.limit = (float)L->d.swiglu_limit;
+    a.gate = mref(L->d.gate);
+    a.up = mref(L->d.up);
+    a.down = mref(L->d.down);
+    a.sh_gate = mref(L->d.sh_gate);
+    a.sh_up = mref(L->d.sh_up);
+    a.sh_down = mref(L->d.sh_down);
+    a.offsets = offsets;
+    a.perm_tok = perm_tok;
+    a.xp = reinterpret_cast<__half *>(base + lay.xp);
+    a.act = reinterpret_cast<__half *>(base + lay.act);
+    a.y = reinterpret_cast<float *>(base + lay.y);
+    a.err = L->dev_err;
+    a.tiles = reinterpret_cast<int4 *>(base + lay.tiles);
+    a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
+    a.tiles_cap = lay.tiles_cap;
+    if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n, L->H,
+                            reinterpret_cast<__half *>(base + lay.xp), st)))
+        return rc;
+    if (L->use_tc && tc_supported(L->tc, a))
+        rc = launch_experts_tc(L->tc, a, st, []() {});
+    else
+        rc = launch_experts_simt(a, st, []() {});
+    if (rc) return rc;
+    // back to the callers' row order: y_out[i] = y[pos_of[i]]
+    return launch_combine(a.y, pos_of, nullptr, (int)n, L->H, 1, nullptr, reinterpret_cast<void *>(y_out),
+                          VFMOE_DT_F32, st);
+}
+
+int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t placement, int64_t n_ranks,
+                  int64_t send_counts, int64_t send_perm, int64_t inv_perm, int64_t err_word, int64_t stream) {
+    if (T < 0 || k <= 0 || n_experts <= 0 || n_ranks <= 0 || n_ranks > 1024 || T * k > ((int64_t)1 << 30) ||
+        (T > 0 && (!idx || !placement || !send_counts || !send_perm || !inv_perm))) {
+        set_error("vfmoe_ep_plan: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    if (T == 0) {
+        VF_CUDA(cudaMemsetAsync(reinterpret_cast<void *>(send_counts), 0, n_ranks * 4,
+                                reinterpret_cast<cudaStream_t>(stream)));
+        return VFMOE_OK;
+    }
+    return launch_ep_plan(reinterpret_cast<const int32_t *>(idx), T * k, (int)n_experts,
+                          reinterpret_cast<const int32_t *>(placement), (int)n_ranks,
+                          reinterpret_cast<int32_t *>(send_counts), reinterpret_cast<int32_t *>(send_perm),
+                          reinterpret_cast<int32_t *>(inv_perm), reinterpret_cast<int *>(err_word),
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
+                  int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream) {
+    const int eb = x_dtype == VFMOE_DT_F32 ? 4 : (x_dtype == VFMOE_DT_BF16 || x_dtype == VFMOE_DT_F16 ? 2 : 0);
+    if (!eb || H <= 0 || (H * eb) % 16 || k <= 0 || n_slots < 0 || (x & 15) || (rows_out & 15) ||
+        (n_slots > 0 && (!x || !idx || !send_perm || !local_slot || !rows_out || !slots_out))) {
+        set_error("vfmoe_ep_pack: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_ep_pack(reinterpret_cast<const void *>(x), eb, (int)H, (int)k, reinterpret_cast<const int32_t *>(idx),
+                          reinterpret_cast<const int32_t *>(send_perm), reinterpret_cast<const int32_t *>(local_slot),
+                          n_slots, reinterpret_cast<void *>(rows_out), reinterpret_cast<int32_t *>(slots_out),
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_combine(int64_t y, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H, int64_t y_shared,
+                  int64_t out, int64_t out_dtype, int64_t stream) {
+    if (T < 0 || k <= 0 || k > 32 || H <= 0 || H % 4 || (out_dtype != VFMOE_DT_F32 && out_dtype != VFMOE_DT_BF16) ||
+        (T > 0 && (!y || !pos_of || !out)) || (y & 15) || (y_shared & 15)) {
+        set_error("vfmoe_combine: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_combine(reinterpret_cast<const float *>(y), reinterpret_cast<const int32_t *>(pos_of),
+                          reinterpret_cast<const float *>(w), (int)T, (int)H, (int)k,
+                          reinterpret_cast<const float *>(y_shared), reinterpret_cast<void *>(out), (int)out_dtype,
+                          reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vfmoe_check_device_error(int64_t handle, int64_t stream) {

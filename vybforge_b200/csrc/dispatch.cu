@@ -16,7 +16,7 @@
 namespace vfmoe {
 
 __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict__ idx, const int32_t *__restrict__ counts,
-                                                       int T, int E, int k, int32_t *__restrict__ perm_tok,
+                                                       int T, int E, int k, int has_shared, int32_t *__restrict__ perm_tok,
                                                        int32_t *__restrict__ pos_of, int32_t *__restrict__ offsets,
                                                        int *__restrict__ err) {
     __shared__ int red[8];
@@ -25,10 +25,11 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t tk = (int64_t)T * k;
     if (e == E) {  // shared expert: identity segment after the routed rows
-        for (int t = tid; t < T; t += 256) perm_tok[tk + t] = t;
+        if (has_shared)
+            for (int t = tid; t < T; t += 256) perm_tok[tk + t] = t;
         if (tid == 0) {
             offsets[E] = (int32_t)tk;
-            offsets[E + 1] = (int32_t)(tk + T);
+            offsets[E + 1] = (int32_t)(tk + (has_shared ? T : 0));
         }
         return;
     }
@@ -112,16 +113,17 @@ __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x,
 // weights are staged in shared memory so the k row loads are independent of each other.
 __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
                                                       const float *__restrict__ w, int T, int H, int k,
-                                                      int has_shared, void *__restrict__ out, int out_dtype) {
+                                                      const float *__restrict__ y_shared, void *__restrict__ out,
+                                                      int out_dtype) {
     __shared__ int64_t sp[33];
     __shared__ float sw[32];
     const int t = blockIdx.x;
     const int64_t tk = (int64_t)T * k;
     if (threadIdx.x < k) {
         sp[threadIdx.x] = (int64_t)pos_of[(int64_t)t * k + threadIdx.x] * H;
-        sw[threadIdx.x] = w[(int64_t)t * k + threadIdx.x];
+        sw[threadIdx.x] = w ? w[(int64_t)t * k + threadIdx.x] : 1.0f;
     }
-    if (threadIdx.x == 32) sp[32] = (tk + t) * H;
+    (void)tk;
     __syncthreads();
     const int c = (blockIdx.y * 256 + threadIdx.x) * 4;
     if (c >= H) return;
@@ -135,8 +137,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
         acc.z = fmaf(wl, v.z, acc.z);
         acc.w = fmaf(wl, v.w, acc.w);
     }
-    if (has_shared) {
-        const float4 v = *reinterpret_cast<const float4 *>(y + sp[32] + c);
+    if (y_shared) {
+        const float4 v = *reinterpret_cast<const float4 *>(y_shared + (int64_t)t * H + c);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -154,9 +156,105 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
     }
 }
 
-int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
+// Per-bucket counts of n ids in [0, nb): counts[b] += 1 (caller zeroes counts).
+__global__ void count_kernel(const int32_t *__restrict__ ids, int64_t n, int nb, int32_t *__restrict__ counts,
+                             int *__restrict__ err) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int b = ids[i];
+    if (b >= 0 && b < nb)
+        atomicAdd(&counts[b], 1);
+    else
+        raise_dev_error(err, DEV_BAD_EXPERT_ID);
+}
+
+// Expert-parallel send plan (one CTA, 1024 threads): the T*k (token, lane) pairs, stably
+// sorted by owner rank placement[idx] (flat index t*k+l ascending within a rank).
+// send_perm[slot] = flat index, inv_perm[flat] = slot, send_counts[rank].
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ idx, int64_t n, int E,
+                                                       const int32_t *__restrict__ placement, int n_ranks,
+                                                       int32_t *__restrict__ send_counts, int32_t *__restrict__ send_perm,
+                                                       int32_t *__restrict__ inv_perm, int *__restrict__ err) {
+    __shared__ int warp_tot[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int base = 0;
+    for (int r = 0; r < n_ranks; ++r) {
+        int running = 0;
+        for (int64_t c = 0; c < n; c += 1024) {
+            const int64_t i = c + tid;
+            bool hit = false;
+            if (i < n) {
+                const int e = idx[i];
+                const int owner = (e >= 0 && e < E) ? placement[e] : -1;
+                if (owner < 0 || owner >= n_ranks) {
+                    if (r == 0) raise_dev_error(err, DEV_BAD_EXPERT_ID);
+                } else {
+                    hit = owner == r;
+                }
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) warp_tot[warp] = __popc(m);
+            __syncthreads();
+            int before = 0, total = 0;
+            for (int w = 0; w < 32; ++w) {
+                const int v = warp_tot[w];
+                before += w < warp ? v : 0;
+                total += v;
+            }
+            if (hit) {
+                const int slot = base + running + before + __popc(m & ((1u << lane) - 1u));
+                send_perm[slot] = (int32_t)i;
+                inv_perm[i] = slot;
+            }
+            running += total;
+            __syncthreads();
+        }
+        if (tid == 0) send_counts[r] = running;
+        base += running;
+    }
+}
+
+// Send rows for the expert-parallel exchange: rows[s] = x[send_perm[s] / k] (same dtype),
+// slots[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index).
+__global__ void __launch_bounds__(128) ep_pack_kernel(const void *__restrict__ x, int elt_bytes, int H, int k,
+                                                      const int32_t *__restrict__ idx, const int32_t *__restrict__ send_perm,
+                                                      const int32_t *__restrict__ local_slot, void *__restrict__ rows,
+                                                      int32_t *__restrict__ slots) {
+    const int64_t s = blockIdx.x;
+    const int flat = send_perm[s];
+    const int t = flat / k;
+    if (threadIdx.x == 0) slots[s] = local_slot[idx[flat]];
+    const int64_t row_bytes = (int64_t)H * elt_bytes;
+    const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(x) + (int64_t)t * row_bytes);
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(rows) + s * row_bytes);
+    for (int64_t i = threadIdx.x; i < row_bytes / 16; i += 128) dst[i] = src[i];
+}
+
+int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st) {
+    if (n == 0) return VFMOE_OK;
+    count_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(ids, n, nb, counts, err);
+    VF_LAUNCH_CHECK("count_kernel");
+    return VFMOE_OK;
+}
+
+int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placement, int n_ranks, int32_t *send_counts,
+                   int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st) {
+    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, n, E, placement, n_ranks, send_counts, send_perm, inv_perm, err);
+    VF_LAUNCH_CHECK("ep_plan_kernel");
+    return VFMOE_OK;
+}
+
+int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
+                   const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st) {
+    if (n_slots == 0) return VFMOE_OK;
+    ep_pack_kernel<<<(unsigned)n_slots, 128, 0, st>>>(x, elt_bytes, H, k, idx, send_perm, local_slot, rows, slots);
+    VF_LAUNCH_CHECK("ep_pack_kernel");
+    return VFMOE_OK;
+}
+
+int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st) {
-    dispatch_kernel<<<E + 1, 256, 0, st>>>(idx, counts, T, E, k, perm_tok, pos_of, offsets, err);
+    dispatch_kernel<<<E + 1, 256, 0, st>>>(idx, counts, T, E, k, has_shared, perm_tok, pos_of, offsets, err);
     VF_LAUNCH_CHECK("dispatch_kernel");
     return VFMOE_OK;
 }
@@ -169,11 +267,11 @@ int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t r
     return VFMOE_OK;
 }
 
-int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, int has_shared,
+int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, const float *y_shared,
                    void *out, int out_dtype, cudaStream_t st) {
     if (T == 0) return VFMOE_OK;
     dim3 grid((unsigned)T, (unsigned)cdiv(H, 1024));
-    combine_kernel<<<grid, 256, 0, st>>>(y, pos_of, w, T, H, k, has_shared, out, out_dtype);
+    combine_kernel<<<grid, 256, 0, st>>>(y, pos_of, w, T, H, k, y_shared, out, out_dtype);
     VF_LAUNCH_CHECK("combine_kernel");
     return VFMOE_OK;
 }

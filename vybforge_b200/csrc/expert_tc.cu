@@ -115,7 +115,7 @@ __device__ __forceinline__ void q8_one_block(const uint32_t (&g)[9], uint32_t (&
 // shared); an expert's rows are split into equal-size tiles.
 __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict__ offsets, int E, int has_shared,
                                                        int n_gu, int n_dn, int4 *__restrict__ tiles, int64_t cap,
-                                                       int32_t *__restrict__ counts) {
+                                                       int32_t *__restrict__ counts, int *__restrict__ err) {
     __shared__ int sc[2][1024];
     const int tid = threadIdx.x;
     const int nexp = E + (has_shared ? 1 : 0);
@@ -156,7 +156,10 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict
                 }
             }
         }
-        if (tid == 1023) counts[which] = (int32_t)(sc[which][1023] < cap ? sc[which][1023] : cap);
+        if (tid == 1023) {
+            counts[which] = (int32_t)(sc[which][1023] < cap ? sc[which][1023] : cap);
+            if (sc[which][1023] > cap) raise_dev_error(err, DEV_BAD_COUNT);
+        }
         __syncthreads();
     }
 }
@@ -482,7 +485,7 @@ int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     int dev = 0;
     VF_CUDA(cudaGetDevice(&dev));
     VF_CUDA(cudaDeviceGetAttribute(&plan.num_sms, cudaDevAttrMultiProcessorCount, dev));
-    const int64_t H = d.hidden, I = d.inter, E = d.n_experts;
+    const int64_t H = d.hidden, I = d.inter, E = d.n_local_experts ? d.n_local_experts : d.n_experts;
     int rc;
     if ((rc = make_q8_map(&plan.gate, (void *)d.gate.data, I, H, E, d.gate.expert_stride))) return rc;
     if ((rc = make_q8_map(&plan.up, (void *)d.up.data, I, H, E, d.up.expert_stride))) return rc;
@@ -504,7 +507,8 @@ bool tc_supported(const TcPlan &plan, const MoeArgs &a) {
     return plan.ready && a.fmt == VFMOE_WFMT_Q8_0 && a.tiles != nullptr && a.H % 256 == 0 && a.I % 256 == 0;
 }
 
-int64_t tc_tiles_capacity(int T, int k, int E) { return ((int64_t)T * k + T) / 16 + E + 2; }
+// Tiles of at least 8 rows (the decode GEMV's smallest): sum_e ceil(n_e / 8) <= rows / 8 + segments.
+int64_t tc_tiles_capacity(int T, int k, int E) { return ((int64_t)T * k + T) / 8 + E + 2; }
 
 static int pick_n(int T, int k, int E) {
     const double avg = (double)T * k / E;
@@ -532,7 +536,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     if ((double)a.T * a.k / a.E <= 16.0 && !plan.decode_tc) {
         // decode: register-operand GEMV, one token-tile size for both GEMMs
         const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
-        tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, ng, ng, a.tiles, a.tiles_cap, a.tile_counts);
+        tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, ng, ng, a.tiles, a.tiles_cap, a.tile_counts, a.err);
         VF_LAUNCH_CHECK("tc_plan_kernel");
         CUtensorMap tg, td;
         int rc;
@@ -544,7 +548,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     const int n_gu = std::min(n, 128);
     const int n_dn = n;
     tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap,
-                                       a.tile_counts);
+                                       a.tile_counts, a.err);
     VF_LAUNCH_CHECK("tc_plan_kernel");
     int rc;
     TcParams g{};

@@ -42,11 +42,16 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
 int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t st);
 int64_t router_logit_floats(int T, int H, int E);
 
-int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int32_t *perm_tok,
+int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);
+int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st);
+int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placement, int n_ranks, int32_t *send_counts,
+                   int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st);
+int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
+                   const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st);
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
                   cudaStream_t st);
-int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, int has_shared,
+int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, const float *y_shared,
                    void *out, int out_dtype, cudaStream_t st);
 
 // `mid` runs between the gate/up and the down launches (profiling marks).

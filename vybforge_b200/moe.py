@@ -48,13 +48,15 @@ class MoELayer:
 
     def __init__(self, *, hidden, inter, n_experts, topk, router_w, router_bias, gate, up, down,
                  shared=None, fmt="q8_0", exl3_bits=3, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
-                 scale=2.5, limit=10.0):
+                 scale=2.5, limit=10.0, n_local_experts=0):
         self.lib = _lib.load()
         self.H, self.I, self.E, self.k = hidden, inter, n_experts, topk
         self.x_dtype, self.out_dtype = x_dtype, out_dtype
         self.fmt = fmt
         d = _lib.LayerDesc()
         d.hidden, d.inter, d.n_experts, d.topk = hidden, inter, n_experts, topk
+        d.n_local_experts = n_local_experts
+        self.n_local = n_local_experts or n_experts
         d.weight_format = WFMT_Q8_0 if fmt == "q8_0" else WFMT_EXL3
         d.exl3_bits = exl3_bits
         d.x_dtype, d.out_dtype = _DT[x_dtype], _DT[out_dtype]
@@ -84,6 +86,7 @@ class MoELayer:
         self.desc = d
         self.handle = check(self.lib.vfmoe_layer_create(C.byref(d)))
         self._ws = None
+        self._rows_ws = None
 
     # ------------------------------------------------------------------ workspace
     def workspace_bytes(self, T: int) -> int:
@@ -123,6 +126,18 @@ class MoELayer:
         out = self.forward(x, idx=idx, w=w)
         return out, idx, w
 
+    def forward_rows(self, rows: torch.Tensor, slots: torch.Tensor, y: torch.Tensor | None = None):
+        """y[i] = FFN_{slots[i]}(rows[i]) in fp32; slot n_local = shared expert."""
+        n = rows.shape[0]
+        if y is None:
+            y = torch.empty((n, self.H), dtype=torch.float32, device=rows.device)
+        need = check(self.lib.vfmoe_rows_workspace_bytes(self.handle, n))
+        if self._rows_ws is None or self._rows_ws.numel() < need:
+            self._rows_ws = torch.empty(need, dtype=torch.uint8, device=rows.device)
+        check(self.lib.vfmoe_forward_rows(self.handle, _ptr(rows), _DT[rows.dtype], _ptr(slots), n, _ptr(y),
+                                          _ptr(self._rows_ws), self._rows_ws.numel(), _stream()))
+        return y
+
     def check_device_error(self):
         check(self.lib.vfmoe_check_device_error(self.handle, _stream()))
 
@@ -153,6 +168,37 @@ def q8_0_dequant(src_u8: torch.Tensor, rows: int, k: int, dtype=torch.float32) -
 def exl3_decode(trellis: torch.Tensor, K: int, N: int, bits: int) -> torch.Tensor:
     out = torch.empty((K, N), dtype=torch.float16, device=trellis.device)
     check(_lib.load().vfmoe_exl3_decode(_ptr(trellis), _ptr(out), K, N, bits, _stream()))
+    return out
+
+
+def ep_plan(idx: torch.Tensor, n_experts: int, placement: torch.Tensor, n_ranks: int):
+    """(send_counts int32 [n_ranks], send_perm int32 [T*k], inv_perm int32 [T*k]) on the device."""
+    T, k = idx.shape
+    counts = torch.empty(n_ranks, dtype=torch.int32, device=idx.device)
+    perm = torch.empty(T * k, dtype=torch.int32, device=idx.device)
+    inv = torch.empty(T * k, dtype=torch.int32, device=idx.device)
+    check(_lib.load().vfmoe_ep_plan(_ptr(idx), T, k, n_experts, _ptr(placement), n_ranks, _ptr(counts), _ptr(perm),
+                                    _ptr(inv), 0, _stream()))
+    return counts, perm, inv
+
+
+def ep_pack(x: torch.Tensor, idx: torch.Tensor, send_perm: torch.Tensor, local_slot: torch.Tensor):
+    """(rows [T*k, H] x.dtype, slots int32 [T*k]) in send order."""
+    T, k = idx.shape
+    n = T * k
+    rows = torch.empty((n, x.shape[1]), dtype=x.dtype, device=x.device)
+    slots = torch.empty(n, dtype=torch.int32, device=x.device)
+    check(_lib.load().vfmoe_ep_pack(_ptr(x), _DT[x.dtype], x.shape[1], k, _ptr(idx), _ptr(send_perm),
+                                    _ptr(local_slot), n, _ptr(rows), _ptr(slots), _stream()))
+    return rows, slots
+
+
+def combine(y: torch.Tensor, pos_of: torch.Tensor, w: torch.Tensor, T: int, k: int, y_shared=None,
+            out_dtype=torch.bfloat16) -> torch.Tensor:
+    H = y.shape[1]
+    out = torch.empty((T, H), dtype=out_dtype, device=y.device)
+    check(_lib.load().vfmoe_combine(_ptr(y), _ptr(pos_of), _ptr(w), T, k, H, _ptr(y_shared), _ptr(out),
+                                    _DT[out_dtype], _stream()))
     return out
 
 

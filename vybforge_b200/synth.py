@@ -196,25 +196,28 @@ def cuda_seed(cfg: LayerConfig, e: int, proj: int, layer: int = 0) -> int:
     return (cfg.seed * 1_000_003 + layer * 7919 + e * 3 + proj) & 0x7FFFFFFFFFFF
 
 
-def expert_q8_cuda(cfg: LayerConfig, lib, device="cuda", layer: int = 0):
-    """All E+1 experts as Q8_0 on the GPU: torch.randn per (expert, projection)
-    from a seeded CUDA generator, times 0.02, quantized by the library's
-    ``vfmoe_q8_0_quantize`` kernel (bit-identical to ``quantize_q8_0``).
+def expert_q8_cuda(cfg: LayerConfig, lib, device="cuda", layer: int = 0, experts=None):
+    """Experts as Q8_0 on the GPU: torch.randn per (expert, projection) from a CUDA
+    generator seeded by (seed, layer, expert, projection), times 0.02, quantized by the
+    library's ``vfmoe_q8_0_quantize`` kernel (bit-identical to ``quantize_q8_0``).
 
-    Returns dict proj -> torch.uint8 [E+1, rows, row_bytes] on `device`."""
+    experts: ids to generate (E = the shared expert); default all 0..E.  Any subset
+    reproduces exactly the same bytes for its experts.
+    Returns dict proj -> torch.uint8 [len(experts), rows, row_bytes] on `device`."""
     import torch
     E = cfg.n_experts
+    ids = list(range(E + 1)) if experts is None else list(experts)
     out = {}
     g = torch.Generator(device=device)
     for proj in (PROJ_GATE, PROJ_UP, PROJ_DOWN):
         rows, cols = _proj_shape(cfg, proj)
-        buf = torch.empty((E + 1, rows, q8_0_row_bytes(cols)), dtype=torch.uint8, device=device)
+        buf = torch.empty((len(ids), rows, q8_0_row_bytes(cols)), dtype=torch.uint8, device=device)
         tmp = torch.empty((rows, cols), dtype=torch.float32, device=device)
-        for e in range(E + 1):
+        for i, e in enumerate(ids):
             g.manual_seed(cuda_seed(cfg, e, proj, layer))
             torch.randn((rows, cols), generator=g, out=tmp)
             tmp.mul_(0.02)
-            lib.q8_0_quantize(tmp, buf[e])
+            lib.q8_0_quantize(tmp, buf[i])
         out[proj] = buf
     return out
 
