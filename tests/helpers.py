@@ -73,3 +73,59 @@ class Built:
         x = self.x if tokens is None else self.x[tokens]
         return orc.moe_block_grouped(x, self.w_r, self.bias, self.expert,
                                      lambda: self.expert(cfg.n_experts), cfg.n_experts, cfg.topk)
+
+
+def run_ranks(target, world, timeout=600):
+    """Start `world` spawned processes target(rank, world, port, queue) and collect
+    {rank: result}.  A worker reports ("error", traceback) on failure; the parent fails as
+    soon as any worker dies or reports an error instead of waiting out the timeout."""
+    import queue as _queue
+    import socket
+    import time
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    t0 = time.time()
+    try:
+        while len(res) < world:
+            try:
+                rank, val = q.get(timeout=5)
+            except _queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                if dead:
+                    raise AssertionError(f"a rank exited with code {dead[0]} before reporting")
+                if time.time() - t0 > timeout:
+                    raise AssertionError("ranks did not report within the timeout")
+                continue
+            if isinstance(val, tuple) and len(val) == 2 and val[0] == "error":
+                raise AssertionError(f"rank {rank} failed:\n{val[1]}")
+            res[rank] = val
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+def _guarded_run(fn, rank, world, port, q):
+    import traceback
+    try:
+        q.put((rank, fn(rank, world, port)))
+    except BaseException:
+        q.put((rank, ("error", traceback.format_exc())))
+        raise
+
+
+def guarded(fn):
+    """Wrap a module-level rank body fn(rank, world, port) -> result for run_ranks
+    (picklable for the spawn start method)."""
+    import functools
+    return functools.partial(_guarded_run, fn)

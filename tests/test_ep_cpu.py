@@ -14,6 +14,8 @@ import torch
 from oracle import moe_oracle as orc
 from vybforge_b200 import ep, synth
 
+from helpers import run_ranks, guarded
+
 
 class NumpyBackend:
     """Oracle compute for one rank (test infrastructure only)."""
@@ -120,7 +122,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _gloo_worker(rank, world, port, q):
+def _gloo_body(rank, world, port):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -130,24 +132,17 @@ def _gloo_worker(rank, world, port, q):
         shard = np.array_split(np.arange(cfg.tokens), world)[rank]
         r = ep.EpRank(rank, world, NumpyBackend(cfg, w_r, bias, experts, placement, rank))
         out = ep.ep_forward_dist(r, torch.from_numpy(x[shard]), ep.DistTransport())
-        q.put((rank, out.numpy()))
+        return out.numpy()
     finally:
         dist.destroy_process_group()
 
 
+_gloo_worker = guarded(_gloo_body)
+
+
 def test_two_gloo_ranks_match_single_device_oracle():
-    import torch.multiprocessing as mp
     world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=300) for _ in range(world))
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    res = run_ranks(_gloo_worker, world, timeout=300)
     cfg, x, w_r, bias, experts, placement = _setup(world)
     got = np.concatenate([res[r] for r in range(world)])
     np.testing.assert_allclose(got, _reference(cfg, x, w_r, bias, experts), rtol=0, atol=1e-6)

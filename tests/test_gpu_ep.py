@@ -16,7 +16,7 @@ from oracle import moe_oracle as orc
 from vybforge_b200 import ep, synth, moe
 from vybforge_b200.moe import MoELayer, quantizer
 
-from helpers import rel_l2
+from helpers import rel_l2, run_ranks, guarded
 
 pytestmark = pytest.mark.gpu
 
@@ -65,7 +65,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_body(rank, world, port):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -79,7 +79,7 @@ def _nccl_worker(rank, world, port, q):
         x, w_r, bias, _ = synth.router_inputs(cfg)
         E = cfg.n_experts
         placement = ep.contiguous_placement(E, world)
-        mine = list(np.nonzero(placement == rank)[0]) + [E]
+        mine = [int(e) for e in np.nonzero(placement == rank)[0]] + [E]
         dev = synth.expert_q8_cuda(cfg, quantizer, experts=mine)
         L = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                      router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
@@ -90,26 +90,20 @@ def _nccl_worker(rank, world, port, q):
         out = ep.ep_forward_dist(ep.EpRank(rank, world, ep.GpuBackend(L, placement, world, torch.float32)), xd,
                                  ep.DistTransport())
         L.check_device_error()
-        q.put((rank, out.cpu().numpy()))
+        res = out.cpu().numpy()
         dist.barrier()
+        return res
     finally:
         dist.destroy_process_group()
 
 
+_nccl_worker = guarded(_nccl_body)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_gpus_nccl_match_single_gpu():
-    import torch.multiprocessing as mp
     world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=600) for _ in range(world))
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    res = run_ranks(_nccl_worker, world, timeout=300)
     got = np.concatenate([res[r] for r in range(world)])
     moe.init(0)
     cfg = synth.config("c1", tokens=32)

@@ -193,7 +193,7 @@ def expert_exl3_numpy(cfg: LayerConfig, rng):
 
 # ----------------------------------------------------------------------------- experts, CUDA
 def cuda_seed(cfg: LayerConfig, e: int, proj: int, layer: int = 0) -> int:
-    return (cfg.seed * 1_000_003 + layer * 7919 + e * 3 + proj) & 0x7FFFFFFFFFFF
+    return int((int(cfg.seed) * 1_000_003 + int(layer) * 7919 + int(e) * 3 + int(proj)) & 0x7FFFFFFFFFFF)
 
 
 def expert_q8_cuda(cfg: LayerConfig, lib, device="cuda", layer: int = 0, experts=None):
