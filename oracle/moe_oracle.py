@@ -200,16 +200,16 @@ def decode_mcg(w16):
     lie in [0.125, 2) in magnitude, so the float32 sum is exact and the single
     rounding to fp16 equals a hardware fp16 add.
     """
-    w = np.asarray(w16).astype(np.uint64)
-    prod = (w * np.uint64(MCG_MUL)) & np.uint64(0xFFFFFFFF)
-    y = ((prod & np.uint64(MCG_AND)) ^ np.uint64(MCG_XOR)).astype(np.uint32)
+    w = np.asarray(w16).astype(np.uint32)
+    prod = w * np.uint32(MCG_MUL)                      # uint32 arithmetic wraps mod 2^32
+    y = (prod & np.uint32(MCG_AND)) ^ np.uint32(MCG_XOR)
     lo = (y & np.uint32(0xFFFF)).astype(np.uint16).view(np.float16)
     hi = (y >> np.uint32(16)).astype(np.uint16).view(np.float16)
     return (lo.astype(np.float32) + hi.astype(np.float32)).astype(np.float16)
 
 
-def exl3_windows_3bpw(tiles):
-    """3-bpw window extraction (the layout this build defines; no reference one exists).
+def exl3_windows_3bpw_bits(tiles):
+    """3-bpw window extraction, bit by bit (the layout this build defines; no reference one exists).
 
     tiles: uint16 [..., 48] -- one 16x16 tile = 768 bits, LSB-first in each word.
     Window j (j = 0..255) is the 16 bits starting at bit 3*j of the tile's
@@ -228,6 +228,23 @@ def exl3_windows_3bpw(tiles):
     w = (bits[..., pos] << np.arange(16, dtype=np.uint64)).sum(axis=-1)  # [..., 256]
     w = w.astype(np.uint16)
     # j = 16*c + r  ->  [..., c, r] -> transpose to [..., r, c]
+    return np.swapaxes(w.reshape(*lead, 16, 16), -1, -2)
+
+def exl3_windows_3bpw(tiles):
+    """Same windows as `exl3_windows_3bpw_bits`, from whole words: window j starts in word
+    (3j) // 16 at bit (3j) % 16 <= 15, so words (3j)//16 and the next one (circularly) hold
+    all 16 of its bits.  Memory O(windows) instead of O(bits); used for full-size matrices."""
+    t = np.asarray(tiles)
+    if t.dtype == np.int16:
+        t = t.view(np.uint16)
+    lead = t.shape[:-1]
+    assert t.shape[-1] == 48
+    j = np.arange(256)
+    w0 = (3 * j) // 16
+    sh = ((3 * j) % 16).astype(np.uint32)
+    t32 = t.astype(np.uint32)
+    v = (t32[..., w0] | (t32[..., (w0 + 1) % 48] << np.uint32(16))) >> sh
+    w = (v & np.uint32(0xFFFF)).astype(np.uint16)
     return np.swapaxes(w.reshape(*lead, 16, 16), -1, -2)
 
 
@@ -290,7 +307,7 @@ def dequant_exl3(trellis, suh, svh, bits, slot_table=None):
     what = exl3_what(trellis, bits, slot_table)
     k, n = what.shape
     hs = hadamard128() * R_SCALE
-    t2 = what.reshape(k // 128, 128, n // 128, 128)
-    t2 = np.einsum("ab,ibjc,cd->iajd", hs, t2, hs, optimize=True)
-    w = t2.reshape(k, n)
+    # per 128x128 block (i, j): Hs . W^[i, j] . Hs
+    w = (hs @ what.reshape(k // 128, 128, n)).reshape(k, n // 128, 128) @ hs
+    w = w.reshape(k, n)
     return w * np.asarray(suh, np.float64)[:, None] * np.asarray(svh, np.float64)[None, :]

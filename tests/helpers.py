@@ -37,7 +37,14 @@ class Built:
             rng = np.random.default_rng(cfg.seed)
         self.x, self.w_r, self.bias = x, w_r, bias
         H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
-        if weights == "numpy":
+        if cfg.fmt == "exl3":
+            if weights == "numpy":
+                ex = synth.expert_exl3_numpy(cfg, rng)
+                self.dev = {p: tuple(torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a).cuda()
+                                     for a in ex[p]) for p in range(3)}
+            else:
+                self.dev = synth.expert_exl3_cuda(cfg)
+        elif weights == "numpy":
             ex = synth.expert_q8_numpy(cfg, rng)
             self.dev = {p: torch.from_numpy(ex[p]).cuda() for p in range(3)}
         else:
@@ -51,6 +58,18 @@ class Built:
     def make_layer(self, out_dtype):
         cfg, E = self.cfg, self.cfg.n_experts
         g, u, d = self.dev[0], self.dev[1], self.dev[2]
+        if cfg.fmt == "exl3":
+            def head(m):
+                return tuple(a[:E] for a in m)
+
+            def tail(m):
+                return tuple(a[E] for a in m)
+            return MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
+                            router_w=self.wr_dev, router_bias=self.bias_dev,
+                            gate=head(g), up=head(u), down=head(d), shared=(tail(g), tail(u), tail(d)),
+                            fmt="exl3", exl3_bits=cfg.exl3_bits,
+                            x_dtype=torch.bfloat16 if cfg.x_dtype == "bf16" else torch.float32,
+                            out_dtype=out_dtype)
         return MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                         router_w=self.wr_dev, router_bias=self.bias_dev,
                         gate=g[:E], up=u[:E], down=d[:E], shared=(g[E], u[E], d[E]),
@@ -58,6 +77,11 @@ class Built:
                         out_dtype=out_dtype)
 
     def expert(self, e):
+        if e not in self._cache and self.cfg.fmt == "exl3":
+            def mat(p):
+                tr, suh, svh = (a[e].cpu().numpy() for a in self.dev[p])
+                return orc.dequant_exl3(tr.view(np.uint16), suh, svh, self.cfg.exl3_bits)
+            self._cache[e] = (mat(0), mat(1), mat(2))
         if e not in self._cache:
             H, I = self.cfg.hidden, self.cfg.inter
             g = self.dev[0][e].cpu().numpy()

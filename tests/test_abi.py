@@ -81,6 +81,27 @@ def test_invalid_descriptor_rejected(built_lib, field, value):
     assert "invalid layer descriptor" in _lib.last_error()
 
 
+def _exl3_desc(bits):
+    d = _desc(weight_format=_lib.WFMT_EXL3, exl3_bits=bits)
+    for m, (k, n) in ((d.gate, (1024, 512)), (d.up, (1024, 512)), (d.down, (512, 1024))):
+        m.expert_stride = k // 16 * n // 16 * 2 * 16 * bits
+        m.suh, m.svh = 16 << 20, 17 << 20
+        m.suh_stride, m.svh_stride = 2 * k, 2 * n
+    return d
+
+
+def test_exl3_descriptors(built_lib):
+    assert built_lib.vfmoe_layer_create(C.byref(_exl3_desc(4))) == _lib.ERR_UNSUPPORTED
+    assert "exl3_bits=4" in _lib.last_error()
+    d = _exl3_desc(3)
+    d.up.suh = 0
+    assert built_lib.vfmoe_layer_create(C.byref(d)) == _lib.ERR_INVALID
+    assert "suh and svh" in _lib.last_error()
+    d = _exl3_desc(3)
+    d.down.expert_stride -= 16
+    assert built_lib.vfmoe_layer_create(C.byref(d)) == _lib.ERR_INVALID
+
+
 def test_null_descriptor_and_unknown_handle(built_lib):
     assert built_lib.vfmoe_layer_create(None) == _lib.ERR_INVALID
     assert built_lib.vfmoe_layer_destroy(12345) == _lib.ERR_HANDLE

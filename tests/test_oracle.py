@@ -125,12 +125,18 @@ def test_exl3_4bpw_dequant_matches_reference():
 def test_exl3_3bpw_windows_bit_by_bit():
     rng = np.random.default_rng(5)
     tiles = rng.integers(0, 1 << 16, size=(3, 48), dtype=np.uint32).astype(np.uint16)
-    w = orc.exl3_windows_3bpw(tiles)
+    w = orc.exl3_windows_3bpw_bits(tiles)
     for t in range(3):
         bits = [(int(tiles[t, i // 16]) >> (i % 16)) & 1 for i in range(768)]
         for j in (0, 1, 15, 16, 100, 250, 255):
             v = sum(bits[(3 * j + i) % 768] << i for i in range(16))
             assert int(w[t, j % 16, j // 16]) == v
+
+
+def test_exl3_3bpw_word_windows_match_bit_windows():
+    rng = np.random.default_rng(6)
+    tiles = rng.integers(0, 1 << 16, size=(4, 5, 48), dtype=np.uint32).astype(np.uint16)
+    np.testing.assert_array_equal(orc.exl3_windows_3bpw(tiles), orc.exl3_windows_3bpw_bits(tiles))
 
 
 def test_exl3_activation_side_hadamard_identity():

@@ -49,6 +49,7 @@ struct Layer {
     void *own_ws = nullptr;      // internal workspace when the caller passes none
     int64_t own_ws_bytes = 0;
     TcPlan tc;                   // tensor-core launch state (tensor maps)
+    Exl3Plan x3;                 // EXL3 trellis tensor maps
     int use_tc = 1;
     // profiling (vfmoe_profile_enable / vfmoe_profile_read)
     int prof = 0;
@@ -108,7 +109,8 @@ static WsLayout ws_layout(const Layer &L, int64_t T, int k = -1) {
     o.idx = take(T * k * 4);
     o.w = take(T * k * 4);
     o.part = take(router_logit_floats((int)T, L.H, L.E) * 4);
-    o.xp = take(rows * L.H * 2);
+    // EXL3 keeps two rotated copies of every row (gate and up input bases)
+    o.xp = take(rows * L.H * 2 * (L.d.weight_format == VFMOE_WFMT_EXL3 ? 2 : 1));
     o.act = take(rows * L.I * 2);
     o.y = take(rows * L.H * 4);
     o.tiles_cap = tc_tiles_capacity((int)T, k, L.n_local > L.E ? L.n_local : L.E);
@@ -186,8 +188,26 @@ static int validate(const vfmoe_layer_desc &d) {
         if (d.sh_gate.data && (!d.sh_up.data || !d.sh_down.data)) return bad("shared expert incomplete");
     } else if (d.weight_format == VFMOE_WFMT_EXL3) {
         if (d.exl3_bits != 3 && d.exl3_bits != 4) return bad("exl3_bits must be 3 or 4");
-        if (d.hidden % 128 || d.inter % 128) return bad("EXL3 needs multiples of 128");
-        return bad("EXL3 expert products are not available in this build yet");
+        if (d.exl3_bits != 3) {
+            set_error("EXL3 expert products: exl3_bits=%d is not supported by this build (3 only)", (int)d.exl3_bits);
+            return VFMOE_ERR_UNSUPPORTED;
+        }
+        const vfmoe_matrix *ms[6] = {&d.gate, &d.up, &d.down, &d.sh_gate, &d.sh_up, &d.sh_down};
+        const int64_t kk[3] = {d.hidden, d.hidden, d.inter}, nn[3] = {d.inter, d.inter, d.hidden};
+        const int64_t nl = d.n_local_experts ? d.n_local_experts : d.n_experts;
+        if (!d.gate.data || !d.up.data || !d.down.data) return bad("routed expert weights missing");
+        if (d.sh_gate.data && (!d.sh_up.data || !d.sh_down.data)) return bad("shared expert incomplete");
+        for (int i = 0; i < 6; ++i) {
+            const vfmoe_matrix &m = *ms[i];
+            if (!m.data) continue;
+            const int64_t K = kk[i % 3], N = nn[i % 3];
+            if (!m.suh || !m.svh) return bad("EXL3 matrices need suh and svh");
+            if (!aligned16(m.data) || (m.suh & 1) || (m.svh & 1)) return bad("EXL3 trellis must be 16-byte aligned");
+            if (i < 3 && nl > 1 &&
+                (m.expert_stride < K / 16 * N / 16 * 2 * 16 * d.exl3_bits || (m.expert_stride & 15) ||
+                 m.suh_stride < K * 2 || m.svh_stride < N * 2 || (m.suh_stride & 1) || (m.svh_stride & 1)))
+                return bad("EXL3 expert strides too small or misaligned");
+        }
     } else {
         return bad("unknown weight_format");
     }
@@ -261,6 +281,7 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
         return VFMOE_ERR_CUDA;
     }
     rc = tc_plan_create(L->d, L->tc);
+    if (!rc) rc = exl3_plan_create(L->d, L->x3);
     if (rc) {
         cudaFree(L->dev_err);
         cudaFree(L->nw);
@@ -339,6 +360,25 @@ int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w
     return route_impl(*L, x, T, base, lay, &idx, &w, reinterpret_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+// Q8_0 expert products on gathered fp16 rows: tensor-core path (decode GEMV or tcgen05
+// grouped GEMM) unless the handle was created with VFMOE_DISABLE_TC (SIMT reference path).
+static int forward_experts(Layer &L, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
+                           int64_t &nlaunch) {
+    int rc;
+    if (L.use_tc && tc_supported(L.tc, a)) {
+        rc = launch_experts_tc(L.tc, a, st, mid);
+        nlaunch += 3;
+    } else {
+        rc = launch_experts_simt(a, st, mid);
+        nlaunch += 2;
+    }
+    return rc;
+}
+
+extern "C" {
+
 int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx_out, int64_t w_out,
                   int64_t workspace, int64_t ws_bytes, int64_t stream) {
     Layer *L = get_layer(handle);
@@ -412,19 +452,22 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, L->has_shared, perm_tok, pos_of, offsets, L->dev_err, st);
     if (rc) return rc;
     const int64_t rows = T * L->k + (L->has_shared ? T : 0);
-    rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
-                       reinterpret_cast<__half *>(base + lay.xp), st);
-    if (rc) return rc;
-    nlaunch += 2;
-    mark();
-    if (L->use_tc && tc_supported(L->tc, a)) {
-        rc = launch_experts_tc(L->tc, a, st, [&]() { mark(); });
+    if (L->x3.ready) {
+        // EXL3: the expert path gathers and rotates the rows itself
         nlaunch += 1;
+        mark();
+        rc = launch_experts_exl3(L->x3, a, reinterpret_cast<const void *>(x), (int)L->d.x_dtype, st,
+                                 [&]() { mark(); });
+        nlaunch += 4;
     } else {
-        rc = launch_experts_simt(a, st, [&]() { mark(); });
+        rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
+                           reinterpret_cast<__half *>(base + lay.xp), st);
+        if (rc) return rc;
+        nlaunch += 2;
+        mark();
+        rc = forward_experts(*L, a, st, [&]() { mark(); }, nlaunch);
     }
     if (rc) return rc;
-    nlaunch += 2;
     mark();
     rc = launch_combine(a.y, pos_of, w, (int)T, L->H, L->k, L->has_shared ? a.y + T * L->k * L->H : nullptr,
                         reinterpret_cast<void *>(out), (int)L->d.out_dtype, st);
@@ -537,13 +580,15 @@ int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t
     a.tiles = reinterpret_cast<int4 *>(base + lay.tiles);
     a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
     a.tiles_cap = lay.tiles_cap;
-    if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n, L->H,
-                            reinterpret_cast<__half *>(base + lay.xp), st)))
-        return rc;
-    if (L->use_tc && tc_supported(L->tc, a))
-        rc = launch_experts_tc(L->tc, a, st, []() {});
-    else
-        rc = launch_experts_simt(a, st, []() {});
+    int64_t nlaunch = 0;
+    if (L->x3.ready) {
+        rc = launch_experts_exl3(L->x3, a, reinterpret_cast<const void *>(rows), (int)rows_dtype, st, []() {});
+    } else {
+        if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n, L->H,
+                                reinterpret_cast<__half *>(base + lay.xp), st)))
+            return rc;
+        rc = forward_experts(*L, a, st, []() {}, nlaunch);
+    }
     if (rc) return rc;
     // back to the callers' row order: y_out[i] = y[pos_of[i]]
     return launch_combine(a.y, pos_of, nullptr, (int)n, L->H, 1, nullptr, reinterpret_cast<void *>(y_out),

@@ -510,6 +510,13 @@ bool tc_supported(const TcPlan &plan, const MoeArgs &a) {
 // Tiles of at least 8 rows (the decode GEMV's smallest): sum_e ceil(n_e / 8) <= rows / 8 + segments.
 int64_t tc_tiles_capacity(int T, int k, int E) { return ((int64_t)T * k + T) / 8 + E + 2; }
 
+int launch_tc_plan(const MoeArgs &a, int n_gu, int n_dn, cudaStream_t st) {
+    tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap, a.tile_counts,
+                                       a.err);
+    VF_LAUNCH_CHECK("tc_plan_kernel");
+    return VFMOE_OK;
+}
+
 static int pick_n(int T, int k, int E) {
     const double avg = (double)T * k / E;
     const int want = (int)std::max(2.0 * avg, (double)std::min(T, 32));

@@ -40,6 +40,22 @@ int gemv_tokens_per_tile(int T, int k, int E);
 int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
                         const CUtensorMap &tok_gu, const CUtensorMap &tok_dn);
 
+// Builds the (expert, token-tile) lists for both GEMMs on the device (n_gu / n_dn rows per tile).
+int launch_tc_plan(const MoeArgs &a, int n_gu, int n_dn, cudaStream_t st);
+
+// EXL3 3-bpw experts (exl3.cu): trellis tensor maps, one per projection.
+struct Exl3Plan {
+    int ready = 0;
+    int num_sms = 0;
+    CUtensorMap gate, up, down;
+    CUtensorMap sh_gate, sh_up, sh_down;
+};
+int exl3_plan_create(const vfmoe_layer_desc &d, Exl3Plan &plan);
+// Gathers and rotates the token rows itself (x_perm holds two rotated copies per row:
+// gate and up input bases), then the decode GEMVs.  `x` = the rows in caller order.
+int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, int x_dtype, cudaStream_t st,
+                        const std::function<void()> &mid);
+
 // Workspace the tensor-core path needs beyond MoeArgs: tile lists for both GEMMs.
 int64_t tc_tiles_capacity(int T, int k, int E);
 
