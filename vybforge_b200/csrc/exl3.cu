@@ -34,8 +34,6 @@ namespace vfmoe {
 using namespace sm100;
 
 constexpr float kRScale = 0.08838834764831845f;  // 1/sqrt(128)
-constexpr int kXcon = 8;                           // consumer warps
-constexpr int kXthreads = 32 * (kXcon + 1);
 constexpr int kKT = 16;                            // k-tiles (of 16) per stage = 256 K
 constexpr int kTileBytes3 = 96;                    // 48 uint16 words
 
@@ -98,10 +96,26 @@ __global__ void __launch_bounds__(256) gather_exl3_kernel(const void *__restrict
 }
 
 // ----------------------------------------------------------------------------- decode GEMV
-template <bool GATEUP, int NT>
+// Shared-memory trellis layout per stage and matrix: [nb 0..7][kt 0..15][48 u16] (a 4D TMA
+// box over the global [K/16][N/16][48] order), so the four threads of an MMA quad (four
+// k-tiles of one column block, 96 B apart) and its eight row groups hit 32 distinct banks.
+// MMA row g of a warp's 16-channel block is channel 2g, row g + 8 is channel 2g + 1: one
+// thread decodes two adjacent trellis columns, 14 bytes at u16 word 6g, with 4 LDS.32.
+//
+// Each window decodes to fp16(lo + hi) of the two halves of its mcg word, as the reference
+// does (one fp16 add per pair of weights, HADD2), so the GEMV multiplies exactly the
+// reference's decoded weights.
+//
+// CW consumer warps: 8 own 16 channels each over the whole 256-K stage; with 16 the second
+// group takes the upper half of every stage (k-tiles 8..15) and the two partial sums meet
+// in the epilogue exchange buffer.
+template <bool GATEUP, int NT, int CW>
 struct XCfg {
     static constexpr int N = 8 * NT;
     static constexpr int MATS = GATEUP ? 2 : 1;
+    static constexpr int KG = CW / 8;                              // k groups
+    static constexpr int PQ = 4 / KG;                              // 64-K quarters per warp and stage
+    static constexpr int THREADS = 32 * (CW + 1);
     static constexpr int WBYTES = MATS * kKT * 8 * kTileBytes3;   // trellis per stage
     static constexpr int TOKROWS = GATEUP ? 2 * N : N;            // gate/up: two rotated versions
     static constexpr int TOK = TOKROWS * 512;                      // 256 K fp16
@@ -110,12 +124,13 @@ struct XCfg {
     static constexpr int XCH = MATS * N * XLD * 4;                 // epilogue exchange [m][token][channel]
     static constexpr int SW = (220000 - XCH) / STAGE > 6 ? 6 : (220000 - XCH) / STAGE;
     static constexpr int SMEM = SW * STAGE + XCH + 2 * SW * 8 + 16 + 1024;
+    static_assert(CW == 8 || CW == 16, "consumer warps");
     static_assert(SW >= 2, "double buffering");
     static_assert(SMEM <= 232448, "shared memory");
 };
 
 struct XParams {
-    CUtensorMap wa, wb, swa, swb;  // trellis [E][K/16][N/16*24 u32] (routed) / shared
+    CUtensorMap wa, wb, swa, swb;  // trellis 4D maps (routed, shared): {24 u32, K/16, N/16, experts}
     CUtensorMap xt;                // token rows fp16
     const int4 *tiles;
     const int32_t *n_tiles;
@@ -126,32 +141,56 @@ struct XParams {
     void *out;
     float limit;
     int *err;
+    uint32_t k65536;               // 65536 as a run-time value: its multiplies stay IMADs
+    uint32_t kxor;                 // 0x3B603B60 in a register: mask and xor in one LOP3
 };
 
-// 16 decoded weights (one tile column, k = 0..15) -> 8 packed fp16 pairs.
-__device__ __forceinline__ void exl3_col16(const uint16_t *tile, int c, uint32_t (&out)[8]) {
-    const int w0 = 3 * c;
-    uint64_t v = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int wi = w0 + i;
-        v |= (uint64_t)tile[wi >= 48 ? wi - 48 : wi] << (16 * i);
-    }
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-        const uint32_t wa = (uint32_t)(v >> (6 * p)) & 0xFFFFu;
-        const uint32_t wb = (uint32_t)(v >> (6 * p + 3)) & 0xFFFFu;
-        const uint32_t ya = ((wa * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
-        const uint32_t yb = ((wb * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
-        const uint32_t lo = __byte_perm(ya, yb, 0x5410), hi = __byte_perm(ya, yb, 0x7632);
-        const __half2 s = __hadd2(*reinterpret_cast<const __half2 *>(&lo), *reinterpret_cast<const __half2 *>(&hi));
-        out[p] = *reinterpret_cast<const uint32_t *>(&s);
+// Window at absolute bit O of the 128-bit little-endian stream w[0..3], as a clean 16-bit
+// value.  The extraction is spread over the ALU and IMAD pipes (both limit this kernel):
+//   byte-aligned inside a word     PRMT with zero fill                 1 ALU
+//   inside one word                SHL to the top, IMAD.HI by 2^16     1 ALU + 1 IMAD
+//   across two words, O >= 81      funnel shift, AND                   2 ALU
+//   across two words, otherwise    funnel shift, IMAD.LO/HI by 2^16    1 ALU + 2 IMAD
+template <int O>
+__device__ __forceinline__ uint32_t window16(const uint32_t (&w)[4], uint32_t k65536) {
+    constexpr int j = O >> 5, s = O & 31;
+    if constexpr (s % 8 == 0 && s <= 16) {
+        return __byte_perm(w[j], 0u, (s / 8) | ((s / 8 + 1) << 4) | (4 << 8) | (4 << 12));
+    } else if constexpr (s < 16) {
+        return __umulhi(w[j] << (16 - s), k65536);
+    } else {
+        const uint32_t u = __funnelshift_r(w[j], w[j + 1], s);
+        if constexpr (O >= 81) {
+            return u & 0xFFFFu;
+        } else {
+            return __umulhi(u * k65536, k65536);
+        }
     }
 }
 
-template <bool GATEUP, int NT>
-__global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_constant__ XParams p) {
-    using C = XCfg<GATEUP, NT>;
+// mcg codebook of two windows -> one packed fp16 pair (first window in the low half):
+// hash, halves of both words regrouped (PRMT), mask/xor, fp16(lo + hi) per weight.
+__device__ __forceinline__ uint32_t mcg_pair(uint32_t wa, uint32_t wb, uint32_t kxor) {
+    const uint32_t pa = wa * 0xCBAC1FEDu, pb = wb * 0xCBAC1FEDu;
+    const uint32_t lo = (__byte_perm(pa, pb, 0x5410) & 0x8FFF8FFFu) ^ kxor;
+    const uint32_t hi = (__byte_perm(pa, pb, 0x7632) & 0x8FFF8FFFu) ^ kxor;
+    const __half2 s = __hadd2(*reinterpret_cast<const __half2 *>(&lo), *reinterpret_cast<const __half2 *>(&hi));
+    return *reinterpret_cast<const uint32_t *>(&s);
+}
+
+// Columns 2g (bits 0..63 of w) and 2g + 1 (bits 48..111): 16 weights each, k = 0..15,
+// as 8 fp16 pairs (k = 2p, 2p + 1).
+template <int P>
+__device__ __forceinline__ void decode_pairs(const uint32_t (&w)[4], uint32_t k65536, uint32_t kxor, uint32_t (&a)[8],
+                                             uint32_t (&b)[8]) {
+    a[P] = mcg_pair(window16<6 * P>(w, k65536), window16<6 * P + 3>(w, k65536), kxor);
+    b[P] = mcg_pair(window16<48 + 6 * P>(w, k65536), window16<48 + 6 * P + 3>(w, k65536), kxor);
+    if constexpr (P < 7) decode_pairs<P + 1>(w, k65536, kxor, a, b);
+}
+
+template <bool GATEUP, int NT, int CW>
+__global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __grid_constant__ XParams p) {
+    using C = XCfg<GATEUP, NT, CW>;
     constexpr int SW = C::SW, N = C::N, MATS = C::MATS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,7 +204,7 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
     if (threadIdx.x == 0) {
         for (int i = 0; i < SW; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kXcon);
+            mbar_init(&empty[i], CW);
         }
         *abort = 0;
         fence_mbar_init();
@@ -173,7 +212,7 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
     __syncthreads();
     const int n_items = (*p.n_tiles) * MT;
 
-    if (warp == kXcon) {
+    if (warp == CW) {
         if (lane == 0) {
             prefetch_tmap(&p.wa);
             prefetch_tmap(&p.xt);
@@ -191,8 +230,8 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
                     if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort))) break;
                     uint8_t *st = smem + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], C::WBYTES + C::TOK);
-                    tma_load_3d(st, ma, &full[s], nb0 * 24, kr * kKT, z);
-                    if (GATEUP) tma_load_3d(st + kKT * 8 * kTileBytes3, mb, &full[s], nb0 * 24, kr * kKT, z);
+                    tma_load_4d(st, ma, &full[s], 0, kr * kKT, nb0, z);
+                    if (GATEUP) tma_load_4d(st + kKT * 8 * kTileBytes3, mb, &full[s], 0, kr * kKT, nb0, z);
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         tma_load_2d(st + C::WBYTES + q * (C::TOKROWS * 128), &p.xt, &full[s], kr * 256 + 64 * q,
@@ -211,7 +250,11 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
 
     // ------------------------------------------------------------------ consumers
     const int g = lane >> 2, c = lane & 3;
-    const int r0 = 16 * warp;  // channels r0 + g, r0 + g + 8 of the 128-channel tile
+    const int wl = warp & 7, kg = warp >> 3;   // channel block, k group
+    const int r0 = 16 * wl;                    // channels r0 + 2g, r0 + 2g + 1 of the 128-channel tile
+    // u32 offsets of this thread's 14 trellis bytes inside a tile (word 6g .. 6g+6, circular)
+    const int wo0 = 3 * g, wo3 = (3 * g + 3) % 24;
+    const uint32_t k65536 = p.k65536, kxor = p.kxor;
     uint32_t n = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -227,16 +270,17 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
             if (!(ok = mbar_wait(&full[s], (n / SW) & 1, abort))) break;
             const uint8_t *st = smem + s * C::STAGE;
 #pragma unroll
-            for (int pq = 0; pq < 4; ++pq) {
+            for (int pi = 0; pi < C::PQ; ++pi) {
+                const int pq = kg * C::PQ + pi;
                 const int kt = 4 * pq + c;  // this thread's k-tile in the stage
                 const uint8_t *tq = st + C::WBYTES + pq * (C::TOKROWS * 128);
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) {
-                    const uint8_t *wbase = st + m * (kKT * 8 * kTileBytes3) + kt * (8 * kTileBytes3);
+                    const uint32_t *tile = reinterpret_cast<const uint32_t *>(
+                        st + m * (kKT * 8 * kTileBytes3) + (wl * kKT + kt) * kTileBytes3);
+                    const uint32_t w[4] = {tile[wo0], tile[wo0 + 1], tile[wo0 + 2], tile[wo3]};
                     uint32_t wa[8], wb[8];
-                    const int ra = r0 + g, rb = r0 + g + 8;
-                    exl3_col16(reinterpret_cast<const uint16_t *>(wbase + (ra >> 4) * kTileBytes3), ra & 15, wa);
-                    exl3_col16(reinterpret_cast<const uint16_t *>(wbase + (rb >> 4) * kTileBytes3), rb & 15, wb);
+                    decode_pairs<0>(w, k65536, kxor, wa, wb);
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < ntv) {
@@ -246,12 +290,11 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
                             const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
                             for (int s4 = 0; s4 < 4; ++s4) {
-                                const uint32_t a[4] = {wa[2 * s4], wb[2 * s4], wa[2 * s4 + 1], wb[2 * s4 + 1]};
-                                asm volatile(
-                                    "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, "
+                                asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, "
                                     "%7}, {%8, %9}, {%0, %1, %2, %3};"
                                     : "+f"(acc[m][j][0]), "+f"(acc[m][j][1]), "+f"(acc[m][j][2]), "+f"(acc[m][j][3])
-                                    : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(xb[2 * s4]), "r"(xb[2 * s4 + 1]));
+                                    : "r"(wa[2 * s4]), "r"(wb[2 * s4]), "r"(wa[2 * s4 + 1]), "r"(wb[2 * s4 + 1]),
+                                      "r"(xb[2 * s4]), "r"(xb[2 * s4 + 1]));
                             }
                         }
                     }
@@ -262,22 +305,29 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
         }
         if (!ok) break;
         // ---------------------------------------------------------------- epilogue
-        // z -> shared memory [m][token][channel], then one warp per token: FWHT over
-        // the 128 channels, * svh, (gate/up) swiglu, * suh_down, FWHT, fp16 store.
+        // z -> shared memory [m][token][channel] (k groups summed), then one warp per token:
+        // FWHT over the 128 channels, * svh, (gate/up) swiglu, * suh_down, FWHT, store.
+        // acc[m][j]: rows g (e 0,1) / g + 8 (e 2,3) = channels r0 + 2g / r0 + 2g + 1,
+        // tokens 8j + 2c + (e & 1).
+        for (int pass = C::KG - 1; pass >= 0; --pass) {
+            if (kg == pass) {
 #pragma unroll
-        for (int m = 0; m < MATS; ++m)
+                for (int m = 0; m < MATS; ++m)
 #pragma unroll
-            for (int j = 0; j < NT; ++j)
+                    for (int j = 0; j < NT; ++j)
 #pragma unroll
-                for (int e4 = 0; e4 < 4; ++e4) {
-                    const int ch = r0 + g + 8 * (e4 >> 1), tok = 8 * j + 2 * c + (e4 & 1);
-                    xch[(m * N + tok) * C::XLD + ch] = acc[m][j][e4];
-                }
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * kXcon) : "memory");
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const int ch = r0 + 2 * g + (e4 >> 1), tok = 8 * j + 2 * c + (e4 & 1);
+                            float *d = &xch[(m * N + tok) * C::XLD + ch];
+                            *d = (pass == C::KG - 1) ? acc[m][j][e4] : *d + acc[m][j][e4];
+                        }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * CW) : "memory");
+        }
         const int e = t.x;
         const bool sh = e == p.E;
         const int ch0 = (item % MT) * 128;
-        for (int tok = warp; tok < t.z; tok += kXcon) {
+        for (int tok = warp; tok < t.z; tok += CW) {
             float v[MATS][4];
 #pragma unroll
             for (int m = 0; m < MATS; ++m) {
@@ -309,7 +359,7 @@ __global__ void __launch_bounds__(kXthreads, 1) expert_gemv_exl3(const __grid_co
                 for (int q = 0; q < 4; ++q) out[(int64_t)(t.y + tok) * p.ld_out + ch0 + lane + 32 * q] = v[0][q];
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * kXcon) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * CW) : "memory");
     }
     if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
 }
@@ -327,7 +377,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 x_encode() {
     return fn;
 }
 
-// Trellis stack [experts][K/16][N/16][48 u16] as u32 elements; box = 8 column blocks x kKT k-tiles.
+// Trellis stack [experts][K/16][N/16][48 u16] as u32 elements, viewed as 4D
+// {24 words, K/16 k-tiles, N/16 column blocks, experts} so that a box of 16 k-tiles x
+// 8 column blocks lands in shared memory as [column block][k-tile][96 B].
 static int make_trellis_map(CUtensorMap *m, const void *base, int64_t K, int64_t N, int64_t experts, int64_t stride) {
     auto enc = x_encode();
     if (!enc) {
@@ -336,11 +388,11 @@ static int make_trellis_map(CUtensorMap *m, const void *base, int64_t K, int64_t
     }
     const int64_t row_u32 = (N / 16) * 24;
     if (experts <= 1) stride = (K / 16) * row_u32 * 4;
-    cuuint64_t dims[3] = {(cuuint64_t)row_u32, (cuuint64_t)(K / 16), (cuuint64_t)experts};
-    cuuint64_t strides[2] = {(cuuint64_t)(row_u32 * 4), (cuuint64_t)stride};
-    cuuint32_t box[3] = {8 * 24, (cuuint32_t)kKT, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(base), dims, strides, box, es,
+    cuuint64_t dims[4] = {24, (cuuint64_t)(K / 16), (cuuint64_t)(N / 16), (cuuint64_t)experts};
+    cuuint64_t strides[3] = {(cuuint64_t)(row_u32 * 4), (cuuint64_t)kTileBytes3, (cuuint64_t)stride};
+    cuuint32_t box[4] = {24, (cuuint32_t)kKT, 8, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void *>(base), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -389,15 +441,16 @@ int exl3_plan_create(const vfmoe_layer_desc &d, Exl3Plan &plan) {
     return VFMOE_OK;
 }
 
-template <bool GATEUP, int NT>
+template <bool GATEUP, int NT, int CW>
 static int launch_x(const XParams &prm, int grid, cudaStream_t st) {
-    using C = XCfg<GATEUP, NT>;
+    using C = XCfg<GATEUP, NT, CW>;
     static bool attr_done = false;
     if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemv_exl3<GATEUP, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        VF_CUDA(cudaFuncSetAttribute(expert_gemv_exl3<GATEUP, NT, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::SMEM));
         attr_done = true;
     }
-    expert_gemv_exl3<GATEUP, NT><<<grid, kXthreads, C::SMEM, st>>>(prm);
+    expert_gemv_exl3<GATEUP, NT, CW><<<grid, C::THREADS, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_exl3<gate_up>" : "expert_gemv_exl3<down>");
     return VFMOE_OK;
 }
@@ -436,11 +489,13 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
     g.out = a.act;
     g.limit = a.limit;
     g.err = a.err;
+    g.k65536 = 65536u;
+    g.kxor = 0x3B603B60u;
     const int grid = plan.num_sms;
     switch (N) {
-        case 8: rc = launch_x<true, 1>(g, grid, st); break;
-        case 16: rc = launch_x<true, 2>(g, grid, st); break;
-        default: rc = launch_x<true, 4>(g, grid, st); break;
+        case 8: rc = launch_x<true, 1, 16>(g, grid, st); break;
+        case 16: rc = launch_x<true, 2, 16>(g, grid, st); break;
+        default: rc = launch_x<true, 4, 8>(g, grid, st); break;
     }
     if (rc) return rc;
     mid();
@@ -463,10 +518,12 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
     dn.out = a.y;
     dn.limit = a.limit;
     dn.err = a.err;
+    dn.k65536 = 65536u;
+    dn.kxor = 0x3B603B60u;
     switch (N) {
-        case 8: return launch_x<false, 1>(dn, grid, st);
-        case 16: return launch_x<false, 2>(dn, grid, st);
-        default: return launch_x<false, 4>(dn, grid, st);
+        case 8: return launch_x<false, 1, 16>(dn, grid, st);
+        case 16: return launch_x<false, 2, 16>(dn, grid, st);
+        default: return launch_x<false, 4, 16>(dn, grid, st);
     }
 }
 
