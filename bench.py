@@ -237,6 +237,102 @@ def prefill_extra(a, cfg1, dev, flush):
                               "zipf_target_max": float(tgt.max())}}
 
 
+def stack_extra(a, rank, world, local_rank, flush):
+    """BASELINE C4: 4 pre-norm MoE layers of the C1 shape, Q8_0, bf16 activations.
+    prefill T=8192 (Zipf(1.1) routers, calibrated per layer) and decode T=256 (plain routers);
+    global token counts fixed (strong scaling).  N=1: MoEStack on one GPU.  N>1: expert-parallel
+    (EpStack over NCCL all-to-all), E/N experts per GPU placed by expected load, shared expert and
+    routers replicated, tokens sharded."""
+    import torch
+    from vybforge_b200 import synth, ep
+    from vybforge_b200.moe import MoELayer, quantizer
+    from vybforge_b200.stack import MoEStack, EpStack, token_shards
+    L = 4
+    t_setup = time.perf_counter()
+    cfgp, cfgd = synth.config("c4p"), synth.config("c4d")
+    xp, norm_p, routers_p = synth.stack_inputs(cfgp, L)
+    xd, norm_d, routers_d = synth.stack_inputs(cfgd, L)
+    E, H, I, k = cfgp.n_experts, cfgp.hidden, cfgp.inter, cfgp.topk
+    placements = [ep.balanced_placement(routers_p[l][2], world) if world > 1 else np.zeros(E, np.int32)
+                  for l in range(L)]
+    layers = {"p": [], "d": []}
+    for l in range(L):
+        mine = [int(e) for e in np.nonzero(placements[l] == rank)[0]] + [E]
+        dev = synth.expert_q8_cuda(cfgp, quantizer, layer=l, experts=mine)
+        for key, routers in (("p", routers_p), ("d", routers_d)):
+            w_r, bias, _ = routers[l]
+            lay = MoELayer(hidden=H, inter=I, n_experts=E, topk=k, router_w=torch.from_numpy(w_r).cuda(),
+                           router_bias=torch.from_numpy(bias).cuda(), gate=dev[0][:-1], up=dev[1][:-1],
+                           down=dev[2][:-1], shared=(dev[0][-1], dev[1][-1], dev[2][-1]),
+                           n_local_experts=E // world if world > 1 else 0,
+                           x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+            layers[key].append(lay)
+    t_setup = time.perf_counter() - t_setup
+    st = torch.cuda.current_stream()
+    tr = ep.DistTransport() if world > 1 else None
+    out = {}
+    for key, cfg, x, norm in (("p", cfgp, xp, norm_p), ("d", cfgd, xd, norm_d)):
+        T = cfg.tokens
+        nw = [torch.from_numpy(w).cuda() for w in norm]
+        if world > 1:
+            stack = EpStack([ep.EpRank(rank, world, ep.GpuBackend(lay, placements[l], world))
+                             for l, lay in enumerate(layers[key])], nw)
+            sh = token_shards(T, world)[rank]
+            xl = torch.from_numpy(x[sh[0]:sh[-1] + 1]).to(torch.bfloat16).cuda()
+            step = lambda: stack.forward_dist(xl, tr)
+        else:
+            stack = MoEStack(layers[key], nw)
+            xl = torch.from_numpy(x).to(torch.bfloat16).cuda()
+            step = lambda: stack.forward(xl)
+        steps = max(5, a.steps // 2)
+        for _ in range(max(3, a.warmup)):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            if world > 1:
+                torch.distributed.barrier()
+            ev[i][0].record(st)
+            step()
+            ev[i][1].record(st)
+        torch.cuda.synchronize()
+        ms = float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        for lay in layers[key]:
+            lay.check_device_error()
+        pk, pk_kind = peaks()
+        res = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4), "n_gpus": world,
+               "global_tokens": T, "layers": L}
+        if key == "p":
+            flops = L * (6.0 * H * I * T * (k + 1) + 2.0 * H * E * T)
+            tf = flops / (ms * 1e-3) / 1e12
+            res.update({"workload": "c4p: 4 layers x (RMSNorm + MoE + residual), prefill T=8192, Zipf(1.1) "
+                                    "routers, Q8_0, bf16 activations",
+                        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s",
+                                     "peak": round(world * pk["bf16_tflops"], 1),
+                                     "frac": round(tf / (world * pk["bf16_tflops"]), 4), "peak_source": pk_kind,
+                                     "algorithmic_flops_per_step": flops}})
+            if world > 1:
+                loads = np.array([[routers_p[l][2][placements[l] == r].sum() for r in range(world)]
+                                  for l in range(L)])
+                res["placement_expected_rows_max_over_mean"] = round(float((loads.max(1) / loads.mean(1)).max()), 3)
+        else:
+            res["workload"] = "c4d: 4 layers x (RMSNorm + MoE + residual), decode T=256, Q8_0, bf16 activations"
+        out["c4" + key] = res
+        del stack
+    out["c4_setup_s"] = round(t_setup, 1)
+    for key in layers:
+        for lay in layers[key]:
+            lay.close()
+    return out
+
+
 def run_ours_ep(a, rank, world, local_rank):
     """N > 1: the C1 layer expert-parallel over NCCL.  Each rank holds E/N routed experts
     (contiguous placement; decode routing is uniform), the router and the shared expert,
@@ -301,6 +397,11 @@ def run_ours_ep(a, rank, world, local_rank):
     t = torch.tensor([e2e_ms], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
+    extra = None
+    if not a.no_extra and a.workload == "c1" and a.tokens is None:
+        layer_keep = layer
+        extra = stack_extra(a, rank, world, local_rank, flush)
+        layer = layer_keep
     # algorithmic bytes of the whole job: distinct experts touched (global routing) + shared per rank
     from vybforge_b200.moe import MoELayer as _L  # noqa: F401
     idx, _ = layer.route(torch.from_numpy(x).to(torch.bfloat16).cuda())
@@ -325,6 +426,8 @@ def run_ours_ep(a, rank, world, local_rank):
                         "unit": "GB/s", "frac": round(frac, 4), "peak_source": pk_kind, "traffic": None},
            "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)}}
+    if extra is not None:
+        res["extra"] = extra
     return res
 
 
@@ -440,6 +543,11 @@ def run_ours(a, rank, world, local_rank):
         res["extra"] = extra
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_ours(cfg, host, dev, idx_np, a.cpu_budget_s)
+    if "extra" in res:
+        del dev
+        layer.close()
+        torch.cuda.empty_cache()
+        res["extra"].update(stack_extra(a, rank, world, local_rank, flush))
     return res
 
 

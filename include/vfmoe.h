@@ -119,8 +119,10 @@ int vfmoe_layer_destroy(int64_t handle);
 int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max);
 
 /* Router only: idx int32 [T, topk], w fp32 [T, topk] from x [T, H].
- * logits = x . W_r^T (fp64 accumulation), score = sigmoid(logit), top-k on
- * score + bias (lowest index wins ties), w = score / (sum + 1e-20) * scale.
+ * logits = x . W_r^T, score = sigmoid(logit), top-k on score + bias (lowest
+ * index wins ties), w = score / (sum + 1e-20) * scale.  The selection equals the
+ * one made on exact (fp64) logits: fp32 logits with rigorous error bounds pick the
+ * candidates, float-float and then fp64 arithmetic order those whose bounds overlap.
  * Replaces moe_route (native/kernels/moe.vyb:32-95) and the host router of
  * glm_engine.vyb:2728-2803.  workspace may be 0 (internal). */
 int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out,
@@ -197,6 +199,17 @@ int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *lau
 int vfmoe_rmsnorm(int64_t x, int64_t w, int64_t y, int64_t S, int64_t D, double eps,
                   int64_t dtype, int64_t stream);
 
+/* Residual step of a pre-norm layer stack, one pass over S rows of D:
+ *   x_out = x + y           when y != 0 (rounded to dtype)
+ *   h     = RMSNorm_w(x_out or x)   when w != 0 (statistics of the rounded values)
+ * so layer l's residual add and layer l+1's input norm share a kernel.  The
+ * reference stack (native/glm53/glm_engine.vyb) mixes layers through
+ * hyper-connections; this entry implements the plain residual x + MoE(RMSNorm(x))
+ * of the expert-parallel stack and has no single reference counterpart.
+ * dtype VFMOE_DT_BF16 or VFMOE_DT_F32; w fp32 [D]; x_out may alias x. */
+int vfmoe_residual_rmsnorm(int64_t x, int64_t y, int64_t w, int64_t x_out, int64_t h, int64_t S,
+                           int64_t D, double eps, int64_t dtype, int64_t stream);
+
 /* Q8_0 rows -> dense [rows, k] (dst_dtype VFMOE_DT_F32 or VFMOE_DT_F16).
  * Replaces q8_0deq (native/kernels/q8_0.vyb:11-30, which widens to f64). */
 int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k,
@@ -208,7 +221,8 @@ int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, i
 
 /* EXL3 trellis -> rotated-basis values W^ as fp16 [K, N] (no Hadamard).
  * Replaces exl3deq / exl3deq32 (native/kernels/exl3.vyb:207-242,375-422).
- * bits = 3 (layout defined by this library) or 4 (reference slot map). */
+ * bits = 3 (layout defined by this library); 4 (the reference slot map) returns
+ * VFMOE_ERR_UNSUPPORTED in this build. */
 int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, int64_t bits,
                       int64_t stream);
 

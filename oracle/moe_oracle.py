@@ -166,6 +166,25 @@ def rmsnorm(x, weight, eps=1e-5):
     return x * r * np.asarray(weight, dtype=np.float64)[None, :]
 
 
+def moe_stack(x, layers, eps=1e-5, round_act=None):
+    """Pre-norm MoE stack: x <- x + MoE_l(RMSNorm_l(x)) for each layer.
+
+    layers: list of (norm_w, run) where run(h) -> (y, idx, w) is one MoE layer
+    (e.g. a closure over ``moe_block_grouped``).  round_act, if given, is applied to
+    every activation the GPU stores (normed input, layer output, residual stream),
+    mirroring bf16 activations.  Returns (x, per-layer list of (h, y, idx))."""
+    rnd = round_act if round_act is not None else (lambda a: a)
+    x = rnd(np.asarray(x, dtype=np.float64))
+    trace = []
+    for norm_w, run in layers:
+        h = rnd(rmsnorm(x, norm_w, eps))
+        y, idx, _ = run(h)
+        y = rnd(y)
+        x = rnd(x + y)
+        trace.append((h, y, idx))
+    return x, trace
+
+
 # --------------------------------------------------------------------------- Q8_0
 def dequant_q8_0(raw, rows, k):
     """Q8_0 rows -> float64 [rows, k] (native/tools/q8_0_ref.py:50-56).

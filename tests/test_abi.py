@@ -115,6 +115,10 @@ def test_standalone_ops_validate_arguments(built_lib):
     assert built_lib.vfmoe_q8_0_quantize(0, 0, 4, 30, 0) == _lib.ERR_INVALID
     assert built_lib.vfmoe_exl3_decode(0, 0, 15, 16, 3, 0) == _lib.ERR_INVALID
     assert built_lib.vfmoe_rmsnorm(0, 0, 0, 2, 0, 1e-5, 0, 0) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_residual_rmsnorm(0, 0, 0, 0, 0, 2, 64, 1e-5, 2, 0) == _lib.ERR_INVALID       # no x
+    assert built_lib.vfmoe_residual_rmsnorm(4096, 0, 0, 0, 0, 2, 64, 1e-5, 2, 0) == _lib.ERR_INVALID    # no y, no w
+    assert built_lib.vfmoe_residual_rmsnorm(4096, 8192, 0, 0, 0, 2, 64, 1e-5, 2, 0) == _lib.ERR_INVALID  # y, no x_out
+    assert built_lib.vfmoe_residual_rmsnorm(4096, 0, 8192, 0, 0, 2, 64, 1e-5, 1, 0) == _lib.ERR_INVALID  # f16
 
 
 def test_init_without_device_returns_status(built_lib):

@@ -1,0 +1,141 @@
+"""Pre-norm MoE stack (BASELINE config 4 form: x <- x + MoE_l(RMSNorm_l(x)), bf16
+activations) on the GPU against the oracle stack, and its expert-parallel form against
+the single-GPU stack.
+
+* Teacher-forced per layer: the oracle runs layer l on the GPU's own normed input h_l.
+  Expert ids are bit-exact and the layer output is within max-abs 2e-2 / rel-L2 1e-3.
+* End to end: the oracle stack mirrors every bf16 rounding the GPU stores, so the
+  final residual stream meets the same bars.
+* Expert parallel: N virtual ranks (token shards, experts placed by expected load)
+  give the single-GPU stack's bytes."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from vybforge_b200 import ep, moe, synth
+from vybforge_b200.moe import MoELayer
+from vybforge_b200.quant import round_bf16
+from vybforge_b200.stack import MoEStack, EpStack, ep_stack_forward_virtual, token_shards
+
+from helpers import rel_l2, TOL_MAX_ABS, TOL_REL_L2
+
+pytestmark = pytest.mark.gpu
+
+L = 4
+
+
+class Stack:
+    """C0-shaped 4-layer stack (H=1024, I=512, 16 experts, top-4), Q8_0, bf16 activations."""
+
+    def __init__(self, T, zipf=0.0):
+        cfg = synth.config("c0", tokens=T)
+        cfg.x_dtype, cfg.zipf_s = "bf16", zipf
+        self.cfg = cfg
+        self.x, self.norm_ws, self.routers = synth.stack_inputs(cfg, L, calib_tokens=T)
+        self.ex = [synth.expert_q8_numpy(cfg, np.random.default_rng((cfg.seed, 3000 + l))) for l in range(L)]
+        self.dev = [{p: torch.from_numpy(e[p]).cuda() for p in range(3)} for e in self.ex]
+        self.norm_dev = [torch.from_numpy(w).cuda() for w in self.norm_ws]
+        self._mats = {}
+
+    def layer(self, l, placement=None, rank=0, world=1):
+        cfg, E = self.cfg, self.cfg.n_experts
+        w_r, bias, _ = self.routers[l]
+        kw = dict(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
+                  router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
+                  x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+        d = self.dev[l]
+        if placement is None:
+            return MoELayer(gate=d[0][:E], up=d[1][:E], down=d[2][:E], shared=(d[0][E], d[1][E], d[2][E]), **kw)
+        g, u, dn, sh = ep.rank_experts(d, placement, rank)
+        return MoELayer(gate=g, up=u, down=dn, shared=sh, n_local_experts=E // world, **kw)
+
+    def mats(self, l, e):
+        if (l, e) not in self._mats:
+            H, I = self.cfg.hidden, self.cfg.inter
+            g, u, d = (self.ex[l][p][e] for p in range(3))
+            self._mats[(l, e)] = (orc.q8_0_expert_inout(g, I, H), orc.q8_0_expert_inout(u, I, H),
+                                  orc.q8_0_expert_inout(d, H, I))
+        return self._mats[(l, e)]
+
+    def oracle_layer(self, l):
+        w_r, bias, _ = self.routers[l]
+        E, k = self.cfg.n_experts, self.cfg.topk
+        return lambda h: orc.moe_block_grouped(h, w_r, bias, lambda e: self.mats(l, e), lambda: self.mats(l, E), E, k)
+
+
+@pytest.fixture(scope="module")
+def st():
+    moe.init(0)
+    return Stack(T=48, zipf=1.1)
+
+
+def _f64(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def test_stack_teacher_forced_per_layer(st):
+    s = MoEStack([st.layer(l) for l in range(L)], st.norm_dev)
+    xd = torch.from_numpy(st.x).to(torch.bfloat16).cuda()
+    out, trace = s.forward(xd, trace=True)
+    torch.cuda.synchronize()
+    for l, (h, y, idx) in enumerate(trace):
+        ro, ri, _ = st.oracle_layer(l)(_f64(h))
+        np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+        got = _f64(y)
+        print(f"[stack layer {l} teacher-forced] max-abs {np.abs(got - ro).max():.3e} rel-L2 {rel_l2(got, ro):.3e}")
+        assert np.abs(got - ro).max() <= TOL_MAX_ABS and rel_l2(got, ro) <= TOL_REL_L2
+    for lay in s.layers:
+        lay.check_device_error()
+
+
+def test_stack_end_to_end(st):
+    s = MoEStack([st.layer(l) for l in range(L)], st.norm_dev)
+    xd = torch.from_numpy(st.x).to(torch.bfloat16).cuda()
+    out, trace = s.forward(xd, trace=True)
+    ref, rtrace = orc.moe_stack(st.x, [(st.norm_ws[l], st.oracle_layer(l)) for l in range(L)], round_act=round_bf16)
+    for l in range(L):
+        np.testing.assert_array_equal(trace[l][2].cpu().numpy(), rtrace[l][2])
+    got = _f64(out)
+    print(f"[stack end-to-end {L} layers] max-abs {np.abs(got - ref).max():.3e} rel-L2 {rel_l2(got, ref):.3e}")
+    assert np.abs(got - ref).max() <= TOL_MAX_ABS and rel_l2(got, ref) <= TOL_REL_L2
+
+
+def test_residual_rmsnorm_matches_oracle(st):
+    xd = torch.from_numpy(st.x).to(torch.bfloat16).cuda()
+    y = (0.5 * xd.float().flip(0)).to(torch.bfloat16)
+    x2, h = moe.residual_rmsnorm(xd, y, st.norm_dev[1])
+    want_x = round_bf16(st.x.astype(np.float64) + _f64(y))
+    np.testing.assert_array_equal(_f64(x2), want_x)
+    want_h = orc.rmsnorm(want_x, st.norm_ws[1])
+    np.testing.assert_allclose(_f64(h), want_h, rtol=8e-3, atol=1e-6)   # bf16 output rounding
+    x3, none = moe.residual_rmsnorm(xd, y, None)
+    assert none is None and torch.equal(x3, x2)
+    same, h1 = moe.residual_rmsnorm(xd, None, st.norm_dev[0])
+    assert same is xd
+    np.testing.assert_allclose(_f64(h1), orc.rmsnorm(st.x, st.norm_ws[0]), rtol=8e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_stack_virtual_ranks_match_single_gpu(st, world):
+    T = st.cfg.tokens
+    single = MoEStack([st.layer(l) for l in range(L)], st.norm_dev)
+    xd = torch.from_numpy(st.x).to(torch.bfloat16).cuda()
+    ref = single.forward(xd)
+    stacks = []
+    for r in range(world):
+        ranks = []
+        for l in range(L):
+            placement = ep.balanced_placement(st.routers[l][2], world)
+            lay = st.layer(l, placement, r, world)
+            ranks.append(ep.EpRank(r, world, ep.GpuBackend(lay, placement, world, out_dtype=torch.bfloat16)))
+        stacks.append(EpStack(ranks, st.norm_dev))
+    shards = token_shards(T, world)
+    outs = ep_stack_forward_virtual(stacks, [xd[s[0]:s[-1] + 1].contiguous() for s in shards],
+                                    ep.VirtualTransport(world))
+    got = torch.cat(outs)
+    for s in stacks:
+        for r in s.ranks:
+            r.b.layer.check_device_error()
+    assert torch.equal(got, ref)

@@ -70,6 +70,7 @@ _SIGS = {
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),
     "vfmoe_profile_read": (C.c_int, [I64, C.POINTER(C.c_double), I64, C.POINTER(I64)]),
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),
+    "vfmoe_residual_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_q8_0_dequant": (C.c_int, [I64] * 6),
     "vfmoe_q8_0_quantize": (C.c_int, [I64] * 5),
     "vfmoe_exl3_decode": (C.c_int, [I64] * 6),

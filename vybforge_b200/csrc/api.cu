@@ -668,6 +668,19 @@ int vfmoe_rmsnorm(int64_t x, int64_t w, int64_t y, int64_t S, int64_t D, double 
                           reinterpret_cast<cudaStream_t>(stream));
 }
 
+int vfmoe_residual_rmsnorm(int64_t x, int64_t y, int64_t w, int64_t x_out, int64_t h, int64_t S, int64_t D,
+                           double eps, int64_t dtype, int64_t stream) {
+    if (S < 0 || D <= 0 || (S > 0 && (!x || (y && !x_out) || (w && !h) || (!y && !w))) ||
+        (dtype != VFMOE_DT_BF16 && dtype != VFMOE_DT_F32)) {
+        set_error("vfmoe_residual_rmsnorm: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_residual_rmsnorm(reinterpret_cast<const void *>(x), reinterpret_cast<const void *>(y),
+                                   reinterpret_cast<const float *>(w), reinterpret_cast<void *>(x_out),
+                                   reinterpret_cast<void *>(h), S, (int)D, (float)eps, (int)dtype,
+                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
 int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k, int64_t dst_dtype, int64_t stream) {
     if (rows < 0 || k <= 0 || k % 32 || (rows > 0 && (!src || !dst)) ||
         (dst_dtype != VFMOE_DT_F32 && dst_dtype != VFMOE_DT_F16)) {

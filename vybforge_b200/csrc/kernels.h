@@ -59,6 +59,8 @@ int launch_experts_simt(const MoeArgs &a, cudaStream_t st, const std::function<v
 
 int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, float eps, int dtype,
                    cudaStream_t st);
+int launch_residual_rmsnorm(const void *x, const void *y, const float *w, void *x_out, void *h, int64_t S, int D,
+                            float eps, int dtype, cudaStream_t st);
 int launch_q8_0_dequant(const uint8_t *src, void *dst, int64_t rows, int64_t k, int dst_dtype,
                         cudaStream_t st);
 int launch_q8_0_quantize(const float *src, uint8_t *dst, int64_t rows, int64_t k, cudaStream_t st);

@@ -117,6 +117,45 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x
     }
 }
 
+// Residual stream step of a pre-norm stack, one CTA per row:
+//   x_out = x + y            (y optional; rounded to dtype)
+//   h     = rmsnorm(x_out)   (w optional; statistics over the rounded x_out)
+// so the residual add of layer l and the norm of layer l + 1 share one pass.
+__global__ void __launch_bounds__(256) residual_rmsnorm_kernel(const void *__restrict__ x, const void *__restrict__ y,
+                                                               const float *__restrict__ w, void *__restrict__ x_out,
+                                                               void *__restrict__ h, int D, float eps, int dtype) {
+    __shared__ float red[8];
+    const int64_t row = blockIdx.x;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < D; c += 256) {
+        float v = ld_act(x, row * D + c, dtype);
+        if (y) {
+            v += ld_act(y, row * D + c, dtype);
+            st_act(x_out, row * D + c, v, dtype);
+            v = ld_act(x_out, row * D + c, dtype);  // the rounded value
+        }
+        ss = fmaf(v, v, ss);
+    }
+    if (!w) return;
+    ss = warp_sum_f32(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float r = rsqrtf(tot / (float)D + eps);
+    const void *src = y ? x_out : x;
+    for (int c = threadIdx.x; c < D; c += 256) st_act(h, row * D + c, ld_act(src, row * D + c, dtype) * r * w[c], dtype);
+}
+
+int launch_residual_rmsnorm(const void *x, const void *y, const float *w, void *x_out, void *h, int64_t S, int D,
+                            float eps, int dtype, cudaStream_t st) {
+    if (S == 0) return VFMOE_OK;
+    residual_rmsnorm_kernel<<<(unsigned)S, 256, 0, st>>>(x, y, w, x_out, h, D, eps, dtype);
+    VF_LAUNCH_CHECK("residual_rmsnorm_kernel");
+    return VFMOE_OK;
+}
+
 int launch_q8_0_dequant(const uint8_t *src, void *dst, int64_t rows, int64_t k, int dst_dtype, cudaStream_t st) {
     const int64_t n = rows * k;
     if (n == 0) return VFMOE_OK;

@@ -209,6 +209,19 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor
     return y
 
 
+def residual_rmsnorm(x: torch.Tensor, y: torch.Tensor | None, w: torch.Tensor | None, eps: float = 1e-5,
+                     x_out: torch.Tensor | None = None, h: torch.Tensor | None = None):
+    """(x + y, RMSNorm_w(x + y)) in one pass; y=None -> (x, RMSNorm_w(x)); w=None -> (x + y, None)."""
+    S, D = x.shape
+    if y is not None and x_out is None:
+        x_out = torch.empty_like(x)
+    if w is not None and h is None:
+        h = torch.empty_like(x)
+    check(_lib.load().vfmoe_residual_rmsnorm(_ptr(x), _ptr(y), _ptr(w), _ptr(x_out), _ptr(h), S, D, eps,
+                                             _DT[x.dtype], _stream()))
+    return (x_out if y is not None else x), h
+
+
 class _Quantizer:
     """Adapter used by synth.expert_q8_cuda."""
 

@@ -45,8 +45,11 @@ def quantize_q8_0(w) -> np.ndarray:
 
 def f32_to_bf16_bits(x) -> np.ndarray:
     """float32 -> bf16 bit patterns (uint16), round to nearest even."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u                     # finite inputs: no uint32 wrap-around (max 0xFF807FFE)
+    r >>= np.uint32(16)
     return r.astype(np.uint16)
 
 

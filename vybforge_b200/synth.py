@@ -142,6 +142,38 @@ def zipf_router_inputs(cfg: LayerConfig):
     return x, w_r, bias, tgt, rng
 
 
+def stack_inputs(cfg: LayerConfig, n_layers: int, calib_tokens: int = 2048):
+    """Inputs of a pre-norm stack of `n_layers` MoE layers of cfg's shape (BASELINE C4).
+
+    Returns (x, norm_ws, routers): x the stack input (cfg's ordinary token draw), norm_ws
+    a list of fp32 [H] RMSNorm weights 1 + N(0, 0.02), routers a list of (w_r, bias,
+    targets) per layer.  Layer l's router (W_r ~ N(0, 0.02), bias ~ N(0, 0.01)) is drawn
+    from the stream seeded (seed, 1000 + l).  With
+    cfg.zipf_s > 0 its selection bias is calibrated (as in zipf_router_inputs) on the
+    first `calib_tokens` rows of RMSNorm_l(x): later layers see the residual stream
+    instead, so their realized popularity is only approximately Zipf.  targets is the
+    expected selection count per expert (Zipf targets, or the uniform T*k/E)."""
+    x, _, _, rng = router_inputs(cfg)
+    norm_ws = [(1.0 + rng.normal(0.0, 0.02, cfg.hidden)).astype(np.float32) for _ in range(n_layers)]
+    routers = []
+    for l in range(n_layers):
+        r_l = np.random.default_rng((cfg.seed, 1000 + l))
+        w_r = r_l.normal(0.0, 0.02, (cfg.n_experts, cfg.hidden)).astype(np.float32)
+        bias0 = r_l.normal(0.0, 0.01, cfg.n_experts).astype(np.float32)
+        if cfg.zipf_s > 0:
+            xs = x[:calib_tokens].astype(np.float64)
+            h = xs / np.sqrt(np.mean(xs * xs, axis=1, keepdims=True) + 1e-5) * norm_ws[l]
+            logits = h @ w_r.astype(np.float64).T
+            tgt = zipf_targets(cfg.n_experts, len(xs), cfg.topk, cfg.zipf_s, np.random.default_rng((cfg.seed, 2000 + l)))
+            bias = calibrate_zipf_bias(logits, bias0, cfg.topk, tgt)
+            tgt = tgt * (cfg.tokens / len(xs))
+        else:
+            bias = bias0
+            tgt = np.full(cfg.n_experts, cfg.tokens * cfg.topk / cfg.n_experts)
+        routers.append((w_r, bias, tgt))
+    return x, norm_ws, routers
+
+
 def realized_counts(idx, n_experts):
     return np.bincount(np.asarray(idx).reshape(-1), minlength=n_experts)
 
