@@ -3,11 +3,22 @@ activations) on the GPU against the oracle stack, and its expert-parallel form a
 the single-GPU stack.
 
 * Teacher-forced per layer: the oracle runs layer l on the GPU's own normed input h_l.
-  Expert ids are bit-exact and the layer output is within max-abs 2e-2 / rel-L2 1e-3.
-* End to end: the oracle stack mirrors every bf16 rounding the GPU stores, so the
-  final residual stream meets the same bars.
+  Expert ids are bit-exact; an fp32-output twin of the layer (same weights) is within
+  max-abs 2e-2 / rel-L2 1e-3 of the oracle, and the stack's bf16 layer output is that
+  fp32 output rounded to bf16, bit for bit.
+* End to end: the same stack with fp32 activations (fp32 residual stream, fp32 layer
+  inputs and outputs) against the unrounded oracle stack.  (A bf16 residual stream
+  differs from the oracle's rounded one by whole-ulp flips wherever the two pre-rounding
+  values straddle a rounding boundary: 1 ulp is already 3e-2 at magnitude 4, so the
+  bf16 stack is pinned by the two per-layer checks above instead.)  A token whose
+  selection is a near tie at some layer (two adjacent choices among the top k+1 closer
+  than 1e-3 in the oracle's own stream) may legitimately route differently there; such
+  tokens are excluded (at most 1 in 8), every other token's routing must match at every
+  layer and the final residual stream meets the same bars.
 * Expert parallel: N virtual ranks (token shards, experts placed by expected load)
-  give the single-GPU stack's bytes."""
+  against the single-GPU stack.  Ranks can pick a different expert-GEMM path (the
+  GEMV / tcgen05 switch depends on rows per expert), so the check is the same bars
+  rather than bit equality."""
 
 import numpy as np
 import pytest
@@ -39,12 +50,12 @@ class Stack:
         self.norm_dev = [torch.from_numpy(w).cuda() for w in self.norm_ws]
         self._mats = {}
 
-    def layer(self, l, placement=None, rank=0, world=1):
+    def layer(self, l, placement=None, rank=0, world=1, out_dtype=torch.bfloat16, x_dtype=torch.bfloat16):
         cfg, E = self.cfg, self.cfg.n_experts
         w_r, bias, _ = self.routers[l]
         kw = dict(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                   router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
-                  x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+                  x_dtype=x_dtype, out_dtype=out_dtype)
         d = self.dev[l]
         if placement is None:
             return MoELayer(gate=d[0][:E], up=d[1][:E], down=d[2][:E], shared=(d[0][E], d[1][E], d[2][E]), **kw)
@@ -83,22 +94,45 @@ def test_stack_teacher_forced_per_layer(st):
     for l, (h, y, idx) in enumerate(trace):
         ro, ri, _ = st.oracle_layer(l)(_f64(h))
         np.testing.assert_array_equal(idx.cpu().numpy(), ri)
-        got = _f64(y)
-        print(f"[stack layer {l} teacher-forced] max-abs {np.abs(got - ro).max():.3e} rel-L2 {rel_l2(got, ro):.3e}")
+        y32 = st.layer(l, out_dtype=torch.float32).forward(h)
+        assert torch.equal(y, y32.to(torch.bfloat16))
+        got = _f64(y32)
+        print(f"[stack layer {l} teacher-forced, fp32 out] max-abs {np.abs(got - ro).max():.3e} "
+              f"rel-L2 {rel_l2(got, ro):.3e}")
         assert np.abs(got - ro).max() <= TOL_MAX_ABS and rel_l2(got, ro) <= TOL_REL_L2
     for lay in s.layers:
         lay.check_device_error()
 
 
+def _selection_margin(h, w_r, bias, k):
+    """Smallest gap between adjacent choices among the top k+1: a near tie there can
+    change the selected set (gap k-1/k) or the order of the selected experts."""
+    s = 1.0 / (1.0 + np.exp(-(h @ w_r.astype(np.float64).T)))
+    c = np.sort(s + bias.astype(np.float64)[None, :], axis=1)[:, ::-1]
+    return (c[:, :k] - c[:, 1:k + 1]).min(axis=1)
+
+
 def test_stack_end_to_end(st):
-    s = MoEStack([st.layer(l) for l in range(L)], st.norm_dev)
-    xd = torch.from_numpy(st.x).to(torch.bfloat16).cuda()
-    out, trace = s.forward(xd, trace=True)
-    ref, rtrace = orc.moe_stack(st.x, [(st.norm_ws[l], st.oracle_layer(l)) for l in range(L)], round_act=round_bf16)
+    f32 = torch.float32
+    s = MoEStack([st.layer(l, out_dtype=f32, x_dtype=f32) for l in range(L)], st.norm_dev)
+    out, trace = s.forward(torch.from_numpy(st.x).cuda(), trace=True)
+    ref, rtrace = orc.moe_stack(st.x, [(st.norm_ws[l], st.oracle_layer(l)) for l in range(L)])
+    T, k = st.cfg.tokens, st.cfg.topk
+    keep = np.ones(T, dtype=bool)
     for l in range(L):
-        np.testing.assert_array_equal(trace[l][2].cpu().numpy(), rtrace[l][2])
-    got = _f64(out)
-    print(f"[stack end-to-end {L} layers] max-abs {np.abs(got - ref).max():.3e} rel-L2 {rel_l2(got, ref):.3e}")
+        diff = (trace[l][2].cpu().numpy() != rtrace[l][2]).any(axis=1)
+        if diff.any():
+            w_r, bias, _ = st.routers[l]
+            margin = _selection_margin(rtrace[l][0], w_r, bias, k)[diff]
+            print(f"[stack end-to-end] layer {l}: {int(diff.sum())} token(s) route differently, "
+                  f"oracle margins {np.round(margin, 6).tolist()}")
+            assert (margin < 1e-3).all()
+            keep &= ~diff
+    assert keep.sum() >= T - T // 8
+    got = _f64(out)[keep]
+    ref = ref[keep]
+    print(f"[stack end-to-end {L} layers fp32 stream, {int(keep.sum())}/{T} tokens] "
+          f"max-abs {np.abs(got - ref).max():.3e} rel-L2 {rel_l2(got, ref):.3e}")
     assert np.abs(got - ref).max() <= TOL_MAX_ABS and rel_l2(got, ref) <= TOL_REL_L2
 
 
@@ -138,4 +172,6 @@ def test_ep_stack_virtual_ranks_match_single_gpu(st, world):
     for s in stacks:
         for r in s.ranks:
             r.b.layer.check_device_error()
-    assert torch.equal(got, ref)
+    g, r_ = _f64(got), _f64(ref)
+    print(f"[ep stack virtual N={world}] max-abs {np.abs(g - r_).max():.3e} rel-L2 {rel_l2(g, r_):.3e}")
+    assert np.abs(g - r_).max() <= TOL_MAX_ABS and rel_l2(g, r_) <= TOL_REL_L2
