@@ -147,7 +147,9 @@ __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__res
 // 128 tokens x 64 experts per CTA, 256 threads x (8 tokens x 4 experts), K in chunks of 32
 // staged k-major in shared memory (float4 reads: 3 per 32 FMAs); the next chunk is loaded
 // into registers while the current one is consumed.  Each chunk is summed on its own and
-// then added to the running total, so the summation depth is 32 + H/32.
+// then added to the running total, so the summation depth is 32 + HS/32 over the CTA's
+// K slice of HS = H / gridDim.z.  Slice z writes partial logits to logits + z*T*E; the
+// refinement kernel adds the gridDim.z partials in slice order (depth + gridDim.z).
 __global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__restrict__ x, int x_dtype,
                                                                const float *__restrict__ wr, int T, int H, int E,
                                                                float *__restrict__ logits) {
@@ -157,6 +159,8 @@ __global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__res
     const int t0 = blockIdx.y * BT, e0 = blockIdx.x * BE;
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;  // experts e0 + 4tx .. +3, tokens t0 + 8ty .. +7
+    const int HS = H / gridDim.z, k0 = blockIdx.z * HS;
+    logits += (int64_t)blockIdx.z * T * E;
     // loader mapping: x tile 128 rows x 32 k = 512 groups of 8 k (2 per thread);
     // w tile 64 rows x 32 k = 512 float4 (2 per thread)
     float xr[2][8], wv[2][4];
@@ -211,12 +215,12 @@ __global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__res
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    load(0);
-    for (int kb = 0; kb < H; kb += KC) {
+    load(k0);
+    for (int kb = k0; kb < k0 + HS; kb += KC) {
         __syncthreads();
         store();
         __syncthreads();
-        if (kb + KC < H) load(kb + KC);
+        if (kb + KC < k0 + HS) load(kb + KC);
         float part[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -622,6 +626,17 @@ static int launch_l1_small(const void *x, int x_dtype, const float *wr, int T, i
     return VFMOE_OK;
 }
 
+// K slices of the tiled logits kernel: enough CTAs for about two waves on 148 SMs, at most
+// kMaxChunks, each slice a multiple of 32 columns of H.
+static int tiled_splits(int T, int H, int E) {
+    const int64_t base = cdiv(E, 64) * cdiv(T, 128);
+    const int want = (int)std::min<int64_t>(kMaxChunks, cdiv(296, base));
+    int s = 1;
+    for (int c = 1; c <= want; ++c)
+        if ((H / 32) % c == 0) s = c;
+    return s;
+}
+
 int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
                   int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
                   cudaStream_t st) {
@@ -639,10 +654,11 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
         if (rc) return rc;
         c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
-        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 128));
+        nchunk = tiled_splits(T, H, E);
+        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 128), (unsigned)nchunk);
         router_logits_f32_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
         VF_LAUNCH_CHECK("router_logits_f32_tiled");
-        c1 = gamma_bound(32 + H / 32);
+        c1 = gamma_bound(32 + H / nchunk / 32 + nchunk);
     }
     // L2: thread owns n = H/256 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
     // exactly (TwoProduct), so the only error is lo's fp32 summation of the r and pe values,
@@ -693,6 +709,8 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     return VFMOE_OK;
 }
 
-int64_t router_logit_floats(int T, int H, int E) { return (int64_t)T * E * (T <= 32 ? std::max(1, H / 512) : 1); }
+int64_t router_logit_floats(int T, int H, int E) {
+    return (int64_t)T * E * (T <= 32 ? std::max(1, H / 512) : tiled_splits(T, H, E));
+}
 
 }  // namespace vfmoe
