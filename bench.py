@@ -300,15 +300,51 @@ def stack_extra(a, rank, world, local_rank, flush):
             ev[i][1].record(st)
         torch.cuda.synchronize()
         ms = float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+        phases = None
         if world > 1:
             t = torch.tensor([ms], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = float(t.item())
+            # one more step with an event after every phase: device ms per phase (this rank)
+            marks = []
+
+            def mark(name):
+                e_ = torch.cuda.Event(enable_timing=True)
+                e_.record(st)
+                marks.append((name, e_))
+            torch.distributed.barrier()
+            mark("start")
+            stack.forward_dist(xl, tr, mark)
+            torch.cuda.synchronize()
+            phases = {}
+            for (_, a_), (n_, b_) in zip(marks[:-1], marks[1:]):
+                phases[n_] = phases.get(n_, 0.0) + a_.elapsed_time(b_)
+            pt = torch.tensor([phases[n_] for n_ in sorted(phases)], device="cuda")
+            torch.distributed.all_reduce(pt, op=torch.distributed.ReduceOp.MAX)
+            phases = {n_: round(float(v), 3) for n_, v in zip(sorted(phases), pt.tolist())}
+        else:
+            # one more step with the library's stage events on: device ms per stage, all layers
+            import ctypes as C
+            for lay in layers[key]:
+                lay.lib.vfmoe_profile_enable(lay.handle, 1)
+                lay.lib.vfmoe_profile_read(lay.handle, (C.c_double * 8)(), 8, None)
+            step()
+            torch.cuda.synchronize()
+            tot = np.zeros(5)
+            for lay in layers[key]:
+                buf = (C.c_double * 8)()
+                lay.lib.vfmoe_profile_read(lay.handle, buf, 8, None)
+                lay.lib.vfmoe_profile_enable(lay.handle, 0)
+                tot += np.array(buf[:5])
+            phases = {n_: round(float(v), 3) for n_, v in
+                      zip(["router", "dispatch_gather", "gate_up", "down", "combine"], tot)}
         for lay in layers[key]:
             lay.check_device_error()
         pk, pk_kind = peaks()
         res = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4), "n_gpus": world,
                "global_tokens": T, "layers": L}
+        if phases:
+            res["phase_ms_per_step" + ("_max_over_ranks" if world > 1 else "")] = phases
         if key == "p":
             flops = L * (6.0 * H * I * T * (k + 1) + 2.0 * H * E * T)
             tf = flops / (ms * 1e-3) / 1e12

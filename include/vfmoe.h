@@ -168,14 +168,41 @@ int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t 
                   int64_t send_counts, int64_t send_perm, int64_t inv_perm, int64_t err_word, int64_t stream);
 
 /* Pack the send buffer: rows_out[s] = x[send_perm[s] / k] (x dtype, [n_slots, H]) and
- * slots_out[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index). */
+ * slots_out[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index).  With
+ * slots_out == 0, idx and local_slot may be 0: k = 1 and send_perm = send_tok gathers the
+ * rows of a token-level plan. */
 int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
                   int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream);
 
-/* Weighted combine: out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] + y_shared[t] (fp32 y rows;
- * w may be 0 for weight 1, y_shared may be 0).  glm_engine.vyb:2925-2938, :2991. */
-int vfmoe_combine(int64_t y, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H, int64_t y_shared,
-                  int64_t out, int64_t out_dtype, int64_t stream);
+/* Weighted combine: out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] + y_shared[t].  y rows and
+ * y_shared are y_dtype VFMOE_DT_F32 or VFMOE_DT_F16; w may be 0 for weight 1; y_shared may
+ * be 0; a negative pos_of entry skips that lane.  out_dtype F32, BF16 or F16.
+ * glm_engine.vyb:2925-2938, :2991. */
+int vfmoe_combine(int64_t y, int64_t y_dtype, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H,
+                  int64_t y_shared, int64_t out, int64_t out_dtype, int64_t stream);
+
+/* Token-level send plan (one row per token per destination rank): entries ordered by
+ * rank, then token, for every (t, r) where a lane of idx int32 [T,k] routes to an expert
+ * r owns (placement int32 [n_experts]).  Entry i: send_tok[i] = t; for lane l,
+ * send_slot[i*k+l] = local_slot[expert] when rank r owns it else -1, send_w[i*k+l] =
+ * w[t,l] or 0.  send_counts int32 [n_ranks]; pos_of int32 [T, n_ranks] = entry or -1.
+ * Buffers sized for T*n_ranks entries.  err_word: device int for a bad id (may be 0). */
+int vfmoe_ep_plan_tokens(int64_t idx, int64_t w, int64_t T, int64_t k, int64_t n_experts, int64_t placement,
+                         int64_t local_slot, int64_t n_ranks, int64_t send_counts, int64_t send_tok,
+                         int64_t send_slot, int64_t send_w, int64_t pos_of, int64_t err_word, int64_t stream);
+
+/* Bytes of workspace vfmoe_forward_routed needs for up to n_max rows of k lanes. */
+int64_t vfmoe_routed_workspace_bytes(int64_t handle, int64_t n_max, int64_t k);
+
+/* Expert products with caller routing: y_out[i] = sum_l w[i,l] * FFN_{slots[i,l]}(rows[i])
+ * over the lanes with slots[i,l] >= 0 (local expert slots; n_local_experts = the shared
+ * expert), lanes added in lane order.  rows [n, H] bf16 or fp32; slots int32 [n, k]; w fp32
+ * [n, k] (0: weight 1); y_out [n, H] of y_dtype F32, F16 or BF16.  The expert side of the
+ * token-level exchange: the received rows with their lanes, plus this rank's own rows
+ * with the shared slot. */
+int vfmoe_forward_routed(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t n, int64_t k, int64_t slots,
+                         int64_t w, int64_t y_out, int64_t y_dtype, int64_t workspace, int64_t ws_bytes,
+                         int64_t stream);
 
 /* Synchronize `stream` and report whether any kernel of this handle flagged a
  * device-side error since the last call (VFMOE_ERR_DEVICE), then clear it. */

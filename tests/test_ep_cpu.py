@@ -18,14 +18,17 @@ from helpers import run_ranks, guarded
 
 
 class NumpyBackend:
-    """Oracle compute for one rank (test infrastructure only)."""
+    """Oracle compute for one rank (test infrastructure only), in the token-level exchange
+    protocol of ep.EpRank: plan / pack / experts / combine restated in numpy."""
 
     def __init__(self, cfg, w_r, bias, experts, placement, rank):
         self.cfg, self.w_r, self.bias = cfg, w_r, bias
         self.placement = np.asarray(placement)
+        self.n_ranks = len(np.unique(self.placement))
         self.local = ep.local_slots(placement)
         self.my = np.nonzero(self.placement == rank)[0]          # global ids of local slots
         self.shared_slot = len(self.my)
+        self.k = cfg.topk
         H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
 
         def mats(e):
@@ -35,44 +38,54 @@ class NumpyBackend:
         self.mats[-1] = mats(E)                                  # shared
 
     def route(self, x):
-        idx, w = orc.route(x.numpy().astype(np.float64), self.w_r, self.bias, self.cfg.topk)
+        idx, w = orc.route(x.numpy().astype(np.float64), self.w_r, self.bias, self.k)
         return torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w.astype(np.float32))
 
-    def plan(self, idx):
-        flat = idx.numpy().reshape(-1)
-        owner = self.placement[flat]
-        perm = np.argsort(owner, kind="stable").astype(np.int32)
-        inv = np.empty_like(perm)
-        inv[perm] = np.arange(len(perm), dtype=np.int32)
-        counts = np.bincount(owner, minlength=len(np.unique(self.placement))).astype(np.int32)
-        return torch.from_numpy(counts), torch.from_numpy(perm), torch.from_numpy(inv)
+    def plan(self, idx, w):
+        idx, w = idx.numpy(), w.numpy()
+        T, k, R = idx.shape[0], self.k, self.n_ranks
+        owner = self.placement[idx]
+        tok, slot, sw = [], [], []
+        pos = np.full((T, R), -1, dtype=np.int32)
+        counts = np.zeros(R, dtype=np.int32)
+        for r in range(R):
+            for t in range(T):
+                mine = owner[t] == r
+                if mine.any():
+                    pos[t, r] = len(tok)
+                    tok.append(t)
+                    slot.append(np.where(mine, self.local[idx[t]], -1))
+                    sw.append(np.where(mine, w[t], 0.0))
+                    counts[r] += 1
+        n = len(tok)
+        return (torch.from_numpy(counts), torch.tensor(tok, dtype=torch.int32),
+                torch.from_numpy(np.array(slot, dtype=np.int32).reshape(n, k)),
+                torch.from_numpy(np.array(sw, dtype=np.float32).reshape(n, k)), torch.from_numpy(pos))
 
-    def pack(self, x, idx, perm):
-        k = idx.shape[1]
-        p = perm.numpy()
-        rows = x[torch.from_numpy(p // k).long()]
-        slots = self.local[idx.numpy().reshape(-1)[p]]
-        return rows, torch.from_numpy(slots.astype(np.int32))
+    def pack(self, x, tok, n):
+        return x[tok[:n].long()]
 
-    def rows(self, rows, slots):
+    def experts(self, rows, slots, w):
         r = rows.numpy().astype(np.float64)
-        s = slots.numpy()
+        s, wv = slots.numpy(), w.numpy().astype(np.float64)
         y = np.zeros_like(r)
-        for sl in np.unique(s):
-            sel = s == sl
-            key = -1 if sl == self.shared_slot else int(self.my[sl])
-            y[sel] = orc.ffn(r[sel], *self.mats[key])
+        for l in range(s.shape[1]):
+            for sl in np.unique(s[:, l]):
+                if sl < 0:
+                    continue
+                sel = s[:, l] == sl
+                key = -1 if sl == self.shared_slot else int(self.my[sl])
+                y[sel] += wv[sel, l:l + 1] * orc.ffn(r[sel], *self.mats[key])
         return torch.from_numpy(y)
 
-    def combine(self, y_back, inv, w, T, y_shared):
-        k = self.cfg.topk
-        yb = y_back.numpy()
-        wv = w.numpy().astype(np.float64)
-        out = np.zeros((T, yb.shape[1]))
+    def combine(self, y_back, pos, T, y_shared):
+        yb, p = y_back.numpy(), pos.numpy()
+        out = y_shared.numpy().copy()
         for t in range(T):
-            for l in range(k):
-                out[t] += wv[t, l] * yb[inv[t * k + l]]
-        return torch.from_numpy(out + y_shared.numpy())
+            for r in range(p.shape[1]):
+                if p[t, r] >= 0:
+                    out[t] += yb[p[t, r]]
+        return torch.from_numpy(out)
 
 
 def _setup(world):

@@ -1,5 +1,5 @@
-"""Expert parallelism on the GPU: the libvfmoe EP kernels (plan, pack, forward_rows,
-combine) driven by vybforge_b200/ep.py, against the fused single-GPU forward.
+"""Expert parallelism on the GPU: the libvfmoe EP kernels (token-level plan, pack,
+forward_routed, combine) driven by vybforge_b200/ep.py, against the fused single-GPU forward.
 
 * N virtual ranks in one process on one GPU (the whole multi-rank data path, with a
   local all-to-all) -- runs wherever a GPU is;
@@ -21,7 +21,7 @@ from helpers import rel_l2, run_ranks, guarded
 pytestmark = pytest.mark.gpu
 
 
-def _layers(cfg, dev, w_r, bias, placement, world):
+def _layers(cfg, dev, w_r, bias, placement, world, partial_dtype=torch.float32):
     E = cfg.n_experts
     kw = dict(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk, router_w=torch.from_numpy(w_r).cuda(),
               router_bias=torch.from_numpy(bias).cuda(), x_dtype=torch.bfloat16 if cfg.x_dtype == "bf16" else torch.float32,
@@ -31,12 +31,16 @@ def _layers(cfg, dev, w_r, bias, placement, world):
     for r in range(world):
         g, u, d, sh = ep.rank_experts(dev, placement, r)
         L = MoELayer(gate=g, up=u, down=d, shared=sh, n_local_experts=E // world, **kw)
-        per.append(ep.EpRank(r, world, ep.GpuBackend(L, placement, world, out_dtype=torch.float32)))
+        per.append(ep.EpRank(r, world, ep.GpuBackend(L, placement, world, out_dtype=torch.float32,
+                                                     partial_dtype=partial_dtype)))
     return full, per
 
 
-@pytest.mark.parametrize("cfg_name,world,T", [("c0", 4, 48), ("c1", 2, 16), ("c1", 8, 64)])
-def test_virtual_ranks_match_single_gpu(cfg_name, world, T):
+# fp32 partial rows: the expert-parallel path reassociates only the fp32 lane sums (1e-4);
+# fp16 partial rows (the default exchange format) add one fp16 rounding per partial (5e-4).
+@pytest.mark.parametrize("cfg_name,world,T,partial", [("c0", 4, 48, "f32"), ("c1", 2, 16, "f32"),
+                                                      ("c1", 8, 64, "f32"), ("c1", 8, 64, "f16")])
+def test_virtual_ranks_match_single_gpu(cfg_name, world, T, partial):
     moe.init(0)
     cfg = synth.config(cfg_name, tokens=T)
     x, w_r, bias, rng = synth.router_inputs(cfg)
@@ -47,7 +51,8 @@ def test_virtual_ranks_match_single_gpu(cfg_name, world, T):
         dev = synth.expert_q8_cuda(cfg, quantizer)
     idx_all, _ = orc.route(x, w_r, bias, cfg.topk)
     placement = ep.balanced_placement(np.bincount(idx_all.reshape(-1), minlength=cfg.n_experts), world)
-    full, ranks = _layers(cfg, dev, w_r, bias, placement, world)
+    pdt = torch.float32 if partial == "f32" else torch.float16
+    full, ranks = _layers(cfg, dev, w_r, bias, placement, world, pdt)
     xd = (torch.from_numpy(x).to(torch.bfloat16) if cfg.x_dtype == "bf16" else torch.from_numpy(x)).cuda()
     ref = full.forward(xd).cpu().numpy()
     shards = np.array_split(np.arange(T), world)
@@ -55,8 +60,8 @@ def test_virtual_ranks_match_single_gpu(cfg_name, world, T):
     got = torch.cat(outs).cpu().numpy()
     for r in ranks:
         r.b.layer.check_device_error()
-    print(f"[ep virtual {cfg_name} N={world} T={T}] rel-L2 vs single GPU {rel_l2(got, ref):.3e}")
-    assert rel_l2(got, ref) < 1e-4
+    print(f"[ep virtual {cfg_name} N={world} T={T} {partial} partials] rel-L2 vs single GPU {rel_l2(got, ref):.3e}")
+    assert rel_l2(got, ref) < (1e-4 if partial == "f32" else 5e-4)
 
 
 def _free_port():
@@ -88,7 +93,7 @@ def _nccl_body(rank, world, port):
         shard = np.array_split(np.arange(cfg.tokens), world)[rank]
         xd = torch.from_numpy(x[shard]).to(torch.bfloat16).cuda()
         out = ep.ep_forward_dist(ep.EpRank(rank, world, ep.GpuBackend(L, placement, world, torch.float32)), xd,
-                                 ep.DistTransport())
+                                 ep.DistTransport())   # default exchange: fp16 partial rows
         L.check_device_error()
         res = out.cpu().numpy()
         dist.barrier()
@@ -115,4 +120,4 @@ def test_two_gpus_nccl_match_single_gpu():
                     shared=(dev[0][E], dev[1][E], dev[2][E]), out_dtype=torch.float32)
     ref = full.forward(torch.from_numpy(x).to(torch.bfloat16).cuda()).cpu().numpy()
     print(f"[ep nccl N=2] rel-L2 vs single GPU {rel_l2(got, ref):.3e}")
-    assert rel_l2(got, ref) < 1e-4
+    assert rel_l2(got, ref) < 5e-4

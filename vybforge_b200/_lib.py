@@ -66,7 +66,10 @@ _SIGS = {
     "vfmoe_forward_rows": (C.c_int, [I64] * 9),
     "vfmoe_ep_plan": (C.c_int, [I64] * 11),
     "vfmoe_ep_pack": (C.c_int, [I64] * 11),
-    "vfmoe_combine": (C.c_int, [I64] * 10),
+    "vfmoe_combine": (C.c_int, [I64] * 11),
+    "vfmoe_ep_plan_tokens": (C.c_int, [I64] * 15),
+    "vfmoe_routed_workspace_bytes": (I64, [I64, I64, I64]),
+    "vfmoe_forward_routed": (C.c_int, [I64] * 12),
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),
     "vfmoe_profile_read": (C.c_int, [I64, C.POINTER(C.c_double), I64, C.POINTER(I64)]),
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),

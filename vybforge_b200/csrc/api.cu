@@ -461,7 +461,7 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
         nlaunch += 4;
     } else {
         rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
-                           reinterpret_cast<__half *>(base + lay.xp), st);
+                           reinterpret_cast<__half *>(base + lay.xp), offsets + L->E + 1, st);
         if (rc) return rc;
         nlaunch += 2;
         mark();
@@ -469,8 +469,9 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     }
     if (rc) return rc;
     mark();
-    rc = launch_combine(a.y, pos_of, w, (int)T, L->H, L->k, L->has_shared ? a.y + T * L->k * L->H : nullptr,
-                        reinterpret_cast<void *>(out), (int)L->d.out_dtype, st);
+    rc = launch_combine(a.y, VFMOE_DT_F32, pos_of, w, (int)T, L->H, L->k,
+                        L->has_shared ? a.y + T * L->k * L->H : nullptr, reinterpret_cast<void *>(out),
+                        (int)L->d.out_dtype, st);
     if (rc) return rc;
     nlaunch += 1;
     mark();
@@ -525,6 +526,76 @@ int64_t vfmoe_rows_workspace_bytes(int64_t handle, int64_t n_max) {
     return ws_layout(*L, n_max, 1).total;
 }
 
+}  // extern "C"
+
+// Expert products on caller-provided rows with caller-provided routing: slots [n, k] are
+// local expert slots (n_local = the shared expert; < 0 = no expert when skip_negative),
+// w [n, k] their weights (0 = weight 1).  y_out[i] = sum_l w[i,l] * FFN_{slots[i,l]}(rows[i]).
+static int rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *sl, int64_t n, int k, const float *w,
+                     int64_t y_out, int y_dtype, int skip_negative, int64_t workspace, int64_t ws_bytes,
+                     cudaStream_t st) {
+    if (n == 0) return VFMOE_OK;
+    if (n * k > (int64_t)1 << 24) {
+        set_error("expert rows: n*k=%lld exceeds 2^24", (long long)(n * k));
+        return VFMOE_ERR_UNSUPPORTED;
+    }
+    char *base;
+    int rc = ensure_ws(L, n, workspace, ws_bytes, &base, k);
+    if (rc) return rc;
+    const WsLayout lay = ws_layout(L, n, k);
+    const int nl = L.n_local;
+    // slot nl = the shared expert: an ordinary bucket of a dispatch over nl + 1 buckets
+    const int nb = nl + (L.has_shared ? 1 : 0);
+    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
+    int32_t *offsets = reinterpret_cast<int32_t *>(base + lay.offsets);
+    int32_t *perm_tok = reinterpret_cast<int32_t *>(base + lay.perm_tok);
+    int32_t *pos_of = reinterpret_cast<int32_t *>(base + lay.pos_of);
+    VF_CUDA(cudaMemsetAsync(counts, 0, (nb + 2) * sizeof(int32_t), st));
+    if ((rc = launch_count(sl, n * k, nb, counts, L.dev_err, st, skip_negative))) return rc;
+    if (skip_negative) VF_CUDA(cudaMemsetAsync(pos_of, 0xFF, n * k * sizeof(int32_t), st));  // -1: no row
+    if ((rc = launch_dispatch(sl, counts, (int)n, nb, k, 0, perm_tok, pos_of, offsets, L.dev_err, st))) return rc;
+    MoeArgs a{};
+    a.T = (int)n;
+    a.H = L.H;
+    a.I = L.I;
+    a.E = nl;
+    a.k = k;
+    a.has_shared = L.has_shared;
+    a.fmt = (int)L.d.weight_format;
+    a.exl3_bits = (int)L.d.exl3_bits;
+    a.limit = (float)L.d.swiglu_limit;
+    a.gate = mref(L.d.gate);
+    a.up = mref(L.d.up);
+    a.down = mref(L.d.down);
+    a.sh_gate = mref(L.d.sh_gate);
+    a.sh_up = mref(L.d.sh_up);
+    a.sh_down = mref(L.d.sh_down);
+    a.offsets = offsets;
+    a.perm_tok = perm_tok;
+    a.xp = reinterpret_cast<__half *>(base + lay.xp);
+    a.act = reinterpret_cast<__half *>(base + lay.act);
+    a.y = reinterpret_cast<float *>(base + lay.y);
+    a.err = L.dev_err;
+    a.tiles = reinterpret_cast<int4 *>(base + lay.tiles);
+    a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
+    a.tiles_cap = lay.tiles_cap;
+    int64_t nlaunch = 0;
+    if (L.x3.ready) {
+        rc = launch_experts_exl3(L.x3, a, reinterpret_cast<const void *>(rows), (int)rows_dtype, st, []() {});
+    } else {
+        if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n * k, L.H,
+                                reinterpret_cast<__half *>(base + lay.xp), offsets + nb + 1, st)))
+            return rc;
+        rc = forward_experts(L, a, st, []() {}, nlaunch);
+    }
+    if (rc) return rc;
+    // back to the callers' row order: y_out[i] = sum_l w[i,l] * y[pos_of[i*k+l]]
+    return launch_combine(a.y, VFMOE_DT_F32, pos_of, w, (int)n, L.H, k, nullptr, reinterpret_cast<void *>(y_out),
+                          y_dtype, st);
+}
+
+extern "C" {
+
 int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t slots, int64_t n, int64_t y_out,
                        int64_t workspace, int64_t ws_bytes, int64_t stream) {
     Layer *L = get_layer(handle);
@@ -534,65 +605,34 @@ int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t
         set_error("vfmoe_forward_rows: bad arguments");
         return VFMOE_ERR_INVALID;
     }
-    if (n == 0) return VFMOE_OK;
-    if (n > (int64_t)1 << 24) {
-        set_error("vfmoe_forward_rows: n=%lld exceeds 2^24", (long long)n);
-        return VFMOE_ERR_UNSUPPORTED;
+    return rows_impl(*L, rows, rows_dtype, reinterpret_cast<const int32_t *>(slots), n, 1, nullptr, y_out,
+                     VFMOE_DT_F32, 0, workspace, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t vfmoe_routed_workspace_bytes(int64_t handle, int64_t n_max, int64_t k) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (n_max < 0 || k <= 0 || k > 32) {
+        set_error("vfmoe_routed_workspace_bytes: bad arguments");
+        return VFMOE_ERR_INVALID;
     }
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    char *base;
-    int rc = ensure_ws(*L, n, workspace, ws_bytes, &base, 1);
-    if (rc) return rc;
-    const WsLayout lay = ws_layout(*L, n, 1);
-    const int nl = L->n_local;
-    // slot nl = the shared expert: an ordinary bucket of a k = 1 dispatch over nl + 1 buckets
-    const int nb = nl + (L->has_shared ? 1 : 0);
-    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
-    int32_t *offsets = reinterpret_cast<int32_t *>(base + lay.offsets);
-    int32_t *perm_tok = reinterpret_cast<int32_t *>(base + lay.perm_tok);
-    int32_t *pos_of = reinterpret_cast<int32_t *>(base + lay.pos_of);
-    const int32_t *sl = reinterpret_cast<const int32_t *>(slots);
-    VF_CUDA(cudaMemsetAsync(counts, 0, (nb + 2) * sizeof(int32_t), st));
-    if ((rc = launch_count(sl, n, nb, counts, L->dev_err, st))) return rc;
-    if ((rc = launch_dispatch(sl, counts, (int)n, nb, 1, 0, perm_tok, pos_of, offsets, L->dev_err, st))) return rc;
-    MoeArgs a{};
-    a.T = (int)n;
-    a.H = L->H;
-    a.I = L->I;
-    a.E = nl;
-    a.k = 1;
-    a.has_shared = L->has_shared;
-    a.fmt = (int)L->d.weight_format;
-    a.exl3_bits = (int)L->d.exl3_bits;
-    a.limit = (float)L->d.swiglu_limit;
-    a.gate = mref(L->d.gate);
-    a.up = mref(L->d.up);
-    a.down = mref(L->d.down);
-    a.sh_gate = mref(L->d.sh_gate);
-    a.sh_up = mref(L->d.sh_up);
-    a.sh_down = mref(L->d.sh_down);
-    a.offsets = offsets;
-    a.perm_tok = perm_tok;
-    a.xp = reinterpret_cast<__half *>(base + lay.xp);
-    a.act = reinterpret_cast<__half *>(base + lay.act);
-    a.y = reinterpret_cast<float *>(base + lay.y);
-    a.err = L->dev_err;
-    a.tiles = reinterpret_cast<int4 *>(base + lay.tiles);
-    a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
-    a.tiles_cap = lay.tiles_cap;
-    int64_t nlaunch = 0;
-    if (L->x3.ready) {
-        rc = launch_experts_exl3(L->x3, a, reinterpret_cast<const void *>(rows), (int)rows_dtype, st, []() {});
-    } else {
-        if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n, L->H,
-                                reinterpret_cast<__half *>(base + lay.xp), st)))
-            return rc;
-        rc = forward_experts(*L, a, st, []() {}, nlaunch);
+    return ws_layout(*L, n_max, (int)k).total;
+}
+
+int vfmoe_forward_routed(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t n, int64_t k, int64_t slots,
+                         int64_t w, int64_t y_out, int64_t y_dtype, int64_t workspace, int64_t ws_bytes,
+                         int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (n < 0 || k <= 0 || k > 32 || (n > 0 && (!rows || !slots || !y_out)) || (rows & 15) ||
+        (rows_dtype != VFMOE_DT_BF16 && rows_dtype != VFMOE_DT_F32) ||
+        (y_dtype != VFMOE_DT_F32 && y_dtype != VFMOE_DT_F16 && y_dtype != VFMOE_DT_BF16)) {
+        set_error("vfmoe_forward_routed: bad arguments");
+        return VFMOE_ERR_INVALID;
     }
-    if (rc) return rc;
-    // back to the callers' row order: y_out[i] = y[pos_of[i]]
-    return launch_combine(a.y, pos_of, nullptr, (int)n, L->H, 1, nullptr, reinterpret_cast<void *>(y_out),
-                          VFMOE_DT_F32, st);
+    return rows_impl(*L, rows, rows_dtype, reinterpret_cast<const int32_t *>(slots), n, (int)k,
+                     reinterpret_cast<const float *>(w), y_out, (int)y_dtype, 1, workspace, ws_bytes,
+                     reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t placement, int64_t n_ranks,
@@ -617,8 +657,9 @@ int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t 
 int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
                   int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream) {
     const int eb = x_dtype == VFMOE_DT_F32 ? 4 : (x_dtype == VFMOE_DT_BF16 || x_dtype == VFMOE_DT_F16 ? 2 : 0);
+    const bool with_slots = slots_out != 0;
     if (!eb || H <= 0 || (H * eb) % 16 || k <= 0 || n_slots < 0 || (x & 15) || (rows_out & 15) ||
-        (n_slots > 0 && (!x || !idx || !send_perm || !local_slot || !rows_out || !slots_out))) {
+        (n_slots > 0 && (!x || !send_perm || !rows_out || (with_slots && (!idx || !local_slot))))) {
         set_error("vfmoe_ep_pack: bad arguments");
         return VFMOE_ERR_INVALID;
     }
@@ -628,17 +669,40 @@ int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx,
                           reinterpret_cast<cudaStream_t>(stream));
 }
 
-int vfmoe_combine(int64_t y, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H, int64_t y_shared,
-                  int64_t out, int64_t out_dtype, int64_t stream) {
-    if (T < 0 || k <= 0 || k > 32 || H <= 0 || H % 4 || (out_dtype != VFMOE_DT_F32 && out_dtype != VFMOE_DT_BF16) ||
+int vfmoe_combine(int64_t y, int64_t y_dtype, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H,
+                  int64_t y_shared, int64_t out, int64_t out_dtype, int64_t stream) {
+    if (T < 0 || k <= 0 || k > 32 || H <= 0 || H % 4 || (y_dtype != VFMOE_DT_F32 && y_dtype != VFMOE_DT_F16) ||
+        (out_dtype != VFMOE_DT_F32 && out_dtype != VFMOE_DT_BF16 && out_dtype != VFMOE_DT_F16) ||
         (T > 0 && (!y || !pos_of || !out)) || (y & 15) || (y_shared & 15)) {
         set_error("vfmoe_combine: bad arguments");
         return VFMOE_ERR_INVALID;
     }
-    return launch_combine(reinterpret_cast<const float *>(y), reinterpret_cast<const int32_t *>(pos_of),
+    return launch_combine(reinterpret_cast<const void *>(y), (int)y_dtype, reinterpret_cast<const int32_t *>(pos_of),
                           reinterpret_cast<const float *>(w), (int)T, (int)H, (int)k,
-                          reinterpret_cast<const float *>(y_shared), reinterpret_cast<void *>(out), (int)out_dtype,
+                          reinterpret_cast<const void *>(y_shared), reinterpret_cast<void *>(out), (int)out_dtype,
                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_ep_plan_tokens(int64_t idx, int64_t w, int64_t T, int64_t k, int64_t n_experts, int64_t placement,
+                         int64_t local_slot, int64_t n_ranks, int64_t send_counts, int64_t send_tok,
+                         int64_t send_slot, int64_t send_w, int64_t pos_of, int64_t err_word, int64_t stream) {
+    if (T < 0 || k <= 0 || k > 32 || n_experts <= 0 || n_ranks <= 0 || n_ranks > 1024 || T > ((int64_t)1 << 24) ||
+        (T > 0 && (!idx || !w || !placement || !local_slot || !send_counts || !send_tok || !send_slot || !send_w ||
+                   !pos_of))) {
+        set_error("vfmoe_ep_plan_tokens: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (T == 0) {
+        VF_CUDA(cudaMemsetAsync(reinterpret_cast<void *>(send_counts), 0, n_ranks * 4, st));
+        return VFMOE_OK;
+    }
+    return launch_ep_plan_tokens(reinterpret_cast<const int32_t *>(idx), reinterpret_cast<const float *>(w), (int)T,
+                                 (int)k, (int)n_experts, reinterpret_cast<const int32_t *>(placement),
+                                 reinterpret_cast<const int32_t *>(local_slot), (int)n_ranks,
+                                 reinterpret_cast<int32_t *>(send_counts), reinterpret_cast<int32_t *>(send_tok),
+                                 reinterpret_cast<int32_t *>(send_slot), reinterpret_cast<float *>(send_w),
+                                 reinterpret_cast<int32_t *>(pos_of), reinterpret_cast<int *>(err_word), st);
 }
 
 int vfmoe_check_device_error(int64_t handle, int64_t stream) {

@@ -25,12 +25,23 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t tk = (int64_t)T * k;
     if (e == E) {  // shared expert: identity segment after the routed rows
+        // routed rows = sum of counts (T*k unless some lanes carry no expert, id < 0)
+        int s = 0;
+        for (int i = tid; i < E; i += 256) s += counts[i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        int routed = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) routed += red[w];
         if (has_shared)
-            for (int t = tid; t < T; t += 256) perm_tok[tk + t] = t;
+            for (int t = tid; t < T; t += 256) perm_tok[routed + t] = t;
         if (tid == 0) {
-            offsets[E] = (int32_t)tk;
-            offsets[E + 1] = (int32_t)(tk + (has_shared ? T : 0));
+            offsets[E] = routed;
+            offsets[E + 1] = routed + (has_shared ? T : 0);
         }
+        (void)tk;
         return;
     }
     int s = 0;
@@ -74,11 +85,13 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
     if (tid == 0 && running != ne) raise_dev_error(err, DEV_BAD_COUNT);
 }
 
-// One CTA (128 threads) per permuted row; H % 8 == 0.
+// One CTA (128 threads) per permuted row; H % 8 == 0.  The grid may exceed the rows the
+// dispatch produced (*n_rows, device-side); the extra CTAs exit.
 __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x, int x_dtype,
                                                      const int32_t *__restrict__ perm_tok, int H,
-                                                     __half *__restrict__ xp) {
+                                                     __half *__restrict__ xp, const int32_t *__restrict__ n_rows) {
     const int64_t pos = blockIdx.x;
+    if (pos >= *n_rows) return;
     const int t = perm_tok[pos];
     __half *dst = xp + pos * H;
     if (x_dtype == VFMOE_DT_BF16) {
@@ -111,34 +124,45 @@ __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x,
 
 // grid (T, H / 1024): 256 threads x 4 columns; H % 4 == 0.  The token's k row positions and
 // weights are staged in shared memory so the k row loads are independent of each other.
-__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
-                                                      const float *__restrict__ w, int T, int H, int k,
-                                                      const float *__restrict__ y_shared, void *__restrict__ out,
-                                                      int out_dtype) {
+// y and y_shared are fp32 or fp16 (y_dtype); a negative position skips its lane.
+__device__ __forceinline__ float4 ld4(const void *p, int64_t i, int dtype) {
+    if (dtype == VFMOE_DT_F16) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(p) + i);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    return *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + i);
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(const void *__restrict__ y, int y_dtype,
+                                                      const int32_t *__restrict__ pos_of, const float *__restrict__ w,
+                                                      int T, int H, int k, const void *__restrict__ y_shared,
+                                                      void *__restrict__ out, int out_dtype) {
     __shared__ int64_t sp[33];
     __shared__ float sw[32];
     const int t = blockIdx.x;
-    const int64_t tk = (int64_t)T * k;
     if (threadIdx.x < k) {
-        sp[threadIdx.x] = (int64_t)pos_of[(int64_t)t * k + threadIdx.x] * H;
+        const int32_t p = pos_of[(int64_t)t * k + threadIdx.x];
+        sp[threadIdx.x] = p < 0 ? -1 : (int64_t)p * H;
         sw[threadIdx.x] = w ? w[(int64_t)t * k + threadIdx.x] : 1.0f;
     }
-    (void)tk;
     __syncthreads();
     const int c = (blockIdx.y * 256 + threadIdx.x) * 4;
     if (c >= H) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
     for (int l = 0; l < k; ++l) {
+        if (sp[l] < 0) continue;
         const float wl = sw[l];
-        const float4 v = *reinterpret_cast<const float4 *>(y + sp[l] + c);
+        const float4 v = ld4(y, sp[l] + c, y_dtype);
         acc.x = fmaf(wl, v.x, acc.x);
         acc.y = fmaf(wl, v.y, acc.y);
         acc.z = fmaf(wl, v.z, acc.z);
         acc.w = fmaf(wl, v.w, acc.w);
     }
     if (y_shared) {
-        const float4 v = *reinterpret_cast<const float4 *>(y_shared + (int64_t)t * H + c);
+        const float4 v = ld4(y_shared, (int64_t)t * H + c, y_dtype);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -151,21 +175,88 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
         pk.x = *reinterpret_cast<const uint32_t *>(&lo);
         pk.y = *reinterpret_cast<const uint32_t *>(&hi);
         *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + o) = pk;
+    } else if (out_dtype == VFMOE_DT_F16) {
+        const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(out) + o) = pk;
     } else {
         *reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + o) = acc;
     }
 }
 
-// Per-bucket counts of n ids in [0, nb): counts[b] += 1 (caller zeroes counts).
+// Per-bucket counts of n ids in [0, nb): counts[b] += 1 (caller zeroes counts).  With
+// skip_negative, ids < 0 mean "no bucket" and are not counted.
 __global__ void count_kernel(const int32_t *__restrict__ ids, int64_t n, int nb, int32_t *__restrict__ counts,
-                             int *__restrict__ err) {
+                             int *__restrict__ err, int skip_negative) {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int b = ids[i];
     if (b >= 0 && b < nb)
         atomicAdd(&counts[b], 1);
-    else
+    else if (!(skip_negative && b < 0))
         raise_dev_error(err, DEV_BAD_EXPERT_ID);
+}
+
+// Token-level expert-parallel send plan (one CTA, 1024 threads): one entry per (token t,
+// rank r) pair where some lane of t routes to an expert r owns, ordered by rank, then
+// token.  Entry i carries send_tok[i] = t and, for each lane l, the owner-local expert
+// slot (or -1 when lane l goes elsewhere) and its routing weight.
+// pos_of[t * n_ranks + r] = entry index or -1.
+__global__ void __launch_bounds__(1024) ep_plan_tokens_kernel(
+    const int32_t *__restrict__ idx, const float *__restrict__ w, int T, int k, int E,
+    const int32_t *__restrict__ placement, const int32_t *__restrict__ local_slot, int n_ranks,
+    int32_t *__restrict__ send_counts, int32_t *__restrict__ send_tok, int32_t *__restrict__ send_slot,
+    float *__restrict__ send_w, int32_t *__restrict__ pos_of, int *__restrict__ err) {
+    __shared__ int warp_tot[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int base = 0;
+    for (int r = 0; r < n_ranks; ++r) {
+        int running = 0;
+        for (int c = 0; c < T; c += 1024) {
+            const int t = c + tid;
+            bool hit = false;
+            if (t < T) {
+                for (int l = 0; l < k; ++l) {
+                    const int e = idx[(int64_t)t * k + l];
+                    const int owner = (e >= 0 && e < E) ? placement[e] : -1;
+                    if (owner < 0 || owner >= n_ranks) {
+                        if (r == 0) raise_dev_error(err, DEV_BAD_EXPERT_ID);
+                    } else if (owner == r) {
+                        hit = true;
+                    }
+                }
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) warp_tot[warp] = __popc(m);
+            __syncthreads();
+            int before = 0, total = 0;
+            for (int q = 0; q < 32; ++q) {
+                const int v = warp_tot[q];
+                before += q < warp ? v : 0;
+                total += v;
+            }
+            if (t < T) {
+                int pos = -1;
+                if (hit) {
+                    pos = base + running + before + __popc(m & ((1u << lane) - 1u));
+                    send_tok[pos] = t;
+                    for (int l = 0; l < k; ++l) {
+                        const int e = idx[(int64_t)t * k + l];
+                        const bool mine = e >= 0 && e < E && placement[e] == r;
+                        send_slot[(int64_t)pos * k + l] = mine ? local_slot[e] : -1;
+                        send_w[(int64_t)pos * k + l] = mine ? w[(int64_t)t * k + l] : 0.f;
+                    }
+                }
+                pos_of[(int64_t)t * n_ranks + r] = pos;
+            }
+            running += total;
+            __syncthreads();
+        }
+        if (tid == 0) send_counts[r] = running;
+        base += running;
+    }
 }
 
 // Expert-parallel send plan (one CTA, 1024 threads): the T*k (token, lane) pairs, stably
@@ -215,7 +306,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict
 }
 
 // Send rows for the expert-parallel exchange: rows[s] = x[send_perm[s] / k] (same dtype),
-// slots[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index).
+// slots[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index) when slots != 0.
 __global__ void __launch_bounds__(128) ep_pack_kernel(const void *__restrict__ x, int elt_bytes, int H, int k,
                                                       const int32_t *__restrict__ idx, const int32_t *__restrict__ send_perm,
                                                       const int32_t *__restrict__ local_slot, void *__restrict__ rows,
@@ -223,16 +314,17 @@ __global__ void __launch_bounds__(128) ep_pack_kernel(const void *__restrict__ x
     const int64_t s = blockIdx.x;
     const int flat = send_perm[s];
     const int t = flat / k;
-    if (threadIdx.x == 0) slots[s] = local_slot[idx[flat]];
+    if (threadIdx.x == 0 && slots) slots[s] = local_slot[idx[flat]];
     const int64_t row_bytes = (int64_t)H * elt_bytes;
     const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(x) + (int64_t)t * row_bytes);
     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(rows) + s * row_bytes);
     for (int64_t i = threadIdx.x; i < row_bytes / 16; i += 128) dst[i] = src[i];
 }
 
-int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st) {
+int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st,
+                 int skip_negative) {
     if (n == 0) return VFMOE_OK;
-    count_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(ids, n, nb, counts, err);
+    count_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(ids, n, nb, counts, err, skip_negative);
     VF_LAUNCH_CHECK("count_kernel");
     return VFMOE_OK;
 }
@@ -241,6 +333,15 @@ int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placemen
                    int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st) {
     ep_plan_kernel<<<1, 1024, 0, st>>>(idx, n, E, placement, n_ranks, send_counts, send_perm, inv_perm, err);
     VF_LAUNCH_CHECK("ep_plan_kernel");
+    return VFMOE_OK;
+}
+
+int launch_ep_plan_tokens(const int32_t *idx, const float *w, int T, int k, int E, const int32_t *placement,
+                          const int32_t *local_slot, int n_ranks, int32_t *send_counts, int32_t *send_tok,
+                          int32_t *send_slot, float *send_w, int32_t *pos_of, int *err, cudaStream_t st) {
+    ep_plan_tokens_kernel<<<1, 1024, 0, st>>>(idx, w, T, k, E, placement, local_slot, n_ranks, send_counts, send_tok,
+                                              send_slot, send_w, pos_of, err);
+    VF_LAUNCH_CHECK("ep_plan_tokens_kernel");
     return VFMOE_OK;
 }
 
@@ -260,18 +361,18 @@ int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int
 }
 
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
-                  cudaStream_t st) {
+                  const int32_t *n_rows, cudaStream_t st) {
     if (rows == 0) return VFMOE_OK;
-    gather_kernel<<<(unsigned)rows, 128, 0, st>>>(x, x_dtype, perm_tok, H, xp);
+    gather_kernel<<<(unsigned)rows, 128, 0, st>>>(x, x_dtype, perm_tok, H, xp, n_rows);
     VF_LAUNCH_CHECK("gather_kernel");
     return VFMOE_OK;
 }
 
-int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, const float *y_shared,
-                   void *out, int out_dtype, cudaStream_t st) {
+int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const float *w, int T, int H, int k,
+                   const void *y_shared, void *out, int out_dtype, cudaStream_t st) {
     if (T == 0) return VFMOE_OK;
     dim3 grid((unsigned)T, (unsigned)cdiv(H, 1024));
-    combine_kernel<<<grid, 256, 0, st>>>(y, pos_of, w, T, H, k, y_shared, out, out_dtype);
+    combine_kernel<<<grid, 256, 0, st>>>(y, y_dtype, pos_of, w, T, H, k, y_shared, out, out_dtype);
     VF_LAUNCH_CHECK("combine_kernel");
     return VFMOE_OK;
 }

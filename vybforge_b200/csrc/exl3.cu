@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(256) gather_exl3_kernel(const void *__restrict
                                                           MatrixRef gate, MatrixRef up, MatrixRef sh_gate,
                                                           MatrixRef sh_up, __half *__restrict__ xp) {
     const int pos = blockIdx.x;
+    if (pos >= offsets[nseg]) return;  // launch size is an upper bound on the rows dispatched
     const int t = perm_tok[pos];
     const int e = segment_of(offsets, nseg, pos);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -458,7 +459,7 @@ static int launch_x(const XParams &prm, int grid, cudaStream_t st) {
 int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, int x_dtype,
                         cudaStream_t st, const std::function<void()> &mid) {
     const int N = gemv_tokens_per_tile(a.T, a.k, a.E);
-    const int64_t rows = (int64_t)a.T * a.k + (a.has_shared ? a.T : 0);
+    const int64_t rows = (int64_t)a.T * a.k + (a.has_shared ? a.T : 0);  // upper bound
     int rc = launch_tc_plan(a, N, N, st);
     if (rc) return rc;
     if (rows > 0) {

@@ -23,7 +23,8 @@ struct MoeArgs {
     int fmt, exl3_bits;
     float limit;
     MatrixRef gate, up, down, sh_gate, sh_up, sh_down;
-    const int32_t *offsets;    // [E+2]: segment e = rows [offsets[e], offsets[e+1]); E = shared
+    const int32_t *offsets;    // [E+2]: segment e = rows [offsets[e], offsets[e+1]); E = shared;
+                               // offsets[E+1] = rows dispatched
     const int32_t *perm_tok;   // [T*k + T]
     const __half *xp;          // [T*k + T, H] gathered activations (fp16)
     __half *act;               // [T*k + T, I] SwiGLU output (fp16)
@@ -44,15 +45,20 @@ int64_t router_logit_floats(int T, int H, int E);
 
 int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);
-int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st);
+int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st,
+                 int skip_negative = 0);
 int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placement, int n_ranks, int32_t *send_counts,
                    int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st);
+int launch_ep_plan_tokens(const int32_t *idx, const float *w, int T, int k, int E, const int32_t *placement,
+                          const int32_t *local_slot, int n_ranks, int32_t *send_counts, int32_t *send_tok,
+                          int32_t *send_slot, float *send_w, int32_t *pos_of, int *err, cudaStream_t st);
 int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
                    const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st);
+// rows = launch size (an upper bound); *n_rows (device) = rows the dispatch produced.
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
-                  cudaStream_t st);
-int launch_combine(const float *y, const int32_t *pos_of, const float *w, int T, int H, int k, const float *y_shared,
-                   void *out, int out_dtype, cudaStream_t st);
+                  const int32_t *n_rows, cudaStream_t st);
+int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const float *w, int T, int H, int k,
+                   const void *y_shared, void *out, int out_dtype, cudaStream_t st);
 
 // `mid` runs between the gate/up and the down launches (profiling marks).
 int launch_experts_simt(const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);

@@ -6,12 +6,17 @@ The reference has no multi-GPU code; this is the expert-parallel form the task a
 - The routed experts are sharded: rank r holds the experts whose `placement[e] == r`, stacked
   in ascending expert order (their local slots).
 
-One forward per rank, in three phases:
-1. route -> `vfmoe_ep_plan` (stable sort of the (token, lane) pairs by owner rank) ->
-   `vfmoe_ep_pack` (send rows + the owner's local slot ids).
-2. exchange counts, then rows and slots (all-to-all-v). Then run `vfmoe_forward_rows` on the
-   received rows plus this rank's own tokens for the shared expert.
-3. all-to-all-v the expert outputs back, then `vfmoe_combine`.
+Token-level exchange, one forward per rank in three phases:
+1. route -> `vfmoe_ep_plan_tokens`: one send entry per (token, destination rank) that owns
+   at least one of the token's experts, carrying the token's k lanes as (owner-local slot
+   or -1, weight) -> `vfmoe_ep_pack` gathers the send rows.
+2. exchange counts, then rows and lane metadata (all-to-all-v). `vfmoe_forward_routed` runs
+   on the received rows plus this rank's own tokens (lane 0 = the shared expert, weight 1),
+   summing each row's local lanes with their weights: one fp16 partial row per entry.
+3. all-to-all-v the partial rows back; `vfmoe_combine` adds, per token, the partials from
+   each rank (rank order) and the shared expert's row.
+A token whose experts live on m ranks crosses the links m times each way, instead of k times
+(once per (token, expert) pair), and the return rows are fp16 partial sums.
 
 The GPU compute is libvfmoe. The all-to-all is a `Transport`:
 - `DistTransport`: torch.distributed over NCCL (NVLink/NVSwitch), or gloo on CPU.
@@ -106,9 +111,14 @@ class VirtualTransport:
 class EpRank:
     """One rank's share of an expert-parallel MoE layer.
 
-    `backend` provides: route(x) -> (idx, w); plan(idx) -> (send_counts, send_perm, inv_perm);
-    pack(x, idx, send_perm) -> (rows, slots); rows(rows, slots) -> y fp32;
-    combine(y_back, inv_perm, w, T, y_shared) -> out.  `GpuBackend` is the libvfmoe one.
+    `backend` provides:
+      route(x) -> (idx, w)
+      plan(idx, w) -> (send_counts, send_tok, send_slot, send_w, pos_of)   (token-level plan)
+      pack(x, send_tok, n) -> rows
+      experts(rows, slots, w) -> partial rows (fp16): sum of the weighted local lanes
+      combine(y_back, pos_of, T, y_shared) -> out
+      shared_slot, k
+    `GpuBackend` is the libvfmoe one.
     """
 
     def __init__(self, rank: int, world: int, backend):
@@ -116,43 +126,66 @@ class EpRank:
 
     def phase1(self, x):
         idx, w = self.b.route(x)
-        counts, perm, inv = self.b.plan(idx)
-        rows, slots = self.b.pack(x, idx, perm)
-        return dict(x=x, idx=idx, w=w, counts=counts, perm=perm, inv=inv, rows=rows, slots=slots)
+        counts, tok, slot, sw, pos = self.b.plan(idx, w)
+        return dict(x=x, counts=counts, tok=tok, slot=slot, sw=sw, pos=pos)
 
-    def phase2(self, st, recv_rows, recv_slots):
+    def pack(self, st, n: int):
+        """Send rows and lane metadata of the n valid entries (n = sum of the send counts)."""
+        st["rows"] = self.b.pack(st["x"], st["tok"], n)
+        # lane metadata as one int32 tensor [n, 2k]: slots, then the weights' bits
+        st["meta"] = torch.cat([st["slot"][:n], st["sw"][:n].view(torch.int32)], dim=1)
+
+    def phase2(self, st, recv_rows, recv_meta):
         x = st["x"]
-        T = x.shape[0]
+        T, k = x.shape[0], self.b.k
         n_recv = recv_rows.shape[0]
-        rows_all = torch.cat([recv_rows, x.to(recv_rows.dtype)]) if T else recv_rows
-        shared = torch.full((T,), self.b.shared_slot, dtype=recv_slots.dtype, device=recv_slots.device)
-        y_all = self.b.rows(rows_all, torch.cat([recv_slots, shared]))
+        slots, wts = recv_meta[:, :k], recv_meta[:, k:].view(torch.float32)
+        # own tokens: lane 0 = shared expert with weight 1, other lanes empty
+        own_s = torch.full((T, k), -1, dtype=torch.int32, device=x.device)
+        own_s[:, 0] = self.b.shared_slot
+        own_w = torch.zeros((T, k), dtype=torch.float32, device=x.device)
+        own_w[:, 0] = 1.0
+        y_all = self.b.experts(torch.cat([recv_rows, x.to(recv_rows.dtype)]), torch.cat([slots, own_s]).contiguous(),
+                               torch.cat([wts, own_w]).contiguous())
         st["y_shared"] = y_all[n_recv:]
         return y_all[:n_recv]
 
     def phase3(self, st, y_back):
         T = st["x"].shape[0]
-        return self.b.combine(y_back, st["inv"], st["w"], T, st["y_shared"])
+        return self.b.combine(y_back, st["pos"], T, st["y_shared"])
 
 
-def ep_forward_dist(rank_state: EpRank, x, transport: DistTransport):
-    """Expert-parallel forward of this process's tokens (one rank per process)."""
+def ep_forward_dist(rank_state: EpRank, x, transport: DistTransport, mark=None):
+    """Expert-parallel forward of this process's tokens (one rank per process).
+    mark(name), if given, is called after each phase (e.g. to record CUDA events)."""
+    mark = mark or (lambda name: None)
     st = rank_state.phase1(x)
+    mark("route_plan")
     recv_splits, send_splits = transport.counts(st["counts"])
+    mark("counts")
+    rank_state.pack(st, sum(send_splits))
+    mark("pack")
     recv_rows = transport.rows(st["rows"], send_splits, recv_splits)
-    recv_slots = transport.rows(st["slots"], send_splits, recv_splits)
-    y_recv = rank_state.phase2(st, recv_rows, recv_slots)
+    recv_meta = transport.rows(st["meta"], send_splits, recv_splits)
+    mark("dispatch")
+    y_recv = rank_state.phase2(st, recv_rows, recv_meta)
+    mark("experts")
     y_back = transport.rows(y_recv, recv_splits, send_splits)
-    return rank_state.phase3(st, y_back)
+    mark("return")
+    out = rank_state.phase3(st, y_back)
+    mark("combine")
+    return out
 
 
 def ep_forward_virtual(ranks, xs, transport: VirtualTransport):
     """Expert-parallel forward of N virtual ranks held by this process."""
     sts = [r.phase1(x) for r, x in zip(ranks, xs)]
     recv_splits, send_splits = transport.counts_all([s["counts"] for s in sts])
+    for r, s, sp in zip(ranks, sts, send_splits):
+        r.pack(s, sum(sp))
     recv_rows = transport.rows_all([s["rows"] for s in sts], send_splits, recv_splits)
-    recv_slots = transport.rows_all([s["slots"] for s in sts], send_splits, recv_splits)
-    y_recv = [r.phase2(s, rr, rs) for r, s, rr, rs in zip(ranks, sts, recv_rows, recv_slots)]
+    recv_meta = transport.rows_all([s["meta"] for s in sts], send_splits, recv_splits)
+    y_recv = [r.phase2(s, rr, rm) for r, s, rr, rm in zip(ranks, sts, recv_rows, recv_meta)]
     y_back = transport.rows_all(y_recv, recv_splits, send_splits)
     return [r.phase3(s, yb) for r, s, yb in zip(ranks, sts, y_back)]
 
@@ -162,31 +195,33 @@ class GpuBackend:
     """libvfmoe kernels for one rank: a MoELayer holding the router (all E experts), the
     shared expert and this rank's routed experts (n_local_experts)."""
 
-    def __init__(self, layer, placement, n_ranks: int, out_dtype=torch.bfloat16):
+    def __init__(self, layer, placement, n_ranks: int, out_dtype=torch.bfloat16, partial_dtype=torch.float16):
         from . import moe
         self.moe = moe
         self.layer = layer
-        self.E = layer.E
+        self.E, self.k = layer.E, layer.k
         self.n_ranks = n_ranks
         self.placement = torch.as_tensor(np.asarray(placement, np.int32)).cuda()
         self.local_slot = torch.as_tensor(local_slots(placement)).cuda()
         self.shared_slot = layer.n_local
         self.out_dtype = out_dtype
+        self.partial_dtype = partial_dtype
 
     def route(self, x):
         return self.layer.route(x)
 
-    def plan(self, idx):
-        return self.moe.ep_plan(idx, self.E, self.placement, self.n_ranks)
+    def plan(self, idx, w):
+        return self.moe.ep_plan_tokens(idx, w, self.E, self.placement, self.local_slot, self.n_ranks)
 
-    def pack(self, x, idx, perm):
-        return self.moe.ep_pack(x, idx, perm, self.local_slot)
+    def pack(self, x, tok, n):
+        return self.moe.gather_rows(x, tok, n)
 
-    def rows(self, rows, slots):
-        return self.layer.forward_rows(rows, slots)
+    def experts(self, rows, slots, w):
+        return self.layer.forward_routed(rows, slots, w, y_dtype=self.partial_dtype)
 
-    def combine(self, y_back, inv, w, T, y_shared):
-        return self.moe.combine(y_back, inv, w, T, self.layer.k, y_shared=y_shared, out_dtype=self.out_dtype)
+    def combine(self, y_back, pos, T, y_shared):
+        return self.moe.combine(y_back, pos.reshape(-1), None, T, self.n_ranks, y_shared=y_shared,
+                                out_dtype=self.out_dtype)
 
 
 def rank_experts(dev, placement, rank: int):

@@ -138,6 +138,21 @@ class MoELayer:
                                           _ptr(self._rows_ws), self._rows_ws.numel(), _stream()))
         return y
 
+    def forward_routed(self, rows: torch.Tensor, slots: torch.Tensor, w: torch.Tensor, y_dtype=torch.float16,
+                       y: torch.Tensor | None = None):
+        """y[i] = sum_l w[i,l] * FFN_{slots[i,l]}(rows[i]) over lanes with slots >= 0; slot n_local =
+        shared expert."""
+        n, k = slots.shape
+        if y is None:
+            y = torch.empty((n, self.H), dtype=y_dtype, device=rows.device)
+        need = check(self.lib.vfmoe_routed_workspace_bytes(self.handle, n, k))
+        if self._rows_ws is None or self._rows_ws.numel() < need:
+            self._rows_ws = torch.empty(need, dtype=torch.uint8, device=rows.device)
+        check(self.lib.vfmoe_forward_routed(self.handle, _ptr(rows), _DT[rows.dtype], n, k, _ptr(slots), _ptr(w),
+                                            _ptr(y), _DT[y.dtype], _ptr(self._rows_ws), self._rows_ws.numel(),
+                                            _stream()))
+        return y
+
     def check_device_error(self):
         check(self.lib.vfmoe_check_device_error(self.handle, _stream()))
 
@@ -193,13 +208,42 @@ def ep_pack(x: torch.Tensor, idx: torch.Tensor, send_perm: torch.Tensor, local_s
     return rows, slots
 
 
-def combine(y: torch.Tensor, pos_of: torch.Tensor, w: torch.Tensor, T: int, k: int, y_shared=None,
+def combine(y: torch.Tensor, pos_of: torch.Tensor, w, T: int, k: int, y_shared=None,
             out_dtype=torch.bfloat16) -> torch.Tensor:
+    """out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] (+ y_shared[t]); y fp32 or fp16; pos < 0 skips."""
     H = y.shape[1]
     out = torch.empty((T, H), dtype=out_dtype, device=y.device)
-    check(_lib.load().vfmoe_combine(_ptr(y), _ptr(pos_of), _ptr(w), T, k, H, _ptr(y_shared), _ptr(out),
+    if y_shared is not None:
+        assert y_shared.dtype == y.dtype
+    check(_lib.load().vfmoe_combine(_ptr(y), _DT[y.dtype], _ptr(pos_of), _ptr(w), T, k, H, _ptr(y_shared), _ptr(out),
                                     _DT[out_dtype], _stream()))
     return out
+
+
+def ep_plan_tokens(idx: torch.Tensor, w: torch.Tensor, n_experts: int, placement: torch.Tensor,
+                   local_slot: torch.Tensor, n_ranks: int):
+    """Token-level send plan: (send_counts [n_ranks], send_tok [T*n_ranks], send_slot [T*n_ranks, k],
+    send_w [T*n_ranks, k], pos_of [T, n_ranks]); entries [0, sum(send_counts)) are valid."""
+    T, k = idx.shape
+    dev = idx.device
+    counts = torch.empty(n_ranks, dtype=torch.int32, device=dev)
+    n = T * n_ranks
+    tok = torch.empty(n, dtype=torch.int32, device=dev)
+    slot = torch.empty((n, k), dtype=torch.int32, device=dev)
+    sw = torch.empty((n, k), dtype=torch.float32, device=dev)
+    pos = torch.empty((T, n_ranks), dtype=torch.int32, device=dev)
+    check(_lib.load().vfmoe_ep_plan_tokens(_ptr(idx), _ptr(w), T, k, n_experts, _ptr(placement), _ptr(local_slot),
+                                           n_ranks, _ptr(counts), _ptr(tok), _ptr(slot), _ptr(sw), _ptr(pos), 0,
+                                           _stream()))
+    return counts, tok, slot, sw, pos
+
+
+def gather_rows(x: torch.Tensor, tok: torch.Tensor, n: int) -> torch.Tensor:
+    """rows[i] = x[tok[i]] for i < n (x dtype)."""
+    rows = torch.empty((n, x.shape[1]), dtype=x.dtype, device=x.device)
+    check(_lib.load().vfmoe_ep_pack(_ptr(x), _DT[x.dtype], x.shape[1], 1, 0, _ptr(tok), 0, n, _ptr(rows), 0,
+                                    _stream()))
+    return rows
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

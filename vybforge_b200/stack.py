@@ -50,13 +50,18 @@ class EpStack:
         assert len(ranks) == len(norm_w) and ranks
         self.ranks, self.norm_w, self.eps = ranks, norm_w, eps
 
-    def forward_dist(self, x: torch.Tensor, transport) -> torch.Tensor:
-        """This rank's tokens through all layers (one rank per process)."""
+    def forward_dist(self, x: torch.Tensor, transport, mark=None) -> torch.Tensor:
+        """This rank's tokens through all layers (one rank per process); mark as in
+        ep.ep_forward_dist, plus "norm" after each residual/norm step."""
         L = len(self.ranks)
         x, h = residual_rmsnorm(x, None, self.norm_w[0], self.eps)
+        if mark:
+            mark("norm")
         for l, r in enumerate(self.ranks):
-            y = ep.ep_forward_dist(r, h, transport)
+            y = ep.ep_forward_dist(r, h, transport, mark)
             x, h = residual_rmsnorm(x, y, self.norm_w[l + 1] if l + 1 < L else None, self.eps)
+            if mark:
+                mark("norm")
         return x
 
 
