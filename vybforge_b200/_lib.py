@@ -1,7 +1,7 @@
 """ctypes binding of libvfmoe.so (the C ABI in include/vfmoe.h).
 
-This is the same binding a non-Python host makes (INTEGRATION.md shows the Vyb
-``extern "C"`` block): plain int64 addresses, int status codes.  If the library
+This is the same binding a non-Python host makes (a Vyb host declares the same functions
+in an ``extern "C"`` block): plain int64 addresses, int status codes.  If the library
 is missing the import fails loudly -- there is no CPU fallback.
 """
 
