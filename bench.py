@@ -464,6 +464,53 @@ def stack_extra(a, rank, world, local_rank, flush):
     return out
 
 
+def exl3_extra(a, flush):
+    """C2 (decode T=32 and T=1) and C3 with EXL3 3-bpw weights (prefill T=4096, Zipf(1.1)),
+    on one GPU: the same layer shapes as C1."""
+    import torch
+    from vybforge_b200 import synth
+    from vybforge_b200.moe import MoELayer
+    cfg = synth.config("c2", tokens=32)
+    x, w_r, bias, _ = synth.router_inputs(cfg)
+    dev = synth.expert_exl3_cuda(cfg)
+    E, H, I = cfg.n_experts, cfg.hidden, cfg.inter
+    pk, pk_kind = peaks()
+    mats = dict(gate=tuple(t[:E] for t in dev[0]), up=tuple(t[:E] for t in dev[1]), down=tuple(t[:E] for t in dev[2]),
+                shared=tuple(tuple(t[E] for t in dev[p]) for p in range(3)), fmt="exl3")
+
+    def make(w_r_, bias_):
+        return MoELayer(hidden=H, inter=I, n_experts=E, topk=cfg.topk, router_w=torch.from_numpy(w_r_).cuda(),
+                        router_bias=torch.from_numpy(bias_).cuda(), x_dtype=torch.bfloat16,
+                        out_dtype=torch.bfloat16, **mats)
+    out = {}
+    layer = make(w_r, bias)
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    for T in (32, 1):
+        ms, st_, _, idx = time_layer(layer, xd[:T].contiguous(), a.steps, a.warmup, flush)
+        c = synth.config("c2", tokens=T)
+        lb, gub = algorithmic_bytes(c, len(np.unique(idx.cpu().numpy())))
+        out[f"c2_t{T}"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                           "gate_up_hbm_frac": round(gub / (st_["gate_up"] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                           "layer_hbm_frac": round(lb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                           "stage_ms_per_step": {n: round(v, 4) for n, v in st_.items()},
+                           "note": "EXL3 decode GEMV is bound by the trellis decode's integer work, not HBM"}
+    layer.close()
+    c3 = synth.config("c3", tokens=4096, fmt="exl3")
+    x3, w3, b3, _, _ = synth.zipf_router_inputs(c3)
+    layer = make(w3, b3)
+    ms, st_, launches, idx = time_layer(layer, torch.from_numpy(x3).to(torch.bfloat16).cuda(), max(5, a.steps // 2),
+                                        a.warmup, flush)
+    T, k = c3.tokens, c3.topk
+    flops = 6.0 * H * I * T * (k + 1) + 2.0 * H * E * T
+    out["c3_prefill_exl3"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                              "layer_tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                              "frac_of_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                              "stage_ms_per_step": {n: round(v, 4) for n, v in st_.items()},
+                              "note": "EXL3 prefill runs the decode GEMV (32-row token tiles): no tcgen05 EXL3 path yet"}
+    layer.close()
+    return out
+
+
 def run_ours_ep(a, rank, world, local_rank):
     """N > 1: the C1 layer expert-parallel over NCCL.  Each rank holds E/N routed experts
     (contiguous placement; decode routing is uniform), the router and the shared expert,
@@ -682,6 +729,8 @@ def run_ours(a, rank, world, local_rank):
         layer.close()
         torch.cuda.empty_cache()
         res["extra"].update(stack_extra(a, rank, world, local_rank, flush))
+        torch.cuda.empty_cache()
+        res["extra"].update(exl3_extra(a, flush))
     return res
 
 
