@@ -29,6 +29,7 @@ class NumpyBackend:
         self.my = np.nonzero(self.placement == rank)[0]          # global ids of local slots
         self.shared_slot = len(self.my)
         self.k = cfg.topk
+        self.partial_dtype = torch.float64
         H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
 
         def mats(e):

@@ -10,9 +10,10 @@ Token-level exchange, one forward per rank in three phases:
 1. route -> `vfmoe_ep_plan_tokens`: one send entry per (token, destination rank) that owns
    at least one of the token's experts, carrying the token's k lanes as (owner-local slot
    or -1, weight) -> `vfmoe_ep_pack` gathers the send rows.
-2. exchange counts, then rows and lane metadata (all-to-all-v). `vfmoe_forward_routed` runs
-   on the received rows plus this rank's own tokens (lane 0 = the shared expert, weight 1),
-   summing each row's local lanes with their weights: one fp16 partial row per entry.
+2. exchange counts, then rows and lane metadata (all-to-all-v). While the rows are in
+   flight, `vfmoe_forward_routed` runs the shared expert on this rank's own tokens; then on
+   the received rows, summing each row's local lanes with their weights: one fp16 partial
+   row per entry.
 3. all-to-all-v the partial rows back; `vfmoe_combine` adds, per token, the partials from
    each rank (rank order) and the shared expert's row.
 A token whose experts live on m ranks crosses the links m times each way, instead of k times
@@ -38,21 +39,27 @@ def contiguous_placement(n_experts: int, n_ranks: int) -> np.ndarray:
     return (np.arange(n_experts) // (n_experts // n_ranks)).astype(np.int32)
 
 
-def balanced_placement(load, n_ranks: int) -> np.ndarray:
+def balanced_placement(load, n_ranks: int, tile_rows: int = 128, tile_cost: float = 1.4) -> np.ndarray:
     """Load-aware placement with exactly E/n_ranks experts per rank: experts in descending
-    load order go to the least-loaded rank that still has room (greedy bin packing)."""
+    cost order go to the least-loaded rank that still has room (greedy bin packing).
+
+    cost(e) = rows(e) + tile_cost * tile_rows * ceil(rows(e) / tile_rows): an expert's prefill
+    GEMM pays per token tile for streaming and dequantizing its weights, whatever the tile's
+    row count, so many cold experts cost more than their rows suggest.  tile_cost = 0 is a
+    balance of rows alone."""
     load = np.asarray(load, dtype=np.float64)
     E = load.shape[0]
     if E % n_ranks:
         raise ValueError("n_experts must be divisible by n_ranks")
+    cost = load + tile_cost * tile_rows * np.ceil(load / tile_rows)
     cap = E // n_ranks
     owner = np.empty(E, dtype=np.int32)
     tot = np.zeros(n_ranks)
     room = np.full(n_ranks, cap)
-    for e in np.argsort(-load, kind="stable"):
+    for e in np.argsort(-cost, kind="stable"):
         r = min((r for r in range(n_ranks) if room[r] > 0), key=lambda r: (tot[r], r))
         owner[e] = r
-        tot[r] += load[e]
+        tot[r] += cost[e]
         room[r] -= 1
     return owner
 
@@ -85,10 +92,17 @@ class DistTransport:
         return out.tolist(), send_counts.tolist()
 
     def rows(self, send, send_splits, recv_splits):
-        recv = torch.empty((sum(recv_splits),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-        self.dist.all_to_all_single(recv, send, output_split_sizes=recv_splits, input_split_sizes=send_splits,
-                                    group=self.group)
+        recv, work = self.rows_async(send, send_splits, recv_splits)
+        work.wait()
         return recv
+
+    def rows_async(self, send, send_splits, recv_splits):
+        """Start the exchange on the collective stream; work.wait() orders later work on the
+        current stream after it.  Work enqueued meanwhile overlaps the transfer."""
+        recv = torch.empty((sum(recv_splits),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        work = self.dist.all_to_all_single(recv, send, output_split_sizes=recv_splits, input_split_sizes=send_splits,
+                                           group=self.group, async_op=True)
+        return recv, work
 
 
 class VirtualTransport:
@@ -116,6 +130,7 @@ class EpRank:
       plan(idx, w) -> (send_counts, send_tok, send_slot, send_w, pos_of)   (token-level plan)
       pack(x, send_tok, n) -> rows
       experts(rows, slots, w) -> partial rows (fp16): sum of the weighted local lanes
+      (also the shared expert: one lane with slot shared_slot, weight 1)
       combine(y_back, pos_of, T, y_shared) -> out
       shared_slot, k
     `GpuBackend` is the libvfmoe one.
@@ -135,20 +150,20 @@ class EpRank:
         # lane metadata as one int32 tensor [n, 2k]: slots, then the weights' bits
         st["meta"] = torch.cat([st["slot"][:n], st["sw"][:n].view(torch.int32)], dim=1)
 
-    def phase2(self, st, recv_rows, recv_meta):
+    def shared(self, st):
+        """The shared expert on this rank's own tokens (weight 1, one lane)."""
         x = st["x"]
-        T, k = x.shape[0], self.b.k
-        n_recv = recv_rows.shape[0]
+        T = x.shape[0]
+        own_s = torch.full((T, 1), self.b.shared_slot, dtype=torch.int32, device=x.device)
+        own_w = torch.ones((T, 1), dtype=torch.float32, device=x.device)
+        st["y_shared"] = self.b.experts(x, own_s, own_w)
+
+    def phase2(self, st, recv_rows, recv_meta):
+        k = self.b.k
+        if recv_rows.shape[0] == 0:
+            return torch.empty((0, st["x"].shape[1]), dtype=self.b.partial_dtype, device=st["x"].device)
         slots, wts = recv_meta[:, :k], recv_meta[:, k:].view(torch.float32)
-        # own tokens: lane 0 = shared expert with weight 1, other lanes empty
-        own_s = torch.full((T, k), -1, dtype=torch.int32, device=x.device)
-        own_s[:, 0] = self.b.shared_slot
-        own_w = torch.zeros((T, k), dtype=torch.float32, device=x.device)
-        own_w[:, 0] = 1.0
-        y_all = self.b.experts(torch.cat([recv_rows, x.to(recv_rows.dtype)]), torch.cat([slots, own_s]).contiguous(),
-                               torch.cat([wts, own_w]).contiguous())
-        st["y_shared"] = y_all[n_recv:]
-        return y_all[:n_recv]
+        return self.b.experts(recv_rows, slots.contiguous(), wts.contiguous())
 
     def phase3(self, st, y_back):
         T = st["x"].shape[0]
@@ -165,8 +180,13 @@ def ep_forward_dist(rank_state: EpRank, x, transport: DistTransport, mark=None):
     mark("counts")
     rank_state.pack(st, sum(send_splits))
     mark("pack")
-    recv_rows = transport.rows(st["rows"], send_splits, recv_splits)
-    recv_meta = transport.rows(st["meta"], send_splits, recv_splits)
+    # the shared expert on this rank's tokens runs while the rows are in flight
+    recv_rows, w_rows = transport.rows_async(st["rows"], send_splits, recv_splits)
+    recv_meta, w_meta = transport.rows_async(st["meta"], send_splits, recv_splits)
+    rank_state.shared(st)
+    mark("shared")
+    w_rows.wait()
+    w_meta.wait()
     mark("dispatch")
     y_recv = rank_state.phase2(st, recv_rows, recv_meta)
     mark("experts")
@@ -185,6 +205,8 @@ def ep_forward_virtual(ranks, xs, transport: VirtualTransport):
         r.pack(s, sum(sp))
     recv_rows = transport.rows_all([s["rows"] for s in sts], send_splits, recv_splits)
     recv_meta = transport.rows_all([s["meta"] for s in sts], send_splits, recv_splits)
+    for r, s in zip(ranks, sts):
+        r.shared(s)
     y_recv = [r.phase2(s, rr, rm) for r, s, rr, rm in zip(ranks, sts, recv_rows, recv_meta)]
     y_back = transport.rows_all(y_recv, recv_splits, send_splits)
     return [r.phase3(s, yb) for r, s, yb in zip(ranks, sts, y_back)]

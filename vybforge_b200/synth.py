@@ -147,12 +147,13 @@ def stack_inputs(cfg: LayerConfig, n_layers: int, calib_tokens: int = 2048):
 
     Returns (x, norm_ws, routers): x the stack input (cfg's ordinary token draw), norm_ws
     a list of fp32 [H] RMSNorm weights 1 + N(0, 0.02), routers a list of (w_r, bias,
-    targets) per layer.  Layer l's router (W_r ~ N(0, 0.02), bias ~ N(0, 0.01)) is drawn
+    load) per layer.  Layer l's router (W_r ~ N(0, 0.02), bias ~ N(0, 0.01)) is drawn
     from the stream seeded (seed, 1000 + l).  With
     cfg.zipf_s > 0 its selection bias is calibrated (as in zipf_router_inputs) on the
     first `calib_tokens` rows of RMSNorm_l(x): later layers see the residual stream
-    instead, so their realized popularity is only approximately Zipf.  targets is the
-    expected selection count per expert (Zipf targets, or the uniform T*k/E)."""
+    instead, so their realized popularity is only approximately Zipf.  load is the layer's
+    selection count per expert on RMSNorm_l(x) over all tokens (the expert-placement input;
+    layers after the first see the residual stream, so it is an estimate there)."""
     x, _, _, rng = router_inputs(cfg)
     norm_ws = [(1.0 + rng.normal(0.0, 0.02, cfg.hidden)).astype(np.float32) for _ in range(n_layers)]
     routers = []
@@ -166,12 +167,24 @@ def stack_inputs(cfg: LayerConfig, n_layers: int, calib_tokens: int = 2048):
             logits = h @ w_r.astype(np.float64).T
             tgt = zipf_targets(cfg.n_experts, len(xs), cfg.topk, cfg.zipf_s, np.random.default_rng((cfg.seed, 2000 + l)))
             bias = calibrate_zipf_bias(logits, bias0, cfg.topk, tgt)
-            tgt = tgt * (cfg.tokens / len(xs))
         else:
             bias = bias0
-            tgt = np.full(cfg.n_experts, cfg.tokens * cfg.topk / cfg.n_experts)
-        routers.append((w_r, bias, tgt))
+        routers.append((w_r, bias, selection_counts(x, norm_ws[l], w_r, bias, cfg.topk)))
     return x, norm_ws, routers
+
+
+def selection_counts(x, norm_w, w_r, bias, topk, chunk=2048):
+    """Per-expert selection counts of RMSNorm(x) under a router (fp32 logits; used only to
+    estimate expert load for placement, so near ties do not matter)."""
+    cnt = np.zeros(w_r.shape[0], dtype=np.int64)
+    wt = np.ascontiguousarray(w_r.T, dtype=np.float32)
+    for a in range(0, x.shape[0], chunk):
+        xs = x[a:a + chunk].astype(np.float32)
+        h = xs / np.sqrt(np.mean(xs * xs, axis=1, keepdims=True) + 1e-5) * norm_w
+        s = 1.0 / (1.0 + np.exp(-(h @ wt)))
+        sel = np.argpartition(-(s + bias[None, :]), topk - 1, axis=1)[:, :topk]
+        cnt += np.bincount(sel.reshape(-1), minlength=w_r.shape[0])
+    return cnt
 
 
 def realized_counts(idx, n_experts):
