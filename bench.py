@@ -506,7 +506,8 @@ def exl3_extra(a, flush):
                               "layer_tflops": round(flops / (ms * 1e-3) / 1e12, 1),
                               "frac_of_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
                               "stage_ms_per_step": {n: round(v, 4) for n, v in st_.items()},
-                              "note": "EXL3 prefill runs the decode GEMV (32-row token tiles): no tcgen05 EXL3 path yet"}
+                              "note": "tcgen05 EXL3 GEMMs (trellis decoded into TMEM, Hadamard epilogues); "
+                                      "bound by the trellis decode's integer work"}
     layer.close()
     return out
 

@@ -42,6 +42,34 @@ def test_exl3_small_parity(small, T):
     _check(small, out.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), np.arange(T), f"exl3 c0-shape T={T}")
 
 
+@pytest.fixture(scope="module")
+def prefill():
+    """C0 shapes with EXL3 weights, 256 tokens: 64 rows per expert on average, so the
+    tcgen05 prefill kernels run (128-row gate/up tiles, 256-row down tiles)."""
+    moe.init(0)
+    return Built(synth.config("c0", tokens=256, fmt="exl3"))
+
+
+def test_exl3_prefill_tcgen05_parity(prefill):
+    b = prefill
+    out, idx, w = b.layer.moe_block(b.x_dev)
+    torch.cuda.synchronize()
+    b.layer.check_device_error()
+    _check(b, out.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), np.arange(b.cfg.tokens),
+           "exl3 c0-shape T=256 tcgen05")
+
+
+def test_exl3_prefill_and_decode_paths_agree(prefill):
+    """Rows 0..15 through the decode GEMV (T=16: 4 rows per expert) and inside the T=256
+    prefill batch (tcgen05): same per-token results up to fp32 summation order."""
+    b = prefill
+    full = b.layer.forward(b.x_dev)
+    part = b.layer.forward(b.x_dev[:16].contiguous())
+    d = rel_l2(part.cpu().numpy(), full[:16].cpu().numpy())
+    print(f"[exl3 prefill vs decode path] rel-L2 {d:.3e}")
+    assert d < 5e-4
+
+
 def test_exl3_bf16_output_is_rounded_fp32_output(small):
     l16 = small.make_layer(torch.bfloat16)
     o16 = l16.forward(small.x_dev)

@@ -365,6 +365,356 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __gri
     if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
 }
 
+// ----------------------------------------------------------------------------- prefill (tcgen05)
+// Many tokens per expert: the trellis of a 128-channel tile is decoded once per tile of up to
+// N token rows and fed to tcgen05.mma, as in the Q8_0 tensor-core GEMM (expert_tc.cu):
+//   A = decoded Ŵ columns, one output channel per TMEM lane, written with tcgen05.st by 16
+//       decode warps (4 sub-stage slots of 64 K in TMEM);
+//   B = rotated token rows (fp16, SWIZZLE_128B TMA tiles; gate/up read the gate and the up
+//       rotation of each row through a 3D view of the interleaved x_perm);
+//   D = fp32 accumulators in TMEM.
+// The trellis streams in by TMA as 16 k-tiles x 8 column blocks per matrix and stage (12 KB,
+// [column block][k-tile][96 B] as for the decode GEMV).  The epilogue applies the output
+// Hadamard across the 128 channels = TMEM lanes: butterflies of stride 1..16 by warp
+// shuffles, strides 32 and 64 through shared memory among the four quarter warps of a group.
+// Warp roles as expert_tc.cu: 0 TMA, 1 MMA issuer, 2 TMEM allocator, 4..19 decode + epilogue.
+// Every mbarrier wait is bounded (2 s).
+constexpr int kXtThreads = 640;
+constexpr int kXtDq = 16;
+constexpr int kXtSA = 4;                           // TMEM A ring slots (64 K each)
+constexpr int kXtRawMat = kKT * 8 * kTileBytes3;  // 12 KB: one matrix, one 256-K stage
+constexpr int kXchLd = 9;                          // exchange row stride (floats), 8 columns + pad
+
+template <bool GATEUP, int N>
+struct XtCfg {
+    static constexpr int MATS = GATEUP ? 2 : 1;
+    static constexpr int TOK_BOX = N * 128;                 // N rows x 64 K fp16
+    static constexpr int TOK_STAGE = MATS * TOK_BOX;        // gate/up: both rotations
+    static constexpr int RAW_STAGE = MATS * kXtRawMat;
+    static constexpr int XCH = 4 * 128 * kXchLd * 4;        // one [128][9] buffer per epilogue group
+    static constexpr int BUDGET = 232448 - 1024 - 256 - XCH;
+    static constexpr int SB = (BUDGET - 3 * RAW_STAGE) / TOK_STAGE >= 4 ? 4 : 3;
+    static constexpr int SW_FIT = (BUDGET - SB * TOK_STAGE) / RAW_STAGE;
+    static constexpr int SW = SW_FIT > 4 ? 4 : SW_FIT;
+    static constexpr int RAW_BYTES = SW * RAW_STAGE;
+    static constexpr int TOK_BYTES = SB * TOK_STAGE;
+    static constexpr int XCH_OFF = RAW_BYTES + TOK_BYTES;
+    static constexpr int BAR_OFF = XCH_OFF + XCH;
+    static constexpr int NBAR = 2 * SW + 2 * kXtSA + 2 * SB + 3;
+    static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;
+    static constexpr int D_COLS = MATS * N;
+    static constexpr int A_COL0 = D_COLS;
+    static constexpr int DQ_PER_SUB = GATEUP ? kXtDq : kXtDq / 2;
+    static_assert(SW >= 2, "double-buffered trellis stages");
+    static_assert(D_COLS + kXtSA * MATS * 32 <= 512, "TMEM budget");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// Window at bit O of the 64-bit little-endian stream (lo, hi), 16 bits.
+template <int O>
+__device__ __forceinline__ uint32_t win64(uint32_t lo, uint32_t hi) {
+    if constexpr (O == 0) {
+        return lo & 0xFFFFu;
+    } else if constexpr (O < 32) {
+        return __funnelshift_r(lo, hi, O) & 0xFFFFu;
+    } else {
+        return (hi >> (O - 32)) & 0xFFFFu;
+    }
+}
+
+// One trellis column c (16 windows at bits [48c, 48c+61) of the tile's circular stream) ->
+// 8 fp16 pairs (k = 2p, 2p + 1), decoded exactly as the reference (fp16(lo + hi)).
+template <int P>
+__device__ __forceinline__ void decode_col(uint32_t lo, uint32_t hi, uint32_t kxor, uint32_t *out) {
+    out[P] = mcg_pair(win64<6 * P>(lo, hi), win64<6 * P + 3>(lo, hi), kxor);
+    if constexpr (P < 7) decode_col<P + 1>(lo, hi, kxor, out);
+}
+
+__device__ __forceinline__ void trellis_column(const uint8_t *tile, int c, uint32_t kxor, uint32_t *out) {
+    const uint32_t *tw = reinterpret_cast<const uint32_t *>(tile);
+    const int i0 = (3 * c) >> 1;                      // u32 holding u16 word 3c
+    const uint32_t a = tw[i0], b = tw[i0 + 1], d = tw[i0 + 2 < 24 ? i0 + 2 : i0 + 2 - 24];
+    const uint32_t lo = (c & 1) ? __funnelshift_r(a, b, 16) : a;
+    const uint32_t hi = (c & 1) ? __funnelshift_r(b, d, 16) : b;
+    decode_col<0>(lo, hi, kxor, out);
+}
+
+// 128-point FWHT over the channels of a group's four quarter warps (channel r = 32q + lane),
+// for 8 columns per thread.  xb: the group's [128][kXchLd] exchange buffer; bar_id: its
+// named barrier (128 threads).
+__device__ __forceinline__ void fwht128_lanes(float (&v)[8], float *xb, int q, int lane, int bar_id) {
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[j], s);
+            v[j] = (lane & s) ? (o - v[j]) : (v[j] + o);
+        }
+    }
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");  // buffer free
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xb[(32 * q + lane) * kXchLd + j] = v[j];
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float x0 = xb[lane * kXchLd + j], x1 = xb[(32 + lane) * kXchLd + j];
+        const float x2 = xb[(64 + lane) * kXchLd + j], x3 = xb[(96 + lane) * kXchLd + j];
+        // 4-point Sylvester Hadamard over the stride-32 / stride-64 index bits (q)
+        const float s01 = (q & 1) ? (x0 - x1) : (x0 + x1);
+        const float s23 = (q & 1) ? (x2 - x3) : (x2 + x3);
+        v[j] = (q & 2) ? (s01 - s23) : (s01 + s23);
+    }
+}
+
+template <bool GATEUP, int N>
+__global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __grid_constant__ XParams p) {
+    using C = XtCfg<GATEUP, N>;
+    constexpr int MATS = C::MATS, SW = C::SW, SB = C::SB;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *raw = smem;
+    uint8_t *tok = smem + C::RAW_BYTES;
+    float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *raw_full = bars, *raw_empty = bars + SW;
+    uint64_t *a_full = bars + 2 * SW, *a_empty = a_full + kXtSA;
+    uint64_t *b_full = a_empty + kXtSA, *b_empty = b_full + SB;
+    uint64_t *d_full = b_empty + SB, *d_empty = d_full + 1, *mma_done = d_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBAR);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int MT = p.M / 128;
+    const int KR = p.K / 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SW; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kXtDq);
+        }
+        for (int i = 0; i < kXtSA; ++i) {
+            mbar_init(&a_full[i], C::DQ_PER_SUB);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < SB; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        mbar_init(d_full, 1);
+        mbar_init(d_empty, kXtDq);
+        mbar_init(mma_done, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.wa);
+        prefetch_tmap(&p.swa);
+        prefetch_tmap(&p.xt);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_items = (*p.n_tiles) * MT;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t nraw = 0, ntok = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int4 t = p.tiles[item / MT];
+                const int nb0 = (item % MT) * 8;
+                const bool sh = t.x == p.E;
+                const CUtensorMap *ma = sh ? &p.swa : &p.wa;
+                const CUtensorMap *mb = sh ? &p.swb : &p.wb;
+                const int z = sh ? 0 : t.x;
+                const int n16 = (t.z + 15) >> 4;
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    const uint32_t rs = nraw % SW;
+                    if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
+                    mbar_arrive_expect_tx(&raw_full[rs], C::RAW_STAGE);
+                    uint8_t *dst = raw + rs * C::RAW_STAGE;
+                    tma_load_4d(dst, ma, &raw_full[rs], 0, kr * kKT, nb0, z);
+                    if (GATEUP) tma_load_4d(dst + kXtRawMat, mb, &raw_full[rs], 0, kr * kKT, nb0, z);
+                    ++nraw;
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t bs = ntok % SB;
+                        if (!(ok = mbar_wait(&b_empty[bs], ((ntok / SB) & 1) ^ 1, abort))) break;
+                        mbar_arrive_expect_tx(&b_full[bs], MATS * n16 * 2048);
+                        uint8_t *tdst = tok + bs * C::TOK_STAGE;
+                        for (int m = 0; m < MATS; ++m)
+                            for (int b = 0; b < n16; ++b) {
+                                if (GATEUP)
+                                    tma_load_3d(tdst + m * C::TOK_BOX + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s,
+                                                m, t.y + 16 * b);
+                                else
+                                    tma_load_2d(tdst + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s, t.y + 16 * b);
+                            }
+                        ++ntok;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+                int dummy = 0;
+                for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
+                    mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
+                for (uint32_t i = (ntok > (uint32_t)SB ? ntok - SB : 0); i < ntok; ++i)
+                    mbar_wait(&b_full[i % SB], (i / SB) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t na = 0, ntok = 0, it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+                const int ntok_rows = p.tiles[item / MT].z;
+                const uint32_t idesc = idesc_f16_f32(128, 16 * ((ntok_rows + 15) >> 4));
+                if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
+                tc_fence_after();
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t as = na % kXtSA, bs = ntok % SB;
+                        if (!(ok = mbar_wait(&a_full[as], (na / kXtSA) & 1, abort))) break;
+                        if (!(ok = mbar_wait(&b_full[bs], (ntok / SB) & 1, abort))) break;
+                        tc_fence_after();
+                        const uint32_t bsm = smem_u32(tok + bs * C::TOK_STAGE);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const uint32_t a_t = tmem + C::A_COL0 + (as * MATS + m) * 32 + 8 * j;
+                                const uint64_t b_d = smem_desc_sw128(bsm + m * C::TOK_BOX + 32 * j);
+                                mma_f16_ts(tmem + m * N, a_t, b_d, idesc, (kr | s | j) != 0);
+                            }
+                        }
+                        mma_commit(&a_empty[as]);
+                        mma_commit(&b_empty[bs]);
+                        ++na;
+                        ++ntok;
+                    }
+                }
+                if (ok) mma_commit(d_full);
+            }
+            mma_commit(mma_done);
+            int dummy = 0;
+            mbar_wait(mma_done, 0, (volatile int *)&dummy, 200000000ull);
+            if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------------ decode + epilogue
+        const int q = warp & 3;            // TMEM lane quarter
+        const int grp = (warp - 4) >> 2;   // 0..3
+        const int r = 32 * q + lane;       // output channel within the tile = TMEM lane
+        const int nb = r >> 4, c = r & 15; // trellis column block and column
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const int mat = GATEUP ? (grp & 1) : 0;
+        const int half = GATEUP ? (grp >> 1) : (grp & 1);   // which 32 K of a sub-stage
+        const int par = GATEUP ? -1 : (grp >> 1);          // down: sub-stage parity it serves
+        const uint32_t kxor = p.kxor;
+        float *xb = xch + grp * 128 * kXchLd;
+        uint32_t nraw = 0, na = 0, it = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+            for (int kr = 0; kr < KR && ok; ++kr) {
+                const uint32_t rs = nraw % SW;
+                if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
+                const uint8_t *stg = raw + rs * C::RAW_STAGE + mat * kXtRawMat;
+#pragma unroll 1
+                for (int s = 0; s < 4; ++s) {
+                    if (GATEUP || (s & 1) == par) {
+                        const uint32_t as = na % kXtSA;
+                        if (!(ok = mbar_wait(&a_empty[as], ((na / kXtSA) & 1) ^ 1, abort))) break;
+                        uint32_t v[16];
+                        const int kt0 = 4 * s + 2 * half;
+                        trellis_column(stg + (nb * kKT + kt0) * kTileBytes3, c, kxor, v);
+                        trellis_column(stg + (nb * kKT + kt0 + 1) * kTileBytes3, c, kxor, v + 8);
+                        tmem_st_32x32b_x16(tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32 + 16 * half, v);
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[as]);
+                    }
+                    ++na;
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                ++nraw;
+            }
+            if (!ok) break;
+            // epilogue: 8-column chunks, chunk c0 handled by group c0/8 % 4 (4 warps = 128 lanes)
+            if (!(ok = mbar_wait(d_full, it & 1, abort))) break;
+            tc_fence_after();
+            const int4 t = p.tiles[item / MT];
+            const int e = t.x;
+            const bool sh = e == p.E;
+            const int ch = (item % MT) * 128 + r;
+            auto vec = [&](const MatrixRef &mr, const __half *base, int64_t stride) {
+                return reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(base) + (sh ? 0 : (int64_t)e * stride));
+            };
+            const MatrixRef &m0 = sh ? p.sma : p.ma;
+            const float svh0 = kRScale * __half2float(vec(m0, m0.svh, m0.svh_stride)[ch]);
+            float svh1 = 0.f, suhd = 0.f;
+            if (GATEUP) {
+                const MatrixRef &m1 = sh ? p.smb : p.mb;
+                const MatrixRef &md = sh ? p.smdown : p.mdown;
+                svh1 = kRScale * __half2float(vec(m1, m1.svh, m1.svh_stride)[ch]);
+                suhd = __half2float(vec(md, md.suh, md.suh_stride)[ch]);
+            }
+#pragma unroll 1
+            for (int c0 = 8 * grp; c0 < t.z; c0 += 32) {
+                uint32_t dg[8];
+                float vg[8];
+                tmem_ld_32x32b_x8(tmem + lane_base + c0, dg);
+                if (GATEUP) {
+                    uint32_t du[8];
+                    float vu[8];
+                    tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        vg[j] = __uint_as_float(dg[j]);
+                        vu[j] = __uint_as_float(du[j]);
+                    }
+                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                    fwht128_lanes(vu, xb, q, lane, 1 + grp);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) vg[j] = swiglu_clamped(vg[j] * svh0, vu[j] * svh1, p.limit) * suhd;
+                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                    __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(vg[j] * kRScale);
+                } else {
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) vg[j] = __uint_as_float(dg[j]);
+                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                    float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = vg[j] * svh0;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty);
+        }
+        if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
 // ----------------------------------------------------------------------------- host
 static PFN_cuTensorMapEncodeTiled_v12000 x_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -423,6 +773,28 @@ static int make_rows_map(CUtensorMap *m, const void *base, int64_t rows, int64_t
     return VFMOE_OK;
 }
 
+// x_perm as [rows][2 rotations][K] fp16 viewed 3D {K, rotation, row}: a box of 64 K x one
+// rotation x 16 rows loads one rotation's rows (SWIZZLE_128B).
+static int make_rot_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k) {
+    auto enc = x_encode();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return VFMOE_ERR_CUDA;
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)k, 2, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {(cuuint64_t)(k * 2), (cuuint64_t)(k * 4)};
+    cuuint32_t box[3] = {64, 1, 16};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (EXL3 rotated rows) failed: %d", (int)r);
+        return VFMOE_ERR_CUDA;
+    }
+    return VFMOE_OK;
+}
+
 int exl3_plan_create(const vfmoe_layer_desc &d, Exl3Plan &plan) {
     plan.ready = 0;
     if (d.weight_format != VFMOE_WFMT_EXL3 || d.exl3_bits != 3) return VFMOE_OK;
@@ -456,11 +828,79 @@ static int launch_x(const XParams &prm, int grid, cudaStream_t st) {
     return VFMOE_OK;
 }
 
+template <bool GATEUP, int N>
+static int launch_xt(const XParams &prm, int grid, cudaStream_t st) {
+    using C = XtCfg<GATEUP, N>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        VF_CUDA(cudaFuncSetAttribute(expert_gemm_exl3_tc<GATEUP, N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::SMEM));
+        attr_done = true;
+    }
+    expert_gemm_exl3_tc<GATEUP, N><<<grid, kXtThreads, C::SMEM, st>>>(prm);
+    VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_exl3_tc<gate_up>" : "expert_gemm_exl3_tc<down>");
+    return VFMOE_OK;
+}
+
+// Prefill (more than 16 rows per expert on average): gather + tile plan + tcgen05 GEMMs with
+// 128-row gate/up tiles and 256-row down tiles.
+static int launch_exl3_tc(const Exl3Plan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
+    const int64_t cap_rows = (int64_t)a.T * a.k + a.T;
+    int rc;
+    XParams g{};
+    g.wa = plan.gate;
+    g.wb = plan.up;
+    g.swa = plan.sh_gate;
+    g.swb = plan.sh_up;
+    if ((rc = make_rot_map(&g.xt, a.xp, cap_rows, a.H))) return rc;
+    g.tiles = a.tiles;
+    g.n_tiles = a.tile_counts;
+    g.E = a.E;
+    g.K = a.H;
+    g.M = a.I;
+    g.ma = a.gate;
+    g.mb = a.up;
+    g.sma = a.sh_gate;
+    g.smb = a.sh_up;
+    g.mdown = a.down;
+    g.smdown = a.sh_down;
+    g.ld_out = a.I;
+    g.out = a.act;
+    g.limit = a.limit;
+    g.err = a.err;
+    g.kxor = 0x3B603B60u;
+    const int grid = plan.num_sms;
+    if ((rc = launch_xt<true, 128>(g, grid, st))) return rc;
+    mid();
+    XParams dn{};
+    dn.wa = plan.down;
+    dn.wb = plan.down;
+    dn.swa = plan.sh_down;
+    dn.swb = plan.sh_down;
+    if ((rc = make_rows_map(&dn.xt, a.act, cap_rows, a.I, 16))) return rc;
+    dn.tiles = a.tiles + a.tiles_cap;
+    dn.n_tiles = a.tile_counts + 1;
+    dn.E = a.E;
+    dn.K = a.I;
+    dn.M = a.H;
+    dn.ma = a.down;
+    dn.mb = a.down;
+    dn.sma = a.sh_down;
+    dn.smb = a.sh_down;
+    dn.ld_out = a.H;
+    dn.out = a.y;
+    dn.limit = a.limit;
+    dn.err = a.err;
+    dn.kxor = 0x3B603B60u;
+    return launch_xt<false, 256>(dn, grid, st);
+}
+
 int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, int x_dtype,
                         cudaStream_t st, const std::function<void()> &mid) {
+    const bool prefill = (double)a.T * a.k / a.E > 16.0;
     const int N = gemv_tokens_per_tile(a.T, a.k, a.E);
     const int64_t rows = (int64_t)a.T * a.k + (a.has_shared ? a.T : 0);  // upper bound
-    int rc = launch_tc_plan(a, N, N, st);
+    int rc = prefill ? launch_tc_plan(a, 128, 256, st) : launch_tc_plan(a, N, N, st);
     if (rc) return rc;
     if (rows > 0) {
         gather_exl3_kernel<<<(unsigned)rows, 256, 0, st>>>(x, x_dtype, a.perm_tok, a.offsets, a.E + (a.has_shared ? 1 : 0),
@@ -468,6 +908,7 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
                                                            const_cast<__half *>(a.xp));
         VF_LAUNCH_CHECK("gather_exl3_kernel");
     }
+    if (prefill) return launch_exl3_tc(plan, a, st, mid);
     const int64_t cap_rows = (int64_t)a.T * a.k + a.T;
     XParams g{};
     g.wa = plan.gate;
