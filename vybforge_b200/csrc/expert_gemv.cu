@@ -116,6 +116,9 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
         fence_mbar_init();
     }
     __syncthreads();
+    // the next kernel (the down GEMV after gate/up) may be scheduled onto SMs as this grid
+    // retires; it reads this grid's output only after griddepcontrol.wait
+    if (threadIdx.x == 0) griddep_launch_dependents();
     const int n_items = (*p.n_tiles) * MT;
 
     if (warp == kGvConsumers) {
@@ -124,6 +127,31 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
             prefetch_tmap(&p.wa);
             prefetch_tmap(&p.swa);
             prefetch_tmap(&p.xt);
+            // The first SW stages are free at start: their weights are requested before the
+            // wait on the previous kernel (programmatic dependent launch: the token rows it
+            // writes are read only after griddepcontrol.wait), their token rows after it.
+            // Without a programmatic launch the wait returns at once.
+            const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            const int pre = my_items * KR < SW ? my_items * KR : SW;
+            for (int i = 0; i < pre; ++i) {
+                const int item = blockIdx.x + (i / KR) * gridDim.x, kr = i % KR;
+                const int4 t = p.tiles[item / MT];
+                const bool sh = t.x == p.E;
+                uint8_t *st = smem + i * C::STAGE;
+                mbar_arrive_expect_tx(&full[i], C::STAGE);
+                tma_load_3d(st, sh ? &p.swa : &p.wa, &full[i], kr * (kRow / 2), (item % MT) * ROWS, sh ? 0 : t.x);
+                if (GATEUP)
+                    tma_load_3d(st + ROWS * kRow, sh ? &p.swb : &p.wb, &full[i], kr * (kRow / 2), (item % MT) * ROWS,
+                                sh ? 0 : t.x);
+            }
+            griddep_wait();
+            for (int i = 0; i < pre; ++i) {
+                const int item = blockIdx.x + (i / KR) * gridDim.x, kr = i % KR;
+                const int4 t = p.tiles[item / MT];
+                uint8_t *st = smem + i * C::STAGE;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[i], kr * 256 + 64 * q, t.y);
+            }
             uint32_t n = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -134,6 +162,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 const CUtensorMap *mb = sh ? &p.swb : &p.wb;
                 const int z = sh ? 0 : t.x;
                 for (int kr = 0; kr < KR; ++kr, ++n) {
+                    if (n < (uint32_t)pre) continue;  // issued above
                     const uint32_t s = n % SW;
                     if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort))) break;
                     uint8_t *st = smem + s * C::STAGE;
@@ -247,7 +276,23 @@ static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
         VF_CUDA(cudaFuncSetAttribute(expert_gemv_mma<GATEUP, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_done = true;
     }
-    expert_gemv_mma<GATEUP, NT><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+    if (GATEUP) {
+        expert_gemv_mma<GATEUP, NT><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+    } else {
+        // programmatic dependent launch: CTAs start streaming down weights on SMs the gate/up
+        // grid has released, before its act rows are complete
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kGvThreads);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT>, prm));
+    }
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_mma<gate_up>" : "expert_gemv_mma<down>");
     return VFMOE_OK;
 }
