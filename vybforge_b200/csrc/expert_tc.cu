@@ -11,13 +11,17 @@
 //   D = fp32 accumulators in TMEM (gate and up side by side for the fused SwiGLU).
 // Raw Q8_0 bytes stream in by TMA as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage.
 //
-// Warp roles (640 threads): warp 0 TMA producer, warp 1 MMA issuer (one thread),
-// warp 2 TMEM allocator, warps 4..19 dequant + epilogue.  Dequant warp w owns TMEM lanes
-// 32*(w%4)..+31 (= weight rows of the tile) and belongs to group g = (w-4)/4: for gate/up,
-// g selects the matrix (g&1) and which of the sub-stage's two Q8_0 blocks it converts (g>>1);
-// for down, g selects the sub-stage (each raw stage holds 4).  Sixteen dequant warps (four
-// per scheduler) keep enough independent work in flight to cover shared-memory and TMEM
-// latencies.
+// Warp roles (640 threads): warp 0 TMA producer of the weight stages, warp 3 TMA producer
+// of the token stages, warps 1 and 2 MMA issuers (one thread each; warp 2 also allocates
+// TMEM), warps 4..19 dequant + epilogue.  Dequant warp w owns TMEM lanes 32*(w%4)..+31
+// (= weight rows of the tile) and belongs to group g = (w-4)/4, which converts sub-stage g of
+// every raw stage (each raw stage holds 4 sub-stages of K = 64), for both matrices of
+// gate/up.  A group therefore has four sub-stages of MMA time to fill its TMEM slot.
+// Sub-stage slot i has one "full" barrier (its dequant group's four warps + the token TMA
+// bytes) and one "empty" barrier (one commit per issuer), so an issuer checks one barrier
+// and commits once per sub-stage: each barrier operation in an issuer's instruction stream
+// stalls its next tcgen05.mma, and a single issuer with two waits and two commits per
+// sub-stage kept the tensor pipe under 60 % busy even with all data in place.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT,
 // drains what it issued and returns.
 //
@@ -39,22 +43,21 @@ constexpr int kThreads = 640;
 constexpr int kDqWarps = 16;
 constexpr int kRawRow = 272;            // 8 Q8_0 blocks = 256 K values
 constexpr int kRawMat = 128 * kRawRow;  // one matrix, one stage
-constexpr int kSA = 4;                  // TMEM A ring slots (K = 64 each)
+constexpr int kSlots = 4;               // sub-stage ring (K = 64 each): TMEM A slots + token stages
 
 template <bool GATEUP, int N>
 struct TcCfg {
     static constexpr int MATS = GATEUP ? 2 : 1;
     static constexpr int SW = GATEUP ? (N <= 32 ? 3 : 2) : (N <= 32 ? 5 : (N == 64 ? 4 : (N == 128 ? 3 : 2)));
-    static constexpr int SB = 4;
     static constexpr int RAW_BYTES = SW * MATS * kRawMat;
     static constexpr int TOK_STAGE = N * 128;
-    static constexpr int TOK_BYTES = SB * TOK_STAGE;
+    static constexpr int TOK_BYTES = kSlots * TOK_STAGE;
     static constexpr int BAR_OFF = RAW_BYTES + TOK_BYTES;
-    static constexpr int NBAR = 2 * SW + 2 * kSA + 2 * SB + 3;
+    static constexpr int NBAR = 2 * SW + 2 * kSlots + 3;
     static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;  // + alignment slack
     static constexpr int D_COLS = MATS * N;
     static constexpr int A_COL0 = D_COLS;
-    static_assert(D_COLS + kSA * MATS * 32 <= 512, "TMEM budget");
+    static_assert(D_COLS + kSlots * MATS * 32 <= 512, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -91,22 +94,6 @@ __device__ __forceinline__ void q8_two_blocks(const uint32_t (&g)[17], uint32_t 
     for (int c = 0; c < 16; ++c) {
         const int b = 36 + 2 * c;
         v[16 + c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d1);
-    }
-}
-
-// One Q8_0 block of a row -> 16 packed fp16 pairs.  g[0..8] are 9 little-endian words that
-// start at the block's word; HB = 0: d is the low half of g[0] and q[j] is byte 2 + j;
-// HB = 1 (block starts at byte 2 of g[0]): d is the high half of g[0], q[j] is byte 4 + j.
-template <int HB>
-__device__ __forceinline__ void q8_one_block(const uint32_t (&g)[9], uint32_t (&v)[16]) {
-    const __half2 d = __half2half2(__ushort_as_half((unsigned short)(HB ? (g[0] >> 16) : (g[0] & 0xFFFFu))));
-    uint32_t x[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) x[i] = g[i] ^ 0x80808080u;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        const int b = 2 + 2 * HB + 2 * c;
-        v[c] = q8_pair(x[b >> 2], (b & 3) ? 0x4342u : 0x4140u, d);
     }
 }
 
@@ -168,16 +155,15 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict
 template <bool GATEUP, int N>
 __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_constant__ TcParams p) {
     using C = TcCfg<GATEUP, N>;
-    constexpr int MATS = C::MATS, SW = C::SW, SB = C::SB;
+    constexpr int MATS = C::MATS, SW = C::SW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *raw = smem;
     uint8_t *tok = smem + C::RAW_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *raw_full = bars, *raw_empty = bars + SW;
-    uint64_t *a_full = bars + 2 * SW, *a_empty = a_full + kSA;
-    uint64_t *b_full = a_empty + kSA, *b_empty = b_full + SB;
-    uint64_t *d_full = b_empty + SB, *d_empty = d_full + 1, *mma_done = d_full + 2;
+    uint64_t *full = bars + 2 * SW, *empty = full + kSlots;
+    uint64_t *d_full = empty + kSlots, *d_empty = d_full + 1, *mma_done = d_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBAR);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -190,17 +176,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], kDqWarps);
         }
-        for (int i = 0; i < kSA; ++i) {
-            mbar_init(&a_full[i], GATEUP ? kDqWarps : 4);
-            mbar_init(&a_empty[i], 1);
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&full[i], 4 + 1);  // the four warps of one dequant group + the token producer (+ tx bytes)
+            mbar_init(&empty[i], 2);     // one tcgen05.commit per MMA issuer
         }
-        for (int i = 0; i < SB; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
-        }
-        mbar_init(d_full, 1);
+        mbar_init(d_full, 2);
         mbar_init(d_empty, kDqWarps);
-        mbar_init(mma_done, 1);
+        mbar_init(mma_done, 2);
         *abort = 0;
         fence_mbar_init();
     }
@@ -208,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         prefetch_tmap(&p.wa);
         prefetch_tmap(&p.swa);
         prefetch_tmap(&p.xt);
+        prefetch_tmap(&p.xt64);
         if (GATEUP) {
             prefetch_tmap(&p.wb);
             prefetch_tmap(&p.swb);
@@ -224,9 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     const int n_items = (*p.n_tiles) * MT;
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------------ TMA producer: weights
         if (lane == 0) {
-            uint32_t nraw = 0, ntok = 0;
+            uint32_t nraw = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 const int4 t = p.tiles[item / MT];
@@ -243,16 +226,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                     tma_load_3d(dst, ma, &raw_full[rs], kr * (kRawRow / 2), m0, z);
                     if (GATEUP) tma_load_3d(dst + kRawMat, mb, &raw_full[rs], kr * (kRawRow / 2), m0, z);
                     ++nraw;
-                    const int n16 = (t.z + 15) >> 4;  // 16-row token boxes actually needed
-                    for (int s = 0; s < 4; ++s) {
-                        const uint32_t bs = ntok % SB;
-                        if (!(ok = mbar_wait(&b_empty[bs], ((ntok / SB) & 1) ^ 1, abort))) break;
-                        mbar_arrive_expect_tx(&b_full[bs], n16 * 16 * 128);
-                        for (int b = 0; b < n16; ++b)
-                            tma_load_2d(tok + bs * C::TOK_STAGE + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s,
-                                        t.y + 16 * b);
-                        ++ntok;
-                    }
                 }
             }
             if (!ok) {
@@ -261,40 +234,79 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                 int dummy = 0;
                 for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
                     mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
-                for (uint32_t i = (ntok > (uint32_t)SB ? ntok - SB : 0); i < ntok; ++i)
-                    mbar_wait(&b_full[i % SB], (i / SB) & 1, (volatile int *)&dummy, 100000000ull);
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issuer
+    } else if (warp == 3) {
+        // ------------------------------------------------------------------ TMA producer: token rows
+        // Refills a slot as soon as both MMA issuers release it.  Rows come in 64-row boxes plus
+        // 16-row boxes for the remainder (the same shared-memory image as 16-row boxes only).
         if (lane == 0) {
-            uint32_t na = 0, ntok = 0, it = 0;
+            uint32_t n = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int4 t = p.tiles[item / MT];
+                const int n16 = (t.z + 15) >> 4;  // 16-row token boxes actually needed
+                const int n64 = n16 >> 2;
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t sl = n % kSlots;
+                        if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
+                        mbar_arrive_expect_tx(&full[sl], n16 * 16 * 128);
+                        uint8_t *dst = tok + sl * C::TOK_STAGE;
+                        for (int b = 0; b < n64; ++b)
+                            tma_load_2d(dst + b * 8192, &p.xt64, &full[sl], kr * 256 + 64 * s, t.y + 64 * b);
+                        for (int b = 4 * n64; b < n16; ++b)
+                            tma_load_2d(dst + b * 2048, &p.xt, &full[sl], kr * 256 + 64 * s, t.y + 16 * b);
+                        ++n;
+                    }
+                }
+            }
+            if (!ok) {
+                // the slots' phases also need the dequant arrivals, so this drain may run out
+                // (bounded) when those warps stopped first
+                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+                int dummy = 0;
+                for (uint32_t i = (n > (uint32_t)kSlots ? n - kSlots : 0); i < n; ++i)
+                    mbar_wait(&full[i % kSlots], (i / kSlots) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------------ MMA issuers
+        // Two issuing threads keep the tensor pipe fed: every barrier check in an issuer's
+        // instruction stream stalls its next MMA.  Gate/up: issuer i owns matrix i.  Down:
+        // issuer i owns one half of the token columns (in 16-column units).
+        if (lane == 0) {
+            const int iss = warp - 1;
+            uint32_t n = 0, it = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-                const int ntok_rows = p.tiles[item / MT].z;
-                const uint32_t idesc = idesc_f16_f32(128, 16 * ((ntok_rows + 15) >> 4));  // N = rows rounded to 16
+                const int n16 = (p.tiles[item / MT].z + 15) >> 4;
+                int c_lo = 0, c_n = 16 * n16;
+                if (!GATEUP) {
+                    const int h0 = 16 * ((n16 + 1) >> 1);
+                    c_lo = iss ? h0 : 0;
+                    c_n = iss ? 16 * n16 - h0 : h0;
+                }
+                const int mat = GATEUP ? iss : 0;
+                const uint32_t idesc = idesc_f16_f32(128, c_n > 0 ? c_n : 16);
                 if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
                 tc_fence_after();
                 for (int kr = 0; kr < KR && ok; ++kr) {
                     for (int s = 0; s < 4; ++s) {
-                        const uint32_t as = na % kSA, bs = ntok % SB;
-                        if (!(ok = mbar_wait(&a_full[as], (na / kSA) & 1, abort))) break;
-                        if (!(ok = mbar_wait(&b_full[bs], (ntok / SB) & 1, abort))) break;
+                        const uint32_t sl = n % kSlots;
+                        if (!(ok = mbar_wait(&full[sl], (n / kSlots) & 1, abort))) break;
                         tc_fence_after();
-                        const uint32_t bsm = smem_u32(tok + bs * C::TOK_STAGE);
-#pragma unroll
-                        for (int m = 0; m < MATS; ++m) {
+                        if (c_n > 0) {
+                            const uint32_t bsm = smem_u32(tok + sl * C::TOK_STAGE + c_lo * 128);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
-                                const uint32_t a_t = tmem + C::A_COL0 + (as * MATS + m) * 32 + 8 * j;
-                                const uint64_t b_d = smem_desc_sw128(bsm + 32 * j);
-                                mma_f16_ts(tmem + m * N, a_t, b_d, idesc, (kr | s | j) != 0);
+                                const uint32_t a_t = tmem + C::A_COL0 + (sl * MATS + mat) * 32 + 8 * j;
+                                mma_f16_ts(tmem + mat * N + c_lo, a_t, smem_desc_sw128(bsm + 32 * j), idesc,
+                                           (kr | s | j) != 0);
                             }
                         }
-                        mma_commit(&a_empty[as]);
-                        mma_commit(&b_empty[bs]);
-                        ++na;
-                        ++ntok;
+                        mma_commit(&empty[sl]);
+                        ++n;
                     }
                 }
                 if (ok) mma_commit(d_full);
@@ -311,48 +323,28 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         const int grp = (warp - 4) >> 2;   // 0..3
         const int r = 32 * q + lane;       // weight row within the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        const int mat = GATEUP ? (grp & 1) : 0;
-        const int hb = GATEUP ? (grp >> 1) : 0;
-        uint32_t nraw = 0, na = 0, it = 0;
+        uint32_t nraw = 0, n = 0, it = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
             for (int kr = 0; kr < KR && ok; ++kr) {
                 const uint32_t rs = nraw % SW;
                 if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
-                const uint8_t *row = raw + rs * (MATS * kRawMat) + mat * kRawMat + r * kRawRow;
+                const uint8_t *row = raw + rs * (MATS * kRawMat) + r * kRawRow;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const bool mine = GATEUP || (s == grp);
-                    if (mine) {
-                        const uint32_t as = na % kSA;
-                        if (!(ok = mbar_wait(&a_empty[as], ((na / kSA) & 1) ^ 1, abort))) break;
-                        const uint32_t tcol = tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32;
-                        if (GATEUP) {
-                            // one block: 9 words at word (17s + 8hb) = 3 x 16 B loads from chunk (68s+32hb)/16
-                            const int c0 = (68 * s + 32 * hb) >> 4;
-                            uint32_t w[12];
+                    if (s == grp) {
+                        // group g converts sub-stage g of every raw stage: K = 64 (two Q8_0
+                        // blocks) of its 32 rows, for each matrix; one wait covers the stores
+                        const uint32_t sl = n % kSlots;
+                        if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
+                        const uint32_t tcol = tmem + lane_base + C::A_COL0 + sl * MATS * 32;
 #pragma unroll
-                            for (int c = 0; c < 3; ++c) {
-                                const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 16 * (c0 + c));
-                                w[4 * c] = v4.x;
-                                w[4 * c + 1] = v4.y;
-                                w[4 * c + 2] = v4.z;
-                                w[4 * c + 3] = v4.w;
-                            }
-                            uint32_t g9[9];
-#pragma unroll
-                            for (int j = 0; j < 9; ++j) g9[j] = w[s + j];
-                            uint32_t v[16];
-                            if (hb == 0)
-                                q8_one_block<0>(g9, v);
-                            else
-                                q8_one_block<1>(g9, v);
-                            tmem_st_32x32b_x16(tcol + 16 * hb, v);
-                        } else {
+                        for (int m = 0; m < MATS; ++m) {
                             uint32_t w[20];
 #pragma unroll
                             for (int c = 0; c < 5; ++c) {
-                                const uint4 v4 = *reinterpret_cast<const uint4 *>(row + 64 * s + 16 * c);
+                                const uint4 v4 =
+                                    *reinterpret_cast<const uint4 *>(row + m * kRawMat + 64 * s + 16 * c);
                                 w[4 * c] = v4.x;
                                 w[4 * c + 1] = v4.y;
                                 w[4 * c + 2] = v4.z;
@@ -363,14 +355,14 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                             for (int j = 0; j < 17; ++j) g[j] = w[s + j];
                             uint32_t v[32];
                             q8_two_blocks(g, v);
-                            tmem_st_32x32b_x32(tcol, v);
+                            tmem_st_32x32b_x32(tcol + m * 32, v);
                         }
                         tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&a_full[as]);
+                        if (lane == 0) mbar_arrive(&full[sl]);
                     }
-                    ++na;
+                    ++n;
                 }
                 if (!ok) break;
                 __syncwarp();
@@ -564,6 +556,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     g.swa = plan.sh_gate;
     g.swb = plan.sh_up;
     if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, 16))) return rc;
+    if ((rc = make_tok_map(&g.xt64, a.xp, rows, a.H, 64))) return rc;
     g.tiles = a.tiles;
     g.n_tiles = a.tile_counts;
     g.E = a.E;
@@ -588,6 +581,7 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     dn.swa = plan.sh_down;
     dn.swb = plan.sh_down;
     if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, 16))) return rc;
+    if ((rc = make_tok_map(&dn.xt64, a.act, rows, a.I, 64))) return rc;
     dn.tiles = a.tiles + a.tiles_cap;
     dn.n_tiles = a.tile_counts + 1;
     dn.E = a.E;
