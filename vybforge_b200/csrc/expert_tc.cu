@@ -11,9 +11,10 @@
 //   D = fp32 accumulators in TMEM (gate and up side by side for the fused SwiGLU).
 // Raw Q8_0 bytes stream in by TMA as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage.
 //
-// Warp roles (640 threads): warp 0 TMA producer of the weight stages, warp 3 TMA producer
-// of the token stages, warps 1 and 2 MMA issuers (one thread each; warp 2 also allocates
-// TMEM), warps 4..19 dequant + epilogue.  Dequant warp w owns TMEM lanes 32*(w%4)..+31
+// Warp roles (640 threads): warps 0 and 3 TMA producers of the weight stages (one matrix
+// each), warps 1 and 2 MMA issuers (one thread each; warp 2 also allocates TMEM), warps
+// 4..19 dequant + epilogue; the first warp of each dequant group also issues its sub-stage's
+// token-row loads (one 16-row box per lane).  Dequant warp w owns TMEM lanes 32*(w%4)..+31
 // (= weight rows of the tile) and belongs to group g = (w-4)/4, which converts sub-stage g of
 // every raw stage (each raw stage holds 4 sub-stages of K = 64), for both matrices of
 // gate/up.  A group therefore has four sub-stages of MMA time to fill its TMEM slot.
@@ -173,11 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < SW; ++i) {
-            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_full[i], MATS);  // one producer thread per matrix (+ tx bytes)
             mbar_init(&raw_empty[i], kDqWarps);
         }
         for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&full[i], 4 + 1);  // the four warps of one dequant group + the token producer (+ tx bytes)
+            mbar_init(&full[i], 4 + 1);  // the four warps of one dequant group + its token loads (+ tx bytes)
             mbar_init(&empty[i], 2);     // one tcgen05.commit per MMA issuer
         }
         mbar_init(d_full, 2);
@@ -190,7 +191,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         prefetch_tmap(&p.wa);
         prefetch_tmap(&p.swa);
         prefetch_tmap(&p.xt);
-        prefetch_tmap(&p.xt64);
         if (GATEUP) {
             prefetch_tmap(&p.wb);
             prefetch_tmap(&p.swb);
@@ -206,25 +206,27 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     const uint32_t tmem = *tmem_slot;
     const int n_items = (*p.n_tiles) * MT;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ TMA producer: weights
+    if (warp == 0 || (GATEUP && warp == 3)) {
+        // ------------------------------------------------------------------ TMA producers: weights
+        // One thread per matrix (warp 0: A / gate or down, warp 3: B / up): a thread sustains
+        // only about one TMA load per ~500 clocks however many it has in flight, so the two
+        // matrices' loads are issued from different threads.
         if (lane == 0) {
+            const int mat = warp == 0 ? 0 : 1;
             uint32_t nraw = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 const int4 t = p.tiles[item / MT];
                 const int m0 = (item % MT) * 128;
                 const bool sh = t.x == p.E;
-                const CUtensorMap *ma = sh ? &p.swa : &p.wa;
-                const CUtensorMap *mb = sh ? &p.swb : &p.wb;
+                const CUtensorMap *mp = mat == 0 ? (sh ? &p.swa : &p.wa) : (sh ? &p.swb : &p.wb);
                 const int z = sh ? 0 : t.x;
                 for (int kr = 0; kr < KR && ok; ++kr) {
                     const uint32_t rs = nraw % SW;
                     if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
-                    mbar_arrive_expect_tx(&raw_full[rs], MATS * kRawMat);
-                    uint8_t *dst = raw + rs * (MATS * kRawMat);
-                    tma_load_3d(dst, ma, &raw_full[rs], kr * (kRawRow / 2), m0, z);
-                    if (GATEUP) tma_load_3d(dst + kRawMat, mb, &raw_full[rs], kr * (kRawRow / 2), m0, z);
+                    mbar_arrive_expect_tx(&raw_full[rs], kRawMat);
+                    tma_load_3d(raw + rs * (MATS * kRawMat) + mat * kRawMat, mp, &raw_full[rs], kr * (kRawRow / 2), m0,
+                                z);
                     ++nraw;
                 }
             }
@@ -234,40 +236,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                 int dummy = 0;
                 for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
                     mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
-            }
-        }
-    } else if (warp == 3) {
-        // ------------------------------------------------------------------ TMA producer: token rows
-        // Refills a slot as soon as both MMA issuers release it.  Rows come in 64-row boxes plus
-        // 16-row boxes for the remainder (the same shared-memory image as 16-row boxes only).
-        if (lane == 0) {
-            uint32_t n = 0;
-            bool ok = true;
-            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-                const int4 t = p.tiles[item / MT];
-                const int n16 = (t.z + 15) >> 4;  // 16-row token boxes actually needed
-                const int n64 = n16 >> 2;
-                for (int kr = 0; kr < KR && ok; ++kr) {
-                    for (int s = 0; s < 4; ++s) {
-                        const uint32_t sl = n % kSlots;
-                        if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
-                        mbar_arrive_expect_tx(&full[sl], n16 * 16 * 128);
-                        uint8_t *dst = tok + sl * C::TOK_STAGE;
-                        for (int b = 0; b < n64; ++b)
-                            tma_load_2d(dst + b * 8192, &p.xt64, &full[sl], kr * 256 + 64 * s, t.y + 64 * b);
-                        for (int b = 4 * n64; b < n16; ++b)
-                            tma_load_2d(dst + b * 2048, &p.xt, &full[sl], kr * 256 + 64 * s, t.y + 16 * b);
-                        ++n;
-                    }
-                }
-            }
-            if (!ok) {
-                // the slots' phases also need the dequant arrivals, so this drain may run out
-                // (bounded) when those warps stopped first
-                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
-                int dummy = 0;
-                for (uint32_t i = (n > (uint32_t)kSlots ? n - kSlots : 0); i < n; ++i)
-                    mbar_wait(&full[i % kSlots], (i / kSlots) & 1, (volatile int *)&dummy, 100000000ull);
             }
         }
     } else if (warp == 1 || warp == 2) {
@@ -325,7 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         uint32_t nraw = 0, n = 0, it = 0;
         bool ok = true;
+        uint32_t tok_issued = 0;  // sub-stages whose token loads this warp issued
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+            const int4 tt = p.tiles[item / MT];
+            const int t_y = tt.y, n16 = (tt.z + 15) >> 4;  // 16-row token boxes actually needed
             for (int kr = 0; kr < KR && ok; ++kr) {
                 const uint32_t rs = nraw % SW;
                 if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
@@ -337,6 +308,16 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                         // blocks) of its 32 rows, for each matrix; one wait covers the stores
                         const uint32_t sl = n % kSlots;
                         if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
+                        if (q == 0) {
+                            // the group's token rows for this sub-stage: one 16-row box per lane,
+                            // all issued by one instruction
+                            if (lane == 0) mbar_arrive_expect_tx(&full[sl], n16 * 16 * 128);
+                            __syncwarp();
+                            if (lane < n16)
+                                tma_load_2d(tok + sl * C::TOK_STAGE + lane * 2048, &p.xt, &full[sl], kr * 256 + 64 * s,
+                                            t_y + 16 * lane);
+                            tok_issued = n + 1;
+                        }
                         const uint32_t tcol = tmem + lane_base + C::A_COL0 + sl * MATS * 32;
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
@@ -404,7 +385,16 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty);
         }
-        if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+        if (!ok) {
+            atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+            // token loads this warp issued land before the CTA exits (bounded: the slot's phase
+            // also needs the dequant arrivals, which may never come after an abort)
+            if (q == 0 && tok_issued > 0) {
+                int dummy = 0;
+                const uint32_t i = tok_issued - 1;
+                mbar_wait(&full[i % kSlots], (i / kSlots) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -556,7 +546,6 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     g.swa = plan.sh_gate;
     g.swb = plan.sh_up;
     if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, 16))) return rc;
-    if ((rc = make_tok_map(&g.xt64, a.xp, rows, a.H, 64))) return rc;
     g.tiles = a.tiles;
     g.n_tiles = a.tile_counts;
     g.E = a.E;
@@ -581,7 +570,6 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     dn.swa = plan.sh_down;
     dn.swb = plan.sh_down;
     if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, 16))) return rc;
-    if ((rc = make_tok_map(&dn.xt64, a.act, rows, a.I, 64))) return rc;
     dn.tiles = a.tiles + a.tiles_cap;
     dn.n_tiles = a.tile_counts + 1;
     dn.E = a.E;

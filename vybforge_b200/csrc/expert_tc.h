@@ -21,8 +21,7 @@ struct TcPlan {
 // Kernel parameters shared by the tcgen05 GEMM and the decode GEMV (passed __grid_constant__).
 struct TcParams {
     CUtensorMap wa, wb, swa, swb;   // weights: routed A/B matrices, shared A/B (3D u16 maps)
-    CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B, 16-row boxes
-    CUtensorMap xt64;               // the same rows in 64-row boxes (prefill GEMM only)
+    CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B
     const int4 *tiles;              // {expert, row0, nrows, 0}
     const int32_t *n_tiles;
     int E, K, M;
