@@ -288,6 +288,9 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     __shared__ double s_logit[kMaxCand];   // L2/L3 logit, then the choice (score + bias)
     __shared__ double s_score[kMaxCand];   // sigmoid(logit)
     __shared__ int s_ncand, s_amb;
+    __shared__ __align__(16) float s_lo[32 * NPL];  // lower bounds of every expert's choice (-inf past E)
+    __shared__ float s_tau;
+    __shared__ int s_wcnt[8];
     __shared__ int s_order[kMaxCand];
     __shared__ unsigned char s_redo[kMaxCand];
     __shared__ float s_phi[8][8], s_plo[8][8];
@@ -346,77 +349,92 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     for (int i = 0; i < 8; ++i) tot += s_red[i];
     const float nx = sqrtf(tot) * 1.001f;
 
-    // ---- L2 candidate selection (warp 0)
-    if (warp == 0) {
-        float ca[NPL], lo[NPL], hi[NPL];
+    // ---- L2 candidate selection, all threads: thread i owns experts i, i + 256, ...
+    // lo/hi = choice -/+ the L1 bound.  tau = the k-th largest lo in the order (lo desc, id
+    // asc): the expert whose rank is k - 1.  Candidates = experts with hi >= tau, compacted in
+    // ascending id order.  All partial loads of a thread are issued before they are summed.
+    constexpr int EPT = (32 * NPL + 255) / 256;  // experts per thread
+    float lo[EPT], hi[EPT];
 #pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E) {
-                float l = 0.f;
-                for (int c0 = 0; c0 < nchunk; c0 += 8) {   // 8 partial loads in flight, summed in chunk order
-                    float pv[8];
+    for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + 256 * i;
+        lo[i] = hi[i] = -INFINITY;
+        if (e < E) {
+            float l = 0.f;
+            for (int c0 = 0; c0 < nchunk; c0 += 8) {  // 8 partial loads in flight, summed in chunk order
+                float pv[8];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) pv[c] = c0 + c < nchunk ? logits[((int64_t)(c0 + c) * T + t) * E + e] : 0.f;
+                for (int c = 0; c < 8; ++c) pv[c] = c0 + c < nchunk ? logits[((int64_t)(c0 + c) * T + t) * E + e] : 0.f;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        if (c0 + c < nchunk) l += pv[c];
+                for (int c = 0; c < 8; ++c)
+                    if (c0 + c < nchunk) l += pv[c];
+            }
+            const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
+            float ca = 1.f / (1.f + expf(-l)) + bias[e];
+            if (isnan(ca)) ca = -INFINITY;
+            lo[i] = ca - b1;
+            hi[i] = ca + b1;
+        }
+        if (e < 32 * NPL) s_lo[e] = lo[i];  // -inf past E: never ranked above a real expert
+    }
+    if (threadIdx.x == 0) {
+        s_amb = 0;
+        s_tau = -INFINITY;  // kept if no rank k - 1 exists (non-finite bounds): every expert is then a candidate
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + 256 * i;
+        if (e < E) {
+            // broadcast float4 reads, 8 in flight per step
+            const float4 *l4 = reinterpret_cast<const float4 *>(s_lo);
+            int rank = 0;
+            for (int o4 = 0; o4 < 8 * NPL; o4 += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = l4[o4 + u];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int o = 4 * (o4 + u);
+                    rank += (v[u].x > lo[i] || (v[u].x == lo[i] && o < e)) ? 1 : 0;
+                    rank += (v[u].y > lo[i] || (v[u].y == lo[i] && o + 1 < e)) ? 1 : 0;
+                    rank += (v[u].z > lo[i] || (v[u].z == lo[i] && o + 2 < e)) ? 1 : 0;
+                    rank += (v[u].w > lo[i] || (v[u].w == lo[i] && o + 3 < e)) ? 1 : 0;
                 }
-                const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
-                ca[j] = 1.f / (1.f + expf(-l)) + bias[e];
-                if (isnan(ca[j])) ca[j] = -INFINITY;
-                lo[j] = ca[j] - b1;
-                hi[j] = ca[j] + b1;
-            } else {
-                ca[j] = lo[j] = hi[j] = -INFINITY;
             }
+            if (rank == k - 1) s_tau = lo[i];
         }
-        // tau = k-th largest lower bound
-        unsigned taken = 0;
-        float tau = -INFINITY;
-        for (int r = 0; r < k; ++r) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
+    }
+    __syncthreads();
+    const float tau = s_tau;
+    int nbase = 0;
 #pragma unroll
-            for (int j = 0; j < NPL; ++j) {
-                const int e = lane + 32 * j;
-                if (e < E && !((taken >> j) & 1u) && (lo[j] > bv || bi == 0x7fffffff)) {
-                    bv = lo[j];
-                    bi = e;
-                }
-            }
+    for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + 256 * i;
+        const bool c = e < E && hi[i] >= tau;
+        const unsigned m = __ballot_sync(0xffffffffu, c);
+        if (lane == 0) s_wcnt[warp] = __popc(m);
+        __syncthreads();
+        int before = nbase, total = 0;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-            tau = bv;
+        for (int w = 0; w < 8; ++w) {
+            before += w < warp ? s_wcnt[w] : 0;
+            total += s_wcnt[w];
         }
-        int n = 0;
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            const bool c = e < E && hi[j] >= tau;
-            const unsigned m = __ballot_sync(0xffffffffu, c);
-            if (c) {
-                const int pos = n + __popc(m & ((1u << lane) - 1u));
-                if (pos < kMaxCand) s_cand[pos] = e;
-            }
-            n += __popc(m);
+        if (c) {
+            const int pos = before + __popc(m & ((1u << lane) - 1u));
+            if (pos < kMaxCand) s_cand[pos] = e;
         }
-        if (lane == 0) {
-            if (n > kMaxCand) {
-                raise_dev_error(err, DEV_BAD_COUNT);
-                n = kMaxCand;
-            }
-            s_ncand = n;
-            s_amb = 0;
+        nbase += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        int n = nbase;
+        if (n > kMaxCand) {
+            raise_dev_error(err, DEV_BAD_COUNT);
+            n = kMaxCand;
         }
+        s_ncand = n;
     }
     __syncthreads();
     const int nc = s_ncand;
