@@ -393,18 +393,19 @@ struct XtCfg {
     static constexpr int RAW_STAGE = MATS * kXtRawMat;
     static constexpr int XCH = 4 * 128 * kXchLd * 4;        // one [128][9] buffer per epilogue group
     static constexpr int BUDGET = 232448 - 1024 - 256 - XCH;
-    static constexpr int SB = (BUDGET - 3 * RAW_STAGE) / TOK_STAGE >= 4 ? 4 : 3;
+    static constexpr int SB = kXtSA;  // token stages = TMEM A slots: one full/empty barrier pair per slot
     static constexpr int SW_FIT = (BUDGET - SB * TOK_STAGE) / RAW_STAGE;
     static constexpr int SW = SW_FIT > 4 ? 4 : SW_FIT;
     static constexpr int RAW_BYTES = SW * RAW_STAGE;
     static constexpr int TOK_BYTES = SB * TOK_STAGE;
     static constexpr int XCH_OFF = RAW_BYTES + TOK_BYTES;
     static constexpr int BAR_OFF = XCH_OFF + XCH;
-    static constexpr int NBAR = 2 * SW + 2 * kXtSA + 2 * SB + 3;
+    static constexpr int NBAR = 2 * SW + 2 * kXtSA + 3;
     static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;
     static constexpr int D_COLS = MATS * N;
     static constexpr int A_COL0 = D_COLS;
     static constexpr int DQ_PER_SUB = GATEUP ? kXtDq : kXtDq / 2;
+    static constexpr int TOK_ISSUERS = GATEUP ? 2 : 1;  // warps issuing a sub-stage's token loads
     static_assert(SW >= 2, "double-buffered trellis stages");
     static_assert(D_COLS + kXtSA * MATS * 32 <= 512, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -477,9 +478,8 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
     float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *raw_full = bars, *raw_empty = bars + SW;
-    uint64_t *a_full = bars + 2 * SW, *a_empty = a_full + kXtSA;
-    uint64_t *b_full = a_empty + kXtSA, *b_empty = b_full + SB;
-    uint64_t *d_full = b_empty + SB, *d_empty = d_full + 1, *mma_done = d_full + 2;
+    uint64_t *full = bars + 2 * SW, *empty = full + kXtSA;
+    uint64_t *d_full = empty + kXtSA, *d_empty = d_full + 1, *mma_done = d_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBAR);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -489,20 +489,16 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < SW; ++i) {
-            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_full[i], MATS);  // one producer thread per matrix (+ tx bytes)
             mbar_init(&raw_empty[i], kXtDq);
         }
         for (int i = 0; i < kXtSA; ++i) {
-            mbar_init(&a_full[i], C::DQ_PER_SUB);
-            mbar_init(&a_empty[i], 1);
+            mbar_init(&full[i], C::DQ_PER_SUB + C::TOK_ISSUERS);  // decode warps + token loads (+ tx bytes)
+            mbar_init(&empty[i], 2);                              // one tcgen05.commit per MMA issuer
         }
-        for (int i = 0; i < SB; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
-        }
-        mbar_init(d_full, 1);
+        mbar_init(d_full, 2);
         mbar_init(d_empty, kXtDq);
-        mbar_init(mma_done, 1);
+        mbar_init(mma_done, 2);
         *abort = 0;
         fence_mbar_init();
     }
@@ -521,42 +517,26 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
     const uint32_t tmem = *tmem_slot;
     const int n_items = (*p.n_tiles) * MT;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ TMA producer
+    if (warp == 0 || (GATEUP && warp == 3)) {
+        // ------------------------------------------------------------------ TMA producers: trellis
+        // One thread per matrix (warp 0: gate or down, warp 3: up): a thread sustains only
+        // about one TMA load per ~500 clocks.
         if (lane == 0) {
-            uint32_t nraw = 0, ntok = 0;
+            const int mat = warp == 0 ? 0 : 1;
+            uint32_t nraw = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 const int4 t = p.tiles[item / MT];
                 const int nb0 = (item % MT) * 8;
                 const bool sh = t.x == p.E;
-                const CUtensorMap *ma = sh ? &p.swa : &p.wa;
-                const CUtensorMap *mb = sh ? &p.swb : &p.wb;
+                const CUtensorMap *mp = mat == 0 ? (sh ? &p.swa : &p.wa) : (sh ? &p.swb : &p.wb);
                 const int z = sh ? 0 : t.x;
-                const int n16 = (t.z + 15) >> 4;
                 for (int kr = 0; kr < KR && ok; ++kr) {
                     const uint32_t rs = nraw % SW;
                     if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
-                    mbar_arrive_expect_tx(&raw_full[rs], C::RAW_STAGE);
-                    uint8_t *dst = raw + rs * C::RAW_STAGE;
-                    tma_load_4d(dst, ma, &raw_full[rs], 0, kr * kKT, nb0, z);
-                    if (GATEUP) tma_load_4d(dst + kXtRawMat, mb, &raw_full[rs], 0, kr * kKT, nb0, z);
+                    mbar_arrive_expect_tx(&raw_full[rs], kXtRawMat);
+                    tma_load_4d(raw + rs * C::RAW_STAGE + mat * kXtRawMat, mp, &raw_full[rs], 0, kr * kKT, nb0, z);
                     ++nraw;
-                    for (int s = 0; s < 4; ++s) {
-                        const uint32_t bs = ntok % SB;
-                        if (!(ok = mbar_wait(&b_empty[bs], ((ntok / SB) & 1) ^ 1, abort))) break;
-                        mbar_arrive_expect_tx(&b_full[bs], MATS * n16 * 2048);
-                        uint8_t *tdst = tok + bs * C::TOK_STAGE;
-                        for (int m = 0; m < MATS; ++m)
-                            for (int b = 0; b < n16; ++b) {
-                                if (GATEUP)
-                                    tma_load_3d(tdst + m * C::TOK_BOX + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s,
-                                                m, t.y + 16 * b);
-                                else
-                                    tma_load_2d(tdst + b * 2048, &p.xt, &b_full[bs], kr * 256 + 64 * s, t.y + 16 * b);
-                            }
-                        ++ntok;
-                    }
                 }
             }
             if (!ok) {
@@ -564,40 +544,45 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                 int dummy = 0;
                 for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
                     mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
-                for (uint32_t i = (ntok > (uint32_t)SB ? ntok - SB : 0); i < ntok; ++i)
-                    mbar_wait(&b_full[i % SB], (i / SB) & 1, (volatile int *)&dummy, 100000000ull);
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------------ MMA issuers
+        // Two issuing threads (gate/up: one per matrix; down: one per half of the token
+        // columns), one barrier check and one commit per sub-stage each: every barrier
+        // operation in an issuer's instruction stream stalls its next tcgen05.mma.
         if (lane == 0) {
-            uint32_t na = 0, ntok = 0, it = 0;
+            const int iss = warp - 1;
+            uint32_t n = 0, it = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-                const int ntok_rows = p.tiles[item / MT].z;
-                const uint32_t idesc = idesc_f16_f32(128, 16 * ((ntok_rows + 15) >> 4));
+                const int n16 = (p.tiles[item / MT].z + 15) >> 4;
+                int c_lo = 0, c_n = 16 * n16;
+                if (!GATEUP) {
+                    const int h0 = 16 * ((n16 + 1) >> 1);
+                    c_lo = iss ? h0 : 0;
+                    c_n = iss ? 16 * n16 - h0 : h0;
+                }
+                const int m = GATEUP ? iss : 0;
+                const uint32_t idesc = idesc_f16_f32(128, c_n > 0 ? c_n : 16);
                 if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
                 tc_fence_after();
                 for (int kr = 0; kr < KR && ok; ++kr) {
                     for (int s = 0; s < 4; ++s) {
-                        const uint32_t as = na % kXtSA, bs = ntok % SB;
-                        if (!(ok = mbar_wait(&a_full[as], (na / kXtSA) & 1, abort))) break;
-                        if (!(ok = mbar_wait(&b_full[bs], (ntok / SB) & 1, abort))) break;
+                        const uint32_t sl = n % kXtSA;
+                        if (!(ok = mbar_wait(&full[sl], (n / kXtSA) & 1, abort))) break;
                         tc_fence_after();
-                        const uint32_t bsm = smem_u32(tok + bs * C::TOK_STAGE);
-#pragma unroll
-                        for (int m = 0; m < MATS; ++m) {
+                        if (c_n > 0) {
+                            const uint32_t bsm = smem_u32(tok + sl * C::TOK_STAGE + m * C::TOK_BOX + c_lo * 128);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
-                                const uint32_t a_t = tmem + C::A_COL0 + (as * MATS + m) * 32 + 8 * j;
-                                const uint64_t b_d = smem_desc_sw128(bsm + m * C::TOK_BOX + 32 * j);
-                                mma_f16_ts(tmem + m * N, a_t, b_d, idesc, (kr | s | j) != 0);
+                                const uint32_t a_t = tmem + C::A_COL0 + (sl * MATS + m) * 32 + 8 * j;
+                                mma_f16_ts(tmem + m * N + c_lo, a_t, smem_desc_sw128(bsm + 32 * j), idesc,
+                                           (kr | s | j) != 0);
                             }
                         }
-                        mma_commit(&a_empty[as]);
-                        mma_commit(&b_empty[bs]);
-                        ++na;
-                        ++ntok;
+                        mma_commit(&empty[sl]);
+                        ++n;
                     }
                 }
                 if (ok) mma_commit(d_full);
@@ -619,9 +604,15 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
         const int par = GATEUP ? -1 : (grp >> 1);          // down: sub-stage parity it serves
         const uint32_t kxor = p.kxor;
         float *xb = xch + grp * 128 * kXchLd;
-        uint32_t nraw = 0, na = 0, it = 0;
+        // token loads of a sub-stage: gate/up, the first warp of groups 0 and 1 (one rotation
+        // each); down, the first warp of the group pair serving the sub-stage.  One 16-row box
+        // per lane, all issued by one instruction.
+        const bool tok_issuer = q == 0 && (GATEUP ? grp < 2 : (grp & 1) == 0);
+        uint32_t nraw = 0, na = 0, it = 0, tok_issued = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+            const int4 tt = p.tiles[item / MT];
+            const int t_y = tt.y, n16t = (tt.z + 15) >> 4;
             for (int kr = 0; kr < KR && ok; ++kr) {
                 const uint32_t rs = nraw % SW;
                 if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
@@ -630,7 +621,19 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                 for (int s = 0; s < 4; ++s) {
                     if (GATEUP || (s & 1) == par) {
                         const uint32_t as = na % kXtSA;
-                        if (!(ok = mbar_wait(&a_empty[as], ((na / kXtSA) & 1) ^ 1, abort))) break;
+                        if (!(ok = mbar_wait(&empty[as], ((na / kXtSA) & 1) ^ 1, abort))) break;
+                        if (tok_issuer) {
+                            if (lane == 0) mbar_arrive_expect_tx(&full[as], n16t * 2048);
+                            __syncwarp();
+                            uint8_t *tdst = tok + as * C::TOK_STAGE + mat * C::TOK_BOX + lane * 2048;
+                            if (lane < n16t) {
+                                if (GATEUP)
+                                    tma_load_3d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, mat, t_y + 16 * lane);
+                                else
+                                    tma_load_2d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, t_y + 16 * lane);
+                            }
+                            tok_issued = na + 1;
+                        }
                         uint32_t v[16];
                         const int kt0 = 4 * s + 2 * half;
                         trellis_column(stg + (nb * kKT + kt0) * kTileBytes3, c, kxor, v);
@@ -639,7 +642,7 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                         tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&a_full[as]);
+                        if (lane == 0) mbar_arrive(&full[as]);
                     }
                     ++na;
                 }
@@ -707,7 +710,16 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty);
         }
-        if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+        if (!ok) {
+            atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+            // token loads this warp issued land before the CTA exits (bounded: the slot's phase
+            // also needs the decode arrivals, which may never come after an abort)
+            if (tok_issuer && tok_issued > 0) {
+                int dummy = 0;
+                const uint32_t i = tok_issued - 1;
+                mbar_wait(&full[i % kXtSA], (i / kXtSA) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
