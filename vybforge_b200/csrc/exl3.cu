@@ -404,8 +404,8 @@ struct XtCfg {
     static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;
     static constexpr int D_COLS = MATS * N;
     static constexpr int A_COL0 = D_COLS;
-    static constexpr int DQ_PER_SUB = GATEUP ? kXtDq : kXtDq / 2;
-    static constexpr int TOK_ISSUERS = GATEUP ? 2 : 1;  // warps issuing a sub-stage's token loads
+    static constexpr int DQ_PER_SUB = 4;   // one decode group (four lane-quarter warps) per sub-stage
+    static constexpr int TOK_ISSUERS = 1;  // its first warp issues the sub-stage's token loads
     static_assert(SW >= 2, "double-buffered trellis stages");
     static_assert(D_COLS + kXtSA * MATS * 32 <= 512, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -599,15 +599,12 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
         const int r = 32 * q + lane;       // output channel within the tile = TMEM lane
         const int nb = r >> 4, c = r & 15; // trellis column block and column
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        const int mat = GATEUP ? (grp & 1) : 0;
-        const int half = GATEUP ? (grp >> 1) : (grp & 1);   // which 32 K of a sub-stage
-        const int par = GATEUP ? -1 : (grp >> 1);          // down: sub-stage parity it serves
         const uint32_t kxor = p.kxor;
         float *xb = xch + grp * 128 * kXchLd;
-        // token loads of a sub-stage: gate/up, the first warp of groups 0 and 1 (one rotation
-        // each); down, the first warp of the group pair serving the sub-stage.  One 16-row box
-        // per lane, all issued by one instruction.
-        const bool tok_issuer = q == 0 && (GATEUP ? grp < 2 : (grp & 1) == 0);
+        // group g decodes sub-stage g of every raw stage: K = 64 of its 32 channels for every
+        // matrix (four independent column decodes per thread), and its first warp issues the
+        // sub-stage's token loads, one 16-row box per lane in one instruction.
+        const bool tok_issuer = q == 0;
         uint32_t nraw = 0, na = 0, it = 0, tok_issued = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
@@ -616,29 +613,33 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
             for (int kr = 0; kr < KR && ok; ++kr) {
                 const uint32_t rs = nraw % SW;
                 if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
-                const uint8_t *stg = raw + rs * C::RAW_STAGE + mat * kXtRawMat;
 #pragma unroll 1
                 for (int s = 0; s < 4; ++s) {
-                    if (GATEUP || (s & 1) == par) {
+                    if (s == grp) {
                         const uint32_t as = na % kXtSA;
                         if (!(ok = mbar_wait(&empty[as], ((na / kXtSA) & 1) ^ 1, abort))) break;
                         if (tok_issuer) {
-                            if (lane == 0) mbar_arrive_expect_tx(&full[as], n16t * 2048);
+                            if (lane == 0) mbar_arrive_expect_tx(&full[as], MATS * n16t * 2048);
                             __syncwarp();
-                            uint8_t *tdst = tok + as * C::TOK_STAGE + mat * C::TOK_BOX + lane * 2048;
-                            if (lane < n16t) {
+                            if (lane < MATS * n16t) {
+                                const int m = lane / n16t, b = lane - m * n16t;
+                                uint8_t *tdst = tok + as * C::TOK_STAGE + m * C::TOK_BOX + b * 2048;
                                 if (GATEUP)
-                                    tma_load_3d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, mat, t_y + 16 * lane);
+                                    tma_load_3d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, m, t_y + 16 * b);
                                 else
-                                    tma_load_2d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, t_y + 16 * lane);
+                                    tma_load_2d(tdst, &p.xt, &full[as], kr * 256 + 64 * s, t_y + 16 * b);
                             }
                             tok_issued = na + 1;
                         }
-                        uint32_t v[16];
-                        const int kt0 = 4 * s + 2 * half;
-                        trellis_column(stg + (nb * kKT + kt0) * kTileBytes3, c, kxor, v);
-                        trellis_column(stg + (nb * kKT + kt0 + 1) * kTileBytes3, c, kxor, v + 8);
-                        tmem_st_32x32b_x16(tmem + lane_base + C::A_COL0 + (as * MATS + mat) * 32 + 16 * half, v);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+                            const uint8_t *stg = raw + rs * C::RAW_STAGE + m * kXtRawMat;
+                            uint32_t v[32];
+#pragma unroll
+                            for (int kt = 0; kt < 4; ++kt)
+                                trellis_column(stg + (nb * kKT + 4 * s + kt) * kTileBytes3, c, kxor, v + 8 * kt);
+                            tmem_st_32x32b_x32(tmem + lane_base + C::A_COL0 + (as * MATS + m) * 32, v);
+                        }
                         tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
