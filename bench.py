@@ -173,30 +173,43 @@ class ClockSampler:
         self.lines = []
 
     def start(self):
+        """Start sampling and return once the first sample has arrived (at most 3 s), so the
+        sampler is live when the timed region begins."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 3.0:
+                time.sleep(0.005)
         except Exception:
             self.proc = None
+        self.t_begin = time.perf_counter()
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
 
     def stop(self):
+        t_end = time.perf_counter()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.03)  # one more sampling period, so the region's last sample is read
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+        # samples taken while the timed region ran (20 ms period): those stamped inside
+        # [begin, end + 25 ms], else the first one after the region began
+        inside = [ln for ts, ln in self.lines if self.t_begin <= ts <= t_end + 0.025]
+        if not inside:
+            inside = [ln for ts, ln in self.lines if ts >= self.t_begin][:1]
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in inside:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
