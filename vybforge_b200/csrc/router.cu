@@ -144,116 +144,120 @@ __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__res
 }
 
 // ----------------------------------------------------------------------------- L1, prefill
-// 128 tokens x 64 experts per CTA, 256 threads x (8 tokens x 4 experts), K in chunks of 32
-// staged k-major in shared memory (float4 reads: 3 per 32 FMAs); the next chunk is loaded
-// into registers while the current one is consumed.  Each chunk is summed on its own and
-// then added to the running total, so the summation depth is 32 + HS/32 over the CTA's
-// K slice of HS = H / gridDim.z.  Slice z writes partial logits to logits + z*T*E; the
-// refinement kernel adds the gridDim.z partials in slice order (depth + gridDim.z).
-__global__ void __launch_bounds__(256) router_logits_f32_tiled(const void *__restrict__ x, int x_dtype,
-                                                               const float *__restrict__ wr, int T, int H, int E,
-                                                               float *__restrict__ logits) {
-    constexpr int BT = 128, BE = 64, KC = 32;
-    __shared__ __align__(16) float xs[KC][BT];
-    __shared__ __align__(16) float ws[KC][BE];
+// 128 tokens x 128 experts per CTA, 256 threads x (8 tokens x 8 experts), K in chunks of 16
+// staged k-major in a double-buffered shared-memory tile (one barrier per chunk; the next
+// chunk is loaded into registers while the current one is consumed): 4 float4 reads per 64
+// FMAs.  Each chunk is summed on its own and then added to the running total, so the
+// summation depth is 16 + HS/16 over the CTA's K slice of HS = H / gridDim.z.  Slice z
+// writes partial logits to logits + z*T*E, added in slice order by router_refine.
+__global__ void __launch_bounds__(256, 1) router_logits_f32_wide(const void *__restrict__ x, int x_dtype,
+                                                                 const float *__restrict__ wr, int T, int H, int E,
+                                                                 float *__restrict__ logits) {
+    constexpr int BT = 128, BE = 128, KC = 16;
+    __shared__ __align__(16) float xs[2][KC][BT];
+    __shared__ __align__(16) float ws[2][KC][BE];
     const int t0 = blockIdx.y * BT, e0 = blockIdx.x * BE;
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;  // experts e0 + 4tx .. +3, tokens t0 + 8ty .. +7
+    const int tx = tid & 15, ty = tid >> 4;  // experts e0 + 4tx.., e0 + 64 + 4tx..; tokens t0 + 8ty ..
     const int HS = H / gridDim.z, k0 = blockIdx.z * HS;
     logits += (int64_t)blockIdx.z * T * E;
-    // loader mapping: x tile 128 rows x 32 k = 512 groups of 8 k (2 per thread);
-    // w tile 64 rows x 32 k = 512 float4 (2 per thread)
-    float xr[2][8], wv[2][4];
+    const int lrow = tid >> 1, lkq = (tid & 1) * 8;  // loader: one row of the x or W tile, 8 k
+    float xr[8], wv[8];
     auto load = [&](int kb) {
+        const int t = t0 + lrow;
+        if (t < T) {
+            if (x_dtype == VFMOE_DT_BF16) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(x) +
+                                                                 (int64_t)t * H + kb + lkq);
+                const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int gi = tid + 256 * r;
-            const int row = gi >> 2, kq = (gi & 3) * 8;
-            const int t = t0 + row;
-            if (t < T) {
-                if (x_dtype == VFMOE_DT_BF16) {
-                    const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(x) +
-                                                                     (int64_t)t * H + kb + kq);
-                    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        xr[r][2 * i] = __uint_as_float(uu[i] << 16);
-                        xr[r][2 * i + 1] = __uint_as_float(uu[i] & 0xFFFF0000u);
-                    }
-                } else {
-                    const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) +
-                                                                         (int64_t)t * H + kb + kq);
-                    const float4 a = src[0], b = src[1];
-                    xr[r][0] = a.x; xr[r][1] = a.y; xr[r][2] = a.z; xr[r][3] = a.w;
-                    xr[r][4] = b.x; xr[r][5] = b.y; xr[r][6] = b.z; xr[r][7] = b.w;
+                for (int i = 0; i < 4; ++i) {
+                    xr[2 * i] = __uint_as_float(uu[i] << 16);
+                    xr[2 * i + 1] = __uint_as_float(uu[i] & 0xFFFF0000u);
                 }
             } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xr[r][i] = 0.f;
+                const float4 *src =
+                    reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + (int64_t)t * H + kb + lkq);
+                const float4 a = src[0], b = src[1];
+                xr[0] = a.x; xr[1] = a.y; xr[2] = a.z; xr[3] = a.w;
+                xr[4] = b.x; xr[5] = b.y; xr[6] = b.z; xr[7] = b.w;
             }
-            const int erow = gi >> 3, ek = (gi & 7) * 4;
-            const int e = e0 + erow;
-            float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < E) w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)e * H + kb + ek);
-            wv[r][0] = w4.x; wv[r][1] = w4.y; wv[r][2] = w4.z; wv[r][3] = w4.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xr[i] = 0.f;
+        }
+        const int e = e0 + lrow;
+        if (e < E) {
+            const float4 *src = reinterpret_cast<const float4 *>(wr + (int64_t)e * H + kb + lkq);
+            const float4 a = src[0], b = src[1];
+            wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+            wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) wv[i] = 0.f;
         }
     };
-    auto store = [&]() {
+    auto store = [&](int buf) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int gi = tid + 256 * r;
-            const int row = gi >> 2, kq = (gi & 3) * 8;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) xs[kq + i][row] = xr[r][i];
-            const int erow = gi >> 3, ek = (gi & 7) * 4;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) ws[ek + i][erow] = wv[r][i];
+        for (int i = 0; i < 8; ++i) {
+            xs[buf][lkq + i][lrow] = xr[i];
+            ws[buf][lkq + i][lrow] = wv[i];
         }
     };
-    float acc[8][4];
+    float acc[8][8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
     load(k0);
-    for (int kb = k0; kb < k0 + HS; kb += KC) {
-        __syncthreads();
-        store();
-        __syncthreads();
-        if (kb + KC < k0 + HS) load(kb + KC);
-        float part[8][4];
+    store(0);
+    __syncthreads();
+    const int nch = HS / KC;
+    for (int c = 0; c < nch; ++c) {
+        const int buf = c & 1;
+        const bool more = c + 1 < nch;
+        if (more) load(k0 + (c + 1) * KC);
+        float part[8][8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) part[i][j] = 0.f;
-#pragma unroll 4
+            for (int j = 0; j < 8; ++j) part[i][j] = 0.f;
+#pragma unroll
         for (int kk = 0; kk < KC; ++kk) {
-            const float4 xa = *reinterpret_cast<const float4 *>(&xs[kk][8 * ty]);
-            const float4 xb = *reinterpret_cast<const float4 *>(&xs[kk][8 * ty + 4]);
-            const float4 w4 = *reinterpret_cast<const float4 *>(&ws[kk][4 * tx]);
+            const float4 xa = *reinterpret_cast<const float4 *>(&xs[buf][kk][8 * ty]);
+            const float4 xb = *reinterpret_cast<const float4 *>(&xs[buf][kk][8 * ty + 4]);
+            const float4 wa = *reinterpret_cast<const float4 *>(&ws[buf][kk][4 * tx]);
+            const float4 wb = *reinterpret_cast<const float4 *>(&ws[buf][kk][64 + 4 * tx]);
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            const float wc[4] = {w4.x, w4.y, w4.z, w4.w};
+            const float wc[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) part[i][j] = fmaf(xv[i], wc[j], part[i][j]);
+                for (int j = 0; j < 8; ++j) part[i][j] = fmaf(xv[i], wc[j], part[i][j]);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] += part[i][j];
+            for (int j = 0; j < 8; ++j) acc[i][j] += part[i][j];
+        if (more) store(buf ^ 1);
+        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int t = t0 + 8 * ty + i;
         if (t >= T) continue;
-        if (e0 + 4 * tx + 3 < E) {
-            *reinterpret_cast<float4 *>(logits + (int64_t)t * E + e0 + 4 * tx) =
-                make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (e0 + 4 * tx + j < E) logits[(int64_t)t * E + e0 + 4 * tx + j] = acc[i][j];
+        for (int h = 0; h < 2; ++h) {
+            const int e = e0 + 64 * h + 4 * tx;
+            float *dst = logits + (int64_t)t * E + e;
+            if (e + 3 < E && (E & 3) == 0) {
+                *reinterpret_cast<float4 *>(dst) =
+                    make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (e + j < E) dst[j] = acc[i][4 * h + j];
+            }
         }
     }
 }
@@ -644,14 +648,14 @@ static int launch_l1_small(const void *x, int x_dtype, const float *wr, int T, i
     return VFMOE_OK;
 }
 
-// K slices of the tiled logits kernel: enough CTAs for about two waves on 148 SMs, at most
-// kMaxChunks, each slice a multiple of 32 columns of H.
+// K slices of the prefill logits kernel: enough CTAs (one per SM) for about two waves on
+// 148 SMs, at most kMaxChunks, each slice a multiple of 16 columns of H.
 static int tiled_splits(int T, int H, int E) {
-    const int64_t base = cdiv(E, 64) * cdiv(T, 128);
+    const int64_t base = cdiv(E, 128) * cdiv(T, 128);
     const int want = (int)std::min<int64_t>(kMaxChunks, cdiv(296, base));
     int s = 1;
     for (int c = 1; c <= want; ++c)
-        if ((H / 32) % c == 0) s = c;
+        if ((H / 16) % c == 0) s = c;
     return s;
 }
 
@@ -673,10 +677,10 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
         c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
         nchunk = tiled_splits(T, H, E);
-        dim3 grid((unsigned)cdiv(E, 64), (unsigned)cdiv(T, 128), (unsigned)nchunk);
-        router_logits_f32_tiled<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
-        VF_LAUNCH_CHECK("router_logits_f32_tiled");
-        c1 = gamma_bound(32 + H / nchunk / 32 + nchunk);
+        dim3 grid((unsigned)cdiv(E, 128), (unsigned)cdiv(T, 128), (unsigned)nchunk);
+        router_logits_f32_wide<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
+        VF_LAUNCH_CHECK("router_logits_f32_wide");
+        c1 = gamma_bound(16 + H / nchunk / 16 + nchunk);
     }
     // L2: thread owns n = H/256 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
     // exactly (TwoProduct), so the only error is lo's fp32 summation of the r and pe values,
