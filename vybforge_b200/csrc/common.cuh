@@ -30,6 +30,34 @@ int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
         if (_e != cudaSuccess) return ::vfmoe::cuda_fail(_e, name, __FILE__, __LINE__); \
     } while (0)
 
+// ----------------------------------------------------------------------------- chained launches
+// Programmatic dependent launch for the small kernels of one forward: the next kernel on the
+// stream is scheduled while this one runs, and waits (griddepcontrol.wait) for its
+// predecessor's completion and memory before touching anything.  A kernel that takes part
+// calls pdl_wait_then_release() first thing, so it releases its own dependents only after its
+// predecessor has completed: any kernel downstream therefore also sees every earlier kernel's
+// output.  Outside a programmatic launch both instructions return at once.
+__device__ __forceinline__ void pdl_wait_then_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Device-side error codes written to a layer's error word (first error wins).
 enum DevErr : int {
     DEV_OK = 0,

@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
                                                        int *__restrict__ err) {
     __shared__ int red[8];
     __shared__ int warp_tot[8];
+    pdl_wait_then_release();
     const int e = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t tk = (int64_t)T * k;
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
 __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x, int x_dtype,
                                                      const int32_t *__restrict__ perm_tok, int H,
                                                      __half *__restrict__ xp, const int32_t *__restrict__ n_rows) {
+    pdl_wait_then_release();
     const int64_t pos = blockIdx.x;
     if (pos >= *n_rows) return;
     const int t = perm_tok[pos];
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void *__restrict__ y
                                                       void *__restrict__ out, int out_dtype) {
     __shared__ int64_t sp[33];
     __shared__ float sw[32];
+    pdl_wait_then_release();
     const int t = blockIdx.x;
     if (threadIdx.x < k) {
         const int32_t p = pos_of[(int64_t)t * k + threadIdx.x];
@@ -355,7 +358,8 @@ int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *id
 
 int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st) {
-    dispatch_kernel<<<E + 1, 256, 0, st>>>(idx, counts, T, E, k, has_shared, perm_tok, pos_of, offsets, err);
+    VF_CUDA(launch_pdl(dispatch_kernel, dim3(E + 1), dim3(256), 0, st, idx, counts, T, E, k, has_shared, perm_tok, pos_of,
+                       offsets, err));
     VF_LAUNCH_CHECK("dispatch_kernel");
     return VFMOE_OK;
 }
@@ -363,7 +367,7 @@ int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
                   const int32_t *n_rows, cudaStream_t st) {
     if (rows == 0) return VFMOE_OK;
-    gather_kernel<<<(unsigned)rows, 128, 0, st>>>(x, x_dtype, perm_tok, H, xp, n_rows);
+    VF_CUDA(launch_pdl(gather_kernel, dim3((unsigned)rows), dim3(128), 0, st, x, x_dtype, perm_tok, H, xp, n_rows));
     VF_LAUNCH_CHECK("gather_kernel");
     return VFMOE_OK;
 }
@@ -372,7 +376,7 @@ int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const floa
                    const void *y_shared, void *out, int out_dtype, cudaStream_t st) {
     if (T == 0) return VFMOE_OK;
     dim3 grid((unsigned)T, (unsigned)cdiv(H, 1024));
-    combine_kernel<<<grid, 256, 0, st>>>(y, y_dtype, pos_of, w, T, H, k, y_shared, out, out_dtype);
+    VF_CUDA(launch_pdl(combine_kernel, grid, dim3(256), 0, st, y, y_dtype, pos_of, w, T, H, k, y_shared, out, out_dtype));
     VF_LAUNCH_CHECK("combine_kernel");
     return VFMOE_OK;
 }

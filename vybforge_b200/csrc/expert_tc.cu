@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict
                                                        int n_gu, int n_dn, int4 *__restrict__ tiles, int64_t cap,
                                                        int32_t *__restrict__ counts, int *__restrict__ err) {
     __shared__ int sc[2][1024];
+    pdl_wait_then_release();
     const int tid = threadIdx.x;
     const int nexp = E + (has_shared ? 1 : 0);
     for (int which = 0; which < 2; ++which) {
@@ -493,8 +494,8 @@ bool tc_supported(const TcPlan &plan, const MoeArgs &a) {
 int64_t tc_tiles_capacity(int T, int k, int E) { return ((int64_t)T * k + T) / 8 + E + 2; }
 
 int launch_tc_plan(const MoeArgs &a, int n_gu, int n_dn, cudaStream_t st) {
-    tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap, a.tile_counts,
-                                       a.err);
+    VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared, n_gu,
+                       n_dn, a.tiles, a.tiles_cap, a.tile_counts, a.err));
     VF_LAUNCH_CHECK("tc_plan_kernel");
     return VFMOE_OK;
 }
@@ -525,7 +526,8 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     if ((double)a.T * a.k / a.E <= 16.0 && !plan.decode_tc) {
         // decode: register-operand GEMV, one token-tile size for both GEMMs
         const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
-        tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, ng, ng, a.tiles, a.tiles_cap, a.tile_counts, a.err);
+        VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared, ng,
+                           ng, a.tiles, a.tiles_cap, a.tile_counts, a.err));
         VF_LAUNCH_CHECK("tc_plan_kernel");
         CUtensorMap tg, td;
         int rc;
@@ -536,8 +538,8 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     const int n = pick_n(a.T, a.k, a.E);
     const int n_gu = std::min(n, 128);
     const int n_dn = n;
-    tc_plan_kernel<<<1, 1024, 0, st>>>(a.offsets, a.E, a.has_shared, n_gu, n_dn, a.tiles, a.tiles_cap,
-                                       a.tile_counts, a.err);
+    VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared, n_gu,
+                       n_dn, a.tiles, a.tiles_cap, a.tile_counts, a.err));
     VF_LAUNCH_CHECK("tc_plan_kernel");
     int rc;
     TcParams g{};

@@ -299,6 +299,7 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     __shared__ unsigned char s_redo[kMaxCand];
     __shared__ float s_phi[8][8], s_plo[8][8];
     __shared__ double s_pd[8][8];
+    pdl_wait_then_release();
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -711,14 +712,16 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
             attr = true;
         }
     }
-#define VF_REFINE(NPL)                                                                                             \
-    do {                                                                                                          \
-        if (T <= 64)                                                                                              \
-            router_refine<NPL, 8, 1><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, \
-                                                                      E, k, c1, c2, scale, idx, w, counts, err);  \
-        else                                                                                                      \
-            router_refine<NPL, 4, 3><<<(unsigned)T, 256, H * 4, st>>>(x, x_dtype, wr, logits, nchunk, nw, bias, T, H, \
-                                                                      E, k, c1, c2, scale, idx, w, counts, err);  \
+#define VF_REFINE(NPL)                                                                                              \
+    do {                                                                                                           \
+        if (T <= 64)                                                                                               \
+            VF_CUDA(launch_pdl(router_refine<NPL, 8, 1>, dim3((unsigned)T), dim3(256), (size_t)H * 4, st, x, x_dtype, \
+                               wr, (const float *)logits, nchunk, nw, bias, T, H, E, k, c1, c2, scale, idx, w, counts, \
+                               err));                                                                              \
+        else                                                                                                       \
+            VF_CUDA(launch_pdl(router_refine<NPL, 4, 3>, dim3((unsigned)T), dim3(256), (size_t)H * 4, st, x, x_dtype, \
+                               wr, (const float *)logits, nchunk, nw, bias, T, H, E, k, c1, c2, scale, idx, w, counts, \
+                               err));                                                                              \
     } while (0)
     if (npl <= 1) VF_REFINE(1);
     else if (npl <= 2) VF_REFINE(2);
