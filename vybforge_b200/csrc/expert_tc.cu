@@ -104,32 +104,55 @@ __device__ __forceinline__ void q8_two_blocks(const uint32_t (&g)[17], uint32_t 
 __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict__ offsets, int E, int has_shared,
                                                        int n_gu, int n_dn, int4 *__restrict__ tiles, int64_t cap,
                                                        int32_t *__restrict__ counts, int *__restrict__ err) {
-    __shared__ int sc[2][1024];
+    __shared__ int wsum[2][32];
     pdl_wait_then_release();
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nexp = E + (has_shared ? 1 : 0);
-    for (int which = 0; which < 2; ++which) {
-        const int N = which == 0 ? n_gu : n_dn;
-        int4 *out = tiles + which * cap;
-        // each thread owns experts [tid*per, (tid+1)*per)
-        const int per = (nexp + 1023) / 1024;
-        int mine = 0;
-        for (int i = 0; i < per; ++i) {
-            const int e = tid * per + i;
-            if (e < nexp) {
-                const int n = offsets[e + 1] - offsets[e];
-                mine += (n + N - 1) / N;
+    const int per = (nexp + 1023) / 1024;  // each thread owns experts [tid*per, (tid+1)*per)
+    const int Ns[2] = {n_gu, n_dn};
+    // tiles of this thread's experts for both lists, then one block-wide exclusive scan of both
+    // (warp shuffles; the 32 warp totals are scanned by warp 0)
+    int mine[2] = {0, 0};
+    for (int i = 0; i < per; ++i) {
+        const int e = tid * per + i;
+        if (e < nexp) {
+            const int n = offsets[e + 1] - offsets[e];
+            mine[0] += (n + Ns[0] - 1) / Ns[0];
+            mine[1] += (n + Ns[1] - 1) / Ns[1];
+        }
+    }
+    int inc[2] = {mine[0], mine[1]};
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+        for (int l = 0; l < 2; ++l) {
+            const int v = __shfl_up_sync(0xffffffffu, inc[l], o);
+            if (lane >= o) inc[l] += v;
+        }
+    }
+    if (lane == 31) {
+        wsum[0][warp] = inc[0];
+        wsum[1][warp] = inc[1];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int l = 0; l < 2; ++l) {
+            int v = wsum[l][lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += u;
             }
+            wsum[l][lane] = v;  // inclusive over warps
         }
-        sc[which][tid] = mine;
-        __syncthreads();
-        for (int o = 1; o < 1024; o <<= 1) {
-            const int v = tid >= o ? sc[which][tid - o] : 0;
-            __syncthreads();
-            sc[which][tid] += v;
-            __syncthreads();
-        }
-        int pos = sc[which][tid] - mine;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int l = 0; l < 2; ++l) {
+        const int N = Ns[l];
+        int4 *out = tiles + l * cap;
+        int pos = inc[l] - mine[l] + (warp > 0 ? wsum[l][warp - 1] : 0);
         for (int i = 0; i < per; ++i) {
             const int e = tid * per + i;
             if (e < nexp) {
@@ -145,11 +168,11 @@ __global__ void __launch_bounds__(1024) tc_plan_kernel(const int32_t *__restrict
                 }
             }
         }
-        if (tid == 1023) {
-            counts[which] = (int32_t)(sc[which][1023] < cap ? sc[which][1023] : cap);
-            if (sc[which][1023] > cap) raise_dev_error(err, DEV_BAD_COUNT);
+        if (tid == 0) {
+            const int tot = wsum[l][31];
+            counts[l] = (int32_t)(tot < cap ? tot : cap);
+            if (tot > cap) raise_dev_error(err, DEV_BAD_COUNT);
         }
-        __syncthreads();
     }
 }
 

@@ -30,6 +30,36 @@ constexpr int kMaxCand = 64;
 constexpr int kMaxH = 16384;     // router_refine keeps x_t in shared memory (fp32)
 constexpr int kMaxChunks = 32;   // L1 decode partial-sum chunks (H / 512)
 
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic, round to nearest even in each lane).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ void two_sum(float a, float b, float &s, float &t) {
     s = a + b;
     const float bb = s - a;
@@ -470,18 +500,26 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
                 if (h >= H) break;
                 const float4 x4 = *reinterpret_cast<const float4 *>(s_x + h);
                 const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+                // two candidates per instruction (packed f32x2, each lane an IEEE fp32 op):
+                // the same operations in the same order as the scalar TwoProduct / TwoSum
 #pragma unroll
-                for (int c = 0; c < CPP; ++c) {
-                    const float wv[4] = {w4[c][j].x, w4[c][j].y, w4[c][j].z, w4[c][j].w};
+                for (int c = 0; c < CPP; c += 2) {
+                    const float wa[4] = {w4[c][j].x, w4[c][j].y, w4[c][j].z, w4[c][j].w};
+                    const float wb[4] = {w4[c + 1][j].x, w4[c + 1][j].y, w4[c + 1][j].z, w4[c + 1][j].w};
+                    uint64_t sh = f2_pack(shi[c], shi[c + 1]), sl = f2_pack(slo[c], slo[c + 1]);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float p = xv[i] * wv[i];
-                        const float pe = fmaf(xv[i], wv[i], -p);  // exact: x*w = p + pe
-                        float sum, r;
-                        two_sum(shi[c], p, sum, r);
-                        shi[c] = sum;
-                        slo[c] += r + pe;
+                        const uint64_t x2 = f2_pack(xv[i], xv[i]), w2 = f2_pack(wa[i], wb[i]);
+                        const uint64_t pp = f2_mul(x2, w2);
+                        const uint64_t pe = f2_fma(x2, w2, pp ^ 0x8000000080000000ull);  // exact: x*w = p + pe
+                        const uint64_t sum = f2_add(sh, pp);
+                        const uint64_t bb = f2_sub(sum, sh);
+                        const uint64_t r = f2_add(f2_sub(sh, f2_sub(sum, bb)), f2_sub(pp, bb));
+                        sh = sum;
+                        sl = f2_add(sl, f2_add(r, pe));
                     }
+                    f2_unpack(sh, shi[c], shi[c + 1]);
+                    f2_unpack(sl, slo[c], slo[c + 1]);
                 }
             }
         }
