@@ -133,7 +133,8 @@ int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w
  * device memory in its own pool).  No counterpart in the reference.  Same result as
  * vfmoe_route.  Scratch is a fixed VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES device array inside
  * the library, held on every GPU that loads it until exit; larger T is rejected with
- * VFMOE_ERR_UNSUPPORTED (about T <= 4000 at E = 256).  The first call on a device looks
+ * VFMOE_ERR_UNSUPPORTED: the scratch holds the router's fp32 partial logits (T x E x K-slices)
+ * plus the expert counts, which allows T <= 127 at E = 256, H = 6144 (decode batches).  The first call on a device looks
  * up the array's address; make it before any stream capture.  Calls share the array:
  * calls that overlap on the GPU race. */
 #define VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES (4 << 20)
