@@ -249,8 +249,9 @@ int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, i
 
 /* EXL3 trellis -> rotated-basis values W^ as fp16 [K, N] (no Hadamard).
  * Replaces exl3deq / exl3deq32 (native/kernels/exl3.vyb:207-242,375-422).
- * bits = 3 (layout defined by this library); 4 (the reference slot map) returns
- * VFMOE_ERR_UNSUPPORTED in this build. */
+ * bits = 3 (layout defined by this library) or 4 (the reference's format: its slot map,
+ * native/exl3/map.bin and exl3_ref.py:66-107, applied in closed form); trellis 16-byte
+ * aligned, 16*bits uint16 words per 16x16 tile. */
 int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, int64_t bits,
                       int64_t stream);
 

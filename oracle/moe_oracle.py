@@ -29,7 +29,8 @@ Deliberate differences from the reference, each required by the task spec:
   the same f64 math, so results agree with ``moe_block`` to f64 rounding.
 * EXL3 at 3 bits/weight uses the bitstream layout defined in
   ``exl3_windows_3bpw`` (the reference only has 4 bpw); 4 bpw uses the
-  reference's verified slot composition table.
+  reference's verified slot composition table, or its closed form
+  ``exl3_windows_4bpw_words`` (equal on every slot; the GPU path uses the latter).
 
 Parity pinning: ``tests/test_oracle.py`` checks this module against the
 reference's committed golden data (native/glm53/prep/ref_{out,idx,w}.f32,
@@ -286,6 +287,33 @@ def exl3_windows_4bpw(tiles, slot_nibble, slot_pos):
     return w.astype(np.uint16).reshape(*lead, 16, 16)
 
 
+def exl3_windows_4bpw_words(tiles):
+    """4-bpw windows in closed form (equal to ``exl3_windows_4bpw`` with the reference's slot
+    table, checked on every slot by tests/test_oracle.py).  Tile words w[0..63] (uint16);
+    output column c takes four 32-bit pairs v_j = A_j | B_j << 16, j = 0..3:
+      c <  8:  A_j = w[8c + 2j + 1], B_j = w[(8c + 2j - 2) mod 64]
+      c >= 8:  A_j = w[8(c-8) + 2j], B_j = w[8(c-8) + 2j + 1]
+    and the window of row 2j + (9, 8, 1, 0)[t] is bits [4t, 4t + 16) of v_j.
+    Returns uint16 [..., 16, 16] (row r, column c)."""
+    t = np.asarray(tiles)
+    if t.dtype == np.int16:
+        t = t.view(np.uint16)
+    t = t.astype(np.uint32)
+    lead = t.shape[:-1]
+    assert t.shape[-1] == 64
+    out = np.zeros((*lead, 16, 16), np.uint32)
+    for c in range(16):
+        for j in range(4):
+            if c < 8:
+                a, b = t[..., 8 * c + 2 * j + 1], t[..., (8 * c + 2 * j - 2) % 64]
+            else:
+                a, b = t[..., 8 * (c - 8) + 2 * j], t[..., 8 * (c - 8) + 2 * j + 1]
+            v = a | (b << np.uint32(16))
+            for tt, r0 in enumerate((9, 8, 1, 0)):
+                out[..., r0 + 2 * j, c] = (v >> np.uint32(4 * tt)) & np.uint32(0xFFFF)
+    return out.astype(np.uint16)
+
+
 def hadamard128():
     """Natural-order Sylvester H_128 (exl3_ref.py:58-63)."""
     h = np.ones((1, 1), dtype=np.float64)
@@ -307,9 +335,8 @@ def exl3_what(trellis, bits, slot_table=None):
     if bits == 3:
         w16 = exl3_windows_3bpw(tr)
     elif bits == 4:
-        if slot_table is None:
-            raise ValueError("4-bpw decode needs the slot composition table")
-        w16 = exl3_windows_4bpw(tr, *slot_table)
+        # the reference's slot table when given, else its closed form (pinned equal)
+        w16 = exl3_windows_4bpw(tr, *slot_table) if slot_table is not None else exl3_windows_4bpw_words(tr)
     else:
         raise ValueError(f"unsupported EXL3 bits {bits}")
     vals = decode_mcg(w16).astype(np.float64)             # [kb, nb, 16, 16]

@@ -91,8 +91,8 @@ def _exl3_desc(bits):
 
 
 def test_exl3_descriptors(built_lib):
-    assert built_lib.vfmoe_layer_create(C.byref(_exl3_desc(4))) == _lib.ERR_UNSUPPORTED
-    assert "exl3_bits=4" in _lib.last_error()
+    assert built_lib.vfmoe_layer_create(C.byref(_exl3_desc(5))) == _lib.ERR_INVALID
+    assert "exl3_bits must be 3 or 4" in _lib.last_error()
     d = _exl3_desc(3)
     d.up.suh = 0
     assert built_lib.vfmoe_layer_create(C.byref(d)) == _lib.ERR_INVALID

@@ -1,4 +1,4 @@
-"""GPU parity of the EXL3 3-bpw expert path against the oracle.
+"""GPU parity of the EXL3 expert paths (3 bpw, and the reference's 4 bpw) against the oracle.
 
 The oracle dequantizes every expert matrix the reference way (exl3_ref.py:84-120:
 W = diag(suh) Hb W^ Hb diag(svh), float64 here) and runs the per-expert FFN; the GPU
@@ -98,16 +98,49 @@ def test_exl3_forward_rows_matches_forward(small):
 
 
 def test_exl3_format_errors():
-    """4 bpw is declined with a status (no kernel for it); strides are validated."""
+    """Bit widths other than 3 and 4 are declined with a status."""
     moe.init(0)
     cfg = synth.config("c0", tokens=4, fmt="exl3")
     b = Built(cfg)
     E = cfg.n_experts
-    with pytest.raises(RuntimeError, match="exl3_bits=4"):
+    with pytest.raises(RuntimeError, match="exl3_bits must be 3 or 4"):
         moe.MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk, router_w=b.wr_dev,
                      router_bias=b.bias_dev, gate=tuple(a[:E] for a in b.dev[0]),
                      up=tuple(a[:E] for a in b.dev[1]), down=tuple(a[:E] for a in b.dev[2]),
-                     fmt="exl3", exl3_bits=4, x_dtype=torch.float32)
+                     fmt="exl3", exl3_bits=5, x_dtype=torch.float32)
+
+
+# ----------------------------------------------------------------------------- 4 bpw
+def _cfg4(tokens):
+    cfg = synth.config("c0", tokens=tokens, fmt="exl3")
+    cfg.exl3_bits = 4
+    return cfg
+
+
+@pytest.fixture(scope="module")
+def small4():
+    """C0 shapes with EXL3 4-bpw weights (the reference's format), 64 tokens."""
+    moe.init(0)
+    return Built(_cfg4(64))
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])   # decode GEMV: token tiles of 8, 16 and 32 rows
+def test_exl3_4bpw_decode_path_parity(small4, T):
+    x = small4.x_dev[:T].contiguous()
+    out, idx, w = small4.layer.moe_block(x)
+    torch.cuda.synchronize()
+    small4.layer.check_device_error()
+    _check(small4, out.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), np.arange(T), f"exl3-4bpw c0-shape T={T}")
+
+
+def test_exl3_4bpw_prefill_tcgen05_parity():
+    """256 tokens (64 rows per expert): the tcgen05 prefill kernels with 4-bpw tiles."""
+    moe.init(0)
+    b = Built(_cfg4(256))
+    out, idx, w = b.layer.moe_block(b.x_dev)
+    torch.cuda.synchronize()
+    b.layer.check_device_error()
+    _check(b, out.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), np.arange(256), "exl3-4bpw c0-shape T=256 tcgen05")
 
 
 # ----------------------------------------------------------------------------- full-size C2

@@ -163,6 +163,24 @@ def test_exl3_3bpw_decode_bit_exact():
     np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
 
 
+def test_exl3_4bpw_decode_bit_exact():
+    """4 bpw (the reference's format) through the GPU's closed-form window extraction against
+    the oracle's decode with the reference's slot table, and against the reference's own
+    trellis fixture."""
+    rng = np.random.default_rng(9)
+    K, N = 256, 384
+    tr = rng.integers(0, 1 << 16, size=(K // 16, N // 16, 64), dtype=np.uint32).astype(np.uint16)
+    got = moe.exl3_decode(torch.from_numpy(tr.view(np.int16)).cuda(), K, N, 4)
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "exl3_kat.npz"))
+    table = (g["slot_nibble"].astype(int), g["slot_pos"].astype(int))
+    want = orc.exl3_what(tr, 4, table).astype(np.float16)
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
+    tr4 = g["tr4"]
+    got4 = moe.exl3_decode(torch.from_numpy(tr4.view(np.int16)).cuda(), 16 * tr4.shape[0], 16 * tr4.shape[1], 4)
+    want4 = orc.exl3_what(tr4, 4, table).astype(np.float16)
+    np.testing.assert_array_equal(got4.cpu().numpy().view(np.uint16), want4.view(np.uint16))
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_rmsnorm(dtype):
     rng = np.random.default_rng(2)

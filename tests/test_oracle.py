@@ -121,6 +121,21 @@ def test_exl3_4bpw_dequant_matches_reference():
     assert np.all(np.abs(ours - ref) <= ulp + 1e-7)
 
 
+def test_exl3_4bpw_closed_form_equals_reference_slot_table():
+    """The GPU's word-pair form of the 4-bpw windows equals the reference's verified slot
+    composition (exl3_ref.py:66-81, 97-107) on every slot of random tiles and of the
+    reference's own trellis fixture."""
+    g = np.load(os.path.join(GOLD, "exl3_kat.npz"))
+    rng = np.random.default_rng(11)
+    tiles = rng.integers(0, 1 << 16, size=(64, 64), dtype=np.uint32).astype(np.uint16)
+    np.testing.assert_array_equal(orc.exl3_windows_4bpw_words(tiles), orc.exl3_windows_4bpw(tiles, *slot_table()))
+    np.testing.assert_array_equal(orc.exl3_windows_4bpw_words(g["tr4"]), orc.exl3_windows_4bpw(g["tr4"], *slot_table()))
+    ref = g["w4"].view(np.float16).astype(np.float64)
+    ours = orc.dequant_exl3(g["tr4"], g["suh4"], g["svh4"], 4)
+    ulp = np.abs(np.spacing(ref.astype(np.float16))).astype(np.float64)
+    assert np.all(np.abs(ours - ref) <= ulp + 1e-7)
+
+
 # ----------------------------------------------------------------------------- restatement-internal checks
 def test_exl3_3bpw_windows_bit_by_bit():
     rng = np.random.default_rng(5)

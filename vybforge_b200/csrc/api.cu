@@ -188,10 +188,6 @@ static int validate(const vfmoe_layer_desc &d) {
         if (d.sh_gate.data && (!d.sh_up.data || !d.sh_down.data)) return bad("shared expert incomplete");
     } else if (d.weight_format == VFMOE_WFMT_EXL3) {
         if (d.exl3_bits != 3 && d.exl3_bits != 4) return bad("exl3_bits must be 3 or 4");
-        if (d.exl3_bits != 3) {
-            set_error("EXL3 expert products: exl3_bits=%d is not supported by this build (3 only)", (int)d.exl3_bits);
-            return VFMOE_ERR_UNSUPPORTED;
-        }
         const vfmoe_matrix *ms[6] = {&d.gate, &d.up, &d.down, &d.sh_gate, &d.sh_up, &d.sh_down};
         const int64_t kk[3] = {d.hidden, d.hidden, d.inter}, nn[3] = {d.inter, d.inter, d.hidden};
         const int64_t nl = d.n_local_experts ? d.n_local_experts : d.n_experts;
@@ -769,9 +765,13 @@ int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, in
         set_error("vfmoe_exl3_decode: bad arguments");
         return VFMOE_ERR_INVALID;
     }
-    if (bits != 3) {
-        set_error("vfmoe_exl3_decode: bits=%lld not supported by this build", (long long)bits);
-        return VFMOE_ERR_UNSUPPORTED;
+    if (bits != 3 && bits != 4) {
+        set_error("vfmoe_exl3_decode: bits=%lld (3 or 4 expected)", (long long)bits);
+        return VFMOE_ERR_INVALID;
+    }
+    if (trellis & 15) {
+        set_error("vfmoe_exl3_decode: trellis must be 16-byte aligned");
+        return VFMOE_ERR_INVALID;
     }
     return launch_exl3_decode(reinterpret_cast<const uint16_t *>(trellis), reinterpret_cast<__half *>(dst_f16), K,
                               N, (int)bits, reinterpret_cast<cudaStream_t>(stream));

@@ -101,6 +101,23 @@ __device__ __forceinline__ __half exl3_mcg(uint32_t w16) {
     return __hadd(lo, hi);
 }
 
+// EXL3 4 bpw (the reference's format; its verified slot table, exl3_ref.py:66-81 and
+// native/exl3/map.bin, in closed form): a 16x16 tile is 64 uint16 words w (32 u32 t32,
+// little-endian pairs).  Output column c's 16 windows come from four 32-bit values
+//   c <  8:  v_j = w[8c + 2j + 1] | w[(8c + 2j - 2) mod 64] << 16
+//   c >= 8:  v_j = w[8(c-8) + 2j] | w[8(c-8) + 2j + 1] << 16   (= t32[4(c-8) + j])
+// and tile row 2j + (9, 8, 1, 0)[t] decodes the window at bits [4t, 4t + 16) of v_j.
+__device__ __forceinline__ void exl3_col4_pairs(const uint32_t *t32, int c, uint32_t (&v)[4]) {
+    if (c >= 8) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = t32[4 * (c - 8) + j];
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)  // high half of t32[4c + j], low half of t32[4c + j - 1]
+            v[j] = __byte_perm(t32[4 * c + j], t32[(4 * c + j + 31) & 31], 0x5432);
+    }
+}
+
 // Q8_0 block: fp16 d at +0, int8 q[32] at +2 (34 bytes, 2-byte aligned).
 __device__ __forceinline__ float q8_scale(const uint8_t *blk) {
     return __half2float(*reinterpret_cast<const __half *>(blk));

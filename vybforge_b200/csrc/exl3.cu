@@ -36,6 +36,8 @@ using namespace sm100;
 constexpr float kRScale = 0.08838834764831845f;  // 1/sqrt(128)
 constexpr int kKT = 16;                            // k-tiles (of 16) per stage = 256 K
 constexpr int kTileBytes3 = 96;                    // 48 uint16 words
+template <int BITS>
+constexpr int kTileBytes = 32 * BITS;             // 3 bpw: 96 B (48 words), 4 bpw: 128 B (64 words)
 
 // ----------------------------------------------------------------------------- FWHT helpers
 // 128-point unnormalised Walsh-Hadamard transform of v[q] = element (lane + 32q), q = 0..3,
@@ -110,14 +112,14 @@ __global__ void __launch_bounds__(256) gather_exl3_kernel(const void *__restrict
 // CW consumer warps: 8 own 16 channels each over the whole 256-K stage; with 16 the second
 // group takes the upper half of every stage (k-tiles 8..15) and the two partial sums meet
 // in the epilogue exchange buffer.
-template <bool GATEUP, int NT, int CW>
+template <bool GATEUP, int NT, int CW, int BITS>
 struct XCfg {
     static constexpr int N = 8 * NT;
     static constexpr int MATS = GATEUP ? 2 : 1;
     static constexpr int KG = CW / 8;                              // k groups
     static constexpr int PQ = 4 / KG;                              // 64-K quarters per warp and stage
     static constexpr int THREADS = 32 * (CW + 1);
-    static constexpr int WBYTES = MATS * kKT * 8 * kTileBytes3;   // trellis per stage
+    static constexpr int WBYTES = MATS * kKT * 8 * kTileBytes<BITS>;  // trellis per stage
     static constexpr int TOKROWS = GATEUP ? 2 * N : N;            // gate/up: two rotated versions
     static constexpr int TOK = TOKROWS * 512;                      // 256 K fp16
     static constexpr int STAGE = ((WBYTES + TOK) + 1023) / 1024 * 1024;
@@ -189,9 +191,24 @@ __device__ __forceinline__ void decode_pairs(const uint32_t (&w)[4], uint32_t k6
     if constexpr (P < 7) decode_pairs<P + 1>(w, k65536, kxor, a, b);
 }
 
-template <bool GATEUP, int NT, int CW>
+// 4 bpw (the reference's format): one output column c of a tile -> 8 fp16 pairs
+// (k = 2p, 2p + 1).  The column's 16 windows come from four 32-bit values v_j
+// (exl3_col4_pairs); rows 2j + (9, 8, 1, 0)[t] take bits [4t, 4t + 16) of v_j, so pair p
+// (rows 2p, 2p + 1) is v_{p & 3} at shifts (12, 8) for p < 4 and (4, 0) otherwise.
+__device__ __forceinline__ void decode_col4(const uint32_t *t32, int c, uint32_t kxor, uint32_t *out) {
+    uint32_t v[4];
+    exl3_col4_pairs(t32, c, v);
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const uint32_t vj = v[p & 3];
+        const int slo = p < 4 ? 12 : 4, shi = p < 4 ? 8 : 0;
+        out[p] = mcg_pair((vj >> slo) & 0xFFFFu, (vj >> shi) & 0xFFFFu, kxor);
+    }
+}
+
+template <bool GATEUP, int NT, int CW, int BITS>
 __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __grid_constant__ XParams p) {
-    using C = XCfg<GATEUP, NT, CW>;
+    using C = XCfg<GATEUP, NT, CW, BITS>;
     constexpr int SW = C::SW, N = C::N, MATS = C::MATS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -232,7 +249,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __gri
                     uint8_t *st = smem + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], C::WBYTES + C::TOK);
                     tma_load_4d(st, ma, &full[s], 0, kr * kKT, nb0, z);
-                    if (GATEUP) tma_load_4d(st + kKT * 8 * kTileBytes3, mb, &full[s], 0, kr * kKT, nb0, z);
+                    if (GATEUP) tma_load_4d(st + kKT * 8 * kTileBytes<BITS>, mb, &full[s], 0, kr * kKT, nb0, z);
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         tma_load_2d(st + C::WBYTES + q * (C::TOKROWS * 128), &p.xt, &full[s], kr * 256 + 64 * q,
@@ -278,10 +295,15 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __gri
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) {
                     const uint32_t *tile = reinterpret_cast<const uint32_t *>(
-                        st + m * (kKT * 8 * kTileBytes3) + (wl * kKT + kt) * kTileBytes3);
-                    const uint32_t w[4] = {tile[wo0], tile[wo0 + 1], tile[wo0 + 2], tile[wo3]};
+                        st + m * (kKT * 8 * kTileBytes<BITS>) + (wl * kKT + kt) * kTileBytes<BITS>);
                     uint32_t wa[8], wb[8];
-                    decode_pairs<0>(w, k65536, kxor, wa, wb);
+                    if constexpr (BITS == 3) {
+                        const uint32_t w[4] = {tile[wo0], tile[wo0 + 1], tile[wo0 + 2], tile[wo3]};
+                        decode_pairs<0>(w, k65536, kxor, wa, wb);
+                    } else {
+                        decode_col4(tile, 2 * g, kxor, wa);
+                        decode_col4(tile, 2 * g + 1, kxor, wb);
+                    }
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < ntv) {
@@ -382,15 +404,15 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __gri
 constexpr int kXtThreads = 640;
 constexpr int kXtDq = 16;
 constexpr int kXtSA = 4;                           // TMEM A ring slots (64 K each)
-constexpr int kXtRawMat = kKT * 8 * kTileBytes3;  // 12 KB: one matrix, one 256-K stage
 constexpr int kXchLd = 9;                          // exchange row stride (floats), 8 columns + pad
 
-template <bool GATEUP, int N>
+template <bool GATEUP, int N, int BITS>
 struct XtCfg {
     static constexpr int MATS = GATEUP ? 2 : 1;
+    static constexpr int RAW_MAT = kKT * 8 * kTileBytes<BITS>;  // one matrix, one 256-K stage (12 / 16 KB)
     static constexpr int TOK_BOX = N * 128;                 // N rows x 64 K fp16
     static constexpr int TOK_STAGE = MATS * TOK_BOX;        // gate/up: both rotations
-    static constexpr int RAW_STAGE = MATS * kXtRawMat;
+    static constexpr int RAW_STAGE = MATS * RAW_MAT;
     static constexpr int XCH = 4 * 128 * kXchLd * 4;        // one [128][9] buffer per epilogue group
     static constexpr int BUDGET = 232448 - 1024 - 256 - XCH;
     static constexpr int SB = kXtSA;  // token stages = TMEM A slots: one full/empty barrier pair per slot
@@ -467,9 +489,9 @@ __device__ __forceinline__ void fwht128_lanes(float (&v)[8], float *xb, int q, i
     }
 }
 
-template <bool GATEUP, int N>
+template <bool GATEUP, int N, int BITS>
 __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __grid_constant__ XParams p) {
-    using C = XtCfg<GATEUP, N>;
+    using C = XtCfg<GATEUP, N, BITS>;
     constexpr int MATS = C::MATS, SW = C::SW, SB = C::SB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -534,8 +556,8 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                 for (int kr = 0; kr < KR && ok; ++kr) {
                     const uint32_t rs = nraw % SW;
                     if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
-                    mbar_arrive_expect_tx(&raw_full[rs], kXtRawMat);
-                    tma_load_4d(raw + rs * C::RAW_STAGE + mat * kXtRawMat, mp, &raw_full[rs], 0, kr * kKT, nb0, z);
+                    mbar_arrive_expect_tx(&raw_full[rs], C::RAW_MAT);
+                    tma_load_4d(raw + rs * C::RAW_STAGE + mat * C::RAW_MAT, mp, &raw_full[rs], 0, kr * kKT, nb0, z);
                     ++nraw;
                 }
             }
@@ -633,11 +655,16 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                         }
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
-                            const uint8_t *stg = raw + rs * C::RAW_STAGE + m * kXtRawMat;
+                            const uint8_t *stg = raw + rs * C::RAW_STAGE + m * C::RAW_MAT;
                             uint32_t v[32];
 #pragma unroll
-                            for (int kt = 0; kt < 4; ++kt)
-                                trellis_column(stg + (nb * kKT + 4 * s + kt) * kTileBytes3, c, kxor, v + 8 * kt);
+                            for (int kt = 0; kt < 4; ++kt) {
+                                const uint8_t *tl = stg + (nb * kKT + 4 * s + kt) * kTileBytes<BITS>;
+                                if constexpr (BITS == 3)
+                                    trellis_column(tl, c, kxor, v + 8 * kt);
+                                else
+                                    decode_col4(reinterpret_cast<const uint32_t *>(tl), c, kxor, v + 8 * kt);
+                            }
                             tmem_st_32x32b_x32(tmem + lane_base + C::A_COL0 + (as * MATS + m) * 32, v);
                         }
                         tmem_wait_st();
@@ -744,17 +771,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 x_encode() {
 // Trellis stack [experts][K/16][N/16][48 u16] as u32 elements, viewed as 4D
 // {24 words, K/16 k-tiles, N/16 column blocks, experts} so that a box of 16 k-tiles x
 // 8 column blocks lands in shared memory as [column block][k-tile][96 B].
-static int make_trellis_map(CUtensorMap *m, const void *base, int64_t K, int64_t N, int64_t experts, int64_t stride) {
+static int make_trellis_map(CUtensorMap *m, const void *base, int64_t K, int64_t N, int64_t experts, int64_t stride,
+                            int bits) {
     auto enc = x_encode();
     if (!enc) {
         set_error("cuTensorMapEncodeTiled unavailable from the driver");
         return VFMOE_ERR_CUDA;
     }
-    const int64_t row_u32 = (N / 16) * 24;
+    const int64_t tile_u32 = 8 * bits;  // 24 (3 bpw) or 32 (4 bpw) words of 32 bits
+    const int64_t row_u32 = (N / 16) * tile_u32;
     if (experts <= 1) stride = (K / 16) * row_u32 * 4;
-    cuuint64_t dims[4] = {24, (cuuint64_t)(K / 16), (cuuint64_t)(N / 16), (cuuint64_t)experts};
-    cuuint64_t strides[3] = {(cuuint64_t)(row_u32 * 4), (cuuint64_t)kTileBytes3, (cuuint64_t)stride};
-    cuuint32_t box[4] = {24, (cuuint32_t)kKT, 8, 1};
+    cuuint64_t dims[4] = {(cuuint64_t)tile_u32, (cuuint64_t)(K / 16), (cuuint64_t)(N / 16), (cuuint64_t)experts};
+    cuuint64_t strides[3] = {(cuuint64_t)(row_u32 * 4), (cuuint64_t)(tile_u32 * 4), (cuuint64_t)stride};
+    cuuint32_t box[4] = {(cuuint32_t)tile_u32, (cuuint32_t)kKT, 8, 1};
     cuuint32_t es[4] = {1, 1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void *>(base), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -810,49 +839,61 @@ static int make_rot_map(CUtensorMap *m, const void *base, int64_t rows, int64_t 
 
 int exl3_plan_create(const vfmoe_layer_desc &d, Exl3Plan &plan) {
     plan.ready = 0;
-    if (d.weight_format != VFMOE_WFMT_EXL3 || d.exl3_bits != 3) return VFMOE_OK;
+    if (d.weight_format != VFMOE_WFMT_EXL3 || (d.exl3_bits != 3 && d.exl3_bits != 4)) return VFMOE_OK;
+    plan.bits = (int)d.exl3_bits;
+    const int b = plan.bits;
     int dev = 0;
     VF_CUDA(cudaGetDevice(&dev));
     VF_CUDA(cudaDeviceGetAttribute(&plan.num_sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t H = d.hidden, I = d.inter, E = d.n_local_experts ? d.n_local_experts : d.n_experts;
     int rc;
-    if ((rc = make_trellis_map(&plan.gate, (void *)d.gate.data, H, I, E, d.gate.expert_stride))) return rc;
-    if ((rc = make_trellis_map(&plan.up, (void *)d.up.data, H, I, E, d.up.expert_stride))) return rc;
-    if ((rc = make_trellis_map(&plan.down, (void *)d.down.data, I, H, E, d.down.expert_stride))) return rc;
+    if ((rc = make_trellis_map(&plan.gate, (void *)d.gate.data, H, I, E, d.gate.expert_stride, b))) return rc;
+    if ((rc = make_trellis_map(&plan.up, (void *)d.up.data, H, I, E, d.up.expert_stride, b))) return rc;
+    if ((rc = make_trellis_map(&plan.down, (void *)d.down.data, I, H, E, d.down.expert_stride, b))) return rc;
     const bool sh = d.sh_gate.data != 0;
-    if ((rc = make_trellis_map(&plan.sh_gate, (void *)(sh ? d.sh_gate.data : d.gate.data), H, I, 1, 0))) return rc;
-    if ((rc = make_trellis_map(&plan.sh_up, (void *)(sh ? d.sh_up.data : d.up.data), H, I, 1, 0))) return rc;
-    if ((rc = make_trellis_map(&plan.sh_down, (void *)(sh ? d.sh_down.data : d.down.data), I, H, 1, 0))) return rc;
+    if ((rc = make_trellis_map(&plan.sh_gate, (void *)(sh ? d.sh_gate.data : d.gate.data), H, I, 1, 0, b))) return rc;
+    if ((rc = make_trellis_map(&plan.sh_up, (void *)(sh ? d.sh_up.data : d.up.data), H, I, 1, 0, b))) return rc;
+    if ((rc = make_trellis_map(&plan.sh_down, (void *)(sh ? d.sh_down.data : d.down.data), I, H, 1, 0, b))) return rc;
     plan.ready = 1;
     return VFMOE_OK;
 }
 
-template <bool GATEUP, int NT, int CW>
-static int launch_x(const XParams &prm, int grid, cudaStream_t st) {
-    using C = XCfg<GATEUP, NT, CW>;
+template <bool GATEUP, int NT, int CW, int BITS>
+static int launch_x1(const XParams &prm, int grid, cudaStream_t st) {
+    using C = XCfg<GATEUP, NT, CW, BITS>;
     static bool attr_done = false;
     if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemv_exl3<GATEUP, NT, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        VF_CUDA(cudaFuncSetAttribute(expert_gemv_exl3<GATEUP, NT, CW, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM));
         attr_done = true;
     }
-    expert_gemv_exl3<GATEUP, NT, CW><<<grid, C::THREADS, C::SMEM, st>>>(prm);
+    expert_gemv_exl3<GATEUP, NT, CW, BITS><<<grid, C::THREADS, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_exl3<gate_up>" : "expert_gemv_exl3<down>");
     return VFMOE_OK;
 }
 
-template <bool GATEUP, int N>
-static int launch_xt(const XParams &prm, int grid, cudaStream_t st) {
-    using C = XtCfg<GATEUP, N>;
+template <bool GATEUP, int NT, int CW>
+static int launch_x(const XParams &prm, int bits, int grid, cudaStream_t st) {
+    return bits == 4 ? launch_x1<GATEUP, NT, CW, 4>(prm, grid, st) : launch_x1<GATEUP, NT, CW, 3>(prm, grid, st);
+}
+
+template <bool GATEUP, int N, int BITS>
+static int launch_xt1(const XParams &prm, int grid, cudaStream_t st) {
+    using C = XtCfg<GATEUP, N, BITS>;
     static bool attr_done = false;
     if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemm_exl3_tc<GATEUP, N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        VF_CUDA(cudaFuncSetAttribute(expert_gemm_exl3_tc<GATEUP, N, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM));
         attr_done = true;
     }
-    expert_gemm_exl3_tc<GATEUP, N><<<grid, kXtThreads, C::SMEM, st>>>(prm);
+    expert_gemm_exl3_tc<GATEUP, N, BITS><<<grid, kXtThreads, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_exl3_tc<gate_up>" : "expert_gemm_exl3_tc<down>");
     return VFMOE_OK;
+}
+
+template <bool GATEUP, int N>
+static int launch_xt(const XParams &prm, int bits, int grid, cudaStream_t st) {
+    return bits == 4 ? launch_xt1<GATEUP, N, 4>(prm, grid, st) : launch_xt1<GATEUP, N, 3>(prm, grid, st);
 }
 
 // Prefill (more than 16 rows per expert on average): gather + tile plan + tcgen05 GEMMs with
@@ -883,7 +924,7 @@ static int launch_exl3_tc(const Exl3Plan &plan, const MoeArgs &a, cudaStream_t s
     g.err = a.err;
     g.kxor = 0x3B603B60u;
     const int grid = plan.num_sms;
-    if ((rc = launch_xt<true, 128>(g, grid, st))) return rc;
+    if ((rc = launch_xt<true, 128>(g, plan.bits, grid, st))) return rc;
     mid();
     XParams dn{};
     dn.wa = plan.down;
@@ -905,7 +946,7 @@ static int launch_exl3_tc(const Exl3Plan &plan, const MoeArgs &a, cudaStream_t s
     dn.limit = a.limit;
     dn.err = a.err;
     dn.kxor = 0x3B603B60u;
-    return launch_xt<false, 256>(dn, grid, st);
+    return launch_xt<false, 256>(dn, plan.bits, grid, st);
 }
 
 int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, int x_dtype,
@@ -948,9 +989,9 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
     g.kxor = 0x3B603B60u;
     const int grid = plan.num_sms;
     switch (N) {
-        case 8: rc = launch_x<true, 1, 16>(g, grid, st); break;
-        case 16: rc = launch_x<true, 2, 16>(g, grid, st); break;
-        default: rc = launch_x<true, 4, 8>(g, grid, st); break;
+        case 8: rc = launch_x<true, 1, 16>(g, plan.bits, grid, st); break;
+        case 16: rc = launch_x<true, 2, 16>(g, plan.bits, grid, st); break;
+        default: rc = launch_x<true, 4, 8>(g, plan.bits, grid, st); break;
     }
     if (rc) return rc;
     mid();
@@ -976,9 +1017,9 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
     dn.k65536 = 65536u;
     dn.kxor = 0x3B603B60u;
     switch (N) {
-        case 8: return launch_x<false, 1, 16>(dn, grid, st);
-        case 16: return launch_x<false, 2, 16>(dn, grid, st);
-        default: return launch_x<false, 4, 16>(dn, grid, st);
+        case 8: return launch_x<false, 1, 16>(dn, plan.bits, grid, st);
+        case 16: return launch_x<false, 2, 16>(dn, plan.bits, grid, st);
+        default: return launch_x<false, 4, 16>(dn, plan.bits, grid, st);
     }
 }
 

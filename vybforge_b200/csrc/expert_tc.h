@@ -47,6 +47,7 @@ int launch_tc_plan(const MoeArgs &a, int n_gu, int n_dn, cudaStream_t st);
 struct Exl3Plan {
     int ready = 0;
     int num_sms = 0;
+    int bits = 3;  // 3 (this library's layout) or 4 (the reference's)
     CUtensorMap gate, up, down;
     CUtensorMap sh_gate, sh_up, sh_down;
 };

@@ -89,6 +89,16 @@ __global__ void exl3_decode_kernel(const uint16_t *__restrict__ trellis, __half 
             const uint32_t w16 = (uint32_t)(v >> (3 * r)) & 0xFFFFu;
             dst[(kb * 16 + r) * N + nb * 16 + c] = exl3_mcg(w16);
         }
+    } else {
+        uint32_t v[4];
+        exl3_col4_pairs(reinterpret_cast<const uint32_t *>(tp), c, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int rows[4] = {9, 8, 1, 0};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                dst[(kb * 16 + 2 * j + rows[t]) * N + nb * 16 + c] = exl3_mcg((v[j] >> (4 * t)) & 0xFFFFu);
+        }
     }
 }
 
