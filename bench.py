@@ -228,8 +228,9 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- workload
 def algorithmic_bytes(cfg, n_distinct_experts, has_shared=True):
     H, I, E, T = cfg.hidden, cfg.inter, cfg.n_experts, cfg.tokens
-    per_expert = 3 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 3 * (H * I * 3 // 8 + 2 * (H + I))
-    gate_up = 2 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 2 * (H * I * 3 // 8 + 2 * (H + I))
+    bits = getattr(cfg, "exl3_bits", 3)
+    per_expert = 3 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 3 * (H * I * bits // 8 + 2 * (H + I))
+    gate_up = 2 * H * I * 34 // 32 if cfg.fmt == "q8_0" else 2 * (H * I * bits // 8 + 2 * (H + I))
     layer = (n_distinct_experts + (1 if has_shared else 0)) * per_expert + E * H * 4 + T * H * 4
     gu = (n_distinct_experts + (1 if has_shared else 0)) * gate_up
     return layer, gu
@@ -521,6 +522,24 @@ def exl3_extra(a, flush):
                               "stage_ms_per_step": {n: round(v, 4) for n, v in st_.items()},
                               "note": "tcgen05 EXL3 GEMMs (trellis decoded into TMEM, Hadamard epilogues); "
                                       "bound by the trellis decode's integer work"}
+    layer.close()
+    # the reference's own EXL3 format (4 bpw, its slot table in closed form) at C2 shapes, T=32
+    del mats, dev
+    torch.cuda.empty_cache()
+    c4 = synth.config("c2", tokens=32)
+    c4.exl3_bits = 4
+    dev4 = synth.expert_exl3_cuda(c4)
+    mats = dict(gate=tuple(t[:E] for t in dev4[0]), up=tuple(t[:E] for t in dev4[1]),
+                down=tuple(t[:E] for t in dev4[2]), shared=tuple(tuple(t[E] for t in dev4[p]) for p in range(3)),
+                fmt="exl3", exl3_bits=4)
+    layer = make(w_r, bias)
+    ms, st_, _, idx = time_layer(layer, xd[:32].contiguous(), a.steps, a.warmup, flush)
+    lb, gub = algorithmic_bytes(c4, len(np.unique(idx.cpu().numpy())))
+    out["c2_4bpw_t32"] = {"tokens_per_s": round(32 / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                          "gate_up_hbm_frac": round(gub / (st_["gate_up"] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                          "layer_hbm_frac": round(lb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                          "stage_ms_per_step": {n: round(v, 4) for n, v in st_.items()},
+                          "note": "EXL3 4 bpw (the reference's format), C2 shapes"}
     layer.close()
     return out
 
