@@ -63,6 +63,9 @@ def args_parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the extra T=1 and prefill measurements")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--q8-layout", default="tiled", choices=["tiled", "rows"],
+                    help="Q8_0 weights in HBM: stage-tiled (converted once at load, outside the timed "
+                         "region) or GGUF row order")
     ap.add_argument("--profile-case", default=None, choices=list(PROFILE_CASES),
                     help="run one small fixed case for an ncu capture (no JSON line) and exit")
     return ap.parse_args()
@@ -70,6 +73,15 @@ def args_parse():
 
 # dram bytes / algorithmic bytes of the Q8_0 gate/up GEMV, from its ncu capture
 GEMV_Q8_TRAFFIC_RATIO = 1.015
+
+def q8_layout_weights(layout, dev):
+    """A layer's Q8_0 weights in the bench's layout: stage-tiled by default (VFMOE_WFMT_Q8_0_TILED,
+    one vfmoe_q8_0_tile pass at load, outside every timed region) or GGUF row order."""
+    if layout == "rows":
+        return dev, "q8_0"
+    from vybforge_b200.moe import q8_0_tile
+    return {p: q8_0_tile(dev[p]) for p in range(3)}, "q8_0_tiled"
+
 
 # ----------------------------------------------------------------------------- ncu cases
 def _profile_decode(fmt):
@@ -84,8 +96,9 @@ def _profile_decode(fmt):
     x, w_r, bias, _ = synth.router_inputs(cfg)
     E = cfg.n_experts
     if fmt == "q8_0":
-        dev = synth.expert_q8_cuda(cfg, quantizer)
-        mats = dict(gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]))
+        dev, wf = q8_layout_weights("tiled", synth.expert_q8_cuda(cfg, quantizer))
+        mats = dict(gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
+                    fmt=wf)
     else:
         dev = synth.expert_exl3_cuda(cfg)
         mats = dict(gate=tuple(a[:E] for a in dev[0]), up=tuple(a[:E] for a in dev[1]),
@@ -112,11 +125,11 @@ def _profile_prefill():
     cfg.n_experts = 64
     x, w_r, bias, _, _ = synth.zipf_router_inputs(cfg)
     E = cfg.n_experts
-    dev = synth.expert_q8_cuda(cfg, quantizer)
+    dev, wf = q8_layout_weights("tiled", synth.expert_q8_cuda(cfg, quantizer))
     layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                      router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
                      gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
-                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16, fmt=wf)
     xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
     for _ in range(3):
         layer.forward(xd)
@@ -236,19 +249,22 @@ def algorithmic_bytes(cfg, n_distinct_experts, has_shared=True):
     return layer, gu
 
 
-def build_ours(cfg, rank):
+def build_ours(cfg, rank, layout):
+    """The layer on GPU weights in `layout`; also returns the GGUF-row weights (for the CPU
+    baseline) and the layer's own weights."""
     import torch
     from vybforge_b200 import synth
     from vybforge_b200.moe import MoELayer, quantizer
     x, w_r, bias, rng = synth.router_inputs(cfg)
     dev = synth.expert_q8_cuda(cfg, quantizer)
+    devl, wf = q8_layout_weights(layout, dev)
     E = cfg.n_experts
     xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
     layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
-                     router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
-                     gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
+                     router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(), fmt=wf,
+                     gate=devl[0][:E], up=devl[1][:E], down=devl[2][:E], shared=(devl[0][E], devl[1][E], devl[2][E]),
                      x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
-    return layer, xd, (x, w_r, bias), dev
+    return layer, xd, (x, w_r, bias), dev, (devl, wf)
 
 
 def cpu_baseline_ours(cfg, host, dev, idx, budget_s):
@@ -309,7 +325,7 @@ def time_layer(layer, xd, steps, warmup, flush, with_profile=True):
     return ms, {n: stage[i] / nf for i, n in enumerate(names)}, int(launches.value), idx
 
 
-def prefill_extra(a, cfg1, dev, flush):
+def prefill_extra(a, cfg1, dev, wf, flush):
     """C3: T=4096 prefill, Zipf(1.1)-skewed routing, same Q8_0 expert weights as C1."""
     import torch
     from vybforge_b200 import synth
@@ -320,7 +336,7 @@ def prefill_extra(a, cfg1, dev, flush):
     layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                      router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
                      gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
-                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+                     x_dtype=torch.bfloat16, out_dtype=torch.bfloat16, fmt=wf)
     xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
     ms, stages, launches, idx = time_layer(layer, xd, max(5, a.steps // 2), a.warmup, flush)
     T, H, I, k = cfg.tokens, cfg.hidden, cfg.inter, cfg.topk
@@ -367,13 +383,14 @@ def stack_extra(a, rank, world, local_rank, flush):
     layers = {"p": [], "d": []}
     for l in range(L):
         mine = [int(e) for e in np.nonzero(placements[l] == rank)[0]] + [E]
-        dev = synth.expert_q8_cuda(cfgp, quantizer, layer=l, experts=mine)
+        dev, wf = q8_layout_weights(a.q8_layout, synth.expert_q8_cuda(cfgp, quantizer, layer=l, experts=mine))
+        torch.cuda.empty_cache()
         for key, routers in (("p", routers_p), ("d", routers_d)):
             w_r, bias, _ = routers[l]
             lay = MoELayer(hidden=H, inter=I, n_experts=E, topk=k, router_w=torch.from_numpy(w_r).cuda(),
                            router_bias=torch.from_numpy(bias).cuda(), gate=dev[0][:-1], up=dev[1][:-1],
                            down=dev[2][:-1], shared=(dev[0][-1], dev[1][-1], dev[2][-1]),
-                           n_local_experts=E // world if world > 1 else 0,
+                           n_local_experts=E // world if world > 1 else 0, fmt=wf,
                            x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
             layers[key].append(lay)
     t_setup = time.perf_counter() - t_setup
@@ -560,10 +577,10 @@ def run_ours_ep(a, rank, world, local_rank):
     E, H = cfg.n_experts, cfg.hidden
     placement = ep.contiguous_placement(E, world)
     mine = [int(e) for e in np.nonzero(placement == rank)[0]] + [E]
-    dev = synth.expert_q8_cuda(cfg, quantizer, experts=mine)
+    dev, wf = q8_layout_weights(a.q8_layout, synth.expert_q8_cuda(cfg, quantizer, experts=mine))
     layer = MoELayer(hidden=H, inter=cfg.inter, n_experts=E, topk=cfg.topk, router_w=torch.from_numpy(w_r).cuda(),
                      router_bias=torch.from_numpy(bias).cuda(), gate=dev[0][:-1], up=dev[1][:-1], down=dev[2][:-1],
-                     shared=(dev[0][-1], dev[1][-1], dev[2][-1]), n_local_experts=E // world,
+                     shared=(dev[0][-1], dev[1][-1], dev[2][-1]), n_local_experts=E // world, fmt=wf,
                      x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
     rs = ep.EpRank(rank, world, ep.GpuBackend(layer, placement, world, out_dtype=torch.bfloat16))
     tr = ep.DistTransport()
@@ -629,7 +646,7 @@ def run_ours_ep(a, rank, world, local_rank):
            "config": {"workload": f"{a.workload}: decode T={T}/GPU, H={H}, I={cfg.inter}, E={E}, top-{cfg.topk} "
                                   f"+ 1 shared, Q8_0, expert-parallel {E // world} experts/GPU",
                       "tokens_per_gpu": T, "global_batch": T * world, "parallelism": f"ep{world} (NCCL all-to-all)",
-                      "distinct_experts": n_distinct,
+                      "distinct_experts": n_distinct, "q8_layout": wf,
                       "l2": "256 MiB memset between timed steps, outside the step events"},
            "gpu_launches": 12 * a.steps, "clocks": clk,
            "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (all ranks)",
@@ -654,7 +671,7 @@ def run_ours(a, rank, world, local_rank):
         cfg.n_experts = a.experts
     if cfg.fmt != "q8_0" or a.workload not in ("c1", "c4d"):
         raise SystemExit(f"workload {a.workload}/{cfg.fmt} not wired into bench yet")
-    layer, xd, host, dev = build_ours(cfg, rank)
+    layer, xd, host, dev, (devl, wf) = build_ours(cfg, rank, a.q8_layout)
     T = cfg.tokens
     st = torch.cuda.current_stream()
     out = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device="cuda")
@@ -739,7 +756,7 @@ def run_ours(a, rank, world, local_rank):
                                   f"E={cfg.n_experts}, top-{cfg.topk} + 1 shared, Q8_0",
                       "tokens_per_gpu": T, "global_batch": T * world, "parallelism":
                           "replicas" if world > 1 else "single",
-                      "distinct_experts": n_distinct,
+                      "distinct_experts": n_distinct, "q8_layout": wf,
                       "l2": "256 MiB memset between timed steps, outside the step events"},
            "gpu_launches": int(launches.value), "clocks": clk, "roofline": roof,
            "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
@@ -753,12 +770,12 @@ def run_ours(a, rank, world, local_rank):
                           "gate_up_hbm_frac": round(gu1b / (st1["gate_up"] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                           "layer_hbm_frac": round(l1b / (ms1 * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                           "stage_ms_per_step": {n: round(v, 4) for n, v in st1.items()}}
-        extra["c3_prefill_q8_0"] = prefill_extra(a, cfg, dev, flush)
+        extra["c3_prefill_q8_0"] = prefill_extra(a, cfg, devl, wf, flush)
         res["extra"] = extra
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_ours(cfg, host, dev, idx_np, a.cpu_budget_s)
     if "extra" in res:
-        del dev
+        del dev, devl
         layer.close()
         torch.cuda.empty_cache()
         res["extra"].update(stack_extra(a, rank, world, local_rank, flush))

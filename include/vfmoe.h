@@ -62,6 +62,13 @@ extern "C" {
 /* expert weight formats */
 #define VFMOE_WFMT_Q8_0 1
 #define VFMOE_WFMT_EXL3 2
+/* Q8_0 blocks of the same matrices in stage-tiled order (no counterpart in the reference,
+ * which reads GGUF rows; made from GGUF rows by vfmoe_q8_0_tile at load time): a matrix
+ * [rows][K] is tiles of 64 rows x 256 K, 64 x 272 B each (every tile row = that row's 8
+ * GGUF blocks), tile (rt, kr) at byte ((rt * K/256) + kr) * 17408.  Same size, expert
+ * strides and values as GGUF rows; the expert kernels stream one tile as one contiguous
+ * copy.  Not accepted by the SIMT path (VFMOE_DISABLE_TC). */
+#define VFMOE_WFMT_Q8_0_TILED 3
 
 /* One projection (gate, up or down) of a stack of experts.  Expert e's data
  * starts at data + e * expert_stride (bytes); for EXL3 its suh/svh start at
@@ -246,6 +253,12 @@ int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k,
 /* fp32 [rows, k] -> Q8_0 rows (ggml quantize_row_q8_0_ref rule; the reference
  * has no quantizer, it reads GGUF bytes). */
 int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, int64_t stream);
+
+/* n_mats Q8_0 matrices [rows][k] in GGUF row order, back to back, -> the same matrices in
+ * VFMOE_WFMT_Q8_0_TILED order at dst (same total size; dst must not overlap src).
+ * rows % 64 == 0, k % 256 == 0, both pointers 16-byte aligned.  No counterpart in the
+ * reference (a load-time layout step; its kernels read GGUF rows in place). */
+int vfmoe_q8_0_tile(int64_t src, int64_t dst, int64_t rows, int64_t k, int64_t n_mats, int64_t stream);
 
 /* EXL3 trellis -> rotated-basis values W^ as fp16 [K, N] (no Hadamard).
  * Replaces exl3deq / exl3deq32 (native/kernels/exl3.vyb:207-242,375-422).

@@ -205,6 +205,29 @@ def q8_0_expert_inout(raw_rows_out, n_out, k_in):
     return dequant_q8_0(raw_rows_out, n_out, k_in).T
 
 
+def q8_0_tile(raw):
+    """GGUF Q8_0 rows -> the stage-tiled byte order (VFMOE_WFMT_Q8_0_TILED, this library's
+    load-time layout; the reference has no counterpart and reads the rows in place).
+
+    raw: uint8 [..., rows, k/32*34], rows % 64 == 0, k % 256 == 0.  Tiles of 64 rows x 256 K
+    (64 x 272 B, each tile row = that row's 8 blocks), tile (rt, kr) at ((rt * k/256) + kr)
+    * 17408.  Returns uint8 of raw's shape."""
+    raw = np.ascontiguousarray(raw)
+    rows, rb = raw.shape[-2], raw.shape[-1]
+    kr = rb // 272
+    t = raw.reshape(-1, rows // 64, 64, kr, 272).transpose(0, 1, 3, 2, 4)
+    return np.ascontiguousarray(t).reshape(raw.shape)
+
+
+def q8_0_untile(tiled):
+    """Inverse of q8_0_tile."""
+    tiled = np.ascontiguousarray(tiled)
+    rows, rb = tiled.shape[-2], tiled.shape[-1]
+    kr = rb // 272
+    t = tiled.reshape(-1, rows // 64, kr, 64, 272).transpose(0, 1, 3, 2, 4)
+    return np.ascontiguousarray(t).reshape(tiled.shape)
+
+
 # --------------------------------------------------------------------------- EXL3
 MCG_MUL = 0xCBAC1FED
 MCG_AND = 0x8FFF8FFF

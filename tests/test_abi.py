@@ -114,6 +114,12 @@ def test_standalone_ops_validate_arguments(built_lib):
     assert built_lib.vfmoe_q8_0_dequant(0, 0, 4, 33, 0, 0) == _lib.ERR_INVALID
     assert built_lib.vfmoe_q8_0_quantize(0, 0, 4, 30, 0) == _lib.ERR_INVALID
     assert built_lib.vfmoe_exl3_decode(0, 0, 15, 16, 3, 0) == _lib.ERR_INVALID
+    assert built_lib.vfmoe_q8_0_tile(4096, 1 << 30, 96, 512, 1, 0) == _lib.ERR_INVALID       # rows % 64
+    assert built_lib.vfmoe_q8_0_tile(4096, 1 << 30, 64, 288, 1, 0) == _lib.ERR_INVALID       # k % 256
+    assert built_lib.vfmoe_q8_0_tile(4104, 1 << 30, 64, 512, 1, 0) == _lib.ERR_INVALID       # misaligned
+    assert built_lib.vfmoe_q8_0_tile(4096, 4096 + 16, 64, 512, 1, 0) == _lib.ERR_INVALID     # overlap
+    assert "overlaps" in _lib.last_error()
+    assert built_lib.vfmoe_q8_0_tile(0, 0, 64, 512, 0, 0) == _lib.OK                          # nothing to do
     assert built_lib.vfmoe_rmsnorm(0, 0, 0, 2, 0, 1e-5, 0, 0) == _lib.ERR_INVALID
     assert built_lib.vfmoe_residual_rmsnorm(0, 0, 0, 0, 0, 2, 64, 1e-5, 2, 0) == _lib.ERR_INVALID       # no x
     assert built_lib.vfmoe_residual_rmsnorm(4096, 0, 0, 0, 0, 2, 64, 1e-5, 2, 0) == _lib.ERR_INVALID    # no y, no w

@@ -193,6 +193,40 @@ def test_rmsnorm(dtype):
     assert rel_l2(y, ref) < tol
 
 
+# ----------------------------------------------------------------------------- stage-tiled Q8_0 layout
+def test_q8_0_tile_matches_oracle():
+    moe.init(0)
+    rng = np.random.default_rng(5)
+    w = rng.integers(0, 256, (3, 128, 1024 // 32 * 34), dtype=np.uint8)
+    got = moe.q8_0_tile(torch.from_numpy(w).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, orc.q8_0_tile(w))
+
+
+@pytest.fixture(scope="module")
+def c1_tiled(c1):
+    E = c1.cfg.n_experts
+    g, u, d = (moe.q8_0_tile(c1.dev[p]) for p in range(3))
+    layer = moe.MoELayer(hidden=c1.cfg.hidden, inter=c1.cfg.inter, n_experts=E, topk=c1.cfg.topk,
+                         router_w=c1.wr_dev, router_bias=c1.bias_dev, gate=g[:E], up=u[:E], down=d[:E],
+                         shared=(g[E], u[E], d[E]), fmt="q8_0_tiled", x_dtype=torch.bfloat16,
+                         out_dtype=torch.float32)
+    yield layer
+    layer.close()
+
+
+@pytest.mark.parametrize("T", [1, 8, 32, 1024, 4096])
+def test_tiled_weights_give_identical_output(c1, c1_tiled, T):
+    """Same kernels, same arithmetic: only the byte order of the weights in HBM differs
+    (decode GEMV at T <= 32, tcgen05 grouped GEMM above)."""
+    g = torch.Generator(device="cuda").manual_seed(T)
+    x = torch.randn((T, c1.cfg.hidden), generator=g, device="cuda").to(torch.bfloat16)
+    ref = c1.layer.forward(x)
+    got = c1_tiled.forward(x)
+    torch.cuda.synchronize()
+    c1_tiled.check_device_error()
+    assert torch.equal(ref, got)
+
+
 # ----------------------------------------------------------------------------- tcgen05 path vs SIMT path
 def _simt_layer(built, out_dtype=torch.float32):
     os.environ["VFMOE_DISABLE_TC"] = "1"

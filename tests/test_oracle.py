@@ -85,6 +85,19 @@ def test_q8_0_decode_matches_reference_kat():
     np.testing.assert_array_equal(ours, deq)
 
 
+def test_q8_0_tiled_layout_is_a_permutation_of_gguf_rows():
+    rng = np.random.default_rng(4)
+    raw = rng.integers(0, 256, (2, 128, 512 // 32 * 34), dtype=np.uint8)
+    t = orc.q8_0_tile(raw)
+    assert t.shape == raw.shape
+    np.testing.assert_array_equal(orc.q8_0_untile(t), raw)
+    flat = t.reshape(2, -1)
+    KR = 2
+    for m, r, kr in [(0, 0, 0), (0, 63, 1), (1, 64, 0), (1, 127, 1), (0, 70, 1)]:
+        off = ((r // 64) * KR + kr) * 17408 + (r % 64) * 272
+        np.testing.assert_array_equal(flat[m, off:off + 272], raw[m, r, kr * 272:(kr + 1) * 272])
+
+
 def test_q8_0_quantizer_matches_gguf():
     gguf = pytest.importorskip("gguf")
     rng = np.random.default_rng(3)

@@ -27,7 +27,7 @@ ERR_NCCL = -8
 # dtype ids (native/dtype/dtype.vyb:26-28)
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # weight formats
-WFMT_Q8_0, WFMT_EXL3 = 1, 2
+WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED = 1, 2, 3
 
 
 class VfmoeError(RuntimeError):
@@ -76,6 +76,7 @@ _SIGS = {
     "vfmoe_residual_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_q8_0_dequant": (C.c_int, [I64] * 6),
     "vfmoe_q8_0_quantize": (C.c_int, [I64] * 5),
+    "vfmoe_q8_0_tile": (C.c_int, [I64] * 6),
     "vfmoe_exl3_decode": (C.c_int, [I64] * 6),
 }
 

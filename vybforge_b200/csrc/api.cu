@@ -173,7 +173,7 @@ static int validate(const vfmoe_layer_desc &d) {
     if (d.out_dtype != VFMOE_DT_BF16 && d.out_dtype != VFMOE_DT_F32) return bad("out_dtype must be BF16 or F32");
     if (!d.router_w || !d.router_bias) return bad("router weights missing");
     if (!aligned16(d.router_w)) return bad("router_w must be 16-byte aligned");
-    if (d.weight_format == VFMOE_WFMT_Q8_0) {
+    if (d.weight_format == VFMOE_WFMT_Q8_0 || d.weight_format == VFMOE_WFMT_Q8_0_TILED) {
         const int64_t rg = d.hidden / 32 * 34, rd = d.inter / 32 * 34;
         if (!d.gate.data || !d.up.data || !d.down.data) return bad("routed expert weights missing");
         const int64_t nl = d.n_local_experts ? d.n_local_experts : d.n_experts;
@@ -366,6 +366,9 @@ static int forward_experts(Layer &L, const MoeArgs &a, cudaStream_t st, const st
     if (L.use_tc && tc_supported(L.tc, a)) {
         rc = launch_experts_tc(L.tc, a, st, mid);
         nlaunch += 3;
+    } else if (a.fmt == VFMOE_WFMT_Q8_0_TILED) {
+        set_error("VFMOE_WFMT_Q8_0_TILED weights need the tensor-core expert path");
+        return VFMOE_ERR_UNSUPPORTED;
     } else {
         rc = launch_experts_simt(a, st, mid);
         nlaunch += 2;
@@ -758,6 +761,25 @@ int vfmoe_q8_0_quantize(int64_t src_f32, int64_t dst, int64_t rows, int64_t k, i
     }
     return launch_q8_0_quantize(reinterpret_cast<const float *>(src_f32), reinterpret_cast<uint8_t *>(dst), rows,
                                 k, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_q8_0_tile(int64_t src, int64_t dst, int64_t rows, int64_t k, int64_t n_mats, int64_t stream) {
+    if (rows < 0 || n_mats < 0 || k <= 0 || k % 256 || rows % 64) {
+        set_error("vfmoe_q8_0_tile: rows must be a multiple of 64 and k of 256");
+        return VFMOE_ERR_INVALID;
+    }
+    const int64_t bytes = rows * (k / 32 * 34) * n_mats;
+    if (bytes == 0) return VFMOE_OK;
+    if (!src || !dst || (src & 15) || (dst & 15)) {
+        set_error("vfmoe_q8_0_tile: src and dst must be non-null and 16-byte aligned");
+        return VFMOE_ERR_INVALID;
+    }
+    if (src < dst + bytes && dst < src + bytes) {
+        set_error("vfmoe_q8_0_tile: dst overlaps src");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_q8_0_tile(reinterpret_cast<const uint8_t *>(src), reinterpret_cast<uint8_t *>(dst), rows, k,
+                            n_mats, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vfmoe_exl3_decode(int64_t trellis, int64_t dst_f16, int64_t K, int64_t N, int64_t bits, int64_t stream) {

@@ -90,6 +90,14 @@ __device__ __forceinline__ float swiglu_clamped(float g, float u, float lim) {
     return (g / (1.0f + expf(-g))) * u;
 }
 
+// swiglu_clamped with the fast exponential and division intrinsics (a few ulp of fp32),
+// for epilogues whose result is rounded to fp16.
+__device__ __forceinline__ float swiglu_clamped_fast(float g, float u, float lim) {
+    g = fminf(g, lim);
+    u = fminf(fmaxf(u, -lim), lim);
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
 // EXL3 "mcg" codebook decode of one 16-bit window (native/exl3/exl3_ref.py:37-47):
 // prod = w * 0xCBAC1FED mod 2^32; y = (prod & 0x8FFF8FFF) ^ 0x3B603B60;
 // value = fp16(lo(y)) + fp16(hi(y)) in fp16 arithmetic.

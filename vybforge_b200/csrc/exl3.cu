@@ -629,6 +629,89 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
         const bool tok_issuer = q == 0;
         uint32_t nraw = 0, na = 0, it = 0, tok_issued = 0;
         bool ok = true;
+        // Epilogue of item `eitem` (the it-th of this CTA): 8-column chunks, chunk c0 handled by
+        // group c0/8 % 4 (4 warps = 128 lanes), read from TMEM in batches; the accumulators
+        // are released (d_empty) once the last batch is in registers, before its Hadamard
+        // transforms and stores, so the next item's MMAs do not wait for them.
+        auto epilogue = [&](int eitem, uint32_t eit) -> bool {
+            if (!mbar_wait(d_full, eit & 1, abort)) return false;
+            tc_fence_after();
+            const int4 t = p.tiles[eitem / MT];
+            const int e = t.x;
+            const bool sh = e == p.E;
+            const int ch = (eitem % MT) * 128 + r;
+            auto vec = [&](const __half *base, int64_t stride) {
+                return reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(base) +
+                                                        (sh ? 0 : (int64_t)e * stride));
+            };
+            const MatrixRef &m0 = sh ? p.sma : p.ma;
+            const float svh0 = kRScale * __half2float(vec(m0.svh, m0.svh_stride)[ch]);
+            float svh1 = 0.f, suhd = 0.f;
+            if (GATEUP) {
+                const MatrixRef &m1 = sh ? p.smb : p.mb;
+                const MatrixRef &md = sh ? p.smdown : p.mdown;
+                svh1 = kRScale * __half2float(vec(m1.svh, m1.svh_stride)[ch]);
+                suhd = __half2float(vec(md.suh, md.suh_stride)[ch]);
+            }
+            constexpr int NCH = (N + 31) / 32;                                     // chunks per group
+            constexpr int G = GATEUP ? 1 : (NCH < 4 ? NCH : 4);  // chunks per batch
+#pragma unroll
+            for (int b0 = 0; b0 < NCH; b0 += G) {
+                uint32_t dg[G][8];
+                uint32_t du[GATEUP ? G : 1][8];
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        tmem_ld_32x32b_x8(tmem + lane_base + c0, dg[i]);
+                        if constexpr (GATEUP) tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du[i]);
+                    }
+                }
+                tmem_wait_ld();
+                if (b0 + G >= NCH) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(d_empty);
+                }
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        float vg[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) vg[j] = __uint_as_float(dg[i][j]);
+                        if constexpr (GATEUP) {
+                            float vu[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) vu[j] = __uint_as_float(du[i][j]);
+                            fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                            fwht128_lanes(vu, xb, q, lane, 1 + grp);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                vg[j] = swiglu_clamped(vg[j] * svh0, vu[j] * svh1, p.limit) * suhd;
+                            fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                            __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (c0 + j < t.z)
+                                    out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(vg[j] * kRScale);
+                        } else {
+                            fwht128_lanes(vg, xb, q, lane, 1 + grp);
+                            float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = vg[j] * svh0;
+                        }
+                    }
+                }
+            }
+            return true;
+        };
+        // Item i's epilogue runs after this warp's share of item i+1's first raw stage (whose
+        // TMEM slots and token stages item i's last MMAs freed): the next item's first
+        // sub-stages are decoded and their token rows in flight while item i's accumulators
+        // drain.  Deferring further would deadlock (item i+1's second raw stage needs slots
+        // that only item i+1's MMAs free, and those wait for d_empty).
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
             const int4 tt = p.tiles[item / MT];
             const int t_y = tt.y, n16t = (tt.z + 15) >> 4;
@@ -678,66 +761,11 @@ __global__ void __launch_bounds__(kXtThreads, 1) expert_gemm_exl3_tc(const __gri
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
                 ++nraw;
+                if (kr == 0 && it > 0 && !(ok = epilogue(item - gridDim.x, it - 1))) break;
             }
-            if (!ok) break;
-            // epilogue: 8-column chunks, chunk c0 handled by group c0/8 % 4 (4 warps = 128 lanes)
-            if (!(ok = mbar_wait(d_full, it & 1, abort))) break;
-            tc_fence_after();
-            const int4 t = p.tiles[item / MT];
-            const int e = t.x;
-            const bool sh = e == p.E;
-            const int ch = (item % MT) * 128 + r;
-            auto vec = [&](const MatrixRef &mr, const __half *base, int64_t stride) {
-                return reinterpret_cast<const __half *>(reinterpret_cast<const uint8_t *>(base) + (sh ? 0 : (int64_t)e * stride));
-            };
-            const MatrixRef &m0 = sh ? p.sma : p.ma;
-            const float svh0 = kRScale * __half2float(vec(m0, m0.svh, m0.svh_stride)[ch]);
-            float svh1 = 0.f, suhd = 0.f;
-            if (GATEUP) {
-                const MatrixRef &m1 = sh ? p.smb : p.mb;
-                const MatrixRef &md = sh ? p.smdown : p.mdown;
-                svh1 = kRScale * __half2float(vec(m1, m1.svh, m1.svh_stride)[ch]);
-                suhd = __half2float(vec(md, md.suh, md.suh_stride)[ch]);
-            }
-#pragma unroll 1
-            for (int c0 = 8 * grp; c0 < t.z; c0 += 32) {
-                uint32_t dg[8];
-                float vg[8];
-                tmem_ld_32x32b_x8(tmem + lane_base + c0, dg);
-                if (GATEUP) {
-                    uint32_t du[8];
-                    float vu[8];
-                    tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        vg[j] = __uint_as_float(dg[j]);
-                        vu[j] = __uint_as_float(du[j]);
-                    }
-                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
-                    fwht128_lanes(vu, xb, q, lane, 1 + grp);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) vg[j] = swiglu_clamped(vg[j] * svh0, vu[j] * svh1, p.limit) * suhd;
-                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
-                    __half *out = reinterpret_cast<__half *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(vg[j] * kRScale);
-                } else {
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) vg[j] = __uint_as_float(dg[j]);
-                    fwht128_lanes(vg, xb, q, lane, 1 + grp);
-                    float *out = reinterpret_cast<float *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = vg[j] * svh0;
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty);
         }
+        // the last item's epilogue
+        if (ok && it > 0) ok = epilogue(blockIdx.x + (it - 1) * gridDim.x, it - 1);
         if (!ok) {
             atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
             // token loads this warp issued land before the CTA exits (bounded: the slot's phase

@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     if (warp == kGvConsumers) {
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            prefetch_tmap(&p.wa);
-            prefetch_tmap(&p.swa);
+            if (!p.tiled) {
+                prefetch_tmap(&p.wa);
+                prefetch_tmap(&p.swa);
+            }
             prefetch_tmap(&p.xt);
             // The first SW stages are free at start: their weights are requested before the
             // wait on the previous kernel (programmatic dependent launch: the token rows it
@@ -139,10 +141,17 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 const bool sh = t.x == p.E;
                 uint8_t *st = smem + i * C::STAGE;
                 mbar_arrive_expect_tx(&full[i], C::STAGE);
-                tma_load_3d(st, sh ? &p.swa : &p.wa, &full[i], kr * (kRow / 2), (item % MT) * ROWS, sh ? 0 : t.x);
-                if (GATEUP)
-                    tma_load_3d(st + ROWS * kRow, sh ? &p.swb : &p.wb, &full[i], kr * (kRow / 2), (item % MT) * ROWS,
-                                sh ? 0 : t.x);
+                if (p.tiled) {
+                    load_q8_tiled(st, sh ? p.spa : p.pa, p.sa, sh ? 0 : t.x, (item % MT) * ROWS, ROWS, KR, kr, &full[i]);
+                    if (GATEUP)
+                        load_q8_tiled(st + ROWS * kRow, sh ? p.spb : p.pb, p.sb, sh ? 0 : t.x, (item % MT) * ROWS, ROWS,
+                                      KR, kr, &full[i]);
+                } else {
+                    tma_load_3d(st, sh ? &p.swa : &p.wa, &full[i], kr * (kRow / 2), (item % MT) * ROWS, sh ? 0 : t.x);
+                    if (GATEUP)
+                        tma_load_3d(st + ROWS * kRow, sh ? &p.swb : &p.wb, &full[i], kr * (kRow / 2),
+                                    (item % MT) * ROWS, sh ? 0 : t.x);
+                }
             }
             griddep_wait();
             for (int i = 0; i < pre; ++i) {
@@ -167,8 +176,13 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                     if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort))) break;
                     uint8_t *st = smem + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], C::STAGE);
-                    tma_load_3d(st, ma, &full[s], kr * (kRow / 2), m0, z);
-                    if (GATEUP) tma_load_3d(st + ROWS * kRow, mb, &full[s], kr * (kRow / 2), m0, z);
+                    if (p.tiled) {
+                        load_q8_tiled(st, sh ? p.spa : p.pa, p.sa, z, m0, ROWS, KR, kr, &full[s]);
+                        if (GATEUP) load_q8_tiled(st + ROWS * kRow, sh ? p.spb : p.pb, p.sb, z, m0, ROWS, KR, kr, &full[s]);
+                    } else {
+                        tma_load_3d(st, ma, &full[s], kr * (kRow / 2), m0, z);
+                        if (GATEUP) tma_load_3d(st + ROWS * kRow, mb, &full[s], kr * (kRow / 2), m0, z);
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[s], kr * 256 + 64 * q, t.y);
                 }
@@ -312,6 +326,13 @@ int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, c
     g.wb = plan.up64;
     g.swa = plan.sh_gate64;
     g.swb = plan.sh_up64;
+    g.tiled = plan.tiled;
+    g.pa = plan.p_gate;
+    g.pb = plan.p_up;
+    g.spa = plan.p_sh_gate;
+    g.spb = plan.p_sh_up;
+    g.sa = plan.s_gate;
+    g.sb = plan.s_up;
     g.xt = tok_gu;
     g.tiles = a.tiles;
     g.n_tiles = a.tile_counts;
@@ -336,6 +357,10 @@ int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, c
     dn.wb = plan.down;
     dn.swa = plan.sh_down;
     dn.swb = plan.sh_down;
+    dn.tiled = plan.tiled;
+    dn.pa = dn.pb = plan.p_down;
+    dn.spa = dn.spb = plan.p_sh_down;
+    dn.sa = dn.sb = plan.s_down;
     dn.xt = tok_dn;
     dn.tiles = a.tiles;            // same token tiles as gate/up (same N)
     dn.n_tiles = a.tile_counts;

@@ -23,6 +23,9 @@
 // and commits once per sub-stage: each barrier operation in an issuer's instruction stream
 // stalls its next tcgen05.mma, and a single issuer with two waits and two commits per
 // sub-stage kept the tensor pipe under 60 % busy even with all data in place.
+// A work item's epilogue runs after the dequant warps' share of their next item's first raw
+// stage and releases the accumulators as soon as they are read into registers, so the MMAs
+// of the next item start with four sub-stages converted and their token rows landed.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT,
 // drains what it issued and returns.
 //
@@ -212,12 +215,14 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&p.wa);
-        prefetch_tmap(&p.swa);
         prefetch_tmap(&p.xt);
-        if (GATEUP) {
-            prefetch_tmap(&p.wb);
-            prefetch_tmap(&p.swb);
+        if (!p.tiled) {
+            prefetch_tmap(&p.wa);
+            prefetch_tmap(&p.swa);
+            if (GATEUP) {
+                prefetch_tmap(&p.wb);
+                prefetch_tmap(&p.swb);
+            }
         }
     }
     if (warp == 2) {
@@ -249,8 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                     const uint32_t rs = nraw % SW;
                     if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
                     mbar_arrive_expect_tx(&raw_full[rs], kRawMat);
-                    tma_load_3d(raw + rs * (MATS * kRawMat) + mat * kRawMat, mp, &raw_full[rs], kr * (kRawRow / 2), m0,
-                                z);
+                    uint8_t *dst = raw + rs * (MATS * kRawMat) + mat * kRawMat;
+                    if (p.tiled)
+                        load_q8_tiled(dst, mat == 0 ? (sh ? p.spa : p.pa) : (sh ? p.spb : p.pb), mat == 0 ? p.sa : p.sb,
+                                      z, m0, 128, KR, kr, &raw_full[rs]);
+                    else
+                        tma_load_3d(dst, mp, &raw_full[rs], kr * (kRawRow / 2), m0, z);
                     ++nraw;
                 }
             }
@@ -318,6 +327,66 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
         uint32_t nraw = 0, n = 0, it = 0;
         bool ok = true;
         uint32_t tok_issued = 0;  // sub-stages whose token loads this warp issued
+        // Epilogue of item `eitem` (the it-th of this CTA): 8-column chunks of the N token
+        // columns, chunk c handled by group c % 4, read from TMEM in batches of 32 registers.
+        // The accumulators are released (d_empty) once the last batch is in registers, before
+        // its SwiGLU and stores, so the next item's MMAs do not wait for them.
+        auto epilogue = [&](int eitem, uint32_t eit) -> bool {
+            if (!mbar_wait(d_full, eit & 1, abort)) return false;
+            tc_fence_after();
+            const int4 t = p.tiles[eitem / MT];
+            const int ch = (eitem % MT) * 128 + r;
+            constexpr int NCH = (N + 31) / 32;                     // chunks per group
+            constexpr int G = GATEUP ? (NCH < 1 ? NCH : 1) : (NCH < 4 ? NCH : 4);  // chunks per batch
+#pragma unroll
+            for (int b0 = 0; b0 < NCH; b0 += G) {
+                uint32_t dg[G][8];
+                uint32_t du[GATEUP ? G : 1][8];
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        tmem_ld_32x32b_x8(tmem + lane_base + c0, dg[i]);
+                        if constexpr (GATEUP) tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du[i]);
+                    }
+                }
+                tmem_wait_ld();
+                if (b0 + G >= NCH) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(d_empty);
+                }
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        if constexpr (GATEUP) {
+                            __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                if (c0 + j < t.z) {
+                                    const float a = swiglu_clamped_fast(__uint_as_float(dg[i][j]),
+                                                                   __uint_as_float(du[i][j]), p.limit);
+                                    out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(a);
+                                }
+                            }
+                        } else {
+                            float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (c0 + j < t.z)
+                                    out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __uint_as_float(dg[i][j]);
+                        }
+                    }
+                }
+            }
+            return true;
+        };
+        // Item i's epilogue runs after this warp's share of item i+1's first raw stage.  That
+        // share's TMEM slots and token stages were freed by item i's last MMAs, so the next
+        // item's first sub-stages are converted and their token rows in flight while item i's
+        // accumulators drain.  Deferring further would deadlock: item i+1's second raw stage
+        // needs slots that only item i+1's MMAs free, and those wait for d_empty.
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
             const int4 tt = p.tiles[item / MT];
             const int t_y = tt.y, n16 = (tt.z + 15) >> 4;  // 16-row token boxes actually needed
@@ -329,7 +398,25 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                 for (int s = 0; s < 4; ++s) {
                     if (s == grp) {
                         // group g converts sub-stage g of every raw stage: K = 64 (two Q8_0
-                        // blocks) of its 32 rows, for each matrix; one wait covers the stores
+                        // blocks) of its 32 rows, for each matrix.  The warp reads its raw
+                        // words of both matrices into registers and releases the raw stage
+                        // before it waits for its TMEM slot: the stage's lifetime is then
+                        // its load latency plus four reads, which sets how fast weights stream.
+                        uint32_t w[MATS][20];
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+#pragma unroll
+                            for (int c = 0; c < 5; ++c) {
+                                const uint4 v4 =
+                                    *reinterpret_cast<const uint4 *>(row + m * kRawMat + 64 * s + 16 * c);
+                                w[m][4 * c] = v4.x;
+                                w[m][4 * c + 1] = v4.y;
+                                w[m][4 * c + 2] = v4.z;
+                                w[m][4 * c + 3] = v4.w;
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&raw_empty[rs]);
                         const uint32_t sl = n % kSlots;
                         if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
                         if (q == 0) {
@@ -345,19 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                         const uint32_t tcol = tmem + lane_base + C::A_COL0 + sl * MATS * 32;
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
-                            uint32_t w[20];
-#pragma unroll
-                            for (int c = 0; c < 5; ++c) {
-                                const uint4 v4 =
-                                    *reinterpret_cast<const uint4 *>(row + m * kRawMat + 64 * s + 16 * c);
-                                w[4 * c] = v4.x;
-                                w[4 * c + 1] = v4.y;
-                                w[4 * c + 2] = v4.z;
-                                w[4 * c + 3] = v4.w;
-                            }
                             uint32_t g[17];
 #pragma unroll
-                            for (int j = 0; j < 17; ++j) g[j] = w[s + j];
+                            for (int j = 0; j < 17; ++j) g[j] = w[m][s + j];
                             uint32_t v[32];
                             q8_two_blocks(g, v);
                             tmem_st_32x32b_x32(tcol + m * 32, v);
@@ -370,45 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                     ++n;
                 }
                 if (!ok) break;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_empty[rs]);
                 ++nraw;
+                if (kr == 0 && it > 0 && !(ok = epilogue(item - gridDim.x, it - 1))) break;
             }
-            if (!ok) break;
-            // epilogue: 8-column chunks of the N token columns, chunk c handled by group c % 4
-            if (!(ok = mbar_wait(d_full, it & 1, abort))) break;
-            tc_fence_after();
-            const int4 t = p.tiles[item / MT];
-            const int ch = (item % MT) * 128 + r;
-#pragma unroll 1
-            for (int c0 = 8 * grp; c0 < N; c0 += 32) {
-                if (c0 >= t.z) break;
-                uint32_t dg[8];
-                tmem_ld_32x32b_x8(tmem + lane_base + c0, dg);
-                if (GATEUP) {
-                    uint32_t du[8];
-                    tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du);
-                    tmem_wait_ld();
-                    __half *out = reinterpret_cast<__half *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        if (c0 + j < t.z) {
-                            const float a = swiglu_clamped(__uint_as_float(dg[j]), __uint_as_float(du[j]), p.limit);
-                            out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(a);
-                        }
-                    }
-                } else {
-                    tmem_wait_ld();
-                    float *out = reinterpret_cast<float *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (c0 + j < t.z) out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __uint_as_float(dg[j]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty);
         }
+        // the last item's epilogue
+        if (ok && it > 0) ok = epilogue(blockIdx.x + (it - 1) * gridDim.x, it - 1);
         if (!ok) {
             atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
             // token loads this warp issued land before the CTA exits (bounded: the slot's phase
@@ -486,17 +530,37 @@ static int make_tok_map(CUtensorMap *m, const void *base, int64_t rows, int64_t 
 
 int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     plan.ready = 0;
-    if (d.weight_format != VFMOE_WFMT_Q8_0) return VFMOE_OK;
-    if (getenv("VFMOE_DISABLE_TC")) return VFMOE_OK;
+    const bool tiled = d.weight_format == VFMOE_WFMT_Q8_0_TILED;
+    if (d.weight_format != VFMOE_WFMT_Q8_0 && !tiled) return VFMOE_OK;
+    if (getenv("VFMOE_DISABLE_TC")) {
+        if (!tiled) return VFMOE_OK;
+        set_error("VFMOE_DISABLE_TC: the SIMT expert path reads GGUF row order, not VFMOE_WFMT_Q8_0_TILED");
+        return VFMOE_ERR_UNSUPPORTED;
+    }
     int dev = 0;
     VF_CUDA(cudaGetDevice(&dev));
     VF_CUDA(cudaDeviceGetAttribute(&plan.num_sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t H = d.hidden, I = d.inter, E = d.n_local_experts ? d.n_local_experts : d.n_experts;
+    const bool sh = d.sh_gate.data != 0;
+    plan.decode_tc = getenv("VFMOE_DECODE_TC") != nullptr;
+    if (tiled) {
+        plan.tiled = 1;
+        plan.p_gate = reinterpret_cast<const uint8_t *>(d.gate.data);
+        plan.p_up = reinterpret_cast<const uint8_t *>(d.up.data);
+        plan.p_down = reinterpret_cast<const uint8_t *>(d.down.data);
+        plan.p_sh_gate = reinterpret_cast<const uint8_t *>(sh ? d.sh_gate.data : d.gate.data);
+        plan.p_sh_up = reinterpret_cast<const uint8_t *>(sh ? d.sh_up.data : d.up.data);
+        plan.p_sh_down = reinterpret_cast<const uint8_t *>(sh ? d.sh_down.data : d.down.data);
+        plan.s_gate = E > 1 ? d.gate.expert_stride : 0;
+        plan.s_up = E > 1 ? d.up.expert_stride : 0;
+        plan.s_down = E > 1 ? d.down.expert_stride : 0;
+        plan.ready = 1;
+        return VFMOE_OK;
+    }
     int rc;
     if ((rc = make_q8_map(&plan.gate, (void *)d.gate.data, I, H, E, d.gate.expert_stride))) return rc;
     if ((rc = make_q8_map(&plan.up, (void *)d.up.data, I, H, E, d.up.expert_stride))) return rc;
     if ((rc = make_q8_map(&plan.down, (void *)d.down.data, H, I, E, d.down.expert_stride))) return rc;
-    const bool sh = d.sh_gate.data != 0;
     if ((rc = make_q8_map(&plan.sh_gate, (void *)(sh ? d.sh_gate.data : d.gate.data), I, H, 1, 0))) return rc;
     if ((rc = make_q8_map(&plan.sh_up, (void *)(sh ? d.sh_up.data : d.up.data), I, H, 1, 0))) return rc;
     if ((rc = make_q8_map(&plan.sh_down, (void *)(sh ? d.sh_down.data : d.down.data), H, I, 1, 0))) return rc;
@@ -504,13 +568,12 @@ int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     if ((rc = make_q8_map(&plan.up64, (void *)d.up.data, I, H, E, d.up.expert_stride, 64))) return rc;
     if ((rc = make_q8_map(&plan.sh_gate64, (void *)(sh ? d.sh_gate.data : d.gate.data), I, H, 1, 0, 64))) return rc;
     if ((rc = make_q8_map(&plan.sh_up64, (void *)(sh ? d.sh_up.data : d.up.data), I, H, 1, 0, 64))) return rc;
-    plan.decode_tc = getenv("VFMOE_DECODE_TC") != nullptr;
     plan.ready = 1;
     return VFMOE_OK;
 }
 
 bool tc_supported(const TcPlan &plan, const MoeArgs &a) {
-    return plan.ready && a.fmt == VFMOE_WFMT_Q8_0 && a.tiles != nullptr && a.H % 256 == 0 && a.I % 256 == 0;
+    return plan.ready && (a.fmt == VFMOE_WFMT_Q8_0 || a.fmt == VFMOE_WFMT_Q8_0_TILED) && a.tiles != nullptr && a.H % 256 == 0 && a.I % 256 == 0;
 }
 
 // Tiles of at least 8 rows (the decode GEMV's smallest): sum_e ceil(n_e / 8) <= rows / 8 + segments.
@@ -570,6 +633,13 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     g.wb = plan.up;
     g.swa = plan.sh_gate;
     g.swb = plan.sh_up;
+    g.tiled = plan.tiled;
+    g.pa = plan.p_gate;
+    g.pb = plan.p_up;
+    g.spa = plan.p_sh_gate;
+    g.spb = plan.p_sh_up;
+    g.sa = plan.s_gate;
+    g.sb = plan.s_up;
     if ((rc = make_tok_map(&g.xt, a.xp, rows, a.H, 16))) return rc;
     g.tiles = a.tiles;
     g.n_tiles = a.tile_counts;
@@ -594,6 +664,10 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     dn.wb = plan.down;
     dn.swa = plan.sh_down;
     dn.swb = plan.sh_down;
+    dn.tiled = plan.tiled;
+    dn.pa = dn.pb = plan.p_down;
+    dn.spa = dn.spb = plan.p_sh_down;
+    dn.sa = dn.sb = plan.s_down;
     if ((rc = make_tok_map(&dn.xt, a.act, rows, a.I, 16))) return rc;
     dn.tiles = a.tiles + a.tiles_cap;
     dn.n_tiles = a.tile_counts + 1;

@@ -4,6 +4,7 @@
 #include <cuda.h>
 
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace vfmoe {
 
@@ -16,12 +17,23 @@ struct TcPlan {
     CUtensorMap sh_gate, sh_up, sh_down; // shared expert (one "expert")
     // 64-row boxes for the decode GEMV's gate/up tiles
     CUtensorMap gate64, up64, sh_gate64, sh_up64;
+    // VFMOE_WFMT_Q8_0_TILED: weight bases and expert strides, read by 1D bulk copies
+    // (no tensor maps)
+    int tiled = 0;
+    const uint8_t *p_gate = nullptr, *p_up = nullptr, *p_down = nullptr;
+    const uint8_t *p_sh_gate = nullptr, *p_sh_up = nullptr, *p_sh_down = nullptr;
+    int64_t s_gate = 0, s_up = 0, s_down = 0;
 };
 
 // Kernel parameters shared by the tcgen05 GEMM and the decode GEMV (passed __grid_constant__).
 struct TcParams {
     CUtensorMap wa, wb, swa, swb;   // weights: routed A/B matrices, shared A/B (3D u16 maps)
     CUtensorMap xt;                 // token rows, fp16 [rows][K], SWIZZLE_128B
+    // tiled != 0: the weights are VFMOE_WFMT_Q8_0_TILED and read from these bases instead of
+    // the maps (routed A/B with expert strides, shared A/B)
+    const uint8_t *pa, *pb, *spa, *spb;
+    int64_t sa, sb;
+    int tiled;
     const int4 *tiles;              // {expert, row0, nrows, 0}
     const int32_t *n_tiles;
     int E, K, M;
@@ -32,6 +44,22 @@ struct TcParams {
 };
 
 int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan);
+
+// VFMOE_WFMT_Q8_0_TILED: a Q8_0 matrix [rows][K] is stored as tiles of 64 rows x 256 K
+// (64 x 272 B = 17,408 B; each tile row is that row's 8 GGUF blocks), tile (rt, kr) at
+// byte ((rt * K/256) + kr) * 17,408.  One weight stage of a 64-row tile is one contiguous
+// copy: the TMA tensor path moves GGUF's 272-byte row pieces at about 70 GB/s per SM, a
+// contiguous bulk copy at about 117 GB/s.
+constexpr int kQ8Tile = 64 * 272;
+
+// Weight stage (rows m0 .. m0 + rows - 1, K = 256 * kr .. + 255) of expert z of a tiled
+// matrix into dst as rows / 64 bulk copies, completion on bar.
+__device__ __forceinline__ void load_q8_tiled(uint8_t *dst, const uint8_t *base, int64_t estride, int z, int m0,
+                                              int rows, int KR, int kr, uint64_t *bar) {
+    const uint8_t *src = base + (int64_t)z * estride + ((int64_t)(m0 >> 6) * KR + kr) * kQ8Tile;
+    for (int h = 0; h < (rows >> 6); ++h)
+        sm100::bulk_load(dst + h * kQ8Tile, src + (int64_t)h * KR * kQ8Tile, kQ8Tile, bar);
+}
 bool tc_supported(const TcPlan &plan, const MoeArgs &a);
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
 

@@ -70,6 +70,7 @@ int launch_residual_rmsnorm(const void *x, const void *y, const float *w, void *
 int launch_q8_0_dequant(const uint8_t *src, void *dst, int64_t rows, int64_t k, int dst_dtype,
                         cudaStream_t st);
 int launch_q8_0_quantize(const float *src, uint8_t *dst, int64_t rows, int64_t k, cudaStream_t st);
+int launch_q8_0_tile(const uint8_t *src, uint8_t *dst, int64_t rows, int64_t k, int64_t n_mats, cudaStream_t st);
 int launch_exl3_decode(const uint16_t *trellis, __half *dst, int64_t K, int64_t N, int bits,
                        cudaStream_t st);
 

@@ -1,4 +1,5 @@
 // Weight-format kernels: Q8_0 quantize/dequantize, EXL3 trellis decode, RMSNorm.
+#include <algorithm>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -179,6 +180,34 @@ int launch_q8_0_quantize(const float *src, uint8_t *dst, int64_t rows, int64_t k
     if (nblk == 0) return VFMOE_OK;
     q8_0_quantize_kernel<<<(unsigned)cdiv(nblk, 128), 128, 0, st>>>(src, dst, nblk);
     VF_LAUNCH_CHECK("q8_0_quantize_kernel");
+    return VFMOE_OK;
+}
+
+// GGUF Q8_0 rows -> stage-tiled order (VFMOE_WFMT_Q8_0_TILED), one 16-byte chunk per
+// thread step, destination order: chunk o of a matrix lies in tile o / 1088 (tile rt, stage
+// kr; 17,408 B = 1088 chunks), tile row (o % 1088) / 17, chunk (o % 1088) % 17 of that row's
+// 272-byte stage kr.
+__global__ void q8_0_tile_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst, int64_t n_chunks,
+                                 int64_t mat_chunks, int64_t KR) {
+    const int64_t row_chunks = 17 * KR;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_chunks;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / mat_chunks, o = i - m * mat_chunks;
+        const int64_t tile = o / 1088, w = o - tile * 1088;
+        const int64_t rt = tile / KR, kr = tile - rt * KR;
+        const int64_t r = w / 17, b = w - r * 17;
+        dst[i] = src[m * mat_chunks + (rt * 64 + r) * row_chunks + kr * 17 + b];
+    }
+}
+
+int launch_q8_0_tile(const uint8_t *src, uint8_t *dst, int64_t rows, int64_t k, int64_t n_mats, cudaStream_t st) {
+    const int64_t mat_chunks = rows * (k / 32 * 34) / 16;
+    const int64_t n = mat_chunks * n_mats;
+    if (n == 0) return VFMOE_OK;
+    const int64_t blocks = std::min<int64_t>(cdiv(n, 256), 148 * 16);
+    q8_0_tile_kernel<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const uint4 *>(src),
+                                                        reinterpret_cast<uint4 *>(dst), n, mat_chunks, k / 256);
+    VF_LAUNCH_CHECK("q8_0_tile_kernel");
     return VFMOE_OK;
 }
 

@@ -20,7 +20,7 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import check, DT_BF16, DT_F16, DT_F32, WFMT_Q8_0, WFMT_EXL3
+from ._lib import check, DT_BF16, DT_F16, DT_F32, WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED
 
 _DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
 
@@ -37,11 +37,24 @@ def init(device: int = 0) -> None:
     check(_lib.load().vfmoe_init(device))
 
 
+def q8_0_tile(w: torch.Tensor) -> torch.Tensor:
+    """Stage-tiled copy (VFMOE_WFMT_Q8_0_TILED) of Q8_0 matrices in GGUF row order:
+    uint8 [..., rows, k/32*34] on the GPU, rows % 64 == 0, k % 256 == 0."""
+    assert w.dtype == torch.uint8 and w.is_cuda and w.is_contiguous()
+    rows, rb = w.shape[-2], w.shape[-1]
+    k = rb // 34 * 32
+    n = w.numel() // (rows * rb)
+    out = torch.empty_like(w)
+    check(_lib.load().vfmoe_q8_0_tile(_ptr(w), _ptr(out), rows, k, n, _stream()))
+    return out
+
+
 class MoELayer:
     """One GLM-style MoE layer (router + routed experts + shared expert) on one GPU.
 
     Q8_0 weights: ``gate``/``up`` uint8 [E, I, H/32*34], ``down`` uint8 [E, H, I/32*34]
     (GGUF block rows = output channels); ``shared`` = (gate [I, ...], up, down) or None.
+    fmt="q8_0_tiled": the same tensors after ``q8_0_tile`` (stage-tiled byte order).
     EXL3 weights: each projection is a tuple (trellis int16 [E, K/16, N/16, 16*bits],
     suh fp16 [E, K], svh fp16 [E, N]); shared likewise without the leading E.
     """
@@ -57,7 +70,7 @@ class MoELayer:
         d.hidden, d.inter, d.n_experts, d.topk = hidden, inter, n_experts, topk
         d.n_local_experts = n_local_experts
         self.n_local = n_local_experts or n_experts
-        d.weight_format = WFMT_Q8_0 if fmt == "q8_0" else WFMT_EXL3
+        d.weight_format = {"q8_0": WFMT_Q8_0, "q8_0_tiled": WFMT_Q8_0_TILED, "exl3": WFMT_EXL3}[fmt]
         d.exl3_bits = exl3_bits
         d.x_dtype, d.out_dtype = _DT[x_dtype], _DT[out_dtype]
         d.routed_scale, d.swiglu_limit = scale, limit
@@ -65,7 +78,7 @@ class MoELayer:
         self._keep = [router_w, router_bias, gate, up, down, shared]
 
         def fill(m, w, stacked):
-            if fmt == "q8_0":
+            if fmt in ("q8_0", "q8_0_tiled"):
                 m.data = _ptr(w)
                 m.expert_stride = w[0].numel() * w.element_size() if stacked else 0
             else:
