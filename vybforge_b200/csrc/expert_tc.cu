@@ -399,24 +399,33 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                     if (s == grp) {
                         // group g converts sub-stage g of every raw stage: K = 64 (two Q8_0
                         // blocks) of its 32 rows, for each matrix.  The warp reads its raw
-                        // words of both matrices into registers and releases the raw stage
-                        // before it waits for its TMEM slot: the stage's lifetime is then
-                        // its load latency plus four reads, which sets how fast weights stream.
-                        uint32_t w[MATS][20];
-#pragma unroll
-                        for (int m = 0; m < MATS; ++m) {
+                        // words into registers and releases the raw stage, and converts the
+                        // first matrix, before it waits for its TMEM slot: the stage's lifetime
+                        // is its load latency plus four reads, and after the slot frees only
+                        // one conversion is left before the MMAs can use it.
+                        auto load_words = [&](int m, uint32_t (&w)[20]) {
 #pragma unroll
                             for (int c = 0; c < 5; ++c) {
                                 const uint4 v4 =
                                     *reinterpret_cast<const uint4 *>(row + m * kRawMat + 64 * s + 16 * c);
-                                w[m][4 * c] = v4.x;
-                                w[m][4 * c + 1] = v4.y;
-                                w[m][4 * c + 2] = v4.z;
-                                w[m][4 * c + 3] = v4.w;
+                                w[4 * c] = v4.x;
+                                w[4 * c + 1] = v4.y;
+                                w[4 * c + 2] = v4.z;
+                                w[4 * c + 3] = v4.w;
                             }
-                        }
+                        };
+                        auto convert = [&](const uint32_t (&w)[20], uint32_t (&v)[32]) {
+                            uint32_t g[17];
+#pragma unroll
+                            for (int j = 0; j < 17; ++j) g[j] = w[s + j];
+                            q8_two_blocks(g, v);
+                        };
+                        uint32_t w0[20], w1[20], v[32];
+                        load_words(0, w0);
+                        if (GATEUP) load_words(1, w1);
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                        convert(w0, v);
                         const uint32_t sl = n % kSlots;
                         if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
                         if (q == 0) {
@@ -430,14 +439,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
                             tok_issued = n + 1;
                         }
                         const uint32_t tcol = tmem + lane_base + C::A_COL0 + sl * MATS * 32;
-#pragma unroll
-                        for (int m = 0; m < MATS; ++m) {
-                            uint32_t g[17];
-#pragma unroll
-                            for (int j = 0; j < 17; ++j) g[j] = w[m][s + j];
-                            uint32_t v[32];
-                            q8_two_blocks(g, v);
-                            tmem_st_32x32b_x32(tcol + m * 32, v);
+                        tmem_st_32x32b_x32(tcol, v);
+                        if (GATEUP) {
+                            convert(w1, v);
+                            tmem_st_32x32b_x32(tcol + 32, v);
                         }
                         tmem_wait_st();
                         tc_fence_before();
