@@ -84,7 +84,7 @@ def q8_layout_weights(layout, dev):
 
 
 # ----------------------------------------------------------------------------- ncu cases
-def _profile_decode(fmt):
+def _profile_decode(fmt, layout="tiled"):
     """C1 (Q8_0) or C2 (EXL3 3 bpw) layer shapes with 64 routed experts, T=32: about 0.9 GB of
     weights (above L2, a few GB on the device at most); three forwards."""
     import torch
@@ -96,7 +96,7 @@ def _profile_decode(fmt):
     x, w_r, bias, _ = synth.router_inputs(cfg)
     E = cfg.n_experts
     if fmt == "q8_0":
-        dev, wf = q8_layout_weights("tiled", synth.expert_q8_cuda(cfg, quantizer))
+        dev, wf = q8_layout_weights(layout, synth.expert_q8_cuda(cfg, quantizer))
         mats = dict(gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
                     fmt=wf)
     else:
@@ -114,7 +114,7 @@ def _profile_decode(fmt):
     layer.check_device_error()
 
 
-def _profile_prefill():
+def _profile_prefill(layout="tiled"):
     """C3 shapes (Q8_0, Zipf(1.1) routing, T=4096) with 64 routed experts: ~0.9 GB of weights;
     three forwards."""
     import torch
@@ -125,7 +125,7 @@ def _profile_prefill():
     cfg.n_experts = 64
     x, w_r, bias, _, _ = synth.zipf_router_inputs(cfg)
     E = cfg.n_experts
-    dev, wf = q8_layout_weights("tiled", synth.expert_q8_cuda(cfg, quantizer))
+    dev, wf = q8_layout_weights(layout, synth.expert_q8_cuda(cfg, quantizer))
     layer = MoELayer(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk,
                      router_w=torch.from_numpy(w_r).cuda(), router_bias=torch.from_numpy(bias).cuda(),
                      gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]),
@@ -170,8 +170,9 @@ def _profile_router():
     print(json.dumps({"route_us": res}))
 
 
-PROFILE_CASES = {"q8_decode_e64": lambda: _profile_decode("q8_0"), "exl3_decode_e64": lambda: _profile_decode("exl3"),
-                 "q8_prefill_e64": _profile_prefill, "router_sweep": _profile_router}
+PROFILE_CASES = {"q8_decode_e64": lambda a: _profile_decode("q8_0", a.q8_layout),
+                 "exl3_decode_e64": lambda a: _profile_decode("exl3"),
+                 "q8_prefill_e64": lambda a: _profile_prefill(a.q8_layout), "router_sweep": lambda a: _profile_router()}
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -837,7 +838,7 @@ def run_reference(a):
 def main():
     a = args_parse()
     if a.profile_case:
-        PROFILE_CASES[a.profile_case]()
+        PROFILE_CASES[a.profile_case](a)
         print("ok")
         return
     rank = int(os.environ.get("RANK", "0"))
