@@ -12,7 +12,9 @@
 //
 // Data path per CTA (one per SM, persistent over (expert, token tile, channel tile)):
 //   warp 8       TMA producer: per stage, 8 Q8_0 blocks (272 B) of each weight row of the
-//                tile plus the 256-K slice of the tile's N token rows (fp16, SWIZZLE_128B).
+//                tile (a TMA box from GGUF rows, or one bulk copy per 64 rows from
+//                stage-tiled weights) plus the 256-K slice of the tile's N token rows
+//                (fp16, SWIZZLE_128B).
 //   warps 0..7   consumers, 16 weight rows each: LDS raw bytes -> fp16(d*q) fragments in
 //                registers -> mma.sync against token fragments -> fp32 accumulators.
 //                gate/up tile = 64 channels x (gate, up): warps 0-3 gate, 4-7 up, SwiGLU

@@ -9,7 +9,8 @@
 //       written straight into TMEM with tcgen05.st (no shared-memory round trip);
 //   B = token rows (fp16), N x 64 per sub-stage, TMA SWIZZLE_128B tiles in shared memory;
 //   D = fp32 accumulators in TMEM (gate and up side by side for the fused SwiGLU).
-// Raw Q8_0 bytes stream in by TMA as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage.
+// Raw Q8_0 bytes stream in as 128 rows x 272 B (8 GGUF blocks = 256 K) per stage: one TMA
+// box from GGUF rows, or two contiguous bulk copies from stage-tiled weights.
 //
 // Warp roles (640 threads): warps 0 and 3 TMA producers of the weight stages (one matrix
 // each), warps 1 and 2 MMA issuers (one thread each; warp 2 also allocates TMEM), warps
