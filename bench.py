@@ -71,8 +71,9 @@ def args_parse():
     return ap.parse_args()
 
 
-# dram bytes / algorithmic bytes of the Q8_0 gate/up GEMV, from its ncu capture
-GEMV_Q8_TRAFFIC_RATIO = 1.015
+# dram bytes / algorithmic bytes of the Q8_0 gate/up GEMV per weight layout, from ncu
+# captures of the 64-expert case (--profile-case q8_decode_e64 [--q8-layout rows])
+GEMV_Q8_TRAFFIC_RATIO = {"q8_0_tiled": 1.006, "q8_0": 1.015}
 
 def q8_layout_weights(layout, dev):
     """A layer's Q8_0 weights in the bench's layout: stage-tiled by default (VFMOE_WFMT_Q8_0_TILED,
@@ -740,10 +741,10 @@ def run_ours(a, rank, world, local_rank):
     layer_gbs = layer_bytes / (ms * 1e-3) / 1e9
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     # traffic: dram read+write per launch, scaled from the ncu capture of the same kernel on the
-    # 64-expert case (--profile-case q8_decode_e64): 1.015 x algorithmic bytes
+    # 64-expert case (--profile-case q8_decode_e64): 1.006 (tiled) or 1.015 (rows) x algorithmic bytes
     roof = {"bound": "hbm", "kernel": "expert gate/up GEMV (Q8_0, fused SwiGLU)", "achieved": round(achieved, 1),
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-            "peak_source": pk_kind, "traffic": round(gu_bytes * GEMV_Q8_TRAFFIC_RATIO),
+            "peak_source": pk_kind, "traffic": round(gu_bytes * GEMV_Q8_TRAFFIC_RATIO[wf]),
             "traffic_source": "ncu capture of the 64-expert case, scaled by algorithmic bytes",
             "algorithmic_bytes_per_launch": gu_bytes,
             "layer_hbm_frac": round(layer_gbs / pk["hbm_gbs"], 4),
