@@ -227,6 +227,35 @@ def test_tiled_weights_give_identical_output(c1, c1_tiled, T):
     assert torch.equal(ref, got)
 
 
+# ----------------------------------------------------------------------------- CUDA graph capture
+@pytest.mark.parametrize("T", [1, 32, 1024])
+def test_forward_is_cuda_graph_capturable(c1_tiled, T):
+    """With a caller workspace, vfmoe_forward makes no host synchronisation and no allocation:
+    it records into a CUDA graph (programmatic-dependent launches included), and a replay
+    reproduces the eager result bit for bit (decode GEMV at T <= 32, tcgen05 GEMM above)."""
+    layer = c1_tiled
+    H, k = layer.H, layer.k
+    g = torch.Generator(device="cuda").manual_seed(100 + T)
+    x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    ws = torch.empty(layer.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    layer.forward(x, out=out, idx=idx, w=w, workspace=ws)
+    torch.cuda.synchronize()
+    ref, ref_idx, ref_w = out.clone(), idx.clone(), w.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer.forward(x, out=out, idx=idx, w=w, workspace=ws)
+    out.zero_()
+    idx.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    layer.check_device_error()
+    assert torch.equal(out, ref) and torch.equal(idx, ref_idx) and torch.equal(w, ref_w)
+    del graph
+
+
 # ----------------------------------------------------------------------------- tcgen05 path vs SIMT path
 def _simt_layer(built, out_dtype=torch.float32):
     os.environ["VFMOE_DISABLE_TC"] = "1"
