@@ -327,6 +327,36 @@ def time_layer(layer, xd, steps, warmup, flush, with_profile=True):
     return ms, {n: stage[i] / nf for i, n in enumerate(names)}, int(launches.value), idx
 
 
+def time_graph(layer, xd, steps, flush):
+    """Device time per forward replayed from a CUDA graph of one vfmoe_forward (caller
+    workspace, no stage events), CUDA events around each replay, L2 flushed between replays."""
+    import torch
+    st = torch.cuda.current_stream()
+    T = xd.shape[0]
+    out = torch.empty((T, layer.H), dtype=layer.out_dtype, device="cuda")
+    idx = torch.empty((T, layer.k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, layer.k), dtype=torch.float32, device="cuda")
+    ws = layer.workspace(T)
+    for _ in range(3):
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer.forward(xd, out=out, idx=idx, w=w, workspace=ws)
+    for _ in range(3):
+        graph.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(st)
+        graph.replay()
+        ev[i][1].record(st)
+    torch.cuda.synchronize()
+    layer.check_device_error()
+    del graph
+    return float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+
+
 def prefill_extra(a, cfg1, dev, wf, flush):
     """C3: T=4096 prefill, Zipf(1.1)-skewed routing, same Q8_0 expert weights as C1."""
     import torch
@@ -768,6 +798,18 @@ def run_ours(a, rank, world, local_rank):
         extra = {}
         ms1, st1, _, idx1 = time_layer(layer, xd[:1].contiguous(), a.steps, a.warmup, flush)
         l1b, gu1b = algorithmic_bytes(synth.config("c1", tokens=1), len(np.unique(idx1.cpu().numpy())))
+        try:
+            ms1_plain = time_layer(layer, xd[:1].contiguous(), a.steps, a.warmup, flush, with_profile=False)[0]
+            ms1_graph = time_graph(layer, xd[:1].contiguous(), a.steps, flush)
+            ms32_graph = time_graph(layer, xd, a.steps, flush)
+            extra["cuda_graph"] = {
+                "note": "one vfmoe_forward recorded in a CUDA graph and replayed; eager time without the "
+                        "library's per-stage events beside it",
+                "t1": {"ms_per_step": round(ms1_graph, 4), "tokens_per_s": round(1 / (ms1_graph * 1e-3), 1),
+                       "eager_ms_per_step": round(ms1_plain, 4)},
+                "t32": {"ms_per_step": round(ms32_graph, 4), "tokens_per_s": round(32 / (ms32_graph * 1e-3), 1)}}
+        except Exception as e:  # an extra must not cost the headline line
+            extra["cuda_graph"] = {"error": str(e)[:300]}
         extra["c1_t1"] = {"tokens_per_s": round(1 / (ms1 * 1e-3), 1), "ms_per_step": round(ms1, 4),
                           "gate_up_hbm_frac": round(gu1b / (st1["gate_up"] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                           "layer_hbm_frac": round(l1b / (ms1 * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
