@@ -26,6 +26,7 @@
  *   router   W_r fp32 [n_experts, hidden], selection bias fp32 [n_experts]
  *   Q8_0     per matrix: output rows, each K/32 GGUF blocks of 34 bytes
  *            (fp16 d, int8 q[32]); gate/up [inter][hidden], down [hidden][inter]
+ *            (or the same blocks stage-tiled, VFMOE_WFMT_Q8_0_TILED / vfmoe_q8_0_tile)
  *   EXL3     per matrix (in, out) = (K, N): trellis uint16 [K/16][N/16][16*bits],
  *            suh fp16 [K], svh fp16 [N] (native/exl3/README.md:26-31)
  *   idx      int32 [T, topk] (the reference stores float32, moe.vyb:76)
