@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
             const int4 t = p.tiles[eitem / MT];
             const int ch = (eitem % MT) * 128 + r;
             constexpr int NCH = (N + 31) / 32;                     // chunks per group
-            constexpr int G = GATEUP ? (NCH < 1 ? NCH : 1) : (NCH < 4 ? NCH : 4);  // chunks per batch
+            constexpr int G = GATEUP ? 1 : (NCH < 4 ? NCH : 4);  // chunks per batch (register budget)
 #pragma unroll
             for (int b0 = 0; b0 < NCH; b0 += G) {
                 uint32_t dg[G][8];
