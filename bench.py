@@ -63,6 +63,8 @@ def args_parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the extra T=1 and prefill measurements")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--ep-replicas", type=int, default=0,
+                    help="C4 at N > 1: copies of the hottest experts on other ranks (0 = none; a multiple of N)")
     ap.add_argument("--q8-layout", default="tiled", choices=["tiled", "rows"],
                     help="Q8_0 weights in HBM: stage-tiled (converted once at load, outside the timed "
                          "region) or GGUF row order")
@@ -410,11 +412,18 @@ def stack_extra(a, rank, world, local_rank, flush):
     xp, norm_p, routers_p = synth.stack_inputs(cfgp, L)
     xd, norm_d, routers_d = synth.stack_inputs(cfgd, L)
     E, H, I, k = cfgp.n_experts, cfgp.hidden, cfgp.inter, cfgp.topk
-    placements = [ep.balanced_placement(routers_p[l][2], world) if world > 1 else np.zeros(E, np.int32)
-                  for l in range(L)]
+    n_rep = a.ep_replicas if world > 1 else 0
+    if n_rep:
+        placed = [ep.replicated_placement(routers_p[l][2], world, n_rep) for l in range(L)]
+        placements, replicas = [p_ for p_, _ in placed], [h for _, h in placed]
+    else:
+        placements = [ep.balanced_placement(routers_p[l][2], world) if world > 1 else np.zeros(E, np.int32)
+                      for l in range(L)]
+        replicas = [np.zeros(0, np.int32)] * L
     layers = {"p": [], "d": []}
     for l in range(L):
-        mine = [int(e) for e in np.nonzero(placements[l] == rank)[0]] + [E]
+        # this rank's (virtual) experts in ascending order; copy E + j holds expert replicas[l][j]
+        mine = [int(e) if e < E else int(replicas[l][e - E]) for e in np.nonzero(placements[l] == rank)[0]] + [E]
         dev, wf = q8_layout_weights(a.q8_layout, synth.expert_q8_cuda(cfgp, quantizer, layer=l, experts=mine))
         torch.cuda.empty_cache()
         for key, routers in (("p", routers_p), ("d", routers_d)):
@@ -422,7 +431,7 @@ def stack_extra(a, rank, world, local_rank, flush):
             lay = MoELayer(hidden=H, inter=I, n_experts=E, topk=k, router_w=torch.from_numpy(w_r).cuda(),
                            router_bias=torch.from_numpy(bias).cuda(), gate=dev[0][:-1], up=dev[1][:-1],
                            down=dev[2][:-1], shared=(dev[0][-1], dev[1][-1], dev[2][-1]),
-                           n_local_experts=E // world if world > 1 else 0, fmt=wf,
+                           n_local_experts=len(placements[l]) // world if world > 1 else 0, fmt=wf,
                            x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
             layers[key].append(lay)
     t_setup = time.perf_counter() - t_setup
@@ -433,7 +442,8 @@ def stack_extra(a, rank, world, local_rank, flush):
         T = cfg.tokens
         nw = [torch.from_numpy(w).cuda() for w in norm]
         if world > 1:
-            stack = EpStack([ep.EpRank(rank, world, ep.GpuBackend(lay, placements[l], world))
+            stack = EpStack([ep.EpRank(rank, world, ep.GpuBackend(lay, placements[l], world),
+                                       replica_of=replicas[l], n_experts=E)
                              for l, lay in enumerate(layers[key])], nw)
             sh = token_shards(T, world)[rank]
             xl = torch.from_numpy(x[sh[0]:sh[-1] + 1]).to(torch.bfloat16).cuda()
@@ -513,9 +523,13 @@ def stack_extra(a, rank, world, local_rank, flush):
                                      "frac": round(tf / (world * pk["bf16_tflops"]), 4), "peak_source": pk_kind,
                                      "algorithmic_flops_per_step": flops}})
             if world > 1:
-                loads = np.array([[routers_p[l][2][placements[l] == r].sum() for r in range(world)]
-                                  for l in range(L)])
+                def vload(l):  # expected rows per (virtual) expert: a copy and its expert share the rows
+                    ld = np.concatenate([routers_p[l][2], np.zeros(len(replicas[l]))]).astype(np.float64)
+                    ld[replicas[l]] = ld[E:] = routers_p[l][2][replicas[l]] / 2
+                    return ld
+                loads = np.array([[vload(l)[placements[l] == r].sum() for r in range(world)] for l in range(L)])
                 res["placement_expected_rows_max_over_mean"] = round(float((loads.max(1) / loads.mean(1)).max()), 3)
+                res["ep_replicas"] = n_rep
         else:
             res["workload"] = "c4d: 4 layers x (RMSNorm + MoE + residual), decode T=256, Q8_0, bf16 activations"
         out["c4" + key] = res

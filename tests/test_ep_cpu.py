@@ -21,12 +21,12 @@ class NumpyBackend:
     """Oracle compute for one rank (test infrastructure only), in the token-level exchange
     protocol of ep.EpRank: plan / pack / experts / combine restated in numpy."""
 
-    def __init__(self, cfg, w_r, bias, experts, placement, rank):
+    def __init__(self, cfg, w_r, bias, experts, placement, rank, replica_of=()):
         self.cfg, self.w_r, self.bias = cfg, w_r, bias
         self.placement = np.asarray(placement)
         self.n_ranks = len(np.unique(self.placement))
         self.local = ep.local_slots(placement)
-        self.my = np.nonzero(self.placement == rank)[0]          # global ids of local slots
+        self.my = np.nonzero(self.placement == rank)[0]          # (virtual) ids of local slots
         self.shared_slot = len(self.my)
         self.k = cfg.topk
         self.partial_dtype = torch.float64
@@ -35,7 +35,9 @@ class NumpyBackend:
         def mats(e):
             return (orc.q8_0_expert_inout(experts[0][e], I, H), orc.q8_0_expert_inout(experts[1][e], I, H),
                     orc.q8_0_expert_inout(experts[2][e], H, I))
-        self.mats = {int(e): mats(e) for e in self.my}
+        def real(e):                                             # copy E + j holds replica_of[j]
+            return int(e) if e < E else int(replica_of[e - E])
+        self.mats = {int(e): mats(real(e)) for e in self.my}
         self.mats[-1] = mats(E)                                  # shared
 
     def route(self, x):
@@ -117,6 +119,50 @@ def test_placements():
     assert max(tot) - min(tot) <= 40
     assert ep.contiguous_placement(8, 4).tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
     assert ep.local_slots(np.array([1, 0, 1, 0])).tolist() == [0, 0, 1, 1]
+
+
+def test_replicated_placement_and_split():
+    cfg = synth.config("c4p")
+    _, _, routers = synth.stack_inputs(cfg, 1)
+    load = routers[0][2]
+    E, W = cfg.n_experts, 8
+    pv, hot = ep.replicated_placement(load, W)
+    assert pv.shape == (E + W,) and np.bincount(pv).tolist() == [(E + W) // W] * W
+    cost = load + 1.4 * 128 * np.ceil(load / 128)
+    assert sorted(hot.tolist()) == sorted(np.argsort(-cost, kind="stable")[:W].tolist())
+    assert all(pv[h] != pv[E + j] for j, h in enumerate(hot))      # each copy on another rank
+
+    def tile_cost(ld):                                              # prefill work per expert
+        return np.ceil(ld / 128) * 752 + np.ceil(ld / 256) * 562
+
+    def spread(placement, ld):
+        per = np.array([tile_cost(ld)[placement == r].sum() for r in range(W)])
+        return per.max() / per.mean()
+    vload = np.concatenate([load, np.zeros(W)])
+    vload[hot] = load[hot] / 2
+    vload[E:] = load[hot] / 2
+    assert spread(pv, vload) < spread(ep.balanced_placement(load, W), load) - 0.05
+    # split: the odd tokens' lanes of a replicated expert move to its copy, nothing else changes
+    idx = torch.tensor([[int(hot[0]), 5], [int(hot[0]), 6], [7, int(hot[1])], [8, int(hot[1])]], dtype=torch.int32)
+    got = ep.split_replicas(idx, hot, E)
+    want = idx.clone()
+    want[1, 0] = E + 0
+    want[3, 1] = E + 1
+    assert torch.equal(got, want)
+    assert torch.equal(ep.split_replicas(idx, np.zeros(0, np.int32), E), idx)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_virtual_ranks_with_replicas_match_single_device_oracle(world):
+    cfg, x, w_r, bias, experts, _ = _setup(world)
+    idx_all, _ = orc.route(x, w_r, bias, cfg.topk)
+    pv, hot = ep.replicated_placement(np.bincount(idx_all.reshape(-1), minlength=cfg.n_experts), world)
+    shards = np.array_split(np.arange(cfg.tokens), world)
+    ranks = [ep.EpRank(r, world, NumpyBackend(cfg, w_r, bias, experts, pv, r, replica_of=hot), replica_of=hot,
+                       n_experts=cfg.n_experts) for r in range(world)]
+    outs = ep.ep_forward_virtual(ranks, [torch.from_numpy(x[s]) for s in shards], ep.VirtualTransport(world))
+    got = np.concatenate([o.numpy() for o in outs])
+    np.testing.assert_allclose(got, _reference(cfg, x, w_r, bias, experts), rtol=0, atol=1e-6)
 
 
 @pytest.mark.parametrize("world", [2, 4])

@@ -21,7 +21,7 @@ from helpers import rel_l2, run_ranks, guarded
 pytestmark = pytest.mark.gpu
 
 
-def _layers(cfg, dev, w_r, bias, placement, world, partial_dtype=torch.float32):
+def _layers(cfg, dev, w_r, bias, placement, world, partial_dtype=torch.float32, replica_of=None):
     E = cfg.n_experts
     kw = dict(hidden=cfg.hidden, inter=cfg.inter, n_experts=E, topk=cfg.topk, router_w=torch.from_numpy(w_r).cuda(),
               router_bias=torch.from_numpy(bias).cuda(), x_dtype=torch.bfloat16 if cfg.x_dtype == "bf16" else torch.float32,
@@ -29,10 +29,10 @@ def _layers(cfg, dev, w_r, bias, placement, world, partial_dtype=torch.float32):
     full = MoELayer(gate=dev[0][:E], up=dev[1][:E], down=dev[2][:E], shared=(dev[0][E], dev[1][E], dev[2][E]), **kw)
     per = []
     for r in range(world):
-        g, u, d, sh = ep.rank_experts(dev, placement, r)
-        L = MoELayer(gate=g, up=u, down=d, shared=sh, n_local_experts=E // world, **kw)
+        g, u, d, sh = ep.rank_experts(dev, placement, r, replica_of)
+        L = MoELayer(gate=g, up=u, down=d, shared=sh, n_local_experts=len(placement) // world, **kw)
         per.append(ep.EpRank(r, world, ep.GpuBackend(L, placement, world, out_dtype=torch.float32,
-                                                     partial_dtype=partial_dtype)))
+                                                     partial_dtype=partial_dtype), replica_of=replica_of, n_experts=E))
     return full, per
 
 
@@ -62,6 +62,28 @@ def test_virtual_ranks_match_single_gpu(cfg_name, world, T, partial):
         r.b.layer.check_device_error()
     print(f"[ep virtual {cfg_name} N={world} T={T} {partial} partials] rel-L2 vs single GPU {rel_l2(got, ref):.3e}")
     assert rel_l2(got, ref) < (1e-4 if partial == "f32" else 5e-4)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_virtual_ranks_with_replicated_experts_match_single_gpu(world):
+    """The hottest experts copied to a second rank (replicated_placement); odd tokens' lanes
+    go to the copies.  Same result as the fused single-GPU forward up to fp32 lane order."""
+    moe.init(0)
+    cfg = synth.config("c1", tokens=64)
+    x, w_r, bias, rng = synth.router_inputs(cfg)
+    dev = synth.expert_q8_cuda(cfg, quantizer)
+    idx_all, _ = orc.route(x, w_r, bias, cfg.topk)
+    pv, hot = ep.replicated_placement(np.bincount(idx_all.reshape(-1), minlength=cfg.n_experts), world)
+    full, ranks = _layers(cfg, dev, w_r, bias, pv, world, torch.float32, replica_of=hot)
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    ref = full.forward(xd).cpu().numpy()
+    shards = np.array_split(np.arange(cfg.tokens), world)
+    outs = ep.ep_forward_virtual(ranks, [xd[s[0]:s[-1] + 1].contiguous() for s in shards], ep.VirtualTransport(world))
+    got = torch.cat(outs).cpu().numpy()
+    for r in ranks:
+        r.b.layer.check_device_error()
+    print(f"[ep virtual replicas N={world}] rel-L2 vs single GPU {rel_l2(got, ref):.3e}")
+    assert rel_l2(got, ref) < 1e-4
 
 
 def _free_port():

@@ -23,6 +23,9 @@ The GPU compute is libvfmoe. The all-to-all is a `Transport`:
 - `DistTransport`: torch.distributed over NCCL (NVLink/NVSwitch), or gloo on CPU.
 - `VirtualTransport`: N virtual ranks held by one process. The whole multi-rank data path
   (plans, packing, per-rank expert sets, exchange order) then runs on one GPU.
+
+Hot experts can be replicated (`replicated_placement`, `split_replicas`): a copy on a second
+rank takes the odd tokens' lanes, so no rank carries a whole hottest expert.
 """
 
 from __future__ import annotations
@@ -62,6 +65,64 @@ def balanced_placement(load, n_ranks: int, tile_rows: int = 128, tile_cost: floa
         tot[r] += cost[e]
         room[r] -= 1
     return owner
+
+
+def replicated_placement(load, n_ranks: int, n_replicas: int | None = None, tile_rows: int = 128,
+                         tile_cost: float = 1.4):
+    """Placement of E + R virtual experts in which the R most expensive experts have a copy.
+
+    Virtual expert E + j is a copy of expert hot[j]; `split_replicas` sends the lanes of hot[j]
+    from odd-numbered tokens to the copy, so each copy carries about half of the expert's rows.
+    A prefill work item costs about the same whatever its row count, so an expert's cost grows
+    with its token tiles, and the rank holding the hottest expert caps an 8-GPU step however
+    the rest is packed; splitting that expert removes the cap.  Copies go to the least-loaded
+    rank other than their sibling's (greedy bin packing as balanced_placement, each rank
+    holding exactly (E + R) / n_ranks virtual experts).
+    Returns (placement int32 [E + R], replica_of int32 [R]).  R defaults to n_ranks."""
+    load = np.asarray(load, dtype=np.float64)
+    E = load.shape[0]
+    R = n_ranks if n_replicas is None else int(n_replicas)
+    if R < 0 or R > E or (E + R) % n_ranks:
+        raise ValueError("n_experts + n_replicas must be divisible by n_ranks")
+    cost = load + tile_cost * tile_rows * np.ceil(load / tile_rows)
+    hot = np.argsort(-cost, kind="stable")[:R].astype(np.int32)
+    vload = np.concatenate([load, np.zeros(R)])
+    sibling = np.full(E + R, -1, dtype=np.int64)
+    for j, h in enumerate(hot):
+        vload[h] = vload[E + j] = load[h] / 2
+        sibling[h], sibling[E + j] = E + j, h
+    vcost = vload + tile_cost * tile_rows * np.ceil(vload / tile_rows)
+    cap = (E + R) // n_ranks
+    owner = np.full(E + R, -1, dtype=np.int32)
+    tot = np.zeros(n_ranks)
+    room = np.full(n_ranks, cap)
+    for v in np.argsort(-vcost, kind="stable"):
+        avoid = owner[sibling[v]] if sibling[v] >= 0 else -1
+        cands = [r for r in range(n_ranks) if room[r] > 0 and r != avoid]
+        if not cands:  # only the sibling's rank has room left: both halves on one rank
+            cands = [r for r in range(n_ranks) if room[r] > 0]
+        r = min(cands, key=lambda r: (tot[r], r))
+        owner[v] = r
+        tot[r] += vcost[v]
+        room[r] -= 1
+    return owner, hot
+
+
+def split_replicas(idx: torch.Tensor, replica_of, n_experts: int) -> torch.Tensor:
+    """Routing ids over the virtual experts of replicated_placement: lane (t, l) of expert
+    replica_of[j] goes to its copy n_experts + j when the token index t is odd.  idx int32
+    [T, k] (any device).  The weights are unchanged: the combined output is the same sum, its
+    partials possibly added in another rank order."""
+    R = len(replica_of)
+    if R == 0:
+        return idx
+    dev = idx.device
+    copy_of = torch.full((n_experts,), -1, dtype=torch.int32, device=dev)
+    copy_of[torch.as_tensor(np.asarray(replica_of), dtype=torch.long, device=dev)] = torch.arange(
+        n_experts, n_experts + R, dtype=torch.int32, device=dev)
+    cand = copy_of[idx.long()]
+    odd = (torch.arange(idx.shape[0], device=dev) % 2 == 1)[:, None]
+    return torch.where((cand >= 0) & odd, cand, idx)
 
 
 def local_slots(placement: np.ndarray) -> np.ndarray:
@@ -133,14 +194,20 @@ class EpRank:
       (also the shared expert: one lane with slot shared_slot, weight 1)
       combine(y_back, pos_of, T, y_shared) -> out
       shared_slot, k
-    `GpuBackend` is the libvfmoe one.
+    `GpuBackend` is the libvfmoe one.  With replica_of (replicated_placement), the backend's
+    placement covers the E + R virtual experts and its layer holds the local ones.
     """
 
-    def __init__(self, rank: int, world: int, backend):
+    def __init__(self, rank: int, world: int, backend, replica_of=None, n_experts: int = 0):
         self.rank, self.world, self.b = rank, world, backend
+        # replicated experts (replicated_placement): the routing ids are split over the copies
+        self.replica_of = np.asarray(replica_of if replica_of is not None else [], dtype=np.int32)
+        self.n_experts = n_experts
 
     def phase1(self, x):
         idx, w = self.b.route(x)
+        if len(self.replica_of):
+            idx = split_replicas(idx, self.replica_of, self.n_experts)
         counts, tok, slot, sw, pos = self.b.plan(idx, w)
         return dict(x=x, counts=counts, tok=tok, slot=slot, sw=sw, pos=pos)
 
@@ -221,7 +288,7 @@ class GpuBackend:
         from . import moe
         self.moe = moe
         self.layer = layer
-        self.E, self.k = layer.E, layer.k
+        self.E, self.k = len(placement), layer.k  # routed ids, copies of replicated experts included
         self.n_ranks = n_ranks
         self.placement = torch.as_tensor(np.asarray(placement, np.int32)).cuda()
         self.local_slot = torch.as_tensor(local_slots(placement)).cuda()
@@ -246,10 +313,18 @@ class GpuBackend:
                                 out_dtype=self.out_dtype)
 
 
-def rank_experts(dev, placement, rank: int):
+def rank_experts(dev, placement, rank: int, replica_of=None):
     """Stacked Q8_0 matrices of the experts `rank` owns (ascending expert id) from full
-    [E+1, rows, bytes] stacks (last = shared).  Returns (gate, up, down, shared tuple)."""
-    E = len(placement)
-    ids = torch.as_tensor(np.nonzero(np.asarray(placement) == rank)[0], device=dev[0].device)
+    [E+1, rows, bytes] stacks (last = shared).  With replica_of, placement covers E + R
+    virtual experts and copy E + j holds expert replica_of[j]'s weights.
+    Returns (gate, up, down, shared tuple)."""
+    P = np.asarray(placement)
+    R = 0 if replica_of is None else len(replica_of)
+    E = len(P) - R
+    v = np.nonzero(P == rank)[0]
+    real = v.copy()
+    if R:
+        real[v >= E] = np.asarray(replica_of)[v[v >= E] - E]
+    ids = torch.as_tensor(real, device=dev[0].device)
     return (dev[0][ids].contiguous(), dev[1][ids].contiguous(), dev[2][ids].contiguous(),
             (dev[0][E], dev[1][E], dev[2][E]))
