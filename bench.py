@@ -63,8 +63,9 @@ def args_parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the extra T=1 and prefill measurements")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
-    ap.add_argument("--ep-replicas", type=int, default=0,
-                    help="C4 at N > 1: copies of the hottest experts on other ranks (0 = none; a multiple of N)")
+    ap.add_argument("--ep-replicas", type=int, default=-1,
+                    help="C4 at N > 1: copies of the hottest experts on other ranks (a multiple of N; 0 = none; "
+                         "-1 = N copies at N >= 8, where one rank would otherwise carry a whole hottest expert)")
     ap.add_argument("--q8-layout", default="tiled", choices=["tiled", "rows"],
                     help="Q8_0 weights in HBM: stage-tiled (converted once at load, outside the timed "
                          "region) or GGUF row order")
@@ -412,7 +413,8 @@ def stack_extra(a, rank, world, local_rank, flush):
     xp, norm_p, routers_p = synth.stack_inputs(cfgp, L)
     xd, norm_d, routers_d = synth.stack_inputs(cfgd, L)
     E, H, I, k = cfgp.n_experts, cfgp.hidden, cfgp.inter, cfgp.topk
-    n_rep = a.ep_replicas if world > 1 else 0
+    n_rep = (world if world >= 8 else 0) if a.ep_replicas < 0 else a.ep_replicas
+    n_rep = n_rep if world > 1 else 0
     if n_rep:
         placed = [ep.replicated_placement(routers_p[l][2], world, n_rep) for l in range(L)]
         placements, replicas = [p_ for p_, _ in placed], [h for _, h in placed]
