@@ -123,9 +123,9 @@ def test_placements():
 
 def test_replicated_placement_and_split():
     cfg = synth.config("c4p")
-    _, _, routers = synth.stack_inputs(cfg, 1)
-    load = routers[0][2]
     E, W = cfg.n_experts, 8
+    # expected selection counts of a C4-prefill layer (Zipf(1.1), T = 8192, top-8)
+    load = np.round(synth.zipf_targets(E, cfg.tokens, cfg.topk, cfg.zipf_s, np.random.default_rng(3)))
     pv, hot = ep.replicated_placement(load, W)
     assert pv.shape == (E + W,) and np.bincount(pv).tolist() == [(E + W) // W] * W
     cost = load + 1.4 * 128 * np.ceil(load / 128)
