@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define VFMOE_ABI_VERSION 1
+#define VFMOE_ABI_VERSION 2
 
 /* status codes */
 #define VFMOE_OK 0
@@ -68,8 +68,20 @@ extern "C" {
  * [rows][K] is tiles of 64 rows x 256 K, 64 x 272 B each (every tile row = that row's 8
  * GGUF blocks), tile (rt, kr) at byte ((rt * K/256) + kr) * 17408.  Same size, expert
  * strides and values as GGUF rows; the expert kernels stream one tile as one contiguous
- * copy.  Not accepted by the SIMT path (VFMOE_DISABLE_TC). */
+ * copy.  Not accepted by the SIMT path (VFMOE_PATH_SIMT). */
 #define VFMOE_WFMT_Q8_0_TILED 3
+
+/* Expert-product kernels (vfmoe_layer_desc.expert_path).  AUTO picks per call: the decode GEMV
+ * (register-operand tensor-core MMAs) while the routed rows average at most 16 per expert, the
+ * tcgen05 grouped GEMM above that; fp32 activations (x_dtype F32) always take the decode GEMV in its
+ * split-precision form (fp16 hi + lo operand planes, about fp32 accuracy).  The other values force
+ * one kernel family for every call: TC the tcgen05 GEMM (fp16 operands, also for fp32 x), GEMV the
+ * decode GEMV, SIMT the plain-SIMT kernels that the tensor-core paths are checked against (GGUF
+ * row order only).  EXL3 layers choose between their own GEMV and GEMM by the same row rule. */
+#define VFMOE_PATH_AUTO 0
+#define VFMOE_PATH_SIMT 1
+#define VFMOE_PATH_TC 2
+#define VFMOE_PATH_GEMV 3
 
 /* One projection (gate, up or down) of a stack of experts.  Expert e's data
  * starts at data + e * expert_stride (bytes); for EXL3 its suh/svh start at
@@ -103,6 +115,7 @@ typedef struct vfmoe_layer_desc {
     vfmoe_matrix sh_gate, sh_up, sh_down; /* shared expert; sh_gate.data == 0: none */
     int64_t n_local_experts; /* routed experts whose weights gate/up/down hold; 0 = n_experts.
                                 Fewer on an expert-parallel rank (vfmoe_forward_rows only). */
+    int64_t expert_path;     /* VFMOE_PATH_*; 0 = AUTO */
 } vfmoe_layer_desc;
 
 /* ABI version (VFMOE_ABI_VERSION). */
@@ -155,6 +168,18 @@ int vfmoe_route_noalloc(int64_t handle, int64_t x, int64_t T, int64_t idx_out, i
 int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out,
                   int64_t idx_out, int64_t w_out,
                   int64_t workspace, int64_t ws_bytes, int64_t stream);
+
+/* The dispatch step of vfmoe_forward on its own: the canonical permutation of the T*k routed
+ * (token, lane) pairs, experts ascending and tokens ascending within an expert (the host gather
+ * of native/glm53/glm_engine.vyb:2827-2845).  Same kernels as inside vfmoe_forward.
+ *   idx      int32 [T, k] expert ids in [0, n_experts)
+ *   counts   int32 [n_experts + 2]: per-expert row counts (scratch and output)
+ *   offsets  int32 [n_experts + 2]: expert e's rows are [offsets[e], offsets[e+1]); offsets[E] = T*k
+ *   perm_tok int32 [T*k]: token of each permuted row
+ *   pos_of   int32 [T*k]: permuted row of lane (t, l) at t*k + l (-1 for an id out of range)
+ * err_word: device int that records an id out of range (DEV_BAD_EXPERT_ID = 1), may be 0. */
+int vfmoe_dispatch(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t counts, int64_t offsets,
+                   int64_t perm_tok, int64_t pos_of, int64_t err_word, int64_t stream);
 
 /* ---- expert parallelism (no counterpart in the reference, which has no multi-GPU code;
  * the exchange itself is NCCL all-to-all between these calls) ---- */
@@ -212,6 +237,17 @@ int64_t vfmoe_routed_workspace_bytes(int64_t handle, int64_t n_max, int64_t k);
 int vfmoe_forward_routed(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t n, int64_t k, int64_t slots,
                          int64_t w, int64_t y_out, int64_t y_dtype, int64_t workspace, int64_t ws_bytes,
                          int64_t stream);
+
+/* Failure injection for tests of the device-error path (no counterpart in the reference, whose
+ * drivers only check CUresult codes).  kind VFMOE_INJECT_STALL_LOADS makes the Q8_0 decode GEMV's
+ * producer warp issue no weight or token loads, so every consumer's bounded wait for its first
+ * stage expires after wait_ns (nothing is in flight when it does); the kernels raise
+ * DEV_WAIT_TIMEOUT (2) in the device error word and return, vfmoe_check_device_error then
+ * reports VFMOE_ERR_DEVICE, and the output of that call is undefined.  wait_ns = 0 keeps the
+ * production bound (2 s).  VFMOE_INJECT_NONE restores normal operation. */
+#define VFMOE_INJECT_NONE 0
+#define VFMOE_INJECT_STALL_LOADS 1
+int vfmoe_debug_inject(int64_t handle, int64_t kind, int64_t wait_ns);
 
 /* Synchronize `stream` and report whether any kernel of this handle flagged a
  * device-side error since the last call (VFMOE_ERR_DEVICE), then clear it. */

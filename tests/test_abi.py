@@ -41,21 +41,24 @@ def test_python_binding_covers_header():
 
 def test_constants_match_header():
     d = header_defines()
-    assert d["VFMOE_ABI_VERSION"] == 1
+    assert d["VFMOE_ABI_VERSION"] == _lib.ABI_VERSION == 2
     for k in ("OK", "ERR_INVALID", "ERR_CUDA", "ERR_NOMEM", "ERR_HANDLE", "ERR_WORKSPACE", "ERR_DEVICE",
               "ERR_UNSUPPORTED", "ERR_NCCL"):
         assert d["VFMOE_" + k] == getattr(_lib, k)
     assert (d["VFMOE_DT_F32"], d["VFMOE_DT_F16"], d["VFMOE_DT_BF16"]) == (0, 1, 2)  # native/dtype/dtype.vyb
     assert (d["VFMOE_WFMT_Q8_0"], d["VFMOE_WFMT_EXL3"]) == (_lib.WFMT_Q8_0, _lib.WFMT_EXL3)
+    assert (d["VFMOE_PATH_AUTO"], d["VFMOE_PATH_SIMT"], d["VFMOE_PATH_TC"], d["VFMOE_PATH_GEMV"]) == (
+        _lib.PATH_AUTO, _lib.PATH_SIMT, _lib.PATH_TC, _lib.PATH_GEMV)
+    assert (d["VFMOE_INJECT_NONE"], d["VFMOE_INJECT_STALL_LOADS"]) == (_lib.INJECT_NONE, _lib.INJECT_STALL_LOADS)
 
 
 def test_descriptor_is_a_block_of_8_byte_words():
     assert C.sizeof(_lib.Matrix) == 6 * 8
-    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6 + 1) * 8
+    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6 + 2) * 8
 
 
 def test_version(built_lib):
-    assert built_lib.vfmoe_version() == 1
+    assert built_lib.vfmoe_version() == 2
 
 
 def _desc(**kw):

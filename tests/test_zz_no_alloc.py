@@ -81,3 +81,54 @@ def test_noalloc_route_rejects_sizes_beyond_its_scratch(routing_layer):
                                        int(w.data_ptr()), _stream())
     assert rc == _lib.ERR_UNSUPPORTED
     assert "static scratch" in _lib.last_error()
+
+
+def test_noalloc_route_limit_is_t127_at_c1_shapes(routing_layer):
+    """The documented limit at E = 256, H = 6144: T = 127 fits the scratch and routes like
+    vfmoe_route; T = 128 is rejected before anything is launched."""
+    layer, x, cfg = routing_layer
+    g = torch.Generator(device="cuda").manual_seed(127)
+    x127 = torch.randn((127, cfg.hidden), generator=g, device="cuda").to(torch.bfloat16)
+    idx_ref, w_ref = layer.route(x127)
+    idx, w = _route_noalloc(layer, x127, 127)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(idx.cpu().numpy(), idx_ref.cpu().numpy())
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref.cpu().numpy(), rtol=0, atol=1e-6)
+    x128 = torch.zeros((128, cfg.hidden), dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty((128, layer.k), dtype=torch.int32, device="cuda")
+    w = torch.empty((128, layer.k), dtype=torch.float32, device="cuda")
+    rc = layer.lib.vfmoe_route_noalloc(layer.handle, int(x128.data_ptr()), 128, int(idx.data_ptr()),
+                                       int(w.data_ptr()), _stream())
+    assert rc == _lib.ERR_UNSUPPORTED
+    assert "static scratch" in _lib.last_error()
+
+
+def test_noalloc_route_hidden_not_multiple_of_512():
+    """H = 1280 is a multiple of 256 but of neither 768 nor 512, so even at T <= 32 the tiled
+    logits kernel runs with its own K-slice count; the scratch sizing must use that count.
+    Both entry points against the f64 oracle, two calls in a row."""
+    from oracle import moe_oracle as orc
+    init(0)
+    rng = np.random.default_rng(1280)
+    H, E, k, T = 1280, 256, 8, 24
+    from vybforge_b200.quant import round_bf16
+    x = round_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    w_r = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    bias = rng.normal(0, 0.01, E).astype(np.float32)
+    I = 256
+    gu = torch.zeros((E, I, H // 32 * 34), dtype=torch.uint8, device="cuda")
+    dn = torch.zeros((E, H, I // 32 * 34), dtype=torch.uint8, device="cuda")
+    layer = MoELayer(hidden=H, inter=I, n_experts=E, topk=k, router_w=torch.from_numpy(w_r).cuda(),
+                     router_bias=torch.from_numpy(bias).cuda(), gate=gu, up=gu, down=dn,
+                     x_dtype=torch.bfloat16, out_dtype=torch.float32)
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    ri, rw = orc.route(x, w_r, bias, k)
+    for _ in range(2):
+        idx_ws, w_ws = layer.route(xd)
+        idx, w = _route_noalloc(layer, xd, T)
+        torch.cuda.synchronize()
+        for a, b in ((idx_ws, w_ws), (idx, w)):
+            np.testing.assert_array_equal(a.cpu().numpy(), ri)
+            np.testing.assert_allclose(b.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    layer.check_device_error()
+    layer.close()

@@ -28,6 +28,11 @@ ERR_NCCL = -8
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # weight formats
 WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED = 1, 2, 3
+# expert kernel families (vfmoe_layer_desc.expert_path)
+PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV = 0, 1, 2, 3
+# failure injection (vfmoe_debug_inject)
+INJECT_NONE, INJECT_STALL_LOADS = 0, 1
+ABI_VERSION = 2
 
 
 class VfmoeError(RuntimeError):
@@ -47,7 +52,8 @@ class LayerDesc(C.Structure):
                 ("out_dtype", C.c_int64), ("routed_scale", C.c_double), ("swiglu_limit", C.c_double),
                 ("router_w", C.c_int64), ("router_bias", C.c_int64),
                 ("gate", Matrix), ("up", Matrix), ("down", Matrix),
-                ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix), ("n_local_experts", C.c_int64)]
+                ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix), ("n_local_experts", C.c_int64),
+                ("expert_path", C.c_int64)]
 
 
 I64 = C.c_int64
@@ -62,6 +68,8 @@ _SIGS = {
     "vfmoe_route_noalloc": (C.c_int, [I64] * 6),
     "vfmoe_forward": (C.c_int, [I64] * 9),
     "vfmoe_check_device_error": (C.c_int, [I64, I64]),
+    "vfmoe_dispatch": (C.c_int, [I64] * 10),
+    "vfmoe_debug_inject": (C.c_int, [I64, I64, I64]),
     "vfmoe_rows_workspace_bytes": (I64, [I64, I64]),
     "vfmoe_forward_rows": (C.c_int, [I64] * 9),
     "vfmoe_ep_plan": (C.c_int, [I64] * 11),
@@ -88,13 +96,18 @@ def load():
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m vybforge_b200.build` "
-                               "(there is no CPU fallback for the MoE path)")
+            # a checkout without the built library compiles it from csrc/ (nvcc, sm_100a); a
+            # failed build raises: there is no CPU fallback for the MoE path
+            from . import build
+            build.build()
         lib = C.CDLL(LIB_PATH)
         for name, (res, args) in _SIGS.items():
             f = getattr(lib, name)
             f.restype = res
             f.argtypes = args
+        if lib.vfmoe_version() != ABI_VERSION:
+            raise RuntimeError(f"{LIB_PATH} has ABI version {lib.vfmoe_version()}, this binding expects "
+                               f"{ABI_VERSION}: rebuild with `python -m vybforge_b200.build`")
         _lib = lib
     return _lib
 

@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -18,6 +20,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "expert_tc.h"
+#include "layer.h"
 
 namespace vfmoe {
 
@@ -37,27 +40,18 @@ int cuda_fail(cudaError_t e, const char *what, const char *file, int line) {
     return e == cudaErrorMemoryAllocation ? VFMOE_ERR_NOMEM : VFMOE_ERR_CUDA;
 }
 
-struct Layer {
-    vfmoe_layer_desc d;
-    int device = 0;
-    int H = 0, I = 0, E = 0, k = 0;
-    int n_local = 0;             // routed experts whose weights this handle holds (E unless expert-parallel)
-    int has_shared = 0;
-    int64_t q8_row_gate = 0, q8_row_down = 0;
-    int *dev_err = nullptr;      // device error word (allocated at create)
-    float *nw = nullptr;         // |W_r row|_2 upper bounds (allocated at create)
-    void *own_ws = nullptr;      // internal workspace when the caller passes none
-    int64_t own_ws_bytes = 0;
-    TcPlan tc;                   // tensor-core launch state (tensor maps)
-    Exl3Plan x3;                 // EXL3 trellis tensor maps
-    int use_tc = 1;
-    // profiling (vfmoe_profile_enable / vfmoe_profile_read)
-    int prof = 0;
-    std::vector<cudaEvent_t> ev_pool;         // free events
-    std::vector<std::vector<cudaEvent_t>> ev_pending;  // per forward: kNumStages + 1 events
-    double stage_ms[8] = {0};
-    int64_t n_fwd = 0, launches = 0;
-};
+int set_smem_attr_once(const void *func, int bytes) {
+    static std::mutex mu;
+    static std::set<std::tuple<const void *, int, int>> done;
+    int dev = 0;
+    VF_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({func, dev, bytes})) return VFMOE_OK;
+    VF_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert({func, dev, bytes});
+    return VFMOE_OK;
+}
+
 
 static constexpr int kNumStages = 5;
 
@@ -76,7 +70,7 @@ static std::mutex g_mu;
 static std::unordered_map<int64_t, Layer *> g_layers;
 static int64_t g_next_handle = 1;
 
-static Layer *get_layer(int64_t h) {
+Layer *get_layer(int64_t h) {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_layers.find(h);
     if (it == g_layers.end()) {
@@ -87,11 +81,15 @@ static Layer *get_layer(int64_t h) {
 }
 
 // ----------------------------------------------------------------------------- workspace
-struct WsLayout {
-    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, tiles, tile_counts, tiles_cap, total;
-};
 
-static WsLayout ws_layout(const Layer &L, int64_t T, int k = -1) {
+// Q8_0 layers with fp32 activations run the split-precision decode GEMV (unless the descriptor
+// forces the tcgen05 or SIMT kernels).
+int layer_prec(const Layer &L) {
+    return L.d.x_dtype == VFMOE_DT_F32 && L.d.weight_format != VFMOE_WFMT_EXL3 &&
+           L.d.expert_path != VFMOE_PATH_TC && L.d.expert_path != VFMOE_PATH_SIMT;
+}
+
+WsLayout ws_layout(const Layer &L, int64_t T, int k) {
     WsLayout o{};
     if (k < 0) k = L.k;
     const int64_t rows = T * k + T;
@@ -109,9 +107,11 @@ static WsLayout ws_layout(const Layer &L, int64_t T, int k = -1) {
     o.idx = take(T * k * 4);
     o.w = take(T * k * 4);
     o.part = take(router_logit_floats((int)T, L.H, L.E) * 4);
-    // EXL3 keeps two rotated copies of every row (gate and up input bases)
-    o.xp = take(rows * L.H * 2 * (L.d.weight_format == VFMOE_WFMT_EXL3 ? 2 : 1));
-    o.act = take(rows * L.I * 2);
+    // EXL3 keeps two rotated copies of every row (gate and up input bases); fp32 activations on
+    // Q8_0 keep two fp16 planes of every row of xp and act (split-precision decode GEMV)
+    const int prec = layer_prec(L);
+    o.xp = take(rows * L.H * 2 * (L.d.weight_format == VFMOE_WFMT_EXL3 || prec ? 2 : 1));
+    o.act = take(rows * L.I * 2 * (prec ? 2 : 1));
     o.y = take(rows * L.H * 4);
     o.tiles_cap = tc_tiles_capacity((int)T, k, L.n_local > L.E ? L.n_local : L.E);
     o.tiles = take(2 * o.tiles_cap * 16);
@@ -120,7 +120,7 @@ static WsLayout ws_layout(const Layer &L, int64_t T, int k = -1) {
     return o;
 }
 
-static int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **base, int k = -1) {
+int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **base, int k) {
     const WsLayout lay = ws_layout(L, T, k);
     if (ws) {
         if (ws_bytes < lay.total) {
@@ -146,7 +146,7 @@ static int ensure_ws(Layer &L, int64_t T, int64_t ws, int64_t ws_bytes, char **b
     return VFMOE_OK;
 }
 
-static MatrixRef mref(const vfmoe_matrix &m) {
+MatrixRef mref(const vfmoe_matrix &m) {
     MatrixRef r;
     r.data = reinterpret_cast<const uint8_t *>(m.data);
     r.expert_stride = m.expert_stride;
@@ -322,7 +322,9 @@ int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max) {
     return ws_layout(*L, t_max).total;
 }
 
-static int route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout &lay, int32_t **idx_p,
+}  // extern "C"
+
+int vfmoe::route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout &lay, int32_t **idx_p,
                       float **w_p, cudaStream_t st) {
     int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
     VF_CUDA(cudaMemsetAsync(counts, 0, (L.E + 2) * sizeof(int32_t), st));
@@ -338,6 +340,8 @@ static int route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout
     return rc;
 }
 
+extern "C" {
+
 int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out, int64_t workspace,
                 int64_t ws_bytes, int64_t stream) {
     Layer *L = get_layer(handle);
@@ -347,6 +351,10 @@ int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w
         return VFMOE_ERR_INVALID;
     }
     if (T == 0) return VFMOE_OK;
+    if (T > (int64_t)1 << 24) {
+        set_error("vfmoe_route: T=%lld exceeds 2^24", (long long)T);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
     char *base;
     int rc = ensure_ws(*L, T, workspace, ws_bytes, &base);
     if (rc) return rc;
@@ -359,11 +367,11 @@ int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w
 }  // extern "C"
 
 // Q8_0 expert products on gathered fp16 rows: tensor-core path (decode GEMV or tcgen05
-// grouped GEMM) unless the handle was created with VFMOE_DISABLE_TC (SIMT reference path).
+// grouped GEMM) unless the descriptor asks for the SIMT kernels (VFMOE_PATH_SIMT).
 static int forward_experts(Layer &L, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
                            int64_t &nlaunch) {
     int rc;
-    if (L.use_tc && tc_supported(L.tc, a)) {
+    if (tc_supported(L.tc, a)) {
         rc = launch_experts_tc(L.tc, a, st, mid);
         nlaunch += 3;
     } else if (a.fmt == VFMOE_WFMT_Q8_0_TILED) {
@@ -428,6 +436,9 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.fmt = (int)L->d.weight_format;
     a.exl3_bits = (int)L->d.exl3_bits;
     a.limit = (float)L->d.swiglu_limit;
+    a.prec = layer_prec(*L);
+    a.wait_ns = L->wait_ns;
+    a.inject = L->inject;
     a.gate = mref(L->d.gate);
     a.up = mref(L->d.up);
     a.down = mref(L->d.down);
@@ -459,8 +470,10 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
                                  [&]() { mark(); });
         nlaunch += 4;
     } else {
-        rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, rows, L->H,
-                           reinterpret_cast<__half *>(base + lay.xp), offsets + L->E + 1, st);
+        // launch bound T*k + T whether or not there is a shared expert: the second plane of a
+        // split-precision layer starts at that row count, as the expert kernels expect
+        rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, T * L->k + T, L->H,
+                           reinterpret_cast<__half *>(base + lay.xp), offsets + L->E + 1, st, a.prec ? 2 : 1);
         if (rc) return rc;
         nlaunch += 2;
         mark();
@@ -530,7 +543,7 @@ int64_t vfmoe_rows_workspace_bytes(int64_t handle, int64_t n_max) {
 // Expert products on caller-provided rows with caller-provided routing: slots [n, k] are
 // local expert slots (n_local = the shared expert; < 0 = no expert when skip_negative),
 // w [n, k] their weights (0 = weight 1).  y_out[i] = sum_l w[i,l] * FFN_{slots[i,l]}(rows[i]).
-static int rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *sl, int64_t n, int k, const float *w,
+int vfmoe::rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *sl, int64_t n, int k, const float *w,
                      int64_t y_out, int y_dtype, int skip_negative, int64_t workspace, int64_t ws_bytes,
                      cudaStream_t st) {
     if (n == 0) return VFMOE_OK;
@@ -551,7 +564,8 @@ static int rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *
     int32_t *pos_of = reinterpret_cast<int32_t *>(base + lay.pos_of);
     VF_CUDA(cudaMemsetAsync(counts, 0, (nb + 2) * sizeof(int32_t), st));
     if ((rc = launch_count(sl, n * k, nb, counts, L.dev_err, st, skip_negative))) return rc;
-    if (skip_negative) VF_CUDA(cudaMemsetAsync(pos_of, 0xFF, n * k * sizeof(int32_t), st));  // -1: no row
+    // -1: no row (a lane with no expert, or a slot out of range that the count flagged)
+    VF_CUDA(cudaMemsetAsync(pos_of, 0xFF, n * k * sizeof(int32_t), st));
     if ((rc = launch_dispatch(sl, counts, (int)n, nb, k, 0, perm_tok, pos_of, offsets, L.dev_err, st))) return rc;
     MoeArgs a{};
     a.T = (int)n;
@@ -563,6 +577,9 @@ static int rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *
     a.fmt = (int)L.d.weight_format;
     a.exl3_bits = (int)L.d.exl3_bits;
     a.limit = (float)L.d.swiglu_limit;
+    a.prec = layer_prec(L) && rows_dtype == VFMOE_DT_F32;
+    a.wait_ns = L.wait_ns;
+    a.inject = L.inject;
     a.gate = mref(L.d.gate);
     a.up = mref(L.d.up);
     a.down = mref(L.d.down);
@@ -582,8 +599,8 @@ static int rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *
     if (L.x3.ready) {
         rc = launch_experts_exl3(L.x3, a, reinterpret_cast<const void *>(rows), (int)rows_dtype, st, []() {});
     } else {
-        if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n * k, L.H,
-                                reinterpret_cast<__half *>(base + lay.xp), offsets + nb + 1, st)))
+        if ((rc = launch_gather(reinterpret_cast<const void *>(rows), (int)rows_dtype, perm_tok, n * k + n, L.H,
+                                reinterpret_cast<__half *>(base + lay.xp), offsets + nb + 1, st, a.prec ? 2 : 1)))
             return rc;
         rc = forward_experts(L, a, st, []() {}, nlaunch);
     }
@@ -704,6 +721,42 @@ int vfmoe_ep_plan_tokens(int64_t idx, int64_t w, int64_t T, int64_t k, int64_t n
                                  reinterpret_cast<int32_t *>(pos_of), reinterpret_cast<int *>(err_word), st);
 }
 
+int vfmoe_dispatch(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t counts, int64_t offsets,
+                   int64_t perm_tok, int64_t pos_of, int64_t err_word, int64_t stream) {
+    if (T < 0 || k <= 0 || k > 32 || n_experts <= 0 || n_experts > 1024 || T * k > ((int64_t)1 << 30) ||
+        !counts || !offsets || (T > 0 && (!idx || !perm_tok || !pos_of))) {
+        set_error("vfmoe_dispatch: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t *cnt = reinterpret_cast<int32_t *>(counts);
+    int32_t *pos = reinterpret_cast<int32_t *>(pos_of);
+    VF_CUDA(cudaMemsetAsync(cnt, 0, (n_experts + 2) * sizeof(int32_t), st));
+    if (T == 0) {
+        VF_CUDA(cudaMemsetAsync(reinterpret_cast<void *>(offsets), 0, (n_experts + 2) * sizeof(int32_t), st));
+        return VFMOE_OK;
+    }
+    // a lane whose id is out of range is counted nowhere and keeps pos_of = -1
+    VF_CUDA(cudaMemsetAsync(pos, 0xFF, T * k * sizeof(int32_t), st));
+    int *err = reinterpret_cast<int *>(err_word);
+    int rc = launch_count(reinterpret_cast<const int32_t *>(idx), T * k, (int)n_experts, cnt, err, st);
+    if (rc) return rc;
+    return launch_dispatch(reinterpret_cast<const int32_t *>(idx), cnt, (int)T, (int)n_experts, (int)k, 0,
+                           reinterpret_cast<int32_t *>(perm_tok), pos, reinterpret_cast<int32_t *>(offsets), err, st);
+}
+
+int vfmoe_debug_inject(int64_t handle, int64_t kind, int64_t wait_ns) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if ((kind != VFMOE_INJECT_NONE && kind != VFMOE_INJECT_STALL_LOADS) || wait_ns < 0) {
+        set_error("vfmoe_debug_inject: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    L->inject = (int)kind;
+    L->wait_ns = wait_ns ? (uint64_t)wait_ns : 2000000000ull;
+    return VFMOE_OK;
+}
+
 int vfmoe_check_device_error(int64_t handle, int64_t stream) {
     Layer *L = get_layer(handle);
     if (!L) return VFMOE_ERR_HANDLE;
@@ -809,6 +862,17 @@ int route_into_scratch(int64_t handle, int64_t x, int64_t T, int64_t idx_out, in
                        int64_t scratch_bytes, int64_t stream) {
     Layer *L = get_layer(handle);
     if (!L) return VFMOE_ERR_HANDLE;
+    int dev = -1;
+    VF_CUDA(cudaGetDevice(&dev));
+    if (dev != L->device) {
+        // the scratch address belongs to the current device, the layer's weights to its own
+        set_error("vfmoe_route_noalloc: the current device is %d but the layer lives on device %d", dev, L->device);
+        return VFMOE_ERR_INVALID;
+    }
+    if (T > (int64_t)1 << 24) {
+        set_error("vfmoe_route_noalloc: T=%lld exceeds 2^24", (long long)T);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
     const int64_t logit_bytes = align_up(router_logit_floats((int)T, L->H, L->E) * 4, 256);
     const int64_t need = logit_bytes + align_up((L->E + 2) * 4, 256);
     if (need > scratch_bytes) {

@@ -18,6 +18,11 @@ namespace vfmoe {
 void set_error(const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
 
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) for the current device, once per
+// (kernel, device, size): the attribute belongs to the device, so a process that drives several
+// GPUs sets it on each.  Thread-safe.
+int set_smem_attr_once(const void *func, int bytes);
+
 #define VF_CUDA(call)                                                                  \
     do {                                                                               \
         cudaError_t _e = (call);                                                       \

@@ -87,15 +87,34 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const int32_t *__restrict
 }
 
 // One CTA (128 threads) per permuted row; H % 8 == 0.  The grid may exceed the rows the
-// dispatch produced (*n_rows, device-side); the extra CTAs exit.
+// dispatch produced (*n_rows, device-side); the extra CTAs exit.  With plane2 != 0 (fp32 x),
+// plane2[pos * H + c] = fp16((x - fp16(x)) * 2^12): the residual that the split-precision decode
+// GEMV multiplies as a second operand plane.
 __global__ void __launch_bounds__(128) gather_kernel(const void *__restrict__ x, int x_dtype,
                                                      const int32_t *__restrict__ perm_tok, int H,
-                                                     __half *__restrict__ xp, const int32_t *__restrict__ n_rows) {
+                                                     __half *__restrict__ xp, const int32_t *__restrict__ n_rows,
+                                                     __half *__restrict__ plane2) {
     pdl_wait_then_release();
     const int64_t pos = blockIdx.x;
     if (pos >= *n_rows) return;
     const int t = perm_tok[pos];
     __half *dst = xp + pos * H;
+    if (plane2 && x_dtype == VFMOE_DT_F32) {
+        const float *src = reinterpret_cast<const float *>(x) + (int64_t)t * H;
+        __half *dst2 = plane2 + pos * H;
+        for (int c = threadIdx.x * 4; c < H; c += 128 * 4) {
+            const float4 a = *reinterpret_cast<const float4 *>(src + c);
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const float2 b0 = __half22float2(h0), b1 = __half22float2(h1);
+            const __half2 l0 = __floats2half2_rn((a.x - b0.x) * 4096.f, (a.y - b0.y) * 4096.f);
+            const __half2 l1 = __floats2half2_rn((a.z - b1.x) * 4096.f, (a.w - b1.y) * 4096.f);
+            *reinterpret_cast<uint2 *>(dst + c) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+            *reinterpret_cast<uint2 *>(dst2 + c) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
+        }
+        return;
+    }
     if (x_dtype == VFMOE_DT_BF16) {
         const __nv_bfloat16 *src = reinterpret_cast<const __nv_bfloat16 *>(x) + (int64_t)t * H;
         for (int c = threadIdx.x * 8; c < H; c += 128 * 8) {
@@ -365,9 +384,11 @@ int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int
 }
 
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
-                  const int32_t *n_rows, cudaStream_t st) {
+                  const int32_t *n_rows, cudaStream_t st, int planes) {
     if (rows == 0) return VFMOE_OK;
-    VF_CUDA(launch_pdl(gather_kernel, dim3((unsigned)rows), dim3(128), 0, st, x, x_dtype, perm_tok, H, xp, n_rows));
+    __half *plane2 = planes == 2 ? xp + rows * H : nullptr;
+    VF_CUDA(launch_pdl(gather_kernel, dim3((unsigned)rows), dim3(128), 0, st, x, x_dtype, perm_tok, H, xp, n_rows,
+                       plane2));
     VF_LAUNCH_CHECK("gather_kernel");
     return VFMOE_OK;
 }

@@ -889,12 +889,7 @@ int exl3_plan_create(const vfmoe_layer_desc &d, Exl3Plan &plan) {
 template <bool GATEUP, int NT, int CW, int BITS>
 static int launch_x1(const XParams &prm, int grid, cudaStream_t st) {
     using C = XCfg<GATEUP, NT, CW, BITS>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemv_exl3<GATEUP, NT, CW, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C::SMEM));
-        attr_done = true;
-    }
+    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_exl3<GATEUP, NT, CW, BITS>), C::SMEM)) return rc_attr;
     expert_gemv_exl3<GATEUP, NT, CW, BITS><<<grid, C::THREADS, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_exl3<gate_up>" : "expert_gemv_exl3<down>");
     return VFMOE_OK;
@@ -908,12 +903,7 @@ static int launch_x(const XParams &prm, int bits, int grid, cudaStream_t st) {
 template <bool GATEUP, int N, int BITS>
 static int launch_xt1(const XParams &prm, int grid, cudaStream_t st) {
     using C = XtCfg<GATEUP, N, BITS>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemm_exl3_tc<GATEUP, N, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C::SMEM));
-        attr_done = true;
-    }
+    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemm_exl3_tc<GATEUP, N, BITS>), C::SMEM)) return rc_attr;
     expert_gemm_exl3_tc<GATEUP, N, BITS><<<grid, kXtThreads, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_exl3_tc<gate_up>" : "expert_gemm_exl3_tc<down>");
     return VFMOE_OK;

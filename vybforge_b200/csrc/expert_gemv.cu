@@ -23,8 +23,17 @@
 // actual k in [16c, 16c + 16) for both A and B, so each thread converts 16 consecutive
 // quants of a row and loads 32 consecutive token bytes.
 //
-// Every mbarrier wait is bounded (2 s); on expiry the CTA raises DEV_WAIT_TIMEOUT and exits
-// after draining its TMA loads.
+// Split precision (PREC, fp32 activations): a Q8_0 weight d*q is exact in fp32; it is carried
+// as w_hi = fp16(d*q) and w_lo = fp16((d*q - w_hi) * 2^12), a token value as x_hi = fp16(x) and
+// x_lo = fp16((x - x_hi) * 2^12) (a second fp16 plane of the token rows).  Each MMA step then
+// issues w_hi.x_hi into one accumulator and w_hi.x_lo + w_lo.x_hi into a second, which is
+// scaled by 2^-12 at the end: the products lose only the w_lo.x_lo term (~2^-24 relative) and
+// the result is close to fp32 arithmetic.  The gate/up epilogue writes act as two planes the
+// same way, so the down GEMV sees act to about fp32 precision too.
+//
+// Every mbarrier wait is bounded (2 s, or p.wait_ns); on expiry the CTA raises DEV_WAIT_TIMEOUT
+// and exits after draining its TMA loads.  p.stall (tests only) makes the producer issue no
+// loads at all, so the consumers' first waits expire with nothing in flight.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -41,11 +50,12 @@ constexpr int kGvThreads = 32 * (kGvConsumers + 1);
 constexpr int kRow = 272;            // 8 Q8_0 blocks (256 K) of one weight row
 constexpr int kWBytes = 128 * kRow;  // weights per stage: 64 rows x 2 matrices or 128 rows
 
-template <bool GATEUP, int NT>
+template <bool GATEUP, int NT, bool PREC>
 struct GvCfg {
     static constexpr int N = 8 * NT;
     static constexpr int ROWS = GATEUP ? 64 : 128;  // channels per tile
-    static constexpr int TOK = N * 512;             // N rows x 256 K fp16
+    static constexpr int TOK1 = N * 512;            // N rows x 256 K fp16: one plane
+    static constexpr int TOK = PREC ? 2 * TOK1 : TOK1;
     static constexpr int STAGE = kWBytes + TOK;
     static constexpr int XCH = GATEUP ? ROWS * N * 4 : 0;
     static constexpr int SW = (230000 - XCH - 1024) / STAGE > 6 ? 6 : (230000 - XCH - 1024) / STAGE;
@@ -95,9 +105,39 @@ __device__ __forceinline__ void q8_frag(const uint8_t *row, int p, int c, uint32
     }
 }
 
-template <bool GATEUP, int NT>
+// q8_frag for the split-precision GEMV: the same 16 quants as fp16 pairs hi = fp16(d*q) and
+// lo = fp16((d*q - hi) * 2^12).  d*q is exact in fp32 (11-bit d times 8-bit q).
+__device__ __forceinline__ void q8_frag_prec(const uint8_t *row, int p, int c, uint32_t (&hi)[8],
+                                             uint32_t (&lo)[8]) {
+    const int blk = 68 * p + 34 * (c >> 1);
+    const int qb = blk + 2 + 16 * (c & 1);
+    const int w0 = qb >> 2;
+    const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
+    uint32_t w[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) w[i] = rw[w0 + i];
+    const uint32_t dw = rw[blk >> 2];
+    const unsigned short dbits = (blk & 2) ? (unsigned short)(dw >> 16) : (unsigned short)(dw & 0xFFFFu);
+    const float d = __half2float(__ushort_as_half(dbits));
+    const int sh = qb & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t q = (sh ? __funnelshift_r(w[i], w[i + 1], 16) : w[i]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float a = d * (float)(int8_t)(q >> (16 * h)), b = d * (float)(int8_t)(q >> (16 * h + 8));
+            const __half2 vh = __floats2half2_rn(a, b);
+            const float2 back = __half22float2(vh);
+            const __half2 vl = __floats2half2_rn((a - back.x) * 4096.f, (b - back.y) * 4096.f);
+            hi[2 * i + h] = *reinterpret_cast<const uint32_t *>(&vh);
+            lo[2 * i + h] = *reinterpret_cast<const uint32_t *>(&vl);
+        }
+    }
+}
+
+template <bool GATEUP, int NT, bool PREC>
 __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_constant__ TcParams p) {
-    using C = GvCfg<GATEUP, NT>;
+    using C = GvCfg<GATEUP, NT, PREC>;
     constexpr int SW = C::SW, N = C::N, ROWS = C::ROWS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -125,7 +165,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
 
     if (warp == kGvConsumers) {
         // ------------------------------------------------------------------ TMA producer
-        if (lane == 0) {
+        if (lane == 0 && !p.stall) {
+            if (PREC) prefetch_tmap(&p.xt2);
             if (!p.tiled) {
                 prefetch_tmap(&p.wa);
                 prefetch_tmap(&p.swa);
@@ -162,6 +203,11 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 uint8_t *st = smem + i * C::STAGE;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[i], kr * 256 + 64 * q, t.y);
+                if (PREC) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        tma_load_2d(st + kWBytes + C::TOK1 + q * (N * 128), &p.xt2, &full[i], kr * 256 + 64 * q, t.y);
+                }
             }
             uint32_t n = 0;
             bool ok = true;
@@ -175,7 +221,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 for (int kr = 0; kr < KR; ++kr, ++n) {
                     if (n < (uint32_t)pre) continue;  // issued above
                     const uint32_t s = n % SW;
-                    if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort))) break;
+                    if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort, p.wait_ns))) break;
                     uint8_t *st = smem + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], C::STAGE);
                     if (p.tiled) {
@@ -187,6 +233,12 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                     }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[s], kr * 256 + 64 * q, t.y);
+                    if (PREC) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            tma_load_2d(st + kWBytes + C::TOK1 + q * (N * 128), &p.xt2, &full[s], kr * 256 + 64 * q,
+                                        t.y);
+                    }
                 }
             }
             if (!ok) {
@@ -208,32 +260,56 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
             const int m0 = (item % MT) * ROWS;
             const int ntv = (t.z + 7) >> 3;                     // n8 tiles with valid token rows
             float acc[NT][4];
+            float acc2[PREC ? NT : 1][4];                       // PREC: w_hi.x_lo + w_lo.x_hi, x 2^12
 #pragma unroll
             for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll
+            for (int j = 0; j < (PREC ? NT : 1); ++j) acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.f;
             for (int kr = 0; kr < KR; ++kr, ++n) {
                 const uint32_t s = n % SW;
-                if (!(ok = mbar_wait(&full[s], (n / SW) & 1, abort))) break;
+                if (!(ok = mbar_wait(&full[s], (n / SW) & 1, abort, p.wait_ns))) break;
                 const uint8_t *st = smem + s * C::STAGE;
                 const uint8_t *rowA = st + (mat * ROWS + r0 + g) * kRow;
                 const uint8_t *rowB = rowA + 8 * kRow;
 #pragma unroll
                 for (int pq = 0; pq < 4; ++pq) {
-                    uint32_t wa[8], wb[8];
-                    q8_frag(rowA, pq, c, wa);
-                    q8_frag(rowB, pq, c, wb);
+                    uint32_t wa[8], wb[8], la[PREC ? 8 : 1], lb[PREC ? 8 : 1];
+                    if constexpr (PREC) {
+                        q8_frag_prec(rowA, pq, c, wa, la);
+                        q8_frag_prec(rowB, pq, c, wb, lb);
+                    } else {
+                        q8_frag(rowA, pq, c, wa);
+                        q8_frag(rowB, pq, c, wb);
+                    }
                     const uint8_t *tq = st + kWBytes + pq * (N * 128);
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < ntv) {
                             // token row 8j+g, 16-byte chunks 2c and 2c+1 (SWIZZLE_128B: chunk ^ (row & 7))
                             const int rr = 8 * j + g;
-                            const uint4 x0 = *reinterpret_cast<const uint4 *>(tq + rr * 128 + (((2 * c) ^ (rr & 7)) << 4));
-                            const uint4 x1 = *reinterpret_cast<const uint4 *>(tq + rr * 128 + (((2 * c + 1) ^ (rr & 7)) << 4));
+                            const int o0 = rr * 128 + (((2 * c) ^ (rr & 7)) << 4);
+                            const int o1 = rr * 128 + (((2 * c + 1) ^ (rr & 7)) << 4);
+                            const uint4 x0 = *reinterpret_cast<const uint4 *>(tq + o0);
+                            const uint4 x1 = *reinterpret_cast<const uint4 *>(tq + o1);
                             const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                            if constexpr (PREC) {
+                                const uint4 y0 = *reinterpret_cast<const uint4 *>(tq + C::TOK1 + o0);
+                                const uint4 y1 = *reinterpret_cast<const uint4 *>(tq + C::TOK1 + o1);
+                                const uint32_t xl[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
 #pragma unroll
-                            for (int s4 = 0; s4 < 4; ++s4) {
-                                const uint32_t a[4] = {wa[2 * s4], wb[2 * s4], wa[2 * s4 + 1], wb[2 * s4 + 1]};
-                                mma_16816(acc[j], a, xb[2 * s4], xb[2 * s4 + 1]);
+                                for (int s4 = 0; s4 < 4; ++s4) {
+                                    const uint32_t a[4] = {wa[2 * s4], wb[2 * s4], wa[2 * s4 + 1], wb[2 * s4 + 1]};
+                                    const uint32_t al[4] = {la[2 * s4], lb[2 * s4], la[2 * s4 + 1], lb[2 * s4 + 1]};
+                                    mma_16816(acc[j], a, xb[2 * s4], xb[2 * s4 + 1]);
+                                    mma_16816(acc2[j], a, xl[2 * s4], xl[2 * s4 + 1]);
+                                    mma_16816(acc2[j], al, xb[2 * s4], xb[2 * s4 + 1]);
+                                }
+                            } else {
+#pragma unroll
+                                for (int s4 = 0; s4 < 4; ++s4) {
+                                    const uint32_t a[4] = {wa[2 * s4], wb[2 * s4], wa[2 * s4 + 1], wb[2 * s4 + 1]};
+                                    mma_16816(acc[j], a, xb[2 * s4], xb[2 * s4 + 1]);
+                                }
                             }
                         }
                     }
@@ -242,6 +318,12 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (!ok) break;
+            if constexpr (PREC) {
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[j][e] = fmaf(acc2[j][e], 1.0f / 4096.f, acc[j][e]);
+            }
             // ---------------------------------------------------------------- epilogue
             // acc[j]: rows r0+g (0,1) and r0+g+8 (2,3) x tokens 8j+2c, 8j+2c+1
             if (GATEUP) {
@@ -264,7 +346,10 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                             const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
                             if (tok < t.z) {
                                 const float a = swiglu_clamped(acc[j][e], xch[rr * N + tok], p.limit);
-                                out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = __float2half_rn(a);
+                                const int64_t o = (int64_t)(t.y + tok) * p.ld_out + m0 + rr;
+                                const __half ah = __float2half_rn(a);
+                                out[o] = ah;
+                                if (PREC) out[o + p.out_plane] = __float2half_rn((a - __half2float(ah)) * 4096.f);
                             }
                         }
                 }
@@ -284,16 +369,13 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     }
 }
 
-template <bool GATEUP, int NT>
+template <bool GATEUP, int NT, bool PREC>
 static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
-    using C = GvCfg<GATEUP, NT>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemv_mma<GATEUP, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_done = true;
-    }
+    using C = GvCfg<GATEUP, NT, PREC>;
+    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_mma<GATEUP, NT, PREC>), C::SMEM))
+        return rc_attr;
     if (GATEUP) {
-        expert_gemv_mma<GATEUP, NT><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+        expert_gemv_mma<GATEUP, NT, PREC><<<grid, kGvThreads, C::SMEM, st>>>(prm);
     } else {
         // programmatic dependent launch: CTAs start streaming down weights on SMs the gate/up
         // grid has released, before its act rows are complete
@@ -307,7 +389,7 @@ static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT>, prm));
+        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT, PREC>, prm));
     }
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_mma<gate_up>" : "expert_gemv_mma<down>");
     return VFMOE_OK;
@@ -320,9 +402,27 @@ int gemv_tokens_per_tile(int T, int k, int E) {
     return 8 * nt;
 }
 
+template <bool PREC>
+static int launch_gv_n(bool gateup, int N, const TcParams &prm, int grid, cudaStream_t st) {
+    if (gateup) {
+        switch (N) {
+            case 8: return launch_gv<true, 1, PREC>(prm, grid, st);
+            case 16: return launch_gv<true, 2, PREC>(prm, grid, st);
+            default: return launch_gv<true, 4, PREC>(prm, grid, st);
+        }
+    }
+    switch (N) {
+        case 8: return launch_gv<false, 1, PREC>(prm, grid, st);
+        case 16: return launch_gv<false, 2, PREC>(prm, grid, st);
+        default: return launch_gv<false, 4, PREC>(prm, grid, st);
+    }
+}
+
 int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
-                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn) {
+                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn, const CUtensorMap *tok_gu2,
+                        const CUtensorMap *tok_dn2) {
     const int N = gemv_tokens_per_tile(a.T, a.k, a.E);
+    const int64_t rows = (int64_t)a.T * a.k + a.T;
     TcParams g{};
     g.wa = plan.gate64;
     g.wb = plan.up64;
@@ -345,13 +445,13 @@ int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, c
     g.out = a.act;
     g.limit = a.limit;
     g.err = a.err;
+    g.prec = a.prec;
+    if (a.prec) g.xt2 = *tok_gu2;
+    g.out_plane = rows * a.I;
+    g.wait_ns = a.wait_ns;
+    g.stall = a.inject == VFMOE_INJECT_STALL_LOADS;
     const int grid = plan.num_sms;
-    int rc;
-    switch (N) {
-        case 8: rc = launch_gv<true, 1>(g, grid, st); break;
-        case 16: rc = launch_gv<true, 2>(g, grid, st); break;
-        default: rc = launch_gv<true, 4>(g, grid, st); break;
-    }
+    int rc = a.prec ? launch_gv_n<true>(true, N, g, grid, st) : launch_gv_n<false>(true, N, g, grid, st);
     if (rc) return rc;
     mid();
     TcParams dn{};
@@ -373,11 +473,12 @@ int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, c
     dn.out = a.y;
     dn.limit = a.limit;
     dn.err = a.err;
-    switch (N) {
-        case 8: return launch_gv<false, 1>(dn, grid, st);
-        case 16: return launch_gv<false, 2>(dn, grid, st);
-        default: return launch_gv<false, 4>(dn, grid, st);
-    }
+    dn.prec = a.prec;
+    if (a.prec) dn.xt2 = *tok_dn2;
+    dn.out_plane = 0;
+    dn.wait_ns = a.wait_ns;
+    dn.stall = g.stall;
+    return a.prec ? launch_gv_n<true>(false, N, dn, grid, st) : launch_gv_n<false>(false, N, dn, grid, st);
 }
 
 }  // namespace vfmoe

@@ -538,9 +538,10 @@ int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     plan.ready = 0;
     const bool tiled = d.weight_format == VFMOE_WFMT_Q8_0_TILED;
     if (d.weight_format != VFMOE_WFMT_Q8_0 && !tiled) return VFMOE_OK;
-    if (getenv("VFMOE_DISABLE_TC")) {
+    plan.path = (int)d.expert_path;
+    if (d.expert_path == VFMOE_PATH_SIMT) {
         if (!tiled) return VFMOE_OK;
-        set_error("VFMOE_DISABLE_TC: the SIMT expert path reads GGUF row order, not VFMOE_WFMT_Q8_0_TILED");
+        set_error("VFMOE_PATH_SIMT: the SIMT expert path reads GGUF row order, not VFMOE_WFMT_Q8_0_TILED");
         return VFMOE_ERR_UNSUPPORTED;
     }
     int dev = 0;
@@ -548,7 +549,6 @@ int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan) {
     VF_CUDA(cudaDeviceGetAttribute(&plan.num_sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t H = d.hidden, I = d.inter, E = d.n_local_experts ? d.n_local_experts : d.n_experts;
     const bool sh = d.sh_gate.data != 0;
-    plan.decode_tc = getenv("VFMOE_DECODE_TC") != nullptr;
     if (tiled) {
         plan.tiled = 1;
         plan.p_gate = reinterpret_cast<const uint8_t *>(d.gate.data);
@@ -603,11 +603,7 @@ static int pick_n(int T, int k, int E) {
 template <bool GATEUP, int N>
 static int launch_one(const TcParams &prm, int grid, cudaStream_t st) {
     using C = TcCfg<GATEUP, N>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        VF_CUDA(cudaFuncSetAttribute(expert_gemm_tc<GATEUP, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_done = true;
-    }
+    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemm_tc<GATEUP, N>), C::SMEM)) return rc_attr;
     expert_gemm_tc<GATEUP, N><<<grid, kThreads, C::SMEM, st>>>(prm);
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_tc<gate_up>" : "expert_gemm_tc<down>");
     return VFMOE_OK;
@@ -615,17 +611,23 @@ static int launch_one(const TcParams &prm, int grid, cudaStream_t st) {
 
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
     const int64_t rows = (int64_t)a.T * a.k + a.T;
-    if ((double)a.T * a.k / a.E <= 16.0 && !plan.decode_tc) {
-        // decode: register-operand GEMV, one token-tile size for both GEMMs
+    const bool decode = (double)a.T * a.k / a.E <= 16.0;
+    if (a.prec || plan.path == VFMOE_PATH_GEMV || (decode && plan.path != VFMOE_PATH_TC)) {
+        // decode: register-operand GEMV, one token-tile size for both GEMMs (fp32 activations:
+        // its split-precision form at every T)
         const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
         VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared, ng,
                            ng, a.tiles, a.tiles_cap, a.tile_counts, a.err));
         VF_LAUNCH_CHECK("tc_plan_kernel");
-        CUtensorMap tg, td;
+        CUtensorMap tg, td, tg2, td2;
         int rc;
         if ((rc = make_tok_map(&tg, a.xp, rows, a.H, ng))) return rc;
         if ((rc = make_tok_map(&td, a.act, rows, a.I, ng))) return rc;
-        return launch_experts_gemv(plan, a, st, mid, tg, td);
+        if (a.prec) {
+            if ((rc = make_tok_map(&tg2, a.xp + rows * a.H, rows, a.H, ng))) return rc;
+            if ((rc = make_tok_map(&td2, a.act + rows * a.I, rows, a.I, ng))) return rc;
+        }
+        return launch_experts_gemv(plan, a, st, mid, tg, td, a.prec ? &tg2 : nullptr, a.prec ? &td2 : nullptr);
     }
     const int n = pick_n(a.T, a.k, a.E);
     const int n_gu = std::min(n, 128);

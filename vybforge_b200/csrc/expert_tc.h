@@ -11,7 +11,7 @@ namespace vfmoe {
 struct TcPlan {
     int ready = 0;
     int num_sms = 0;
-    int decode_tc = 0;  // 1: use the tcgen05 GEMM for decode shapes too (VFMOE_DECODE_TC at create)
+    int path = VFMOE_PATH_AUTO;  // the descriptor's expert_path
     // Q8_0 weight tensor maps (3D: [experts][rows][row bytes as u16]).
     CUtensorMap gate, up, down;          // routed, stacked
     CUtensorMap sh_gate, sh_up, sh_down; // shared expert (one "expert")
@@ -41,6 +41,15 @@ struct TcParams {
     void *out;
     float limit;
     int *err;
+    // decode GEMV only:
+    // prec != 0 (fp32 activations): xt2 maps the second fp16 plane of the token rows (the
+    // residual x - fp16(x), times 2^12); gate/up write act as two fp16 planes, the second at
+    // out + out_plane elements
+    CUtensorMap xt2;
+    int prec;
+    int64_t out_plane;
+    uint64_t wait_ns;  // bound of every mbarrier wait (2 s unless a test shortens it)
+    int stall;         // test-only injection: the producer issues no loads (VFMOE_INJECT_STALL_LOADS)
 };
 
 int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan);
@@ -65,8 +74,10 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
 
 // Decode path (few tokens per expert): TMA + register-operand MMA GEMV (expert_gemv.cu).
 int gemv_tokens_per_tile(int T, int k, int E);
+// a.prec: tok_gu2 / tok_dn2 map the second fp16 planes of xp and act.
 int launch_experts_gemv(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid,
-                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn);
+                        const CUtensorMap &tok_gu, const CUtensorMap &tok_dn, const CUtensorMap *tok_gu2 = nullptr,
+                        const CUtensorMap *tok_dn2 = nullptr);
 
 // Builds the (expert, token-tile) lists for both GEMMs on the device (n_gu / n_dn rows per tile).
 int launch_tc_plan(const MoeArgs &a, int n_gu, int n_dn, cudaStream_t st);

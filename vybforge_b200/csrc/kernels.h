@@ -30,6 +30,10 @@ struct MoeArgs {
     __half *act;               // [T*k + T, I] SwiGLU output (fp16)
     float *y;                  // [T*k + T, H] expert outputs (fp32)
     int *err;
+    int prec;                  // fp32 activations: split-precision decode GEMV (two fp16 planes per
+                               // row of xp and act, the second at + rows * H / + rows * I elements)
+    uint64_t wait_ns;          // bound of the decode GEMV's mbarrier waits
+    int inject;                // VFMOE_INJECT_* (tests only; 0 in production)
     int4 *tiles;               // tensor-core path: two tile lists of tiles_cap entries each
     int32_t *tile_counts;      // [2]
     int64_t tiles_cap;
@@ -55,8 +59,9 @@ int launch_ep_plan_tokens(const int32_t *idx, const float *w, int T, int k, int 
 int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
                    const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st);
 // rows = launch size (an upper bound); *n_rows (device) = rows the dispatch produced.
+// planes = 2 (fp32 x): xp + rows * H receives fp16((x - fp16(x)) * 2^12) of every row.
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,
-                  const int32_t *n_rows, cudaStream_t st);
+                  const int32_t *n_rows, cudaStream_t st, int planes = 1);
 int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const float *w, int T, int H, int k,
                    const void *y_shared, void *out, int out_dtype, cudaStream_t st);
 

@@ -11,10 +11,15 @@
 // below: VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES on every GPU that loads libvfmoe.so, held until
 // the process exits.  Host code cannot use the array's name as a device address, so the
 // first call on each device (with that device current) fetches the address with
-// cudaGetSymbolAddress and caches it; make that first call before any stream capture.
+// cudaGetSymbolAddress and caches it together with the device's current context; make that
+// first call before any stream capture.  If the context changes (cudaDeviceReset tears the
+// primary context down and the module, and with it the array, is loaded again), the next call
+// fetches the address again.  The call must be made with the layer's own device current.
 // All calls share the one array and it keeps the last call's contents: the counts are
 // cleared on every call, and calls whose kernels overlap on the GPU (different streams,
 // different threads) race on the array.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -28,7 +33,26 @@ int route_into_scratch(int64_t handle, int64_t x, int64_t T, int64_t idx_out, in
 static __device__ __align__(256) unsigned char g_route_scratch[VFMOE_ROUTE_NOALLOC_SCRATCH_BYTES];
 
 static std::mutex g_scratch_mu;
-static void *g_scratch_addr[256];  // per device ordinal
+static void *g_scratch_addr[256];     // per device ordinal
+static CUcontext g_scratch_ctx[256];  // the context the address belongs to
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+
+// The calling thread's current driver context (fetched through the runtime's driver entry
+// point; the library does not link libcuda).  nullptr if it cannot be read.
+static CUcontext current_context() {
+    static CtxGetCurrentFn fn = []() -> CtxGetCurrentFn {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<CtxGetCurrentFn>(ptr);
+        return nullptr;
+    }();
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
 
 static int scratch_address(void **out) {
     int dev = 0;
@@ -37,8 +61,11 @@ static int scratch_address(void **out) {
         set_error("vfmoe_route_noalloc: device ordinal %d out of range", dev);
         return VFMOE_ERR_INVALID;
     }
+    // No context current on this thread yet (nullptr): the set-up below makes the runtime's
+    // context current, and the address is cached against that context.
+    CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!g_scratch_addr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
         if (e != cudaSuccess || !p) {
@@ -46,7 +73,9 @@ static int scratch_address(void **out) {
                       cudaGetErrorString(e));
             return VFMOE_ERR_CUDA;
         }
+        if (!ctx) ctx = current_context();
         g_scratch_addr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_addr[dev];
     return VFMOE_OK;

@@ -675,12 +675,8 @@ template <int TB, int KCH>
 static int launch_l1_small(const void *x, int x_dtype, const float *wr, int T, int H, int E, float *part,
                            cudaStream_t st) {
     const int smem = TB * KCH * 4;
-    static bool attr = false;
-    if (!attr) {
-        VF_CUDA(cudaFuncSetAttribute(router_logits_f32_small<TB, KCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
-        attr = true;
-    }
+    int rc = set_smem_attr_once(reinterpret_cast<const void *>(router_logits_f32_small<TB, KCH>), smem);
+    if (rc) return rc;
     dim3 grid((unsigned)cdiv(E, 16), (unsigned)(H / KCH));
     router_logits_f32_small<TB, KCH><<<grid, 256, smem, st>>>(x, x_dtype, wr, T, H, E, part);
     VF_LAUNCH_CHECK("router_logits_f32_small");
@@ -698,14 +694,29 @@ static int tiled_splits(int T, int H, int E) {
     return s;
 }
 
+// The decode logits kernel (T <= 32) takes H in chunks of 768 or 512 columns, one partial sum per
+// chunk; 0 = H is a multiple of neither and the tiled kernel runs at every T.
+static int router_l1_chunk(int H) { return H % 768 == 0 ? 768 : (H % 512 == 0 ? 512 : 0); }
+
+// Partial-sum slices the logits kernel writes for (T, H, E): H / chunk on the decode kernel, else
+// tiled_splits.  launch_router and the scratch sizing (router_logit_floats) both use this count.
+static int router_splits(int T, int H, int E) {
+    const int kch = router_l1_chunk(H);
+    return (T <= 32 && kch) ? H / kch : tiled_splits(T, H, E);
+}
+
 int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
                   int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
                   cudaStream_t st) {
+    if (H > kMaxH || H / 512 > kMaxChunks) {
+        set_error("router: hidden size %d exceeds %d", H, kMaxH);
+        return VFMOE_ERR_UNSUPPORTED;
+    }
     float c1;
-    int nchunk = 1, rc = VFMOE_OK;
-    const int kch = H % 768 == 0 ? 768 : (H % 512 == 0 ? 512 : 0);
+    int rc = VFMOE_OK;
+    const int kch = router_l1_chunk(H);
+    const int nchunk = router_splits(T, H, E);
     if (T <= 32 && kch) {
-        nchunk = H / kch;
         if (kch == 768)
             rc = T <= 8 ? launch_l1_small<8, 768>(x, x_dtype, wr, T, H, E, logits, st)
                         : launch_l1_small<32, 768>(x, x_dtype, wr, T, H, E, logits, st);
@@ -715,7 +726,6 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
         if (rc) return rc;
         c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
-        nchunk = tiled_splits(T, H, E);
         dim3 grid((unsigned)cdiv(E, 128), (unsigned)cdiv(T, 128), (unsigned)nchunk);
         router_logits_f32_wide<<<grid, 256, 0, st>>>(x, x_dtype, wr, T, H, E, logits);
         VF_LAUNCH_CHECK("router_logits_f32_wide");
@@ -728,27 +738,19 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     const int n2 = H / 256;
     const float c2 = gamma_bound(2 * n2 + 24) * (float)(n2 + 1 + 24) * 5.9604645e-8f;
     const int npl = (int)cdiv(E, 32);
-    if (H > kMaxH || H / 512 > kMaxChunks) {
-        set_error("router: hidden size %d exceeds %d", H, kMaxH);
-        return VFMOE_ERR_UNSUPPORTED;
-    }
     if (H * 4 > 48 * 1024) {
-        static bool attr = false;
-        if (!attr) {
-            VF_CUDA(cudaFuncSetAttribute(router_refine<1, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<1, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<2, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<2, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<4, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<4, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<8, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<8, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<16, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<16, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<32, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            VF_CUDA(cudaFuncSetAttribute(router_refine<32, 4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxH * 4));
-            attr = true;
-        }
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<1, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<1, 4, 3>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<2, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<2, 4, 3>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<4, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<4, 4, 3>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<8, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<8, 4, 3>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<16, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<16, 4, 3>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<32, 8, 1>), kMaxH * 4))) return rc;
+        if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<32, 4, 3>), kMaxH * 4))) return rc;
     }
 #define VF_REFINE(NPL)                                                                                              \
     do {                                                                                                           \
@@ -773,7 +775,7 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
 }
 
 int64_t router_logit_floats(int T, int H, int E) {
-    return (int64_t)T * E * (T <= 32 ? std::max(1, H / 512) : tiled_splits(T, H, E));
+    return (int64_t)T * E * router_splits(T, H, E);
 }
 
 }  // namespace vfmoe

@@ -21,6 +21,9 @@ import torch
 
 from . import _lib
 from ._lib import check, DT_BF16, DT_F16, DT_F32, WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED
+from ._lib import PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV
+
+_PATHS = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC, "gemv": PATH_GEMV}
 
 _DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
 
@@ -57,11 +60,12 @@ class MoELayer:
     fmt="q8_0_tiled": the same tensors after ``q8_0_tile`` (stage-tiled byte order).
     EXL3 weights: each projection is a tuple (trellis int16 [E, K/16, N/16, 16*bits],
     suh fp16 [E, K], svh fp16 [E, N]); shared likewise without the leading E.
+    path: expert kernels, "auto" (default), "tc", "gemv" or "simt" (vfmoe_layer_desc.expert_path).
     """
 
     def __init__(self, *, hidden, inter, n_experts, topk, router_w, router_bias, gate, up, down,
                  shared=None, fmt="q8_0", exl3_bits=3, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
-                 scale=2.5, limit=10.0, n_local_experts=0):
+                 scale=2.5, limit=10.0, n_local_experts=0, path="auto"):
         self.lib = _lib.load()
         self.H, self.I, self.E, self.k = hidden, inter, n_experts, topk
         self.x_dtype, self.out_dtype = x_dtype, out_dtype
@@ -69,6 +73,7 @@ class MoELayer:
         d = _lib.LayerDesc()
         d.hidden, d.inter, d.n_experts, d.topk = hidden, inter, n_experts, topk
         d.n_local_experts = n_local_experts
+        d.expert_path = _PATHS[path]
         self.n_local = n_local_experts or n_experts
         d.weight_format = {"q8_0": WFMT_Q8_0, "q8_0_tiled": WFMT_Q8_0_TILED, "exl3": WFMT_EXL3}[fmt]
         d.exl3_bits = exl3_bits
@@ -169,6 +174,10 @@ class MoELayer:
     def check_device_error(self):
         check(self.lib.vfmoe_check_device_error(self.handle, _stream()))
 
+    def debug_inject(self, kind: int, wait_ns: int = 0):
+        """Failure injection for tests (vfmoe_debug_inject); kind _lib.INJECT_NONE restores."""
+        check(self.lib.vfmoe_debug_inject(self.handle, kind, wait_ns))
+
     def close(self):
         if getattr(self, "handle", 0) > 0:
             self.lib.vfmoe_layer_destroy(self.handle)
@@ -197,6 +206,20 @@ def exl3_decode(trellis: torch.Tensor, K: int, N: int, bits: int) -> torch.Tenso
     out = torch.empty((K, N), dtype=torch.float16, device=trellis.device)
     check(_lib.load().vfmoe_exl3_decode(_ptr(trellis), _ptr(out), K, N, bits, _stream()))
     return out
+
+
+def dispatch(idx: torch.Tensor, n_experts: int, err: torch.Tensor | None = None):
+    """Canonical permutation of idx int32 [T, k] (vfmoe_dispatch): (perm_tok [T*k], pos_of [T*k],
+    offsets [E+1], counts [E]) on the device; err (int32 [1], device) records an id out of range."""
+    T, k = idx.shape
+    dev = idx.device
+    counts = torch.empty(n_experts + 2, dtype=torch.int32, device=dev)
+    offsets = torch.empty(n_experts + 2, dtype=torch.int32, device=dev)
+    perm = torch.empty(T * k, dtype=torch.int32, device=dev)
+    pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+    check(_lib.load().vfmoe_dispatch(_ptr(idx), T, k, n_experts, _ptr(counts), _ptr(offsets), _ptr(perm), _ptr(pos),
+                                     _ptr(err), _stream()))
+    return perm, pos, offsets[:n_experts + 1], counts[:n_experts]
 
 
 def ep_plan(idx: torch.Tensor, n_experts: int, placement: torch.Tensor, n_ranks: int):
