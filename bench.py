@@ -401,8 +401,9 @@ def stack_extra(a, rank, world, local_rank, flush):
     """BASELINE C4: 4 pre-norm MoE layers of the C1 shape, Q8_0, bf16 activations.
     prefill T=8192 (Zipf(1.1) routers, calibrated per layer) and decode T=256 (plain routers);
     global token counts fixed (strong scaling).  N=1: MoEStack on one GPU.  N>1: expert-parallel
-    (EpStack over NCCL all-to-all), E/N experts per GPU placed by expected load, shared expert and
-    routers replicated, tokens sharded."""
+    (EpStack: vfmoe_ep_forward, the library's NCCL exchange), E/N experts per GPU placed by the
+    load measured on calibration tokens disjoint from the timed ones, shared expert and routers
+    replicated, tokens sharded."""
     import torch
     from vybforge_b200 import synth, ep
     from vybforge_b200.moe import MoELayer, quantizer
@@ -438,18 +439,19 @@ def stack_extra(a, rank, world, local_rank, flush):
             layers[key].append(lay)
     t_setup = time.perf_counter() - t_setup
     st = torch.cuda.current_stream()
-    tr = ep.DistTransport() if world > 1 else None
+    comm = ep.EpComm.from_torch_dist() if world > 1 else None
     out = {}
     for key, cfg, x, norm in (("p", cfgp, xp, norm_p), ("d", cfgd, xd, norm_d)):
         T = cfg.tokens
         nw = [torch.from_numpy(w).cuda() for w in norm]
         if world > 1:
-            stack = EpStack([ep.EpRank(rank, world, ep.GpuBackend(lay, placements[l], world),
-                                       replica_of=replicas[l], n_experts=E)
+            shards = token_shards(T, world)
+            cap = max(len(s_) for s_ in shards)
+            stack = EpStack([ep.EpLayer(lay, placements[l], rank, world, cap, replicas[l])
                              for l, lay in enumerate(layers[key])], nw)
-            sh = token_shards(T, world)[rank]
+            sh = shards[rank]
             xl = torch.from_numpy(x[sh[0]:sh[-1] + 1]).to(torch.bfloat16).cuda()
-            step = lambda: stack.forward_dist(xl, tr)
+            step = lambda: stack.forward(comm, xl)
         else:
             stack = MoEStack(layers[key], nw)
             xl = torch.from_numpy(x).to(torch.bfloat16).cuda()
@@ -475,23 +477,25 @@ def stack_extra(a, rank, world, local_rank, flush):
             t = torch.tensor([ms], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = float(t.item())
-            # one more step with an event after every phase: device ms per phase (this rank)
-            marks = []
-
-            def mark(name):
-                e_ = torch.cuda.Event(enable_timing=True)
-                e_.record(st)
-                marks.append((name, e_))
+            # one more step with the library's phase events on (vfmoe_ep_forward stages), all
+            # layers summed, max over ranks per phase
+            import ctypes as C
+            for lay in layers[key]:
+                lay.lib.vfmoe_profile_enable(lay.handle, 1)
+                lay.lib.vfmoe_profile_read(lay.handle, (C.c_double * 8)(), 8, None)
             torch.distributed.barrier()
-            mark("start")
-            stack.forward_dist(xl, tr, mark)
+            step()
             torch.cuda.synchronize()
-            phases = {}
-            for (_, a_), (n_, b_) in zip(marks[:-1], marks[1:]):
-                phases[n_] = phases.get(n_, 0.0) + a_.elapsed_time(b_)
-            pt = torch.tensor([phases[n_] for n_ in sorted(phases)], device="cuda")
+            tot = np.zeros(6)
+            for lay in layers[key]:
+                buf = (C.c_double * 8)()
+                lay.lib.vfmoe_profile_read(lay.handle, buf, 8, None)
+                lay.lib.vfmoe_profile_enable(lay.handle, 0)
+                tot += np.array(buf[:6])
+            names = ["route_plan_pack", "shared_expert", "dispatch_wait", "experts", "return_exchange", "combine"]
+            pt = torch.tensor(tot, device="cuda")
             torch.distributed.all_reduce(pt, op=torch.distributed.ReduceOp.MAX)
-            phases = {n_: round(float(v), 3) for n_, v in zip(sorted(phases), pt.tolist())}
+            phases = {n_: round(float(v), 3) for n_, v in zip(names, pt.tolist())}
         else:
             # one more step with the library's stage events on: device ms per stage, all layers
             import ctypes as C
@@ -540,6 +544,8 @@ def stack_extra(a, rank, world, local_rank, flush):
     for key in layers:
         for lay in layers[key]:
             lay.close()
+    if comm is not None:
+        comm.close()
     return out
 
 
@@ -630,13 +636,14 @@ def run_ours_ep(a, rank, world, local_rank):
                      router_bias=torch.from_numpy(bias).cuda(), gate=dev[0][:-1], up=dev[1][:-1], down=dev[2][:-1],
                      shared=(dev[0][-1], dev[1][-1], dev[2][-1]), n_local_experts=E // world, fmt=wf,
                      x_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
-    rs = ep.EpRank(rank, world, ep.GpuBackend(layer, placement, world, out_dtype=torch.bfloat16))
-    tr = ep.DistTransport()
+    comm = ep.EpComm.from_torch_dist()
+    rs = ep.EpLayer(layer, placement, rank, world, T)
     xl = torch.from_numpy(x[rank * T:(rank + 1) * T]).to(torch.bfloat16).cuda()
+    out_l = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     st = torch.cuda.current_stream()
     for _ in range(max(3, a.warmup)):
-        ep.ep_forward_dist(rs, xl, tr)
+        rs.forward(comm, xl, out=out_l)
     dist.barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local_rank)
@@ -646,7 +653,7 @@ def run_ours_ep(a, rank, world, local_rank):
         flush.zero_()
         dist.barrier()
         ev[i][0].record(st)
-        ep.ep_forward_dist(rs, xl, tr)
+        rs.forward(comm, xl, out=out_l)
         ev[i][1].record(st)
     torch.cuda.synchronize()
     dist.barrier()
@@ -665,7 +672,7 @@ def run_ours_ep(a, rank, world, local_rank):
         dist.barrier()
         ev2[i][0].record(st)
         xin.copy_(xh, non_blocking=True)
-        o = ep.ep_forward_dist(rs, xin, tr)
+        o = rs.forward(comm, xin, out=out_l)
         oh.copy_(o, non_blocking=True)
         ev2[i][1].record(st)
     torch.cuda.synchronize()
@@ -673,6 +680,7 @@ def run_ours_ep(a, rank, world, local_rank):
     t = torch.tensor([e2e_ms], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
+    comm.close()
     extra = None
     if not a.no_extra and a.workload == "c1" and a.tokens is None:
         layer_keep = layer
@@ -693,10 +701,12 @@ def run_ours_ep(a, rank, world, local_rank):
            "data": "synthetic (seeded N(0,1) bf16 tokens, N(0,0.02) weights quantized to Q8_0)",
            "config": {"workload": f"{a.workload}: decode T={T}/GPU, H={H}, I={cfg.inter}, E={E}, top-{cfg.topk} "
                                   f"+ 1 shared, Q8_0, expert-parallel {E // world} experts/GPU",
-                      "tokens_per_gpu": T, "global_batch": T * world, "parallelism": f"ep{world} (NCCL all-to-all)",
+                      "tokens_per_gpu": T, "global_batch": T * world, "parallelism": f"ep{world} (vfmoe_ep_forward: NCCL send/recv inside libvfmoe)",
                       "distinct_experts": n_distinct, "q8_layout": wf,
                       "l2": "256 MiB memset between timed steps, outside the step events"},
-           "gpu_launches": 12 * a.steps, "clocks": clk,
+           # per vfmoe_ep_forward: router 2, plan 1, pack 1, shared expert 8 (fill, count, dispatch,
+           # gather, tile plan, gate/up, down, combine), routed experts 7, final combine 1
+           "gpu_launches": 20 * a.steps, "clocks": clk,
            "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer (all ranks)",
                         "achieved": round(job_bytes / (ms * 1e-3) / 1e9, 1), "peak": world * pk["hbm_gbs"],
                         "unit": "GB/s", "frac": round(frac, 4), "peak_source": pk_kind, "traffic": None},

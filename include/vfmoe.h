@@ -194,36 +194,12 @@ int64_t vfmoe_rows_workspace_bytes(int64_t handle, int64_t n_max);
 int vfmoe_forward_rows(int64_t handle, int64_t rows, int64_t rows_dtype, int64_t slots, int64_t n, int64_t y_out,
                        int64_t workspace, int64_t ws_bytes, int64_t stream);
 
-/* Send plan of an expert-parallel dispatch: the T*k (token, lane) pairs of idx int32 [T,k]
- * sorted by owner rank placement[expert] (int32 [n_experts]), stable in t*k+l order.
- * send_counts int32 [n_ranks]; send_perm int32 [T*k] (slot -> t*k+l); inv_perm int32
- * [T*k] (t*k+l -> slot).  err_word: device int that records a bad id (may be 0). */
-int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t placement, int64_t n_ranks,
-                  int64_t send_counts, int64_t send_perm, int64_t inv_perm, int64_t err_word, int64_t stream);
-
-/* Pack the send buffer: rows_out[s] = x[send_perm[s] / k] (x dtype, [n_slots, H]) and
- * slots_out[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index).  With
- * slots_out == 0, idx and local_slot may be 0: k = 1 and send_perm = send_tok gathers the
- * rows of a token-level plan. */
-int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
-                  int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream);
-
 /* Weighted combine: out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] + y_shared[t].  y rows and
  * y_shared are y_dtype VFMOE_DT_F32 or VFMOE_DT_F16; w may be 0 for weight 1; y_shared may
  * be 0; a negative pos_of entry skips that lane.  out_dtype F32, BF16 or F16.
  * glm_engine.vyb:2925-2938, :2991. */
 int vfmoe_combine(int64_t y, int64_t y_dtype, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H,
                   int64_t y_shared, int64_t out, int64_t out_dtype, int64_t stream);
-
-/* Token-level send plan (one row per token per destination rank): entries ordered by
- * rank, then token, for every (t, r) where a lane of idx int32 [T,k] routes to an expert
- * r owns (placement int32 [n_experts]).  Entry i: send_tok[i] = t; for lane l,
- * send_slot[i*k+l] = local_slot[expert] when rank r owns it else -1, send_w[i*k+l] =
- * w[t,l] or 0.  send_counts int32 [n_ranks]; pos_of int32 [T, n_ranks] = entry or -1.
- * Buffers sized for T*n_ranks entries.  err_word: device int for a bad id (may be 0). */
-int vfmoe_ep_plan_tokens(int64_t idx, int64_t w, int64_t T, int64_t k, int64_t n_experts, int64_t placement,
-                         int64_t local_slot, int64_t n_ranks, int64_t send_counts, int64_t send_tok,
-                         int64_t send_slot, int64_t send_w, int64_t pos_of, int64_t err_word, int64_t stream);
 
 /* Bytes of workspace vfmoe_forward_routed needs for up to n_max rows of k lanes. */
 int64_t vfmoe_routed_workspace_bytes(int64_t handle, int64_t n_max, int64_t k);
@@ -249,6 +225,83 @@ int vfmoe_forward_routed(int64_t handle, int64_t rows, int64_t rows_dtype, int64
 #define VFMOE_INJECT_STALL_LOADS 1
 int vfmoe_debug_inject(int64_t handle, int64_t kind, int64_t wait_ns);
 
+/* ---- expert parallelism inside the library: NCCL between ranks, one process per GPU ----
+ *
+ * The reference has no multi-GPU code; these entry points serve the callers that would run the
+ * MoE expert-parallel: tail_site's router, expert loop and shared expert
+ * (native/glm53/glm_engine.vyb:2728-2991) and the prefill driver (native/host/glm_prefill.vyb:1458).
+ *
+ * Tokens are sharded over ranks; the router and the shared expert are replicated; routed experts
+ * (plus optional copies of hot experts) are sharded by a placement.  Per layer forward:
+ *   prepare  route this rank's T tokens, plan one send entry per (token, rank owning one of its k
+ *            experts), pack the rows; entries for rank d sit at d * t_cap + i (i < count[d]).
+ *   exchange every peer block is t_cap entries, whatever its count: rows (x dtype), lane slots
+ *            (int32 [t_cap][k]) and lane weights (fp32 [t_cap][k]); padding entries carry slot -1.
+ *   shared   the shared expert on this rank's tokens (overlaps the exchange).
+ *   experts  this rank's experts on the n_ranks * t_cap received rows, each row's local lanes summed
+ *            with their weights into one partial row (fp16; fp32 when out_dtype is F32).
+ *   exchange partial rows back, block d to rank d.
+ *   combine  out[t] = the partials returned for t, in rank order, + shared(x[t]).
+ * t_cap (>= every rank's T, the same on all ranks) fixes every transfer size, so no count
+ * crosses to the host and the whole forward is one stream of device work.
+ * vfmoe_ep_forward runs all of it with NCCL send/recv; a host with its own transport calls the
+ * phases and moves the blocks that vfmoe_ep_buffers locates. */
+
+/* 128 bytes of NCCL unique id for vfmoe_ep_init; one rank makes it, the host shares it. */
+int vfmoe_ep_unique_id(void *id_out, int64_t n);
+
+/* Communicator over nranks processes (one GPU each, the calling thread's current device).
+ * NCCL is opened at run time (libnccl.so.2; VFMOE_ERR_NCCL if absent).  Waits for every rank to
+ * join for at most timeout_ms (0 = no limit); on expiry the partial communicator is aborted and
+ * VFMOE_ERR_NCCL returned.  Returns a communicator handle > 0. */
+int64_t vfmoe_ep_init(int64_t nranks, int64_t rank, const void *unique_id, int64_t timeout_ms);
+int vfmoe_ep_destroy(int64_t comm);
+
+/* Placement of a layer handle that holds rank `rank`'s experts (n_local_experts of them, in
+ * ascending virtual id): owner int32 [n_virtual] (host) gives the rank of each virtual expert,
+ * n_virtual = n_experts + n_replicas; virtual expert n_experts + j is a copy of expert
+ * replica_of[j] (host int32 [n_replicas]) and takes the lanes (t, l) of that expert with t + l
+ * odd.  Copies the placement to the device (call at set-up, not per forward). */
+int vfmoe_ep_set_placement(int64_t handle, int64_t n_ranks, int64_t rank, const int32_t *owner, int64_t n_virtual,
+                           const int32_t *replica_of, int64_t n_replicas);
+
+/* Workspace bytes of the expert-parallel calls for capacity t_cap. */
+int64_t vfmoe_ep_workspace_bytes(int64_t handle, int64_t t_cap);
+
+/* Byte offsets in that workspace of the exchange buffers (and block sizes), indexed by: */
+#define VFMOE_EP_SEND_ROWS 0
+#define VFMOE_EP_RECV_ROWS 1
+#define VFMOE_EP_ROWS_BLOCK 2       /* bytes of one peer block of rows */
+#define VFMOE_EP_SEND_SLOTS 3
+#define VFMOE_EP_RECV_SLOTS 4
+#define VFMOE_EP_SEND_WEIGHTS 5
+#define VFMOE_EP_RECV_WEIGHTS 6
+#define VFMOE_EP_LANES_BLOCK 7      /* bytes of one peer block of slots (or of weights) */
+#define VFMOE_EP_SEND_PARTIALS 8    /* partial rows computed here, block d belongs to rank d */
+#define VFMOE_EP_RECV_PARTIALS 9    /* partial rows returned to this rank, block d from rank d */
+#define VFMOE_EP_PARTIALS_BLOCK 10
+#define VFMOE_EP_SEND_COUNTS 11     /* int32 [n_ranks]: valid entries per send block */
+#define VFMOE_EP_BUF_COUNT 12
+int vfmoe_ep_buffers(int64_t handle, int64_t t_cap, int64_t *offsets, int64_t n);
+
+/* The phases (all on `stream`, no host synchronization).  Between prepare and experts the send
+ * blocks of rows, slots and weights of rank d must reach rank d's receive blocks (this rank's own
+ * block is already in place); between experts and combine the partial blocks likewise. */
+int vfmoe_ep_prepare(int64_t handle, int64_t x, int64_t T, int64_t t_cap, int64_t idx_out, int64_t w_out,
+                     int64_t workspace, int64_t ws_bytes, int64_t stream);
+int vfmoe_ep_shared(int64_t handle, int64_t x, int64_t T, int64_t t_cap, int64_t workspace, int64_t ws_bytes,
+                    int64_t stream);
+int vfmoe_ep_experts(int64_t handle, int64_t t_cap, int64_t workspace, int64_t ws_bytes, int64_t stream);
+int vfmoe_ep_combine(int64_t handle, int64_t T, int64_t t_cap, int64_t out, int64_t workspace, int64_t ws_bytes,
+                     int64_t stream);
+
+/* The whole expert-parallel layer forward over NCCL: out [T, H] for this rank's x [T, H].
+ * The dispatch exchange runs on the communicator's own stream, forked from and joined back to
+ * `stream` with events, while the shared expert runs on `stream`.  Every rank must make the
+ * same calls with the same t_cap.  idx_out / w_out (optional) receive the routing. */
+int vfmoe_ep_forward(int64_t comm, int64_t handle, int64_t x, int64_t T, int64_t t_cap, int64_t out, int64_t idx_out,
+                     int64_t w_out, int64_t workspace, int64_t ws_bytes, int64_t stream);
+
 /* Synchronize `stream` and report whether any kernel of this handle flagged a
  * device-side error since the last call (VFMOE_ERR_DEVICE), then clear it. */
 int vfmoe_check_device_error(int64_t handle, int64_t stream);
@@ -260,7 +313,8 @@ int vfmoe_profile_enable(int64_t handle, int enable);
 
 /* Synchronize on the recorded events and return, in stage_ms[0..n), the summed
  * device milliseconds per stage since the last read: 0 router, 1 dispatch+gather,
- * 2 gate/up+SwiGLU, 3 down, 4 combine.  *launches (if non-null) gets the number of
+ * 2 gate/up+SwiGLU, 3 down, 4 combine (vfmoe_ep_forward: 0 route+plan+pack, 1 shared expert,
+ * 2 wait for the dispatch exchange, 3 experts, 4 return exchange, 5 combine).  *launches (if non-null) gets the number of
  * kernels launched by those forwards.  Returns the number of forwards measured and
  * resets the accumulators. */
 int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *launches);

@@ -155,26 +155,27 @@ def test_residual_rmsnorm_matches_oracle(st):
 @pytest.mark.parametrize("world", [2, 4])
 def test_ep_stack_virtual_ranks_match_single_gpu(st, world):
     """fp32 residual streams on both sides (bf16 streams differ by whole-ulp flips; see
-    above); the expert-parallel side uses the default exchange (fp16 partial rows)."""
+    above); the expert-parallel side runs the library's phases with fp32 partial rows (the
+    partials follow the output dtype), blocks moved by device copies between virtual ranks."""
     T, f32 = st.cfg.tokens, torch.float32
     single = MoEStack([st.layer(l, out_dtype=f32, x_dtype=f32) for l in range(L)], st.norm_dev)
     xd = torch.from_numpy(st.x).cuda()
     ref = single.forward(xd)
+    shards = token_shards(T, world)
+    cap = max(len(s) for s in shards)
     stacks = []
     for r in range(world):
-        ranks = []
+        lays = []
         for l in range(L):
             placement = ep.balanced_placement(st.routers[l][2], world)
             lay = st.layer(l, placement, r, world, out_dtype=f32, x_dtype=f32)
-            ranks.append(ep.EpRank(r, world, ep.GpuBackend(lay, placement, world, out_dtype=f32)))
-        stacks.append(EpStack(ranks, st.norm_dev))
-    shards = token_shards(T, world)
-    outs = ep_stack_forward_virtual(stacks, [xd[s[0]:s[-1] + 1].contiguous() for s in shards],
-                                    ep.VirtualTransport(world))
+            lays.append(ep.EpLayer(lay, placement, r, world, cap))
+        stacks.append(EpStack(lays, st.norm_dev))
+    outs = ep_stack_forward_virtual(stacks, [xd[s[0]:s[-1] + 1].contiguous() for s in shards])
     got = torch.cat(outs)
     for s in stacks:
-        for r in s.ranks:
-            r.b.layer.check_device_error()
+        for lay in s.layers:
+            lay.layer.check_device_error()
     g, r_ = _f64(got), _f64(ref)
     print(f"[ep stack virtual N={world}] max-abs {np.abs(g - r_).max():.3e} rel-L2 {rel_l2(g, r_):.3e}")
     assert np.abs(g - r_).max() <= TOL_MAX_ABS and rel_l2(g, r_) <= TOL_REL_L2

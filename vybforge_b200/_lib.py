@@ -69,13 +69,21 @@ _SIGS = {
     "vfmoe_forward": (C.c_int, [I64] * 9),
     "vfmoe_check_device_error": (C.c_int, [I64, I64]),
     "vfmoe_dispatch": (C.c_int, [I64] * 10),
+    "vfmoe_ep_unique_id": (C.c_int, [C.c_void_p, I64]),
+    "vfmoe_ep_init": (I64, [I64, I64, C.c_void_p, I64]),
+    "vfmoe_ep_destroy": (C.c_int, [I64]),
+    "vfmoe_ep_set_placement": (C.c_int, [I64, I64, I64, C.POINTER(C.c_int32), I64, C.POINTER(C.c_int32), I64]),
+    "vfmoe_ep_workspace_bytes": (I64, [I64, I64]),
+    "vfmoe_ep_buffers": (C.c_int, [I64, I64, C.POINTER(I64), I64]),
+    "vfmoe_ep_prepare": (C.c_int, [I64] * 9),
+    "vfmoe_ep_shared": (C.c_int, [I64] * 7),
+    "vfmoe_ep_experts": (C.c_int, [I64] * 5),
+    "vfmoe_ep_combine": (C.c_int, [I64] * 7),
+    "vfmoe_ep_forward": (C.c_int, [I64] * 11),
     "vfmoe_debug_inject": (C.c_int, [I64, I64, I64]),
     "vfmoe_rows_workspace_bytes": (I64, [I64, I64]),
     "vfmoe_forward_rows": (C.c_int, [I64] * 9),
-    "vfmoe_ep_plan": (C.c_int, [I64] * 11),
-    "vfmoe_ep_pack": (C.c_int, [I64] * 11),
     "vfmoe_combine": (C.c_int, [I64] * 11),
-    "vfmoe_ep_plan_tokens": (C.c_int, [I64] * 15),
     "vfmoe_routed_workspace_bytes": (I64, [I64, I64, I64]),
     "vfmoe_forward_routed": (C.c_int, [I64] * 12),
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),

@@ -55,7 +55,7 @@ int set_smem_attr_once(const void *func, int bytes) {
 
 static constexpr int kNumStages = 5;
 
-static cudaEvent_t take_event(Layer &L) {
+cudaEvent_t take_event(Layer &L) {
     cudaEvent_t e = nullptr;
     if (!L.ev_pool.empty()) {
         e = L.ev_pool.back();
@@ -510,7 +510,7 @@ int vfmoe_profile_read(int64_t handle, double *stage_ms, int64_t n, int64_t *lau
     if (!L) return VFMOE_ERR_HANDLE;
     for (auto &ev : L->ev_pending) {
         VF_CUDA(cudaEventSynchronize(ev.back()));
-        for (int s = 0; s < kNumStages; ++s) {
+        for (int s = 0; s + 1 < (int)ev.size() && s < 8; ++s) {
             float ms = 0.f;
             VF_CUDA(cudaEventElapsedTime(&ms, ev[s], ev[s + 1]));
             L->stage_ms[s] += ms;
@@ -651,40 +651,6 @@ int vfmoe_forward_routed(int64_t handle, int64_t rows, int64_t rows_dtype, int64
                      reinterpret_cast<cudaStream_t>(stream));
 }
 
-int vfmoe_ep_plan(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t placement, int64_t n_ranks,
-                  int64_t send_counts, int64_t send_perm, int64_t inv_perm, int64_t err_word, int64_t stream) {
-    if (T < 0 || k <= 0 || n_experts <= 0 || n_ranks <= 0 || n_ranks > 1024 || T * k > ((int64_t)1 << 30) ||
-        (T > 0 && (!idx || !placement || !send_counts || !send_perm || !inv_perm))) {
-        set_error("vfmoe_ep_plan: bad arguments");
-        return VFMOE_ERR_INVALID;
-    }
-    if (T == 0) {
-        VF_CUDA(cudaMemsetAsync(reinterpret_cast<void *>(send_counts), 0, n_ranks * 4,
-                                reinterpret_cast<cudaStream_t>(stream)));
-        return VFMOE_OK;
-    }
-    return launch_ep_plan(reinterpret_cast<const int32_t *>(idx), T * k, (int)n_experts,
-                          reinterpret_cast<const int32_t *>(placement), (int)n_ranks,
-                          reinterpret_cast<int32_t *>(send_counts), reinterpret_cast<int32_t *>(send_perm),
-                          reinterpret_cast<int32_t *>(inv_perm), reinterpret_cast<int *>(err_word),
-                          reinterpret_cast<cudaStream_t>(stream));
-}
-
-int vfmoe_ep_pack(int64_t x, int64_t x_dtype, int64_t H, int64_t k, int64_t idx, int64_t send_perm,
-                  int64_t local_slot, int64_t n_slots, int64_t rows_out, int64_t slots_out, int64_t stream) {
-    const int eb = x_dtype == VFMOE_DT_F32 ? 4 : (x_dtype == VFMOE_DT_BF16 || x_dtype == VFMOE_DT_F16 ? 2 : 0);
-    const bool with_slots = slots_out != 0;
-    if (!eb || H <= 0 || (H * eb) % 16 || k <= 0 || n_slots < 0 || (x & 15) || (rows_out & 15) ||
-        (n_slots > 0 && (!x || !send_perm || !rows_out || (with_slots && (!idx || !local_slot))))) {
-        set_error("vfmoe_ep_pack: bad arguments");
-        return VFMOE_ERR_INVALID;
-    }
-    return launch_ep_pack(reinterpret_cast<const void *>(x), eb, (int)H, (int)k, reinterpret_cast<const int32_t *>(idx),
-                          reinterpret_cast<const int32_t *>(send_perm), reinterpret_cast<const int32_t *>(local_slot),
-                          n_slots, reinterpret_cast<void *>(rows_out), reinterpret_cast<int32_t *>(slots_out),
-                          reinterpret_cast<cudaStream_t>(stream));
-}
-
 int vfmoe_combine(int64_t y, int64_t y_dtype, int64_t pos_of, int64_t w, int64_t T, int64_t k, int64_t H,
                   int64_t y_shared, int64_t out, int64_t out_dtype, int64_t stream) {
     if (T < 0 || k <= 0 || k > 32 || H <= 0 || H % 4 || (y_dtype != VFMOE_DT_F32 && y_dtype != VFMOE_DT_F16) ||
@@ -697,28 +663,6 @@ int vfmoe_combine(int64_t y, int64_t y_dtype, int64_t pos_of, int64_t w, int64_t
                           reinterpret_cast<const float *>(w), (int)T, (int)H, (int)k,
                           reinterpret_cast<const void *>(y_shared), reinterpret_cast<void *>(out), (int)out_dtype,
                           reinterpret_cast<cudaStream_t>(stream));
-}
-
-int vfmoe_ep_plan_tokens(int64_t idx, int64_t w, int64_t T, int64_t k, int64_t n_experts, int64_t placement,
-                         int64_t local_slot, int64_t n_ranks, int64_t send_counts, int64_t send_tok,
-                         int64_t send_slot, int64_t send_w, int64_t pos_of, int64_t err_word, int64_t stream) {
-    if (T < 0 || k <= 0 || k > 32 || n_experts <= 0 || n_ranks <= 0 || n_ranks > 1024 || T > ((int64_t)1 << 24) ||
-        (T > 0 && (!idx || !w || !placement || !local_slot || !send_counts || !send_tok || !send_slot || !send_w ||
-                   !pos_of))) {
-        set_error("vfmoe_ep_plan_tokens: bad arguments");
-        return VFMOE_ERR_INVALID;
-    }
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (T == 0) {
-        VF_CUDA(cudaMemsetAsync(reinterpret_cast<void *>(send_counts), 0, n_ranks * 4, st));
-        return VFMOE_OK;
-    }
-    return launch_ep_plan_tokens(reinterpret_cast<const int32_t *>(idx), reinterpret_cast<const float *>(w), (int)T,
-                                 (int)k, (int)n_experts, reinterpret_cast<const int32_t *>(placement),
-                                 reinterpret_cast<const int32_t *>(local_slot), (int)n_ranks,
-                                 reinterpret_cast<int32_t *>(send_counts), reinterpret_cast<int32_t *>(send_tok),
-                                 reinterpret_cast<int32_t *>(send_slot), reinterpret_cast<float *>(send_w),
-                                 reinterpret_cast<int32_t *>(pos_of), reinterpret_cast<int *>(err_word), st);
 }
 
 int vfmoe_dispatch(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t counts, int64_t offsets,

@@ -221,157 +221,11 @@ __global__ void count_kernel(const int32_t *__restrict__ ids, int64_t n, int nb,
         raise_dev_error(err, DEV_BAD_EXPERT_ID);
 }
 
-// Token-level expert-parallel send plan (one CTA, 1024 threads): one entry per (token t,
-// rank r) pair where some lane of t routes to an expert r owns, ordered by rank, then
-// token.  Entry i carries send_tok[i] = t and, for each lane l, the owner-local expert
-// slot (or -1 when lane l goes elsewhere) and its routing weight.
-// pos_of[t * n_ranks + r] = entry index or -1.
-__global__ void __launch_bounds__(1024) ep_plan_tokens_kernel(
-    const int32_t *__restrict__ idx, const float *__restrict__ w, int T, int k, int E,
-    const int32_t *__restrict__ placement, const int32_t *__restrict__ local_slot, int n_ranks,
-    int32_t *__restrict__ send_counts, int32_t *__restrict__ send_tok, int32_t *__restrict__ send_slot,
-    float *__restrict__ send_w, int32_t *__restrict__ pos_of, int *__restrict__ err) {
-    __shared__ int warp_tot[32];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int base = 0;
-    for (int r = 0; r < n_ranks; ++r) {
-        int running = 0;
-        for (int c = 0; c < T; c += 1024) {
-            const int t = c + tid;
-            bool hit = false;
-            if (t < T) {
-                for (int l = 0; l < k; ++l) {
-                    const int e = idx[(int64_t)t * k + l];
-                    const int owner = (e >= 0 && e < E) ? placement[e] : -1;
-                    if (owner < 0 || owner >= n_ranks) {
-                        if (r == 0) raise_dev_error(err, DEV_BAD_EXPERT_ID);
-                    } else if (owner == r) {
-                        hit = true;
-                    }
-                }
-            }
-            const unsigned m = __ballot_sync(0xffffffffu, hit);
-            if (lane == 0) warp_tot[warp] = __popc(m);
-            __syncthreads();
-            int before = 0, total = 0;
-            for (int q = 0; q < 32; ++q) {
-                const int v = warp_tot[q];
-                before += q < warp ? v : 0;
-                total += v;
-            }
-            if (t < T) {
-                int pos = -1;
-                if (hit) {
-                    pos = base + running + before + __popc(m & ((1u << lane) - 1u));
-                    send_tok[pos] = t;
-                    for (int l = 0; l < k; ++l) {
-                        const int e = idx[(int64_t)t * k + l];
-                        const bool mine = e >= 0 && e < E && placement[e] == r;
-                        send_slot[(int64_t)pos * k + l] = mine ? local_slot[e] : -1;
-                        send_w[(int64_t)pos * k + l] = mine ? w[(int64_t)t * k + l] : 0.f;
-                    }
-                }
-                pos_of[(int64_t)t * n_ranks + r] = pos;
-            }
-            running += total;
-            __syncthreads();
-        }
-        if (tid == 0) send_counts[r] = running;
-        base += running;
-    }
-}
-
-// Expert-parallel send plan (one CTA, 1024 threads): the T*k (token, lane) pairs, stably
-// sorted by owner rank placement[idx] (flat index t*k+l ascending within a rank).
-// send_perm[slot] = flat index, inv_perm[flat] = slot, send_counts[rank].
-__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ idx, int64_t n, int E,
-                                                       const int32_t *__restrict__ placement, int n_ranks,
-                                                       int32_t *__restrict__ send_counts, int32_t *__restrict__ send_perm,
-                                                       int32_t *__restrict__ inv_perm, int *__restrict__ err) {
-    __shared__ int warp_tot[32];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    int base = 0;
-    for (int r = 0; r < n_ranks; ++r) {
-        int running = 0;
-        for (int64_t c = 0; c < n; c += 1024) {
-            const int64_t i = c + tid;
-            bool hit = false;
-            if (i < n) {
-                const int e = idx[i];
-                const int owner = (e >= 0 && e < E) ? placement[e] : -1;
-                if (owner < 0 || owner >= n_ranks) {
-                    if (r == 0) raise_dev_error(err, DEV_BAD_EXPERT_ID);
-                } else {
-                    hit = owner == r;
-                }
-            }
-            const unsigned m = __ballot_sync(0xffffffffu, hit);
-            if (lane == 0) warp_tot[warp] = __popc(m);
-            __syncthreads();
-            int before = 0, total = 0;
-            for (int w = 0; w < 32; ++w) {
-                const int v = warp_tot[w];
-                before += w < warp ? v : 0;
-                total += v;
-            }
-            if (hit) {
-                const int slot = base + running + before + __popc(m & ((1u << lane) - 1u));
-                send_perm[slot] = (int32_t)i;
-                inv_perm[i] = slot;
-            }
-            running += total;
-            __syncthreads();
-        }
-        if (tid == 0) send_counts[r] = running;
-        base += running;
-    }
-}
-
-// Send rows for the expert-parallel exchange: rows[s] = x[send_perm[s] / k] (same dtype),
-// slots[s] = local_slot[idx[send_perm[s]]] (the owner's local expert index) when slots != 0.
-__global__ void __launch_bounds__(128) ep_pack_kernel(const void *__restrict__ x, int elt_bytes, int H, int k,
-                                                      const int32_t *__restrict__ idx, const int32_t *__restrict__ send_perm,
-                                                      const int32_t *__restrict__ local_slot, void *__restrict__ rows,
-                                                      int32_t *__restrict__ slots) {
-    const int64_t s = blockIdx.x;
-    const int flat = send_perm[s];
-    const int t = flat / k;
-    if (threadIdx.x == 0 && slots) slots[s] = local_slot[idx[flat]];
-    const int64_t row_bytes = (int64_t)H * elt_bytes;
-    const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(x) + (int64_t)t * row_bytes);
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(rows) + s * row_bytes);
-    for (int64_t i = threadIdx.x; i < row_bytes / 16; i += 128) dst[i] = src[i];
-}
-
 int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st,
                  int skip_negative) {
     if (n == 0) return VFMOE_OK;
     count_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(ids, n, nb, counts, err, skip_negative);
     VF_LAUNCH_CHECK("count_kernel");
-    return VFMOE_OK;
-}
-
-int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placement, int n_ranks, int32_t *send_counts,
-                   int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st) {
-    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, n, E, placement, n_ranks, send_counts, send_perm, inv_perm, err);
-    VF_LAUNCH_CHECK("ep_plan_kernel");
-    return VFMOE_OK;
-}
-
-int launch_ep_plan_tokens(const int32_t *idx, const float *w, int T, int k, int E, const int32_t *placement,
-                          const int32_t *local_slot, int n_ranks, int32_t *send_counts, int32_t *send_tok,
-                          int32_t *send_slot, float *send_w, int32_t *pos_of, int *err, cudaStream_t st) {
-    ep_plan_tokens_kernel<<<1, 1024, 0, st>>>(idx, w, T, k, E, placement, local_slot, n_ranks, send_counts, send_tok,
-                                              send_slot, send_w, pos_of, err);
-    VF_LAUNCH_CHECK("ep_plan_tokens_kernel");
-    return VFMOE_OK;
-}
-
-int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
-                   const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st) {
-    if (n_slots == 0) return VFMOE_OK;
-    ep_pack_kernel<<<(unsigned)n_slots, 128, 0, st>>>(x, elt_bytes, H, k, idx, send_perm, local_slot, rows, slots);
-    VF_LAUNCH_CHECK("ep_pack_kernel");
     return VFMOE_OK;
 }
 

@@ -51,13 +51,6 @@ int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);
 int launch_count(const int32_t *ids, int64_t n, int nb, int32_t *counts, int *err, cudaStream_t st,
                  int skip_negative = 0);
-int launch_ep_plan(const int32_t *idx, int64_t n, int E, const int32_t *placement, int n_ranks, int32_t *send_counts,
-                   int32_t *send_perm, int32_t *inv_perm, int *err, cudaStream_t st);
-int launch_ep_plan_tokens(const int32_t *idx, const float *w, int T, int k, int E, const int32_t *placement,
-                          const int32_t *local_slot, int n_ranks, int32_t *send_counts, int32_t *send_tok,
-                          int32_t *send_slot, float *send_w, int32_t *pos_of, int *err, cudaStream_t st);
-int launch_ep_pack(const void *x, int elt_bytes, int H, int k, const int32_t *idx, const int32_t *send_perm,
-                   const int32_t *local_slot, int64_t n_slots, void *rows, int32_t *slots, cudaStream_t st);
 // rows = launch size (an upper bound); *n_rows (device) = rows the dispatch produced.
 // planes = 2 (fp32 x): xp + rows * H receives fp16((x - fp16(x)) * 2^12) of every row.
 int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t rows, int H, __half *xp,

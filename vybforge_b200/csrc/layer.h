@@ -52,6 +52,8 @@ struct WsLayout {
 };
 
 Layer *get_layer(int64_t h);
+// A timing event from the handle's pool (nullptr if none could be made).
+cudaEvent_t take_event(Layer &L);
 int layer_prec(const Layer &L);
 WsLayout ws_layout(const Layer &L, int64_t T, int k = -1);
 // Workspace base for a call: the caller's (checked against ws_layout) or the handle's own.

@@ -1,34 +1,31 @@
-"""Expert-parallel MoE layer across the GPUs of one node.
+"""Expert-parallel MoE layer across the GPUs of one node: a thin caller of libvfmoe.
 
 The reference has no multi-GPU code; this is the expert-parallel form the task asks for.
 - Tokens are sharded over ranks. Each rank routes its own tokens (router replicated) and runs
   the shared expert on them (shared expert replicated).
-- The routed experts are sharded: rank r holds the experts whose `placement[e] == r`, stacked
-  in ascending expert order (their local slots).
+- The routed experts are sharded: rank r holds the (virtual) experts whose `placement[v] == r`,
+  stacked in ascending id order (their local slots).  Hot experts may have copies
+  (`replicated_placement`): virtual expert E + j holds expert hot[j]'s weights on another rank
+  and takes that expert's lanes (t, l) with t + l odd.
 
-Token-level exchange, one forward per rank in three phases:
-1. route -> `vfmoe_ep_plan_tokens`: one send entry per (token, destination rank) that owns
-   at least one of the token's experts, carrying the token's k lanes as (owner-local slot
-   or -1, weight) -> `vfmoe_ep_pack` gathers the send rows.
-2. exchange counts, then rows and lane metadata (all-to-all-v). While the rows are in
-   flight, `vfmoe_forward_routed` runs the shared expert on this rank's own tokens; then on
-   the received rows, summing each row's local lanes with their weights: one fp16 partial
-   row per entry.
-3. all-to-all-v the partial rows back; `vfmoe_combine` adds, per token, the partials from
-   each rank (rank order) and the shared expert's row.
-A token whose experts live on m ranks crosses the links m times each way, instead of k times
-(once per (token, expert) pair), and the return rows are fp16 partial sums.
+The whole forward lives in the library (include/vfmoe.h, "expert parallelism inside the
+library"): plan, pack, a fixed-capacity exchange (every peer block is t_cap entries, so no count
+crosses to the host), the shared expert overlapping the exchange, the rank's experts on the
+received rows (one fp16 partial row per entry), the exchange back and the combine.
+- `EpComm`: the library's NCCL communicator (`vfmoe_ep_init`), bootstrapped by sharing the
+  unique id over torch.distributed (or any other host channel).
+- `EpLayer`: one rank's layer (`vfmoe_ep_set_placement`, workspace), `forward(comm, x)` =
+  `vfmoe_ep_forward`, and the phase entry points for a caller's own transport.
+- `ep_forward_virtual`: N virtual ranks in one process on one GPU, the blocks moved between their
+  workspaces by device copies (tests the whole multi-rank data path on a single GPU).
 
-The GPU compute is libvfmoe. The all-to-all is a `Transport`:
-- `DistTransport`: torch.distributed over NCCL (NVLink/NVSwitch), or gloo on CPU.
-- `VirtualTransport`: N virtual ranks held by one process. The whole multi-rank data path
-  (plans, packing, per-rank expert sets, exchange order) then runs on one GPU.
-
-Hot experts can be replicated (`replicated_placement`, `split_replicas`): a copy on a second
-rank takes the odd tokens' lanes, so no rank carries a whole hottest expert.
+Placement helpers (`balanced_placement`, `replicated_placement`, `local_slots`) are host logic
+with no GPU work.
 """
 
 from __future__ import annotations
+
+import ctypes as C
 
 import numpy as np
 import torch
@@ -110,7 +107,8 @@ def replicated_placement(load, n_ranks: int, n_replicas: int | None = None, tile
 
 def split_replicas(idx: torch.Tensor, replica_of, n_experts: int) -> torch.Tensor:
     """Routing ids over the virtual experts of replicated_placement: lane (t, l) of expert
-    replica_of[j] goes to its copy n_experts + j when the token index t is odd.  idx int32
+    replica_of[j] goes to its copy n_experts + j when t + l is odd (the rule the library's plan
+    kernel applies; lane parity splits an expert's lanes even at one token per rank).  idx int32
     [T, k] (any device).  The weights are unchanged: the combined output is the same sum, its
     partials possibly added in another rank order."""
     R = len(replica_of)
@@ -121,7 +119,8 @@ def split_replicas(idx: torch.Tensor, replica_of, n_experts: int) -> torch.Tenso
     copy_of[torch.as_tensor(np.asarray(replica_of), dtype=torch.long, device=dev)] = torch.arange(
         n_experts, n_experts + R, dtype=torch.int32, device=dev)
     cand = copy_of[idx.long()]
-    odd = (torch.arange(idx.shape[0], device=dev) % 2 == 1)[:, None]
+    T, k = idx.shape
+    odd = ((torch.arange(T, device=dev)[:, None] + torch.arange(k, device=dev)[None, :]) % 2) == 1
     return torch.where((cand >= 0) & odd, cand, idx)
 
 
@@ -135,182 +134,143 @@ def local_slots(placement: np.ndarray) -> np.ndarray:
     return slot.astype(np.int32)
 
 
-# ----------------------------------------------------------------------------- transports
-class DistTransport:
-    """All-to-all(v) through torch.distributed (NCCL on GPUs, gloo on CPU)."""
+# ----------------------------------------------------------------------------- library EP
+class EpComm:
+    """NCCL communicator inside libvfmoe (one per process / GPU)."""
 
-    def __init__(self, group=None):
+    def __init__(self, rank: int, world: int, unique_id: bytes, timeout_ms: int = 120000):
+        from . import _lib
+        self.lib = _lib.load()
+        self.rank, self.world = rank, world
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        self.handle = _lib.check(self.lib.vfmoe_ep_init(world, rank, buf, timeout_ms))
+
+    @staticmethod
+    def unique_id() -> bytes:
+        from . import _lib
+        buf = C.create_string_buffer(128)
+        _lib.check(_lib.load().vfmoe_ep_unique_id(buf, 128))
+        return buf.raw
+
+    @classmethod
+    def from_torch_dist(cls, group=None, timeout_ms: int = 120000):
+        """Rank 0 makes the unique id; torch.distributed carries it to the other ranks (the only
+        use of torch.distributed here: the exchange itself is the library's NCCL)."""
         import torch.distributed as dist
-        self.dist = dist
-        self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        obj = [cls.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(rank, world, obj[0], timeout_ms)
 
-    def counts(self, send_counts):
-        """send_counts: int tensor [world] -> recv_counts python list (host sync)."""
-        out = torch.empty_like(send_counts)
-        self.dist.all_to_all_single(out, send_counts, group=self.group)
-        return out.tolist(), send_counts.tolist()
+    def close(self):
+        if getattr(self, "handle", 0) > 0:
+            self.lib.vfmoe_ep_destroy(self.handle)
+            self.handle = 0
 
-    def rows(self, send, send_splits, recv_splits):
-        recv, work = self.rows_async(send, send_splits, recv_splits)
-        work.wait()
-        return recv
-
-    def rows_async(self, send, send_splits, recv_splits):
-        """Start the exchange on the collective stream; work.wait() orders later work on the
-        current stream after it.  Work enqueued meanwhile overlaps the transfer."""
-        recv = torch.empty((sum(recv_splits),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-        work = self.dist.all_to_all_single(recv, send, output_split_sizes=recv_splits, input_split_sizes=send_splits,
-                                           group=self.group, async_op=True)
-        return recv, work
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
-class VirtualTransport:
-    """N ranks held by one process: a collective is a gather over the per-rank inputs."""
-
-    def __init__(self, world: int):
-        self.world = world
-
-    def counts_all(self, send_counts_per_rank):
-        sc = [c.tolist() for c in send_counts_per_rank]
-        recv = [[sc[src][dst] for src in range(self.world)] for dst in range(self.world)]
-        return recv, sc
-
-    def rows_all(self, sends, send_splits, recv_splits):
-        parts = [list(torch.split(s, sp)) for s, sp in zip(sends, send_splits)]
-        return [torch.cat([parts[src][dst] for src in range(self.world)]) for dst in range(self.world)]
+_BUF_NAMES = ["send_rows", "recv_rows", "rows_block", "send_slots", "recv_slots", "send_weights", "recv_weights",
+              "lanes_block", "send_partials", "recv_partials", "partials_block", "send_counts"]
 
 
-# ----------------------------------------------------------------------------- one rank
-class EpRank:
-    """One rank's share of an expert-parallel MoE layer.
+class EpLayer:
+    """One rank's share of an expert-parallel MoE layer over libvfmoe.
 
-    `backend` provides:
-      route(x) -> (idx, w)
-      plan(idx, w) -> (send_counts, send_tok, send_slot, send_w, pos_of)   (token-level plan)
-      pack(x, send_tok, n) -> rows
-      experts(rows, slots, w) -> partial rows (fp16): sum of the weighted local lanes
-      (also the shared expert: one lane with slot shared_slot, weight 1)
-      combine(y_back, pos_of, T, y_shared) -> out
-      shared_slot, k
-    `GpuBackend` is the libvfmoe one.  With replica_of (replicated_placement), the backend's
-    placement covers the E + R virtual experts and its layer holds the local ones.
-    """
+    layer: a MoELayer holding the router (all E experts), the shared expert and this rank's
+    (virtual) experts (n_local_experts); placement int32 [E + R] (owner rank per virtual
+    expert); replica_of int32 [R] (copies); t_cap: capacity per rank, >= every rank's token
+    count and equal on all ranks."""
 
-    def __init__(self, rank: int, world: int, backend, replica_of=None, n_experts: int = 0):
-        self.rank, self.world, self.b = rank, world, backend
-        # replicated experts (replicated_placement): the routing ids are split over the copies
-        self.replica_of = np.asarray(replica_of if replica_of is not None else [], dtype=np.int32)
-        self.n_experts = n_experts
+    def __init__(self, layer, placement, rank: int, world: int, t_cap: int, replica_of=None):
+        from . import _lib
+        self._lib = _lib
+        self.layer, self.rank, self.world, self.t_cap = layer, rank, world, t_cap
+        pl = np.ascontiguousarray(np.asarray(placement, dtype=np.int32))
+        rep = np.ascontiguousarray(np.asarray(replica_of if replica_of is not None else [], dtype=np.int32))
+        self.placement, self.replica_of = pl, rep
+        i32p = C.POINTER(C.c_int32)
+        _lib.check(layer.lib.vfmoe_ep_set_placement(layer.handle, world, rank, pl.ctypes.data_as(i32p), len(pl),
+                                                     rep.ctypes.data_as(i32p) if len(rep) else None, len(rep)))
+        need = _lib.check(layer.lib.vfmoe_ep_workspace_bytes(layer.handle, t_cap))
+        self.ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        offs = (C.c_int64 * 12)()
+        _lib.check(layer.lib.vfmoe_ep_buffers(layer.handle, t_cap, offs, 12))
+        self.buf = dict(zip(_BUF_NAMES, list(offs)))
 
-    def phase1(self, x):
-        idx, w = self.b.route(x)
-        if len(self.replica_of):
-            idx = split_replicas(idx, self.replica_of, self.n_experts)
-        counts, tok, slot, sw, pos = self.b.plan(idx, w)
-        return dict(x=x, counts=counts, tok=tok, slot=slot, sw=sw, pos=pos)
+    def _args(self):
+        return int(self.ws.data_ptr()), self.ws.numel(), int(torch.cuda.current_stream().cuda_stream)
 
-    def pack(self, st, n: int):
-        """Send rows and lane metadata of the n valid entries (n = sum of the send counts)."""
-        st["rows"] = self.b.pack(st["x"], st["tok"], n)
-        # lane metadata as one int32 tensor [n, 2k]: slots, then the weights' bits
-        st["meta"] = torch.cat([st["slot"][:n], st["sw"][:n].view(torch.int32)], dim=1)
-
-    def shared(self, st):
-        """The shared expert on this rank's own tokens (weight 1, one lane)."""
-        x = st["x"]
+    def forward(self, comm: EpComm, x: torch.Tensor, out=None, idx=None, w=None):
+        """This rank's tokens x [T, H] through the layer (vfmoe_ep_forward)."""
         T = x.shape[0]
-        own_s = torch.full((T, 1), self.b.shared_slot, dtype=torch.int32, device=x.device)
-        own_w = torch.ones((T, 1), dtype=torch.float32, device=x.device)
-        st["y_shared"] = self.b.experts(x, own_s, own_w)
+        if out is None:
+            out = torch.empty((T, self.layer.H), dtype=self.layer.out_dtype, device=x.device)
+        ws, nb, st = self._args()
+        p = lambda t: 0 if t is None else int(t.data_ptr())  # noqa: E731
+        self._lib.check(self.layer.lib.vfmoe_ep_forward(comm.handle, self.layer.handle, p(x), T, self.t_cap, p(out),
+                                                        p(idx), p(w), ws, nb, st))
+        return out
 
-    def phase2(self, st, recv_rows, recv_meta):
-        k = self.b.k
-        if recv_rows.shape[0] == 0:
-            return torch.empty((0, st["x"].shape[1]), dtype=self.b.partial_dtype, device=st["x"].device)
-        slots, wts = recv_meta[:, :k], recv_meta[:, k:].view(torch.float32)
-        return self.b.experts(recv_rows, slots.contiguous(), wts.contiguous())
+    # ---- phases (a caller's own transport moves the blocks between them)
+    def prepare(self, x, idx=None, w=None):
+        ws, nb, st = self._args()
+        p = lambda t: 0 if t is None else int(t.data_ptr())  # noqa: E731
+        self._lib.check(self.layer.lib.vfmoe_ep_prepare(self.layer.handle, p(x), x.shape[0], self.t_cap, p(idx), p(w),
+                                                        ws, nb, st))
 
-    def phase3(self, st, y_back):
-        T = st["x"].shape[0]
-        return self.b.combine(y_back, st["pos"], T, st["y_shared"])
+    def shared(self, x):
+        ws, nb, st = self._args()
+        self._lib.check(self.layer.lib.vfmoe_ep_shared(self.layer.handle, int(x.data_ptr()), x.shape[0], self.t_cap,
+                                                       ws, nb, st))
 
+    def experts(self):
+        ws, nb, st = self._args()
+        self._lib.check(self.layer.lib.vfmoe_ep_experts(self.layer.handle, self.t_cap, ws, nb, st))
 
-def ep_forward_dist(rank_state: EpRank, x, transport: DistTransport, mark=None):
-    """Expert-parallel forward of this process's tokens (one rank per process).
-    mark(name), if given, is called after each phase (e.g. to record CUDA events)."""
-    mark = mark or (lambda name: None)
-    st = rank_state.phase1(x)
-    mark("route_plan")
-    recv_splits, send_splits = transport.counts(st["counts"])
-    mark("counts")
-    rank_state.pack(st, sum(send_splits))
-    mark("pack")
-    # the shared expert on this rank's tokens runs while the rows are in flight
-    recv_rows, w_rows = transport.rows_async(st["rows"], send_splits, recv_splits)
-    recv_meta, w_meta = transport.rows_async(st["meta"], send_splits, recv_splits)
-    rank_state.shared(st)
-    mark("shared")
-    w_rows.wait()
-    w_meta.wait()
-    mark("dispatch")
-    y_recv = rank_state.phase2(st, recv_rows, recv_meta)
-    mark("experts")
-    y_back = transport.rows(y_recv, recv_splits, send_splits)
-    mark("return")
-    out = rank_state.phase3(st, y_back)
-    mark("combine")
-    return out
+    def combine(self, T: int, out=None):
+        if out is None:
+            out = torch.empty((T, self.layer.H), dtype=self.layer.out_dtype, device="cuda")
+        ws, nb, st = self._args()
+        self._lib.check(self.layer.lib.vfmoe_ep_combine(self.layer.handle, T, self.t_cap, int(out.data_ptr()), ws,
+                                                        nb, st))
+        return out
 
+    def block(self, name: str, d: int) -> torch.Tensor:
+        """Byte view of peer block d of an exchange buffer ("send_rows", "recv_slots", ...)."""
+        size = self.buf[{"rows": "rows_block", "slots": "lanes_block", "weights": "lanes_block",
+                         "partials": "partials_block"}[name.split("_", 1)[1]]]
+        at = self.buf[name] + d * size
+        return self.ws[at:at + size]
 
-def ep_forward_virtual(ranks, xs, transport: VirtualTransport):
-    """Expert-parallel forward of N virtual ranks held by this process."""
-    sts = [r.phase1(x) for r, x in zip(ranks, xs)]
-    recv_splits, send_splits = transport.counts_all([s["counts"] for s in sts])
-    for r, s, sp in zip(ranks, sts, send_splits):
-        r.pack(s, sum(sp))
-    recv_rows = transport.rows_all([s["rows"] for s in sts], send_splits, recv_splits)
-    recv_meta = transport.rows_all([s["meta"] for s in sts], send_splits, recv_splits)
-    for r, s in zip(ranks, sts):
-        r.shared(s)
-    y_recv = [r.phase2(s, rr, rm) for r, s, rr, rm in zip(ranks, sts, recv_rows, recv_meta)]
-    y_back = transport.rows_all(y_recv, recv_splits, send_splits)
-    return [r.phase3(s, yb) for r, s, yb in zip(ranks, sts, y_back)]
+    def send_counts(self) -> torch.Tensor:
+        at = self.buf["send_counts"]
+        return self.ws[at:at + 4 * self.world].view(torch.int32)
 
 
-# ----------------------------------------------------------------------------- GPU backend
-class GpuBackend:
-    """libvfmoe kernels for one rank: a MoELayer holding the router (all E experts), the
-    shared expert and this rank's routed experts (n_local_experts)."""
-
-    def __init__(self, layer, placement, n_ranks: int, out_dtype=torch.bfloat16, partial_dtype=torch.float16):
-        from . import moe
-        self.moe = moe
-        self.layer = layer
-        self.E, self.k = len(placement), layer.k  # routed ids, copies of replicated experts included
-        self.n_ranks = n_ranks
-        self.placement = torch.as_tensor(np.asarray(placement, np.int32)).cuda()
-        self.local_slot = torch.as_tensor(local_slots(placement)).cuda()
-        self.shared_slot = layer.n_local
-        self.out_dtype = out_dtype
-        self.partial_dtype = partial_dtype
-
-    def route(self, x):
-        return self.layer.route(x)
-
-    def plan(self, idx, w):
-        return self.moe.ep_plan_tokens(idx, w, self.E, self.placement, self.local_slot, self.n_ranks)
-
-    def pack(self, x, tok, n):
-        return self.moe.gather_rows(x, tok, n)
-
-    def experts(self, rows, slots, w):
-        return self.layer.forward_routed(rows, slots, w, y_dtype=self.partial_dtype)
-
-    def combine(self, y_back, pos, T, y_shared):
-        return self.moe.combine(y_back, pos.reshape(-1), None, T, self.n_ranks, y_shared=y_shared,
-                                out_dtype=self.out_dtype)
+def ep_forward_virtual(ranks, xs, outs=None):
+    """N virtual ranks (EpLayer, one per rank, same t_cap) in one process on one GPU: the phases,
+    with every peer block moved by a device copy where the NCCL exchange would move it."""
+    N = len(ranks)
+    for r, x in zip(ranks, xs):
+        r.prepare(x)
+    for kind in ("rows", "slots", "weights"):
+        for s in range(N):
+            for d in range(N):
+                if s != d:
+                    ranks[d].block("recv_" + kind, s).copy_(ranks[s].block("send_" + kind, d))
+    for r, x in zip(ranks, xs):
+        r.shared(x)
+        r.experts()
+    for s in range(N):
+        for d in range(N):
+            if s != d:
+                ranks[d].block("recv_partials", s).copy_(ranks[s].block("send_partials", d))
+    return [r.combine(x.shape[0], None if outs is None else outs[i]) for i, (r, x) in enumerate(zip(ranks, xs))]
 
 
 def rank_experts(dev, placement, rank: int, replica_of=None):

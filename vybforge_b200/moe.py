@@ -222,28 +222,6 @@ def dispatch(idx: torch.Tensor, n_experts: int, err: torch.Tensor | None = None)
     return perm, pos, offsets[:n_experts + 1], counts[:n_experts]
 
 
-def ep_plan(idx: torch.Tensor, n_experts: int, placement: torch.Tensor, n_ranks: int):
-    """(send_counts int32 [n_ranks], send_perm int32 [T*k], inv_perm int32 [T*k]) on the device."""
-    T, k = idx.shape
-    counts = torch.empty(n_ranks, dtype=torch.int32, device=idx.device)
-    perm = torch.empty(T * k, dtype=torch.int32, device=idx.device)
-    inv = torch.empty(T * k, dtype=torch.int32, device=idx.device)
-    check(_lib.load().vfmoe_ep_plan(_ptr(idx), T, k, n_experts, _ptr(placement), n_ranks, _ptr(counts), _ptr(perm),
-                                    _ptr(inv), 0, _stream()))
-    return counts, perm, inv
-
-
-def ep_pack(x: torch.Tensor, idx: torch.Tensor, send_perm: torch.Tensor, local_slot: torch.Tensor):
-    """(rows [T*k, H] x.dtype, slots int32 [T*k]) in send order."""
-    T, k = idx.shape
-    n = T * k
-    rows = torch.empty((n, x.shape[1]), dtype=x.dtype, device=x.device)
-    slots = torch.empty(n, dtype=torch.int32, device=x.device)
-    check(_lib.load().vfmoe_ep_pack(_ptr(x), _DT[x.dtype], x.shape[1], k, _ptr(idx), _ptr(send_perm),
-                                    _ptr(local_slot), n, _ptr(rows), _ptr(slots), _stream()))
-    return rows, slots
-
-
 def combine(y: torch.Tensor, pos_of: torch.Tensor, w, T: int, k: int, y_shared=None,
             out_dtype=torch.bfloat16) -> torch.Tensor:
     """out[t] = sum_l w[t,l] * y[pos_of[t*k+l]] (+ y_shared[t]); y fp32 or fp16; pos < 0 skips."""
@@ -254,32 +232,6 @@ def combine(y: torch.Tensor, pos_of: torch.Tensor, w, T: int, k: int, y_shared=N
     check(_lib.load().vfmoe_combine(_ptr(y), _DT[y.dtype], _ptr(pos_of), _ptr(w), T, k, H, _ptr(y_shared), _ptr(out),
                                     _DT[out_dtype], _stream()))
     return out
-
-
-def ep_plan_tokens(idx: torch.Tensor, w: torch.Tensor, n_experts: int, placement: torch.Tensor,
-                   local_slot: torch.Tensor, n_ranks: int):
-    """Token-level send plan: (send_counts [n_ranks], send_tok [T*n_ranks], send_slot [T*n_ranks, k],
-    send_w [T*n_ranks, k], pos_of [T, n_ranks]); entries [0, sum(send_counts)) are valid."""
-    T, k = idx.shape
-    dev = idx.device
-    counts = torch.empty(n_ranks, dtype=torch.int32, device=dev)
-    n = T * n_ranks
-    tok = torch.empty(n, dtype=torch.int32, device=dev)
-    slot = torch.empty((n, k), dtype=torch.int32, device=dev)
-    sw = torch.empty((n, k), dtype=torch.float32, device=dev)
-    pos = torch.empty((T, n_ranks), dtype=torch.int32, device=dev)
-    check(_lib.load().vfmoe_ep_plan_tokens(_ptr(idx), _ptr(w), T, k, n_experts, _ptr(placement), _ptr(local_slot),
-                                           n_ranks, _ptr(counts), _ptr(tok), _ptr(slot), _ptr(sw), _ptr(pos), 0,
-                                           _stream()))
-    return counts, tok, slot, sw, pos
-
-
-def gather_rows(x: torch.Tensor, tok: torch.Tensor, n: int) -> torch.Tensor:
-    """rows[i] = x[tok[i]] for i < n (x dtype)."""
-    rows = torch.empty((n, x.shape[1]), dtype=x.dtype, device=x.device)
-    check(_lib.load().vfmoe_ep_pack(_ptr(x), _DT[x.dtype], x.shape[1], 1, 0, _ptr(tok), 0, n, _ptr(rows), 0,
-                                    _stream()))
-    return rows
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

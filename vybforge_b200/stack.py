@@ -6,7 +6,7 @@ uses the plain pre-norm residual instead.  The oracle's ``moe_stack`` mirrors it
 
 - ``MoEStack``: all layers on one GPU.
 - ``EpStack``: one rank's share of the expert-parallel stack.  Tokens are sharded over
-  ranks; each layer is an ``ep.EpRank`` over this rank's experts.
+  ranks; each layer is an ``ep.EpLayer`` over this rank's experts (``vfmoe_ep_forward``).
 
 Every step is a libvfmoe kernel:
 - ``vfmoe_residual_rmsnorm`` fuses layer l's residual add with layer l+1's input norm.
@@ -45,33 +45,35 @@ class MoEStack:
 
 
 class EpStack:
-    def __init__(self, ranks, norm_w, eps: float = 1e-5):
-        """ranks: list (one per layer) of ep.EpRank of this process's rank."""
-        assert len(ranks) == len(norm_w) and ranks
-        self.ranks, self.norm_w, self.eps = ranks, norm_w, eps
+    def __init__(self, layers, norm_w, eps: float = 1e-5):
+        """layers: list (one per layer) of ep.EpLayer of this process's rank."""
+        assert len(layers) == len(norm_w) and layers
+        self.layers, self.norm_w, self.eps = layers, norm_w, eps
 
-    def forward_dist(self, x: torch.Tensor, transport, mark=None) -> torch.Tensor:
-        """This rank's tokens through all layers (one rank per process); mark as in
-        ep.ep_forward_dist, plus "norm" after each residual/norm step."""
-        L = len(self.ranks)
+    def forward(self, comm, x: torch.Tensor, mark=None) -> torch.Tensor:
+        """This rank's tokens through all layers over the library's NCCL communicator `comm`
+        (ep.EpComm); mark(name), if given, is called after each norm and each layer."""
+        L = len(self.layers)
         x, h = residual_rmsnorm(x, None, self.norm_w[0], self.eps)
         if mark:
             mark("norm")
-        for l, r in enumerate(self.ranks):
-            y = ep.ep_forward_dist(r, h, transport, mark)
+        for l, lay in enumerate(self.layers):
+            y = lay.forward(comm, h)
+            if mark:
+                mark("layer")
             x, h = residual_rmsnorm(x, y, self.norm_w[l + 1] if l + 1 < L else None, self.eps)
             if mark:
                 mark("norm")
         return x
 
 
-def ep_stack_forward_virtual(stacks, xs, transport):
-    """N virtual ranks held by one process (see ep.VirtualTransport)."""
-    L = len(stacks[0].ranks)
+def ep_stack_forward_virtual(stacks, xs):
+    """N virtual ranks held by one process (see ep.ep_forward_virtual)."""
+    L = len(stacks[0].layers)
     eps = stacks[0].eps
     state = [residual_rmsnorm(x, None, s.norm_w[0], eps) for s, x in zip(stacks, xs)]
     for l in range(L):
-        ys = ep.ep_forward_virtual([s.ranks[l] for s in stacks], [h for _, h in state], transport)
+        ys = ep.ep_forward_virtual([s.layers[l] for s in stacks], [h for _, h in state])
         state = [residual_rmsnorm(x, y, s.norm_w[l + 1] if l + 1 < L else None, eps)
                  for s, (x, _), y in zip(stacks, state, ys)]
     return [x for x, _ in state]

@@ -148,28 +148,34 @@ def stack_inputs(cfg: LayerConfig, n_layers: int, calib_tokens: int = 2048):
     Returns (x, norm_ws, routers): x the stack input (cfg's ordinary token draw), norm_ws
     a list of fp32 [H] RMSNorm weights 1 + N(0, 0.02), routers a list of (w_r, bias,
     load) per layer.  Layer l's router (W_r ~ N(0, 0.02), bias ~ N(0, 0.01)) is drawn
-    from the stream seeded (seed, 1000 + l).  With
-    cfg.zipf_s > 0 its selection bias is calibrated (as in zipf_router_inputs) on the
-    first `calib_tokens` rows of RMSNorm_l(x): later layers see the residual stream
-    instead, so their realized popularity is only approximately Zipf.  load is the layer's
-    selection count per expert on RMSNorm_l(x) over all tokens (the expert-placement input;
-    layers after the first see the residual stream, so it is an estimate there)."""
+    from the stream seeded (seed, 1000 + l).
+
+    Everything fitted to tokens is fitted on a calibration batch drawn from its own stream
+    (seed, 3000), disjoint from x, as a server fits its placement on earlier traffic: with
+    cfg.zipf_s > 0 the selection bias is calibrated (as in zipf_router_inputs) on the first
+    `calib_tokens` calibration rows of RMSNorm_l, and load is the layer's selection count per
+    expert over a calibration batch of x's size (the expert-placement input).  Layers after the
+    first see the residual stream, so their realized popularity is only approximately Zipf and
+    their load an estimate."""
     x, _, _, rng = router_inputs(cfg)
     norm_ws = [(1.0 + rng.normal(0.0, 0.02, cfg.hidden)).astype(np.float32) for _ in range(n_layers)]
+    xc = np.random.default_rng((cfg.seed, 3000)).standard_normal(x.shape).astype(np.float32)
+    if cfg.x_dtype == "bf16":
+        xc = round_bf16(xc)
     routers = []
     for l in range(n_layers):
         r_l = np.random.default_rng((cfg.seed, 1000 + l))
         w_r = r_l.normal(0.0, 0.02, (cfg.n_experts, cfg.hidden)).astype(np.float32)
         bias0 = r_l.normal(0.0, 0.01, cfg.n_experts).astype(np.float32)
         if cfg.zipf_s > 0:
-            xs = x[:calib_tokens].astype(np.float64)
+            xs = xc[:calib_tokens].astype(np.float64)
             h = xs / np.sqrt(np.mean(xs * xs, axis=1, keepdims=True) + 1e-5) * norm_ws[l]
             logits = h @ w_r.astype(np.float64).T
             tgt = zipf_targets(cfg.n_experts, len(xs), cfg.topk, cfg.zipf_s, np.random.default_rng((cfg.seed, 2000 + l)))
             bias = calibrate_zipf_bias(logits, bias0, cfg.topk, tgt)
         else:
             bias = bias0
-        routers.append((w_r, bias, selection_counts(x, norm_ws[l], w_r, bias, cfg.topk)))
+        routers.append((w_r, bias, selection_counts(xc, norm_ws[l], w_r, bias, cfg.topk)))
     return x, norm_ws, routers
 
 
