@@ -373,7 +373,13 @@ def dequant_exl3(trellis, suh, svh, bits, slot_table=None):
     The reference evaluates this in float32 and rounds W to fp16; the oracle
     keeps float64 so the only rounding left is the GPU's own.
     """
-    what = exl3_what(trellis, bits, slot_table)
+    return dequant_exl3_from_what(exl3_what(trellis, bits, slot_table), suh, svh)
+
+
+def dequant_exl3_from_what(what, suh, svh):
+    """The reconstruction step of dequant_exl3 alone (exl3_ref.py:116-120): W from the decoded
+    rotated-basis values W^ [K, N], float64."""
+    what = np.asarray(what, np.float64)
     k, n = what.shape
     hs = hadamard128() * R_SCALE
     # per 128x128 block (i, j): Hs . W^[i, j] . Hs

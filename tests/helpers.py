@@ -29,8 +29,13 @@ def to_dev_x(x, cfg):
 class Built:
     """A device layer + host-side copies for the oracle."""
 
-    def __init__(self, cfg, weights="numpy", out_dtype=torch.float32, router=None, path="auto"):
+    def __init__(self, cfg, weights="numpy", out_dtype=torch.float32, router=None, path="auto", what="oracle"):
+        """what="gpu" (EXL3 only): the oracle takes each expert's rotated-basis values W^ from
+        vfmoe_exl3_decode, which tests/test_gpu_parity.py pins bit-exact to the oracle's own
+        decode (and the reference's 4-bpw fixture), and reconstructs W in float64 itself; the
+        numpy trellis decode costs seconds per full-size matrix."""
         self.path = path
+        self.what = what
         self.cfg = cfg
         if router is None:
             x, w_r, bias, rng = synth.router_inputs(cfg)
@@ -82,6 +87,12 @@ class Built:
     def expert(self, e):
         if e not in self._cache and self.cfg.fmt == "exl3":
             def mat(p):
+                if self.what == "gpu":
+                    from vybforge_b200 import moe as _moe
+                    tr_d, suh_d, svh_d = (a[e] for a in self.dev[p])
+                    K, N = suh_d.shape[0], svh_d.shape[0]
+                    what = _moe.exl3_decode(tr_d.contiguous(), K, N, self.cfg.exl3_bits).cpu().numpy()
+                    return orc.dequant_exl3_from_what(what, suh_d.cpu().numpy(), svh_d.cpu().numpy())
                 tr, suh, svh = (a[e].cpu().numpy() for a in self.dev[p])
                 return orc.dequant_exl3(tr.view(np.uint16), suh, svh, self.cfg.exl3_bits)
             self._cache[e] = (mat(0), mat(1), mat(2))
