@@ -336,6 +336,38 @@ int vfmoe_rmsnorm(int64_t x, int64_t w, int64_t y, int64_t S, int64_t D, double 
 int vfmoe_residual_rmsnorm(int64_t x, int64_t y, int64_t w, int64_t x_out, int64_t h, int64_t S,
                            int64_t D, double eps, int64_t dtype, int64_t stream);
 
+/* ---- hyper-connections around the MoE (GLM-5.3 multi-stream residual) ----
+ * A layer keeps n_streams = 4 residual streams of width hidden per token, fp32 [R][4][hidden].
+ * Per sublayer site the checkpoint holds fn [24][4 * hidden] (bf16 or fp32; 24 = 4 pre + 4 post
+ * + 16 comb), base fp32 [24] and scale fp32 [3]. */
+typedef struct vfmoe_hc_desc {
+    int64_t n_streams;      /* 4 */
+    int64_t hidden;         /* D: 2048, 4096, 6144 or 8192 */
+    int64_t fn;             /* device [24][4 * hidden] */
+    int64_t fn_dtype;       /* VFMOE_DT_BF16 or VFMOE_DT_F32 */
+    int64_t base;           /* device fp32 [24] */
+    int64_t scale;          /* device fp32 [3]: pre, post, comb */
+    double rms_eps;         /* unweighted RMSNorm of the flattened streams */
+    double hc_eps;          /* 1e-6 in GLM-5.3 */
+    int64_t sinkhorn_iters; /* 20 in GLM-5.3 */
+    int64_t norm_w;         /* device fp32 [hidden]: the layernorm before the sublayer; 0 = none */
+    double norm_eps;
+} vfmoe_hc_desc;
+
+/* Mix (hc_glue, native/glm53/glm_engine.vyb:437-612; hc_ref.mix, native/glm53/hc_ref.py:27-57)
+ * fused with the RMSNorm that feeds the sublayer:
+ *   pre, post, comb from RMSNorm(streams[r]) . fn^T (Sinkhorn-normalised comb),
+ *   h[r] = RMSNorm_norm_w(sum_h pre[h] * streams[r, h])   (h_dtype BF16 or F32)
+ * post fp32 [R][4] and comb fp32 [R][4][4] are kept for vfmoe_hc_apply. */
+int vfmoe_hc_mix(const vfmoe_hc_desc *desc, int64_t streams, int64_t R, int64_t h_out, int64_t h_dtype,
+                 int64_t post_out, int64_t comb_out, int64_t stream);
+
+/* Apply (hc_apply, glm_engine.vyb:783-809; hc_ref.apply_, hc_ref.py:60-63):
+ *   out[r, h] = post[r, h] * y[r] + sum_j comb[r, j, h] * streams[r, j]
+ * y [R][hidden] (y_dtype BF16 or F32), out fp32 [R][4][hidden]; out may be streams itself. */
+int vfmoe_hc_apply(int64_t streams, int64_t y, int64_t y_dtype, int64_t post, int64_t comb, int64_t R,
+                   int64_t n_streams, int64_t hidden, int64_t out, int64_t stream);
+
 /* Q8_0 rows -> dense [rows, k] (dst_dtype VFMOE_DT_F32 or VFMOE_DT_F16).
  * Replaces q8_0deq (native/kernels/q8_0.vyb:11-30, which widens to f64). */
 int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k,

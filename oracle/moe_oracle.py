@@ -14,6 +14,8 @@ rickenator/VybForge for this path (paths relative to the reference project):
 * EXL3 value decode native/exl3/exl3_ref.py:37-47   (``decode_mcg``)
 * EXL3 reconstruct  native/exl3/exl3_ref.py:58-63, 84-120
 * RMSNorm           native/kernels/rmsnorm.vyb (y = x * w / sqrt(mean(x^2) + eps))
+* hyper-connections native/glm53/hc_ref.py:27-63 (``hc_mix``, ``hc_apply``); the engine's
+                    hc_glue / hc_apply, native/glm53/glm_engine.vyb:437-612, :783-809
 
 Deliberate differences from the reference, each required by the task spec:
 
@@ -386,3 +388,41 @@ def dequant_exl3_from_what(what, suh, svh):
     w = (hs @ what.reshape(k // 128, 128, n)).reshape(k, n // 128, 128) @ hs
     w = w.reshape(k, n)
     return w * np.asarray(suh, np.float64)[:, None] * np.asarray(svh, np.float64)[None, :]
+
+
+# --------------------------------------------------------------------------- hyper-connections
+HC_EPS = 1e-6          # hc_eps (hc_ref.py:23)
+SINKHORN_ITERS = 20    # hc_sinkhorn_iters (hc_ref.py:24)
+
+
+def hc_mix(streams, fn, base, scale, rms_eps, hc_eps=HC_EPS, sinkhorn_iters=SINKHORN_ITERS):
+    """Multi-stream mix of hc_ref.py:31-57 in float64.
+
+    streams (R, HC, D); fn (24, HC*D) (out, in); base (24,); scale (3,).
+    Returns (post (R, HC), comb (R, HC, HC), collapsed (R, D), pre (R, HC))."""
+    streams = np.asarray(streams, np.float64)
+    R, hc, D = streams.shape
+    flat = streams.reshape(R, hc * D)
+    flat = flat / np.sqrt(np.mean(flat * flat, axis=-1, keepdims=True) + rms_eps)
+    mv = flat @ np.asarray(fn, np.float64).T
+    base = np.asarray(base, np.float64)
+    s0, s1, s2 = (float(v) for v in scale)
+    pre = sigmoid(mv[:, :hc] * s0 + base[:hc]) + hc_eps
+    post = 2.0 * sigmoid(mv[:, hc:2 * hc] * s1 + base[hc:2 * hc])
+    comb = mv[:, 2 * hc:].reshape(R, hc, hc) * s2 + base[2 * hc:].reshape(hc, hc)
+    e = np.exp(comb - comb.max(axis=-1, keepdims=True))
+    comb = e / e.sum(axis=-1, keepdims=True) + hc_eps
+    comb = comb / (comb.sum(axis=-2, keepdims=True) + hc_eps)
+    for _ in range(sinkhorn_iters - 1):
+        comb = comb / (comb.sum(axis=-1, keepdims=True) + hc_eps)
+        comb = comb / (comb.sum(axis=-2, keepdims=True) + hc_eps)
+    collapsed = (pre[:, :, None] * streams).sum(axis=1)
+    return post, comb, collapsed, pre
+
+
+def hc_apply(streams, y, post, comb):
+    """Residual update of hc_ref.py:60-63: out[r, h] = post[r, h] y[r] + sum_j comb[r, j, h] streams[r, j]."""
+    streams = np.asarray(streams, np.float64)
+    return (np.asarray(post, np.float64)[:, :, None] * np.asarray(y, np.float64)[:, None, :]
+            + np.einsum("rjh,rjd->rhd", np.asarray(comb, np.float64), streams))
+

@@ -4,11 +4,15 @@ Python modules (rickenator/VybForge):
   native/glm53/moe_ref.py   route / moe_block (router + clamped SwiGLU block)
   native/tools/q8_0_ref.py  q8_0_ours (Q8_0 block decode)
   native/exl3/exl3_ref.py   decode_mcg, dequant_exl3 (4-bpw, verified slot map)
+  native/glm53/hc_ref.py    mix / apply_ (GLM-5.3 hyper-connections)
 
 Usage (needs the reference checkout; the fixtures are committed, so the tests
 themselves never read the reference):
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py [REFERENCE_ROOT [c0 q8 exl3 hc]]
+
+REFERENCE_ROOT defaults to $VYBFORGE_REFERENCE, else a "reference" checkout beside this
+repository.
 
 Inputs are regenerated from seeds by vybforge_b200.synth; each fixture stores
 the sha256 of every input array so generator drift is caught, plus the
@@ -29,7 +33,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 from vybforge_b200 import synth  # noqa: E402
-from vybforge_b200.quant import quantize_q8_0  # noqa: E402
+from vybforge_b200.quant import quantize_q8_0, f32_to_bf16_bits  # noqa: E402
 
 
 def sha(a) -> str:
@@ -101,13 +105,35 @@ def exl3_fixture(ref):
     print("exl3_kat.npz: 65536 windows, W", w4.shape)
 
 
+def hc_fixture(ref):
+    """Hyper-connections: the reference's hc_ref.mix / apply_ on seeded streams (R=3, HC=4, D=2048)
+    with bf16-valued fn, and the reference engine's default eps values."""
+    hc = load_module("hc_ref", os.path.join(ref, "native/glm53/hc_ref.py"))
+    rng = np.random.default_rng(23)
+    R, HC, D = 3, 4, 2048
+    streams = (rng.standard_normal((R, HC, D)) * rng.uniform(0.5, 2.0, (R, HC, 1))).astype(np.float32)
+    fn_bits = f32_to_bf16_bits((rng.standard_normal((24, HC * D)) * 0.02).astype(np.float32))
+    fn = (fn_bits.astype(np.uint32) << 16).view(np.float32)
+    base = rng.normal(0, 0.5, 24).astype(np.float32)
+    scale = np.array([0.8, 1.3, 2.0], np.float32)
+    y = rng.standard_normal((R, D)).astype(np.float32)
+    post, comb, collapsed, pre = hc.mix(streams, fn, base, scale, 1e-5)
+    out = hc.apply_(streams, y, post, comb)
+    np.savez_compressed(os.path.join(HERE, "hc_kat.npz"), streams=streams, fn_bits=fn_bits, base=base, scale=scale,
+                        y=y, rms_eps=np.float64(1e-5), hc_eps=np.float64(hc.Hc_EPS),
+                        iters=np.int64(hc.SINKHORN_ITERS), post=post, comb=comb, collapsed=collapsed, pre=pre,
+                        out=out)
+    print("hc_kat.npz: R", R, "D", D)
+
+
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
+        "VYBFORGE_REFERENCE", os.path.normpath(os.path.join(REPO, os.pardir, "reference")))
     if not os.path.isdir(os.path.join(ref, "native")):
         sys.exit(f"reference checkout not found at {ref}")
-    c0_fixture(ref)
-    q8_fixture(ref)
-    exl3_fixture(ref)
+    which = sys.argv[2:] or ["c0", "q8", "exl3", "hc"]
+    for name in which:
+        {"c0": c0_fixture, "q8": q8_fixture, "exl3": exl3_fixture, "hc": hc_fixture}[name](ref)
 
 
 if __name__ == "__main__":

@@ -56,6 +56,12 @@ class LayerDesc(C.Structure):
                 ("expert_path", C.c_int64)]
 
 
+class HcDesc(C.Structure):
+    _fields_ = [("n_streams", C.c_int64), ("hidden", C.c_int64), ("fn", C.c_int64), ("fn_dtype", C.c_int64),
+                ("base", C.c_int64), ("scale", C.c_int64), ("rms_eps", C.c_double), ("hc_eps", C.c_double),
+                ("sinkhorn_iters", C.c_int64), ("norm_w", C.c_int64), ("norm_eps", C.c_double)]
+
+
 I64 = C.c_int64
 _SIGS = {
     "vfmoe_version": (C.c_int, []),
@@ -89,6 +95,8 @@ _SIGS = {
     "vfmoe_profile_enable": (C.c_int, [I64, C.c_int]),
     "vfmoe_profile_read": (C.c_int, [I64, C.POINTER(C.c_double), I64, C.POINTER(I64)]),
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),
+    "vfmoe_hc_mix": (C.c_int, [C.POINTER(HcDesc), I64, I64, I64, I64, I64, I64, I64]),
+    "vfmoe_hc_apply": (C.c_int, [I64] * 10),
     "vfmoe_residual_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_q8_0_dequant": (C.c_int, [I64] * 6),
     "vfmoe_q8_0_quantize": (C.c_int, [I64] * 5),

@@ -741,6 +741,37 @@ int vfmoe_residual_rmsnorm(int64_t x, int64_t y, int64_t w, int64_t x_out, int64
                                    reinterpret_cast<cudaStream_t>(stream));
 }
 
+int vfmoe_hc_mix(const vfmoe_hc_desc *d, int64_t streams, int64_t R, int64_t h_out, int64_t h_dtype,
+                 int64_t post_out, int64_t comb_out, int64_t stream) {
+    if (!d || d->n_streams != 4 || d->hidden <= 0 || d->hidden % 2048 || d->hidden > 8192 || !d->fn || !d->base ||
+        !d->scale || (d->fn_dtype != VFMOE_DT_BF16 && d->fn_dtype != VFMOE_DT_F32) || d->sinkhorn_iters < 1 ||
+        d->sinkhorn_iters > 1000 || d->rms_eps < 0 || d->hc_eps < 0 || d->norm_eps < 0 || R < 0 ||
+        (R > 0 && (!streams || !h_out || !post_out || !comb_out)) || (streams & 15) || (d->fn & 15) ||
+        (d->norm_w & 15) || (h_dtype != VFMOE_DT_BF16 && h_dtype != VFMOE_DT_F32)) {
+        set_error("vfmoe_hc_mix: bad arguments (4 streams, hidden a multiple of 2048 up to 8192, 16-byte aligned "
+                  "streams / fn / norm_w)");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_hc_mix(reinterpret_cast<const float *>(streams), R, (int)d->hidden, reinterpret_cast<const void *>(d->fn),
+                         (int)d->fn_dtype, reinterpret_cast<const float *>(d->base),
+                         reinterpret_cast<const float *>(d->scale), (float)d->rms_eps, d->hc_eps, (int)d->sinkhorn_iters,
+                         reinterpret_cast<const float *>(d->norm_w), (float)d->norm_eps, reinterpret_cast<void *>(h_out),
+                         (int)h_dtype, reinterpret_cast<float *>(post_out), reinterpret_cast<float *>(comb_out),
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vfmoe_hc_apply(int64_t streams, int64_t y, int64_t y_dtype, int64_t post, int64_t comb, int64_t R,
+                   int64_t n_streams, int64_t hidden, int64_t out, int64_t stream) {
+    if (n_streams != 4 || hidden <= 0 || hidden % 4 || R < 0 || (y_dtype != VFMOE_DT_BF16 && y_dtype != VFMOE_DT_F32) ||
+        (R > 0 && (!streams || !y || !post || !comb || !out)) || (streams & 15) || (out & 15)) {
+        set_error("vfmoe_hc_apply: bad arguments (4 streams, hidden a multiple of 4, 16-byte aligned streams/out)");
+        return VFMOE_ERR_INVALID;
+    }
+    return launch_hc_apply(reinterpret_cast<const float *>(streams), reinterpret_cast<const void *>(y), (int)y_dtype,
+                           reinterpret_cast<const float *>(post), reinterpret_cast<const float *>(comb), R, (int)hidden,
+                           reinterpret_cast<float *>(out), reinterpret_cast<cudaStream_t>(stream));
+}
+
 int vfmoe_q8_0_dequant(int64_t src, int64_t dst, int64_t rows, int64_t k, int64_t dst_dtype, int64_t stream) {
     if (rows < 0 || k <= 0 || k % 32 || (rows > 0 && (!src || !dst)) ||
         (dst_dtype != VFMOE_DT_F32 && dst_dtype != VFMOE_DT_F16)) {

@@ -1,0 +1,235 @@
+// Hyper-connections around the MoE sublayer of a GLM-5.3 layer (multi-stream residual, "mHC").
+//
+// Reference: hc_glue / hc_apply (native/glm53/glm_engine.vyb:437-612, :783-809) and their numpy
+// definition native/glm53/hc_ref.py:27-63 (mix, apply_), used by tail_site around the MoE
+// (glm_engine.vyb:1922-1952 shows the same pattern at the attention site).  Per token row r
+// the layer keeps HC = 4 residual streams of width D (fp32):
+//
+//   flat      = streams[r] / rms(streams[r])                      (unweighted, over HC*D)
+//   mv        = flat . fn^T                                       (24 = HC + HC + HC*HC values)
+//   pre[h]    = sigmoid(mv[h] * scale0 + base[h]) + hc_eps
+//   post[h]   = 2 sigmoid(mv[HC+h] * scale1 + base[HC+h])
+//   comb      = softmax_rows(mv[2HC..] * scale2 + base[2HC..]) + hc_eps, then column-normalised,
+//               then (iters - 1) x {row-normalise, column-normalise}     (Sinkhorn)
+//   collapsed = sum_h pre[h] * streams[r, h]                       (the sublayer's input)
+//   h         = RMSNorm_w(collapsed)                               (the post-attention layernorm)
+// and after the sublayer (y = MoE(h)):
+//   streams'[r, h] = post[h] * y[r] + sum_j comb[j, h] * streams[r, j]
+//
+// hc_mix_kernel: one CTA (512 threads) per row, the whole mix fused.  Thread t holds the four
+// streams' values at d = 4t + 2048q (q < D/2048) in registers, so the collapse and both norms
+// need no exchange beyond two block reductions; fn (bf16 or fp32 [24][HC*D]) is read once per
+// row (L2-resident across rows).  The 4x4 normalisation runs in fp64 on one thread.
+// hc_apply_kernel: streaming, HBM-bound (HC*D reads + D reads + HC*D writes per row).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vfmoe {
+
+constexpr int kHc = 4;                 // streams (hc_mult of GLM-5.3)
+constexpr int kHcMix = 2 * kHc + kHc * kHc;   // 24 mix values per row
+constexpr int kHcThreads = 512;
+
+__device__ __forceinline__ float4 ld_fn4(const void *fn, int fn_dtype, int64_t i) {
+    if (fn_dtype == VFMOE_DT_BF16) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(fn) + i);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xFFFF0000u));
+    }
+    return *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(fn) + i);
+}
+
+// Block-wide sum of NV doubles per thread (512 threads); every thread gets the totals.
+template <int NV>
+__device__ __forceinline__ void block_sum(double (&v)[NV], double *red /* [16][NV] */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = warp_sum_f64(v[i]);
+    if (lane == 0)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) red[warp * NV + i] = v[i];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        double s = 0.0;
+        for (int w = 0; w < kHcThreads / 32; ++w) s += red[w * NV + i];
+        v[i] = s;
+    }
+    __syncthreads();
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(const float *__restrict__ streams, int D,
+                                                            const void *__restrict__ fn, int fn_dtype,
+                                                            const float *__restrict__ base, const float *__restrict__ scale,
+                                                            float rms_eps, double hc_eps, int iters,
+                                                            const float *__restrict__ norm_w, float norm_eps,
+                                                            void *__restrict__ h_out, int h_dtype,
+                                                            float *__restrict__ post_out, float *__restrict__ comb_out) {
+    __shared__ double red[16 * (kHcMix + 1)];
+    __shared__ float s_pre[kHc];
+    const int64_t r = blockIdx.x;
+    const int t = threadIdx.x;
+    const float *row = streams + r * kHc * D;
+    float4 x[kHc][VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int h = 0; h < kHc; ++h)
+#pragma unroll
+        for (int q = 0; q < VPT; ++q) {
+            x[h][q] = *reinterpret_cast<const float4 *>(row + h * D + 4 * t + 2048 * q);
+            ss += x[h][q].x * x[h][q].x + x[h][q].y * x[h][q].y + x[h][q].z * x[h][q].z + x[h][q].w * x[h][q].w;
+        }
+    // mix values of the raw row (the 1/rms factor is applied to the totals); per-thread partial
+    // sums in fp32 (64 VPT products), the block reduction in fp64
+    double acc[kHcMix + 1];
+#pragma unroll
+    for (int j = 0; j < kHcMix; ++j) {
+        float a = 0.f;
+#pragma unroll
+        for (int h = 0; h < kHc; ++h)
+#pragma unroll
+            for (int q = 0; q < VPT; ++q) {
+                const float4 f = ld_fn4(fn, fn_dtype, (int64_t)j * kHc * D + h * D + 4 * t + 2048 * q);
+                a = fmaf(x[h][q].x, f.x, a);
+                a = fmaf(x[h][q].y, f.y, a);
+                a = fmaf(x[h][q].z, f.z, a);
+                a = fmaf(x[h][q].w, f.w, a);
+            }
+        acc[j] = a;
+    }
+    acc[kHcMix] = ss;
+    block_sum<kHcMix + 1>(acc, red);
+    const double inv = 1.0 / sqrt(acc[kHcMix] / (double)(kHc * D) + (double)rms_eps);
+    if (t == 0) {
+        double pre[kHc], post[kHc], c[kHc][kHc];
+        const double s0 = scale[0], s1 = scale[1], s2 = scale[2];
+        for (int h = 0; h < kHc; ++h) {
+            pre[h] = 1.0 / (1.0 + exp(-(acc[h] * inv * s0 + base[h]))) + hc_eps;
+            post[h] = 2.0 / (1.0 + exp(-(acc[kHc + h] * inv * s1 + base[kHc + h])));
+        }
+        for (int a = 0; a < kHc; ++a) {
+            double mx = -1e300;
+            for (int b = 0; b < kHc; ++b) {
+                c[a][b] = acc[2 * kHc + a * kHc + b] * inv * s2 + base[2 * kHc + a * kHc + b];
+                mx = fmax(mx, c[a][b]);
+            }
+            double sm = 0.0;
+            for (int b = 0; b < kHc; ++b) sm += (c[a][b] = exp(c[a][b] - mx));
+            for (int b = 0; b < kHc; ++b) c[a][b] = c[a][b] / sm + hc_eps;
+        }
+        for (int it = 0; it < iters; ++it) {
+            if (it > 0)
+                for (int a = 0; a < kHc; ++a) {
+                    double sm = 0.0;
+                    for (int b = 0; b < kHc; ++b) sm += c[a][b];
+                    for (int b = 0; b < kHc; ++b) c[a][b] /= sm + hc_eps;
+                }
+            for (int b = 0; b < kHc; ++b) {
+                double sm = 0.0;
+                for (int a = 0; a < kHc; ++a) sm += c[a][b];
+                for (int a = 0; a < kHc; ++a) c[a][b] /= sm + hc_eps;
+            }
+        }
+        for (int h = 0; h < kHc; ++h) {
+            s_pre[h] = (float)pre[h];
+            post_out[r * kHc + h] = (float)post[h];
+        }
+        for (int a = 0; a < kHc; ++a)
+            for (int b = 0; b < kHc; ++b) comb_out[(r * kHc + a) * kHc + b] = (float)c[a][b];
+    }
+    __syncthreads();
+    // collapse, then the weighted RMSNorm over D
+    float4 col[VPT];
+    double ss2[1] = {0.0};
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < kHc; ++h) {
+            const float p = s_pre[h];
+            v.x = fmaf(p, x[h][q].x, v.x);
+            v.y = fmaf(p, x[h][q].y, v.y);
+            v.z = fmaf(p, x[h][q].z, v.z);
+            v.w = fmaf(p, x[h][q].w, v.w);
+        }
+        col[q] = v;
+        ss2[0] += (double)(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    }
+    float inv2 = 1.f;
+    if (norm_w) {
+        block_sum<1>(ss2, red);
+        inv2 = (float)(1.0 / sqrt(ss2[0] / (double)D + (double)norm_eps));
+    }
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+        const int d = 4 * t + 2048 * q;
+        float4 wv = norm_w ? *reinterpret_cast<const float4 *>(norm_w + d) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float o[4] = {col[q].x * inv2 * wv.x, col[q].y * inv2 * wv.y, col[q].z * inv2 * wv.z,
+                            col[q].w * inv2 * wv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st_act(h_out, r * D + d + i, o[i], h_dtype);
+    }
+}
+
+// grid (R, D / 1024), 256 threads x 4 columns.  out may alias streams: every thread reads its
+// four streams' values at its columns before writing them.
+__global__ void __launch_bounds__(256) hc_apply_kernel(const float *__restrict__ streams, const void *__restrict__ y,
+                                                       int y_dtype, const float *__restrict__ post,
+                                                       const float *__restrict__ comb, int D, float *out) {
+    const int64_t r = blockIdx.x;
+    const int d = (blockIdx.y * 256 + threadIdx.x) * 4;
+    if (d >= D) return;
+    float p[kHc], c[kHc][kHc];
+#pragma unroll
+    for (int h = 0; h < kHc; ++h) p[h] = post[r * kHc + h];
+#pragma unroll
+    for (int j = 0; j < kHc; ++j)
+#pragma unroll
+        for (int h = 0; h < kHc; ++h) c[j][h] = comb[(r * kHc + j) * kHc + h];
+    float4 s[kHc];
+#pragma unroll
+    for (int j = 0; j < kHc; ++j) s[j] = *reinterpret_cast<const float4 *>(streams + (r * kHc + j) * D + d);
+    const float yv[4] = {ld_act(y, r * D + d, y_dtype), ld_act(y, r * D + d + 1, y_dtype),
+                         ld_act(y, r * D + d + 2, y_dtype), ld_act(y, r * D + d + 3, y_dtype)};
+#pragma unroll
+    for (int h = 0; h < kHc; ++h) {
+        float4 o = make_float4(p[h] * yv[0], p[h] * yv[1], p[h] * yv[2], p[h] * yv[3]);
+#pragma unroll
+        for (int j = 0; j < kHc; ++j) {
+            o.x = fmaf(c[j][h], s[j].x, o.x);
+            o.y = fmaf(c[j][h], s[j].y, o.y);
+            o.z = fmaf(c[j][h], s[j].z, o.z);
+            o.w = fmaf(c[j][h], s[j].w, o.w);
+        }
+        *reinterpret_cast<float4 *>(out + (r * kHc + h) * D + d) = o;
+    }
+}
+
+int launch_hc_mix(const float *streams, int64_t R, int D, const void *fn, int fn_dtype, const float *base,
+                  const float *scale, float rms_eps, double hc_eps, int iters, const float *norm_w, float norm_eps,
+                  void *h_out, int h_dtype, float *post, float *comb, cudaStream_t st) {
+    if (R == 0) return VFMOE_OK;
+    switch (D / 2048) {
+        case 1: hc_mix_kernel<1><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
+        case 2: hc_mix_kernel<2><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
+        case 3: hc_mix_kernel<3><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
+        case 4: hc_mix_kernel<4><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
+        default:
+            set_error("hyper-connection mix: D = %d (2048, 4096, 6144 or 8192 supported)", D);
+            return VFMOE_ERR_UNSUPPORTED;
+    }
+    VF_LAUNCH_CHECK("hc_mix_kernel");
+    return VFMOE_OK;
+}
+
+int launch_hc_apply(const float *streams, const void *y, int y_dtype, const float *post, const float *comb, int64_t R,
+                    int D, float *out, cudaStream_t st) {
+    if (R == 0) return VFMOE_OK;
+    dim3 grid((unsigned)R, (unsigned)cdiv(D, 1024));
+    hc_apply_kernel<<<grid, 256, 0, st>>>(streams, y, y_dtype, post, comb, D, out);
+    VF_LAUNCH_CHECK("hc_apply_kernel");
+    return VFMOE_OK;
+}
+
+}  // namespace vfmoe

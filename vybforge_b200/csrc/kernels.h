@@ -61,6 +61,13 @@ int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const floa
 // `mid` runs between the gate/up and the down launches (profiling marks).
 int launch_experts_simt(const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
 
+// Hyper-connections (hc.cu): streams fp32 [R, 4, D], D in {2048, 4096, 6144, 8192}.
+int launch_hc_mix(const float *streams, int64_t R, int D, const void *fn, int fn_dtype, const float *base,
+                  const float *scale, float rms_eps, double hc_eps, int iters, const float *norm_w, float norm_eps,
+                  void *h_out, int h_dtype, float *post, float *comb, cudaStream_t st);
+int launch_hc_apply(const float *streams, const void *y, int y_dtype, const float *post, const float *comb, int64_t R,
+                    int D, float *out, cudaStream_t st);
+
 int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, float eps, int dtype,
                    cudaStream_t st);
 int launch_residual_rmsnorm(const void *x, const void *y, const float *w, void *x_out, void *h, int64_t S, int D,

@@ -254,6 +254,53 @@ def residual_rmsnorm(x: torch.Tensor, y: torch.Tensor | None, w: torch.Tensor | 
     return (x_out if y is not None else x), h
 
 
+class HyperConnection:
+    """One hyper-connection site of a GLM-5.3 layer (the multi-stream residual around the MoE):
+    fn [24, 4*D] (bf16 or fp32), base fp32 [24], scale fp32 [3], and the RMSNorm weight fp32 [D]
+    that feeds the sublayer (None: collapsed streams unnormalised).  Streams are fp32 [R, 4, D].
+    Mirrors hc_glue / hc_apply (native/glm53/glm_engine.vyb:437, :783)."""
+
+    def __init__(self, fn, base, scale, norm_w=None, rms_eps=1e-5, hc_eps=1e-6, sinkhorn_iters=20,
+                 norm_eps=1e-5):
+        D = fn.shape[1] // 4
+        d = _lib.HcDesc()
+        d.n_streams, d.hidden = 4, D
+        d.fn, d.fn_dtype = _ptr(fn), _DT[fn.dtype]
+        d.base, d.scale = _ptr(base), _ptr(scale)
+        d.rms_eps, d.hc_eps, d.sinkhorn_iters = rms_eps, hc_eps, sinkhorn_iters
+        d.norm_w, d.norm_eps = _ptr(norm_w), norm_eps
+        self.desc, self.D = d, D
+        self._keep = (fn, base, scale, norm_w)
+        self.lib = _lib.load()
+
+    def mix(self, streams: torch.Tensor, h_dtype=torch.bfloat16):
+        """(h [R, D] h_dtype, post fp32 [R, 4], comb fp32 [R, 4, 4]) from streams fp32 [R, 4, D]."""
+        R = streams.shape[0]
+        h = torch.empty((R, self.D), dtype=h_dtype, device=streams.device)
+        post = torch.empty((R, 4), dtype=torch.float32, device=streams.device)
+        comb = torch.empty((R, 4, 4), dtype=torch.float32, device=streams.device)
+        check(self.lib.vfmoe_hc_mix(C.byref(self.desc), _ptr(streams), R, _ptr(h), _DT[h_dtype], _ptr(post),
+                                    _ptr(comb), _stream()))
+        return h, post, comb
+
+    def apply(self, streams: torch.Tensor, y: torch.Tensor, post, comb, out: torch.Tensor | None = None):
+        """post * y + comb^T streams -> fp32 [R, 4, D] (out may be streams: in place)."""
+        R = streams.shape[0]
+        if out is None:
+            out = torch.empty_like(streams)
+        check(self.lib.vfmoe_hc_apply(_ptr(streams), _ptr(y), _DT[y.dtype], _ptr(post), _ptr(comb), R, 4, self.D,
+                                      _ptr(out), _stream()))
+        return out
+
+
+def hc_moe_site(site: HyperConnection, layer: MoELayer, streams: torch.Tensor, out: torch.Tensor | None = None):
+    """The MoE site of a GLM-5.3 layer (tail_site, native/glm53/glm_engine.vyb:2562-3019): mix the
+    streams, normalise, MoE, then the residual update of the streams."""
+    h, post, comb = site.mix(streams, h_dtype=layer.x_dtype)
+    y = layer.forward(h)
+    return site.apply(streams, y, post, comb, out=out)
+
+
 class _Quantizer:
     """Adapter used by synth.expert_q8_cuda."""
 
