@@ -272,6 +272,16 @@ def build_ours(cfg, rank, layout):
     return layer, xd, (x, w_r, bias), dev, (devl, wf)
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline_ours(cfg, host, dev, idx, budget_s):
     """Oracle (numpy, f64) on a bounded sample of this step's tokens, same bytes as the GPU."""
     from oracle import moe_oracle as orc
@@ -291,7 +301,7 @@ def cpu_baseline_ours(cfg, host, dev, idx, budget_s):
     orc.moe_block_grouped(x[:n], w_r, bias, get, lambda: get(E), E, cfg.topk)
     dt = time.perf_counter() - t0
     cores = os.cpu_count()
-    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port", "cpu_model": cpu_model(),
             "sample": f"first {n} of {cfg.tokens} tokens ({len(need)} experts incl. shared), oracle "
                       f"dequant+f64 GEMM per expert, numpy/OpenBLAS on {cores} host threads, {dt:.1f} s"}
 
@@ -713,7 +723,7 @@ def run_ours_ep(a, rank, world, local_rank):
            "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)}}
     if extra is not None:
-        res["extra"] = extra
+        res.update(extra)
     return res
 
 
@@ -841,66 +851,82 @@ def run_ours(a, rank, world, local_rank):
                           "layer_hbm_frac": round(l1b / (ms1 * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                           "stage_ms_per_step": {n: round(v, 4) for n, v in st1.items()}}
         extra["c3_prefill_q8_0"] = prefill_extra(a, cfg, devl, wf, flush)
-        res["extra"] = extra
+        res.update(extra)
     if rank == 0 and not a.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_ours(cfg, host, dev, idx_np, a.cpu_budget_s)
-    if "extra" in res:
+    if not a.no_extra and a.workload == "c1" and a.tokens is None and not a.experts:
         del dev, devl
         layer.close()
         torch.cuda.empty_cache()
-        res["extra"].update(stack_extra(a, rank, world, local_rank, flush))
+        res.update(stack_extra(a, rank, world, local_rank, flush))
         torch.cuda.empty_cache()
-        res["extra"].update(exl3_extra(a, flush))
+        res.update(exl3_extra(a, flush))
     return res
 
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(a):
-    """The reference algorithm on the host cores (numpy restatement of
-    native/glm53/moe_ref.py; Q8_0 decode of native/tools/q8_0_ref.py)."""
+    """The reference algorithm on the host cores: the numpy restatement of
+    native/glm53/moe_ref.py (router, per-expert f64 FFN, combine) with the Q8_0 decode of
+    native/tools/q8_0_ref.py, on the same workload, metric and config as our arm.  Each step is a
+    bounded sample of the workload (the first n tokens, n chosen so that warm-up + steps end within
+    a few minutes); value and ms_per_step are the sample's own (no extrapolation)."""
     from oracle import moe_oracle as orc
     from vybforge_b200 import synth
     cfg = synth.config(a.workload, tokens=a.tokens, fmt=a.fmt, seed=0)
     x, w_r, bias, rng = synth.router_inputs(cfg)
-    H, I, E = cfg.hidden, cfg.inter, cfg.n_experts
+    H, I, E, T = cfg.hidden, cfg.inter, cfg.n_experts, cfg.tokens
     idx, wt = orc.route(x, w_r, bias, cfg.topk)
-    n = 1
-    while n < cfg.tokens and len(np.unique(idx[:n + 1])) + 1 <= max(4, int(a.cpu_budget_s / 0.25)):
-        n += 1
-    need = sorted(set(np.unique(idx[:n]).tolist()) | {E})
-    gen = np.random.default_rng(1)
+    per_step_s = min(a.cpu_budget_s, 150.0 / max(1, a.steps + a.warmup))
+    # Q8_0 expert bytes from a seeded stream per (expert, projection); the CPU time of the
+    # dequant + f64 GEMMs does not depend on the values
+    raw = {}
 
-    def rand_q8(rows, cols):   # random Q8_0 bytes: dequant+GEMM cost does not depend on values
-        b = gen.integers(0, 256, size=(rows, cols // 32, 34), dtype=np.uint8)
-        b[:, :, 0:2] = np.frombuffer(np.full(rows * cols // 32, 6e-4, np.float16).tobytes(),
-                                     np.uint8).reshape(rows, cols // 32, 2)
-        return b.reshape(rows, -1)
-    raw = {e: (rand_q8(I, H), rand_q8(I, H), rand_q8(H, I)) for e in need}
+    def make(e):
+        g = np.random.default_rng((cfg.seed, 5000 + e))
+        raw[e] = tuple(np.ascontiguousarray(
+            g.integers(0, 256, size=(r, c // 32, 34), dtype=np.uint8).reshape(r, -1)) for r, c in ((I, H), (I, H), (H, I)))
+        for m in raw[e]:
+            m.reshape(m.shape[0], -1, 34)[:, :, 0:2] = np.frombuffer(
+                np.full(m.shape[0] * (m.shape[1] // 34), 6e-4, np.float16).tobytes(), np.uint8).reshape(
+                m.shape[0], -1, 2)
 
     def get(e):
+        if e not in raw:
+            make(e)
         g, u, d = raw[e]
         return (orc.q8_0_expert_inout(g, I, H), orc.q8_0_expert_inout(u, I, H), orc.q8_0_expert_inout(d, H, I))
+    # sample size: one untimed calibration step on the first token sets the cost per expert, then
+    # the first n tokens whose experts fit the per-step budget
+    for e in set(np.unique(idx[:1]).tolist()) | {E}:
+        make(e)
+    t0 = time.perf_counter()
+    orc.moe_block_grouped(x[:1], w_r, bias, get, lambda: get(E), E, cfg.topk)
+    per_expert = (time.perf_counter() - t0) / (len(np.unique(idx[:1])) + 1)
+    n = 1
+    while n < T and (len(np.unique(idx[:n + 1])) + 1) * per_expert <= per_step_s:
+        n += 1
+    need = sorted(set(np.unique(idx[:n]).tolist()) | {E})
     times = []
     for i in range(a.warmup + a.steps):
         t0 = time.perf_counter()
         orc.moe_block_grouped(x[:n], w_r, bias, get, lambda: get(E), E, cfg.topk)
         if i >= a.warmup:
             times.append(time.perf_counter() - t0)
-        if sum(times) > 120:
-            break
     dt = float(np.mean(times))
     v = n / dt
     cores = os.cpu_count()
-    sample = (f"first {n} of {cfg.tokens} tokens ({len(need)} experts incl. shared) per step; "
-              f"numpy f64 dequant + GEMM per expert on {cores} host threads; {len(times)} timed steps")
+    sample = (f"first {n} of {T} tokens ({len(need)} experts incl. shared) per step; numpy f64 dequant + GEMM per "
+              f"expert on {cores} host threads ({cpu_model()}); value and ms_per_step are the sample's")
     return {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": "tokens/s", "n_gpus": a.gpus,
-            "steps": len(times), "warmup": a.warmup, "ms_per_step": round(dt * 1e3 * cfg.tokens / n, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (seeded); expert bytes random Q8_0 blocks",
-            "config": {"workload": f"{a.workload}: decode T={cfg.tokens}, H={H}, I={I}, E={E}, top-{cfg.topk}",
-                       "tokens_per_gpu": cfg.tokens},
+            "steps": len(times), "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 3),
+            "tokens_per_step": n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded N(0,1) bf16 tokens; Q8_0 expert bytes from a seeded stream)",
+            "config": {"workload": f"{a.workload}: decode T={T}/GPU, H={H}, I={I}, E={E}, top-{cfg.topk} "
+                                   f"+ 1 shared, Q8_0", "tokens_per_gpu": T, "global_batch": T * a.gpus,
+                       "parallelism": "host cores (reference CPU path)"},
             "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+                             "cpu_model": cpu_model(), "sample": sample},
             "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
