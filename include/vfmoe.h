@@ -149,6 +149,13 @@ int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max);
 int vfmoe_route(int64_t handle, int64_t x, int64_t T, int64_t idx_out, int64_t w_out,
                 int64_t workspace, int64_t ws_bytes, int64_t stream);
 
+/* The router's first level alone, for diagnostics: fp32 logits [T, n_experts] of x . W_r^T (the
+ * kernel vfmoe_route would use for this T and dtype: SIMT fp32, or tcgen05 on bf16 parts of W_r
+ * for bf16 x and T > 32) and *bound_out = c with |logit - exact| <= c * |x_t|_2 * |w_e|_2, the
+ * bound vfmoe_route's refinement relies on.  No counterpart in the reference. */
+int vfmoe_route_logits(int64_t handle, int64_t x, int64_t T, int64_t logits_out, double *bound_out,
+                       int64_t workspace, int64_t ws_bytes, int64_t stream);
+
 /* Router with no device allocation, for hosts that cannot call cudaMalloc at routing
  * time (it may synchronize the device, and it fails once the host has reserved all of
  * device memory in its own pool).  No counterpart in the reference.  Same result as
@@ -367,6 +374,20 @@ int vfmoe_hc_mix(const vfmoe_hc_desc *desc, int64_t streams, int64_t R, int64_t 
  * y [R][hidden] (y_dtype BF16 or F32), out fp32 [R][4][hidden]; out may be streams itself. */
 int vfmoe_hc_apply(int64_t streams, int64_t y, int64_t y_dtype, int64_t post, int64_t comb, int64_t R,
                    int64_t n_streams, int64_t hidden, int64_t out, int64_t stream);
+
+/* ---- packed layer files (replace the reference's dequant cache, native/glm53/deq_cache.vyb:1-93,
+ * which stores dequantized f64 tensors): the router and the expert stacks on disk in the byte
+ * layout the kernels stream (stage-tiled Q8_0 or EXL3 trellis + suh/svh), 4096-aligned sections
+ * behind a 4096-byte header holding the descriptor with device pointers as offsets. ---- */
+
+/* Write the layer that desc describes (device pointers) to path.  Synchronous. */
+int vfmoe_pack_save(const char *path, const vfmoe_layer_desc *desc);
+/* Device bytes a vfmoe_pack_load of path needs (or a negative status). */
+int64_t vfmoe_pack_bytes(const char *path);
+/* Read path into the caller's device buffer (256-byte aligned, at least vfmoe_pack_bytes) with
+ * chunked reads through pinned staging buffers, and fill *desc_out with pointers into it, ready
+ * for vfmoe_layer_create.  Synchronous; allocates only the pinned staging. */
+int vfmoe_pack_load(const char *path, int64_t dev_base, int64_t dev_bytes, vfmoe_layer_desc *desc_out);
 
 /* Q8_0 rows -> dense [rows, k] (dst_dtype VFMOE_DT_F32 or VFMOE_DT_F16).
  * Replaces q8_0deq (native/kernels/q8_0.vyb:11-30, which widens to f64). */

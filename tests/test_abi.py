@@ -137,3 +137,11 @@ def test_init_without_device_returns_status(built_lib):
     rc = built_lib.vfmoe_init(0)
     assert rc < 0
     assert _lib.last_error()
+
+
+def test_pack_load_rejects_a_file_that_is_not_a_pack(built_lib, tmp_path):
+    p = tmp_path / "junk.vfpk"
+    p.write_bytes(b"not a pack" * 1000)
+    assert built_lib.vfmoe_pack_bytes(str(p).encode()) == _lib.ERR_INVALID
+    assert "not a version-1 vfmoe pack" in _lib.last_error()
+    assert built_lib.vfmoe_pack_bytes(str(tmp_path / "missing").encode()) == _lib.ERR_INVALID

@@ -268,3 +268,57 @@ def test_expert_slot_out_of_range_is_reported(c0_bf16):
     one = L.forward_routed(rows[3:4].contiguous(), slots[3:4, :1].contiguous(), w[3:4, :1].contiguous(),
                            y_dtype=torch.float32)
     torch.testing.assert_close(y[3:4], one, rtol=1e-5, atol=1e-6)
+
+
+# ----------------------------------------------------------------------------- router first level
+def _cancelling_router(rng, T, H, E):
+    """bf16 tokens (columns scaled by 2^-2 .. 2^2) and a router in which every 16th row nearly
+    cancels against one token: its products span 2^-4 .. 2^4 in magnitude and sum to ~0 on that
+    token, so sum |x_i w_i| is orders of magnitude above |sum x_i w_i| there."""
+    from vybforge_b200.quant import round_bf16
+    x = round_bf16((rng.standard_normal((T, H)) * np.exp2(rng.integers(-2, 3, (1, H)))).astype(np.float32))
+    w_r = rng.normal(0, 0.02, (E, H)).astype(np.float64)
+    for e in range(0, E, 16):
+        t = (e // 16) % T
+        sign = np.where(rng.random(H) < 0.5, -1.0, 1.0)
+        w = 0.004 * sign * np.exp2(rng.integers(-4, 5, H)) / np.maximum(np.abs(x[t]), 1e-3)
+        w -= (x[t] @ w) / (x[t] @ x[t]) * x[t]                   # cancellation on token t
+        w_r[e] = w
+    return x, w_r.astype(np.float32)
+
+
+@pytest.mark.parametrize("case,T", [("random", 40), ("random", 4096), ("cancel", 64), ("cancel", 1024)])
+def test_router_first_level_error_within_its_bound(case, T):
+    """The first-level logits (tcgen05 on bf16 parts of W_r for bf16 x at T > 32) against exact fp64
+    logits: every |error| stays below the bound c |x_t| |w_e| the refinement relies on, and the
+    routing is bit-exact."""
+    moe.init(0)
+    rng = np.random.default_rng(T + (7 if case == "cancel" else 0))
+    H, E, k = 6144, 256, 8
+    if case == "random":
+        cfg = synth.config("c1", tokens=T)
+        x, w_r, bias, _ = synth.router_inputs(cfg)
+    else:
+        x, w_r = _cancelling_router(rng, T, H, E)
+        bias = rng.normal(0, 0.01, E).astype(np.float32)
+    from test_gpu_parity import _router_layer
+    layer = _router_layer(w_r, bias, H, E, k)
+    xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    logits, c = layer.route_logits(xd)
+    torch.cuda.synchronize()
+    layer.check_device_error()
+    exact = x.astype(np.float64) @ w_r.astype(np.float64).T
+    bound = c * np.linalg.norm(x.astype(np.float64), axis=1)[:, None] * np.linalg.norm(w_r.astype(np.float64), axis=1)[None, :]
+    err = np.abs(logits.cpu().numpy().astype(np.float64) - exact)
+    ratio = float((err / bound).max())
+    scale = np.abs(x.astype(np.float64)) @ np.abs(w_r.astype(np.float64)).T
+    print(f"[router L1 {case} T={T}] c = {c:.3e}; max |err| / bound = {ratio:.3e}; "
+          f"max |err| / sum|x w| = {float((err / scale).max()):.3e}")
+    assert ratio < 1.0
+    idx, w = layer.route(xd)
+    torch.cuda.synchronize()
+    layer.check_device_error()
+    ri, rw = orc.route(x, w_r, bias, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    layer.close()

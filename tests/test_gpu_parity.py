@@ -396,3 +396,28 @@ def test_c3_zipf_prefill_parity():
     print(f"[parity c3 zipf T=4096 tokens {toks}] max-abs {np.abs(o - ro).max():.3e} rel-L2 {rel_l2(o, ro):.3e}")
     assert np.abs(o - ro).max() <= TOL_MAX_ABS and rel_l2(o, ro) <= TOL_REL_L2
     b.layer.check_device_error()
+
+
+# ----------------------------------------------------------------------------- packed layer files
+@pytest.mark.parametrize("which", ["q8_0_tiled", "exl3"])
+def test_packed_layer_file_round_trip(c1_tiled, tmp_path, which):
+    """A layer written with vfmoe_pack_save and read back with vfmoe_pack_load (one device buffer,
+    chunked reads) gives bit-identical forwards: the file holds the kernels' own byte layout."""
+    if which == "exl3":
+        moe.init(0)
+        src = Built(synth.config("c0", tokens=64, fmt="exl3")).layer
+        x = torch.randn((64, src.H), generator=torch.Generator(device="cuda").manual_seed(3), device="cuda")
+    else:
+        src = c1_tiled
+        g = torch.Generator(device="cuda").manual_seed(11)
+        x = torch.randn((32, src.H), generator=g, device="cuda").to(torch.bfloat16)
+    path = str(tmp_path / f"layer_{which}.vfpk")
+    src.save_packed(path)
+    back = moe.MoELayer.from_packed(path)
+    assert back.fmt == which and back.E == src.E
+    a = src.forward(x.to(src.x_dtype))
+    b = back.forward(x.to(back.x_dtype))
+    torch.cuda.synchronize()
+    back.check_device_error()
+    assert torch.equal(a, b)
+    back.close()

@@ -72,6 +72,7 @@ _SIGS = {
     "vfmoe_workspace_bytes": (I64, [I64, I64]),
     "vfmoe_route": (C.c_int, [I64] * 8),
     "vfmoe_route_noalloc": (C.c_int, [I64] * 6),
+    "vfmoe_route_logits": (C.c_int, [I64, I64, I64, I64, C.POINTER(C.c_double), I64, I64, I64]),
     "vfmoe_forward": (C.c_int, [I64] * 9),
     "vfmoe_check_device_error": (C.c_int, [I64, I64]),
     "vfmoe_dispatch": (C.c_int, [I64] * 10),
@@ -97,6 +98,9 @@ _SIGS = {
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_hc_mix": (C.c_int, [C.POINTER(HcDesc), I64, I64, I64, I64, I64, I64, I64]),
     "vfmoe_hc_apply": (C.c_int, [I64] * 10),
+    "vfmoe_pack_save": (C.c_int, [C.c_char_p, C.POINTER(LayerDesc)]),
+    "vfmoe_pack_bytes": (I64, [C.c_char_p]),
+    "vfmoe_pack_load": (C.c_int, [C.c_char_p, I64, I64, C.POINTER(LayerDesc)]),
     "vfmoe_residual_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_q8_0_dequant": (C.c_int, [I64] * 6),
     "vfmoe_q8_0_quantize": (C.c_int, [I64] * 5),

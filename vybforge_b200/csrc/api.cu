@@ -106,7 +106,7 @@ WsLayout ws_layout(const Layer &L, int64_t T, int k) {
     o.pos_of = take(T * k * 4);
     o.idx = take(T * k * 4);
     o.w = take(T * k * 4);
-    o.part = take(router_logit_floats((int)T, L.H, L.E) * 4);
+    o.part = take(router_logit_floats((int)T, L.H, L.E, L.wr_split != nullptr) * 4);
     // EXL3 keeps two rotated copies of every row (gate and up input bases); fp32 activations on
     // Q8_0 keep two fp16 planes of every row of xp and act (split-precision decode GEMV)
     const int prec = layer_prec(L);
@@ -268,11 +268,19 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
     if (e == cudaSuccess) e = cudaMalloc(&L->nw, L->E * sizeof(float));
     if (e == cudaSuccess && launch_router_norms(reinterpret_cast<const float *>(desc->router_w), L->H, L->E, L->nw, 0))
         e = cudaErrorLaunchFailure;
+    if (e == cudaSuccess && desc->x_dtype == VFMOE_DT_BF16 && L->H % 128 == 0 && L->E % 128 == 0) {
+        const int64_t n = (int64_t)L->E * L->H;
+        e = cudaMalloc(&L->wr_split, 2 * n * sizeof(__nv_bfloat16));
+        if (e == cudaSuccess &&
+            launch_router_split(reinterpret_cast<const float *>(desc->router_w), n, L->wr_split, L->wr_split + n, 0))
+            e = cudaErrorLaunchFailure;
+    }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
-        cuda_fail(e, "layer set-up (error word, router norms)", __FILE__, __LINE__);
+        cuda_fail(e, "layer set-up (error word, router norms and split)", __FILE__, __LINE__);
         if (L->dev_err) cudaFree(L->dev_err);
         if (L->nw) cudaFree(L->nw);
+        if (L->wr_split) cudaFree(L->wr_split);
         delete L;
         return VFMOE_ERR_CUDA;
     }
@@ -281,6 +289,7 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
     if (rc) {
         cudaFree(L->dev_err);
         cudaFree(L->nw);
+        if (L->wr_split) cudaFree(L->wr_split);
         delete L;
         return rc;
     }
@@ -305,6 +314,8 @@ int vfmoe_layer_destroy(int64_t handle) {
     if (L->own_ws) cudaFree(L->own_ws);
     if (L->dev_err) cudaFree(L->dev_err);
     if (L->nw) cudaFree(L->nw);
+    if (L->wr_split) cudaFree(L->wr_split);
+    if (L->ep.owner) cudaFree(L->ep.owner);
     for (auto &ev : L->ev_pending)
         for (auto e : ev) L->ev_pool.push_back(e);
     for (auto e : L->ev_pool) cudaEventDestroy(e);
@@ -331,7 +342,7 @@ int vfmoe::route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout
     int32_t *idx = *idx_p ? *idx_p : reinterpret_cast<int32_t *>(base + lay.idx);
     float *w = *w_p ? *w_p : reinterpret_cast<float *>(base + lay.w);
     int rc = launch_router(reinterpret_cast<const void *>(x), (int)L.d.x_dtype,
-                           reinterpret_cast<const float *>(L.d.router_w), L.nw,
+                           reinterpret_cast<const float *>(L.d.router_w), L.wr_split, L.nw,
                            reinterpret_cast<const float *>(L.d.router_bias), (int)T, L.H, L.E, L.k,
                            L.d.routed_scale, reinterpret_cast<float *>(base + lay.part), idx, w, counts, L.dev_err,
                            st);
@@ -689,6 +700,27 @@ int vfmoe_dispatch(int64_t idx, int64_t T, int64_t k, int64_t n_experts, int64_t
                            reinterpret_cast<int32_t *>(perm_tok), pos, reinterpret_cast<int32_t *>(offsets), err, st);
 }
 
+int vfmoe_route_logits(int64_t handle, int64_t x, int64_t T, int64_t logits_out, double *bound_out,
+                       int64_t workspace, int64_t ws_bytes, int64_t stream) {
+    Layer *L = get_layer(handle);
+    if (!L) return VFMOE_ERR_HANDLE;
+    if (T <= 0 || T > ((int64_t)1 << 24) || !x || !logits_out || !bound_out) {
+        set_error("vfmoe_route_logits: bad arguments");
+        return VFMOE_ERR_INVALID;
+    }
+    char *base;
+    int rc = ensure_ws(*L, T, workspace, ws_bytes, &base);
+    if (rc) return rc;
+    const WsLayout lay = ws_layout(*L, T);
+    float c1 = 0.f;
+    rc = launch_route_logits(reinterpret_cast<const void *>(x), (int)L->d.x_dtype,
+                             reinterpret_cast<const float *>(L->d.router_w), L->wr_split, (int)T, L->H, L->E,
+                             reinterpret_cast<float *>(base + lay.part), reinterpret_cast<float *>(logits_out),
+                             L->dev_err, reinterpret_cast<cudaStream_t>(stream), &c1);
+    *bound_out = c1;
+    return rc;
+}
+
 int vfmoe_debug_inject(int64_t handle, int64_t kind, int64_t wait_ns) {
     Layer *L = get_layer(handle);
     if (!L) return VFMOE_ERR_HANDLE;
@@ -848,7 +880,7 @@ int route_into_scratch(int64_t handle, int64_t x, int64_t T, int64_t idx_out, in
         set_error("vfmoe_route_noalloc: T=%lld exceeds 2^24", (long long)T);
         return VFMOE_ERR_UNSUPPORTED;
     }
-    const int64_t logit_bytes = align_up(router_logit_floats((int)T, L->H, L->E) * 4, 256);
+    const int64_t logit_bytes = align_up(router_logit_floats((int)T, L->H, L->E, L->wr_split != nullptr) * 4, 256);
     const int64_t need = logit_bytes + align_up((L->E + 2) * 4, 256);
     if (need > scratch_bytes) {
         set_error("vfmoe_route_noalloc: T=%lld needs %lld bytes of router scratch; the static scratch holds %lld "
@@ -860,7 +892,7 @@ int route_into_scratch(int64_t handle, int64_t x, int64_t T, int64_t idx_out, in
     int32_t *counts = reinterpret_cast<int32_t *>(scratch + logit_bytes);
     VF_CUDA(cudaMemsetAsync(counts, 0, (L->E + 2) * sizeof(int32_t), st));
     return launch_router(reinterpret_cast<const void *>(x), (int)L->d.x_dtype,
-                         reinterpret_cast<const float *>(L->d.router_w), L->nw,
+                         reinterpret_cast<const float *>(L->d.router_w), L->wr_split, L->nw,
                          reinterpret_cast<const float *>(L->d.router_bias), (int)T, L->H, L->E, L->k,
                          L->d.routed_scale, reinterpret_cast<float *>(scratch), reinterpret_cast<int32_t *>(idx_out),
                          reinterpret_cast<float *>(w_out), counts, L->dev_err, st);

@@ -40,12 +40,25 @@ struct MoeArgs {
 };
 
 // Router: fp32 logits -> candidate filter -> float-float / f64 refinement (exact f64 ordering).
-// nw = |W_r row|_2 upper bounds (launch_router_norms, once per layer); logits = T*E floats scratch.
-int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
-                  int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
-                  cudaStream_t st);
+// nw = |W_r row|_2 upper bounds (launch_router_norms, once per layer); logits = scratch of
+// router_logit_floats(T, H, E, wr_split != 0) floats.  wr_split (bf16 [2][E][H], w_hi then w_lo,
+// launch_router_split once per layer; may be 0) enables the tensor-core logits for bf16 x at T > 32.
+int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, const float *nw,
+                  const float *bias, int T, int H, int E, int k, double scale, float *logits, int32_t *idx, float *w,
+                  int32_t *counts, int *err, cudaStream_t st);
 int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t st);
-int64_t router_logit_floats(int T, int H, int E);
+int64_t router_logit_floats(int T, int H, int E, bool tc);
+// First level only: fp32 logits [T][E] into out (partials in part), and the constant c1 with
+// |logit - exact| <= c1 * |x_t|_2 * |w_e|_2.
+int launch_route_logits(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, int T, int H,
+                        int E, float *part, float *out, int *err, cudaStream_t st, float *c1);
+// tensor-core logits (router_tc.cu)
+bool router_tc_shape(int T, int H, int E);
+int router_tc_splits(int T, int H, int E);
+float router_tc_bound(int H);
+int launch_router_split(const float *wr, int64_t n, __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t st);
+int launch_router_logits_tc(const void *x, const __nv_bfloat16 *wr_split, int T, int H, int E, float *logits, int *err,
+                            cudaStream_t st);
 
 int launch_dispatch(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, int32_t *perm_tok,
                     int32_t *pos_of, int32_t *offsets, int *err, cudaStream_t st);

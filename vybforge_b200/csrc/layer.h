@@ -32,6 +32,8 @@ struct Layer {
     int64_t q8_row_gate = 0, q8_row_down = 0;
     int *dev_err = nullptr;      // device error word (allocated at create)
     float *nw = nullptr;         // |W_r row|_2 upper bounds (allocated at create)
+    __nv_bfloat16 *wr_split = nullptr;  // W_r as bf16 hi and lo parts [2][E][H] for the tensor-core
+                                        // router logits (bf16 x, H and E multiples of 128), else 0
     void *own_ws = nullptr;      // internal workspace when the caller passes none
     int64_t own_ws_bytes = 0;
     TcPlan tc;                   // tensor-core launch state (tensor maps)

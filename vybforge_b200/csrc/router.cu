@@ -26,7 +26,7 @@
 
 namespace vfmoe {
 
-constexpr int kMaxCand = 64;
+constexpr int kMaxCand = 128;
 constexpr int kMaxH = 16384;     // router_refine keeps x_t in shared memory (fp32)
 constexpr int kMaxChunks = 32;   // L1 decode partial-sum chunks (H / 512)
 
@@ -700,14 +700,14 @@ static int router_l1_chunk(int H) { return H % 768 == 0 ? 768 : (H % 512 == 0 ? 
 
 // Partial-sum slices the logits kernel writes for (T, H, E): H / chunk on the decode kernel, else
 // tiled_splits.  launch_router and the scratch sizing (router_logit_floats) both use this count.
-static int router_splits(int T, int H, int E) {
+static int router_splits(int T, int H, int E, bool tc) {
+    if (tc && router_tc_shape(T, H, E)) return router_tc_splits(T, H, E);
     const int kch = router_l1_chunk(H);
     return (T <= 32 && kch) ? H / kch : tiled_splits(T, H, E);
 }
 
-int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, const float *bias, int T, int H,
-                  int E, int k, double scale, float *logits, int32_t *idx, float *w, int32_t *counts, int *err,
-                  cudaStream_t st) {
+int launch_router_l1(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, int T, int H, int E,
+                     float *logits, int *err, cudaStream_t st, int *nchunk_out, float *c1_out) {
     if (H > kMaxH || H / 512 > kMaxChunks) {
         set_error("router: hidden size %d exceeds %d", H, kMaxH);
         return VFMOE_ERR_UNSUPPORTED;
@@ -715,8 +715,14 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     float c1;
     int rc = VFMOE_OK;
     const int kch = router_l1_chunk(H);
-    const int nchunk = router_splits(T, H, E);
-    if (T <= 32 && kch) {
+    const bool tc = wr_split && x_dtype == VFMOE_DT_BF16 && router_tc_shape(T, H, E) &&
+                    (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const int nchunk = router_splits(T, H, E, tc);
+    if (tc) {
+        rc = launch_router_logits_tc(x, wr_split, T, H, E, logits, err, st);
+        if (rc) return rc;
+        c1 = router_tc_bound(H);
+    } else if (T <= 32 && kch) {
         if (kch == 768)
             rc = T <= 8 ? launch_l1_small<8, 768>(x, x_dtype, wr, T, H, E, logits, st)
                         : launch_l1_small<32, 768>(x, x_dtype, wr, T, H, E, logits, st);
@@ -731,6 +737,18 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
         VF_LAUNCH_CHECK("router_logits_f32_wide");
         c1 = gamma_bound(16 + H / nchunk / 16 + nchunk);
     }
+    *nchunk_out = nchunk;
+    *c1_out = c1;
+    return VFMOE_OK;
+}
+
+int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, const float *nw,
+                  const float *bias, int T, int H, int E, int k, double scale, float *logits, int32_t *idx, float *w,
+                  int32_t *counts, int *err, cudaStream_t st) {
+    int nchunk = 1;
+    float c1 = 0.f;
+    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, logits, err, st, &nchunk, &c1);
+    if (rc) return rc;
     // L2: thread owns n = H/256 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
     // exactly (TwoProduct), so the only error is lo's fp32 summation of the r and pe values,
     // sum(|r| + |pe|) <= (n + 1) u S:  |err| <= gamma_{2n} (n + 1) u S; the 5 + 7 level lane and
@@ -774,8 +792,28 @@ int launch_router(const void *x, int x_dtype, const float *wr, const float *nw, 
     return VFMOE_OK;
 }
 
-int64_t router_logit_floats(int T, int H, int E) {
-    return (int64_t)T * E * router_splits(T, H, E);
+// out[i] = sum over c < nchunk of part[c * n + i], in chunk order (as router_refine sums them).
+__global__ void sum_partials_kernel(const float *__restrict__ part, int nchunk, int64_t n, float *__restrict__ out) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float s = 0.f;
+    for (int c = 0; c < nchunk; ++c) s += part[c * n + i];
+    out[i] = s;
+}
+
+int launch_route_logits(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, int T, int H,
+                        int E, float *part, float *out, int *err, cudaStream_t st, float *c1) {
+    int nchunk = 1;
+    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, part, err, st, &nchunk, c1);
+    if (rc) return rc;
+    const int64_t n = (int64_t)T * E;
+    sum_partials_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(part, nchunk, n, out);
+    VF_LAUNCH_CHECK("sum_partials_kernel");
+    return VFMOE_OK;
+}
+
+int64_t router_logit_floats(int T, int H, int E, bool tc) {
+    return (int64_t)T * E * std::max(router_splits(T, H, E, tc), router_splits(T, H, E, false));
 }
 
 }  // namespace vfmoe

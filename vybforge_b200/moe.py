@@ -106,6 +106,34 @@ class MoELayer:
         self._ws = None
         self._rows_ws = None
 
+    # ------------------------------------------------------------------ packed files
+    def save_packed(self, path: str) -> None:
+        """Write this layer's weights to a packed layer file (vfmoe_pack_save)."""
+        check(self.lib.vfmoe_pack_save(path.encode(), C.byref(self.desc)))
+
+    @classmethod
+    def from_packed(cls, path: str):
+        """A layer whose weights live in one device buffer read from a packed layer file
+        (vfmoe_pack_load + vfmoe_layer_create)."""
+        lib = _lib.load()
+        need = check(lib.vfmoe_pack_bytes(path.encode()))
+        buf = torch.empty(need, dtype=torch.uint8, device="cuda")
+        d = _lib.LayerDesc()
+        check(lib.vfmoe_pack_load(path.encode(), _ptr(buf), need, C.byref(d)))
+        self = cls.__new__(cls)
+        self.lib = lib
+        self.H, self.I, self.E, self.k = d.hidden, d.inter, d.n_experts, d.topk
+        inv = {v: k for k, v in _DT.items()}
+        self.x_dtype, self.out_dtype = inv[d.x_dtype], inv[d.out_dtype]
+        self.fmt = {WFMT_Q8_0: "q8_0", WFMT_Q8_0_TILED: "q8_0_tiled", WFMT_EXL3: "exl3"}[d.weight_format]
+        self.n_local = d.n_local_experts or d.n_experts
+        self._keep = [buf]
+        self.desc = d
+        self.handle = check(lib.vfmoe_layer_create(C.byref(d)))
+        self._ws = None
+        self._rows_ws = None
+        return self
+
     # ------------------------------------------------------------------ workspace
     def workspace_bytes(self, T: int) -> int:
         return check(self.lib.vfmoe_workspace_bytes(self.handle, T))
@@ -124,6 +152,17 @@ class MoELayer:
         ws = self.workspace(T)
         check(self.lib.vfmoe_route(self.handle, _ptr(x), T, _ptr(idx), _ptr(w), _ptr(ws), ws.numel(), _stream()))
         return idx, w
+
+    def route_logits(self, x: torch.Tensor):
+        """(fp32 logits [T, E] of the router's first level, c) with |logit - exact| <= c |x_t| |w_e|
+        (vfmoe_route_logits; diagnostics)."""
+        T = x.shape[0]
+        out = torch.empty((T, self.E), dtype=torch.float32, device=x.device)
+        ws = self.workspace(T)
+        c = C.c_double(0.0)
+        check(self.lib.vfmoe_route_logits(self.handle, _ptr(x), T, _ptr(out), C.byref(c), _ptr(ws), ws.numel(),
+                                          _stream()))
+        return out, c.value
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, idx=None, w=None,
                 workspace: torch.Tensor | None = None):
