@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define VFMOE_ABI_VERSION 2
+#define VFMOE_ABI_VERSION 3
 
 /* status codes */
 #define VFMOE_OK 0
@@ -70,6 +70,11 @@ extern "C" {
  * strides and values as GGUF rows; the expert kernels stream one tile as one contiguous
  * copy.  Not accepted by the SIMT path (VFMOE_PATH_SIMT). */
 #define VFMOE_WFMT_Q8_0_TILED 3
+/* Dense bf16 matrices, rows = output channels ([out][in], the Hugging Face layout).  Accepted for
+ * the shared expert (vfmoe_layer_desc.shared_format): GLM-5.3 stores its routed experts EXL3 and
+ * its shared expert bf16.  Converted to fp16 at create (exact for |w| in [2^-14, 65504]; smaller
+ * values keep an absolute error below 2^-25) and run by a dense variant of the decode GEMV. */
+#define VFMOE_WFMT_BF16 4
 
 /* Expert-product kernels (vfmoe_layer_desc.expert_path).  AUTO picks per call: the decode GEMV
  * (register-operand tensor-core MMAs) while the routed rows average at most 16 per expert, the
@@ -116,6 +121,7 @@ typedef struct vfmoe_layer_desc {
     int64_t n_local_experts; /* routed experts whose weights gate/up/down hold; 0 = n_experts.
                                 Fewer on an expert-parallel rank (vfmoe_forward_rows only). */
     int64_t expert_path;     /* VFMOE_PATH_*; 0 = AUTO */
+    int64_t shared_format;   /* format of sh_gate/sh_up/sh_down: 0 = weight_format, or VFMOE_WFMT_BF16 */
 } vfmoe_layer_desc;
 
 /* ABI version (VFMOE_ABI_VERSION). */
@@ -388,6 +394,45 @@ int64_t vfmoe_pack_bytes(const char *path);
  * chunked reads through pinned staging buffers, and fill *desc_out with pointers into it, ready
  * for vfmoe_layer_create.  Synchronous; allocates only the pinned staging. */
 int vfmoe_pack_load(const char *path, int64_t dev_base, int64_t dev_bytes, vfmoe_layer_desc *desc_out);
+
+/* ---- checkpoint access: safetensors shards behind model.safetensors.index.json ----
+ * Replaces the gx index (native/glm53/gx.vyb:41-99: gx_shard_for, gx_resolve) and the safetensors
+ * reader (native/torchload/safetensors.vyb): a name resolves through the index to its shard, the
+ * shard's header (parsed once, checked against the file's size) to its dtype, shape and byte range,
+ * and the bytes are read straight into host or device memory.  A directory without an index is
+ * read as the single file model.safetensors. */
+#define VFMOE_ST_F32 0
+#define VFMOE_ST_F16 1
+#define VFMOE_ST_BF16 2
+#define VFMOE_ST_F64 3
+#define VFMOE_ST_I64 4
+#define VFMOE_ST_I32 5
+#define VFMOE_ST_I16 6
+#define VFMOE_ST_I8 7
+#define VFMOE_ST_U8 8
+#define VFMOE_ST_BOOL 9
+#define VFMOE_ST_U16 10
+#define VFMOE_ST_U32 11
+#define VFMOE_ST_U64 12
+#define VFMOE_ST_F8_E4M3 13
+#define VFMOE_ST_F8_E5M2 14
+
+typedef struct vfmoe_tensor_info {
+    int64_t dtype;        /* VFMOE_ST_* */
+    int64_t ndim;
+    int64_t shape[8];
+    int64_t nbytes;
+    int64_t file_offset;  /* absolute offset of the data in its shard */
+    int64_t shard;        /* index of the shard file */
+} vfmoe_tensor_info;
+
+int64_t vfmoe_ckpt_open(const char *dir);
+int vfmoe_ckpt_close(int64_t ckpt);
+/* dtype, shape and byte range of a tensor (VFMOE_ERR_INVALID if the checkpoint lacks it). */
+int vfmoe_ckpt_find(int64_t ckpt, const char *name, vfmoe_tensor_info *info);
+/* The tensor's bytes into dst (device memory when device != 0, through pinned staging; else host
+ * memory).  Synchronous. */
+int vfmoe_ckpt_read(int64_t ckpt, const char *name, int64_t dst, int64_t dst_bytes, int64_t device);
 
 /* Q8_0 rows -> dense [rows, k] (dst_dtype VFMOE_DT_F32 or VFMOE_DT_F16).
  * Replaces q8_0deq (native/kernels/q8_0.vyb:11-30, which widens to f64). */

@@ -41,7 +41,7 @@ def test_python_binding_covers_header():
 
 def test_constants_match_header():
     d = header_defines()
-    assert d["VFMOE_ABI_VERSION"] == _lib.ABI_VERSION == 2
+    assert d["VFMOE_ABI_VERSION"] == _lib.ABI_VERSION == 3
     for k in ("OK", "ERR_INVALID", "ERR_CUDA", "ERR_NOMEM", "ERR_HANDLE", "ERR_WORKSPACE", "ERR_DEVICE",
               "ERR_UNSUPPORTED", "ERR_NCCL"):
         assert d["VFMOE_" + k] == getattr(_lib, k)
@@ -54,11 +54,11 @@ def test_constants_match_header():
 
 def test_descriptor_is_a_block_of_8_byte_words():
     assert C.sizeof(_lib.Matrix) == 6 * 8
-    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6 + 2) * 8
+    assert C.sizeof(_lib.LayerDesc) == (12 + 6 * 6 + 3) * 8
 
 
 def test_version(built_lib):
-    assert built_lib.vfmoe_version() == 2
+    assert built_lib.vfmoe_version() == 3
 
 
 def _desc(**kw):

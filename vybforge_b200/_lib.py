@@ -27,12 +27,12 @@ ERR_NCCL = -8
 # dtype ids (native/dtype/dtype.vyb:26-28)
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # weight formats
-WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED = 1, 2, 3
+WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED, WFMT_BF16 = 1, 2, 3, 4
 # expert kernel families (vfmoe_layer_desc.expert_path)
 PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV = 0, 1, 2, 3
 # failure injection (vfmoe_debug_inject)
 INJECT_NONE, INJECT_STALL_LOADS = 0, 1
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class VfmoeError(RuntimeError):
@@ -53,7 +53,7 @@ class LayerDesc(C.Structure):
                 ("router_w", C.c_int64), ("router_bias", C.c_int64),
                 ("gate", Matrix), ("up", Matrix), ("down", Matrix),
                 ("sh_gate", Matrix), ("sh_up", Matrix), ("sh_down", Matrix), ("n_local_experts", C.c_int64),
-                ("expert_path", C.c_int64)]
+                ("expert_path", C.c_int64), ("shared_format", C.c_int64)]
 
 
 class HcDesc(C.Structure):
@@ -61,6 +61,15 @@ class HcDesc(C.Structure):
                 ("base", C.c_int64), ("scale", C.c_int64), ("rms_eps", C.c_double), ("hc_eps", C.c_double),
                 ("sinkhorn_iters", C.c_int64), ("norm_w", C.c_int64), ("norm_eps", C.c_double)]
 
+
+class TensorInfo(C.Structure):
+    _fields_ = [("dtype", C.c_int64), ("ndim", C.c_int64), ("shape", C.c_int64 * 8), ("nbytes", C.c_int64),
+                ("file_offset", C.c_int64), ("shard", C.c_int64)]
+
+
+# safetensors dtype ids (vfmoe.h VFMOE_ST_*)
+ST_NAMES = ["F32", "F16", "BF16", "F64", "I64", "I32", "I16", "I8", "U8", "BOOL", "U16", "U32", "U64", "F8_E4M3",
+            "F8_E5M2"]
 
 I64 = C.c_int64
 _SIGS = {
@@ -98,6 +107,10 @@ _SIGS = {
     "vfmoe_rmsnorm": (C.c_int, [I64, I64, I64, I64, I64, C.c_double, I64, I64]),
     "vfmoe_hc_mix": (C.c_int, [C.POINTER(HcDesc), I64, I64, I64, I64, I64, I64, I64]),
     "vfmoe_hc_apply": (C.c_int, [I64] * 10),
+    "vfmoe_ckpt_open": (I64, [C.c_char_p]),
+    "vfmoe_ckpt_close": (C.c_int, [I64]),
+    "vfmoe_ckpt_find": (C.c_int, [I64, C.c_char_p, C.POINTER(TensorInfo)]),
+    "vfmoe_ckpt_read": (C.c_int, [I64, C.c_char_p, I64, I64, I64]),
     "vfmoe_pack_save": (C.c_int, [C.c_char_p, C.POINTER(LayerDesc)]),
     "vfmoe_pack_bytes": (I64, [C.c_char_p]),
     "vfmoe_pack_load": (C.c_int, [C.c_char_p, I64, I64, C.POINTER(LayerDesc)]),

@@ -116,6 +116,11 @@ WsLayout ws_layout(const Layer &L, int64_t T, int k) {
     o.tiles_cap = tc_tiles_capacity((int)T, k, L.n_local > L.E ? L.n_local : L.E);
     o.tiles = take(2 * o.tiles_cap * 16);
     o.tile_counts = take(2 * 4);
+    if (L.dense_sh) {
+        o.xs = take(T * L.H * 2);
+        o.act_s = take(T * L.I * 2);
+        o.y_s = take(T * L.H * 4);
+    }
     o.total = p;
     return o;
 }
@@ -173,6 +178,14 @@ static int validate(const vfmoe_layer_desc &d) {
     if (d.out_dtype != VFMOE_DT_BF16 && d.out_dtype != VFMOE_DT_F32) return bad("out_dtype must be BF16 or F32");
     if (!d.router_w || !d.router_bias) return bad("router weights missing");
     if (!aligned16(d.router_w)) return bad("router_w must be 16-byte aligned");
+    if (d.shared_format != 0 && d.shared_format != d.weight_format && d.shared_format != VFMOE_WFMT_BF16)
+        return bad("shared_format must be 0, the routed format or VFMOE_WFMT_BF16");
+    const bool dense_sh = d.shared_format == VFMOE_WFMT_BF16;
+    if (dense_sh) {
+        if (!d.sh_gate.data || !d.sh_up.data || !d.sh_down.data) return bad("bf16 shared expert incomplete");
+        if (!aligned16(d.sh_gate.data) || !aligned16(d.sh_up.data) || !aligned16(d.sh_down.data))
+            return bad("shared expert pointers must be 16-byte aligned");
+    }
     if (d.weight_format == VFMOE_WFMT_Q8_0 || d.weight_format == VFMOE_WFMT_Q8_0_TILED) {
         const int64_t rg = d.hidden / 32 * 34, rd = d.inter / 32 * 34;
         if (!d.gate.data || !d.up.data || !d.down.data) return bad("routed expert weights missing");
@@ -195,7 +208,7 @@ static int validate(const vfmoe_layer_desc &d) {
         if (d.sh_gate.data && (!d.sh_up.data || !d.sh_down.data)) return bad("shared expert incomplete");
         for (int i = 0; i < 6; ++i) {
             const vfmoe_matrix &m = *ms[i];
-            if (!m.data) continue;
+            if (!m.data || (i >= 3 && dense_sh)) continue;
             const int64_t K = kk[i % 3], N = nn[i % 3];
             if (!m.suh || !m.svh) return bad("EXL3 matrices need suh and svh");
             if (!aligned16(m.data) || (m.suh & 1) || (m.svh & 1)) return bad("EXL3 trellis must be 16-byte aligned");
@@ -284,9 +297,27 @@ int64_t vfmoe_layer_create(const vfmoe_layer_desc *desc) {
         delete L;
         return VFMOE_ERR_CUDA;
     }
-    rc = tc_plan_create(L->d, L->tc);
-    if (!rc) rc = exl3_plan_create(L->d, L->x3);
+    cudaDeviceGetAttribute(&L->num_sms, cudaDevAttrMultiProcessorCount, L->device);
+    vfmoe_layer_desc dplan = L->d;  // the routed kernels' plans never see a dense shared expert
+    if (desc->shared_format == VFMOE_WFMT_BF16) {
+        L->dense_sh = 1;
+        dplan.sh_gate = dplan.sh_up = dplan.sh_down = vfmoe_matrix{};
+        const int64_t gi = (int64_t)L->I * L->H;
+        cudaError_t e2 = cudaMalloc(&L->sh_dense, 3 * gi * sizeof(__half));
+        rc = e2 == cudaSuccess ? VFMOE_OK : cuda_fail(e2, "dense shared expert copy", __FILE__, __LINE__);
+        const int64_t src[3] = {desc->sh_gate.data, desc->sh_up.data, desc->sh_down.data};
+        for (int i = 0; i < 3 && !rc; ++i)
+            rc = launch_to_f16(reinterpret_cast<const void *>(src[i]), VFMOE_DT_BF16, gi, L->sh_dense + i * gi, 0);
+        if (!rc) rc = make_dense_map(&L->dsh_gate, L->sh_dense, L->I, L->H, 64);
+        if (!rc) rc = make_dense_map(&L->dsh_up, L->sh_dense + gi, L->I, L->H, 64);
+        if (!rc) rc = make_dense_map(&L->dsh_down, L->sh_dense + 2 * gi, L->H, L->I, 128);
+        if (!rc && (e2 = cudaDeviceSynchronize()) != cudaSuccess)
+            rc = cuda_fail(e2, "dense shared expert conversion", __FILE__, __LINE__);
+    }
+    if (!rc) rc = tc_plan_create(dplan, L->tc);
+    if (!rc) rc = exl3_plan_create(dplan, L->x3);
     if (rc) {
+        if (L->sh_dense) cudaFree(L->sh_dense);
         cudaFree(L->dev_err);
         cudaFree(L->nw);
         if (L->wr_split) cudaFree(L->wr_split);
@@ -315,6 +346,7 @@ int vfmoe_layer_destroy(int64_t handle) {
     if (L->dev_err) cudaFree(L->dev_err);
     if (L->nw) cudaFree(L->nw);
     if (L->wr_split) cudaFree(L->wr_split);
+    if (L->sh_dense) cudaFree(L->sh_dense);
     if (L->ep.owner) cudaFree(L->ep.owner);
     for (auto &ev : L->ev_pending)
         for (auto e : ev) L->ev_pool.push_back(e);
@@ -443,7 +475,8 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.I = L->I;
     a.E = L->E;
     a.k = L->k;
-    a.has_shared = L->has_shared;
+    const int fused_shared = L->has_shared && !L->dense_sh;  // shared expert inside the routed launches
+    a.has_shared = fused_shared;
     a.fmt = (int)L->d.weight_format;
     a.exl3_bits = (int)L->d.exl3_bits;
     a.limit = (float)L->d.swiglu_limit;
@@ -470,9 +503,18 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
     a.tiles_cap = lay.tiles_cap;
 
-    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, L->has_shared, perm_tok, pos_of, offsets, L->dev_err, st);
+    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, fused_shared, perm_tok, pos_of, offsets, L->dev_err, st);
     if (rc) return rc;
-    const int64_t rows = T * L->k + (L->has_shared ? T : 0);
+    if (L->dense_sh) {
+        // the bf16-stored shared expert: its own dense GEMVs on fp16 x, ahead of the routed experts
+        __half *xs = reinterpret_cast<__half *>(base + lay.xs);
+        if ((rc = launch_to_f16(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, T * L->H, xs, st))) return rc;
+        if ((rc = launch_dense_expert(L->dsh_gate, L->dsh_up, L->dsh_down, xs, (int)T, L->H, L->I,
+                                      reinterpret_cast<__half *>(base + lay.act_s), reinterpret_cast<float *>(base + lay.y_s),
+                                      a.limit, L->dev_err, L->num_sms, L->wait_ns, st)))
+            return rc;
+        nlaunch += 3;
+    }
     if (L->x3.ready) {
         // EXL3: the expert path gathers and rotates the rows itself
         nlaunch += 1;
@@ -493,7 +535,9 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     if (rc) return rc;
     mark();
     rc = launch_combine(a.y, VFMOE_DT_F32, pos_of, w, (int)T, L->H, L->k,
-                        L->has_shared ? a.y + T * L->k * L->H : nullptr, reinterpret_cast<void *>(out),
+                        L->dense_sh ? reinterpret_cast<float *>(base + lay.y_s)
+                                    : (fused_shared ? a.y + T * L->k * L->H : nullptr),
+                        reinterpret_cast<void *>(out),
                         (int)L->d.out_dtype, st);
     if (rc) return rc;
     nlaunch += 1;
@@ -568,7 +612,7 @@ int vfmoe::rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *
     const WsLayout lay = ws_layout(L, n, k);
     const int nl = L.n_local;
     // slot nl = the shared expert: an ordinary bucket of a dispatch over nl + 1 buckets
-    const int nb = nl + (L.has_shared ? 1 : 0);
+    const int nb = nl + (L.has_shared && !L.dense_sh ? 1 : 0);
     int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
     int32_t *offsets = reinterpret_cast<int32_t *>(base + lay.offsets);
     int32_t *perm_tok = reinterpret_cast<int32_t *>(base + lay.perm_tok);
@@ -584,7 +628,7 @@ int vfmoe::rows_impl(Layer &L, int64_t rows, int64_t rows_dtype, const int32_t *
     a.I = L.I;
     a.E = nl;
     a.k = k;
-    a.has_shared = L.has_shared;
+    a.has_shared = L.has_shared && !L.dense_sh;
     a.fmt = (int)L.d.weight_format;
     a.exl3_bits = (int)L.d.exl3_bits;
     a.limit = (float)L.d.swiglu_limit;

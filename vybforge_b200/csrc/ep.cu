@@ -260,6 +260,25 @@ static int ep_shared_impl(Layer &L, int64_t x, int64_t T, char *base, const EpLa
         VF_CUDA(cudaMemsetAsync(base + lay.y_shared, 0, T * lay.part_bytes, st));
         return VFMOE_OK;
     }
+    if (L.dense_sh) {
+        // the bf16-stored shared expert runs its own dense GEMVs (workspace regions of a T-row
+        // forward inside the inner workspace), then its rows become partial rows
+        char *in = base + lay.inner;
+        const WsLayout wl = ws_layout(L, T);
+        __half *xs = reinterpret_cast<__half *>(in + wl.xs);
+        float *ys = reinterpret_cast<float *>(in + wl.y_s);
+        int rc = launch_to_f16(reinterpret_cast<const void *>(x), (int)L.d.x_dtype, T * L.H, xs, st);
+        if (!rc)
+            rc = launch_dense_expert(L.dsh_gate, L.dsh_up, L.dsh_down, xs, (int)T, L.H, L.I,
+                                     reinterpret_cast<__half *>(in + wl.act_s), ys, (float)L.d.swiglu_limit, L.dev_err,
+                                     L.num_sms, L.wait_ns, st);
+        if (rc) return rc;
+        if (part_dtype(L) == VFMOE_DT_F32) {
+            VF_CUDA(cudaMemcpyAsync(base + lay.y_shared, ys, T * lay.part_bytes, cudaMemcpyDeviceToDevice, st));
+            return VFMOE_OK;
+        }
+        return launch_to_f16(ys, VFMOE_DT_F32, T * L.H, reinterpret_cast<__half *>(base + lay.y_shared), st);
+    }
     int32_t *ss = reinterpret_cast<int32_t *>(base + lay.shared_slot);
     fill_i32_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(ss, T, L.n_local);
     VF_LAUNCH_CHECK("fill_i32_kernel");

@@ -50,13 +50,17 @@ constexpr int kGvThreads = 32 * (kGvConsumers + 1);
 constexpr int kRow = 272;            // 8 Q8_0 blocks (256 K) of one weight row
 constexpr int kWBytes = 128 * kRow;  // weights per stage: 64 rows x 2 matrices or 128 rows
 
-template <bool GATEUP, int NT, bool PREC>
+template <bool GATEUP, int NT, bool PREC, bool DENSE = false>
 struct GvCfg {
     static constexpr int N = 8 * NT;
     static constexpr int ROWS = GATEUP ? 64 : 128;  // channels per tile
     static constexpr int TOK1 = N * 512;            // N rows x 256 K fp16: one plane
     static constexpr int TOK = PREC ? 2 * TOK1 : TOK1;
-    static constexpr int STAGE = kWBytes + TOK;
+    // weight bytes of a stage: Q8_0 rows of 272 B, or dense fp16 as 4 boxes of 64 K x ROWS rows
+    // per matrix (128-byte rows, SWIZZLE_128B)
+    static constexpr int WBOX = ROWS * 128;
+    static constexpr int WB = DENSE ? (GATEUP ? 2 : 1) * 4 * WBOX : kWBytes;
+    static constexpr int STAGE = WB + TOK;
     static constexpr int XCH = GATEUP ? ROWS * N * 4 : 0;
     static constexpr int SW = (230000 - XCH - 1024) / STAGE > 6 ? 6 : (230000 - XCH - 1024) / STAGE;
     static constexpr int SMEM = SW * STAGE + XCH + 2 * SW * 8 + 16 + 1024;
@@ -135,9 +139,9 @@ __device__ __forceinline__ void q8_frag_prec(const uint8_t *row, int p, int c, u
     }
 }
 
-template <bool GATEUP, int NT, bool PREC>
+template <bool GATEUP, int NT, bool PREC, bool DENSE>
 __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_constant__ TcParams p) {
-    using C = GvCfg<GATEUP, NT, PREC>;
+    using C = GvCfg<GATEUP, NT, PREC, DENSE>;
     constexpr int SW = C::SW, N = C::N, ROWS = C::ROWS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,7 +165,16 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     // the next kernel (the down GEMV after gate/up) may be scheduled onto SMs as this grid
     // retires; it reads this grid's output only after griddepcontrol.wait
     if (threadIdx.x == 0) griddep_launch_dependents();
-    const int n_items = (*p.n_tiles) * MT;
+    const int n_items = (DENSE ? (p.dense_T + N - 1) / N : *p.n_tiles) * MT;
+    // the item's token tile: the tile list, or for a dense expert tiles of N rows in order
+    auto tile_of = [&](int item) -> int4 {
+        if constexpr (DENSE) {
+            const int y = (item / MT) * N;
+            return make_int4(p.E, y, min(N, p.dense_T - y), 0);
+        } else {
+            return p.tiles[item / MT];
+        }
+    };
 
     if (warp == kGvConsumers) {
         // ------------------------------------------------------------------ TMA producer
@@ -180,11 +193,18 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
             const int pre = my_items * KR < SW ? my_items * KR : SW;
             for (int i = 0; i < pre; ++i) {
                 const int item = blockIdx.x + (i / KR) * gridDim.x, kr = i % KR;
-                const int4 t = p.tiles[item / MT];
+                const int4 t = tile_of(item);
                 const bool sh = t.x == p.E;
                 uint8_t *st = smem + i * C::STAGE;
                 mbar_arrive_expect_tx(&full[i], C::STAGE);
-                if (p.tiled) {
+                if constexpr (DENSE) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        tma_load_2d(st + q * C::WBOX, &p.wa, &full[i], kr * 256 + 64 * q, (item % MT) * ROWS);
+                        if (GATEUP)
+                            tma_load_2d(st + (4 + q) * C::WBOX, &p.wb, &full[i], kr * 256 + 64 * q, (item % MT) * ROWS);
+                    }
+                } else if (p.tiled) {
                     load_q8_tiled(st, sh ? p.spa : p.pa, p.sa, sh ? 0 : t.x, (item % MT) * ROWS, ROWS, KR, kr, &full[i]);
                     if (GATEUP)
                         load_q8_tiled(st + ROWS * kRow, sh ? p.spb : p.pb, p.sb, sh ? 0 : t.x, (item % MT) * ROWS, ROWS,
@@ -199,20 +219,20 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
             griddep_wait();
             for (int i = 0; i < pre; ++i) {
                 const int item = blockIdx.x + (i / KR) * gridDim.x, kr = i % KR;
-                const int4 t = p.tiles[item / MT];
+                const int4 t = tile_of(item);
                 uint8_t *st = smem + i * C::STAGE;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[i], kr * 256 + 64 * q, t.y);
+                for (int q = 0; q < 4; ++q) tma_load_2d(st + C::WB + q * (N * 128), &p.xt, &full[i], kr * 256 + 64 * q, t.y);
                 if (PREC) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
-                        tma_load_2d(st + kWBytes + C::TOK1 + q * (N * 128), &p.xt2, &full[i], kr * 256 + 64 * q, t.y);
+                        tma_load_2d(st + C::WB + C::TOK1 + q * (N * 128), &p.xt2, &full[i], kr * 256 + 64 * q, t.y);
                 }
             }
             uint32_t n = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-                const int4 t = p.tiles[item / MT];
+                const int4 t = tile_of(item);
                 const int m0 = (item % MT) * ROWS;
                 const bool sh = t.x == p.E;
                 const CUtensorMap *ma = sh ? &p.swa : &p.wa;
@@ -224,7 +244,13 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                     if (!(ok = mbar_wait(&empty[s], ((n / SW) & 1) ^ 1, abort, p.wait_ns))) break;
                     uint8_t *st = smem + s * C::STAGE;
                     mbar_arrive_expect_tx(&full[s], C::STAGE);
-                    if (p.tiled) {
+                    if constexpr (DENSE) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            tma_load_2d(st + q * C::WBOX, &p.wa, &full[s], kr * 256 + 64 * q, m0);
+                            if (GATEUP) tma_load_2d(st + (4 + q) * C::WBOX, &p.wb, &full[s], kr * 256 + 64 * q, m0);
+                        }
+                    } else if (p.tiled) {
                         load_q8_tiled(st, sh ? p.spa : p.pa, p.sa, z, m0, ROWS, KR, kr, &full[s]);
                         if (GATEUP) load_q8_tiled(st + ROWS * kRow, sh ? p.spb : p.pb, p.sb, z, m0, ROWS, KR, kr, &full[s]);
                     } else {
@@ -232,11 +258,11 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                         if (GATEUP) tma_load_3d(st + ROWS * kRow, mb, &full[s], kr * (kRow / 2), m0, z);
                     }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) tma_load_2d(st + kWBytes + q * (N * 128), &p.xt, &full[s], kr * 256 + 64 * q, t.y);
+                    for (int q = 0; q < 4; ++q) tma_load_2d(st + C::WB + q * (N * 128), &p.xt, &full[s], kr * 256 + 64 * q, t.y);
                     if (PREC) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q)
-                            tma_load_2d(st + kWBytes + C::TOK1 + q * (N * 128), &p.xt2, &full[s], kr * 256 + 64 * q,
+                            tma_load_2d(st + C::WB + C::TOK1 + q * (N * 128), &p.xt2, &full[s], kr * 256 + 64 * q,
                                         t.y);
                     }
                 }
@@ -256,7 +282,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
         uint32_t n = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-            const int4 t = p.tiles[item / MT];
+            const int4 t = tile_of(item);
             const int m0 = (item % MT) * ROWS;
             const int ntv = (t.z + 7) >> 3;                     // n8 tiles with valid token rows
             float acc[NT][4];
@@ -274,14 +300,26 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
 #pragma unroll
                 for (int pq = 0; pq < 4; ++pq) {
                     uint32_t wa[8], wb[8], la[PREC ? 8 : 1], lb[PREC ? 8 : 1];
-                    if constexpr (PREC) {
+                    if constexpr (DENSE) {
+                        // rows r0+g and r0+g+8 of this matrix's box pq, 16-byte chunks 2c and 2c+1
+                        const uint8_t *box = st + (mat * 4 + pq) * C::WBOX;
+                        const int ra = r0 + g, rb = ra + 8;
+                        const uint4 a0 = *reinterpret_cast<const uint4 *>(box + ra * 128 + (((2 * c) ^ (ra & 7)) << 4));
+                        const uint4 a1 = *reinterpret_cast<const uint4 *>(box + ra * 128 + (((2 * c + 1) ^ (ra & 7)) << 4));
+                        const uint4 b0 = *reinterpret_cast<const uint4 *>(box + rb * 128 + (((2 * c) ^ (rb & 7)) << 4));
+                        const uint4 b1 = *reinterpret_cast<const uint4 *>(box + rb * 128 + (((2 * c + 1) ^ (rb & 7)) << 4));
+                        wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w;
+                        wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
+                        wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w;
+                        wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
+                    } else if constexpr (PREC) {
                         q8_frag_prec(rowA, pq, c, wa, la);
                         q8_frag_prec(rowB, pq, c, wb, lb);
                     } else {
                         q8_frag(rowA, pq, c, wa);
                         q8_frag(rowB, pq, c, wb);
                     }
-                    const uint8_t *tq = st + kWBytes + pq * (N * 128);
+                    const uint8_t *tq = st + C::WB + pq * (N * 128);
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
                         if (j < ntv) {
@@ -369,13 +407,14 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     }
 }
 
-template <bool GATEUP, int NT, bool PREC>
+template <bool GATEUP, int NT, bool PREC, bool DENSE = false>
 static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
-    using C = GvCfg<GATEUP, NT, PREC>;
-    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_mma<GATEUP, NT, PREC>), C::SMEM))
+    using C = GvCfg<GATEUP, NT, PREC, DENSE>;
+    if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_mma<GATEUP, NT, PREC, DENSE>),
+                                         C::SMEM))
         return rc_attr;
     if (GATEUP) {
-        expert_gemv_mma<GATEUP, NT, PREC><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+        expert_gemv_mma<GATEUP, NT, PREC, DENSE><<<grid, kGvThreads, C::SMEM, st>>>(prm);
     } else {
         // programmatic dependent launch: CTAs start streaming down weights on SMs the gate/up
         // grid has released, before its act rows are complete
@@ -389,10 +428,88 @@ static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT, PREC>, prm));
+        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT, PREC, DENSE>, prm));
     }
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_mma<gate_up>" : "expert_gemv_mma<down>");
     return VFMOE_OK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 gv_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// fp16 [rows][k], box 64 x box_rows, SWIZZLE_128B (dense weights and token rows alike).
+int make_dense_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k, int box_rows) {
+    auto enc = gv_encode();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return VFMOE_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (dense fp16) failed: %d", (int)r);
+        return VFMOE_ERR_CUDA;
+    }
+    return VFMOE_OK;
+}
+
+template <bool GATEUP>
+static int launch_gv_dense(int N, const TcParams &prm, int grid, cudaStream_t st) {
+    switch (N) {
+        case 8: return launch_gv<GATEUP, 1, false, true>(prm, grid, st);
+        case 16: return launch_gv<GATEUP, 2, false, true>(prm, grid, st);
+        default: return launch_gv<GATEUP, 4, false, true>(prm, grid, st);
+    }
+}
+
+int launch_dense_expert(const CUtensorMap &gate, const CUtensorMap &up, const CUtensorMap &down, const __half *xs,
+                        int T, int H, int I, __half *act_s, float *y_s, float limit, int *err, int num_sms,
+                        uint64_t wait_ns, cudaStream_t st) {
+    if (T == 0) return VFMOE_OK;
+    const int N = T <= 8 ? 8 : (T <= 16 ? 16 : 32);
+    int rc;
+    TcParams g{};
+    g.wa = gate;
+    g.wb = up;
+    if ((rc = make_dense_map(&g.xt, xs, T, H, N))) return rc;
+    g.dense_T = T;
+    g.E = -1;
+    g.K = H;
+    g.M = I;
+    g.ld_out = I;
+    g.out = act_s;
+    g.limit = limit;
+    g.err = err;
+    g.wait_ns = wait_ns;
+    if ((rc = launch_gv_dense<true>(N, g, num_sms, st))) return rc;
+    TcParams dn{};
+    dn.wa = down;
+    dn.wb = down;
+    if ((rc = make_dense_map(&dn.xt, act_s, T, I, N))) return rc;
+    dn.dense_T = T;
+    dn.E = -1;
+    dn.K = I;
+    dn.M = H;
+    dn.ld_out = H;
+    dn.out = y_s;
+    dn.limit = limit;
+    dn.err = err;
+    dn.wait_ns = wait_ns;
+    return launch_gv_dense<false>(N, dn, num_sms, st);
 }
 
 int gemv_tokens_per_tile(int T, int k, int E) {

@@ -50,6 +50,10 @@ struct TcParams {
     int64_t out_plane;
     uint64_t wait_ns;  // bound of every mbarrier wait (2 s unless a test shortens it)
     int stall;         // test-only injection: the producer issues no loads (VFMOE_INJECT_STALL_LOADS)
+    // dense fp16 weights (a shared expert stored as bf16, converted at create): wa / wb map the
+    // single matrices [rows][K] with 64 x ROWS boxes, SWIZZLE_128B; no tile list: dense_T token
+    // rows of the token map, tiles of N rows in order
+    int dense_T;
 };
 
 int tc_plan_create(const vfmoe_layer_desc &d, TcPlan &plan);
@@ -71,6 +75,13 @@ __device__ __forceinline__ void load_q8_tiled(uint8_t *dst, const uint8_t *base,
 }
 bool tc_supported(const TcPlan &plan, const MoeArgs &a);
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
+
+// Dense fp16 expert (expert_gemv.cu): gate/up + SwiGLU then down over T token rows of xs
+// (fp16 [T][H]), act_s fp16 [T][I], y_s fp32 [T][H]; maps from make_dense_map.
+int make_dense_map(CUtensorMap *m, const void *base, int64_t rows, int64_t k, int box_rows);
+int launch_dense_expert(const CUtensorMap &gate, const CUtensorMap &up, const CUtensorMap &down, const __half *xs,
+                        int T, int H, int I, __half *act_s, float *y_s, float limit, int *err, int num_sms,
+                        uint64_t wait_ns, cudaStream_t st);
 
 // Decode path (few tokens per expert): TMA + register-operand MMA GEMV (expert_gemv.cu).
 int gemv_tokens_per_tile(int T, int k, int E);

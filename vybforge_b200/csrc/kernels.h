@@ -81,6 +81,9 @@ int launch_hc_mix(const float *streams, int64_t R, int D, const void *fn, int fn
 int launch_hc_apply(const float *streams, const void *y, int y_dtype, const float *post, const float *comb, int64_t R,
                     int D, float *out, cudaStream_t st);
 
+// dst[i] = fp16(src[i]), src BF16 / F16 / F32.
+int launch_to_f16(const void *src, int dtype, int64_t n, __half *dst, cudaStream_t st);
+
 int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, float eps, int dtype,
                    cudaStream_t st);
 int launch_residual_rmsnorm(const void *x, const void *y, const float *w, void *x_out, void *h, int64_t S, int D,

@@ -36,6 +36,12 @@ struct Layer {
                                         // router logits (bf16 x, H and E multiples of 128), else 0
     void *own_ws = nullptr;      // internal workspace when the caller passes none
     int64_t own_ws_bytes = 0;
+    int num_sms = 0;
+    // dense shared expert (shared_format VFMOE_WFMT_BF16): fp16 copies [I][H], [I][H], [H][I] in one
+    // allocation, and their tensor maps; the routed launches then run without the shared expert
+    int dense_sh = 0;
+    __half *sh_dense = nullptr;
+    CUtensorMap dsh_gate, dsh_up, dsh_down;
     TcPlan tc;                   // tensor-core launch state (tensor maps)
     Exl3Plan x3;                 // EXL3 trellis tensor maps
     uint64_t wait_ns = 2000000000ull;  // decode GEMV mbarrier wait bound (vfmoe_debug_inject)
@@ -50,7 +56,9 @@ struct Layer {
 };
 
 struct WsLayout {
-    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, tiles, tile_counts, tiles_cap, total;
+    int64_t counts, offsets, perm_tok, pos_of, idx, w, part, xp, act, y, tiles, tile_counts, tiles_cap;
+    int64_t xs, act_s, y_s;  // dense shared expert: fp16 x [T][H], fp16 act [T][I], fp32 y [T][H]
+    int64_t total;
 };
 
 Layer *get_layer(int64_t h);

@@ -46,8 +46,11 @@ static int desc_sections(vfmoe_layer_desc &d, std::vector<PackSection> &out) {
         if (!m.data) continue;
         const int64_t K = kk[i % 3], N = nn[i % 3];
         const int64_t count = i < 3 ? E : 1;
+        const bool dense = i >= 3 && d.shared_format == VFMOE_WFMT_BF16;
         int64_t one;
-        if (d.weight_format == VFMOE_WFMT_EXL3)
+        if (dense)
+            one = N * K * 2;  // bf16 rows [out][in]
+        else if (d.weight_format == VFMOE_WFMT_EXL3)
             one = K / 16 * (N / 16) * 2 * 16 * d.exl3_bits;
         else
             one = N * (K / 32 * 34);  // Q8_0 rows = output channels
@@ -57,7 +60,7 @@ static int desc_sections(vfmoe_layer_desc &d, std::vector<PackSection> &out) {
             return VFMOE_ERR_INVALID;
         }
         out.push_back({&m.data, count > 1 ? stride * (count - 1) + one : one});
-        if (d.weight_format == VFMOE_WFMT_EXL3) {
+        if (d.weight_format == VFMOE_WFMT_EXL3 && !dense) {
             const int64_t ss = count > 1 ? m.suh_stride : K * 2, vs = count > 1 ? m.svh_stride : N * 2;
             out.push_back({&m.suh, count > 1 ? ss * (count - 1) + K * 2 : K * 2});
             out.push_back({&m.svh, count > 1 ? vs * (count - 1) + N * 2 : N * 2});
@@ -87,6 +90,67 @@ static int read_header(FILE *f, PackHeader &h, const char *path) {
         return VFMOE_ERR_INVALID;
     }
     return VFMOE_OK;
+}
+
+// n bytes of f at offset off into dst: host memory by one read, or device memory through two
+// pinned 32 MiB staging buffers, each chunk's copy overlapping the next chunk's read.
+// Synchronous.  `what` names the source in error messages.
+int read_range(FILE *f, int64_t off, int64_t n, char *dst, bool device, const char *what) {
+    if (fseek(f, off, SEEK_SET) != 0) {
+        set_error("%s: seek to %lld failed", what, (long long)off);
+        return VFMOE_ERR_INVALID;
+    }
+    if (!device) {
+        if (n > 0 && fread(dst, 1, n, f) != (size_t)n) {
+            set_error("%s: short read", what);
+            return VFMOE_ERR_INVALID;
+        }
+        return VFMOE_OK;
+    }
+    if (n == 0) return VFMOE_OK;
+    const int64_t chunk = 32 << 20;
+    char *stage = nullptr;
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    int rc = VFMOE_OK;
+    cudaError_t e = cudaHostAlloc(&stage, 2 * std::min<int64_t>(chunk, n), cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
+    if (e != cudaSuccess) rc = cuda_fail(e, "staging for a device read", __FILE__, __LINE__);
+    const int64_t cs = std::min<int64_t>(chunk, n);
+    bool used[2] = {false, false};
+    int which = 0;
+    for (int64_t p = 0; !rc && p < n; p += cs) {
+        const int64_t m = std::min(cs, n - p);
+        char *buf = stage + which * cs;
+        if (used[which] && (e = cudaEventSynchronize(done[which])) != cudaSuccess) {
+            rc = cuda_fail(e, "device read", __FILE__, __LINE__);
+            break;
+        }
+        if (fread(buf, 1, m, f) != (size_t)m) {
+            set_error("%s: short read", what);
+            rc = VFMOE_ERR_INVALID;
+            break;
+        }
+        e = cudaMemcpyAsync(dst + p, buf, m, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(done[which], st);
+        if (e != cudaSuccess) {
+            rc = cuda_fail(e, "device read", __FILE__, __LINE__);
+            break;
+        }
+        used[which] = true;
+        which ^= 1;
+    }
+    if (st) {
+        e = cudaStreamSynchronize(st);
+        if (!rc && e != cudaSuccess) rc = cuda_fail(e, "device read", __FILE__, __LINE__);
+        cudaStreamDestroy(st);
+    }
+    for (int b = 0; b < 2; ++b)
+        if (done[b]) cudaEventDestroy(done[b]);
+    if (stage) cudaFreeHost(stage);
+    return rc;
 }
 
 }  // namespace vfmoe
@@ -198,60 +262,9 @@ int vfmoe_pack_load(const char *path, int64_t dev_base, int64_t dev_bytes, vfmoe
                   (long long)dev_bytes);
         rc = VFMOE_ERR_WORKSPACE;
     }
-    // sequential read through two pinned staging buffers; each chunk's copy overlaps the next read
-    const int64_t chunk = 32 << 20;
-    char *stage[2] = {nullptr, nullptr};
-    cudaEvent_t done[2] = {nullptr, nullptr};
-    cudaStream_t st = nullptr;
-    if (!rc) {
-        cudaError_t e = cudaHostAlloc(&stage[0], 2 * chunk, cudaHostAllocDefault);
-        if (e == cudaSuccess) stage[1] = stage[0] + chunk;
-        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
-        if (e != cudaSuccess) rc = cuda_fail(e, "vfmoe_pack_load: staging", __FILE__, __LINE__);
-    }
-    int which = 0;
-    bool used[2] = {false, false};
-    for (uint32_t i = 0; !rc && i < h.n_sections; ++i) {
-        if (fseek(f, kPackAlign + h.sec_off[i], SEEK_SET) != 0) {
-            set_error("vfmoe_pack_load: %s: seek failed", path);
-            rc = VFMOE_ERR_INVALID;
-            break;
-        }
-        for (int64_t p = 0; !rc && p < h.sec_bytes[i]; p += chunk) {
-            const int64_t n = std::min(chunk, h.sec_bytes[i] - p);
-            if (used[which]) {
-                cudaError_t e = cudaEventSynchronize(done[which]);
-                if (e != cudaSuccess) {
-                    rc = cuda_fail(e, "vfmoe_pack_load: copy", __FILE__, __LINE__);
-                    break;
-                }
-            }
-            if (fread(stage[which], 1, n, f) != (size_t)n) {
-                set_error("vfmoe_pack_load: %s: short read in section %u", path, i);
-                rc = VFMOE_ERR_INVALID;
-                break;
-            }
-            cudaError_t e = cudaMemcpyAsync(reinterpret_cast<char *>(dev_base) + h.sec_off[i] + p, stage[which], n,
-                                            cudaMemcpyHostToDevice, st);
-            if (e == cudaSuccess) e = cudaEventRecord(done[which], st);
-            if (e != cudaSuccess) {
-                rc = cuda_fail(e, "vfmoe_pack_load: copy", __FILE__, __LINE__);
-                break;
-            }
-            used[which] = true;
-            which ^= 1;
-        }
-    }
-    if (st) {
-        cudaError_t e = cudaStreamSynchronize(st);
-        if (!rc && e != cudaSuccess) rc = cuda_fail(e, "vfmoe_pack_load: copy", __FILE__, __LINE__);
-        cudaStreamDestroy(st);
-    }
-    for (int b = 0; b < 2; ++b)
-        if (done[b]) cudaEventDestroy(done[b]);
-    if (stage[0]) cudaFreeHost(stage[0]);
+    for (uint32_t i = 0; !rc && i < h.n_sections; ++i)
+        rc = read_range(f, kPackAlign + h.sec_off[i], h.sec_bytes[i], reinterpret_cast<char *>(dev_base) + h.sec_off[i],
+                        true, path);
     fclose(f);
     if (rc) return rc;
     for (auto &s : secs) *s.desc_word = dev_base + *s.desc_word;

@@ -227,4 +227,17 @@ int launch_rmsnorm(const void *x, const float *w, void *y, int64_t S, int D, flo
     return VFMOE_OK;
 }
 
+// dst[i] = fp16(src[i]) for src of dtype BF16, F16 or F32 (round to nearest even).
+__global__ void to_f16_kernel(const void *__restrict__ src, int dtype, int64_t n, __half *__restrict__ dst) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __float2half_rn(ld_act(src, i, dtype));
+}
+
+int launch_to_f16(const void *src, int dtype, int64_t n, __half *dst, cudaStream_t st) {
+    if (n == 0) return VFMOE_OK;
+    to_f16_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(src, dtype, n, dst);
+    VF_LAUNCH_CHECK("to_f16_kernel");
+    return VFMOE_OK;
+}
+
 }  // namespace vfmoe

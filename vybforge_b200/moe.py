@@ -61,11 +61,13 @@ class MoELayer:
     EXL3 weights: each projection is a tuple (trellis int16 [E, K/16, N/16, 16*bits],
     suh fp16 [E, K], svh fp16 [E, N]); shared likewise without the leading E.
     path: expert kernels, "auto" (default), "tc", "gemv" or "simt" (vfmoe_layer_desc.expert_path).
+    shared_format="bf16": the shared expert is (gate, up, down) bf16 [out, in] matrices as a Hugging
+    Face checkpoint stores them (GLM-5.3: EXL3 routed experts, bf16 shared expert).
     """
 
     def __init__(self, *, hidden, inter, n_experts, topk, router_w, router_bias, gate, up, down,
                  shared=None, fmt="q8_0", exl3_bits=3, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16,
-                 scale=2.5, limit=10.0, n_local_experts=0, path="auto"):
+                 scale=2.5, limit=10.0, n_local_experts=0, path="auto", shared_format=None):
         self.lib = _lib.load()
         self.H, self.I, self.E, self.k = hidden, inter, n_experts, topk
         self.x_dtype, self.out_dtype = x_dtype, out_dtype
@@ -97,7 +99,12 @@ class MoELayer:
         fill(d.gate, gate, True)
         fill(d.up, up, True)
         fill(d.down, down, True)
-        if shared is not None:
+        if shared is not None and shared_format == "bf16":
+            d.shared_format = _lib.WFMT_BF16
+            for m, w in zip((d.sh_gate, d.sh_up, d.sh_down), shared):
+                assert w.dtype == torch.bfloat16 and w.is_contiguous()
+                m.data = _ptr(w)
+        elif shared is not None:
             fill(d.sh_gate, shared[0], False)
             fill(d.sh_up, shared[1], False)
             fill(d.sh_down, shared[2], False)
