@@ -6,10 +6,14 @@ Python modules (rickenator/VybForge):
   native/exl3/exl3_ref.py   decode_mcg, dequant_exl3 (4-bpw, verified slot map)
   native/glm53/hc_ref.py    mix / apply_ (GLM-5.3 hyper-connections)
 
+and by copying the reference's committed real-weight router case (native/glm53/prep: GLM router
+weights of one layer, bf16-valued, its correction bias, four hidden rows and the reference's
+ids and weights for them).
+
 Usage (needs the reference checkout; the fixtures are committed, so the tests
 themselves never read the reference):
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT [c0 q8 exl3 hc]]
+    python tests/golden/make_golden.py [REFERENCE_ROOT [c0 q8 exl3 hc prep]]
 
 REFERENCE_ROOT defaults to $VYBFORGE_REFERENCE, else a "reference" checkout beside this
 repository.
@@ -126,14 +130,31 @@ def hc_fixture(ref):
     print("hc_kat.npz: R", R, "D", D)
 
 
+def prep_router_fixture(ref):
+    """The router part of native/glm53/prep (S=4, H=4096, E=288, k=8): gate.f32 holds bf16 values,
+    so it is stored as bf16 bits; y, bias and the reference's ref_idx / ref_w as they are."""
+    d = os.path.join(ref, "native/glm53/prep")
+    H, E, k = 4096, 288, 8
+
+    def f(n, shape):
+        return np.fromfile(os.path.join(d, n + ".f32"), dtype="<f4").reshape(shape)
+    gate = f("gate", (E, H))
+    bits = (gate.view(np.uint32) >> 16).astype(np.uint16)
+    assert np.array_equal((bits.astype(np.uint32) << 16).view(np.float32), gate), "gate.f32 is not bf16-valued"
+    np.savez_compressed(os.path.join(HERE, "glm_router_prep.npz"), gate_bits=bits, bias=f("bias", (E,)),
+                        y=f("y", (4, H)), ref_idx=f("ref_idx", (4, k)).astype(np.int32), ref_w=f("ref_w", (4, k)))
+    print("glm_router_prep.npz: S 4, H", H, "E", E, "k", k)
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
         "VYBFORGE_REFERENCE", os.path.normpath(os.path.join(REPO, os.pardir, "reference")))
     if not os.path.isdir(os.path.join(ref, "native")):
         sys.exit(f"reference checkout not found at {ref}")
-    which = sys.argv[2:] or ["c0", "q8", "exl3", "hc"]
+    which = sys.argv[2:] or ["c0", "q8", "exl3", "hc", "prep"]
     for name in which:
-        {"c0": c0_fixture, "q8": q8_fixture, "exl3": exl3_fixture, "hc": hc_fixture}[name](ref)
+        {"c0": c0_fixture, "q8": q8_fixture, "exl3": exl3_fixture, "hc": hc_fixture,
+         "prep": prep_router_fixture}[name](ref)
 
 
 if __name__ == "__main__":

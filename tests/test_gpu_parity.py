@@ -101,6 +101,30 @@ def test_route_ties_lowest_index():
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
 
 
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
+def test_route_ties_lowest_index_prefill_batch(x_dtype):
+    """Exact ties at a prefill batch (T=300: tensor-core or tiled first level, one warp per token in
+    the refinement): experts 2 and 9 have zero router rows and equal bias, so their choices tie
+    exactly on every token and the lower id must come first, as in the f64 oracle."""
+    moe.init(0)
+    cfg = synth.config("c1", tokens=300)
+    x, w_r, bias, _ = synth.router_inputs(cfg)
+    w_r = w_r.copy()
+    bias = bias.copy()
+    w_r[2] = 0.0
+    w_r[9] = 0.0
+    bias[2] = bias[9] = 1.0
+    layer = _router_layer(w_r, bias, cfg.hidden, cfg.n_experts, cfg.topk, x_dtype=x_dtype)
+    xd = torch.from_numpy(x).to(x_dtype).cuda()
+    idx, w = layer.route(xd)
+    ri, rw = orc.route(xd.float().cpu().numpy(), w_r, bias, cfg.topk)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=1e-6)
+    assert (idx.cpu().numpy()[:, :2] == [2, 9]).all()
+    layer.check_device_error()
+    layer.close()
+
+
 # ----------------------------------------------------------------------------- full-size C1 (Q8_0 decode)
 @pytest.fixture(scope="module")
 def c1():
@@ -293,7 +317,31 @@ def _router_layer(w_r, bias, H, E, k, x_dtype=torch.bfloat16):
                     out_dtype=torch.float32)
 
 
-@pytest.mark.parametrize("T", [16, 96])
+@pytest.mark.parametrize("reps", [1, 12, 75])
+def test_router_on_real_glm_router_weights(reps):
+    """The reference's real-weight router case (tests/golden/glm_router_prep.npz, from its
+    native/glm53/prep: GLM router weights of one layer, E=288, H=4096, k=8, four fp32 hidden rows):
+    ids equal the reference's ref_idx and weights its ref_w.  reps=12 and 75 repeat the rows (T=48,
+    T=300) to take the multi-token first level and the one-warp-per-token refinement; every copy
+    must route alike."""
+    moe.init(0)
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "glm_router_prep.npz"))
+    w_r = (g["gate_bits"].astype(np.uint32) << 16).view(np.float32)
+    H, E, k = 4096, 288, 8
+    layer = _router_layer(np.ascontiguousarray(w_r), g["bias"], H, E, k, x_dtype=torch.float32)
+    x = torch.from_numpy(np.tile(g["y"], (reps, 1))).cuda()
+    idx, w = layer.route(x)
+    torch.cuda.synchronize()
+    layer.check_device_error()
+    ref_idx, ref_w = np.tile(g["ref_idx"], (reps, 1)), np.tile(g["ref_w"], (reps, 1))
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
+    d = float(np.abs(w.cpu().numpy() - ref_w).max())
+    print(f"[real GLM router T={4 * reps}] ids equal ref_idx; max |w - ref_w| {d:.2e}")
+    assert d <= 1e-6
+    layer.close()
+
+
+@pytest.mark.parametrize("T", [16, 96, 300])
 def test_router_near_ties_take_the_f64_level(T):
     """Pairs of experts whose router rows differ by one fp32 ulp in one element: their
     logits differ by ~1e-9, below the float-float bound, so the f64 level must order them."""

@@ -80,6 +80,17 @@ def test_prep_fixture_bit_exact():
     np.testing.assert_array_equal(out.astype(np.float32), f("ref_out", (4, H)))
 
 
+def test_real_router_fixture_reproduced():
+    """tests/golden/glm_router_prep.npz (the router part of the reference's native/glm53/prep: real
+    GLM router weights of one layer, its correction bias, four hidden rows): the oracle's route
+    gives the reference's ids exactly and its weights to the f32 rounding."""
+    g = np.load(os.path.join(GOLD, "glm_router_prep.npz"))
+    w_r = (g["gate_bits"].astype(np.uint32) << 16).view(np.float32)
+    idx, w = orc.route(g["y"].astype(np.float64), w_r, g["bias"], 8)
+    np.testing.assert_array_equal(idx, g["ref_idx"])
+    np.testing.assert_array_equal(w.astype(np.float32), g["ref_w"])
+
+
 def test_q8_0_decode_matches_reference_kat():
     g = np.load(os.path.join(GOLD, "q8_0_kat.npz"))
     raw, deq = g["raw"], g["deq"]
