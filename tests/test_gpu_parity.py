@@ -103,11 +103,11 @@ def test_route_ties_lowest_index():
 
 @pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
 def test_route_ties_lowest_index_prefill_batch(x_dtype):
-    """Exact ties at a prefill batch (T=300: tensor-core or tiled first level, one warp per token in
-    the refinement): experts 2 and 9 have zero router rows and equal bias, so their choices tie
+    """Exact ties at a prefill batch (T=4096: tensor-core or tiled first level, one warp per token
+    in the refinement): experts 2 and 9 have zero router rows and equal bias, so their choices tie
     exactly on every token and the lower id must come first, as in the f64 oracle."""
     moe.init(0)
-    cfg = synth.config("c1", tokens=300)
+    cfg = synth.config("c1", tokens=4096)
     x, w_r, bias, _ = synth.router_inputs(cfg)
     w_r = w_r.copy()
     bias = bias.copy()
@@ -317,12 +317,12 @@ def _router_layer(w_r, bias, H, E, k, x_dtype=torch.bfloat16):
                     out_dtype=torch.float32)
 
 
-@pytest.mark.parametrize("reps", [1, 12, 75])
+@pytest.mark.parametrize("reps", [1, 12, 1024])
 def test_router_on_real_glm_router_weights(reps):
     """The reference's real-weight router case (tests/golden/glm_router_prep.npz, from its
     native/glm53/prep: GLM router weights of one layer, E=288, H=4096, k=8, four fp32 hidden rows):
-    ids equal the reference's ref_idx and weights its ref_w.  reps=12 and 75 repeat the rows (T=48,
-    T=300) to take the multi-token first level and the one-warp-per-token refinement; every copy
+    ids equal the reference's ref_idx and weights its ref_w.  reps=12 and 1024 repeat the rows (T=48,
+    T=4096) to take the multi-token first level and the one-warp-per-token refinement; every copy
     must route alike."""
     moe.init(0)
     g = np.load(os.path.join(os.path.dirname(__file__), "golden", "glm_router_prep.npz"))
@@ -341,7 +341,7 @@ def test_router_on_real_glm_router_weights(reps):
     layer.close()
 
 
-@pytest.mark.parametrize("T", [16, 96, 300])
+@pytest.mark.parametrize("T", [16, 96, 4096])
 def test_router_near_ties_take_the_f64_level(T):
     """Pairs of experts whose router rows differ by one fp32 ulp in one element: their
     logits differ by ~1e-9, below the float-float bound, so the f64 level must order them."""

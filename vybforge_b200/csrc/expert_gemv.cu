@@ -11,14 +11,19 @@
 // from shared memory exactly once, as raw Q8_0 bytes.
 //
 // Data path per CTA (one per SM, persistent over (expert, token tile, channel tile)):
-//   warp 8       TMA producer: per stage, 8 Q8_0 blocks (272 B) of each weight row of the
+//   warp 16      TMA producer: per stage, 8 Q8_0 blocks (272 B) of each weight row of the
 //                tile (a TMA box from GGUF rows, or one bulk copy per 64 rows from
 //                stage-tiled weights) plus the 256-K slice of the tile's N token rows
 //                (fp16, SWIZZLE_128B).
-//   warps 0..7   consumers, 16 weight rows each: LDS raw bytes -> fp16(d*q) fragments in
-//                registers -> mma.sync against token fragments -> fp32 accumulators.
-//                gate/up tile = 64 channels x (gate, up): warps 0-3 gate, 4-7 up, SwiGLU
-//                after an exchange through shared memory; down tile = 128 channels.
+//   warps 0..15  consumers in two K halves: warps 8h..8h+7 take the 64-K pairs 2h and 2h+1 of
+//                every stage, 16 weight rows each: LDS raw bytes -> fp16(d*q) fragments in
+//                registers -> mma.sync against token fragments -> fp32 accumulators.  The
+//                second half's partial sums join the first half's in the epilogue (shared
+//                memory).  gate/up tile = 64 channels x (gate, up): warps 0-3 gate, 4-7 up,
+//                SwiGLU after an exchange through shared memory; down tile = 128 channels.
+//                Two warps per scheduler left the kernel stalled on the fixed latency between
+//                the Q8_0 -> fp16 conversion and its mma.sync (0.77 of HBM); four reach 0.92.
+//                (The split-precision form keeps 8 consumers, one K range: warp 8 produces.)
 // K permutation: within each 64-K pair of Q8_0 blocks, thread (g, c) of the MMA quad owns
 // actual k in [16c, 16c + 16) for both A and B, so each thread converts 16 consecutive
 // quants of a row and loads 32 consecutive token bytes.
@@ -45,13 +50,17 @@ namespace vfmoe {
 
 using namespace sm100;
 
-constexpr int kGvConsumers = 8;
-constexpr int kGvThreads = 32 * (kGvConsumers + 1);
 constexpr int kRow = 272;            // 8 Q8_0 blocks (256 K) of one weight row
 constexpr int kWBytes = 128 * kRow;  // weights per stage: 64 rows x 2 matrices or 128 rows
 
 template <bool GATEUP, int NT, bool PREC, bool DENSE = false>
 struct GvCfg {
+    // consumer warps: 16 split each stage's K in two halves (pairs 0-1 and 2-3), whose partial
+    // sums meet in the epilogue; the split-precision form keeps 8 (its three accumulators need
+    // the registers)
+    static constexpr int CONS = PREC ? 8 : 16;
+    static constexpr int HALVES = CONS / 8;
+    static constexpr int THREADS = 32 * (CONS + 1);
     static constexpr int N = 8 * NT;
     static constexpr int ROWS = GATEUP ? 64 : 128;  // channels per tile
     static constexpr int TOK1 = N * 512;            // N rows x 256 K fp16: one plane
@@ -61,7 +70,9 @@ struct GvCfg {
     static constexpr int WBOX = ROWS * 128;
     static constexpr int WB = DENSE ? (GATEUP ? 2 : 1) * 4 * WBOX : kWBytes;
     static constexpr int STAGE = WB + TOK;
-    static constexpr int XCH = GATEUP ? ROWS * N * 4 : 0;
+    // epilogue exchange, fp32 [rows of the tile][N]: the second K half's partial sums, then (gate/up)
+    // the up rows for the SwiGLU
+    static constexpr int XCH = HALVES == 2 ? (GATEUP ? 2 : 1) * ROWS * N * 4 : (GATEUP ? ROWS * N * 4 : 0);
     static constexpr int SW = (230000 - XCH - 1024) / STAGE > 6 ? 6 : (230000 - XCH - 1024) / STAGE;
     static constexpr int SMEM = SW * STAGE + XCH + 2 * SW * 8 + 16 + 1024;
     static_assert(SW >= 2, "at least double buffering");
@@ -140,9 +151,10 @@ __device__ __forceinline__ void q8_frag_prec(const uint8_t *row, int p, int c, u
 }
 
 template <bool GATEUP, int NT, bool PREC, bool DENSE>
-__global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(GvCfg<GATEUP, NT, PREC, DENSE>::THREADS, 1)
+    expert_gemv_mma(const __grid_constant__ TcParams p) {
     using C = GvCfg<GATEUP, NT, PREC, DENSE>;
-    constexpr int SW = C::SW, N = C::N, ROWS = C::ROWS;
+    constexpr int SW = C::SW, N = C::N, ROWS = C::ROWS, CONS = C::CONS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *xch = reinterpret_cast<float *>(smem + SW * C::STAGE);
@@ -156,7 +168,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     if (threadIdx.x == 0) {
         for (int i = 0; i < SW; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kGvConsumers);
+            mbar_init(&empty[i], CONS);
         }
         *abort = 0;
         fence_mbar_init();
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
         }
     };
 
-    if (warp == kGvConsumers) {
+    if (warp == CONS) {
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0 && !p.stall) {
             if (PREC) prefetch_tmap(&p.xt2);
@@ -277,8 +289,10 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
     } else {
         // ------------------------------------------------------------------ consumers
         const int g = lane >> 2, c = lane & 3;
-        const int mat = GATEUP ? (warp >> 2) : 0;
-        const int r0 = GATEUP ? 16 * (warp & 3) : 16 * warp;  // first row of this warp in its matrix tile
+        const int half = warp >> 3, lw = warp & 7;            // K half (pairs 2 half .. 2 half + 4 / HALVES - 1)
+        const int mat = GATEUP ? (lw >> 2) : 0;
+        const int r0 = GATEUP ? 16 * (lw & 3) : 16 * lw;      // first row of this warp in its matrix tile
+        const int xrow0 = mat * ROWS + r0;                    // the warp's rows in the exchange buffer
         uint32_t n = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -298,7 +312,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                 const uint8_t *rowA = st + (mat * ROWS + r0 + g) * kRow;
                 const uint8_t *rowB = rowA + 8 * kRow;
 #pragma unroll
-                for (int pq = 0; pq < 4; ++pq) {
+                for (int pi = 0; pi < 4 / C::HALVES; ++pi) {
+                    const int pq = half * (4 / C::HALVES) + pi;
                     uint32_t wa[8], wb[8], la[PREC ? 8 : 1], lb[PREC ? 8 : 1];
                     if constexpr (DENSE) {
                         // rows r0+g and r0+g+8 of this matrix's box pq, 16-byte chunks 2c and 2c+1
@@ -364,18 +379,39 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
             }
             // ---------------------------------------------------------------- epilogue
             // acc[j]: rows r0+g (0,1) and r0+g+8 (2,3) x tokens 8j+2c, 8j+2c+1
+            if constexpr (C::HALVES == 2) {
+                // the second K half hands its partial sums to the first through xch
+                if (half == 1) {
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            xch[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)] = acc[j][e];
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
+                if (half == 0) {
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            acc[j][e] += xch[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)];
+                }
+            }
+            // up rows for the SwiGLU: with two halves each first-half warp overwrites only the
+            // xch entries it has just read (its own rows)
+            float *xup = xch + (C::HALVES == 2 ? ROWS * N : 0);
             if (GATEUP) {
-                if (mat == 1) {
+                if (mat == 1 && half == 0) {
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
-                            xch[rr * N + tok] = acc[j][e];
+                            xup[rr * N + tok] = acc[j][e];
                         }
                 }
-                asm volatile("bar.sync 1, %0;" ::"r"(32 * kGvConsumers) : "memory");
-                if (mat == 0) {
+                asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
+                if (mat == 0 && half == 0) {
                     __half *out = reinterpret_cast<__half *>(p.out);
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
@@ -383,7 +419,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                         for (int e = 0; e < 4; ++e) {
                             const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
                             if (tok < t.z) {
-                                const float a = swiglu_clamped(acc[j][e], xch[rr * N + tok], p.limit);
+                                const float a = swiglu_clamped(acc[j][e], xup[rr * N + tok], p.limit);
                                 const int64_t o = (int64_t)(t.y + tok) * p.ld_out + m0 + rr;
                                 const __half ah = __float2half_rn(a);
                                 out[o] = ah;
@@ -391,16 +427,20 @@ __global__ void __launch_bounds__(kGvThreads, 1) expert_gemv_mma(const __grid_co
                             }
                         }
                 }
-                asm volatile("bar.sync 1, %0;" ::"r"(32 * kGvConsumers) : "memory");
+                asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
             } else {
-                float *out = reinterpret_cast<float *>(p.out);
+                if (half == 0) {
+                    float *out = reinterpret_cast<float *>(p.out);
 #pragma unroll
-                for (int j = 0; j < NT; ++j)
+                    for (int j = 0; j < NT; ++j)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
-                        if (tok < t.z) out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = acc[j][e];
-                    }
+                        for (int e = 0; e < 4; ++e) {
+                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                            if (tok < t.z) out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = acc[j][e];
+                        }
+                }
+                // xch is rewritten by the next item's second half only after this point
+                if constexpr (C::HALVES == 2) asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
             }
         }
         if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
@@ -414,13 +454,13 @@ static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
                                          C::SMEM))
         return rc_attr;
     if (GATEUP) {
-        expert_gemv_mma<GATEUP, NT, PREC, DENSE><<<grid, kGvThreads, C::SMEM, st>>>(prm);
+        expert_gemv_mma<GATEUP, NT, PREC, DENSE><<<grid, C::THREADS, C::SMEM, st>>>(prm);
     } else {
         // programmatic dependent launch: CTAs start streaming down weights on SMs the gate/up
         // grid has released, before its act rows are complete
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(kGvThreads);
+        cfg.blockDim = dim3(C::THREADS);
         cfg.dynamicSmemBytes = C::SMEM;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];

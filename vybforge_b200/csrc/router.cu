@@ -29,6 +29,11 @@ namespace vfmoe {
 constexpr int kMaxCand = 128;
 constexpr int kMaxH = 16384;     // router_refine keeps x_t in shared memory (fp32)
 constexpr int kMaxChunks = 32;   // L1 decode partial-sum chunks (H / 512)
+// router_refine_warp (one warp per token) from this batch size up.  Its per-token latency is
+// longer (one warp streams every candidate row of W_r) but it has no block barriers and no
+// all-pairs ranking, so it wins once the batch fills the GPU several times over (C1 shapes:
+// T = 2048 148 vs 179 us, T = 4096 276 vs 236 us, T = 8192 516 vs 378 us for the whole route).
+constexpr int kRefineWarpMinT = 3072;
 
 // Packed pairs of fp32 (sm_100 f32x2 arithmetic, round to nearest even in each lane).
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
@@ -562,6 +567,7 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
             const double sc = 1.0 / (1.0 + exp(-s_logit[c]));
             s_score[c] = sc;
             s_logit[c] = sc + (double)bias[e];  // reuse: now the choice
+            s_order[c] = -1;                    // stays -1 where NaN choices collide in rank
         }
         __syncwarp();
         for (int c = lane; c < nc; c += 32) {
@@ -578,6 +584,7 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
         __syncwarp();
         for (int r = lane; r < k && r + 1 < nc; r += 32) {
             const int a = s_order[r], b = s_order[r + 1];
+            if (a < 0 || b < 0) continue;
             const double ba = 0.25 * (double)c2 * nx * nw[s_cand[a]], bb = 0.25 * (double)c2 * nx * nw[s_cand[b]];
             if (s_logit[a] - s_logit[b] <= 2.0 * (ba + bb) + 1e-15) {
                 s_redo[a] = 1;
@@ -646,8 +653,10 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
         int e = -1;
         if (lane < k && lane < nc) {
             const int c = s_order[lane];
-            e = s_cand[c];
-            sc = s_score[c];
+            if (c >= 0) {
+                e = s_cand[c];
+                sc = s_score[c];
+            }
         }
         double sum = 0.0;
         for (int r = 0; r < k; ++r) sum += __shfl_sync(0xffffffffu, sc, r);
@@ -659,6 +668,272 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
             else
                 raise_dev_error(err, DEV_BAD_EXPERT_ID);
         }
+    }
+}
+
+// ----------------------------------------------------------------------------- L2 + L3, one warp per token
+// The same three levels as router_refine, for batches large enough to fill the GPU with one warp
+// per token (four tokens per CTA), so that no step waits on a block barrier:
+//   * tau, the k-th largest lower bound in the order (lo desc, id asc), is the k-th of k rounds
+//     of a warp-wide max over 64-bit keys (orderable lo, ~id): about 40 instructions per lane and
+//     round, where router_refine ranks every expert against every other;
+//   * a candidate's float-float logit is accumulated by the 32 lanes over H (lane l holds
+//     h = 4 l + 128 j, two candidates per packed f32x2 instruction) and reduced by a TwoSum
+//     butterfly across the lanes;
+//   * the f64 ordering, the f64 level for close neighbours and the weights run on the same warp.
+// Lane l owns experts l, l + 32, ... (NPL of them, E <= 32 NPL).  Candidate lists, f64 logits and
+// scores live in the warp's slice of shared memory.
+constexpr int kRwWarps = 4;
+
+__device__ __forceinline__ uint32_t f32_order_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float f32_from_order_key(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+template <int NPL>
+__global__ void __launch_bounds__(32 * kRwWarps) router_refine_warp(
+    const void *__restrict__ x, int x_dtype, const float *__restrict__ wr, const float *__restrict__ logits,
+    int nchunk, const float *__restrict__ nw, const float *__restrict__ bias, int T, int H, int E, int k, float c1,
+    float c2, double scale, int32_t *__restrict__ idx_out, float *__restrict__ w_out, int32_t *__restrict__ counts,
+    int *__restrict__ err) {
+    __shared__ int s_cand[kRwWarps][kMaxCand];
+    __shared__ double s_logit[kRwWarps][kMaxCand];   // L2/L3 logit, then the choice (score + bias)
+    __shared__ double s_score[kRwWarps][kMaxCand];   // sigmoid(logit)
+    __shared__ int s_order[kRwWarps][kMaxCand];
+    __shared__ unsigned char s_redo[kRwWarps][kMaxCand];
+    pdl_wait_then_release();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kRwWarps + warp;
+    if (t >= T) return;
+    int *cand = s_cand[warp];
+    double *lg = s_logit[warp];
+    double *scr = s_score[warp];
+    int *order = s_order[warp];
+    unsigned char *redo = s_redo[warp];
+    const int64_t xrow = (int64_t)t * H;
+
+    // |x_t|_2, rounded up
+    float ss = 0.f;
+#pragma unroll 4
+    for (int h = 4 * lane; h < H; h += 128) {
+        float v[4];
+        ld_x4(x, x_dtype, xrow + h, v);
+        ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
+    }
+    const float nx = sqrtf(warp_sum_f32(ss)) * 1.001f;
+
+    // ---- L1 intervals [lo, hi] of every expert's choice, and tau
+    float hi[NPL];
+    uint64_t key[NPL];
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+        const int e = lane + 32 * i;
+        hi[i] = -INFINITY;
+        key[i] = 0ull;  // below every real expert's key
+        if (e < E) {
+            float l = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < nchunk; ++c) l += logits[((int64_t)c * T + t) * E + e];  // chunk order
+            const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;  // sigmoid slope <= 1/4; fp32 sigmoid + bias slack
+            float ca = 1.f / (1.f + expf(-l)) + bias[e];
+            if (isnan(ca)) ca = -INFINITY;
+            const float lo = ca - b1;
+            hi[i] = ca + b1;
+            bad |= isnan(lo);
+            key[i] = ((uint64_t)f32_order_key(lo) << 32) | (uint64_t)(~(uint32_t)e);
+        }
+    }
+    uint64_t kth = 0ull;
+    for (int r = 0; r < k; ++r) {
+        uint64_t m = 0ull;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) m = key[i] > m ? key[i] : m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t v = __shfl_xor_sync(0xffffffffu, m, o);
+            m = v > m ? v : m;
+        }
+#pragma unroll
+        for (int i = 0; i < NPL; ++i)
+            if (m != 0ull && key[i] == m) key[i] = 0ull;
+        kth = m;
+    }
+    // no k-th expert, or a NaN bound somewhere: every expert is a candidate
+    const float tau = (kth == 0ull || __any_sync(0xffffffffu, bad)) ? -INFINITY : f32_from_order_key((uint32_t)(kth >> 32));
+
+    // ---- candidates (hi >= tau) in ascending id order
+    int nc = 0;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+        const int e = lane + 32 * i;
+        const bool c = e < E && hi[i] >= tau;
+        const unsigned m = __ballot_sync(0xffffffffu, c);
+        const int pos = nc + __popc(m & ((1u << lane) - 1u));
+        if (c && pos < kMaxCand) cand[pos] = e;
+        nc += __popc(m);
+    }
+    if (nc > kMaxCand) {
+        if (lane == 0) raise_dev_error(err, DEV_BAD_COUNT);
+        nc = kMaxCand;
+    }
+    __syncwarp();
+
+    // ---- L2 float-float logits, two candidates at a time (a lone last candidate is paired with
+    // itself and its second copy discarded)
+    for (int c0 = 0; c0 < nc; c0 += 2) {
+        const int ea = cand[c0];
+        const int eb = c0 + 1 < nc ? cand[c0 + 1] : ea;
+        const float *wa = wr + (int64_t)ea * H;
+        const float *wb = wr + (int64_t)eb * H;
+        uint64_t sh = 0ull, sl = 0ull;  // packed {candidate a, candidate b}
+        for (int h0 = 4 * lane; h0 < H; h0 += 512) {
+            float4 va[4], vb[4];
+            float xv[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int h = h0 + 128 * u;
+                if (h < H) {
+                    va[u] = *reinterpret_cast<const float4 *>(wa + h);
+                    vb[u] = *reinterpret_cast<const float4 *>(wb + h);
+                    ld_x4(x, x_dtype, xrow + h, xv[u]);
+                } else {
+                    va[u] = vb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    xv[u][0] = xv[u][1] = xv[u][2] = xv[u][3] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float a4[4] = {va[u].x, va[u].y, va[u].z, va[u].w};
+                const float b4[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    // TwoProduct (x*w = p + pe exactly) and TwoSum (sh + p = sum + r exactly), per lane of the pair
+                    const uint64_t x2 = f2_pack(xv[u][i], xv[u][i]), w2 = f2_pack(a4[i], b4[i]);
+                    const uint64_t pp = f2_mul(x2, w2);
+                    const uint64_t pe = f2_fma(x2, w2, pp ^ 0x8000000080000000ull);
+                    const uint64_t sum = f2_add(sh, pp);
+                    const uint64_t bb = f2_sub(sum, sh);
+                    const uint64_t r = f2_add(f2_sub(sh, f2_sub(sum, bb)), f2_sub(pp, bb));
+                    sh = sum;
+                    sl = f2_add(sl, f2_add(r, pe));
+                }
+            }
+        }
+        float ha, hb, la, lb;
+        f2_unpack(sh, ha, hb);
+        f2_unpack(sl, la, lb);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oha = __shfl_xor_sync(0xffffffffu, ha, o), ola = __shfl_xor_sync(0xffffffffu, la, o);
+            const float ohb = __shfl_xor_sync(0xffffffffu, hb, o), olb = __shfl_xor_sync(0xffffffffu, lb, o);
+            float s, r;
+            two_sum(ha, oha, s, r);
+            ha = s;
+            la = la + ola + r;
+            two_sum(hb, ohb, s, r);
+            hb = s;
+            lb = lb + olb + r;
+        }
+        if (lane == 0) {
+            lg[c0] = (double)ha + (double)la;
+            if (c0 + 1 < nc) lg[c0 + 1] = (double)hb + (double)lb;
+        }
+    }
+    __syncwarp();
+
+    // ---- order candidates in f64 (choice desc, id asc); flag neighbours closer than the L2 bound
+    for (int c = lane; c < nc; c += 32) {
+        const double sc = 1.0 / (1.0 + exp(-lg[c]));
+        scr[c] = sc;
+        lg[c] = sc + (double)bias[cand[c]];
+    }
+    for (int c = lane; c < nc; c += 32) order[c] = -1;  // stays -1 where NaN choices collide in rank
+    __syncwarp();
+    for (int c = lane; c < nc; c += 32) {
+        const double ch = lg[c];
+        const int e = cand[c];
+        int rank = 0;
+        for (int o = 0; o < nc; ++o) {
+            const double oc = lg[o];
+            rank += (oc > ch || (oc == ch && cand[o] < e)) ? 1 : 0;
+        }
+        order[rank] = c;
+        redo[c] = 0;
+    }
+    __syncwarp();
+    bool amb = false;
+    for (int r = lane; r < k && r + 1 < nc; r += 32) {
+        const int a = order[r], b = order[r + 1];
+        if (a < 0 || b < 0) continue;
+        const double ba = 0.25 * (double)c2 * nx * nw[cand[a]], bb = 0.25 * (double)c2 * nx * nw[cand[b]];
+        if (lg[a] - lg[b] <= 2.0 * (ba + bb) + 1e-15) {
+            redo[a] = 1;
+            redo[b] = 1;
+            amb = true;
+        }
+    }
+    amb = __any_sync(0xffffffffu, amb);
+    __syncwarp();
+
+    // ---- L3: fp64 logits of the flagged candidates (rare), then reorder
+    if (amb) {
+        for (int c = 0; c < nc; ++c) {
+            if (!redo[c]) continue;
+            const float *wc = wr + (int64_t)cand[c] * H;
+            double acc = 0.0;
+            for (int h = 4 * lane; h < H; h += 128) {
+                float v[4];
+                ld_x4(x, x_dtype, xrow + h, v);
+                const float4 w4 = *reinterpret_cast<const float4 *>(wc + h);
+                acc = fma((double)v[0], (double)w4.x, acc);
+                acc = fma((double)v[1], (double)w4.y, acc);
+                acc = fma((double)v[2], (double)w4.z, acc);
+                acc = fma((double)v[3], (double)w4.w, acc);
+            }
+            acc = warp_sum_f64(acc);
+            if (lane == 0) {
+                const double sc = 1.0 / (1.0 + exp(-acc));
+                scr[c] = sc;
+                lg[c] = sc + (double)bias[cand[c]];
+            }
+        }
+        __syncwarp();
+        for (int c = lane; c < nc; c += 32) {
+            const double ch = lg[c];
+            const int e = cand[c];
+            int rank = 0;
+            for (int o = 0; o < nc; ++o) {
+                const double oc = lg[o];
+                rank += (oc > ch || (oc == ch && cand[o] < e)) ? 1 : 0;
+            }
+            order[rank] = c;
+        }
+        __syncwarp();
+    }
+
+    // ---- top-k and weights: scores = choice - bias, in f64
+    double sc = 0.0;
+    int e = -1;
+    if (lane < k && lane < nc) {
+        const int c = order[lane];
+        if (c >= 0) {
+            e = cand[c];
+            sc = scr[c];
+        }
+    }
+    double sum = 0.0;
+    for (int r = 0; r < k; ++r) sum += __shfl_sync(0xffffffffu, sc, r);
+    if (lane < k) {
+        idx_out[(int64_t)t * k + lane] = e;
+        w_out[(int64_t)t * k + lane] = (float)(sc / (sum + 1e-20) * scale);
+        if (e >= 0 && e < E)
+            atomicAdd(&counts[e], 1);
+        else
+            raise_dev_error(err, DEV_BAD_EXPERT_ID);
     }
 }
 
@@ -756,6 +1031,25 @@ int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat
     const int n2 = H / 256;
     const float c2 = gamma_bound(2 * n2 + 24) * (float)(n2 + 1 + 24) * 5.9604645e-8f;
     const int npl = (int)cdiv(E, 32);
+    if (T >= kRefineWarpMinT && npl <= 16) {
+        // One warp per token: a lane owns nl = 4 ceil(H / 128) terms; the 5-level lane butterfly adds
+        // 31 TwoSum error terms (each <= u S) and 10 fp32 additions of depth to lo's summation:
+        // |err| <= gamma_{2 nl + 10} (nl + 32) u S.
+        const int nl = 4 * (int)cdiv(H, 128);
+        const float c2w = gamma_bound(2 * nl + 10) * (float)(nl + 32) * 5.9604645e-8f;
+        const dim3 grid((unsigned)cdiv(T, kRwWarps));
+#define VF_REFINE_W(NPL)                                                                                           \
+    VF_CUDA(launch_pdl(router_refine_warp<NPL>, grid, dim3(32 * kRwWarps), 0, st, x, x_dtype, wr, (const float *)logits, \
+                       nchunk, nw, bias, T, H, E, k, c1, c2w, scale, idx, w, counts, err))
+        if (npl <= 1) VF_REFINE_W(1);
+        else if (npl <= 2) VF_REFINE_W(2);
+        else if (npl <= 4) VF_REFINE_W(4);
+        else if (npl <= 8) VF_REFINE_W(8);
+        else VF_REFINE_W(16);
+#undef VF_REFINE_W
+        VF_LAUNCH_CHECK("router_refine_warp");
+        return VFMOE_OK;
+    }
     if (H * 4 > 48 * 1024) {
         if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<1, 8, 1>), kMaxH * 4))) return rc;
         if ((rc = set_smem_attr_once(reinterpret_cast<const void *>(router_refine<1, 4, 3>), kMaxH * 4))) return rc;
