@@ -87,6 +87,10 @@ extern "C" {
 #define VFMOE_PATH_SIMT 1
 #define VFMOE_PATH_TC 2
 #define VFMOE_PATH_GEMV 3
+/* TC1: the tcgen05 GEMM with single-CTA tiles only.  AUTO and TC run tiles of N >= 32 token rows
+ * on CTA pairs (tcgen05 cta_group::2: 256 channels per tile, 128 per SM); TC1 is the form they are
+ * checked against. */
+#define VFMOE_PATH_TC1 4
 
 /* One projection (gate, up or down) of a stack of experts.  Expert e's data
  * starts at data + e * expert_stride (bytes); for EXL3 its suh/svh start at

@@ -47,8 +47,8 @@ def test_constants_match_header():
         assert d["VFMOE_" + k] == getattr(_lib, k)
     assert (d["VFMOE_DT_F32"], d["VFMOE_DT_F16"], d["VFMOE_DT_BF16"]) == (0, 1, 2)  # native/dtype/dtype.vyb
     assert (d["VFMOE_WFMT_Q8_0"], d["VFMOE_WFMT_EXL3"]) == (_lib.WFMT_Q8_0, _lib.WFMT_EXL3)
-    assert (d["VFMOE_PATH_AUTO"], d["VFMOE_PATH_SIMT"], d["VFMOE_PATH_TC"], d["VFMOE_PATH_GEMV"]) == (
-        _lib.PATH_AUTO, _lib.PATH_SIMT, _lib.PATH_TC, _lib.PATH_GEMV)
+    assert (d["VFMOE_PATH_AUTO"], d["VFMOE_PATH_SIMT"], d["VFMOE_PATH_TC"], d["VFMOE_PATH_GEMV"], d["VFMOE_PATH_TC1"]) == (
+        _lib.PATH_AUTO, _lib.PATH_SIMT, _lib.PATH_TC, _lib.PATH_GEMV, _lib.PATH_TC1)
     assert (d["VFMOE_INJECT_NONE"], d["VFMOE_INJECT_STALL_LOADS"]) == (_lib.INJECT_NONE, _lib.INJECT_STALL_LOADS)
 
 

@@ -392,6 +392,30 @@ def test_decode_gemv_matches_tcgen05_gemm(c1, T):
     assert rel_l2(gv, tc) < 5e-4
 
 
+@pytest.mark.parametrize("T", [32, 1024, 4096])
+def test_cta_pair_gemm_matches_single_cta_tiles(c1, c1_tiled, T):
+    """Prefill tiles (N >= 32) run on CTA pairs (tcgen05 cta_group::2, 256 channels per tile);
+    expert_path "tc1" keeps single-CTA tiles.  Same fp16 operands, same K order per output: the
+    outputs agree to fp32 accumulation (GGUF rows and stage-tiled weights alike)."""
+    g = torch.Generator(device="cuda").manual_seed(7 + T)
+    x = torch.randn((T, c1.cfg.hidden), generator=g, device="cuda").to(torch.bfloat16)
+    path = "tc" if T == 32 else "auto"   # T = 32 averages one row per expert: force the GEMM
+    pair = c1.make_layer(torch.float32, path=path)
+    single = c1.make_layer(torch.float32, path="tc1")
+    a, b = pair.forward(x), single.forward(x)
+    t = c1_tiled.forward(x) if T > 32 else a   # the tiled layer takes the GEMV at T = 32
+    torch.cuda.synchronize()
+    for L in (pair, single, c1_tiled):
+        L.check_device_error()
+    d = rel_l2(a.cpu().numpy(), b.cpu().numpy())
+    print(f"[cta pair vs single-CTA tiles T={T}] rel-L2 {d:.3e}, bit-identical {bool(torch.equal(a, b))}, "
+          f"tiled weights identical {bool(torch.equal(a, t))}")
+    assert d < 1e-6
+    assert torch.equal(a, t)
+    pair.close()
+    single.close()
+
+
 def test_c0_prefill_size_tcgen05_path(c0):
     """T=256 at C0 shapes: 64 tokens per routed expert on average, tcgen05 GEMM forced (C0's fp32
     activations would otherwise take the split-precision GEMV)."""

@@ -29,7 +29,7 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # weight formats
 WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED, WFMT_BF16 = 1, 2, 3, 4
 # expert kernel families (vfmoe_layer_desc.expert_path)
-PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV = 0, 1, 2, 3
+PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV, PATH_TC1 = 0, 1, 2, 3, 4
 # failure injection (vfmoe_debug_inject)
 INJECT_NONE, INJECT_STALL_LOADS = 0, 1
 ABI_VERSION = 3

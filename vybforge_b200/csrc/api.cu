@@ -86,7 +86,7 @@ Layer *get_layer(int64_t h) {
 // forces the tcgen05 or SIMT kernels).
 int layer_prec(const Layer &L) {
     return L.d.x_dtype == VFMOE_DT_F32 && L.d.weight_format != VFMOE_WFMT_EXL3 &&
-           L.d.expert_path != VFMOE_PATH_TC && L.d.expert_path != VFMOE_PATH_SIMT;
+           L.d.expert_path != VFMOE_PATH_TC && L.d.expert_path != VFMOE_PATH_TC1 && L.d.expert_path != VFMOE_PATH_SIMT;
 }
 
 WsLayout ws_layout(const Layer &L, int64_t T, int k) {
@@ -175,6 +175,7 @@ static int validate(const vfmoe_layer_desc &d) {
     if (d.n_local_experts < 0 || d.n_local_experts > 1024) return bad("n_local_experts out of range");
     if (d.topk > 32 || d.topk > d.n_experts) return bad("topk must be <= 32 and <= n_experts");
     if (d.x_dtype != VFMOE_DT_BF16 && d.x_dtype != VFMOE_DT_F32) return bad("x_dtype must be BF16 or F32");
+    if (d.expert_path < VFMOE_PATH_AUTO || d.expert_path > VFMOE_PATH_TC1) return bad("expert_path out of range");
     if (d.out_dtype != VFMOE_DT_BF16 && d.out_dtype != VFMOE_DT_F32) return bad("out_dtype must be BF16 or F32");
     if (!d.router_w || !d.router_bias) return bad("router weights missing");
     if (!aligned16(d.router_w)) return bad("router_w must be 16-byte aligned");

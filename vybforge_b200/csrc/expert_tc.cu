@@ -36,6 +36,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "expert_tc.h"
 #include "sm100.cuh"
@@ -476,6 +477,310 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_tc(const __grid_const
     if (warp == 2) tmem_dealloc(tmem, 512);
 }
 
+// ----------------------------------------------------------------------------- GEMM over CTA pairs
+// The same grouped GEMM with every work item spread over a cluster of two CTAs on two SMs
+// (tcgen05 cta_group::2).  A pair covers 256 output channels x N token rows: each CTA converts
+// and holds (TMEM) its own 128 weight rows and accumulators, and loads half of the token rows
+// (N / 2, shared memory); one thread of the even CTA issues every MMA with M = 256.  Each MMA and
+// each barrier operation of an issuer thus carries twice the work of the single-CTA kernel,
+// whose issuers' per-instruction cost was the limit (about 860 clocks per 64-K sub-stage where
+// the tensor pipe needs 512).  D column j is token j of the tile: the MMA takes B columns
+// [0, N/2) from the even CTA's shared memory and [N/2, N) from the odd CTA's.
+// Cross-CTA barriers (all in the even CTA unless noted): a sub-stage's "full" barrier counts both
+// CTAs' dequant warps and token-load bytes; the accumulator "empty" barrier counts both CTAs'
+// epilogue warps; the issuers' commits arrive on the "empty" and accumulator "full" barriers of
+// both CTAs (multicast commit).  Weight stages (raw_full / raw_empty) stay per CTA.  Every
+// mbarrier wait is bounded; the two cluster barriers (after set-up, before TMEM release) are
+// reached by every thread of both CTAs on every path.  No load uses multicast.
+template <bool GATEUP, int N>
+struct TcPairCfg {
+    static constexpr int MATS = GATEUP ? 2 : 1;
+    static constexpr int NH = N / 2;                // token rows per CTA and sub-stage
+    static constexpr int TOK_STAGE = NH * 128;
+    static constexpr int TOK_BYTES = kSlots * TOK_STAGE;
+    static constexpr int SW_FIT = (225000 - TOK_BYTES - 2048) / (MATS * kRawMat);
+    static constexpr int SW = SW_FIT > 5 ? 5 : SW_FIT;
+    static constexpr int RAW_BYTES = SW * MATS * kRawMat;
+    static constexpr int BAR_OFF = RAW_BYTES + TOK_BYTES;
+    static constexpr int NBAR = 2 * SW + 2 * kSlots + 3;
+    static constexpr int SMEM = BAR_OFF + NBAR * 8 + 16 + 1024;
+    static constexpr int ISSUERS = GATEUP ? 2 : 1;  // gate/up: one per matrix; down: one
+    static constexpr int D_COLS = MATS * N;
+    static constexpr int A_COL0 = D_COLS;
+    static_assert(N % 32 == 0 && N >= 32 && N <= 256, "pair MMA: N a multiple of 32 in [32, 256]");
+    static_assert(D_COLS + kSlots * MATS * 32 <= 512, "TMEM budget");
+    static_assert(SW >= 2, "at least two weight stages");
+    static_assert(TOK_STAGE % 1024 == 0 && (MATS * kRawMat) % 1024 == 0, "1024-byte aligned token stages");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <bool GATEUP, int N>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    expert_gemm_tc_pair(const __grid_constant__ TcParams p) {
+    using C = TcPairCfg<GATEUP, N>;
+    constexpr int MATS = C::MATS, SW = C::SW;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *raw = smem;
+    uint8_t *tok = smem + C::RAW_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *raw_full = bars, *raw_empty = bars + SW;
+    uint64_t *full = bars + 2 * SW, *empty = full + kSlots;
+    uint64_t *d_full = empty + kSlots, *d_empty = d_full + 1, *mma_done = d_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBAR);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cid = (int)cluster_id_x(), ncl = (int)cluster_count_x();
+    const int MT = p.M / 256;
+    const int KR = p.K / 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SW; ++i) {
+            mbar_init(&raw_full[i], MATS);
+            mbar_init(&raw_empty[i], kDqWarps);
+        }
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&full[i], 2 * (4 + 1));  // both CTAs: a dequant group's four warps + its token loads
+            mbar_init(&empty[i], C::ISSUERS);  // one commit per issuer (arrives in both CTAs)
+        }
+        mbar_init(d_full, C::ISSUERS);
+        mbar_init(d_empty, 2 * kDqWarps);      // both CTAs' epilogue warps
+        mbar_init(mma_done, C::ISSUERS);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.xt);
+        if (!p.tiled) {
+            prefetch_tmap(&p.wa);
+            prefetch_tmap(&p.swa);
+            if (GATEUP) {
+                prefetch_tmap(&p.wb);
+                prefetch_tmap(&p.swb);
+            }
+        }
+    }
+    if (warp == 2) {
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_items = (*p.n_tiles) * MT;
+    const uint32_t full0 = mapa_shared(full, 0);      // the even CTA's full[i] at full0 + 8 i
+    const uint32_t d_empty0 = mapa_shared(d_empty, 0);
+
+    if (warp == 0 || (GATEUP && warp == 3)) {
+        // ------------------------------------------------------------------ TMA producers: this CTA's weight rows
+        if (lane == 0) {
+            const int mat = warp == 0 ? 0 : 1;
+            uint32_t nraw = 0;
+            bool ok = true;
+            for (int item = cid; item < n_items && ok; item += ncl) {
+                const int4 t = p.tiles[item / MT];
+                const int m0 = (item % MT) * 256 + 128 * (int)rank;
+                const bool sh = t.x == p.E;
+                const CUtensorMap *mp = mat == 0 ? (sh ? &p.swa : &p.wa) : (sh ? &p.swb : &p.wb);
+                const int z = sh ? 0 : t.x;
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    const uint32_t rs = nraw % SW;
+                    if (!(ok = mbar_wait(&raw_empty[rs], ((nraw / SW) & 1) ^ 1, abort))) break;
+                    mbar_arrive_expect_tx(&raw_full[rs], kRawMat);
+                    uint8_t *dst = raw + rs * (MATS * kRawMat) + mat * kRawMat;
+                    if (p.tiled)
+                        load_q8_tiled(dst, mat == 0 ? (sh ? p.spa : p.pa) : (sh ? p.spb : p.pb), mat == 0 ? p.sa : p.sb,
+                                      z, m0, 128, KR, kr, &raw_full[rs]);
+                    else
+                        tma_load_3d(dst, mp, &raw_full[rs], kr * (kRawRow / 2), m0, z);
+                    ++nraw;
+                }
+            }
+            if (!ok) {
+                atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+                int dummy = 0;
+                for (uint32_t i = (nraw > (uint32_t)SW ? nraw - SW : 0); i < nraw; ++i)
+                    mbar_wait(&raw_full[i % SW], (i / SW) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    } else if (warp == 1 || (GATEUP && warp == 2)) {
+        // ------------------------------------------------------------------ MMA issuers (even CTA)
+        if (lane == 0 && rank == 0) {
+            const int mat = warp - 1;
+            uint32_t n = 0, it = 0;
+            bool ok = true;
+            for (int item = cid; item < n_items && ok; item += ncl, ++it) {
+                const int c_n = 32 * ((p.tiles[item / MT].z + 31) >> 5);  // <= N: the plan's tiles hold <= N rows
+                const uint32_t idesc = idesc_f16_f32(256, c_n);
+                if (!(ok = mbar_wait(d_empty, (it & 1) ^ 1, abort))) break;
+                tc_fence_after();
+                for (int kr = 0; kr < KR && ok; ++kr) {
+                    for (int s = 0; s < 4; ++s) {
+                        const uint32_t sl = n % kSlots;
+                        if (!(ok = mbar_wait(&full[sl], (n / kSlots) & 1, abort))) break;
+                        tc_fence_after();
+                        const uint32_t bsm = smem_u32(tok + sl * C::TOK_STAGE);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint32_t a_t = tmem + C::A_COL0 + (sl * MATS + mat) * 32 + 8 * j;
+                            mma_f16_ts_pair(tmem + mat * N, a_t, smem_desc_sw128(bsm + 32 * j), idesc,
+                                            (kr | s | j) != 0);
+                        }
+                        mma_commit_pair_both(&empty[sl]);
+                        ++n;
+                    }
+                }
+                if (ok) mma_commit_pair_both(d_full);
+            }
+            mma_commit_pair(mma_done);
+            int dummy = 0;
+            mbar_wait(mma_done, 0, (volatile int *)&dummy, 200000000ull);
+            if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------------ dequant + epilogue (both CTAs)
+        const int q = warp & 3;
+        const int grp = (warp - 4) >> 2;
+        const int r = 32 * q + lane;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t nraw = 0, n = 0, it = 0;
+        bool ok = true;
+        uint32_t tok_issued = 0;
+        auto epilogue = [&](int eitem, uint32_t eit) -> bool {
+            if (!mbar_wait(d_full, eit & 1, abort)) return false;
+            tc_fence_after();
+            const int4 t = p.tiles[eitem / MT];
+            const int ch = (eitem % MT) * 256 + 128 * (int)rank + r;
+            constexpr int NCH = (N + 31) / 32;
+            constexpr int G = GATEUP ? 1 : (NCH < 4 ? NCH : 4);
+#pragma unroll
+            for (int b0 = 0; b0 < NCH; b0 += G) {
+                uint32_t dg[G][8];
+                uint32_t du[GATEUP ? G : 1][8];
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        tmem_ld_32x32b_x8(tmem + lane_base + c0, dg[i]);
+                        if constexpr (GATEUP) tmem_ld_32x32b_x8(tmem + lane_base + N + c0, du[i]);
+                    }
+                }
+                tmem_wait_ld();
+                if (b0 + G >= NCH) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cl(d_empty0);
+                }
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    const int c0 = 8 * grp + 32 * (b0 + i);
+                    if (c0 < N && c0 < t.z) {
+                        if constexpr (GATEUP) {
+                            __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                if (c0 + j < t.z) {
+                                    const float a = swiglu_clamped_fast(__uint_as_float(dg[i][j]),
+                                                                       __uint_as_float(du[i][j]), p.limit);
+                                    out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __float2half_rn(a);
+                                }
+                            }
+                        } else {
+                            float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (c0 + j < t.z)
+                                    out[(int64_t)(t.y + c0 + j) * p.ld_out + ch] = __uint_as_float(dg[i][j]);
+                        }
+                    }
+                }
+            }
+            return true;
+        };
+        for (int item = cid; item < n_items && ok; item += ncl, ++it) {
+            const int4 tt = p.tiles[item / MT];
+            const int n32 = (tt.z + 31) >> 5;              // 16-row token boxes per CTA
+            const int y0 = tt.y + (int)rank * 16 * n32;    // this CTA's half of the token rows
+            for (int kr = 0; kr < KR && ok; ++kr) {
+                const uint32_t rs = nraw % SW;
+                if (!(ok = mbar_wait(&raw_full[rs], (nraw / SW) & 1, abort))) break;
+                const uint8_t *row = raw + rs * (MATS * kRawMat) + r * kRawRow;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    if (s == grp) {
+                        auto load_words = [&](int m, uint32_t (&w)[20]) {
+#pragma unroll
+                            for (int c = 0; c < 5; ++c) {
+                                const uint4 v4 =
+                                    *reinterpret_cast<const uint4 *>(row + m * kRawMat + 64 * s + 16 * c);
+                                w[4 * c] = v4.x;
+                                w[4 * c + 1] = v4.y;
+                                w[4 * c + 2] = v4.z;
+                                w[4 * c + 3] = v4.w;
+                            }
+                        };
+                        auto convert = [&](const uint32_t (&w)[20], uint32_t (&v)[32]) {
+                            uint32_t g[17];
+#pragma unroll
+                            for (int j = 0; j < 17; ++j) g[j] = w[s + j];
+                            q8_two_blocks(g, v);
+                        };
+                        uint32_t w0[20], w1[20], v[32];
+                        load_words(0, w0);
+                        if (GATEUP) load_words(1, w1);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                        convert(w0, v);
+                        const uint32_t sl = n % kSlots;
+                        if (!(ok = mbar_wait(&empty[sl], ((n / kSlots) & 1) ^ 1, abort))) break;
+                        if (q == 0) {
+                            // this CTA's token rows of the sub-stage, counted on the even CTA's barrier
+                            if (lane == 0) mbar_arrive_expect_tx_cl(full0 + 8 * sl, (uint32_t)n32 * 16 * 128);
+                            __syncwarp();
+                            if (lane < n32)
+                                tma_load_2d_pair(tok + sl * C::TOK_STAGE + lane * 2048, &p.xt, full0 + 8 * sl,
+                                                 kr * 256 + 64 * s, y0 + 16 * lane);
+                            tok_issued = n + 1;
+                        }
+                        const uint32_t tcol = tmem + lane_base + C::A_COL0 + sl * MATS * 32;
+                        tmem_st_32x32b_x32(tcol, v);
+                        if (GATEUP) {
+                            convert(w1, v);
+                            tmem_st_32x32b_x32(tcol + 32, v);
+                        }
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cl(full0 + 8 * sl);
+                    }
+                    ++n;
+                }
+                if (!ok) break;
+                ++nraw;
+                if (kr == 0 && it > 0 && !(ok = epilogue(item - ncl, it - 1))) break;
+            }
+        }
+        if (ok && it > 0) ok = epilogue(cid + (int)(it - 1) * ncl, it - 1);
+        if (!ok) {
+            atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);
+            // token loads in flight land before the pair releases its memory: the even CTA's
+            // barrier counts both CTAs' bytes (bounded: after an abort its phase may never complete)
+            if (rank == 0 && q == 0 && tok_issued > 0) {
+                int dummy = 0;
+                const uint32_t i = tok_issued - 1;
+                mbar_wait(&full[i % kSlots], (i / kSlots) & 1, (volatile int *)&dummy, 100000000ull);
+            }
+        }
+    }
+    tc_fence_before();
+    cluster_sync_all();  // every MMA of the pair complete and no cross-CTA access left
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc_pair(tmem, 512);
+}
+
 // ----------------------------------------------------------------------------- host
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -609,10 +914,57 @@ static int launch_one(const TcParams &prm, int grid, cudaStream_t st) {
     return VFMOE_OK;
 }
 
+// Grid of a CTA-pair launch: every pair resident at once (the kernel is persistent), as many as
+// the device holds with this kernel's shared memory; 0 if the query fails.
+template <bool GATEUP, int N>
+static int pair_grid() {
+    static std::mutex mu;
+    static int dev_cached = -1, grid_cached = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev == dev_cached) return grid_cached;
+    using C = TcPairCfg<GATEUP, N>;
+    if (set_smem_attr_once(reinterpret_cast<const void *>(expert_gemm_tc_pair<GATEUP, N>), C::SMEM)) return 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, reinterpret_cast<const void *>(expert_gemm_tc_pair<GATEUP, N>), &cfg) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        nc = 0;
+    }
+    dev_cached = dev;
+    grid_cached = 2 * nc;
+    return grid_cached;
+}
+
+template <bool GATEUP, int N>
+static int launch_pair(const TcParams &prm, cudaStream_t st, bool *launched) {
+    using C = TcPairCfg<GATEUP, N>;
+    *launched = false;
+    const int grid = pair_grid<GATEUP, N>();
+    if (grid < 2) return VFMOE_OK;  // the caller runs the single-CTA kernel
+    expert_gemm_tc_pair<GATEUP, N><<<grid, kThreads, C::SMEM, st>>>(prm);
+    VF_LAUNCH_CHECK(GATEUP ? "expert_gemm_tc_pair<gate_up>" : "expert_gemm_tc_pair<down>");
+    *launched = true;
+    return VFMOE_OK;
+}
+
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
     const int64_t rows = (int64_t)a.T * a.k + a.T;
     const bool decode = (double)a.T * a.k / a.E <= 16.0;
-    if (a.prec || plan.path == VFMOE_PATH_GEMV || (decode && plan.path != VFMOE_PATH_TC)) {
+    const bool forced_tc = plan.path == VFMOE_PATH_TC || plan.path == VFMOE_PATH_TC1;
+    if (a.prec || plan.path == VFMOE_PATH_GEMV || (decode && !forced_tc)) {
         // decode: register-operand GEMV, one token-tile size for both GEMMs (fp32 activations:
         // its split-precision form at every T)
         const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
@@ -659,13 +1011,27 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     g.limit = a.limit;
     g.err = a.err;
     const int grid = plan.num_sms;
-    switch (n_gu) {
-        case 16: rc = launch_one<true, 16>(g, grid, st); break;
-        case 32: rc = launch_one<true, 32>(g, grid, st); break;
-        case 64: rc = launch_one<true, 64>(g, grid, st); break;
-        default: rc = launch_one<true, 128>(g, grid, st); break;
+    // CTA pairs (M = 256 per MMA) whenever the tiles allow their N (a multiple of 32); single-CTA
+    // tiles for N = 16, when forced (VFMOE_PATH_TC1), or if the device holds no pair
+    const bool try_pair = n_gu >= 32 && plan.path != VFMOE_PATH_TC1;
+    bool paired = false;
+    if (try_pair) {
+        switch (n_gu) {
+            case 32: rc = launch_pair<true, 32>(g, st, &paired); break;
+            case 64: rc = launch_pair<true, 64>(g, st, &paired); break;
+            default: rc = launch_pair<true, 128>(g, st, &paired); break;
+        }
+        if (rc) return rc;
     }
-    if (rc) return rc;
+    if (!paired) {
+        switch (n_gu) {
+            case 16: rc = launch_one<true, 16>(g, grid, st); break;
+            case 32: rc = launch_one<true, 32>(g, grid, st); break;
+            case 64: rc = launch_one<true, 64>(g, grid, st); break;
+            default: rc = launch_one<true, 128>(g, grid, st); break;
+        }
+        if (rc) return rc;
+    }
     mid();
     TcParams dn{};
     dn.wa = plan.down;
@@ -686,6 +1052,16 @@ int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, con
     dn.out = a.y;
     dn.limit = a.limit;
     dn.err = a.err;
+    if (try_pair) {
+        bool dn_paired = false;
+        switch (n_dn) {
+            case 32: rc = launch_pair<false, 32>(dn, st, &dn_paired); break;
+            case 64: rc = launch_pair<false, 64>(dn, st, &dn_paired); break;
+            case 128: rc = launch_pair<false, 128>(dn, st, &dn_paired); break;
+            default: rc = launch_pair<false, 256>(dn, st, &dn_paired); break;
+        }
+        if (rc || dn_paired) return rc;
+    }
     switch (n_dn) {
         case 16: return launch_one<false, 16>(dn, grid, st);
         case 32: return launch_one<false, 32>(dn, grid, st);

@@ -1,5 +1,6 @@
-// Thin inline-PTX wrappers for the sm_100a features the expert GEMM uses:
-// mbarriers, TMA tensor loads (no multicast), tcgen05 TMEM alloc / st / ld / mma / commit.
+// Thin inline-PTX wrappers for the sm_100a features the expert GEMMs use:
+// mbarriers, TMA tensor loads (no multicast), tcgen05 TMEM alloc / st / ld / mma / commit, and
+// their two-CTA (cta_group::2) forms.
 #pragma once
 
 #include <cuda.h>
@@ -208,6 +209,106 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
     d |= (uint64_t)2 << 61;                           // layout: SWIZZLE_128B
     return d;
+}
+
+// ----------------------------------------------------------------------------- CTA pairs (cta_group::2)
+// A cluster of two CTAs on two SMs issues one tcgen05.mma over M = 256 rows: each CTA holds 128
+// rows of A (in its TMEM) and of D, and half of B's N columns (in its shared memory).  Only the
+// even CTA (rank 0) issues MMAs and commits.  No load here uses multicast.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory variable in CTA `rank` of the cluster (shared::cluster window).
+__device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+    return d;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes, wait for the peer's.  Not .aligned:
+// the lanes of a warp may arrive at different times.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Arrive on a barrier of either CTA of the pair (cl_addr: shared::cluster address).  Default
+// semantics, as the two-SM pipelines of CUTLASS use them: the data handed over is TMEM written
+// with tcgen05.st (ordered by tcgen05.wait::st and fence::before_thread_sync before the arrive,
+// fence::after_thread_sync after the wait) or shared memory written by TMA (complete_tx).
+__device__ __forceinline__ void mbar_arrive_cl(uint32_t cl_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cl(uint32_t cl_addr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(cl_addr), "r"(bytes) : "memory");
+}
+
+// 2D tensor load into this CTA's shared memory whose completion is counted on a barrier of
+// either CTA of the pair (cl_bar: a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t cl_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(cl_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// TMEM allocation for the pair: the same warp of both CTAs issues it; both get the same columns.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[tmem] x B[smem desc] over the pair: M = 256 (128 rows per CTA), kind::f16.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the barrier at this offset in both CTAs of the pair when every MMA this thread
+// issued has completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t *bar) {
+    const uint16_t mask = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(mask)
+        : "memory");
+}
+
+// The same, on this CTA's barrier only.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
 }
 
 }  // namespace sm100

@@ -21,9 +21,9 @@ import torch
 
 from . import _lib
 from ._lib import check, DT_BF16, DT_F16, DT_F32, WFMT_Q8_0, WFMT_EXL3, WFMT_Q8_0_TILED
-from ._lib import PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV
+from ._lib import PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV, PATH_TC1
 
-_PATHS = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC, "gemv": PATH_GEMV}
+_PATHS = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC, "gemv": PATH_GEMV, "tc1": PATH_TC1}
 
 _DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
 
@@ -60,7 +60,8 @@ class MoELayer:
     fmt="q8_0_tiled": the same tensors after ``q8_0_tile`` (stage-tiled byte order).
     EXL3 weights: each projection is a tuple (trellis int16 [E, K/16, N/16, 16*bits],
     suh fp16 [E, K], svh fp16 [E, N]); shared likewise without the leading E.
-    path: expert kernels, "auto" (default), "tc", "gemv" or "simt" (vfmoe_layer_desc.expert_path).
+    path: expert kernels, "auto" (default), "tc", "tc1" (tcgen05 with single-CTA tiles only), "gemv"
+        or "simt" (vfmoe_layer_desc.expert_path).
     shared_format="bf16": the shared expert is (gate, up, down) bf16 [out, in] matrices as a Hugging
     Face checkpoint stores them (GLM-5.3: EXL3 routed experts, bf16 shared expert).
     """
