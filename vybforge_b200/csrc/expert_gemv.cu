@@ -71,8 +71,10 @@ struct GvCfg {
     static constexpr int WB = DENSE ? (GATEUP ? 2 : 1) * 4 * WBOX : kWBytes;
     static constexpr int STAGE = WB + TOK;
     // epilogue exchange, fp32 [rows of the tile][N]: the second K half's partial sums, then (gate/up)
-    // the up rows for the SwiGLU
-    static constexpr int XCH = HALVES == 2 ? (GATEUP ? 2 : 1) * ROWS * N * 4 : (GATEUP ? ROWS * N * 4 : 0);
+    // the up rows for the SwiGLU.  With two halves it is double-buffered by item parity, so the
+    // second half starts its next item while the first writes this item's outputs.
+    static constexpr int XBUF = (GATEUP ? 2 : 1) * ROWS * N;  // floats per buffer
+    static constexpr int XCH = HALVES == 2 ? 2 * XBUF * 4 : (GATEUP ? ROWS * N * 4 : 0);
     static constexpr int SW = (230000 - XCH - 1024) / STAGE > 6 ? 6 : (230000 - XCH - 1024) / STAGE;
     static constexpr int SMEM = SW * STAGE + XCH + 2 * SW * 8 + 16 + 1024;
     static_assert(SW >= 2, "at least double buffering");
@@ -293,9 +295,9 @@ __global__ void __launch_bounds__(GvCfg<GATEUP, NT, PREC, DENSE>::THREADS, 1)
         const int mat = GATEUP ? (lw >> 2) : 0;
         const int r0 = GATEUP ? 16 * (lw & 3) : 16 * lw;      // first row of this warp in its matrix tile
         const int xrow0 = mat * ROWS + r0;                    // the warp's rows in the exchange buffer
-        uint32_t n = 0;
+        uint32_t n = 0, it = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
             const int4 t = tile_of(item);
             const int m0 = (item % MT) * ROWS;
             const int ntv = (t.z + 7) >> 3;                     // n8 tiles with valid token rows
@@ -379,14 +381,52 @@ __global__ void __launch_bounds__(GvCfg<GATEUP, NT, PREC, DENSE>::THREADS, 1)
             }
             // ---------------------------------------------------------------- epilogue
             // acc[j]: rows r0+g (0,1) and r0+g+8 (2,3) x tokens 8j+2c, 8j+2c+1
+            auto store_gate_up = [&](const float *xup) {
+                __half *out = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                        if (tok < t.z) {
+                            const float a = swiglu_clamped(acc[j][e], xup[rr * N + tok], p.limit);
+                            const int64_t o = (int64_t)(t.y + tok) * p.ld_out + m0 + rr;
+                            const __half ah = __float2half_rn(a);
+                            out[o] = ah;
+                            if (PREC) out[o + p.out_plane] = __float2half_rn((a - __half2float(ah)) * 4096.f);
+                        }
+                    }
+            };
+            auto store_down = [&]() {
+                float *out = reinterpret_cast<float *>(p.out);
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
+                        if (tok < t.z) out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = acc[j][e];
+                    }
+            };
+            auto put_up = [&](float *xup) {
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) xup[(r0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)] = acc[j][e];
+            };
             if constexpr (C::HALVES == 2) {
-                // the second K half hands its partial sums to the first through xch
+                // The second K half hands its partial sums to the first through this item's buffer
+                // (one barrier of all consumers) and goes on to its next item, which uses the other
+                // buffer; it can write this buffer again only after the next item's barrier, which
+                // the first half reaches after it has finished reading it.  Gate/up: the first
+                // half's up warps then pass their rows to its gate warps (a barrier of the first
+                // half only).
+                float *xb = xch + (it & 1) * C::XBUF;
                 if (half == 1) {
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
-                            xch[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)] = acc[j][e];
+                            xb[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)] = acc[j][e];
                 }
                 asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
                 if (half == 0) {
@@ -394,53 +434,25 @@ __global__ void __launch_bounds__(GvCfg<GATEUP, NT, PREC, DENSE>::THREADS, 1)
                     for (int j = 0; j < NT; ++j)
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
-                            acc[j][e] += xch[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)];
+                            acc[j][e] += xb[(xrow0 + g + 8 * (e >> 1)) * N + 8 * j + 2 * c + (e & 1)];
+                    if (GATEUP) {
+                        float *xup = xb + ROWS * N;  // each up warp overwrites only the rows it has just read
+                        if (mat == 1) put_up(xup);
+                        asm volatile("bar.sync 2, 256;" ::: "memory");
+                        if (mat == 0) store_gate_up(xup);
+                    } else {
+                        store_down();
+                    }
                 }
-            }
-            // up rows for the SwiGLU: with two halves each first-half warp overwrites only the
-            // xch entries it has just read (its own rows)
-            float *xup = xch + (C::HALVES == 2 ? ROWS * N : 0);
-            if (GATEUP) {
-                if (mat == 1 && half == 0) {
-#pragma unroll
-                    for (int j = 0; j < NT; ++j)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
-                            xup[rr * N + tok] = acc[j][e];
-                        }
-                }
-                asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
-                if (mat == 0 && half == 0) {
-                    __half *out = reinterpret_cast<__half *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < NT; ++j)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
-                            if (tok < t.z) {
-                                const float a = swiglu_clamped(acc[j][e], xup[rr * N + tok], p.limit);
-                                const int64_t o = (int64_t)(t.y + tok) * p.ld_out + m0 + rr;
-                                const __half ah = __float2half_rn(a);
-                                out[o] = ah;
-                                if (PREC) out[o + p.out_plane] = __float2half_rn((a - __half2float(ah)) * 4096.f);
-                            }
-                        }
-                }
-                asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
             } else {
-                if (half == 0) {
-                    float *out = reinterpret_cast<float *>(p.out);
-#pragma unroll
-                    for (int j = 0; j < NT; ++j)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int rr = r0 + g + 8 * (e >> 1), tok = 8 * j + 2 * c + (e & 1);
-                            if (tok < t.z) out[(int64_t)(t.y + tok) * p.ld_out + m0 + rr] = acc[j][e];
-                        }
+                if (GATEUP) {
+                    if (mat == 1) put_up(xch);
+                    asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
+                    if (mat == 0) store_gate_up(xch);
+                    asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
+                } else {
+                    store_down();
                 }
-                // xch is rewritten by the next item's second half only after this point
-                if constexpr (C::HALVES == 2) asm volatile("bar.sync 1, %0;" ::"r"(32 * CONS) : "memory");
             }
         }
         if (!ok) atomicCAS(p.err, 0, DEV_WAIT_TIMEOUT);

@@ -23,7 +23,6 @@
 
 #include "common.cuh"
 #include "kernels.h"
-#include "sm100.cuh"
 
 namespace vfmoe {
 
@@ -679,359 +678,6 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     }
 }
 
-// ----------------------------------------------------------------------------- L2 + L3, a cluster of CTAs per token
-// Decode batches (T <= kRefineSplitMaxT).  In router_refine a token's L2 level is two passes over
-// the candidates' rows of W_r, each two L2 round trips plus a block reduction: most of its
-// latency.  Here a cluster of kSplit CTAs serves one token.  Every CTA makes the same candidate
-// selection (the same inputs and code as router_refine), then reduces all candidates' float-float
-// dot products over its 1/kSplit of H, with the loads of a group of candidates in flight at once,
-// and stores its (hi, lo) partials into the leader CTA's shared memory.  After a cluster barrier
-// the leader adds the kSplit partials in rank order with TwoSum and runs the f64 ordering, the f64
-// level for close neighbours and the weights exactly as router_refine does.
-// Error of a candidate's L2 logit: a thread adds n = 4 F products; its lo adds the 2n TwoProduct
-// and TwoSum error terms; the warp butterfly (5 levels), the warps (7 additions) and the CTAs
-// (7 additions) add 45 TwoSum terms, each <= u S, and 38 additions of depth:
-// |err| <= gamma_{2n + 38} (n + 46) u S, S = sum |x_i w_i| <= |x| |w|.
-constexpr int kSplit = 8;
-constexpr int kRefineSplitMaxT = 64;
-constexpr int kSplitGroup = 8;  // candidates whose loads are in flight together
-
-__device__ __forceinline__ void st_cluster_f32(uint32_t cl_addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cl_addr), "f"(v) : "memory");
-}
-
-template <int NPL, int F>
-__global__ void __cluster_dims__(kSplit, 1, 1) __launch_bounds__(256) router_refine_split(
-    const void *__restrict__ x, int x_dtype, const float *__restrict__ wr, const float *__restrict__ logits,
-    int nchunk, const float *__restrict__ nw, const float *__restrict__ bias, int T, int H, int E, int k, float c1,
-    float c2, double scale, int32_t *__restrict__ idx_out, float *__restrict__ w_out, int32_t *__restrict__ counts,
-    int *__restrict__ err) {
-    __shared__ float s_red[8];
-    __shared__ int s_cand[kMaxCand];
-    __shared__ double s_logit[kMaxCand];   // L2/L3 logit, then the choice (score + bias) (leader)
-    __shared__ double s_score[kMaxCand];   // sigmoid(logit) (leader)
-    __shared__ int s_ncand, s_amb;
-    __shared__ __align__(16) float s_lo[32 * NPL];
-    __shared__ float s_tau;
-    __shared__ int s_wcnt[8];
-    __shared__ int s_order[kMaxCand];
-    __shared__ unsigned char s_redo[kMaxCand];
-    __shared__ float s_phi[8][kSplitGroup], s_plo[8][kSplitGroup];
-    __shared__ float s_part_hi[kMaxCand][kSplit], s_part_lo[kMaxCand][kSplit];  // leader: every CTA's partials
-    __shared__ double s_pd[8][8];
-    pdl_wait_then_release();
-    const uint32_t rank = sm100::cluster_ctarank();
-    const int t = (int)sm100::cluster_id_x();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hs = H / kSplit, h0 = (int)rank * hs;  // this CTA's slice of H (hs a multiple of 4)
-
-    // |x_t|_2 over the whole row (upper bound), and this CTA's slice of x_t in registers
-    float ss = 0.f;
-    for (int h = 4 * threadIdx.x; h < H; h += 1024) {
-        float v[4];
-        ld_x4(x, x_dtype, (int64_t)t * H + h, v);
-        ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
-    }
-    float xv[F][4];
-#pragma unroll
-    for (int q = 0; q < F; ++q) {
-        const int f = threadIdx.x + 256 * q;
-        if (4 * f < hs) {
-            ld_x4(x, x_dtype, (int64_t)t * H + h0 + 4 * f, xv[q]);
-        } else {
-            xv[q][0] = xv[q][1] = xv[q][2] = xv[q][3] = 0.f;
-        }
-    }
-    ss = warp_sum_f32(ss);
-    if (lane == 0) s_red[warp] = ss;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) tot += s_red[i];
-    const float nx = sqrtf(tot) * 1.001f;
-
-    // ---- candidate selection (router_refine's, step for step)
-    constexpr int EPT = (32 * NPL + 255) / 256;
-    float lo[EPT], hi[EPT];
-#pragma unroll
-    for (int i = 0; i < EPT; ++i) {
-        const int e = threadIdx.x + 256 * i;
-        lo[i] = hi[i] = -INFINITY;
-        if (e < E) {
-            float l = 0.f;
-            for (int c0 = 0; c0 < nchunk; c0 += 8) {
-                float pv[8];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) pv[c] = c0 + c < nchunk ? logits[((int64_t)(c0 + c) * T + t) * E + e] : 0.f;
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    if (c0 + c < nchunk) l += pv[c];
-            }
-            const float b1 = 0.25f * c1 * nx * nw[e] + 4e-6f;
-            float ca = 1.f / (1.f + expf(-l)) + bias[e];
-            if (isnan(ca)) ca = -INFINITY;
-            lo[i] = ca - b1;
-            hi[i] = ca + b1;
-        }
-        if (e < 32 * NPL) s_lo[e] = lo[i];
-    }
-    if (threadIdx.x == 0) {
-        s_amb = 0;
-        s_tau = -INFINITY;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < EPT; ++i) {
-        const int e = threadIdx.x + 256 * i;
-        if (e < E) {
-            const float4 *l4 = reinterpret_cast<const float4 *>(s_lo);
-            int rk = 0;
-            for (int o4 = 0; o4 < 8 * NPL; o4 += 8) {
-                float4 v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = l4[o4 + u];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int o = 4 * (o4 + u);
-                    rk += (v[u].x > lo[i] || (v[u].x == lo[i] && o < e)) ? 1 : 0;
-                    rk += (v[u].y > lo[i] || (v[u].y == lo[i] && o + 1 < e)) ? 1 : 0;
-                    rk += (v[u].z > lo[i] || (v[u].z == lo[i] && o + 2 < e)) ? 1 : 0;
-                    rk += (v[u].w > lo[i] || (v[u].w == lo[i] && o + 3 < e)) ? 1 : 0;
-                }
-            }
-            if (rk == k - 1) s_tau = lo[i];
-        }
-    }
-    __syncthreads();
-    const float tau = s_tau;
-    int nbase = 0;
-#pragma unroll
-    for (int i = 0; i < EPT; ++i) {
-        const int e = threadIdx.x + 256 * i;
-        const bool c = e < E && hi[i] >= tau;
-        const unsigned m = __ballot_sync(0xffffffffu, c);
-        if (lane == 0) s_wcnt[warp] = __popc(m);
-        __syncthreads();
-        int before = nbase, total = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            before += w < warp ? s_wcnt[w] : 0;
-            total += s_wcnt[w];
-        }
-        if (c) {
-            const int pos = before + __popc(m & ((1u << lane) - 1u));
-            if (pos < kMaxCand) s_cand[pos] = e;
-        }
-        nbase += total;
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-        int n = nbase;
-        if (n > kMaxCand) {
-            if (rank == 0) raise_dev_error(err, DEV_BAD_COUNT);
-            n = kMaxCand;
-        }
-        s_ncand = n;
-    }
-    __syncthreads();
-    const int nc = s_ncand;
-
-    // ---- this CTA's slice of every candidate's float-float logit, kSplitGroup candidates at a time
-    const uint32_t part_hi0 = sm100::mapa_shared(&s_part_hi[0][0], 0);
-    const uint32_t part_lo0 = sm100::mapa_shared(&s_part_lo[0][0], 0);
-    for (int c0 = 0; c0 < nc; c0 += kSplitGroup) {
-        float4 w4[kSplitGroup][F];
-#pragma unroll
-        for (int c = 0; c < kSplitGroup; ++c) {
-            const int e = c0 + c < nc ? s_cand[c0 + c] : -1;
-#pragma unroll
-            for (int q = 0; q < F; ++q) {
-                const int f = threadIdx.x + 256 * q;
-                w4[c][q] = (e >= 0 && 4 * f < hs) ? *reinterpret_cast<const float4 *>(wr + (int64_t)e * H + h0 + 4 * f)
-                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-        float shi[kSplitGroup], slo[kSplitGroup];
-#pragma unroll
-        for (int c = 0; c < kSplitGroup; ++c) {
-            float sh = 0.f, sl = 0.f;
-#pragma unroll
-            for (int q = 0; q < F; ++q) {
-                const float wv[4] = {w4[c][q].x, w4[c][q].y, w4[c][q].z, w4[c][q].w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float p = xv[q][i] * wv[i];
-                    const float pe = fmaf(xv[q][i], wv[i], -p);  // TwoProduct: x*w = p + pe exactly
-                    float sum, r;
-                    two_sum(sh, p, sum, r);
-                    sh = sum;
-                    sl = sl + (r + pe);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float oh = __shfl_xor_sync(0xffffffffu, sh, o);
-                const float ol = __shfl_xor_sync(0xffffffffu, sl, o);
-                float sum, r;
-                two_sum(sh, oh, sum, r);
-                sh = sum;
-                sl = sl + ol + r;
-            }
-            shi[c] = sh;
-            slo[c] = sl;
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int c = 0; c < kSplitGroup; ++c) {
-                s_phi[warp][c] = shi[c];
-                s_plo[warp][c] = slo[c];
-            }
-        }
-        __syncthreads();
-        if (threadIdx.x < kSplitGroup && c0 + threadIdx.x < nc) {
-            const int c = threadIdx.x;
-            float h = s_phi[0][c], l = s_plo[0][c];
-            for (int w = 1; w < 8; ++w) {
-                float sum, r;
-                two_sum(h, s_phi[w][c], sum, r);
-                h = sum;
-                l = l + s_plo[w][c] + r;
-            }
-            const uint32_t off = (uint32_t)(((c0 + c) * kSplit + (int)rank) * 4);
-            st_cluster_f32(part_hi0 + off, h);
-            st_cluster_f32(part_lo0 + off, l);
-        }
-        __syncthreads();
-    }
-    // every CTA's partials are in the leader's shared memory after this barrier; the other CTAs
-    // are done (nothing reads their shared memory afterwards)
-    sm100::cluster_sync_all();
-    if (rank != 0) return;
-
-    if (threadIdx.x < nc) {
-        const int c = threadIdx.x;
-        float h = s_part_hi[c][0], l = s_part_lo[c][0];
-        for (int r8 = 1; r8 < kSplit; ++r8) {
-            float sum, r;
-            two_sum(h, s_part_hi[c][r8], sum, r);
-            h = sum;
-            l = l + s_part_lo[c][r8] + r;
-        }
-        s_logit[c] = (double)h + (double)l;
-    }
-    __syncthreads();
-
-    // ---- order candidates in f64; flag neighbours closer than the L2 bound (warp 0)
-    if (warp == 0) {
-        for (int c = lane; c < nc; c += 32) {
-            const int e = s_cand[c];
-            const double sc = 1.0 / (1.0 + exp(-s_logit[c]));
-            s_score[c] = sc;
-            s_logit[c] = sc + (double)bias[e];
-            s_order[c] = -1;
-        }
-        __syncwarp();
-        for (int c = lane; c < nc; c += 32) {
-            const double ch = s_logit[c];
-            const int e = s_cand[c];
-            int rk = 0;
-            for (int o = 0; o < nc; ++o) {
-                const double oc = s_logit[o];
-                rk += (oc > ch || (oc == ch && s_cand[o] < e)) ? 1 : 0;
-            }
-            s_order[rk] = c;
-            s_redo[c] = 0;
-        }
-        __syncwarp();
-        for (int r = lane; r < k && r + 1 < nc; r += 32) {
-            const int a = s_order[r], b = s_order[r + 1];
-            if (a < 0 || b < 0) continue;
-            const double ba = 0.25 * (double)c2 * nx * nw[s_cand[a]], bb = 0.25 * (double)c2 * nx * nw[s_cand[b]];
-            if (s_logit[a] - s_logit[b] <= 2.0 * (ba + bb) + 1e-15) {
-                s_redo[a] = 1;
-                s_redo[b] = 1;
-                s_amb = 1;
-            }
-        }
-    }
-    __syncthreads();
-
-    // ---- L3: fp64 logits for ambiguous neighbours (rare), over the whole row
-    if (s_amb) {
-        for (int c0 = 0; c0 < nc; c0 += 8) {
-            double acc[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) acc[c] = 0.0;
-            for (int h = threadIdx.x * 4; h < H; h += 1024) {
-                float xq[4];
-                ld_x4(x, x_dtype, (int64_t)t * H + h, xq);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    if (c0 + c < nc && s_redo[c0 + c]) {
-                        const float4 w4 = *reinterpret_cast<const float4 *>(wr + (int64_t)s_cand[c0 + c] * H + h);
-                        acc[c] = fma((double)xq[0], (double)w4.x, acc[c]);
-                        acc[c] = fma((double)xq[1], (double)w4.y, acc[c]);
-                        acc[c] = fma((double)xq[2], (double)w4.z, acc[c]);
-                        acc[c] = fma((double)xq[3], (double)w4.w, acc[c]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const double v = warp_sum_f64(acc[c]);
-                if (lane == 0) s_pd[warp][c] = v;
-            }
-            __syncthreads();
-            if (threadIdx.x < 8 && c0 + threadIdx.x < nc && s_redo[c0 + threadIdx.x]) {
-                const int c = threadIdx.x;
-                double v = 0.0;
-                for (int w = 0; w < 8; ++w) v += s_pd[w][c];
-                const int e = s_cand[c0 + c];
-                const double sc = 1.0 / (1.0 + exp(-v));
-                s_score[c0 + c] = sc;
-                s_logit[c0 + c] = sc + (double)bias[e];
-            }
-            __syncthreads();
-        }
-        if (warp == 0) {
-            for (int c = lane; c < nc; c += 32) {
-                const double ch = s_logit[c];
-                const int e = s_cand[c];
-                int rk = 0;
-                for (int o = 0; o < nc; ++o) {
-                    const double oc = s_logit[o];
-                    rk += (oc > ch || (oc == ch && s_cand[o] < e)) ? 1 : 0;
-                }
-                s_order[rk] = c;
-            }
-        }
-        __syncthreads();
-    }
-
-    // ---- final top-k and weights (warp 0)
-    if (warp == 0) {
-        double sc = 0.0;
-        int e = -1;
-        if (lane < k && lane < nc) {
-            const int c = s_order[lane];
-            if (c >= 0) {
-                e = s_cand[c];
-                sc = s_score[c];
-            }
-        }
-        double sum = 0.0;
-        for (int r = 0; r < k; ++r) sum += __shfl_sync(0xffffffffu, sc, r);
-        if (lane < k) {
-            idx_out[(int64_t)t * k + lane] = e;
-            w_out[(int64_t)t * k + lane] = (float)(sc / (sum + 1e-20) * scale);
-            if (e >= 0 && e < E)
-                atomicAdd(&counts[e], 1);
-            else
-                raise_dev_error(err, DEV_BAD_EXPERT_ID);
-        }
-    }
-}
-
 // ----------------------------------------------------------------------------- L2 + L3, one warp per token
 // The same three levels as router_refine, for batches large enough to fill the GPU with one warp
 // per token (four tokens per CTA), so that no step waits on a block barrier:
@@ -1390,32 +1036,6 @@ int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat
     const int n2 = H / 256;
     const float c2 = gamma_bound(2 * n2 + 24) * (float)(n2 + 1 + 24) * 5.9604645e-8f;
     const int npl = (int)cdiv(E, 32);
-    const int hs = H / kSplit;
-    if (T <= kRefineSplitMaxT && npl <= 16 && H % (4 * kSplit) == 0 && hs <= 2048) {
-        const int F = hs <= 1024 ? 1 : 2;
-        const int nl = 4 * F;
-        const float c2s = gamma_bound(2 * nl + 38) * (float)(nl + 46) * 5.9604645e-8f;
-        const dim3 grid((unsigned)(T * kSplit));
-#define VF_REFINE_S(NPL, FF)                                                                                       \
-    VF_CUDA(launch_pdl(router_refine_split<NPL, FF>, grid, dim3(256), 0, st, x, x_dtype, wr, (const float *)logits,   \
-                       nchunk, nw, bias, T, H, E, k, c1, c2s, scale, idx, w, counts, err))
-        if (F == 1) {
-            if (npl <= 1) VF_REFINE_S(1, 1);
-            else if (npl <= 2) VF_REFINE_S(2, 1);
-            else if (npl <= 4) VF_REFINE_S(4, 1);
-            else if (npl <= 8) VF_REFINE_S(8, 1);
-            else VF_REFINE_S(16, 1);
-        } else {
-            if (npl <= 1) VF_REFINE_S(1, 2);
-            else if (npl <= 2) VF_REFINE_S(2, 2);
-            else if (npl <= 4) VF_REFINE_S(4, 2);
-            else if (npl <= 8) VF_REFINE_S(8, 2);
-            else VF_REFINE_S(16, 2);
-        }
-#undef VF_REFINE_S
-        VF_LAUNCH_CHECK("router_refine_split");
-        return VFMOE_OK;
-    }
     if (T >= kRefineWarpMinT && npl <= 16) {
         // One warp per token: a lane owns nl = 4 ceil(H / 128) terms; the 5-level lane butterfly adds
         // 31 TwoSum error terms (each <= u S) and 10 fp32 additions of depth to lo's summation:
