@@ -559,6 +559,51 @@ def stack_extra(a, rank, world, local_rank, flush):
     return out
 
 
+def hc_extra(a, flush):
+    """The hyper-connection kernels around the MoE (vfmoe_hc_mix with the fused post-attention
+    RMSNorm, vfmoe_hc_apply) at the C3 token count: R = 4096 rows of 4 fp32 streams, H = 6144, bf16
+    hc_fn and h.  HBM-bound: mix moves 16 H + 2 H bytes per row (streams in, h out), apply 16 H + 2 H
+    + 16 H (streams and y in, streams out)."""
+    import torch
+    from vybforge_b200.moe import HyperConnection
+    try:
+        R, D = 4096, 6144
+        g = torch.Generator(device="cuda").manual_seed(5)
+        fn = (torch.randn((24, 4 * D), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        base = torch.randn(24, generator=g, device="cuda") * 0.5
+        scale = torch.tensor([0.8, 1.3, 2.0], device="cuda")
+        norm_w = 1 + 0.02 * torch.randn(D, generator=g, device="cuda")
+        site = HyperConnection(fn, base, scale, norm_w)
+        streams = torch.randn((R, 4, D), generator=g, device="cuda")
+        out = torch.empty_like(streams)
+        st = torch.cuda.current_stream()
+        h, post, comb = site.mix(streams)
+        site.apply(streams, h, post, comb, out=out)
+        torch.cuda.synchronize()
+        times = {"mix": [], "apply": []}
+        for _ in range(max(3, a.steps // 2)):
+            for name in ("mix", "apply"):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                if name == "mix":
+                    site.mix(streams)
+                else:
+                    site.apply(streams, h, post, comb, out=out)
+                e1.record(st)
+                torch.cuda.synchronize()
+                times[name].append(e0.elapsed_time(e1))
+        pk, pk_kind = peaks()
+        res = {}
+        for name, nbytes in (("mix", 18.0 * D * R), ("apply", 34.0 * D * R)):
+            ms = float(np.mean(times[name]))
+            res[name] = {"ms": round(ms, 4), "hbm_bytes": nbytes, "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+        return {"hc_site_c3": {"workload": "hyper-connection mix (+ RMSNorm) and apply, R=4096 rows x 4 fp32 streams, H=6144",
+                               "peak_source": pk_kind, **res}}
+    except Exception as e:  # an extra must not cost the headline line
+        return {"hc_site_c3": {"error": str(e)[:300]}}
+
+
 def exl3_extra(a, flush):
     """C2 (decode T=32 and T=1) and C3 with EXL3 3-bpw weights (prefill T=4096, Zipf(1.1)),
     on one GPU: the same layer shapes as C1."""
@@ -861,6 +906,8 @@ def run_ours(a, rank, world, local_rank):
         res.update(stack_extra(a, rank, world, local_rank, flush))
         torch.cuda.empty_cache()
         res.update(exl3_extra(a, flush))
+        torch.cuda.empty_cache()
+        res.update(hc_extra(a, flush))
     return res
 
 

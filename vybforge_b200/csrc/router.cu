@@ -84,6 +84,16 @@ __device__ __forceinline__ void ld_x4(const void *x, int x_dtype, int64_t off, f
     }
 }
 
+// Unsigned keys that order floats as their values (-0 below +0); the inverse.  Selection keys put
+// the key in the high word and ~expert id in the low word: ties by value go to the lowest id.
+__device__ __forceinline__ uint32_t f32_order_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float f32_from_order_key(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
 // ----------------------------------------------------------------------------- L1, decode
 // T <= 32: CTA = 16 experts x one K chunk of KCH (768 or 512) x TB tokens (grid z: token groups
 // t0 = TB z, so each thread keeps 2 x TB accumulators and several CTAs fit an SM); x[t0..t0+TB)
@@ -334,7 +344,7 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     __shared__ double s_logit[kMaxCand];   // L2/L3 logit, then the choice (score + bias)
     __shared__ double s_score[kMaxCand];   // sigmoid(logit)
     __shared__ int s_ncand, s_amb;
-    __shared__ __align__(16) float s_lo[32 * NPL];  // lower bounds of every expert's choice (-inf past E)
+    __shared__ uint64_t s_keys[8 * 32];             // every warp's k largest keys (orderable lo, ~id)
     __shared__ float s_tau;
     __shared__ int s_wcnt[8];
     __shared__ int s_order[kMaxCand];
@@ -398,8 +408,10 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
 
     // ---- L2 candidate selection, all threads: thread i owns experts i, i + 256, ...
     // lo/hi = choice -/+ the L1 bound.  tau = the k-th largest lo in the order (lo desc, id
-    // asc): the expert whose rank is k - 1.  Candidates = experts with hi >= tau, compacted in
-    // ascending id order.  All partial loads of a thread are issued before they are summed.
+    // asc): every warp finds its k largest 64-bit keys (orderable lo, ~id) in k rounds of a
+    // warp-wide max, and warp 0 takes the k-th largest of those 8 k keys.  Candidates = experts
+    // with hi >= tau, compacted in ascending id order.  All partial loads of a thread are issued
+    // before they are summed.
     constexpr int EPT = (32 * NPL + 255) / 256;  // experts per thread
     float lo[EPT], hi[EPT];
 #pragma unroll
@@ -422,34 +434,62 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
             lo[i] = ca - b1;
             hi[i] = ca + b1;
         }
-        if (e < 32 * NPL) s_lo[e] = lo[i];  // -inf past E: never ranked above a real expert
     }
-    if (threadIdx.x == 0) {
-        s_amb = 0;
-        s_tau = -INFINITY;  // kept if no rank k - 1 exists (non-finite bounds): every expert is then a candidate
-    }
-    __syncthreads();
+    {
+        uint64_t key[EPT];
+        bool bad = false;
 #pragma unroll
-    for (int i = 0; i < EPT; ++i) {
-        const int e = threadIdx.x + 256 * i;
-        if (e < E) {
-            // broadcast float4 reads, 8 in flight per step
-            const float4 *l4 = reinterpret_cast<const float4 *>(s_lo);
-            int rank = 0;
-            for (int o4 = 0; o4 < 8 * NPL; o4 += 8) {
-                float4 v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = l4[o4 + u];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int o = 4 * (o4 + u);
-                    rank += (v[u].x > lo[i] || (v[u].x == lo[i] && o < e)) ? 1 : 0;
-                    rank += (v[u].y > lo[i] || (v[u].y == lo[i] && o + 1 < e)) ? 1 : 0;
-                    rank += (v[u].z > lo[i] || (v[u].z == lo[i] && o + 2 < e)) ? 1 : 0;
-                    rank += (v[u].w > lo[i] || (v[u].w == lo[i] && o + 3 < e)) ? 1 : 0;
-                }
+        for (int i = 0; i < EPT; ++i) {
+            const int e = threadIdx.x + 256 * i;
+            key[i] = 0ull;  // below every real expert's key
+            if (e < E) {
+                key[i] = ((uint64_t)f32_order_key(lo[i]) << 32) | (uint64_t)(~(uint32_t)e);
+                bad |= isnan(lo[i]);
             }
-            if (rank == k - 1) s_tau = lo[i];
+        }
+        for (int r = 0; r < k; ++r) {
+            uint64_t m = 0ull;
+#pragma unroll
+            for (int i = 0; i < EPT; ++i) m = key[i] > m ? key[i] : m;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t v = __shfl_xor_sync(0xffffffffu, m, o);
+                m = v > m ? v : m;
+            }
+#pragma unroll
+            for (int i = 0; i < EPT; ++i)
+                if (m != 0ull && key[i] == m) key[i] = 0ull;
+            if (lane == 0) s_keys[warp * 32 + r] = m;
+        }
+        const int nbad = __syncthreads_count(bad);
+        if (warp == 0) {
+            // the k-th largest of the 8 warps' k keys each (lane l holds keys l, l + 32, ...)
+            uint64_t kk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int w2 = i, r = lane;
+                kk[i] = r < k ? s_keys[w2 * 32 + r] : 0ull;
+            }
+            uint64_t kth = 0ull;
+            for (int r = 0; r < k; ++r) {
+                uint64_t m = 0ull;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) m = kk[i] > m ? kk[i] : m;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const uint64_t v = __shfl_xor_sync(0xffffffffu, m, o);
+                    m = v > m ? v : m;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (m != 0ull && kk[i] == m) kk[i] = 0ull;
+                kth = m;
+            }
+            if (lane == 0) {
+                s_amb = 0;
+                // no k-th expert, or a NaN bound somewhere: every expert is a candidate
+                s_tau = (kth == 0ull || nbad) ? -INFINITY : f32_from_order_key((uint32_t)(kth >> 32));
+            }
         }
     }
     __syncthreads();
@@ -692,13 +732,6 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
 // scores live in the warp's slice of shared memory.
 constexpr int kRwWarps = 4;
 
-__device__ __forceinline__ uint32_t f32_order_key(float f) {
-    const uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float f32_from_order_key(uint32_t key) {
-    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
-}
 
 template <int NPL>
 __global__ void __launch_bounds__(32 * kRwWarps) router_refine_warp(
