@@ -19,7 +19,9 @@
 // hc_mix_kernel: one CTA (512 threads) per row, the whole mix fused.  Thread t holds the four
 // streams' values at d = 4t + 2048q (q < D/2048) in registers, so the collapse and both norms
 // need no exchange beyond two block reductions; fn (bf16 or fp32 [24][HC*D]) is read once per
-// row (L2-resident across rows).  The 4x4 normalisation runs in fp64 on one thread.
+// row (L2-resident across rows).  Per-thread partial sums are fp32; the block reductions are
+// float-float.  The gates and the 4x4 normalisation run in fp32 on warp 0, one matrix entry per
+// lane (row and column sums by shuffles).
 // hc_apply_kernel: streaming, HBM-bound (HC*D reads + D reads + HC*D writes per row).
 #include "common.cuh"
 #include "kernels.h"
@@ -39,21 +41,43 @@ __device__ __forceinline__ float4 ld_fn4(const void *fn, int fn_dtype, int64_t i
     return *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(fn) + i);
 }
 
-// Block-wide sum of NV doubles per thread (512 threads); every thread gets the totals.
+// Block-wide sums of NV fp32 values per thread (512 threads), in float-float: a TwoSum butterfly
+// per warp, then threads 0..NV-1 add the 16 warps' (hi, lo) pairs in warp order; the totals
+// (hi + lo, about 48 bits) land in out[] (shared memory) for every thread to read.  All of it runs on the fp32
+// pipe: fp64 arithmetic on this part issues at a small fraction of the fp32 rate.
+__device__ __forceinline__ void two_sum_f(float a, float b, float &s, float &t) {
+    s = a + b;
+    const float bb = s - a;
+    t = (a - (s - bb)) + (b - bb);
+}
+
 template <int NV>
-__device__ __forceinline__ void block_sum(double (&v)[NV], double *red /* [16][NV] */) {
+__device__ __forceinline__ void block_sum(const float (&v)[NV], float2 *red /* [16][NV] */, double *out /* [NV] */) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = warp_sum_f64(v[i]);
-    if (lane == 0)
-#pragma unroll
-        for (int i = 0; i < NV; ++i) red[warp * NV + i] = v[i];
-    __syncthreads();
-#pragma unroll
     for (int i = 0; i < NV; ++i) {
-        double s = 0.0;
-        for (int w = 0; w < kHcThreads / 32; ++w) s += red[w * NV + i];
-        v[i] = s;
+        float hi = v[i], lo = 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oh = __shfl_xor_sync(0xffffffffu, hi, o), ol = __shfl_xor_sync(0xffffffffu, lo, o);
+            float sm, r;
+            two_sum_f(hi, oh, sm, r);
+            hi = sm;
+            lo = lo + ol + r;
+        }
+        if (lane == 0) red[warp * NV + i] = make_float2(hi, lo);
+    }
+    __syncthreads();
+    if (threadIdx.x < NV) {
+        const int i = threadIdx.x;
+        float hi = red[i].x, lo = red[i].y;
+        for (int w = 1; w < kHcThreads / 32; ++w) {
+            float sm, r;
+            two_sum_f(hi, red[w * NV + i].x, sm, r);
+            hi = sm;
+            lo = lo + red[w * NV + i].y + r;
+        }
+        out[i] = (double)hi + (double)lo;
     }
     __syncthreads();
 }
@@ -66,7 +90,8 @@ __global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(const float *__restr
                                                             const float *__restrict__ norm_w, float norm_eps,
                                                             void *__restrict__ h_out, int h_dtype,
                                                             float *__restrict__ post_out, float *__restrict__ comb_out) {
-    __shared__ double red[16 * (kHcMix + 1)];
+    __shared__ float2 red[16 * (kHcMix + 1)];
+    __shared__ double s_tot[kHcMix + 1];
     __shared__ float s_pre[kHc];
     const int64_t r = blockIdx.x;
     const int t = threadIdx.x;
@@ -82,7 +107,7 @@ __global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(const float *__restr
         }
     // mix values of the raw row (the 1/rms factor is applied to the totals); per-thread partial
     // sums in fp32 (64 VPT products), the block reduction in fp64
-    double acc[kHcMix + 1];
+    float part[kHcMix + 1];
 #pragma unroll
     for (int j = 0; j < kHcMix; ++j) {
         float a = 0.f;
@@ -96,52 +121,52 @@ __global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(const float *__restr
                 a = fmaf(x[h][q].z, f.z, a);
                 a = fmaf(x[h][q].w, f.w, a);
             }
-        acc[j] = a;
+        part[j] = a;
     }
-    acc[kHcMix] = ss;
-    block_sum<kHcMix + 1>(acc, red);
-    const double inv = 1.0 / sqrt(acc[kHcMix] / (double)(kHc * D) + (double)rms_eps);
-    if (t == 0) {
-        double pre[kHc], post[kHc], c[kHc][kHc];
-        const double s0 = scale[0], s1 = scale[1], s2 = scale[2];
-        for (int h = 0; h < kHc; ++h) {
-            pre[h] = 1.0 / (1.0 + exp(-(acc[h] * inv * s0 + base[h]))) + hc_eps;
-            post[h] = 2.0 / (1.0 + exp(-(acc[kHc + h] * inv * s1 + base[kHc + h])));
-        }
-        for (int a = 0; a < kHc; ++a) {
-            double mx = -1e300;
-            for (int b = 0; b < kHc; ++b) {
-                c[a][b] = acc[2 * kHc + a * kHc + b] * inv * s2 + base[2 * kHc + a * kHc + b];
-                mx = fmax(mx, c[a][b]);
-            }
-            double sm = 0.0;
-            for (int b = 0; b < kHc; ++b) sm += (c[a][b] = exp(c[a][b] - mx));
-            for (int b = 0; b < kHc; ++b) c[a][b] = c[a][b] / sm + hc_eps;
-        }
+    part[kHcMix] = ss;
+    block_sum<kHcMix + 1>(part, red, s_tot);
+    if (t < 32) {
+        // warp 0: lane 4a + b holds comb[a][b] (rows: shuffles over lane bits 0-1, columns: bits
+        // 2-3); lanes 16-19 pre[h], lanes 20-23 post[h].  fp32 from the float-float totals: the
+        // 20 normalisation rounds add about 20 roundings of 2^-24 each.
+        const int lane = t;
+        const float inv = (float)(1.0 / sqrt(s_tot[kHcMix] / (double)(kHc * D) + (double)rms_eps));
+        const float s0 = scale[0], s1 = scale[1], s2 = scale[2];
+        const float eps = (float)hc_eps;
+        const int a = (lane >> 2) & 3, b = lane & 3;
+        float c = (float)s_tot[2 * kHc + a * kHc + b] * inv * s2 + base[2 * kHc + a * kHc + b];
+        float mx = c;
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        c = expf(c - mx);
+        float sm = c + __shfl_xor_sync(0xffffffffu, c, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        c = c / sm + eps;
         for (int it = 0; it < iters; ++it) {
-            if (it > 0)
-                for (int a = 0; a < kHc; ++a) {
-                    double sm = 0.0;
-                    for (int b = 0; b < kHc; ++b) sm += c[a][b];
-                    for (int b = 0; b < kHc; ++b) c[a][b] /= sm + hc_eps;
-                }
-            for (int b = 0; b < kHc; ++b) {
-                double sm = 0.0;
-                for (int a = 0; a < kHc; ++a) sm += c[a][b];
-                for (int a = 0; a < kHc; ++a) c[a][b] /= sm + hc_eps;
+            if (it > 0) {
+                float rs = c + __shfl_xor_sync(0xffffffffu, c, 1);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+                c /= rs + eps;
             }
+            float cs = c + __shfl_xor_sync(0xffffffffu, c, 4);
+            cs += __shfl_xor_sync(0xffffffffu, cs, 8);
+            c /= cs + eps;
         }
-        for (int h = 0; h < kHc; ++h) {
-            s_pre[h] = (float)pre[h];
-            post_out[r * kHc + h] = (float)post[h];
+        const int h = lane & 3;
+        const float zp = (float)s_tot[h] * inv * s0 + base[h];
+        const float zq = (float)s_tot[kHc + h] * inv * s1 + base[kHc + h];
+        if (lane < 16) {
+            comb_out[(r * kHc + a) * kHc + b] = c;
+        } else if (lane < 20) {
+            s_pre[h] = 1.f / (1.f + expf(-zp)) + eps;
+        } else if (lane < 24) {
+            post_out[r * kHc + h] = 2.f / (1.f + expf(-zq));
         }
-        for (int a = 0; a < kHc; ++a)
-            for (int b = 0; b < kHc; ++b) comb_out[(r * kHc + a) * kHc + b] = (float)c[a][b];
     }
     __syncthreads();
     // collapse, then the weighted RMSNorm over D
     float4 col[VPT];
-    double ss2[1] = {0.0};
+    float ss2[1] = {0.f};
 #pragma unroll
     for (int q = 0; q < VPT; ++q) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -154,12 +179,14 @@ __global__ void __launch_bounds__(kHcThreads) hc_mix_kernel(const float *__restr
             v.w = fmaf(p, x[h][q].w, v.w);
         }
         col[q] = v;
-        ss2[0] += (double)(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        ss2[0] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     float inv2 = 1.f;
     if (norm_w) {
-        block_sum<1>(ss2, red);
-        inv2 = (float)(1.0 / sqrt(ss2[0] / (double)D + (double)norm_eps));
+        block_sum<1>(ss2, red, s_tot);
+        if (t == 0) s_pre[0] = (float)(1.0 / sqrt(s_tot[0] / (double)D + (double)norm_eps));  // s_pre is free now
+        __syncthreads();
+        inv2 = s_pre[0];
     }
 #pragma unroll
     for (int q = 0; q < VPT; ++q) {
