@@ -48,11 +48,13 @@ def test_hc_matches_reference_golden():
     assert d_col < 1e-6 and d_out < 1e-6
 
 
-@pytest.mark.parametrize("D,fn_bf16", [(4096, True), (6144, True), (2048, False), (8192, True)])
-def test_hc_mix_and_apply_match_oracle(D, fn_bf16):
+@pytest.mark.parametrize("D,fn_bf16,R", [(4096, True, 37), (6144, True, 37), (2048, False, 37), (8192, True, 37),
+                                          (6144, True, 1030), (2048, False, 1030)])
+def test_hc_mix_and_apply_match_oracle(D, fn_bf16, R):
+    """R = 37 takes the one-row-per-CTA mix, R = 1030 the four-rows-per-CTA one (with a partial
+    last block)."""
     moe.init(0)
-    rng = np.random.default_rng(D)
-    R = 37
+    rng = np.random.default_rng(D + R)
     streams = (rng.standard_normal((R, 4, D)) * rng.uniform(0.2, 3.0, (R, 4, 1))).astype(np.float32)
     fn = (rng.standard_normal((24, 4 * D)) * 0.02).astype(np.float32)
     if fn_bf16:
@@ -83,7 +85,7 @@ def test_hc_mix_and_apply_match_oracle(D, fn_bf16):
     inplace = sd.clone()
     site.apply(inplace, yd, post, comb, out=inplace)
     torch.cuda.synchronize()
-    print(f"[hc D={D} fn {'bf16' if fn_bf16 else 'f32'}] h fp32 {d32:.2e}, h bf16 {d16:.2e}, apply {d_out:.2e}")
+    print(f"[hc D={D} R={R} fn {'bf16' if fn_bf16 else 'f32'}] h fp32 {d32:.2e}, h bf16 {d16:.2e}, apply {d_out:.2e}")
     assert d32 < 1e-5 and d16 < 4e-3 and d_out < 1e-6
     assert torch.equal(inplace, out)
 

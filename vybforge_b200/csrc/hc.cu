@@ -233,10 +233,205 @@ __global__ void __launch_bounds__(256) hc_apply_kernel(const float *__restrict__
     }
 }
 
+// hc_mix_rows_kernel: the same mix for large batches, kHcRows rows per CTA (256 threads, two CTAs
+// per SM), so that every hc_fn load serves kHcRows rows (hc_mix_kernel reads all of hc_fn, 24 x 4D
+// values, once per row).  Thread t owns float4 chunks g = t + 256 i of the flattened 4 x D row and
+// keeps kHcRows x 25 partial sums; the collapse then re-reads the block's rows (L2-resident)
+// twice: for the RMSNorm's sum of squares, then for the output.  R = 4096, H = 6144: 0.51 ms
+// (one row per CTA: 0.61 ms; four rows per CTA at 255 registers, one CTA per SM: 0.59 ms).  Both
+// forms wait on the 24 hc_fn loads of every chunk (L2 latency), not on HBM.
+constexpr int kHcRows = 2;
+constexpr int64_t kHcRowsMinR = 1024;  // below this, one row per CTA keeps more SMs busy
+
+// The gates and the 4x4 normalisation of one row on one warp (fp32; lane 4a + b holds comb[a][b]).
+__device__ __forceinline__ void hc_tail_warp(const double *tot /* 25 */, int D, const float *base, const float *scale,
+                                             float rms_eps, double hc_eps, int iters, int64_t r, bool valid,
+                                             float *post_out, float *comb_out, float *pre_smem) {
+    const int lane = threadIdx.x & 31;
+    const float inv = (float)(1.0 / sqrt(tot[kHcMix] / (double)(kHc * D) + (double)rms_eps));
+    const float s0 = scale[0], s1 = scale[1], s2 = scale[2];
+    const float eps = (float)hc_eps;
+    const int a = (lane >> 2) & 3, b = lane & 3;
+    float c = (float)tot[2 * kHc + a * kHc + b] * inv * s2 + base[2 * kHc + a * kHc + b];
+    float mx = c;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    c = expf(c - mx);
+    float sm = c + __shfl_xor_sync(0xffffffffu, c, 1);
+    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+    c = c / sm + eps;
+    for (int it = 0; it < iters; ++it) {
+        if (it > 0) {
+            float rs = c + __shfl_xor_sync(0xffffffffu, c, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            c /= rs + eps;
+        }
+        float cs = c + __shfl_xor_sync(0xffffffffu, c, 4);
+        cs += __shfl_xor_sync(0xffffffffu, cs, 8);
+        c /= cs + eps;
+    }
+    const int h = lane & 3;
+    const float zp = (float)tot[h] * inv * s0 + base[h];
+    const float zq = (float)tot[kHc + h] * inv * s1 + base[kHc + h];
+    if (lane < 16) {
+        if (valid) comb_out[(r * kHc + a) * kHc + b] = c;
+    } else if (lane < 20) {
+        pre_smem[h] = 1.f / (1.f + expf(-zp)) + eps;
+    } else if (lane < 24) {
+        if (valid) post_out[r * kHc + h] = 2.f / (1.f + expf(-zq));
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) hc_mix_rows_kernel(const float *__restrict__ streams, int64_t R, int D,
+                                                          const void *__restrict__ fn, int fn_dtype,
+                                                          const float *__restrict__ base, const float *__restrict__ scale,
+                                                          float rms_eps, double hc_eps, int iters,
+                                                          const float *__restrict__ norm_w, float norm_eps,
+                                                          void *__restrict__ h_out, int h_dtype,
+                                                          float *__restrict__ post_out, float *__restrict__ comb_out) {
+    constexpr int NV = kHcRows * (kHcMix + 1);
+    __shared__ float2 red[8 * NV];
+    __shared__ double s_tot[NV];
+    __shared__ float s_pre[kHcRows][kHc];
+    __shared__ float s_inv2[kHcRows];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int64_t r0 = (int64_t)blockIdx.x * kHcRows;
+    const int nch = kHc * D / 4;  // float4 chunks of a row
+    float part[kHcRows][kHcMix + 1];
+#pragma unroll
+    for (int rb = 0; rb < kHcRows; ++rb)
+#pragma unroll
+        for (int j = 0; j <= kHcMix; ++j) part[rb][j] = 0.f;
+    for (int g = t; g < nch; g += 256) {
+        float4 xv[kHcRows];
+#pragma unroll
+        for (int rb = 0; rb < kHcRows; ++rb) {
+            xv[rb] = r0 + rb < R ? *reinterpret_cast<const float4 *>(streams + (r0 + rb) * kHc * D + 4 * (int64_t)g)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            part[rb][kHcMix] += xv[rb].x * xv[rb].x + xv[rb].y * xv[rb].y + xv[rb].z * xv[rb].z + xv[rb].w * xv[rb].w;
+        }
+#pragma unroll
+        for (int j = 0; j < kHcMix; ++j) {
+            const float4 f = ld_fn4(fn, fn_dtype, (int64_t)j * kHc * D + 4 * (int64_t)g);
+#pragma unroll
+            for (int rb = 0; rb < kHcRows; ++rb) {
+                float a = part[rb][j];
+                a = fmaf(xv[rb].x, f.x, a);
+                a = fmaf(xv[rb].y, f.y, a);
+                a = fmaf(xv[rb].z, f.z, a);
+                a = fmaf(xv[rb].w, f.w, a);
+                part[rb][j] = a;
+            }
+        }
+    }
+    // float-float block sums of the kHcRows x 25 values (8 warps)
+#pragma unroll
+    for (int rb = 0; rb < kHcRows; ++rb)
+#pragma unroll
+        for (int j = 0; j <= kHcMix; ++j) {
+            float hi = part[rb][j], lo = 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oh = __shfl_xor_sync(0xffffffffu, hi, o), ol = __shfl_xor_sync(0xffffffffu, lo, o);
+                float sm, rr;
+                two_sum_f(hi, oh, sm, rr);
+                hi = sm;
+                lo = lo + ol + rr;
+            }
+            if (lane == 0) red[warp * NV + rb * (kHcMix + 1) + j] = make_float2(hi, lo);
+        }
+    __syncthreads();
+    if (t < NV) {
+        float hi = red[t].x, lo = red[t].y;
+        for (int w = 1; w < 8; ++w) {
+            float sm, rr;
+            two_sum_f(hi, red[w * NV + t].x, sm, rr);
+            hi = sm;
+            lo = lo + red[w * NV + t].y + rr;
+        }
+        s_tot[t] = (double)hi + (double)lo;
+    }
+    __syncthreads();
+    if (warp < kHcRows)
+        hc_tail_warp(s_tot + warp * (kHcMix + 1), D, base, scale, rms_eps, hc_eps, iters, r0 + warp, r0 + warp < R,
+                     post_out, comb_out, s_pre[warp]);
+    __syncthreads();
+    // collapse: sum of squares per row (first pass), then the normalised output (second pass)
+    auto collapsed = [&](int rb, int d) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < kHc; ++h) {
+            const float p = s_pre[rb][h];
+            const float4 x = *reinterpret_cast<const float4 *>(streams + ((r0 + rb) * kHc + h) * D + d);
+            v.x = fmaf(p, x.x, v.x);
+            v.y = fmaf(p, x.y, v.y);
+            v.z = fmaf(p, x.z, v.z);
+            v.w = fmaf(p, x.w, v.w);
+        }
+        return v;
+    };
+    if (norm_w) {
+        float ss2[kHcRows];
+#pragma unroll
+        for (int rb = 0; rb < kHcRows; ++rb) {
+            ss2[rb] = 0.f;
+            if (r0 + rb < R)
+                for (int d = 4 * t; d < D; d += 1024) {
+                    const float4 v = collapsed(rb, d);
+                    ss2[rb] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+        }
+#pragma unroll
+        for (int rb = 0; rb < kHcRows; ++rb) {
+            float hi = ss2[rb], lo = 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oh = __shfl_xor_sync(0xffffffffu, hi, o), ol = __shfl_xor_sync(0xffffffffu, lo, o);
+                float sm, rr;
+                two_sum_f(hi, oh, sm, rr);
+                hi = sm;
+                lo = lo + ol + rr;
+            }
+            if (lane == 0) red[warp * kHcRows + rb] = make_float2(hi, lo);
+        }
+        __syncthreads();
+        if (t < kHcRows) {
+            float hi = red[t].x, lo = red[t].y;
+            for (int w = 1; w < 8; ++w) {
+                float sm, rr;
+                two_sum_f(hi, red[w * kHcRows + t].x, sm, rr);
+                hi = sm;
+                lo = lo + red[w * kHcRows + t].y + rr;
+            }
+            s_inv2[t] = (float)(1.0 / sqrt(((double)hi + (double)lo) / (double)D + (double)norm_eps));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int rb = 0; rb < kHcRows; ++rb) {
+        if (r0 + rb >= R) continue;
+        const float inv2 = norm_w ? s_inv2[rb] : 1.f;
+        for (int d = 4 * t; d < D; d += 1024) {
+            const float4 v = collapsed(rb, d);
+            const float4 wv = norm_w ? *reinterpret_cast<const float4 *>(norm_w + d) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float o[4] = {v.x * inv2 * wv.x, v.y * inv2 * wv.y, v.z * inv2 * wv.z, v.w * inv2 * wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st_act(h_out, (r0 + rb) * D + d + i, o[i], h_dtype);
+        }
+    }
+}
+
 int launch_hc_mix(const float *streams, int64_t R, int D, const void *fn, int fn_dtype, const float *base,
                   const float *scale, float rms_eps, double hc_eps, int iters, const float *norm_w, float norm_eps,
                   void *h_out, int h_dtype, float *post, float *comb, cudaStream_t st) {
     if (R == 0) return VFMOE_OK;
+    if (R >= kHcRowsMinR && D % 1024 == 0) {
+        hc_mix_rows_kernel<<<(unsigned)cdiv(R, kHcRows), 256, 0, st>>>(streams, R, D, fn, fn_dtype, base, scale, rms_eps,
+                                                                      hc_eps, iters, norm_w, norm_eps, h_out, h_dtype,
+                                                                      post, comb);
+        VF_LAUNCH_CHECK("hc_mix_rows_kernel");
+        return VFMOE_OK;
+    }
     switch (D / 2048) {
         case 1: hc_mix_kernel<1><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
         case 2: hc_mix_kernel<2><<<(unsigned)R, kHcThreads, 0, st>>>(streams, D, fn, fn_dtype, base, scale, rms_eps, hc_eps, iters, norm_w, norm_eps, h_out, h_dtype, post, comb); break;
