@@ -416,6 +416,39 @@ def test_cta_pair_gemm_matches_single_cta_tiles(c1, c1_tiled, T):
     single.close()
 
 
+@pytest.mark.parametrize("T", [1, 8, 32, 64, 65])
+def test_decode_front_end_matches_separate_launches(c1, T):
+    """At T <= 64 the AUTO path runs dispatch, gather and the GEMV's tile plan as one launch
+    (decode_front_kernel); a layer forced onto the GEMV path keeps the separate launches (as AUTO
+    does from T = 65).  Same permutation, rows and tiles into the same GEMV: outputs, ids and
+    weights bit-identical."""
+    g = torch.Generator(device="cuda").manual_seed(11 + T)
+    x = torch.randn((T, c1.cfg.hidden), generator=g, device="cuda").to(torch.bfloat16)
+    sep = c1.make_layer(torch.float32, path="gemv")
+    a, ia, wa = c1.layer.moe_block(x)
+    b, ib, wb = sep.moe_block(x)
+    torch.cuda.synchronize()
+    c1.layer.check_device_error()
+    sep.check_device_error()
+    print(f"[decode front end T={T}] bit-identical {bool(torch.equal(a, b))}")
+    assert torch.equal(ia, ib) and torch.equal(wa, wb)
+    assert torch.equal(a, b)
+    sep.close()
+
+
+def test_decode_front_end_split_precision(c0):
+    """The same at C0 (fp32 activations: the front end also writes the residual plane)."""
+    sep = c0.make_layer(torch.float32, path="gemv")
+    a, ia, wa = c0.layer.moe_block(c0.x_dev)
+    b, ib, wb = sep.moe_block(c0.x_dev)
+    torch.cuda.synchronize()
+    c0.layer.check_device_error()
+    sep.check_device_error()
+    assert torch.equal(ia, ib) and torch.equal(wa, wb)
+    assert torch.equal(a, b)
+    sep.close()
+
+
 def test_c0_prefill_size_tcgen05_path(c0):
     """T=256 at C0 shapes: 64 tokens per routed expert on average, tcgen05 GEMM forced (C0's fp32
     activations would otherwise take the split-precision GEMV)."""

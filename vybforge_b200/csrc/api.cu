@@ -504,7 +504,19 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     a.tile_counts = reinterpret_cast<int32_t *>(base + lay.tile_counts);
     a.tiles_cap = lay.tiles_cap;
 
-    rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, fused_shared, perm_tok, pos_of, offsets, L->dev_err, st);
+    // decode sizes on the GEMV path: dispatch, gather and the GEMV's tile lists in one launch
+    const bool front = !L->x3.ready && L->tc.path == VFMOE_PATH_AUTO && tc_supported(L->tc, a) &&
+                       tc_decode_gemv(L->tc, a) && T <= kDecodeFrontMaxT && L->E <= 1024;
+    if (front) {
+        a.plan_ready = 1;
+        rc = launch_decode_front(idx, counts, (int)T, L->E, L->k, fused_shared, reinterpret_cast<const void *>(x),
+                                 (int)L->d.x_dtype, L->H, perm_tok, pos_of, offsets,
+                                 reinterpret_cast<__half *>(base + lay.xp), a.prec ? 2 : 1,
+                                 gemv_tokens_per_tile((int)T, L->k, L->E), a.tiles, a.tiles_cap, a.tile_counts,
+                                 L->dev_err, st);
+    } else {
+        rc = launch_dispatch(idx, counts, (int)T, L->E, L->k, fused_shared, perm_tok, pos_of, offsets, L->dev_err, st);
+    }
     if (rc) return rc;
     if (L->dense_sh) {
         // the bf16-stored shared expert: its own dense GEMVs on fp16 x, ahead of the routed experts
@@ -526,12 +538,15 @@ int vfmoe_forward(int64_t handle, int64_t x, int64_t T, int64_t out, int64_t idx
     } else {
         // launch bound T*k + T whether or not there is a shared expert: the second plane of a
         // split-precision layer starts at that row count, as the expert kernels expect
-        rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, T * L->k + T, L->H,
-                           reinterpret_cast<__half *>(base + lay.xp), offsets + L->E + 1, st, a.prec ? 2 : 1);
-        if (rc) return rc;
-        nlaunch += 2;
+        if (!front) {
+            rc = launch_gather(reinterpret_cast<const void *>(x), (int)L->d.x_dtype, perm_tok, T * L->k + T, L->H,
+                               reinterpret_cast<__half *>(base + lay.xp), offsets + L->E + 1, st, a.prec ? 2 : 1);
+            if (rc) return rc;
+        }
+        nlaunch += front ? 1 : 2;
         mark();
         rc = forward_experts(*L, a, st, [&]() { mark(); }, nlaunch);
+        if (front) nlaunch -= 1;  // no tile-plan launch
     }
     if (rc) return rc;
     mark();

@@ -960,17 +960,23 @@ static int launch_pair(const TcParams &prm, cudaStream_t st, bool *launched) {
     return VFMOE_OK;
 }
 
-int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
-    const int64_t rows = (int64_t)a.T * a.k + a.T;
+bool tc_decode_gemv(const TcPlan &plan, const MoeArgs &a) {
     const bool decode = (double)a.T * a.k / a.E <= 16.0;
     const bool forced_tc = plan.path == VFMOE_PATH_TC || plan.path == VFMOE_PATH_TC1;
-    if (a.prec || plan.path == VFMOE_PATH_GEMV || (decode && !forced_tc)) {
+    return a.prec || plan.path == VFMOE_PATH_GEMV || (decode && !forced_tc);
+}
+
+int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid) {
+    const int64_t rows = (int64_t)a.T * a.k + a.T;
+    if (tc_decode_gemv(plan, a)) {
         // decode: register-operand GEMV, one token-tile size for both GEMMs (fp32 activations:
         // its split-precision form at every T)
         const int ng = gemv_tokens_per_tile(a.T, a.k, a.E);
-        VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared, ng,
-                           ng, a.tiles, a.tiles_cap, a.tile_counts, a.err));
-        VF_LAUNCH_CHECK("tc_plan_kernel");
+        if (!a.plan_ready) {
+            VF_CUDA(launch_pdl(tc_plan_kernel, dim3(1), dim3(1024), 0, st, (const int32_t *)a.offsets, a.E, a.has_shared,
+                               ng, ng, a.tiles, a.tiles_cap, a.tile_counts, a.err));
+            VF_LAUNCH_CHECK("tc_plan_kernel");
+        }
         CUtensorMap tg, td, tg2, td2;
         int rc;
         if ((rc = make_tok_map(&tg, a.xp, rows, a.H, ng))) return rc;

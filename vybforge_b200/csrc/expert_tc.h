@@ -74,6 +74,8 @@ __device__ __forceinline__ void load_q8_tiled(uint8_t *dst, const uint8_t *base,
         sm100::bulk_load(dst + h * kQ8Tile, src + (int64_t)h * KR * kQ8Tile, kQ8Tile, bar);
 }
 bool tc_supported(const TcPlan &plan, const MoeArgs &a);
+// launch_experts_tc runs the decode GEMV (few rows per expert, forced GEMV, or fp32 activations).
+bool tc_decode_gemv(const TcPlan &plan, const MoeArgs &a);
 int launch_experts_tc(const TcPlan &plan, const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
 
 // Dense fp16 expert (expert_gemv.cu): gate/up + SwiGLU then down over T token rows of xs

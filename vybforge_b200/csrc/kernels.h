@@ -37,6 +37,7 @@ struct MoeArgs {
     int4 *tiles;               // tensor-core path: two tile lists of tiles_cap entries each
     int32_t *tile_counts;      // [2]
     int64_t tiles_cap;
+    int plan_ready;            // the decode front end already wrote the decode GEMV's tile lists
 };
 
 // Router: fp32 logits -> candidate filter -> float-float / f64 refinement (exact f64 ordering).
@@ -70,6 +71,12 @@ int launch_gather(const void *x, int x_dtype, const int32_t *perm_tok, int64_t r
                   const int32_t *n_rows, cudaStream_t st, int planes = 1);
 int launch_combine(const void *y, int y_dtype, const int32_t *pos_of, const float *w, int T, int H, int k,
                    const void *y_shared, void *out, int out_dtype, cudaStream_t st);
+// Decode front end (T <= kDecodeFrontMaxT, E <= 1024): launch_dispatch + launch_gather + the decode
+// GEMV's tile lists (ng rows per tile, both lists) in one launch, with the same results.
+constexpr int kDecodeFrontMaxT = 64;
+int launch_decode_front(const int32_t *idx, const int32_t *counts, int T, int E, int k, int has_shared, const void *x,
+                        int x_dtype, int H, int32_t *perm_tok, int32_t *pos_of, int32_t *offsets, __half *xp, int planes,
+                        int ng, int4 *tiles, int64_t cap, int32_t *tile_counts, int *err, cudaStream_t st);
 
 // `mid` runs between the gate/up and the down launches (profiling marks).
 int launch_experts_simt(const MoeArgs &a, cudaStream_t st, const std::function<void()> &mid);
