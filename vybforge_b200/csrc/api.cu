@@ -370,8 +370,7 @@ int64_t vfmoe_workspace_bytes(int64_t handle, int64_t t_max) {
 
 int vfmoe::route_impl(Layer &L, int64_t x, int64_t T, char *base, const WsLayout &lay, int32_t **idx_p,
                       float **w_p, cudaStream_t st) {
-    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);
-    VF_CUDA(cudaMemsetAsync(counts, 0, (L.E + 2) * sizeof(int32_t), st));
+    int32_t *counts = reinterpret_cast<int32_t *>(base + lay.counts);  // zeroed by launch_router
     int32_t *idx = *idx_p ? *idx_p : reinterpret_cast<int32_t *>(base + lay.idx);
     float *w = *w_p ? *w_p : reinterpret_cast<float *>(base + lay.w);
     int rc = launch_router(reinterpret_cast<const void *>(x), (int)L.d.x_dtype,

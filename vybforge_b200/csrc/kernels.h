@@ -44,6 +44,8 @@ struct MoeArgs {
 // nw = |W_r row|_2 upper bounds (launch_router_norms, once per layer); logits = scratch of
 // router_logit_floats(T, H, E, wr_split != 0) floats.  wr_split (bf16 [2][E][H], w_hi then w_lo,
 // launch_router_split once per layer; may be 0) enables the tensor-core logits for bf16 x at T > 32.
+// counts [E + 2] is zeroed here (by the first level's kernel at T <= 32, else a memset) and then
+// accumulates the selections per expert.
 int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, const float *nw,
                   const float *bias, int T, int H, int E, int k, double scale, float *logits, int32_t *idx, float *w,
                   int32_t *counts, int *err, cudaStream_t st);

@@ -100,11 +100,16 @@ __device__ __forceinline__ float f32_from_order_key(uint32_t key) {
 // [chunk] is staged in shared memory as fp32, each thread issues all of its W loads before any
 // FMA.  Lane l owns k = 4l + 128j + i of the chunk.  Per-chunk partials part[chunk][t][e] are
 // summed in chunk order by router_refine.  Summation depth: KCH/32 sequential FMAs + 5 (warp
-// tree) + nchunk.
+// tree) + nchunk.  CTA (0, 0, 0) also zeroes zero[0..nzero) (the per-expert counts that the
+// refinement accumulates), in place of a memset before the launch.
 template <int TB, int KCH>
 __global__ void __launch_bounds__(256) router_logits_f32_small(const void *__restrict__ x, int x_dtype,
                                                                const float *__restrict__ wr, int T_all, int H, int E,
-                                                               float *__restrict__ part) {
+                                                               float *__restrict__ part, int32_t *__restrict__ zero,
+                                                               int nzero) {
+    pdl_wait_then_release();
+    if (zero && (blockIdx.x | blockIdx.y | blockIdx.z) == 0)
+        for (int i = threadIdx.x; i < nzero; i += 256) zero[i] = 0;
     int T = T_all;
     extern __shared__ float xs[];  // [TB][KCH]
     constexpr int J = KCH / 128;
@@ -351,11 +356,13 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
     __shared__ unsigned char s_redo[kMaxCand];
     __shared__ float s_phi[8][8], s_plo[8][8];
     __shared__ double s_pd[8][8];
-    pdl_wait_then_release();
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // x_t -> shared memory as fp32 (16-byte loads, issued four at a time) and |x_t|_2 (upper bound)
+    // x_t -> shared memory as fp32 (16-byte loads, issued four at a time) and |x_t|_2 (upper bound).
+    // This runs before the wait on the first level: x comes from a kernel before that one, which
+    // released this launch only after its own wait on x's producer (pdl_wait_then_release), or
+    // ran to completion first.
     float ss = 0.f;
     if (x_dtype == VFMOE_DT_BF16) {
         for (int i0 = 0; i0 < kMaxH / 2048; i0 += 4) {
@@ -405,6 +412,7 @@ __global__ void __launch_bounds__(256, MINB) router_refine(const void *__restric
 #pragma unroll
     for (int i = 0; i < 8; ++i) tot += s_red[i];
     const float nx = sqrtf(tot) * 1.001f;
+    pdl_wait_then_release();  // the first level's partial logits and the zeroed counts
 
     // ---- L2 candidate selection, all threads: thread i owns experts i, i + 256, ...
     // lo/hi = choice -/+ the L1 bound.  tau = the k-th largest lo in the order (lo desc, id
@@ -988,12 +996,13 @@ int launch_router_norms(const float *wr, int H, int E, float *nw, cudaStream_t s
 
 template <int TB, int KCH>
 static int launch_l1_small(const void *x, int x_dtype, const float *wr, int T, int H, int E, float *part,
-                           cudaStream_t st) {
+                           int32_t *zero, int nzero, cudaStream_t st) {
     const int smem = TB * KCH * 4;
     int rc = set_smem_attr_once(reinterpret_cast<const void *>(router_logits_f32_small<TB, KCH>), smem);
     if (rc) return rc;
     dim3 grid((unsigned)cdiv(E, 16), (unsigned)(H / KCH), (unsigned)cdiv(T, TB));
-    router_logits_f32_small<TB, KCH><<<grid, 256, smem, st>>>(x, x_dtype, wr, T, H, E, part);
+    VF_CUDA(launch_pdl(router_logits_f32_small<TB, KCH>, grid, dim3(256), (size_t)smem, st, x, x_dtype, wr, T, H, E,
+                       part, zero, nzero));
     VF_LAUNCH_CHECK("router_logits_f32_small");
     return VFMOE_OK;
 }
@@ -1022,7 +1031,8 @@ static int router_splits(int T, int H, int E, bool tc) {
 }
 
 int launch_router_l1(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, int T, int H, int E,
-                     float *logits, int *err, cudaStream_t st, int *nchunk_out, float *c1_out) {
+                     float *logits, int *err, cudaStream_t st, int *nchunk_out, float *c1_out, int32_t *zero,
+                     int nzero) {
     if (H > kMaxH || H / 512 > kMaxChunks) {
         set_error("router: hidden size %d exceeds %d", H, kMaxH);
         return VFMOE_ERR_UNSUPPORTED;
@@ -1033,15 +1043,16 @@ int launch_router_l1(const void *x, int x_dtype, const float *wr, const __nv_bfl
     const bool tc = wr_split && x_dtype == VFMOE_DT_BF16 && router_tc_shape(T, H, E) &&
                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const int nchunk = router_splits(T, H, E, tc);
+    if (zero && !(T <= 32 && kch && !tc)) VF_CUDA(cudaMemsetAsync(zero, 0, (size_t)nzero * sizeof(int32_t), st));
     if (tc) {
         rc = launch_router_logits_tc(x, wr_split, T, H, E, logits, err, st);
         if (rc) return rc;
         c1 = router_tc_bound(H);
     } else if (T <= 32 && kch) {
         if (kch == 768)
-            rc = launch_l1_small<8, 768>(x, x_dtype, wr, T, H, E, logits, st);
+            rc = launch_l1_small<8, 768>(x, x_dtype, wr, T, H, E, logits, zero, nzero, st);
         else
-            rc = launch_l1_small<8, 512>(x, x_dtype, wr, T, H, E, logits, st);
+            rc = launch_l1_small<8, 512>(x, x_dtype, wr, T, H, E, logits, zero, nzero, st);
         if (rc) return rc;
         c1 = gamma_bound(kch / 32 + 5 + nchunk);
     } else {
@@ -1060,7 +1071,7 @@ int launch_router(const void *x, int x_dtype, const float *wr, const __nv_bfloat
                   int32_t *counts, int *err, cudaStream_t st) {
     int nchunk = 1;
     float c1 = 0.f;
-    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, logits, err, st, &nchunk, &c1);
+    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, logits, err, st, &nchunk, &c1, counts, E + 2);
     if (rc) return rc;
     // L2: thread owns n = H/256 terms.  hi + sum(r) = sum(p) exactly (TwoSum) and x*w = p + pe
     // exactly (TwoProduct), so the only error is lo's fp32 summation of the r and pe values,
@@ -1136,7 +1147,7 @@ __global__ void sum_partials_kernel(const float *__restrict__ part, int nchunk, 
 int launch_route_logits(const void *x, int x_dtype, const float *wr, const __nv_bfloat16 *wr_split, int T, int H,
                         int E, float *part, float *out, int *err, cudaStream_t st, float *c1) {
     int nchunk = 1;
-    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, part, err, st, &nchunk, c1);
+    int rc = launch_router_l1(x, x_dtype, wr, wr_split, T, H, E, part, err, st, &nchunk, c1, nullptr, 0);
     if (rc) return rc;
     const int64_t n = (int64_t)T * E;
     sum_partials_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(part, nchunk, n, out);
