@@ -49,10 +49,12 @@ def test_hc_matches_reference_golden():
 
 
 @pytest.mark.parametrize("D,fn_bf16,R", [(4096, True, 37), (6144, True, 37), (2048, False, 37), (8192, True, 37),
-                                          (6144, True, 1030), (2048, False, 1030)])
+                                          (6144, True, 1030), (2048, False, 1030), (4096, True, 257),
+                                          (8192, True, 300)])
 def test_hc_mix_and_apply_match_oracle(D, fn_bf16, R):
-    """R = 37 takes the one-row-per-CTA mix, R = 1030 the four-rows-per-CTA one (with a partial
-    last block)."""
+    """R = 37 takes the one-row-per-CTA mix; from R = 256 a bf16 hc_fn takes the tensor-core mix
+    (16 rows per CTA; R = 257 and 300 end in a partial block), an fp32 one the two-rows-per-CTA
+    mix (R = 1030)."""
     moe.init(0)
     rng = np.random.default_rng(D + R)
     streams = (rng.standard_normal((R, 4, D)) * rng.uniform(0.2, 3.0, (R, 4, 1))).astype(np.float32)

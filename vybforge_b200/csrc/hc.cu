@@ -421,10 +421,253 @@ __global__ void __launch_bounds__(256, 2) hc_mix_rows_kernel(const float *__rest
     }
 }
 
+// hc_mix_tc_kernel: the mix for batches of rows with a bf16 hc_fn, the 24 dot products on the
+// tensor pipe.  A CTA takes kHcTcRows = 16 rows (one m16 tile); warp w takes the flattened K = 4D
+// range [w K/8, (w + 1) K/8) of all 16 rows, so every hc_fn value loaded serves 16 rows.
+//   mma.sync m16n8k8 tf32, three n8 tiles (the 24 mix values): A = stream values, B = hc_fn rows.
+//   A value x is split into hi = x with the low 13 mantissa bits cleared (exact in tf32) and
+//   lo = tf32_rn(x - hi) (x - hi is exact in fp32, |x - hi| < 2^-10 |x|), so x = hi + lo to
+//   about 2^-21 |x|; bf16 hc_fn is exact in tf32 and every product exact in fp32.
+//   K permutation inside a k16 chunk: thread (g, c) loads the float4 at k = 4c of rows g and g + 8
+//   and the four bf16 at k = 4c of hc_fn row 8 nt + g; its MMA slots c and c + 4 of step s take
+//   k = 4c + 2s and 4c + 2s + 1, the same for A and B, so the products are those of the plain
+//   dot product.
+//   Accuracy: the fp32 accumulators restart every 64 K (16 MMAs) and are added into float-float
+//   totals (TwoSum); the sum of squares likewise.  The warps' totals are added in warp order.
+// Then, as hc_mix_rows_kernel: the gates and the normalisation (hc_tail_warp, two rows per warp),
+// and the collapse with its RMSNorm (two passes over the block's rows, L2-resident).
+constexpr int kHcTcRows = 16;
+constexpr int64_t kHcTcMinR = 256;
+
+__device__ __forceinline__ void mma_tf32_16808(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t tf32_rn(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ void ff_acc(float &hi, float &lo, float v) {
+    float sm, r;
+    two_sum_f(hi, v, sm, r);
+    hi = sm;
+    lo += r;
+}
+
+template <int CH>  // D / 1024
+__global__ void __launch_bounds__(256, 2) hc_mix_tc_kernel(const float *__restrict__ streams, int64_t R, int D,
+                                                         const __nv_bfloat16 *__restrict__ fn,
+                                                         const float *__restrict__ base, const float *__restrict__ scale,
+                                                         float rms_eps, double hc_eps, int iters,
+                                                         const float *__restrict__ norm_w, float norm_eps,
+                                                         void *__restrict__ h_out, int h_dtype,
+                                                         float *__restrict__ post_out, float *__restrict__ comb_out) {
+    constexpr int NV = kHcMix + 1;
+    __shared__ float2 red[8][kHcTcRows][NV];
+    __shared__ double s_tot[kHcTcRows][NV];
+    __shared__ float s_pre[kHcTcRows][kHc];
+    __shared__ float s_inv2[kHcTcRows];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const int64_t r0 = (int64_t)blockIdx.x * kHcTcRows;
+    const int64_t K = (int64_t)kHc * D;
+    const int kw = (int)(K / 8);
+    const bool va = r0 + g < R, vb = r0 + g + 8 < R;
+    const float *xa = streams + (va ? (r0 + g) * K : 0) + (int64_t)warp * kw + 4 * c;
+    const float *xb = streams + (vb ? (r0 + g + 8) * K : 0) + (int64_t)warp * kw + 4 * c;
+    const __nv_bfloat16 *f0 = fn + (int64_t)g * K + (int64_t)warp * kw + 4 * c;  // n tile nt: + 8 nt K
+
+    float acc[3][4], fh[3][4], fl[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = fh[nt][e] = fl[nt][e] = 0.f;
+    float ssa = 0.f, ssb = 0.f, sha = 0.f, sla = 0.f, shb = 0.f, slb = 0.f;
+    for (int k = 0; k < kw; k += 64) {
+        float4 xv[2][4];
+        uint2 fv[3][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xv[0][q] = va ? *reinterpret_cast<const float4 *>(xa + k + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[1][q] = vb ? *reinterpret_cast<const float4 *>(xb + k + 16 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int nt = 0; nt < 3; ++nt)
+                fv[nt][q] = *reinterpret_cast<const uint2 *>(f0 + 8 * nt * K + k + 16 * q);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            ssa = fmaf(xv[0][q].x, xv[0][q].x, fmaf(xv[0][q].y, xv[0][q].y, fmaf(xv[0][q].z, xv[0][q].z, fmaf(xv[0][q].w, xv[0][q].w, ssa))));
+            ssb = fmaf(xv[1][q].x, xv[1][q].x, fmaf(xv[1][q].y, xv[1][q].y, fmaf(xv[1][q].z, xv[1][q].z, fmaf(xv[1][q].w, xv[1][q].w, ssb))));
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+                const float a0 = s2 ? xv[0][q].z : xv[0][q].x, a1 = s2 ? xv[0][q].w : xv[0][q].y;
+                const float b0 = s2 ? xv[1][q].z : xv[1][q].x, b1 = s2 ? xv[1][q].w : xv[1][q].y;
+                const uint32_t ha0 = __float_as_uint(a0) & 0xFFFFE000u, ha1 = __float_as_uint(a1) & 0xFFFFE000u;
+                const uint32_t hb0 = __float_as_uint(b0) & 0xFFFFE000u, hb1 = __float_as_uint(b1) & 0xFFFFE000u;
+                const uint32_t la0 = tf32_rn(a0 - __uint_as_float(ha0)), la1 = tf32_rn(a1 - __uint_as_float(ha1));
+                const uint32_t lb0 = tf32_rn(b0 - __uint_as_float(hb0)), lb1 = tf32_rn(b1 - __uint_as_float(hb1));
+#pragma unroll
+                for (int nt = 0; nt < 3; ++nt) {
+                    const uint32_t w = s2 ? fv[nt][q].y : fv[nt][q].x;
+                    const uint32_t f_lo = w << 16, f_hi = w & 0xFFFF0000u;  // k = 4c + 2 s2, 4c + 2 s2 + 1
+                    // A slots: (row g, c) (row g + 8, c) (row g, c + 4) (row g + 8, c + 4)
+                    mma_tf32_16808(acc[nt], ha0, hb0, ha1, hb1, f_lo, f_hi);
+                    mma_tf32_16808(acc[nt], la0, lb0, la1, lb1, f_lo, f_hi);
+                }
+            }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ff_acc(fh[nt][e], fl[nt][e], acc[nt][e]);
+                acc[nt][e] = 0.f;
+            }
+        ff_acc(sha, sla, ssa);
+        ff_acc(shb, slb, ssb);
+        ssa = ssb = 0.f;
+    }
+    // sums of squares: the quad's four threads share a row pair
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        float oh = __shfl_xor_sync(0xffffffffu, sha, o), ol = __shfl_xor_sync(0xffffffffu, sla, o);
+        float sm, rr;
+        two_sum_f(sha, oh, sm, rr);
+        sha = sm;
+        sla = sla + ol + rr;
+        oh = __shfl_xor_sync(0xffffffffu, shb, o);
+        ol = __shfl_xor_sync(0xffffffffu, slb, o);
+        two_sum_f(shb, oh, sm, rr);
+        shb = sm;
+        slb = slb + ol + rr;
+    }
+    // accumulator element e of tile nt: row g + 8 (e >> 1), mix value 8 nt + 2c + (e & 1)
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][g + 8 * (e >> 1)][8 * nt + 2 * c + (e & 1)] = make_float2(fh[nt][e], fl[nt][e]);
+    if (c == 0) {
+        red[warp][g][kHcMix] = make_float2(sha, sla);
+        red[warp][g + 8][kHcMix] = make_float2(shb, slb);
+    }
+    __syncthreads();
+    for (int i = t; i < kHcTcRows * NV; i += 256) {
+        const int rr = i / NV, j = i % NV;
+        float hi = red[0][rr][j].x, lo = red[0][rr][j].y;
+#pragma unroll
+        for (int w = 1; w < 8; ++w) {
+            float sm, e2;
+            two_sum_f(hi, red[w][rr][j].x, sm, e2);
+            hi = sm;
+            lo = lo + red[w][rr][j].y + e2;
+        }
+        s_tot[rr][j] = (double)hi + (double)lo;
+    }
+    __syncthreads();
+    for (int rr = warp; rr < kHcTcRows; rr += 8)
+        hc_tail_warp(s_tot[rr], D, base, scale, rms_eps, hc_eps, iters, r0 + rr, r0 + rr < R, post_out, comb_out,
+                     s_pre[rr]);
+    __syncthreads();
+    // collapse and RMSNorm, one row at a time: thread t holds the row's collapsed values at
+    // d = 4t + 1024q (q < CH) in registers, its loads issued in batches of four chunks (16 float4)
+    // before they are used; one float-float block sum for the row's sum of squares, then the
+    // normalised output from the same registers.
+    const int nrow = (int)(R - r0 < kHcTcRows ? R - r0 : kHcTcRows);
+    float2 *red2 = &red[0][0][0];  // [8 warps], per row
+    for (int rb = 0; rb < nrow; ++rb) {
+        float4 hv[CH];
+        float ss2 = 0.f;
+        const float *rowp = streams + (r0 + rb) * K + 4 * t;
+#pragma unroll
+        for (int q0 = 0; q0 < CH; q0 += 4) {
+            float4 xs[4][kHc];
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq)
+                if (q0 + qq < CH)
+#pragma unroll
+                    for (int h = 0; h < kHc; ++h)
+                        xs[qq][h] = *reinterpret_cast<const float4 *>(rowp + (int64_t)h * D + 1024 * (q0 + qq));
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq)
+                if (q0 + qq < CH) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int h = 0; h < kHc; ++h) {
+                        const float p = s_pre[rb][h];
+                        v.x = fmaf(p, xs[qq][h].x, v.x);
+                        v.y = fmaf(p, xs[qq][h].y, v.y);
+                        v.z = fmaf(p, xs[qq][h].z, v.z);
+                        v.w = fmaf(p, xs[qq][h].w, v.w);
+                    }
+                    hv[q0 + qq] = v;
+                    ss2 += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+        }
+        float inv2 = 1.f;
+        if (norm_w) {
+            float hi = ss2, lo = 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oh = __shfl_xor_sync(0xffffffffu, hi, o), ol = __shfl_xor_sync(0xffffffffu, lo, o);
+                float sm, rr;
+                two_sum_f(hi, oh, sm, rr);
+                hi = sm;
+                lo = lo + ol + rr;
+            }
+            if (lane == 0) red2[(rb & 1) * 8 + warp] = make_float2(hi, lo);  // two buffers: no second barrier
+            __syncthreads();
+            hi = red2[(rb & 1) * 8].x;
+            lo = red2[(rb & 1) * 8].y;
+#pragma unroll
+            for (int w = 1; w < 8; ++w) {
+                float sm, rr;
+                two_sum_f(hi, red2[(rb & 1) * 8 + w].x, sm, rr);
+                hi = sm;
+                lo = lo + red2[(rb & 1) * 8 + w].y + rr;
+            }
+            inv2 = (float)(1.0 / sqrt(((double)hi + (double)lo) / (double)D + (double)norm_eps));
+        }
+#pragma unroll
+        for (int q = 0; q < CH; ++q) {
+            const int d = 4 * t + 1024 * q;
+            const float4 wv = norm_w ? *reinterpret_cast<const float4 *>(norm_w + d) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float o[4] = {hv[q].x * inv2 * wv.x, hv[q].y * inv2 * wv.y, hv[q].z * inv2 * wv.z,
+                                hv[q].w * inv2 * wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st_act(h_out, (r0 + rb) * D + d + i, o[i], h_dtype);
+        }
+    }
+}
+
 int launch_hc_mix(const float *streams, int64_t R, int D, const void *fn, int fn_dtype, const float *base,
                   const float *scale, float rms_eps, double hc_eps, int iters, const float *norm_w, float norm_eps,
                   void *h_out, int h_dtype, float *post, float *comb, cudaStream_t st) {
     if (R == 0) return VFMOE_OK;
+    if (fn_dtype == VFMOE_DT_BF16 && R >= kHcTcMinR && D % 2048 == 0 && D >= 2048 && D <= 8192) {
+        const dim3 grid((unsigned)cdiv(R, kHcTcRows));
+        const __nv_bfloat16 *f = reinterpret_cast<const __nv_bfloat16 *>(fn);
+        switch (D / 1024) {
+#define VF_HC_TC(CH)                                                                                                 \
+    case CH:                                                                                                        \
+        hc_mix_tc_kernel<CH><<<grid, 256, 0, st>>>(streams, R, D, f, base, scale, rms_eps, hc_eps, iters, norm_w,      \
+                                                   norm_eps, h_out, h_dtype, post, comb);                           \
+        break;
+            VF_HC_TC(2)
+            VF_HC_TC(4)
+            VF_HC_TC(6)
+            VF_HC_TC(8)
+#undef VF_HC_TC
+        }
+        VF_LAUNCH_CHECK("hc_mix_tc_kernel");
+        return VFMOE_OK;
+    }
     if (R >= kHcRowsMinR && D % 1024 == 0) {
         hc_mix_rows_kernel<<<(unsigned)cdiv(R, kHcRows), 256, 0, st>>>(streams, R, D, fn, fn_dtype, base, scale, rms_eps,
                                                                       hc_eps, iters, norm_w, norm_eps, h_out, h_dtype,
