@@ -174,9 +174,28 @@ def _profile_router():
     print(json.dumps({"route_us": res}))
 
 
+def _profile_hc_mix():
+    """vfmoe_hc_mix at the C3 token count (R = 4096 rows of 4 fp32 streams, H = 6144, bf16 hc_fn,
+    the tensor-core mix), three calls; 0.5 GB on the device."""
+    import torch
+    from vybforge_b200.moe import HyperConnection, init
+    init(0)
+    R, D = 4096, 6144
+    g = torch.Generator(device="cuda").manual_seed(5)
+    fn = (torch.randn((24, 4 * D), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    site = HyperConnection(fn, torch.randn(24, generator=g, device="cuda") * 0.5,
+                           torch.tensor([0.8, 1.3, 2.0], device="cuda"), 1 + 0.02 * torch.randn(D, generator=g, device="cuda"))
+    streams = torch.randn((R, 4, D), generator=g, device="cuda")
+    for _ in range(3):
+        h, post, comb = site.mix(streams)
+    torch.cuda.synchronize()
+    print(json.dumps({"hc_mix_h_mean_abs": float(h.float().abs().mean())}))
+
+
 PROFILE_CASES = {"q8_decode_e64": lambda a: _profile_decode("q8_0", a.q8_layout),
                  "exl3_decode_e64": lambda a: _profile_decode("exl3"),
-                 "q8_prefill_e64": lambda a: _profile_prefill(a.q8_layout), "router_sweep": lambda a: _profile_router()}
+                 "q8_prefill_e64": lambda a: _profile_prefill(a.q8_layout), "router_sweep": lambda a: _profile_router(),
+                 "hc_mix": lambda a: _profile_hc_mix()}
 
 
 # ----------------------------------------------------------------------------- clocks
