@@ -176,8 +176,13 @@ __global__ void __launch_bounds__(GvCfg<GATEUP, NT, PREC, DENSE>::THREADS, 1)
         fence_mbar_init();
     }
     __syncthreads();
-    // the next kernel (the down GEMV after gate/up) may be scheduled onto SMs as this grid
-    // retires; it reads this grid's output only after griddepcontrol.wait
+    // Programmatic dependent launch: the routed gate/up reads the tile list that the kernel
+    // before it writes, so every thread waits for that kernel first (the barriers and the tensor
+    // maps above are set up while it runs).  The down GEMV reads a tile list written two kernels
+    // back and waits only before its token rows (below).  The next kernel (the down GEMV after
+    // gate/up) may be scheduled onto SMs as this grid retires; it reads this grid's output only
+    // after griddepcontrol.wait.
+    if constexpr (GATEUP && !DENSE) griddep_wait();
     if (threadIdx.x == 0) griddep_launch_dependents();
     const int n_items = (DENSE ? (p.dense_T + N - 1) / N : *p.n_tiles) * MT;
     // the item's token tile: the tile list, or for a dense expert tiles of N rows in order
@@ -465,23 +470,11 @@ static int launch_gv(const TcParams &prm, int grid, cudaStream_t st) {
     if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_mma<GATEUP, NT, PREC, DENSE>),
                                          C::SMEM))
         return rc_attr;
-    if (GATEUP) {
-        expert_gemv_mma<GATEUP, NT, PREC, DENSE><<<grid, C::THREADS, C::SMEM, st>>>(prm);
-    } else {
-        // programmatic dependent launch: CTAs start streaming down weights on SMs the gate/up
-        // grid has released, before its act rows are complete
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(C::THREADS);
-        cfg.dynamicSmemBytes = C::SMEM;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        VF_CUDA(cudaLaunchKernelEx(&cfg, expert_gemv_mma<GATEUP, NT, PREC, DENSE>, prm));
-    }
+    // programmatic dependent launch: gate/up sets up while the kernel before it finishes; the down
+    // GEMV's CTAs start streaming weights on SMs the gate/up grid has released, before its act
+    // rows are complete
+    VF_CUDA(launch_pdl(expert_gemv_mma<GATEUP, NT, PREC, DENSE>, dim3(grid), dim3(C::THREADS), (size_t)C::SMEM, st,
+                       prm));
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_mma<gate_up>" : "expert_gemv_mma<down>");
     return VFMOE_OK;
 }
