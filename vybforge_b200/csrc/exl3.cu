@@ -74,6 +74,7 @@ __global__ void __launch_bounds__(256) gather_exl3_kernel(const void *__restrict
                                                           const int32_t *__restrict__ offsets, int nseg, int E, int H,
                                                           MatrixRef gate, MatrixRef up, MatrixRef sh_gate,
                                                           MatrixRef sh_up, __half *__restrict__ xp) {
+    pdl_wait_then_release();
     const int pos = blockIdx.x;
     if (pos >= offsets[nseg]) return;  // launch size is an upper bound on the rows dispatched
     const int t = perm_tok[pos];
@@ -228,6 +229,10 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) expert_gemv_exl3(const __gri
         fence_mbar_init();
     }
     __syncthreads();
+    // programmatic dependent launch: the set-up above overlaps the previous kernel; every thread
+    // waits for it before reading the tile list or issuing a load of its rows
+    griddep_wait();
+    if (threadIdx.x == 0) griddep_launch_dependents();
     const int n_items = (*p.n_tiles) * MT;
 
     if (warp == CW) {
@@ -890,7 +895,7 @@ template <bool GATEUP, int NT, int CW, int BITS>
 static int launch_x1(const XParams &prm, int grid, cudaStream_t st) {
     using C = XCfg<GATEUP, NT, CW, BITS>;
     if (int rc_attr = set_smem_attr_once(reinterpret_cast<const void *>(expert_gemv_exl3<GATEUP, NT, CW, BITS>), C::SMEM)) return rc_attr;
-    expert_gemv_exl3<GATEUP, NT, CW, BITS><<<grid, C::THREADS, C::SMEM, st>>>(prm);
+    VF_CUDA(launch_pdl(expert_gemv_exl3<GATEUP, NT, CW, BITS>, dim3(grid), dim3(C::THREADS), (size_t)C::SMEM, st, prm));
     VF_LAUNCH_CHECK(GATEUP ? "expert_gemv_exl3<gate_up>" : "expert_gemv_exl3<down>");
     return VFMOE_OK;
 }
@@ -975,9 +980,9 @@ int launch_experts_exl3(const Exl3Plan &plan, const MoeArgs &a, const void *x, i
     int rc = prefill ? launch_tc_plan(a, 128, 256, st) : launch_tc_plan(a, N, N, st);
     if (rc) return rc;
     if (rows > 0) {
-        gather_exl3_kernel<<<(unsigned)rows, 256, 0, st>>>(x, x_dtype, a.perm_tok, a.offsets, a.E + (a.has_shared ? 1 : 0),
-                                                           a.E, a.H, a.gate, a.up, a.sh_gate, a.sh_up,
-                                                           const_cast<__half *>(a.xp));
+        VF_CUDA(launch_pdl(gather_exl3_kernel, dim3((unsigned)rows), dim3(256), 0, st, x, x_dtype, a.perm_tok,
+                           (const int32_t *)a.offsets, a.E + (a.has_shared ? 1 : 0), a.E, a.H, a.gate, a.up, a.sh_gate,
+                           a.sh_up, const_cast<__half *>(a.xp)));
         VF_LAUNCH_CHECK("gather_exl3_kernel");
     }
     if (prefill) return launch_exl3_tc(plan, a, st, mid);
